@@ -1,0 +1,225 @@
+/*
+ * qkv.h -- C ABI of the B200 (sm_100a) Qwen3-ASR text-decoder KV-cache path.
+ *
+ * This is the drop-in boundary for the reference's decoder operator surface
+ * (qwenasr.cpp src/text-decoder.h).  All entry points are extern "C", take
+ * plain pointers and sizes, and return an int status (QKV_OK == 0).  A handle
+ * owns one CUDA device: its weights, its paged KV pool and its stream table.
+ * It is driven by one host thread at a time.  Multi-GPU = one handle per GPU.
+ *
+ * Every entry point whose arguments are host buffers synchronises the handle's
+ * CUDA stream before it returns.  Entry points taking device pointers run on
+ * the CUDA stream passed in (NULL = the handle's own stream) and do not
+ * synchronise.
+ *
+ * Errors: a non-zero status; the message is kept per handle and read with
+ * qkv_last_error().  Kernels never trap: device-side failures (a bounded wait
+ * that ran out, an out-of-range page index) set a device error word that the
+ * next synchronising call turns into QKV_ERR_DEVICE.
+ */
+#ifndef QKV_H
+#define QKV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QKV_ABI_VERSION 1
+
+typedef struct qkv_handle qkv_handle;
+typedef struct qkv_pager qkv_pager;
+
+enum qkv_status {
+    QKV_OK = 0,
+    QKV_ERR_INVALID_ARG = 1,   /* bad argument or configuration */
+    QKV_ERR_OUT_OF_PAGES = 2,  /* the KV pool has no free page */
+    QKV_ERR_CAPACITY = 3,      /* stream / context / batch limit exceeded */
+    QKV_ERR_CUDA = 4,          /* a CUDA runtime call failed */
+    QKV_ERR_DEVICE = 5,        /* a kernel reported an error (bounds, bounded wait) */
+    QKV_ERR_IO = 6,            /* file could not be opened / mapped */
+    QKV_ERR_FORMAT = 7,        /* GGUF parse error, missing tensor, shape or type mismatch */
+    QKV_ERR_STATE = 8,         /* call not valid in the current state */
+    QKV_ERR_NO_DEVICE = 9      /* no CUDA device / wrong architecture */
+};
+
+enum qkv_dtype {
+    QKV_F32 = 0,
+    QKV_BF16 = 1,
+    QKV_FP8_E4M3 = 2           /* KV cache only: e4m3 values, fp32 scale per (page, kv head) */
+};
+
+/* Decoder hyper-parameters (GGUF keys qwen3-asr.text.*).
+ * Mirrors the int/float parameters of qwenasr_text_decoder_backend_init
+ * (text-decoder.h:85-99). */
+typedef struct qkv_model_config {
+    int32_t n_layers;
+    int32_t hidden;
+    int32_t n_heads;
+    int32_t n_kv_heads;
+    int32_t head_dim;        /* must be 128 */
+    int32_t intermediate;
+    int32_t vocab;
+    float rope_theta;
+    float rms_norm_eps;
+} qkv_model_config;
+
+/* Runtime / memory plan of a handle.  Replaces the reference's single
+ * max_seq_len (text-decoder.h:101-116) with a paged pool. */
+typedef struct qkv_runtime_config {
+    int32_t device;            /* CUDA device ordinal */
+    int32_t weight_dtype;      /* QKV_F32 or QKV_BF16 (f32 GGUF values are rounded RNE) */
+    int32_t kv_dtype;          /* QKV_F32, QKV_BF16 or QKV_FP8_E4M3 */
+    int32_t page_tokens;       /* tokens per page; must be 16 */
+    int32_t max_streams;       /* stream slots */
+    int32_t max_context;       /* tokens per stream (prompt + generated) */
+    int64_t max_pages;         /* pages in the pool; 0 = max_streams * ceil(max_context/page_tokens) */
+    int32_t max_batch_tokens;  /* prompt tokens one qkv_prefill call may carry; 0 = max_context */
+    uint32_t page_order_seed;  /* 0: pages handed out in pool order; else a seeded permutation */
+} qkv_runtime_config;
+
+/* Fill *cfg from the qwen3-asr.text.* keys of a GGUF file
+ * (the reference reads them in native-model.cpp:187-218). */
+int qkv_read_gguf_config(const char *gguf_path, qkv_model_config *cfg, char *err, size_t err_len);
+
+/* Load the decoder weights of a GGUF file onto rt->device and allocate the KV
+ * pool.  Replaces qwenasr_text_decoder_backend_init / _init_cached
+ * (text-decoder.h:85-116, text-decoder.cpp:1476-1639).  cfg may be NULL, in
+ * which case it is read from the file.  Tensors must be F32, F16 or BF16 with
+ * the reference's names and shapes (text-decoder.cpp:191-228, 523-537).  The
+ * file is not needed after the call returns. */
+int qkv_create(const char *gguf_path, const qkv_model_config *cfg, const qkv_runtime_config *rt,
+               qkv_handle **out, char *err, size_t err_len);
+
+/* A handle with a KV pool and the per-layer QK-norm weights only (no
+ * projection weights): the operator-level entry points below work on it.
+ * q_norm_w / k_norm_w are host arrays [n_layers][head_dim]. */
+int qkv_create_kv_only(const qkv_model_config *cfg, const qkv_runtime_config *rt,
+                       const float *q_norm_w, const float *k_norm_w, qkv_handle **out, char *err,
+                       size_t err_len);
+
+/* Replaces qwenasr_text_decoder_backend_free (text-decoder.h:118). NULL-safe. */
+void qkv_destroy(qkv_handle *h);
+
+const char *qkv_last_error(const qkv_handle *h);
+
+/* ---- stream table (the reference keeps one stream: cur_len, text-decoder.cpp:186) ---- */
+int qkv_stream_open(qkv_handle *h, int32_t *stream_id);
+int qkv_stream_close(qkv_handle *h, int32_t stream_id);           /* frees the stream's pages */
+int qkv_stream_length(const qkv_handle *h, int32_t stream_id, int32_t *tokens);
+int qkv_pool_stats(const qkv_handle *h, int64_t *free_pages, int64_t *total_pages);
+/* Move live pages to the low end of the pool (device page copies + page-table
+ * rewrite); *moved = pages moved. */
+int qkv_compact(qkv_handle *h, int64_t *moved);
+
+/* ---- model-level path (host buffers; synchronising) ---- */
+
+/* Prefill n streams (each must be open and empty) with their prompt rows
+ * embeddings[Σ lens][hidden] f32 (audio rows already spliced in, the layout of
+ * QwenAsrDecoderInputOutput::values, decoder-input.h:11-17), positions 0..len-1.
+ * Writes every layer's K/V into the streams' pages and the greedy id of each
+ * stream's last row to out_ids[n].  out_logits (nullable) receives [n][vocab]
+ * f32.  Replaces the prefill half of text_decoder_backend_cached_logits
+ * (text-decoder.cpp:1641-1755) and qwenasr_text_prefill_backend_forward
+ * (:1757-1854). */
+int qkv_prefill(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *lens,
+                const float *embeddings, int32_t *out_ids, float *out_logits);
+
+/* One greedy decode step for n streams: embed in_ids (NULL = each stream's
+ * last greedy id kept on the device), run all layers appending one token per
+ * stream, and write the next greedy ids to out_ids[n] (first maximum, as
+ * text-decoder.cpp:2266-2274).  out_logits nullable [n][vocab]. */
+int qkv_decode_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *in_ids,
+                    int32_t *out_ids, float *out_logits);
+
+/* The reference's cached greedy loop for one stream: prefill, then up to
+ * max_new_tokens-1 decode steps, stopping after an id in stop_ids.  Uses (and
+ * closes) a temporary stream.  Replaces qwenasr_text_generate_cached_backend
+ * (text-decoder.h:156-163, text-decoder.cpp:2209-2311). */
+int qkv_generate(qkv_handle *h, const float *embeddings, int32_t tokens, int32_t max_new_tokens,
+                 const int32_t *stop_ids, int32_t n_stop, int32_t *out_ids, int32_t *n_out,
+                 int32_t *stopped);
+
+/* ---- operator level: one layer's K/V append and decode attention ----
+ * Device pointers; stream = cudaStream_t or NULL for the handle's stream.
+ * Rows: slots[i] is an open stream id, positions[i] its token position. */
+
+/* K1: qkv[n][Hq*D + 2*Hkv*D] f32 (raw projections) -> QK-RMSNorm + NEOX RoPE;
+ * K, V stored into the page of (slot, position); q_out[n][Hq*D] f32.
+ * Replaces text-decoder.cpp:375-433 (norm, rope, cpy into the cache view). */
+int qkv_kv_append(qkv_handle *h, int32_t layer, int32_t n, const int32_t *slots_dev,
+                  const int32_t *positions_dev, const float *qkv_dev, float *q_out_dev, void *stream);
+
+/* K2: decode attention of q[n][Hq*D] f32 over tokens [0, lens[i]) of each
+ * row's pages; out[n][Hq*D] f32.  Replaces text-decoder.cpp:435-463. */
+int qkv_kv_attend(qkv_handle *h, int32_t layer, int32_t n, const int32_t *slots_dev,
+                  const int32_t *lens_dev, const float *q_dev, float *out_dev, void *stream);
+
+/* One KV-cache step of the microbench: for each of the n streams append one
+ * token and attend, for every layer.  qkv[n_layers][n][Hq*D+2*Hkv*D] f32,
+ * out[n_layers][n][Hq*D] f32 (layer-major), device pointers; the streams'
+ * lengths grow by 1.  stream_ids is a host array. */
+int qkv_kv_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const float *qkv_dev,
+                float *out_dev, void *stream);
+
+/* qkv_kv_step with pinned-or-pageable HOST qkv/out buffers: the copies in and
+ * out are part of the call (synchronising). */
+int qkv_kv_step_host(qkv_handle *h, int32_t n, const int32_t *stream_ids, const float *qkv_host,
+                     float *out_host);
+
+/* Grow an open stream's length by `tokens` without writing K/V (pages are
+ * allocated; their contents are whatever the pool holds).  For benches that
+ * need long contexts quickly. */
+int qkv_stream_extend(qkv_handle *h, int32_t stream_id, int32_t tokens);
+
+/* Fill every page currently owned by open streams, in every layer, with
+ * seeded N(0,1) values in the cache dtype (fp8: per-page scales set). */
+int qkv_fill_random(qkv_handle *h, uint64_t seed);
+
+/* Page gather: copy tokens [0, len) of one stream's layer cache to host as
+ * contiguous k[len][Hkv*D] and v[len][Hkv*D] in the cache dtype (fp8: raw
+ * e4m3 bytes; scales via scales_out[n_pages][2][Hkv] when non-NULL). */
+int qkv_gather(qkv_handle *h, int32_t layer, int32_t stream_id, void *k_host, void *v_host,
+               float *scales_out);
+
+/* Page table of a stream: up to cap page ids into pages_out; *n = pages used. */
+int qkv_stream_pages(const qkv_handle *h, int32_t stream_id, int32_t *pages_out, int32_t cap,
+                     int32_t *n);
+
+/* Synchronise the handle's stream and surface any device error. */
+int qkv_sync(qkv_handle *h);
+
+/* Device scratch / launch accounting of the last call (for benches). */
+int qkv_last_launches(const qkv_handle *h, int64_t *kernels);
+
+/* Host-only GGUF probe (no GPU): shape / type of one tensor, and up to
+ * cap_bytes of its raw data copied to data_out (nullable).  ne_out[4] gets
+ * GGML ne (unused dims 1).  The loader checks of gguf-model.cpp:110-162 apply. */
+int qkv_gguf_tensor(const char *gguf_path, const char *name, int64_t *ne_out, int32_t *n_dims, int32_t *ggml_type,
+                    void *data_out, size_t cap_bytes, char *err, size_t err_len);
+
+/* ---- host-only page allocator (no GPU needed; used inside every handle) ----
+ * Pages hold page_tokens tokens of every layer's K and V for one stream. */
+qkv_pager *qkv_pager_create(int64_t n_pages, int32_t page_tokens, int32_t max_streams,
+                            int32_t max_pages_per_stream, uint32_t seed);
+void qkv_pager_destroy(qkv_pager *p);
+int qkv_pager_open(qkv_pager *p, int32_t *stream_id);
+int qkv_pager_close(qkv_pager *p, int32_t stream_id);
+/* Reserve room for `tokens` more tokens; *new_pages = pages added. */
+int qkv_pager_append(qkv_pager *p, int32_t stream_id, int32_t tokens, int32_t *new_pages);
+int qkv_pager_length(const qkv_pager *p, int32_t stream_id, int32_t *tokens);
+int qkv_pager_pages(const qkv_pager *p, int32_t stream_id, int32_t *pages_out, int32_t cap,
+                    int32_t *n);
+int64_t qkv_pager_free_pages(const qkv_pager *p);
+/* Plan a compaction: live pages above the live count move down into free
+ * slots.  Writes up to cap (src, dst) pairs and rewrites the page lists. */
+int qkv_pager_compact(qkv_pager *p, int32_t *src, int32_t *dst, int64_t cap, int64_t *n_moves);
+/* Consistency check (every page owned once, free list disjoint): 0 if sound. */
+int qkv_pager_check(const qkv_pager *p);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,571 @@
+// K2: paged GQA decode attention (one query token per row), HBM-bound, no
+// tensor cores.  Replaces text-decoder.cpp:435-463 (mul_mat over the full
+// cache view, soft_max_ext with a host mask, cont(transpose(V)) copy of all of
+// V every step, second mul_mat) and the scalar twin :1029-1075.
+//
+// Work split ("stream-K over pages"): all rows' pages are laid end to end
+// (prefix sums of ceil(len/16)); CTA c of G takes the page range
+// [c*T/G, (c+1)*T/G), so every CTA streams the same number of bytes whatever
+// the context-length mix.  A range may cover the tail of one row, several
+// whole rows and the head of another: each (CTA, row) piece is a segment.  A
+// row covered by one CTA writes its output directly; a row split over CTAs
+// c0..c1 writes unnormalised partials (O, m, l) to scratch slot row + c (that
+// index is unique per segment) and the last of its segments to finish (per kv
+// head, atomic counter) merges them.  Counters reset themselves.
+//
+// CTA = 8 consumer warps (warp g <-> kv head g, serving q heads 2g and 2g+1)
+// + 1 producer warp.  The producer streams each page chunk (all 8 heads, K and
+// V) into an NS-stage shared-memory ring with cp.async.bulk (no tensor map,
+// no multicast), completion on mbarriers.  Every wait is bounded.
+//
+// Consumer math per chunk of CH tokens (bf16/fp8: CH = 16 = one page, f32: 8):
+//   QK: lane = (quarter qt, dim group j): tokens qt*CH/4.., dims = 16 per lane
+//       in 16-byte chunks j, j+8, ... (conflict-free smem reads), partial dots
+//       reduce-scattered over the 8 lanes of the quarter.
+//   softmax: online (running max m, sum l) in the log2 domain (q pre-scaled
+//       by log2(e)/sqrt(D)); p exchanged through a per-warp smem row.
+//   PV: lane owns dims [4*lane, 4*lane+4) of both heads.
+#include "kernels.h"
+
+namespace qkv {
+
+namespace {
+
+template <typename TC> struct AttnTraits;
+template <> struct AttnTraits<__nv_bfloat16> { static constexpr int CH = 16, NS = 3; };
+template <> struct AttnTraits<float> { static constexpr int CH = 8, NS = 3; };
+template <> struct AttnTraits<uint8_t> { static constexpr int CH = 16, NS = 6; };
+
+constexpr int kConsumers = 8;
+constexpr int kThreads = (kConsumers + 1) * 32;
+
+template <typename TC> __host__ __device__ constexpr uint32_t stage_bytes() {
+    return 2u * kHkv * AttnTraits<TC>::CH * kHeadDim * sizeof(TC);
+}
+template <typename TC> __host__ __device__ constexpr size_t smem_bytes() {
+    return static_cast<size_t>(AttnTraits<TC>::NS) * stage_bytes<TC>()    // stages
+           + 2 * AttnTraits<TC>::NS * sizeof(uint64_t)                      // full/empty barriers
+           + AttnTraits<TC>::NS * 2 * kHkv * sizeof(float)                  // fp8 scales per stage
+           + kConsumers * 2 * AttnTraits<TC>::CH * sizeof(float)            // p exchange (16B aligned)
+           + (kAttnMaxRows + 1) * sizeof(int)                               // row page prefix
+           + 16 * sizeof(int);                                              // scan scratch + abort flag
+}
+
+// Load 16 bytes of cache elements as floats.
+template <typename TC> struct Chunk16;
+template <> struct Chunk16<__nv_bfloat16> {
+    static constexpr int E = 8;
+    static __device__ __forceinline__ void load(const __nv_bfloat16 *p, float (&o)[8]) {
+        const uint4 w = *reinterpret_cast<const uint4 *>(p);
+        o[0] = bf16lo(w.x); o[1] = bf16hi(w.x); o[2] = bf16lo(w.y); o[3] = bf16hi(w.y);
+        o[4] = bf16lo(w.z); o[5] = bf16hi(w.z); o[6] = bf16lo(w.w); o[7] = bf16hi(w.w);
+    }
+};
+template <> struct Chunk16<float> {
+    static constexpr int E = 4;
+    static __device__ __forceinline__ void load(const float *p, float (&o)[4]) {
+        const float4 w = *reinterpret_cast<const float4 *>(p);
+        o[0] = w.x; o[1] = w.y; o[2] = w.z; o[3] = w.w;
+    }
+};
+template <> struct Chunk16<uint8_t> {
+    static constexpr int E = 16;
+    static __device__ __forceinline__ void load(const uint8_t *p, float (&o)[16]) {
+        const uint4 w = *reinterpret_cast<const uint4 *>(p);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 a = e4m3x2_to_f2(static_cast<uint16_t>(ws[k] & 0xffffu));
+            const float2 b = e4m3x2_to_f2(static_cast<uint16_t>(ws[k] >> 16));
+            o[4 * k + 0] = a.x; o[4 * k + 1] = a.y; o[4 * k + 2] = b.x; o[4 * k + 3] = b.y;
+        }
+    }
+};
+
+// Four consecutive cache elements as floats (PV rows).
+template <typename TC> __device__ __forceinline__ float4 load4(const TC *p);
+template <> __device__ __forceinline__ float4 load4<float>(const float *p) {
+    return *reinterpret_cast<const float4 *>(p);
+}
+template <> __device__ __forceinline__ float4 load4<__nv_bfloat16>(const __nv_bfloat16 *p) {
+    const uint2 w = *reinterpret_cast<const uint2 *>(p);
+    return make_float4(bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y));
+}
+template <> __device__ __forceinline__ float4 load4<uint8_t>(const uint8_t *p) {
+    const uint32_t w = *reinterpret_cast<const uint32_t *>(p);
+    const float2 a = e4m3x2_to_f2(static_cast<uint16_t>(w & 0xffffu));
+    const float2 b = e4m3x2_to_f2(static_cast<uint16_t>(w >> 16));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+
+template <typename TOut> __device__ __forceinline__ void store4(TOut *p, float4 v);
+template <> __device__ __forceinline__ void store4<float>(float *p, float4 v) {
+    *reinterpret_cast<float4 *>(p) = v;
+}
+template <> __device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16 *p, float4 v) {
+    *reinterpret_cast<uint2 *>(p) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+}
+
+// Reduce-scatter NV values over the 8 lanes of a quarter (offsets 4, 2, 1):
+// afterwards v[0] holds the full sum of value index k(j); leftover offsets
+// are all-reduced.
+template <int NV> __device__ __forceinline__ void reduce_scatter8(float (&v)[NV], int j) {
+    int o = 4;
+#pragma unroll
+    for (int cnt = NV; cnt > 1; cnt >>= 1, o >>= 1) {
+        const bool upper = (j & o) != 0;
+#pragma unroll
+        for (int i = 0; i < cnt / 2; ++i) {
+            const float send = upper ? v[i] : v[i + cnt / 2];
+            const float keep = upper ? v[i + cnt / 2] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+#pragma unroll
+    for (; o >= 1; o >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+}
+
+__device__ __forceinline__ int64_t cta_of_page(int64_t pg, int64_t total, int64_t G) {
+    return ((pg + 1) * G + total - 1) / total - 1;
+}
+
+// Bounded wait that also gives up when another role raised the abort flag.
+__device__ __forceinline__ bool stage_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*abort_flag) return false;
+        if (clock64() - t0 > kWaitLimitCycles) return false;
+    }
+    return true;
+}
+
+template <typename TC, typename TOut>
+__global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(AttendParams p) {
+    constexpr int CH = AttnTraits<TC>::CH;
+    constexpr int NS = AttnTraits<TC>::NS;
+    constexpr int CPP = kPageTokens / CH;          // chunks per page
+    constexpr int HALF = kHkv * CH * kHeadDim;      // elements of K (or V) in a stage
+    constexpr int TPQ = CH / 4;                     // tokens per quarter-warp
+    constexpr int NV = 2 * TPQ;                     // partial dots per lane
+    constexpr int E = Chunk16<TC>::E;               // elements per 16-byte chunk
+    constexpr int NC = 16 / E;                      // chunks per lane per row (16 dims)
+    constexpr int KSHIFT = (NV == 8) ? 0 : 1;       // value index k = j >> KSHIFT
+    constexpr int HB = (NV == 8) ? 1 : 2;           // lane bit that selects the head
+    constexpr bool kFp8 = sizeof(TC) == 1;
+
+    extern __shared__ __align__(128) uint8_t smem[];
+    TC *stages = reinterpret_cast<TC *>(smem);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + static_cast<size_t>(NS) * stage_bytes<TC>());
+    uint64_t *empty = full + NS;
+    float *sscale = reinterpret_cast<float *>(empty + NS);
+    float *pbuf = sscale + NS * 2 * kHkv;                                  // [kConsumers][2*CH]
+    int *row_start = reinterpret_cast<int *>(pbuf + kConsumers * 2 * CH);  // [kAttnMaxRows + 1]
+    int *scan = row_start + kAttnMaxRows + 1;       // [0..9] warp totals, [12] abort flag
+    volatile int *abort_flag = scan + 12;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n = p.n;
+
+    // ---- row page prefix sums (each thread owns 4 consecutive rows) ----
+    int cnt[4];
+    int local = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int r = tid * 4 + k;
+        int pg = 0;
+        if (r < n) {
+            const int len = p.lens[r];
+            pg = (len + kPageTokens - 1) / kPageTokens;
+            if (len < 1 || pg > p.maxp) {
+                report_error(p.err, kErrRowBounds, kWhereAttend, r, len);
+                pg = 0;
+            }
+        }
+        cnt[k] = pg;
+        local += pg;
+    }
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) scan[warp] = incl;
+    if (tid == 0) {
+        *abort_flag = 0;
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumers);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    int warp_off = 0;
+    for (int w = 0; w < warp; ++w) warp_off += scan[w];
+    int excl = warp_off + incl - local;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int r = tid * 4 + k;
+        if (r < n) row_start[r] = excl;
+        excl += cnt[k];
+    }
+    if (tid == kThreads - 1) row_start[n] = warp_off + incl;
+    __syncthreads();
+
+    const int64_t T = row_start[n];
+    const int64_t G = gridDim.x;
+    const int64_t c = blockIdx.x;
+    const int64_t pb = c * T / G, pe = (c + 1) * T / G;
+    if (pb >= pe) return;   // no pages for this CTA (nothing armed yet)
+    int r0 = 0;
+    {
+        int lo = 0, hi = n - 1;
+        while (lo < hi) {   // largest r with row_start[r] <= pb
+            const int mid = (lo + hi + 1) >> 1;
+            if (row_start[mid] <= pb) lo = mid; else hi = mid - 1;
+        }
+        r0 = lo;
+    }
+
+    if (warp == kConsumers) {
+        // ================= producer warp =================
+        const uint64_t pol = l2_evict_first_policy();
+        const TC *pool = static_cast<const TC *>(p.pool);
+        int iter = 0;
+        bool abort = false;
+        int r = r0;
+        int64_t gp = pb;
+        while (gp < pe && !abort) {
+            while (row_start[r + 1] <= gp) ++r;
+            const int rs = row_start[r];
+            const int j0 = static_cast<int>(gp - rs);
+            const int j1 = static_cast<int>((pe < row_start[r + 1] ? pe : row_start[r + 1]) - rs);
+            const int slot = p.slots[r];
+            if (slot < 0 || slot >= p.max_streams) {
+                if (lane == 0) report_error(p.err, kErrRowBounds, kWhereAttend, r, slot);
+                abort = true;
+                break;
+            }
+            for (int jb = j0; jb < j1 && !abort; jb += 32) {
+                const int jj = jb + lane;
+                int pid = 0;
+                bool bad = false;
+                if (jj < j1) {
+                    pid = p.page_table[static_cast<size_t>(slot) * p.maxp + jj];
+                    bad = pid < 0 || pid >= p.n_pages;
+                }
+                if (__any_sync(0xffffffffu, bad)) {
+                    if (bad) report_error(p.err, kErrPageIndex, kWhereAttend, r, pid);
+                    abort = true;
+                    break;
+                }
+                const int cntp = (j1 - jb) < 32 ? (j1 - jb) : 32;
+                for (int k = 0; k < cntp && !abort; ++k) {
+                    const int page = __shfl_sync(0xffffffffu, pid, k);
+#pragma unroll 1
+                    for (int cp = 0; cp < CPP; ++cp) {
+                        const int s = iter % NS;
+                        const uint32_t ph = static_cast<uint32_t>(iter / NS) & 1u;
+                        int ok = 1;
+                        if (lane == 0) {
+                            if (!stage_wait(&empty[s], ph ^ 1u, abort_flag)) {
+                                ok = 0;
+                            } else {
+                                TC *dst = stages + static_cast<size_t>(s) * (2 * HALF);
+                                const size_t kbase = (static_cast<size_t>(page) * 2) * kPageHalfElems;
+                                const size_t vbase = kbase + kPageHalfElems;
+                                if constexpr (CH == kPageTokens) {
+                                    constexpr uint32_t half_bytes = HALF * sizeof(TC);
+                                    mbar_arrive_expect_tx(&full[s], 2 * half_bytes + (kFp8 ? 64u : 0u));
+                                    bulk_g2s(dst, pool + kbase, half_bytes, &full[s], pol);
+                                    bulk_g2s(dst + HALF, pool + vbase, half_bytes, &full[s], pol);
+                                    if constexpr (kFp8) {
+                                        bulk_g2s(sscale + s * 2 * kHkv, p.scales + static_cast<size_t>(page) * 2 * kHkv,
+                                                 64u, &full[s], pol);
+                                    }
+                                } else {
+                                    constexpr uint32_t rows_bytes = CH * kHeadDim * sizeof(TC);
+                                    mbar_arrive_expect_tx(&full[s], 2 * kHkv * rows_bytes);
+#pragma unroll 1
+                                    for (int g = 0; g < kHkv; ++g) {
+                                        const size_t off = static_cast<size_t>(g) * kPageTokens * kHeadDim +
+                                                           static_cast<size_t>(cp) * CH * kHeadDim;
+                                        bulk_g2s(dst + g * CH * kHeadDim, pool + kbase + off, rows_bytes, &full[s], pol);
+                                        bulk_g2s(dst + HALF + g * CH * kHeadDim, pool + vbase + off, rows_bytes, &full[s], pol);
+                                    }
+                                }
+                            }
+                        }
+                        ok = __shfl_sync(0xffffffffu, ok, 0);
+                        if (!ok) {
+                            if (lane == 0) {
+                                report_error(p.err, kErrWaitTimeout, kWhereAttend, static_cast<int>(c), iter);
+                                *abort_flag = 1;
+                            }
+                            abort = true;
+                            break;
+                        }
+                        ++iter;
+                    }
+                }
+            }
+            gp = rs + j1;
+        }
+        if (abort && lane == 0) *abort_flag = 1;
+        // Drain: every copy this warp issued has landed before the CTA can exit.
+        if (lane == 0) {
+            const int first = iter > NS ? iter - NS : 0;
+            for (int it = first; it < iter; ++it) {
+                if (!mbar_wait(&full[it % NS], static_cast<uint32_t>(it / NS) & 1u, kWaitLimitCycles)) {
+                    report_error(p.err, kErrWaitTimeout, kWhereAttend, static_cast<int>(c), -it);
+                    break;
+                }
+            }
+        }
+        return;
+    }
+
+    // ================= consumer warps: warp g <-> kv head g =================
+    const int g = warp;
+    const int qt = lane >> 3, j = lane & 7;
+    const int k_idx = j >> KSHIFT;
+    const int my_head = k_idx & 1;                   // which of the two q heads this lane's score is
+    const int my_tok = qt * TPQ + (k_idx >> 1);      // token within the chunk
+    float *my_p = pbuf + warp * (2 * CH);
+    TOut *out = static_cast<TOut *>(p.out);
+
+    int iter = 0;
+    int r = r0;
+    int64_t gp = pb;
+    bool abort = false;
+    while (gp < pe && !abort) {
+        while (row_start[r + 1] <= gp) ++r;
+        const int rs = row_start[r];
+        const int re = row_start[r + 1];
+        const int j0 = static_cast<int>(gp - rs);
+        const int j1 = static_cast<int>((pe < re ? pe : re) - rs);
+        const int len = p.lens[r];
+
+        // q of heads 2g (a) and 2g+1 (b) for this lane's QK dims, pre-scaled.
+        float qa[NC * E], qb[NC * E];
+        {
+            const float *qrow = p.q + static_cast<size_t>(r) * kQDim + (2 * g) * kHeadDim;
+#pragma unroll
+            for (int cc = 0; cc < NC; ++cc) {
+#pragma unroll
+                for (int e = 0; e < E; e += 4) {
+                    const int d = (j + 8 * cc) * E + e;
+                    const float4 a = *reinterpret_cast<const float4 *>(qrow + d);
+                    const float4 b = *reinterpret_cast<const float4 *>(qrow + kHeadDim + d);
+                    qa[cc * E + e + 0] = a.x * p.scale_log2; qa[cc * E + e + 1] = a.y * p.scale_log2;
+                    qa[cc * E + e + 2] = a.z * p.scale_log2; qa[cc * E + e + 3] = a.w * p.scale_log2;
+                    qb[cc * E + e + 0] = b.x * p.scale_log2; qb[cc * E + e + 1] = b.y * p.scale_log2;
+                    qb[cc * E + e + 2] = b.z * p.scale_log2; qb[cc * E + e + 3] = b.w * p.scale_log2;
+                }
+            }
+        }
+        float m_run = -INFINITY, l_run = 0.0f;
+        float oa[4] = {0.f, 0.f, 0.f, 0.f}, ob[4] = {0.f, 0.f, 0.f, 0.f};
+
+        for (int jp = j0; jp < j1 && !abort; ++jp) {
+#pragma unroll 1
+            for (int cp = 0; cp < CPP; ++cp) {
+                const int s = iter % NS;
+                const uint32_t ph = static_cast<uint32_t>(iter / NS) & 1u;
+                if (!stage_wait(&full[s], ph, abort_flag)) {
+                    if (lane == 0) {
+                        report_error(p.err, kErrWaitTimeout, kWhereAttend, static_cast<int>(c), iter);
+                        *abort_flag = 1;
+                    }
+                    abort = true;
+                    break;
+                }
+                const int tok0 = jp * kPageTokens + cp * CH;
+                const int nvalid = len - tok0 < CH ? len - tok0 : CH;
+                if (nvalid > 0) {
+                    const TC *kst = stages + static_cast<size_t>(s) * (2 * HALF) + g * CH * kHeadDim;
+                    const TC *vst = kst + HALF;
+                    float sk = 1.0f, sv = 1.0f;
+                    if constexpr (kFp8) {
+                        sk = sscale[s * 2 * kHkv + g];
+                        sv = sscale[s * 2 * kHkv + kHkv + g];
+                    }
+                    // ---- QK ----
+                    float part[NV];
+#pragma unroll
+                    for (int t = 0; t < TPQ; ++t) {
+                        const TC *krow = kst + (qt * TPQ + t) * kHeadDim;
+                        float acc_a = 0.f, acc_b = 0.f;
+#pragma unroll
+                        for (int cc = 0; cc < NC; ++cc) {
+                            float kv[E];
+                            Chunk16<TC>::load(krow + (j + 8 * cc) * E, kv);
+#pragma unroll
+                            for (int e = 0; e < E; ++e) {
+                                acc_a = fmaf(qa[cc * E + e], kv[e], acc_a);
+                                acc_b = fmaf(qb[cc * E + e], kv[e], acc_b);
+                            }
+                        }
+                        part[2 * t + 0] = acc_a;
+                        part[2 * t + 1] = acc_b;
+                    }
+                    reduce_scatter8<NV>(part, j);
+                    float sc = part[0] * sk;
+                    if (my_tok >= nvalid) sc = -INFINITY;
+                    // ---- online softmax (per head, over the lanes of that head) ----
+                    float mx = sc;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        if (o != HB) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                    }
+                    const float m_new = fmaxf(m_run, mx);
+                    const float pv = exp2f(sc - m_new);
+                    const float alpha = exp2f(m_run - m_new);
+                    float ps = pv;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        if (o != HB && !(KSHIFT == 1 && o == 1)) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+                    }
+                    l_run = l_run * alpha + ps;
+                    m_run = m_new;
+                    my_p[my_head * CH + my_tok] = pv * sv;
+                    const float al_a = __shfl_sync(0xffffffffu, alpha, 0);
+                    const float al_b = __shfl_sync(0xffffffffu, alpha, HB);
+                    __syncwarp();
+                    // ---- PV ----
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        oa[e] *= al_a;
+                        ob[e] *= al_b;
+                    }
+#pragma unroll
+                    for (int t4 = 0; t4 < CH; t4 += 4) {
+                        const float4 pa4 = *reinterpret_cast<const float4 *>(my_p + t4);
+                        const float4 pb4 = *reinterpret_cast<const float4 *>(my_p + CH + t4);
+                        const float pa[4] = {pa4.x, pa4.y, pa4.z, pa4.w};
+                        const float pbv[4] = {pb4.x, pb4.y, pb4.z, pb4.w};
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int t = t4 + u;
+                            if (t < nvalid) {
+                                const float4 v = load4<TC>(vst + t * kHeadDim + 4 * lane);
+                                oa[0] = fmaf(pa[u], v.x, oa[0]); oa[1] = fmaf(pa[u], v.y, oa[1]);
+                                oa[2] = fmaf(pa[u], v.z, oa[2]); oa[3] = fmaf(pa[u], v.w, oa[3]);
+                                ob[0] = fmaf(pbv[u], v.x, ob[0]); ob[1] = fmaf(pbv[u], v.y, ob[1]);
+                                ob[2] = fmaf(pbv[u], v.z, ob[2]); ob[3] = fmaf(pbv[u], v.w, ob[3]);
+                            }
+                        }
+                    }
+                    __syncwarp();
+                }
+                if (lane == 0) mbar_arrive(&empty[s]);
+                ++iter;
+            }
+        }
+        if (abort) break;
+
+        // ---- segment end ----
+        const float m_a = __shfl_sync(0xffffffffu, m_run, 0), m_b = __shfl_sync(0xffffffffu, m_run, HB);
+        const float l_a = __shfl_sync(0xffffffffu, l_run, 0), l_b = __shfl_sync(0xffffffffu, l_run, HB);
+        const int64_t c0 = cta_of_page(rs, T, G);
+        const int64_t c1 = cta_of_page(re - 1, T, G);
+        TOut *orow = out + static_cast<size_t>(r) * kQDim + (2 * g) * kHeadDim + 4 * lane;
+        if (c0 == c1) {
+            const float ia = 1.0f / l_a, ib = 1.0f / l_b;
+            store4<TOut>(orow, make_float4(oa[0] * ia, oa[1] * ia, oa[2] * ia, oa[3] * ia));
+            store4<TOut>(orow + kHeadDim, make_float4(ob[0] * ib, ob[1] * ib, ob[2] * ib, ob[3] * ib));
+        } else {
+            const size_t slot_idx = static_cast<size_t>(r) + static_cast<size_t>(c);
+            float *po = p.part_o + (slot_idx * kHq + 2 * g) * kHeadDim + 4 * lane;
+            *reinterpret_cast<float4 *>(po) = make_float4(oa[0], oa[1], oa[2], oa[3]);
+            *reinterpret_cast<float4 *>(po + kHeadDim) = make_float4(ob[0], ob[1], ob[2], ob[3]);
+            if (lane == 0) {
+                float *pml = p.part_ml + (slot_idx * kHq + 2 * g) * 2;
+                pml[0] = m_a; pml[1] = l_a; pml[2] = m_b; pml[3] = l_b;
+            }
+            __threadfence();
+            __syncwarp();
+            int last = 0;
+            if (lane == 0) {
+                const int old = atomicAdd(&p.counters[r * kHkv + g], 1);
+                last = (old == static_cast<int>(c1 - c0));
+            }
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (last) {
+                __threadfence();
+                float M_a = -INFINITY, M_b = -INFINITY;
+                for (int64_t cc = c0; cc <= c1; ++cc) {
+                    const float *pml = p.part_ml + ((static_cast<size_t>(r) + cc) * kHq + 2 * g) * 2;
+                    M_a = fmaxf(M_a, __ldcg(pml + 0));
+                    M_b = fmaxf(M_b, __ldcg(pml + 2));
+                }
+                float4 A = make_float4(0.f, 0.f, 0.f, 0.f), B = A;
+                float La = 0.f, Lb = 0.f;
+                for (int64_t cc = c0; cc <= c1; ++cc) {
+                    const size_t si = static_cast<size_t>(r) + static_cast<size_t>(cc);
+                    const float *pml = p.part_ml + (si * kHq + 2 * g) * 2;
+                    const float wa = exp2f(__ldcg(pml + 0) - M_a), wb = exp2f(__ldcg(pml + 2) - M_b);
+                    La += wa * __ldcg(pml + 1);
+                    Lb += wb * __ldcg(pml + 3);
+                    const float *pp = p.part_o + (si * kHq + 2 * g) * kHeadDim + 4 * lane;
+                    const float4 x = __ldcg(reinterpret_cast<const float4 *>(pp));
+                    const float4 y = __ldcg(reinterpret_cast<const float4 *>(pp + kHeadDim));
+                    A.x += wa * x.x; A.y += wa * x.y; A.z += wa * x.z; A.w += wa * x.w;
+                    B.x += wb * y.x; B.y += wb * y.y; B.z += wb * y.z; B.w += wb * y.w;
+                }
+                const float ia = 1.0f / La, ib = 1.0f / Lb;
+                store4<TOut>(orow, make_float4(A.x * ia, A.y * ia, A.z * ia, A.w * ia));
+                store4<TOut>(orow + kHeadDim, make_float4(B.x * ib, B.y * ib, B.z * ib, B.w * ib));
+                if (lane == 0) p.counters[r * kHkv + g] = 0;
+            }
+        }
+        gp = rs + j1;
+    }
+}
+
+template <typename TC, typename TOut> cudaError_t prepare_t() {
+    return cudaFuncSetAttribute(decode_attn_kernel<TC, TOut>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(smem_bytes<TC>()));
+}
+
+template <typename TC, typename TOut> cudaError_t launch_t(const AttendParams &p, int grid, cudaStream_t st) {
+    decode_attn_kernel<TC, TOut><<<grid, kThreads, smem_bytes<TC>(), st>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+// Opt the kernels into > 48 KB of dynamic shared memory on the current device.
+cudaError_t prepare_decode_attn() {
+    cudaError_t e;
+    if ((e = prepare_t<float, float>()) != cudaSuccess) return e;
+    if ((e = prepare_t<float, __nv_bfloat16>()) != cudaSuccess) return e;
+    if ((e = prepare_t<__nv_bfloat16, float>()) != cudaSuccess) return e;
+    if ((e = prepare_t<__nv_bfloat16, __nv_bfloat16>()) != cudaSuccess) return e;
+    if ((e = prepare_t<uint8_t, float>()) != cudaSuccess) return e;
+    return prepare_t<uint8_t, __nv_bfloat16>();
+}
+
+size_t attn_smem_bytes(int kv_dtype) {
+    switch (kv_dtype) {
+        case kKvF32: return smem_bytes<float>();
+        case kKvBF16: return smem_bytes<__nv_bfloat16>();
+        case kKvFP8: return smem_bytes<uint8_t>();
+        default: return 0;
+    }
+}
+
+cudaError_t launch_decode_attn(const AttendParams &p, int kv_dtype, bool out_bf16, int grid, cudaStream_t st) {
+    if (p.n <= 0) return cudaSuccess;
+    if (p.n > kAttnMaxRows) return cudaErrorInvalidValue;
+    switch (kv_dtype) {
+        case kKvF32: return out_bf16 ? launch_t<float, __nv_bfloat16>(p, grid, st) : launch_t<float, float>(p, grid, st);
+        case kKvBF16:
+            return out_bf16 ? launch_t<__nv_bfloat16, __nv_bfloat16>(p, grid, st) : launch_t<__nv_bfloat16, float>(p, grid, st);
+        case kKvFP8: return out_bf16 ? launch_t<uint8_t, __nv_bfloat16>(p, grid, st) : launch_t<uint8_t, float>(p, grid, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace qkv

@@ -1,0 +1,328 @@
+// Dense per-token kernels of the decoder block around the KV-cache path:
+// RMSNorm (text-decoder.cpp:542-557), embedding-row gather (:2297 / :2167),
+// projections (:559-598, W[out][in] row-major), SwiGLU (:600, :794-797) and
+// the first-maximum argmax of the greedy loop (:2266-2274).
+#include "kernels.h"
+
+#include <cuda_fp16.h>
+
+namespace qkv {
+
+namespace {
+
+template <typename T> __device__ __forceinline__ void put(T *p, float v);
+template <> __device__ __forceinline__ void put<float>(float *p, float v) { *p = v; }
+template <> __device__ __forceinline__ void put<__nv_bfloat16>(__nv_bfloat16 *p, float v) { *p = __float2bfloat16_rn(v); }
+
+template <typename TOut>
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const int *rows, int hidden, const float *w,
+                                                      float eps, TOut *out) {
+    const int r = blockIdx.x;
+    const float *xr = x + static_cast<size_t>(rows ? rows[r] : r) * hidden;
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) ss += static_cast<double>(xr[i]) * xr[i];
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    __shared__ double part[8];
+    __shared__ float s_scale;
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) t += part[k];
+        const double ms = t / static_cast<double>(hidden);
+        s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(ms), eps)));
+    }
+    __syncthreads();
+    const float scale = s_scale;
+    TOut *o = out + static_cast<size_t>(r) * hidden;
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) put<TOut>(o + i, __fmul_rn(__fmul_rn(xr[i], scale), w[i]));
+}
+
+template <typename TW>
+__global__ void embed_kernel(const int *ids, const TW *embd, int hidden, int vocab, float *x, DevError *err) {
+    const int r = blockIdx.x;
+    const int id = ids[r];
+    if (id < 0 || id >= vocab) {
+        if (threadIdx.x == 0) report_error(err, kErrRowBounds, kWhereEmbed, r, id);
+        return;
+    }
+    const TW *src = embd + static_cast<size_t>(id) * hidden;
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+        if constexpr (sizeof(TW) == 4) x[static_cast<size_t>(r) * hidden + i] = src[i];
+        else x[static_cast<size_t>(r) * hidden + i] = __bfloat162float(src[i]);
+    }
+}
+
+// Four consecutive elements -> float4.
+template <typename T> __device__ __forceinline__ float4 ld4(const T *p);
+template <> __device__ __forceinline__ float4 ld4<float>(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+template <> __device__ __forceinline__ float4 ld4<__nv_bfloat16>(const __nv_bfloat16 *p) {
+    const uint2 w = *reinterpret_cast<const uint2 *>(p);
+    return make_float4(bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y));
+}
+
+// SIMT tiled GEMM: 64 (m) x 64 (n) tile, BK = 16, 256 threads, 4x4 per
+// thread, optional split-K over gridDim.z (atomic accumulate).
+constexpr int BM = 64, BN = 64, BK = 16, PAD = 4;
+
+template <typename TX, typename TW>
+__global__ void __launch_bounds__(256) gemm_simt_kernel(const TX *X, const TW *W, float *C, int M, int N, int K,
+                                                        int k_per_split, int atomic_out) {
+    __shared__ __align__(16) float As[BK][BM + PAD];
+    __shared__ __align__(16) float Bs[BK][BN + PAD];
+    const int tid = threadIdx.x;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int kb = blockIdx.z * k_per_split;
+    const int ke = min(K, kb + k_per_split);
+    const int lr = tid >> 2, lk = (tid & 3) * 4;   // loader: row within tile, k offset
+    const int tx = tid & 15, ty = tid >> 4;
+    float acc[4][4] = {};
+    const bool xm = (m0 + lr) < M, wn = (n0 + lr) < N;
+    const TX *xp = X + static_cast<size_t>(m0 + lr) * K + lk;
+    const TW *wp = W + static_cast<size_t>(n0 + lr) * K + lk;
+    float4 xa = make_float4(0.f, 0.f, 0.f, 0.f), wa = xa;
+    if (kb < ke) {
+        if (xm) xa = ld4<TX>(xp + kb);
+        if (wn) wa = ld4<TW>(wp + kb);
+    }
+    for (int k0 = kb; k0 < ke; k0 += BK) {
+        As[lk + 0][lr] = xa.x; As[lk + 1][lr] = xa.y; As[lk + 2][lr] = xa.z; As[lk + 3][lr] = xa.w;
+        Bs[lk + 0][lr] = wa.x; Bs[lk + 1][lr] = wa.y; Bs[lk + 2][lr] = wa.z; Bs[lk + 3][lr] = wa.w;
+        __syncthreads();
+        if (k0 + BK < ke) {
+            if (xm) xa = ld4<TX>(xp + k0 + BK);
+            if (wn) wa = ld4<TW>(wp + k0 + BK);
+        }
+#pragma unroll
+        for (int k = 0; k < BK; ++k) {
+            const float4 a = *reinterpret_cast<const float4 *>(&As[k][ty * 4]);
+            const float4 b = *reinterpret_cast<const float4 *>(&Bs[k][tx * 4]);
+            const float av[4] = {a.x, a.y, a.z, a.w};
+            const float bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int jn = 0; jn < 4; ++jn) acc[i][jn] = fmaf(av[i], bv[jn], acc[i][jn]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int m = m0 + ty * 4 + i;
+        if (m >= M) continue;
+#pragma unroll
+        for (int jn = 0; jn < 4; ++jn) {
+            const int n = n0 + tx * 4 + jn;
+            if (n >= N) continue;
+            float *c = C + static_cast<size_t>(m) * N + n;
+            if (atomic_out) atomicAdd(c, acc[i][jn]);
+            else *c = acc[i][jn];
+        }
+    }
+}
+
+// Small-M path (M <= 4): one warp per output column n, lanes stride over K,
+// X rows staged in shared memory as f32.
+template <typename TX, typename TW, int MM>
+__global__ void __launch_bounds__(256) gemv_kernel(const TX *X, const TW *W, float *C, int M, int N, int K,
+                                                   int accumulate) {
+    extern __shared__ __align__(16) float xs[];   // [MM][K]
+    for (int e = threadIdx.x * 4; e < M * K; e += blockDim.x * 4) {
+        const float4 v = ld4<TX>(X + e);
+        *reinterpret_cast<float4 *>(xs + e) = v;
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = blockIdx.x * 8 + warp;
+    if (n >= N) return;
+    const TW *w = W + static_cast<size_t>(n) * K;
+    float acc[MM] = {};
+    for (int k = lane * 4; k < K; k += 128) {
+        const float4 wv = ld4<TW>(w + k);
+#pragma unroll
+        for (int m = 0; m < MM; ++m) {
+            if (m < M) {
+                const float4 xv = *reinterpret_cast<const float4 *>(xs + m * K + k);
+                acc[m] = fmaf(wv.x, xv.x, acc[m]);
+                acc[m] = fmaf(wv.y, xv.y, acc[m]);
+                acc[m] = fmaf(wv.z, xv.z, acc[m]);
+                acc[m] = fmaf(wv.w, xv.w, acc[m]);
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < MM; ++m) {
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int m = 0; m < MM; ++m) {
+            if (m < M) {
+                float *c = C + static_cast<size_t>(m) * N + n;
+                *c = accumulate ? *c + acc[m] : acc[m];
+            }
+        }
+    }
+}
+
+template <typename TOut>
+__global__ void swiglu_kernel(const float *gu, int M, int F, TOut *out) {
+    const size_t total = static_cast<size_t>(M) * F;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const size_t m = i / F, jf = i % F;
+        const float g = gu[m * 2 * F + jf];
+        const float u = gu[m * 2 * F + F + jf];
+        const float s = g / (1.0f + expf(-g));
+        put<TOut>(out + i, s * u);
+    }
+}
+
+// Block per row; ties keep the smaller index (strict '>' scan from 0); NaN never wins.
+__global__ void __launch_bounds__(1024) argmax_kernel(const float *logits, int V, int *ids) {
+    const float *row = logits + static_cast<size_t>(blockIdx.x) * V;
+    float best = -INFINITY;
+    int idx = -1;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const float v = row[i];
+        if (v > best) { best = v; idx = i; }
+    }
+    __shared__ float sb[32];
+    __shared__ int si[32];
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ob > best || (ob == best && oi >= 0 && (idx < 0 || oi < idx))) { best = ob; idx = oi; }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) { sb[warp] = best; si[warp] = idx; }
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = blockDim.x >> 5;
+        best = lane < nw ? sb[lane] : -INFINITY;
+        idx = lane < nw ? si[lane] : -1;
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+            if (ob > best || (ob == best && oi >= 0 && (idx < 0 || oi < idx))) { best = ob; idx = oi; }
+        }
+        if (lane == 0) ids[blockIdx.x] = idx;
+    }
+}
+
+// GGUF tensor bytes (f32 / f16 / bf16) -> device weight dtype (f32 / bf16, RNE).
+template <typename TD>
+__global__ void convert_kernel(const void *src, int src_type, TD *dst, size_t n) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        float v;
+        if (src_type == 0) v = static_cast<const float *>(src)[i];
+        else if (src_type == 1) v = __half2float(static_cast<const __half *>(src)[i]);
+        else v = __bfloat162float(static_cast<const __nv_bfloat16 *>(src)[i]);
+        put<TD>(dst + i, v);
+    }
+}
+
+int g_num_sms = 148;
+
+}  // namespace
+
+cudaError_t launch_convert(const void *src, int src_ggml_type, void *dst, int dst_dtype, size_t n, cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    const int blocks = static_cast<int>((n + 255) / 256 < 8192 ? (n + 255) / 256 : 8192);
+    if (dst_dtype == kActF32) convert_kernel<float><<<blocks, 256, 0, st>>>(src, src_ggml_type, static_cast<float *>(dst), n);
+    else convert_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(src, src_ggml_type, static_cast<__nv_bfloat16 *>(dst), n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm(const float *x, const int *rows, int n, int hidden, const float *w, float eps, void *out,
+                           int out_dtype, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    if (out_dtype == kActF32) rmsnorm_kernel<float><<<n, 256, 0, st>>>(x, rows, hidden, w, eps, static_cast<float *>(out));
+    else rmsnorm_kernel<__nv_bfloat16><<<n, 256, 0, st>>>(x, rows, hidden, w, eps, static_cast<__nv_bfloat16 *>(out));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_embed(const int *ids, int n, const void *embd, int w_dtype, int hidden, int vocab, float *x,
+                         DevError *err, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    if (w_dtype == kActF32) embed_kernel<float><<<n, 256, 0, st>>>(ids, static_cast<const float *>(embd), hidden, vocab, x, err);
+    else embed_kernel<__nv_bfloat16><<<n, 256, 0, st>>>(ids, static_cast<const __nv_bfloat16 *>(embd), hidden, vocab, x, err);
+    return cudaGetLastError();
+}
+
+template <typename TX, typename TW>
+static cudaError_t gemm_t(const TX *X, const TW *W, float *C, int M, int N, int K, int epilogue, cudaStream_t st) {
+    if (M <= 4) {
+        const size_t sm = static_cast<size_t>(M) * K * sizeof(float);
+        static_assert(sizeof(float) == 4, "");
+        if (sm > 48 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(gemv_kernel<TX, TW, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(sm));
+            if (e != cudaSuccess) return e;
+        }
+        gemv_kernel<TX, TW, 4><<<(N + 7) / 8, 256, sm, st>>>(X, W, C, M, N, K, epilogue);
+        return cudaGetLastError();
+    }
+    const int tm = (M + BM - 1) / BM, tn = (N + BN - 1) / BN;
+    int splits = 1;
+    const int want = 2 * g_num_sms;
+    if (tm * tn < want) {
+        splits = (want + tm * tn - 1) / (tm * tn);
+        const int max_splits = K / 256 > 0 ? K / 256 : 1;
+        if (splits > max_splits) splits = max_splits;
+    }
+    int kps = (K + splits - 1) / splits;
+    kps = (kps + BK - 1) / BK * BK;
+    splits = (K + kps - 1) / kps;
+    const bool atomic = splits > 1 || epilogue == 1;
+    if (splits > 1 && epilogue == 0) {
+        cudaError_t e = cudaMemsetAsync(C, 0, static_cast<size_t>(M) * N * sizeof(float), st);
+        if (e != cudaSuccess) return e;
+    }
+    dim3 grid(tn, tm, splits);
+    gemm_simt_kernel<TX, TW><<<grid, 256, 0, st>>>(X, W, C, M, N, K, kps, atomic ? 1 : 0);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gemm(const void *X, int x_dtype, const void *W, int w_dtype, float *C, int M, int N, int K,
+                        int epilogue, cudaStream_t st) {
+    if (M <= 0 || N <= 0) return cudaSuccess;
+    if (K % BK != 0) return cudaErrorInvalidValue;
+    static bool sm_known = false;
+    if (!sm_known) {
+        int dev = 0, sms = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess &&
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms > 0)
+            g_num_sms = sms;
+        sm_known = true;
+    }
+    if (x_dtype == kActF32 && w_dtype == kActF32)
+        return gemm_t(static_cast<const float *>(X), static_cast<const float *>(W), C, M, N, K, epilogue, st);
+    if (x_dtype == kActBF16 && w_dtype == kActBF16)
+        return gemm_t(static_cast<const __nv_bfloat16 *>(X), static_cast<const __nv_bfloat16 *>(W), C, M, N, K, epilogue, st);
+    if (x_dtype == kActF32 && w_dtype == kActBF16)
+        return gemm_t(static_cast<const float *>(X), static_cast<const __nv_bfloat16 *>(W), C, M, N, K, epilogue, st);
+    return gemm_t(static_cast<const __nv_bfloat16 *>(X), static_cast<const float *>(W), C, M, N, K, epilogue, st);
+}
+
+cudaError_t launch_swiglu(const float *gu, int M, int F, void *out, int out_dtype, cudaStream_t st) {
+    if (M <= 0) return cudaSuccess;
+    const size_t total = static_cast<size_t>(M) * F;
+    const int blocks = static_cast<int>((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+    if (out_dtype == kActF32) swiglu_kernel<float><<<blocks, 256, 0, st>>>(gu, M, F, static_cast<float *>(out));
+    else swiglu_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(gu, M, F, static_cast<__nv_bfloat16 *>(out));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_argmax(const float *logits, int M, int V, int *ids, cudaStream_t st) {
+    if (M <= 0) return cudaSuccess;
+    argmax_kernel<<<M, 1024, 0, st>>>(logits, V, ids);
+    return cudaGetLastError();
+}
+
+}  // namespace qkv

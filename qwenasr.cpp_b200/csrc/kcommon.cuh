@@ -1,0 +1,139 @@
+// Device helpers shared by the sm_100a kernels: model constants, element
+// conversions, the device error word, and thin inline-PTX wrappers for
+// mbarriers and the bulk (non-tensor) async copy engine.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace qkv {
+
+// Qwen3 text-decoder attention geometry served by these kernels.
+constexpr int kHeadDim = 128;   // head_dim
+constexpr int kHq = 16;         // query heads
+constexpr int kHkv = 8;         // kv heads (GQA 2:1)
+constexpr int kPageTokens = 16; // tokens per KV page
+constexpr int kQkvDim = (kHq + 2 * kHkv) * kHeadDim;   // 4096
+constexpr int kQDim = kHq * kHeadDim;                   // 2048
+constexpr int kKvDim = kHkv * kHeadDim;                 // 1024
+// Elements of one (page, K|V) block: [kHkv][kPageTokens][kHeadDim].
+constexpr int kPageHalfElems = kHkv * kPageTokens * kHeadDim;   // 16384
+
+// Device error word: first error wins.  The host reads it after a sync.
+struct DevError {
+    int code;    // 0 = none
+    int where;   // kernel id
+    int a, b;    // detail (index, value)
+};
+enum DevErrCode { kErrPageIndex = 1, kErrWaitTimeout = 2, kErrPosition = 3, kErrRowBounds = 4 };
+enum DevErrWhere { kWhereAppend = 1, kWhereAttend = 2, kWherePrefillAttn = 3, kWhereGather = 4,
+                   kWhereEmbed = 5, kWhereGemm = 6 };
+
+__device__ __forceinline__ void report_error(DevError *e, int code, int where, int a, int b) {
+    if (e && atomicCAS(&e->code, 0, code) == 0) {
+        e->where = where;
+        e->a = a;
+        e->b = b;
+    }
+}
+
+// ---- element conversions ----
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+    static __device__ __forceinline__ float load(const float *p) { return *p; }
+    static __device__ __forceinline__ float to_f(float v) { return v; }
+    static __device__ __forceinline__ float from_f(float v) { return v; }
+};
+template <> struct Elem<__nv_bfloat16> {
+    static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+    static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+// Two e4m3 bytes (low byte first) -> two floats.
+__device__ __forceinline__ float2 e4m3x2_to_f2(uint16_t v) {
+    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(v), __NV_E4M3);
+    const __half2 hh = *reinterpret_cast<const __half2 *>(&h);
+    return __half22float2(hh);
+}
+__device__ __forceinline__ uint8_t f_to_e4m3(float v) {
+    return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+}
+constexpr float kE4m3Max = 448.0f;
+
+// ---- shared-memory address + mbarrier + bulk copy (inline PTX) ----
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for the phase of `parity` to complete, for at most `limit` SM cycles.
+// Returns false when the limit ran out (the caller records an error and stops).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, long long limit) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > limit) return false;
+    }
+    return true;
+}
+
+// Global -> shared bulk copy completing on `bar` (bytes: multiple of 16,
+// both addresses 16-byte aligned).  No multicast.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                         uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+// L2 policy: KV pages are streamed once per step -> evict first.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// Cycle budget for any single wait before it is treated as a hang (~2 s at 1.9 GHz).
+constexpr long long kWaitLimitCycles = 4000000000ll;
+
+}  // namespace qkv

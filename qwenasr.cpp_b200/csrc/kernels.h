@@ -1,0 +1,104 @@
+// Kernel parameter blocks and host launch wrappers of the sm_100a kernels.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include "kcommon.cuh"
+
+namespace qkv {
+
+enum KvDtype { kKvF32 = 0, kKvBF16 = 1, kKvFP8 = 2 };
+enum ActDtype { kActF32 = 0, kActBF16 = 1 };
+
+constexpr int kAttnMaxRows = 1024;   // rows (streams) per decode-attention launch
+
+// Pool layout of one layer: [n_pages][2 (K,V)][kHkv][kPageTokens][kHeadDim]
+// elements of the cache dtype; FP8 scales: [n_pages][2][kHkv] f32.
+struct AppendParams {
+    int n;                     // rows
+    const int *slots;          // [n] stream ids (page-table rows)
+    const int *positions;      // [n] token position of each row
+    const float *qkv;          // [n][kQkvDim] raw projections
+    float *q_out;              // [n][kQDim]
+    const float *q_norm_w;     // [kHeadDim]
+    const float *k_norm_w;     // [kHeadDim]
+    const float2 *rope;        // [rope_len][kHeadDim/2] (cos, sin)
+    int rope_len;
+    void *pool;                // this layer's pool
+    float *scales;             // this layer's FP8 scales (or null)
+    const int *page_table;     // [max_streams][maxp]
+    int maxp;
+    int max_streams;
+    int n_pages;
+    float eps;
+    int mode;                  // 0 all rows, 1 page-opening rows only, 2 the others
+    DevError *err;
+};
+
+struct AttendParams {
+    int n;                     // rows (<= kAttnMaxRows)
+    const int *slots;          // [n]
+    const int *lens;           // [n] tokens to attend over (including the new one)
+    const float *q;            // [n][kQDim] post-RoPE queries
+    void *out;                 // [n][kQDim] f32 or bf16
+    const void *pool;          // this layer's pool
+    const float *scales;       // this layer's FP8 scales (or null)
+    const int *page_table;
+    int maxp;
+    int max_streams;
+    int n_pages;
+    float *part_o;             // [n + grid][kHq][kHeadDim] scratch
+    float *part_ml;            // [n + grid][kHq][2] scratch
+    int *counters;             // [n][kHkv], zero between launches
+    float scale_log2;          // log2(e) / sqrt(head_dim)
+    DevError *err;
+};
+
+struct PrefillAttnParams {
+    int n;                     // query rows
+    const int *slots;          // [n]
+    const int *positions;      // [n] query position; keys are [0, position]
+    const float *q;            // [n][kQDim]
+    void *out;                 // [n][kQDim] f32 or bf16
+    const void *pool;
+    const float *scales;
+    const int *page_table;
+    int maxp;
+    int max_streams;
+    int n_pages;
+    float scale_log2;
+    DevError *err;
+};
+
+cudaError_t launch_kv_append(const AppendParams &p, int kv_dtype, cudaStream_t st);
+cudaError_t prepare_decode_attn();
+size_t attn_smem_bytes(int kv_dtype);
+cudaError_t launch_decode_attn(const AttendParams &p, int kv_dtype, bool out_bf16, int grid, cudaStream_t st);
+cudaError_t launch_prefill_attn(const PrefillAttnParams &p, int kv_dtype, bool out_bf16, cudaStream_t st);
+cudaError_t launch_page_gather(const void *pool, int kv_dtype, const int *pages, int n_pages_row, int len,
+                               int n_pages, void *k_out, void *v_out, DevError *err, cudaStream_t st);
+cudaError_t launch_page_copy(void *pool_layer, size_t page_bytes, const int *src, const int *dst, int n,
+                             cudaStream_t st);
+cudaError_t launch_page_fill(void *pool_layer, float *scales_layer, int kv_dtype, const int *pages, int n,
+                             uint64_t seed, cudaStream_t st);
+
+// ---- dense kernels ----
+// out[r] = rmsnorm(x[rows? rows[r] : r]) * w   (double mean square, as text-decoder.cpp:542-557)
+cudaError_t launch_rmsnorm(const float *x, const int *rows, int n, int hidden, const float *w, float eps,
+                           void *out, int out_dtype, cudaStream_t st);
+// x[r] = embd[ids[r]] as f32
+cudaError_t launch_embed(const int *ids, int n, const void *embd, int w_dtype, int hidden, int vocab, float *x,
+                         DevError *err, cudaStream_t st);
+// C[m][n] (+)= sum_k X[m][k] * W[n][k];  X: act dtype, W: weight dtype, C f32.
+// epilogue 0: store, 1: accumulate into C (residual add).
+cudaError_t launch_gemm(const void *X, int x_dtype, const void *W, int w_dtype, float *C, int M, int N, int K,
+                        int epilogue, cudaStream_t st);
+// out[m][j] = silu(gu[m][j]) * gu[m][F + j]
+cudaError_t launch_swiglu(const float *gu, int M, int F, void *out, int out_dtype, cudaStream_t st);
+// GGUF tensor data (ggml type 0 f32, 1 f16, 30 bf16 passed as 2) -> weight dtype.
+cudaError_t launch_convert(const void *src, int src_ggml_type, void *dst, int dst_dtype, size_t n, cudaStream_t st);
+// ids[m] = first index of the maximum of logits[m][0..V)
+cudaError_t launch_argmax(const float *logits, int M, int V, int *ids, cudaStream_t st);
+
+}  // namespace qkv

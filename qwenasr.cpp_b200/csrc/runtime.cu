@@ -1,0 +1,1052 @@
+// C ABI implementation: handle creation (weights, pool, scratch), the stream
+// table, and the prefill / decode / operator-level entry points.
+#include "runtime.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+
+#include "gguf.h"
+
+using qkv::DevError;
+
+namespace qkv {
+
+int fail(qkv_handle *h, int code, const std::string &msg) {
+    if (h) h->last_error = msg;
+    return code;
+}
+
+int cuda_fail(qkv_handle *h, cudaError_t e, const char *what) {
+    return fail(h, QKV_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+}  // namespace qkv
+
+#define CK(call)                                                  \
+    do {                                                          \
+        cudaError_t e_ = (call);                                  \
+        if (e_ != cudaSuccess) return qkv::cuda_fail(h, e_, #call); \
+    } while (0)
+
+namespace {
+
+using namespace qkv;
+
+void set_err(char *err, size_t len, const std::string &msg) {
+    if (err && len > 0) {
+        std::strncpy(err, msg.c_str(), len - 1);
+        err[len - 1] = '\0';
+    }
+}
+
+size_t kv_elem_bytes(int kv_dtype) { return kv_dtype == kKvF32 ? 4 : kv_dtype == kKvBF16 ? 2 : 1; }
+
+int validate_model(const qkv_model_config &c, std::string *e) {
+    if (c.n_layers <= 0 || c.hidden <= 0 || c.intermediate <= 0 || c.vocab <= 0) {
+        *e = "model config: non-positive dimension";
+        return QKV_ERR_INVALID_ARG;
+    }
+    if (c.head_dim != kHeadDim || c.n_heads != kHq || c.n_kv_heads != kHkv) {
+        *e = "model config: kernels serve head_dim 128 with 16 q heads and 8 kv heads (got " +
+             std::to_string(c.head_dim) + "/" + std::to_string(c.n_heads) + "/" + std::to_string(c.n_kv_heads) + ")";
+        return QKV_ERR_INVALID_ARG;
+    }
+    if (c.hidden % 16 != 0 || c.intermediate % 16 != 0) {
+        *e = "model config: hidden and intermediate must be multiples of 16";
+        return QKV_ERR_INVALID_ARG;
+    }
+    if (!(c.rope_theta > 0.0f) || !(c.rms_norm_eps >= 0.0f)) {
+        *e = "model config: bad rope_theta or rms_norm_eps";
+        return QKV_ERR_INVALID_ARG;
+    }
+    return QKV_OK;
+}
+
+int validate_rt(const qkv_runtime_config &r, std::string *e) {
+    if (r.page_tokens != kPageTokens) {
+        *e = "runtime config: page_tokens must be 16";
+        return QKV_ERR_INVALID_ARG;
+    }
+    if (r.kv_dtype < QKV_F32 || r.kv_dtype > QKV_FP8_E4M3 || (r.weight_dtype != QKV_F32 && r.weight_dtype != QKV_BF16)) {
+        *e = "runtime config: bad dtype";
+        return QKV_ERR_INVALID_ARG;
+    }
+    if (r.max_streams <= 0 || r.max_context <= 0 || r.max_pages < 0 || r.max_batch_tokens < 0) {
+        *e = "runtime config: bad capacity";
+        return QKV_ERR_INVALID_ARG;
+    }
+    return QKV_OK;
+}
+
+// Device, stream, pool, page table, RoPE table, pager, per-step scratch.
+int setup_common(qkv_handle *h, bool with_model_scratch) {
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev <= 0) return fail(h, QKV_ERR_NO_DEVICE, "no CUDA device");
+    if (h->rt.device < 0 || h->rt.device >= ndev) return fail(h, QKV_ERR_NO_DEVICE, "device ordinal out of range");
+    h->device = h->rt.device;
+    CK(cudaSetDevice(h->device));
+    cudaDeviceProp prop{};
+    CK(cudaGetDeviceProperties(&prop, h->device));
+    if (prop.major != 10) {
+        return fail(h, QKV_ERR_NO_DEVICE, std::string("kernels are built for sm_100a; device is ") + prop.name);
+    }
+    h->num_sms = prop.multiProcessorCount;
+    CK(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
+
+    const qkv_model_config &c = h->cfg;
+    h->maxp = (h->rt.max_context + kPageTokens - 1) / kPageTokens;
+    const int64_t pages = h->rt.max_pages > 0 ? h->rt.max_pages : static_cast<int64_t>(h->rt.max_streams) * h->maxp;
+    if (pages > (int64_t{1} << 30)) return fail(h, QKV_ERR_INVALID_ARG, "max_pages too large");
+    h->n_pages = static_cast<int>(pages);
+    h->page_bytes = static_cast<size_t>(2) * kPageHalfElems * kv_elem_bytes(h->rt.kv_dtype);
+    h->pool_layer_bytes = h->page_bytes * static_cast<size_t>(h->n_pages);
+    CK(cudaMalloc(&h->pool, h->pool_layer_bytes * c.n_layers));
+    CK(cudaMemsetAsync(h->pool, 0, h->pool_layer_bytes * c.n_layers, h->stream));
+    if (h->rt.kv_dtype == kKvFP8) {
+        h->scales_layer_elems = static_cast<size_t>(h->n_pages) * 2 * kHkv;
+        CK(cudaMalloc(&h->scales, h->scales_layer_elems * c.n_layers * sizeof(float)));
+        std::vector<float> ones(h->scales_layer_elems * c.n_layers, 1.0f);
+        CK(cudaMemcpy(h->scales, ones.data(), ones.size() * sizeof(float), cudaMemcpyHostToDevice));
+    }
+    const size_t pt = static_cast<size_t>(h->rt.max_streams) * h->maxp;
+    CK(cudaMalloc(&h->d_page_table, pt * sizeof(int)));
+    CK(cudaMallocHost(&h->h_page_table, pt * sizeof(int)));
+    std::fill(h->h_page_table, h->h_page_table + pt, -1);
+    CK(cudaMemcpy(h->d_page_table, h->h_page_table, pt * sizeof(int), cudaMemcpyHostToDevice));
+
+    // RoPE (cos, sin) per (position, i): the reference's double-angle formula
+    // (text-decoder.cpp:610-616) evaluated on the host, rounded to float once.
+    h->rope_len = h->rt.max_context;
+    std::vector<float2> rope(static_cast<size_t>(h->rope_len) * (kHeadDim / 2));
+    const double log_theta = std::log(static_cast<double>(c.rope_theta));
+    for (int i = 0; i < kHeadDim / 2; ++i) {
+        const double inv_freq = std::exp(-log_theta * static_cast<double>(2 * i) / static_cast<double>(kHeadDim));
+        for (int pos = 0; pos < h->rope_len; ++pos) {
+            const double angle = static_cast<double>(pos) * inv_freq;
+            rope[static_cast<size_t>(pos) * (kHeadDim / 2) + i] =
+                make_float2(static_cast<float>(std::cos(angle)), static_cast<float>(std::sin(angle)));
+        }
+    }
+    CK(cudaMalloc(&h->d_rope, rope.size() * sizeof(float2)));
+    CK(cudaMemcpy(h->d_rope, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice));
+
+    h->pager = new Pager(h->n_pages, kPageTokens, h->rt.max_streams, h->maxp, h->rt.page_order_seed);
+    h->last_id.assign(static_cast<size_t>(h->rt.max_streams), -1);
+
+    const int batch_tokens = h->rt.max_batch_tokens > 0 ? h->rt.max_batch_tokens : h->rt.max_context;
+    h->max_rows = std::max(batch_tokens, h->rt.max_streams);
+    const size_t R = static_cast<size_t>(h->max_rows);
+    const size_t act = h->act_dtype == kActF32 ? 4 : 2;
+    CK(cudaMalloc(&h->qkv, R * kQkvDim * sizeof(float)));
+    CK(cudaMalloc(&h->q, R * kQDim * sizeof(float)));
+    if (with_model_scratch) {
+        CK(cudaMalloc(&h->x, R * c.hidden * sizeof(float)));
+        CK(cudaMalloc(&h->xn, R * c.hidden * act));
+        CK(cudaMalloc(&h->attn, R * kQDim * act));
+        CK(cudaMalloc(&h->gu, R * 2 * c.intermediate * sizeof(float)));
+        CK(cudaMalloc(&h->act, R * c.intermediate * act));
+        CK(cudaMalloc(&h->logits, static_cast<size_t>(h->rt.max_streams) * c.vocab * sizeof(float)));
+    }
+    CK(cudaMalloc(&h->d_rowbuf, 4 * R * sizeof(int)));
+    CK(cudaMallocHost(&h->h_rowbuf, qkv_handle::kRowRing * 4 * R * sizeof(int)));
+    for (auto &ev : h->row_ev) CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    CK(cudaMalloc(&h->d_out_ids, R * sizeof(int)));
+    CK(cudaMallocHost(&h->h_out_ids, R * sizeof(int)));
+    const size_t slots = static_cast<size_t>(kAttnMaxRows + h->num_sms);
+    CK(cudaMalloc(&h->part_o, slots * kHq * kHeadDim * sizeof(float)));
+    CK(cudaMalloc(&h->part_ml, slots * kHq * 2 * sizeof(float)));
+    CK(cudaMalloc(&h->counters, static_cast<size_t>(kAttnMaxRows) * kHkv * sizeof(int)));
+    CK(cudaMemset(h->counters, 0, static_cast<size_t>(kAttnMaxRows) * kHkv * sizeof(int)));
+    CK(cudaMalloc(&h->d_err, sizeof(DevError)));
+    CK(cudaMemset(h->d_err, 0, sizeof(DevError)));
+    CK(cudaMallocHost(&h->h_err, sizeof(DevError)));
+    CK(prepare_decode_attn());
+    CK(cudaStreamSynchronize(h->stream));
+    return QKV_OK;
+}
+
+void destroy(qkv_handle *h) {
+    if (!h) return;
+    cudaSetDevice(h->device);
+    if (h->stream) cudaStreamSynchronize(h->stream);
+    for (auto &L : h->layers) {
+        cudaFree(L.attn_norm); cudaFree(L.ffn_norm); cudaFree(L.q_norm); cudaFree(L.k_norm);
+        cudaFree(L.w_qkv); cudaFree(L.w_o); cudaFree(L.w_gu); cudaFree(L.w_down);
+    }
+    cudaFree(h->embd); cudaFree(h->w_out); cudaFree(h->out_norm);
+    cudaFree(h->pool); cudaFree(h->scales); cudaFree(h->d_page_table); cudaFree(h->d_rope);
+    cudaFree(h->x); cudaFree(h->qkv); cudaFree(h->q); cudaFree(h->gu); cudaFree(h->logits);
+    cudaFree(h->xn); cudaFree(h->attn); cudaFree(h->act); cudaFree(h->host_stage);
+    cudaFree(h->d_rowbuf); cudaFree(h->d_out_ids); cudaFree(h->part_o); cudaFree(h->part_ml);
+    cudaFree(h->counters); cudaFree(h->d_err);
+    cudaFreeHost(h->h_page_table); cudaFreeHost(h->h_rowbuf); cudaFreeHost(h->h_out_ids); cudaFreeHost(h->h_err);
+    for (auto &ev : h->row_ev) {
+        if (ev) cudaEventDestroy(ev);
+    }
+    if (h->stream) cudaStreamDestroy(h->stream);
+    delete h->pager;
+    delete h;
+}
+
+// ---- weights ----
+
+struct Uploader {
+    qkv_handle *h;
+    void *staging = nullptr;
+    size_t staging_bytes = size_t{64} << 20;
+    ~Uploader() { cudaFree(staging); }
+
+    // Copy a GGUF tensor (f32/f16/bf16) to dst (+dst_off elements) in dtype.
+    int put(const GgufTensor *t, void *dst, int dtype, size_t dst_off) {
+        if (!staging) CK(cudaMalloc(&staging, staging_bytes));
+        const size_t es = ggml_type_size(t->type);
+        const int src_code = t->type == kGgmlF32 ? 0 : t->type == kGgmlF16 ? 1 : 2;
+        const size_t n = t->nbytes / es;
+        const size_t chunk = staging_bytes / es;
+        const size_t out_es = dtype == kActF32 ? 4 : 2;
+        for (size_t off = 0; off < n; off += chunk) {
+            const size_t cnt = std::min(chunk, n - off);
+            CK(cudaMemcpyAsync(staging, t->data + off * es, cnt * es, cudaMemcpyHostToDevice, h->stream));
+            CK(launch_convert(staging, src_code, static_cast<uint8_t *>(dst) + (dst_off + off) * out_es, dtype, cnt,
+                              h->stream));
+            CK(cudaStreamSynchronize(h->stream));   // staging is reused
+        }
+        return QKV_OK;
+    }
+};
+
+int find_tensor(qkv_handle *h, const GgufFile &f, const std::string &name, const std::vector<int64_t> &ne,
+                const GgufTensor **out) {
+    const GgufTensor *t = f.find(name);
+    if (!t) return fail(h, QKV_ERR_FORMAT, "missing GGUF tensor: " + name);
+    if (ggml_type_size(t->type) == 0) return fail(h, QKV_ERR_FORMAT, "tensor is not f32/f16/bf16: " + name);
+    if (t->ne != ne) return fail(h, QKV_ERR_FORMAT, "tensor shape mismatch: " + name);
+    *out = t;
+    return QKV_OK;
+}
+
+// Names and shapes as text-decoder.cpp:191-228 and :523-537 (GGML ne = [in, out]).
+int load_weights(qkv_handle *h, const GgufFile &f) {
+    const qkv_model_config &c = h->cfg;
+    const int64_t H = c.hidden, QD = kQDim, KD = kKvDim, F = c.intermediate, V = c.vocab, D = kHeadDim;
+    const size_t we = h->w_elem;
+    Uploader up{h};
+    h->layers.resize(static_cast<size_t>(c.n_layers));
+    int rc;
+    for (int l = 0; l < c.n_layers; ++l) {
+        const std::string p = "text.blk." + std::to_string(l) + ".";
+        const GgufTensor *an, *fn, *wq, *wk, *wv, *wo, *qn, *kn, *wg, *wu, *wd;
+        if ((rc = find_tensor(h, f, p + "attn_norm.weight", {H}, &an)) ||
+            (rc = find_tensor(h, f, p + "ffn_norm.weight", {H}, &fn)) ||
+            (rc = find_tensor(h, f, p + "attn_q.weight", {H, QD}, &wq)) ||
+            (rc = find_tensor(h, f, p + "attn_k.weight", {H, KD}, &wk)) ||
+            (rc = find_tensor(h, f, p + "attn_v.weight", {H, KD}, &wv)) ||
+            (rc = find_tensor(h, f, p + "attn_output.weight", {QD, H}, &wo)) ||
+            (rc = find_tensor(h, f, p + "attn_q_norm.weight", {D}, &qn)) ||
+            (rc = find_tensor(h, f, p + "attn_k_norm.weight", {D}, &kn)) ||
+            (rc = find_tensor(h, f, p + "ffn_gate.weight", {H, F}, &wg)) ||
+            (rc = find_tensor(h, f, p + "ffn_up.weight", {H, F}, &wu)) ||
+            (rc = find_tensor(h, f, p + "ffn_down.weight", {F, H}, &wd)))
+            return rc;
+        qkv_handle::Layer &L = h->layers[static_cast<size_t>(l)];
+        CK(cudaMalloc(&L.attn_norm, H * sizeof(float)));
+        CK(cudaMalloc(&L.ffn_norm, H * sizeof(float)));
+        CK(cudaMalloc(&L.q_norm, D * sizeof(float)));
+        CK(cudaMalloc(&L.k_norm, D * sizeof(float)));
+        CK(cudaMalloc(&L.w_qkv, static_cast<size_t>(QD + 2 * KD) * H * we));
+        CK(cudaMalloc(&L.w_o, static_cast<size_t>(H) * QD * we));
+        CK(cudaMalloc(&L.w_gu, static_cast<size_t>(2 * F) * H * we));
+        CK(cudaMalloc(&L.w_down, static_cast<size_t>(H) * F * we));
+        if ((rc = up.put(an, L.attn_norm, kActF32, 0)) || (rc = up.put(fn, L.ffn_norm, kActF32, 0)) ||
+            (rc = up.put(qn, L.q_norm, kActF32, 0)) || (rc = up.put(kn, L.k_norm, kActF32, 0)) ||
+            (rc = up.put(wq, L.w_qkv, h->w_dtype, 0)) ||
+            (rc = up.put(wk, L.w_qkv, h->w_dtype, static_cast<size_t>(QD) * H)) ||
+            (rc = up.put(wv, L.w_qkv, h->w_dtype, static_cast<size_t>(QD + KD) * H)) ||
+            (rc = up.put(wo, L.w_o, h->w_dtype, 0)) || (rc = up.put(wg, L.w_gu, h->w_dtype, 0)) ||
+            (rc = up.put(wu, L.w_gu, h->w_dtype, static_cast<size_t>(F) * H)) ||
+            (rc = up.put(wd, L.w_down, h->w_dtype, 0)))
+            return rc;
+    }
+    const GgufTensor *te, *on, *ow;
+    if ((rc = find_tensor(h, f, "text.token_embd.weight", {H, V}, &te)) ||
+        (rc = find_tensor(h, f, "text.output_norm.weight", {H}, &on)) ||
+        (rc = find_tensor(h, f, "text.output.weight", {H, V}, &ow)))
+        return rc;
+    CK(cudaMalloc(&h->embd, static_cast<size_t>(V) * H * we));
+    CK(cudaMalloc(&h->w_out, static_cast<size_t>(V) * H * we));
+    CK(cudaMalloc(&h->out_norm, H * sizeof(float)));
+    if ((rc = up.put(te, h->embd, h->w_dtype, 0)) || (rc = up.put(ow, h->w_out, h->w_dtype, 0)) ||
+        (rc = up.put(on, h->out_norm, kActF32, 0)))
+        return rc;
+    h->has_weights = true;
+    return QKV_OK;
+}
+
+// ---- per-call helpers ----
+
+int check_device_error(qkv_handle *h) {
+    CK(cudaMemcpyAsync(h->h_err, h->d_err, sizeof(DevError), cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    if (h->h_err->code != 0) {
+        const DevError e = *h->h_err;
+        CK(cudaMemsetAsync(h->d_err, 0, sizeof(DevError), h->stream));
+        CK(cudaStreamSynchronize(h->stream));
+        static const char *what[] = {"", "page index out of range", "bounded wait ran out", "position out of range",
+                                     "row out of bounds"};
+        const char *w = (e.code >= 0 && e.code <= 4) ? what[e.code] : "unknown";
+        return fail(h, QKV_ERR_DEVICE, std::string("device error: ") + w + " (kernel " + std::to_string(e.where) +
+                                           ", " + std::to_string(e.a) + ", " + std::to_string(e.b) + ")");
+    }
+    return QKV_OK;
+}
+
+int stream_len(qkv_handle *h, int32_t s) {
+    int32_t t = 0;
+    h->pager->length(s, &t, nullptr);
+    return t;
+}
+
+// Grow each row's stream by `tokens` (pages from the pager) and push changed
+// page-table rows to the device.
+int grow_streams(qkv_handle *h, int n, const int32_t *streams, const int32_t *tokens, cudaStream_t st) {
+    // All-or-nothing for the batch: check the page budget first.
+    int64_t need = 0;
+    for (int i = 0; i < n; ++i) {
+        const int64_t len = stream_len(h, streams[i]);
+        const int64_t t = tokens ? tokens[i] : 1;
+        const int64_t have = static_cast<int64_t>(h->pager->pages(streams[i])->size());
+        const int64_t want = (len + t + kPageTokens - 1) / kPageTokens;
+        if (want > h->maxp) return fail(h, QKV_ERR_CAPACITY, "stream would exceed max_context pages");
+        need += want - have;
+    }
+    if (need > h->pager->free_pages()) {
+        return fail(h, QKV_ERR_OUT_OF_PAGES, "KV pool out of pages (need " + std::to_string(need) + ", free " +
+                                                 std::to_string(h->pager->free_pages()) + ")");
+    }
+    std::vector<int32_t> added;
+    for (int i = 0; i < n; ++i) {
+        added.clear();
+        std::string e;
+        const int rc = h->pager->append(streams[i], tokens ? tokens[i] : 1, &added, &e);
+        if (rc != QKV_OK) return fail(h, rc, e);
+        if (!added.empty()) {
+            const std::vector<int32_t> *pg = h->pager->pages(streams[i]);
+            const size_t first = pg->size() - added.size();
+            int *row = h->h_page_table + static_cast<size_t>(streams[i]) * h->maxp;
+            for (size_t k = first; k < pg->size(); ++k) row[k] = (*pg)[k];
+            CK(cudaMemcpyAsync(h->d_page_table + static_cast<size_t>(streams[i]) * h->maxp + first, row + first,
+                               added.size() * sizeof(int), cudaMemcpyHostToDevice, st));
+        }
+    }
+    return QKV_OK;
+}
+
+// Pinned staging for the per-call row arrays.  A slot is reused only after the
+// copy that last read it has run (its event), so callers never block on the
+// previous step's kernels.
+int *row_stage(qkv_handle *h) {
+    h->row_slot = (h->row_slot + 1) % qkv_handle::kRowRing;
+    cudaEventSynchronize(h->row_ev[h->row_slot]);
+    return h->h_rowbuf + static_cast<size_t>(h->row_slot) * 4 * h->max_rows;
+}
+
+int row_upload(qkv_handle *h, const int *host, size_t count, cudaStream_t st) {
+    CK(cudaMemcpyAsync(h->d_rowbuf, host, count * sizeof(int), cudaMemcpyHostToDevice, st));
+    CK(cudaEventRecord(h->row_ev[h->row_slot], st));
+    return QKV_OK;
+}
+
+int check_streams(qkv_handle *h, int n, const int32_t *streams) {
+    if (n <= 0 || !streams) return fail(h, QKV_ERR_INVALID_ARG, "empty batch");
+    if (n > h->rt.max_streams) return fail(h, QKV_ERR_CAPACITY, "batch larger than max_streams");
+    std::vector<uint8_t> seen(static_cast<size_t>(h->rt.max_streams), 0);
+    for (int i = 0; i < n; ++i) {
+        if (!h->pager->is_open(streams[i])) return fail(h, QKV_ERR_INVALID_ARG, "stream " + std::to_string(streams[i]) + " is not open");
+        if (seen[static_cast<size_t>(streams[i])]++) return fail(h, QKV_ERR_INVALID_ARG, "stream listed twice in one batch");
+    }
+    return QKV_OK;
+}
+
+AppendParams append_params(qkv_handle *h, int layer, int n, const int *slots, const int *pos, const float *qkv,
+                           float *q_out, const float *qn, const float *kn) {
+    AppendParams p{};
+    p.n = n;
+    p.slots = slots;
+    p.positions = pos;
+    p.qkv = qkv;
+    p.q_out = q_out;
+    p.q_norm_w = qn;
+    p.k_norm_w = kn;
+    p.rope = h->d_rope;
+    p.rope_len = h->rope_len;
+    p.pool = static_cast<uint8_t *>(h->pool) + h->pool_layer_bytes * static_cast<size_t>(layer);
+    p.scales = h->scales ? h->scales + h->scales_layer_elems * static_cast<size_t>(layer) : nullptr;
+    p.page_table = h->d_page_table;
+    p.maxp = h->maxp;
+    p.max_streams = h->rt.max_streams;
+    p.n_pages = h->n_pages;
+    p.eps = h->cfg.rms_norm_eps;
+    p.mode = 0;
+    p.err = h->d_err;
+    return p;
+}
+
+AttendParams attend_params(qkv_handle *h, int layer, int n, const int *slots, const int *lens, const float *q,
+                           void *out) {
+    AttendParams p{};
+    p.n = n;
+    p.slots = slots;
+    p.lens = lens;
+    p.q = q;
+    p.out = out;
+    p.pool = static_cast<uint8_t *>(h->pool) + h->pool_layer_bytes * static_cast<size_t>(layer);
+    p.scales = h->scales ? h->scales + h->scales_layer_elems * static_cast<size_t>(layer) : nullptr;
+    p.page_table = h->d_page_table;
+    p.maxp = h->maxp;
+    p.max_streams = h->rt.max_streams;
+    p.n_pages = h->n_pages;
+    p.part_o = h->part_o;
+    p.part_ml = h->part_ml;
+    p.counters = h->counters;
+    p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(kHeadDim)));
+    p.err = h->d_err;
+    return p;
+}
+
+// Append + attend for `n` rows of one layer (rows: slots/pos/lens device arrays).
+int layer_kv(qkv_handle *h, int layer, int n, const int *slots, const int *pos, const int *lens, const float *qkv,
+             float *q, void *out, bool out_bf16, const float *qn, const float *kn, cudaStream_t st) {
+    AppendParams ap = append_params(h, layer, n, slots, pos, qkv, q, qn, kn);
+    CK(launch_kv_append(ap, h->rt.kv_dtype, st));
+    AttendParams at = attend_params(h, layer, n, slots, lens, q, out);
+    CK(launch_decode_attn(at, h->rt.kv_dtype, out_bf16, h->num_sms, st));
+    h->launches += 2;
+    return QKV_OK;
+}
+
+// Logits of the rows listed in d_rows (indices into x) -> ids (device), logits into h->logits.
+int head_and_argmax(qkv_handle *h, int n, const int *d_rows) {
+    const qkv_model_config &c = h->cfg;
+    CK(launch_rmsnorm(h->x, d_rows, n, c.hidden, h->out_norm, c.rms_norm_eps, h->xn, h->act_dtype, h->stream));
+    CK(launch_gemm(h->xn, h->act_dtype, h->w_out, h->w_dtype, h->logits, n, c.vocab, c.hidden, 0, h->stream));
+    CK(launch_argmax(h->logits, n, c.vocab, h->d_out_ids, h->stream));
+    h->launches += 3;
+    return QKV_OK;
+}
+
+// All layers over `n` rows whose inputs are in h->x; decode rows attend with
+// K2, prompt rows with the causal prefill kernel.
+int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int *lens, bool prompt) {
+    const qkv_model_config &c = h->cfg;
+    const bool bf = h->act_dtype == kActBF16;
+    int rc;
+    for (int l = 0; l < c.n_layers; ++l) {
+        const qkv_handle::Layer &L = h->layers[static_cast<size_t>(l)];
+        CK(launch_rmsnorm(h->x, nullptr, n, c.hidden, L.attn_norm, c.rms_norm_eps, h->xn, h->act_dtype, h->stream));
+        CK(launch_gemm(h->xn, h->act_dtype, L.w_qkv, h->w_dtype, h->qkv, n, kQkvDim, c.hidden, 0, h->stream));
+        if (!prompt) {
+            if ((rc = layer_kv(h, l, n, slots, pos, lens, h->qkv, h->q, h->attn, bf, L.q_norm, L.k_norm, h->stream)))
+                return rc;
+        } else {
+            AppendParams ap = append_params(h, l, n, slots, pos, h->qkv, h->q, L.q_norm, L.k_norm);
+            if (h->rt.kv_dtype == kKvFP8) {
+                ap.mode = 1;
+                CK(launch_kv_append(ap, h->rt.kv_dtype, h->stream));
+                ap.mode = 2;
+            }
+            CK(launch_kv_append(ap, h->rt.kv_dtype, h->stream));
+            PrefillAttnParams pp{};
+            pp.n = n;
+            pp.slots = slots;
+            pp.positions = pos;
+            pp.q = h->q;
+            pp.out = h->attn;
+            pp.pool = ap.pool;
+            pp.scales = ap.scales;
+            pp.page_table = h->d_page_table;
+            pp.maxp = h->maxp;
+            pp.max_streams = h->rt.max_streams;
+            pp.n_pages = h->n_pages;
+            pp.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(kHeadDim)));
+            pp.err = h->d_err;
+            CK(launch_prefill_attn(pp, h->rt.kv_dtype, bf, h->stream));
+            h->launches += 2;
+        }
+        CK(launch_gemm(h->attn, h->act_dtype, L.w_o, h->w_dtype, h->x, n, c.hidden, kQDim, 1, h->stream));
+        CK(launch_rmsnorm(h->x, nullptr, n, c.hidden, L.ffn_norm, c.rms_norm_eps, h->xn, h->act_dtype, h->stream));
+        CK(launch_gemm(h->xn, h->act_dtype, L.w_gu, h->w_dtype, h->gu, n, 2 * c.intermediate, c.hidden, 0, h->stream));
+        CK(launch_swiglu(h->gu, n, c.intermediate, h->act, h->act_dtype, h->stream));
+        CK(launch_gemm(h->act, h->act_dtype, L.w_down, h->w_dtype, h->x, n, c.hidden, c.intermediate, 1, h->stream));
+        h->launches += 7;
+    }
+    return QKV_OK;
+}
+
+int finish_ids(qkv_handle *h, int n, const int32_t *streams, int32_t *out_ids, float *out_logits) {
+    CK(cudaMemcpyAsync(h->h_out_ids, h->d_out_ids, static_cast<size_t>(n) * sizeof(int), cudaMemcpyDeviceToHost,
+                       h->stream));
+    if (out_logits) {
+        CK(cudaMemcpyAsync(out_logits, h->logits, static_cast<size_t>(n) * h->cfg.vocab * sizeof(float),
+                           cudaMemcpyDeviceToHost, h->stream));
+    }
+    int rc = check_device_error(h);
+    if (rc) return rc;
+    for (int i = 0; i < n; ++i) {
+        const int id = h->h_out_ids[i];
+        if (id < 0 || id >= h->cfg.vocab) return fail(h, QKV_ERR_DEVICE, "generated token id is out of range");
+        h->last_id[static_cast<size_t>(streams[i])] = id;
+        if (out_ids) out_ids[i] = id;
+    }
+    return QKV_OK;
+}
+
+}  // namespace
+
+// =====================================================================
+extern "C" {
+
+int qkv_read_gguf_config(const char *gguf_path, qkv_model_config *cfg, char *err, size_t err_len) {
+    if (!cfg) {
+        set_err(err, err_len, "cfg is null");
+        return QKV_ERR_INVALID_ARG;
+    }
+    GgufFile f;
+    std::string e;
+    int rc = f.open(gguf_path, &e);
+    if (rc) {
+        set_err(err, err_len, e);
+        return rc;
+    }
+    uint32_t L, H, Hq, Hkv, D, F, V;
+    float theta, eps;
+    const bool ok = f.get_u32("qwen3-asr.text.num_hidden_layers", &L) && f.get_u32("qwen3-asr.text.hidden_size", &H) &&
+                    f.get_u32("qwen3-asr.text.num_attention_heads", &Hq) &&
+                    f.get_u32("qwen3-asr.text.num_key_value_heads", &Hkv) && f.get_u32("qwen3-asr.text.head_dim", &D) &&
+                    f.get_u32("qwen3-asr.text.intermediate_size", &F) && f.get_u32("qwen3-asr.text.vocab_size", &V) &&
+                    f.get_f32("qwen3-asr.text.rope_theta", &theta) && f.get_f32("qwen3-asr.text.rms_norm_eps", &eps);
+    if (!ok) {
+        set_err(err, err_len, "GGUF lacks a qwen3-asr.text.* key (or it has the wrong type)");
+        return QKV_ERR_FORMAT;
+    }
+    cfg->n_layers = static_cast<int32_t>(L);
+    cfg->hidden = static_cast<int32_t>(H);
+    cfg->n_heads = static_cast<int32_t>(Hq);
+    cfg->n_kv_heads = static_cast<int32_t>(Hkv);
+    cfg->head_dim = static_cast<int32_t>(D);
+    cfg->intermediate = static_cast<int32_t>(F);
+    cfg->vocab = static_cast<int32_t>(V);
+    cfg->rope_theta = theta;
+    cfg->rms_norm_eps = eps;
+    return QKV_OK;
+}
+
+int qkv_create(const char *gguf_path, const qkv_model_config *cfg, const qkv_runtime_config *rt, qkv_handle **out,
+               char *err, size_t err_len) {
+    if (!out || !rt) {
+        set_err(err, err_len, "out or rt is null");
+        return QKV_ERR_INVALID_ARG;
+    }
+    *out = nullptr;
+    qkv_model_config c{};
+    int rc;
+    if (cfg) {
+        c = *cfg;
+    } else if ((rc = qkv_read_gguf_config(gguf_path, &c, err, err_len)) != QKV_OK) {
+        return rc;
+    }
+    std::string e;
+    if ((rc = validate_model(c, &e)) || (rc = validate_rt(*rt, &e))) {
+        set_err(err, err_len, e);
+        return rc;
+    }
+    GgufFile f;
+    if ((rc = f.open(gguf_path, &e))) {
+        set_err(err, err_len, e);
+        return rc;
+    }
+    qkv_handle *h = new qkv_handle();
+    h->cfg = c;
+    h->rt = *rt;
+    h->w_dtype = rt->weight_dtype == QKV_BF16 ? kActBF16 : kActF32;
+    h->act_dtype = h->w_dtype;
+    h->w_elem = h->w_dtype == kActBF16 ? 2 : 4;
+    if ((rc = setup_common(h, true)) || (rc = load_weights(h, f))) {
+        set_err(err, err_len, h->last_error);
+        destroy(h);
+        return rc;
+    }
+    *out = h;
+    return QKV_OK;
+}
+
+int qkv_create_kv_only(const qkv_model_config *cfg, const qkv_runtime_config *rt, const float *q_norm_w,
+                       const float *k_norm_w, qkv_handle **out, char *err, size_t err_len) {
+    if (!out || !rt || !cfg || !q_norm_w || !k_norm_w) {
+        set_err(err, err_len, "null argument");
+        return QKV_ERR_INVALID_ARG;
+    }
+    *out = nullptr;
+    std::string e;
+    int rc;
+    if ((rc = validate_model(*cfg, &e)) || (rc = validate_rt(*rt, &e))) {
+        set_err(err, err_len, e);
+        return rc;
+    }
+    qkv_handle *h = new qkv_handle();
+    h->cfg = *cfg;
+    h->rt = *rt;
+    h->w_dtype = kActF32;
+    h->act_dtype = kActF32;
+    if ((rc = setup_common(h, false))) {
+        set_err(err, err_len, h->last_error);
+        destroy(h);
+        return rc;
+    }
+    h->layers.resize(static_cast<size_t>(cfg->n_layers));
+    for (int l = 0; l < cfg->n_layers; ++l) {
+        qkv_handle::Layer &L = h->layers[static_cast<size_t>(l)];
+        if (cudaMalloc(&L.q_norm, kHeadDim * sizeof(float)) != cudaSuccess ||
+            cudaMalloc(&L.k_norm, kHeadDim * sizeof(float)) != cudaSuccess ||
+            cudaMemcpy(L.q_norm, q_norm_w + static_cast<size_t>(l) * kHeadDim, kHeadDim * sizeof(float),
+                       cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(L.k_norm, k_norm_w + static_cast<size_t>(l) * kHeadDim, kHeadDim * sizeof(float),
+                       cudaMemcpyHostToDevice) != cudaSuccess) {
+            set_err(err, err_len, "failed to upload QK-norm weights");
+            destroy(h);
+            return QKV_ERR_CUDA;
+        }
+    }
+    *out = h;
+    return QKV_OK;
+}
+
+void qkv_destroy(qkv_handle *h) { destroy(h); }
+
+const char *qkv_last_error(const qkv_handle *h) { return h ? h->last_error.c_str() : "null handle"; }
+
+int qkv_stream_open(qkv_handle *h, int32_t *stream_id) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    std::string e;
+    const int rc = h->pager->open(stream_id, &e);
+    if (rc) return fail(h, rc, e);
+    h->last_id[static_cast<size_t>(*stream_id)] = -1;
+    return QKV_OK;
+}
+
+int qkv_stream_close(qkv_handle *h, int32_t stream_id) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    // In-flight work may still read this stream's page-table row.
+    CK(cudaSetDevice(h->device));
+    CK(cudaStreamSynchronize(h->stream));
+    std::string e;
+    const std::vector<int32_t> *pg = h->pager->pages(stream_id);
+    const size_t used = pg ? pg->size() : 0;
+    const int rc = h->pager->close(stream_id, &e);
+    if (rc) return fail(h, rc, e);
+    int *row = h->h_page_table + static_cast<size_t>(stream_id) * h->maxp;
+    std::fill(row, row + used, -1);
+    CK(cudaMemcpyAsync(h->d_page_table + static_cast<size_t>(stream_id) * h->maxp, row, used * sizeof(int),
+                       cudaMemcpyHostToDevice, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    return QKV_OK;
+}
+
+int qkv_stream_length(const qkv_handle *h, int32_t stream_id, int32_t *tokens) {
+    if (!h || !tokens) return QKV_ERR_INVALID_ARG;
+    return h->pager->length(stream_id, tokens, nullptr);
+}
+
+int qkv_pool_stats(const qkv_handle *h, int64_t *free_pages, int64_t *total_pages) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    if (free_pages) *free_pages = h->pager->free_pages();
+    if (total_pages) *total_pages = h->n_pages;
+    return QKV_OK;
+}
+
+int qkv_compact(qkv_handle *h, int64_t *moved) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    CK(cudaSetDevice(h->device));
+    CK(cudaStreamSynchronize(h->stream));
+    std::vector<int32_t> src, dst;
+    h->pager->compact(&src, &dst);
+    if (moved) *moved = static_cast<int64_t>(src.size());
+    if (!src.empty()) {
+        int *d_moves = nullptr;
+        CK(cudaMalloc(&d_moves, 2 * src.size() * sizeof(int)));
+        CK(cudaMemcpy(d_moves, src.data(), src.size() * sizeof(int), cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(d_moves + src.size(), dst.data(), dst.size() * sizeof(int), cudaMemcpyHostToDevice));
+        for (int l = 0; l < h->cfg.n_layers; ++l) {
+            CK(launch_page_copy(static_cast<uint8_t *>(h->pool) + h->pool_layer_bytes * static_cast<size_t>(l),
+                                h->page_bytes, d_moves, d_moves + src.size(), static_cast<int>(src.size()), h->stream));
+            if (h->scales) {
+                CK(launch_page_copy(h->scales + h->scales_layer_elems * static_cast<size_t>(l), 2 * kHkv * sizeof(float),
+                                    d_moves, d_moves + src.size(), static_cast<int>(src.size()), h->stream));
+            }
+        }
+        CK(cudaStreamSynchronize(h->stream));
+        cudaFree(d_moves);
+    }
+    // Rewrite the whole page table from the pager.
+    std::fill(h->h_page_table, h->h_page_table + static_cast<size_t>(h->rt.max_streams) * h->maxp, -1);
+    for (int s = 0; s < h->rt.max_streams; ++s) {
+        const std::vector<int32_t> *pg = h->pager->pages(s);
+        if (!pg) continue;
+        std::copy(pg->begin(), pg->end(), h->h_page_table + static_cast<size_t>(s) * h->maxp);
+    }
+    CK(cudaMemcpyAsync(h->d_page_table, h->h_page_table, static_cast<size_t>(h->rt.max_streams) * h->maxp * sizeof(int),
+                       cudaMemcpyHostToDevice, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    return QKV_OK;
+}
+
+int qkv_prefill(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *lens, const float *embeddings,
+                int32_t *out_ids, float *out_logits) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    if (!h->has_weights) return fail(h, QKV_ERR_STATE, "handle has no model weights");
+    if (!lens || !embeddings) return fail(h, QKV_ERR_INVALID_ARG, "null lens or embeddings");
+    int rc;
+    if ((rc = check_streams(h, n, stream_ids))) return rc;
+    int64_t total = 0;
+    for (int i = 0; i < n; ++i) {
+        if (lens[i] <= 0) return fail(h, QKV_ERR_INVALID_ARG, "prompt length must be positive");
+        if (stream_len(h, stream_ids[i]) + static_cast<int64_t>(lens[i]) > h->rt.max_context)
+            return fail(h, QKV_ERR_CAPACITY, "prompt exceeds max_context");
+        total += lens[i];
+    }
+    if (total > h->max_rows) return fail(h, QKV_ERR_CAPACITY, "prompt tokens exceed max_batch_tokens");
+    CK(cudaSetDevice(h->device));
+    const int T = static_cast<int>(total);
+    int *hs = row_stage(h), *hp = hs + T, *hr = hp + T;   // slots, positions, last-row indices
+    int t = 0;
+    for (int i = 0; i < n; ++i) {
+        const int base = stream_len(h, stream_ids[i]);
+        for (int k = 0; k < lens[i]; ++k, ++t) {
+            hs[t] = stream_ids[i];
+            hp[t] = base + k;
+        }
+        hr[i] = t - 1;
+    }
+    if ((rc = grow_streams(h, n, stream_ids, lens, h->stream))) return rc;
+    int *ds = h->d_rowbuf, *dp = ds + T, *dr = dp + T;
+    if ((rc = row_upload(h, hs, static_cast<size_t>(2 * T + n), h->stream))) return rc;
+    CK(cudaMemcpyAsync(h->x, embeddings, static_cast<size_t>(T) * h->cfg.hidden * sizeof(float), cudaMemcpyHostToDevice,
+                       h->stream));
+    if ((rc = run_layers(h, T, ds, dp, nullptr, true))) return rc;
+    if ((rc = head_and_argmax(h, n, dr))) return rc;
+    return finish_ids(h, n, stream_ids, out_ids, out_logits);
+}
+
+int qkv_decode_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *in_ids, int32_t *out_ids,
+                    float *out_logits) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    if (!h->has_weights) return fail(h, QKV_ERR_STATE, "handle has no model weights");
+    int rc;
+    if ((rc = check_streams(h, n, stream_ids))) return rc;
+    if (n > kAttnMaxRows) return fail(h, QKV_ERR_CAPACITY, "decode batch larger than 1024 rows");
+    int *hs = row_stage(h), *hp = hs + n, *hl = hp + n, *hi = hl + n;
+    for (int i = 0; i < n; ++i) {
+        const int len = stream_len(h, stream_ids[i]);
+        if (len <= 0) return fail(h, QKV_ERR_STATE, "decode on a stream with no prompt");
+        if (len + 1 > h->rt.max_context) return fail(h, QKV_ERR_CAPACITY, "stream reached max_context");
+        const int id = in_ids ? in_ids[i] : h->last_id[static_cast<size_t>(stream_ids[i])];
+        if (id < 0 || id >= h->cfg.vocab) return fail(h, QKV_ERR_INVALID_ARG, "input id out of range");
+        hs[i] = stream_ids[i];
+        hp[i] = len;
+        hl[i] = len + 1;
+        hi[i] = id;
+    }
+    CK(cudaSetDevice(h->device));
+    if ((rc = grow_streams(h, n, stream_ids, nullptr, h->stream))) return rc;
+    int *ds = h->d_rowbuf, *dp = ds + n, *dl = dp + n, *di = dl + n;
+    if ((rc = row_upload(h, hs, static_cast<size_t>(4 * n), h->stream))) return rc;
+    CK(launch_embed(di, n, h->embd, h->w_dtype, h->cfg.hidden, h->cfg.vocab, h->x, h->d_err, h->stream));
+    h->launches += 1;
+    if ((rc = run_layers(h, n, ds, dp, dl, false))) return rc;
+    if ((rc = head_and_argmax(h, n, nullptr))) return rc;
+    return finish_ids(h, n, stream_ids, out_ids, out_logits);
+}
+
+int qkv_generate(qkv_handle *h, const float *embeddings, int32_t tokens, int32_t max_new_tokens, const int32_t *stop_ids,
+                 int32_t n_stop, int32_t *out_ids, int32_t *n_out, int32_t *stopped) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    if (n_out) *n_out = 0;
+    if (stopped) *stopped = 0;
+    if (max_new_tokens < 0) return fail(h, QKV_ERR_INVALID_ARG, "max_new_tokens must be non-negative");
+    if (tokens <= 0 || !embeddings) return fail(h, QKV_ERR_INVALID_ARG, "invalid generation input");
+    if (static_cast<int64_t>(tokens) + max_new_tokens > h->rt.max_context)
+        return fail(h, QKV_ERR_CAPACITY, "generation exceeds KV-cache capacity");
+    if (max_new_tokens == 0) return QKV_OK;
+    int32_t s = -1;
+    int rc = qkv_stream_open(h, &s);
+    if (rc) return rc;
+    int32_t id = -1;
+    rc = qkv_prefill(h, 1, &s, &tokens, embeddings, &id, nullptr);
+    for (int step = 0; rc == QKV_OK && step < max_new_tokens; ++step) {
+        out_ids[step] = id;
+        if (n_out) *n_out = step + 1;
+        bool stop = false;
+        for (int k = 0; k < n_stop; ++k) stop = stop || id == stop_ids[k];
+        if (stop) {
+            if (stopped) *stopped = 1;
+            break;
+        }
+        if (step + 1 >= max_new_tokens) break;
+        rc = qkv_decode_step(h, 1, &s, &id, &id, nullptr);
+    }
+    const std::string keep = h->last_error;
+    const int rc2 = qkv_stream_close(h, s);
+    if (rc) {
+        h->last_error = keep;
+        return rc;
+    }
+    return rc2;
+}
+
+int qkv_kv_append(qkv_handle *h, int32_t layer, int32_t n, const int32_t *slots_dev, const int32_t *positions_dev,
+                  const float *qkv_dev, float *q_out_dev, void *stream) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    if (layer < 0 || layer >= h->cfg.n_layers || n < 0 || (n > 0 && (!slots_dev || !positions_dev || !qkv_dev || !q_out_dev)))
+        return fail(h, QKV_ERR_INVALID_ARG, "kv_append: bad layer or pointer");
+    CK(cudaSetDevice(h->device));
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    const qkv_handle::Layer &L = h->layers[static_cast<size_t>(layer)];
+    AppendParams ap = append_params(h, layer, n, slots_dev, positions_dev, qkv_dev, q_out_dev, L.q_norm, L.k_norm);
+    CK(launch_kv_append(ap, h->rt.kv_dtype, st));
+    h->launches += 1;
+    return QKV_OK;
+}
+
+int qkv_kv_attend(qkv_handle *h, int32_t layer, int32_t n, const int32_t *slots_dev, const int32_t *lens_dev,
+                  const float *q_dev, float *out_dev, void *stream) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    if (layer < 0 || layer >= h->cfg.n_layers || n < 0 || n > kAttnMaxRows ||
+        (n > 0 && (!slots_dev || !lens_dev || !q_dev || !out_dev)))
+        return fail(h, QKV_ERR_INVALID_ARG, "kv_attend: bad layer, row count or pointer");
+    CK(cudaSetDevice(h->device));
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    AttendParams at = attend_params(h, layer, n, slots_dev, lens_dev, q_dev, out_dev);
+    CK(launch_decode_attn(at, h->rt.kv_dtype, false, h->num_sms, st));
+    h->launches += 1;
+    return QKV_OK;
+}
+
+int qkv_kv_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const float *qkv_dev, float *out_dev, void *stream) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    int rc;
+    if ((rc = check_streams(h, n, stream_ids))) return rc;
+    if (n > kAttnMaxRows) return fail(h, QKV_ERR_CAPACITY, "kv_step batch larger than 1024 rows");
+    if (!qkv_dev || !out_dev) return fail(h, QKV_ERR_INVALID_ARG, "null device pointer");
+    CK(cudaSetDevice(h->device));
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    int *hs = row_stage(h), *hp = hs + n, *hl = hp + n;
+    for (int i = 0; i < n; ++i) {
+        const int len = stream_len(h, stream_ids[i]);
+        if (len + 1 > h->rt.max_context) return fail(h, QKV_ERR_CAPACITY, "stream reached max_context");
+        hs[i] = stream_ids[i];
+        hp[i] = len;
+        hl[i] = len + 1;
+    }
+    if ((rc = grow_streams(h, n, stream_ids, nullptr, st))) return rc;
+    int *ds = h->d_rowbuf, *dp = ds + n, *dl = dp + n;
+    if ((rc = row_upload(h, hs, static_cast<size_t>(3 * n), st))) return rc;
+    const size_t in_stride = static_cast<size_t>(n) * kQkvDim, out_stride = static_cast<size_t>(n) * kQDim;
+    for (int l = 0; l < h->cfg.n_layers; ++l) {
+        const qkv_handle::Layer &L = h->layers[static_cast<size_t>(l)];
+        if ((rc = layer_kv(h, l, n, ds, dp, dl, qkv_dev + in_stride * l, h->q, out_dev + out_stride * l, false, L.q_norm,
+                           L.k_norm, st)))
+            return rc;
+    }
+    return QKV_OK;
+}
+
+int qkv_kv_step_host(qkv_handle *h, int32_t n, const int32_t *stream_ids, const float *qkv_host, float *out_host) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    if (!qkv_host || !out_host || n <= 0) return fail(h, QKV_ERR_INVALID_ARG, "null host pointer or empty batch");
+    CK(cudaSetDevice(h->device));
+    const size_t in_elems = static_cast<size_t>(h->cfg.n_layers) * n * kQkvDim;
+    const size_t out_elems = static_cast<size_t>(h->cfg.n_layers) * n * kQDim;
+    const size_t need = (in_elems + out_elems) * sizeof(float);
+    if (need > h->host_stage_bytes) {   // device staging, grown on demand and kept
+        CK(cudaStreamSynchronize(h->stream));
+        cudaFree(h->host_stage);
+        h->host_stage = nullptr;
+        h->host_stage_bytes = 0;
+        CK(cudaMalloc(&h->host_stage, need));
+        h->host_stage_bytes = need;
+    }
+    float *stage = h->host_stage;
+    CK(cudaMemcpyAsync(stage, qkv_host, in_elems * sizeof(float), cudaMemcpyHostToDevice, h->stream));
+    int rc = qkv_kv_step(h, n, stream_ids, stage, stage + in_elems, h->stream);
+    if (rc == QKV_OK) {
+        CK(cudaMemcpyAsync(out_host, stage + in_elems, out_elems * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+    }
+    const int rc2 = check_device_error(h);
+    return rc ? rc : rc2;
+}
+
+int qkv_stream_extend(qkv_handle *h, int32_t stream_id, int32_t tokens) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    if (tokens < 0) return fail(h, QKV_ERR_INVALID_ARG, "tokens must be non-negative");
+    if (!h->pager->is_open(stream_id)) return fail(h, QKV_ERR_INVALID_ARG, "stream is not open");
+    if (stream_len(h, stream_id) + static_cast<int64_t>(tokens) > h->rt.max_context)
+        return fail(h, QKV_ERR_CAPACITY, "extend exceeds max_context");
+    CK(cudaSetDevice(h->device));
+    int rc = grow_streams(h, 1, &stream_id, &tokens, h->stream);
+    if (rc) return rc;
+    CK(cudaStreamSynchronize(h->stream));
+    return QKV_OK;
+}
+
+int qkv_fill_random(qkv_handle *h, uint64_t seed) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    CK(cudaSetDevice(h->device));
+    std::vector<int> pages;
+    for (int s = 0; s < h->rt.max_streams; ++s) {
+        const std::vector<int32_t> *pg = h->pager->pages(s);
+        if (pg) pages.insert(pages.end(), pg->begin(), pg->end());
+    }
+    if (pages.empty()) return QKV_OK;
+    int *d = nullptr;
+    CK(cudaMalloc(&d, pages.size() * sizeof(int)));
+    CK(cudaMemcpy(d, pages.data(), pages.size() * sizeof(int), cudaMemcpyHostToDevice));
+    for (int l = 0; l < h->cfg.n_layers; ++l) {
+        CK(launch_page_fill(static_cast<uint8_t *>(h->pool) + h->pool_layer_bytes * static_cast<size_t>(l),
+                            h->scales ? h->scales + h->scales_layer_elems * static_cast<size_t>(l) : nullptr,
+                            h->rt.kv_dtype, d, static_cast<int>(pages.size()), seed * 1000003ull + static_cast<uint64_t>(l),
+                            h->stream));
+    }
+    CK(cudaStreamSynchronize(h->stream));
+    cudaFree(d);
+    return QKV_OK;
+}
+
+int qkv_gather(qkv_handle *h, int32_t layer, int32_t stream_id, void *k_host, void *v_host, float *scales_out) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    if (layer < 0 || layer >= h->cfg.n_layers || !h->pager->is_open(stream_id) || !k_host || !v_host)
+        return fail(h, QKV_ERR_INVALID_ARG, "gather: bad layer, stream or pointer");
+    CK(cudaSetDevice(h->device));
+    CK(cudaStreamSynchronize(h->stream));
+    const int len = stream_len(h, stream_id);
+    const std::vector<int32_t> *pg = h->pager->pages(stream_id);
+    if (len == 0) return QKV_OK;
+    const size_t eb = kv_elem_bytes(h->rt.kv_dtype);
+    const size_t bytes = static_cast<size_t>(len) * kKvDim * eb;
+    uint8_t *d = nullptr;
+    CK(cudaMalloc(&d, 2 * bytes + pg->size() * sizeof(int)));
+    int *dpages = reinterpret_cast<int *>(d + 2 * bytes);
+    CK(cudaMemcpy(dpages, pg->data(), pg->size() * sizeof(int), cudaMemcpyHostToDevice));
+    CK(launch_page_gather(static_cast<uint8_t *>(h->pool) + h->pool_layer_bytes * static_cast<size_t>(layer),
+                          h->rt.kv_dtype, dpages, static_cast<int>(pg->size()), len, h->n_pages, d, d + bytes, h->d_err,
+                          h->stream));
+    CK(cudaMemcpyAsync(k_host, d, bytes, cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaMemcpyAsync(v_host, d + bytes, bytes, cudaMemcpyDeviceToHost, h->stream));
+    if (scales_out && h->scales) {
+        for (size_t i = 0; i < pg->size(); ++i) {
+            CK(cudaMemcpyAsync(scales_out + i * 2 * kHkv,
+                               h->scales + h->scales_layer_elems * static_cast<size_t>(layer) +
+                                   static_cast<size_t>((*pg)[i]) * 2 * kHkv,
+                               2 * kHkv * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+        }
+    }
+    const int rc = check_device_error(h);
+    cudaFree(d);
+    return rc;
+}
+
+int qkv_stream_pages(const qkv_handle *h, int32_t stream_id, int32_t *pages_out, int32_t cap, int32_t *n) {
+    if (!h || !n) return QKV_ERR_INVALID_ARG;
+    const std::vector<int32_t> *pg = h->pager->pages(stream_id);
+    if (!pg) return QKV_ERR_INVALID_ARG;
+    *n = static_cast<int32_t>(pg->size());
+    for (int32_t i = 0; i < cap && i < *n; ++i) pages_out[i] = (*pg)[static_cast<size_t>(i)];
+    return QKV_OK;
+}
+
+int qkv_sync(qkv_handle *h) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    CK(cudaSetDevice(h->device));
+    return check_device_error(h);
+}
+
+int qkv_last_launches(const qkv_handle *h, int64_t *kernels) {
+    if (!h || !kernels) return QKV_ERR_INVALID_ARG;
+    *kernels = h->launches;
+    return QKV_OK;
+}
+
+int qkv_gguf_tensor(const char *gguf_path, const char *name, int64_t *ne_out, int32_t *n_dims, int32_t *ggml_type,
+                    void *data_out, size_t cap_bytes, char *err, size_t err_len) {
+    if (!name || !ne_out || !n_dims || !ggml_type) {
+        set_err(err, err_len, "null argument");
+        return QKV_ERR_INVALID_ARG;
+    }
+    GgufFile f;
+    std::string e;
+    const int rc = f.open(gguf_path, &e);
+    if (rc) {
+        set_err(err, err_len, e);
+        return rc;
+    }
+    const GgufTensor *t = f.find(name);
+    if (!t) {
+        set_err(err, err_len, std::string("missing GGUF tensor: ") + name);
+        return QKV_ERR_FORMAT;
+    }
+    for (int i = 0; i < 4; ++i) ne_out[i] = i < static_cast<int>(t->ne.size()) ? t->ne[static_cast<size_t>(i)] : 1;
+    *n_dims = static_cast<int32_t>(t->ne.size());
+    *ggml_type = static_cast<int32_t>(t->type);
+    if (data_out && t->nbytes) std::memcpy(data_out, t->data, std::min(cap_bytes, t->nbytes));
+    return QKV_OK;
+}
+
+// ---- host-only pager ----
+qkv_pager *qkv_pager_create(int64_t n_pages, int32_t page_tokens, int32_t max_streams, int32_t max_pages_per_stream,
+                            uint32_t seed) {
+    if (n_pages <= 0 || n_pages > (int64_t{1} << 30) || page_tokens <= 0 || max_streams <= 0 || max_pages_per_stream <= 0)
+        return nullptr;
+    return reinterpret_cast<qkv_pager *>(new Pager(n_pages, page_tokens, max_streams, max_pages_per_stream, seed));
+}
+void qkv_pager_destroy(qkv_pager *p) { delete reinterpret_cast<Pager *>(p); }
+int qkv_pager_open(qkv_pager *p, int32_t *stream_id) {
+    return p ? reinterpret_cast<Pager *>(p)->open(stream_id, nullptr) : QKV_ERR_INVALID_ARG;
+}
+int qkv_pager_close(qkv_pager *p, int32_t stream_id) {
+    return p ? reinterpret_cast<Pager *>(p)->close(stream_id, nullptr) : QKV_ERR_INVALID_ARG;
+}
+int qkv_pager_append(qkv_pager *p, int32_t stream_id, int32_t tokens, int32_t *new_pages) {
+    if (!p) return QKV_ERR_INVALID_ARG;
+    std::vector<int32_t> added;
+    const int rc = reinterpret_cast<Pager *>(p)->append(stream_id, tokens, &added, nullptr);
+    if (new_pages) *new_pages = rc == QKV_OK ? static_cast<int32_t>(added.size()) : 0;
+    return rc;
+}
+int qkv_pager_length(const qkv_pager *p, int32_t stream_id, int32_t *tokens) {
+    return p ? reinterpret_cast<const Pager *>(p)->length(stream_id, tokens, nullptr) : QKV_ERR_INVALID_ARG;
+}
+int qkv_pager_pages(const qkv_pager *p, int32_t stream_id, int32_t *pages_out, int32_t cap, int32_t *n) {
+    if (!p || !n) return QKV_ERR_INVALID_ARG;
+    const std::vector<int32_t> *pg = reinterpret_cast<const Pager *>(p)->pages(stream_id);
+    if (!pg) return QKV_ERR_INVALID_ARG;
+    *n = static_cast<int32_t>(pg->size());
+    for (int32_t i = 0; i < cap && i < *n; ++i) pages_out[i] = (*pg)[static_cast<size_t>(i)];
+    return QKV_OK;
+}
+int64_t qkv_pager_free_pages(const qkv_pager *p) { return p ? reinterpret_cast<const Pager *>(p)->free_pages() : -1; }
+int qkv_pager_compact(qkv_pager *p, int32_t *src, int32_t *dst, int64_t cap, int64_t *n_moves) {
+    if (!p) return QKV_ERR_INVALID_ARG;
+    std::vector<int32_t> s, d;
+    reinterpret_cast<Pager *>(p)->compact(&s, &d);
+    if (n_moves) *n_moves = static_cast<int64_t>(s.size());
+    for (int64_t i = 0; i < cap && i < static_cast<int64_t>(s.size()); ++i) {
+        if (src) src[i] = s[static_cast<size_t>(i)];
+        if (dst) dst[i] = d[static_cast<size_t>(i)];
+    }
+    return QKV_OK;
+}
+int qkv_pager_check(const qkv_pager *p) {
+    return p ? reinterpret_cast<const Pager *>(p)->check(nullptr) : QKV_ERR_INVALID_ARG;
+}
+
+}  // extern "C"

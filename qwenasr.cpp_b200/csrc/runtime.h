@@ -1,0 +1,84 @@
+// The handle behind the C ABI: one CUDA device, its weights, its paged KV pool
+// and stream table, and the per-step scratch.  Replaces the reference's
+// QwenAsrTextDecoderBackend (text-decoder.cpp:165-189): weights are uploaded
+// once at create (:1476-1592), the cache is a page pool instead of one
+// contiguous max_seq_len tensor per layer (:1420-1474), and every forward is a
+// fixed sequence of kernel launches instead of a GGML graph rebuilt per call
+// (:1641-1755).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <string>
+#include <vector>
+
+#include "kernels.h"
+#include "pager.h"
+#include "qkv.h"
+
+struct qkv_handle {
+    struct Layer {
+        float *attn_norm = nullptr, *ffn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+        void *w_qkv = nullptr;   // [(Hq+2Hkv)D][H]  q rows, then k rows, then v rows
+        void *w_o = nullptr;     // [H][Hq D]
+        void *w_gu = nullptr;    // [2F][H]  gate rows, then up rows
+        void *w_down = nullptr;  // [H][F]
+    };
+
+    int device = 0;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    qkv_model_config cfg{};
+    qkv_runtime_config rt{};
+    bool has_weights = false;
+    int w_dtype = 0;     // kActF32 / kActBF16 (weights and GEMM inputs)
+    int act_dtype = 0;   // activations feeding GEMMs
+    size_t w_elem = 4;
+
+    std::vector<Layer> layers;
+    void *embd = nullptr;      // [V][H]
+    void *w_out = nullptr;     // [V][H]
+    float *out_norm = nullptr; // [H]
+
+    // KV pool
+    void *pool = nullptr;
+    size_t pool_layer_bytes = 0;
+    size_t page_bytes = 0;      // one page of one layer
+    float *scales = nullptr;    // FP8: [L][n_pages][2][Hkv]
+    size_t scales_layer_elems = 0;
+    int n_pages = 0;
+    int maxp = 0;               // pages per stream
+    int *d_page_table = nullptr;
+    int *h_page_table = nullptr;    // pinned mirror [max_streams][maxp]
+    float2 *d_rope = nullptr;
+    int rope_len = 0;
+    qkv::Pager *pager = nullptr;
+
+    // scratch (rows = max(max_batch_tokens, max_streams))
+    int max_rows = 0;
+    float *x = nullptr, *qkv = nullptr, *q = nullptr, *gu = nullptr, *logits = nullptr;
+    float *host_stage = nullptr;    // device staging of qkv_kv_step_host
+    size_t host_stage_bytes = 0;
+    void *xn = nullptr, *attn = nullptr, *act = nullptr;
+    int *d_rowbuf = nullptr;    // [4][max_rows]: slots, positions, lens, ids
+    int *h_rowbuf = nullptr;    // pinned staging, kRowRing slots of [4][max_rows]
+    static constexpr int kRowRing = 4;
+    cudaEvent_t row_ev[kRowRing] = {};   // recorded after the copy out of each slot
+    int row_slot = 0;
+    int *d_out_ids = nullptr;   // [max_rows]
+    int *h_out_ids = nullptr;   // pinned
+    float *part_o = nullptr, *part_ml = nullptr;
+    int *counters = nullptr;
+    qkv::DevError *d_err = nullptr;
+    qkv::DevError *h_err = nullptr;
+    std::vector<int32_t> last_id;   // per slot: last greedy id
+
+    std::string last_error;
+    int64_t launches = 0;
+};
+
+namespace qkv {
+// Status helpers shared by the C ABI implementation files.
+int fail(qkv_handle *h, int code, const std::string &msg);
+int cuda_fail(qkv_handle *h, cudaError_t e, const char *what);
+}  // namespace qkv

@@ -1,0 +1,91 @@
+"""GGUF: the synthetic writer produces files the third-party `gguf` reader and
+the native reader agree on; the native reader passes the reference loader's
+known-answer checks (tools/qwen-asr-weights.cpp:97-143 exact floats,
+native-model.cpp:299-330 names/shapes) and rejects damaged files."""
+import struct
+
+import numpy as np
+import pytest
+
+
+def test_known_answer_tensor(pkg, tmp_path):
+    gguf = pytest.importorskip("gguf")
+    p = tmp_path / "kat.gguf"
+    w = gguf.GGUFWriter(str(p), "qwen3-asr")
+    w.add_tensor("kat.weight", np.array([1.25, -2.5, 3.75, 4.5], np.float32))
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    dims, ty, data = pkg.gguf_tensor(p, "kat.weight")
+    assert dims == [4] and ty == 0
+    assert data.view(np.float32).tolist() == [1.25, -2.5, 3.75, 4.5]
+
+
+def test_writer_matches_third_party_reader(pkg, synth, tiny_files):
+    gguf = pytest.importorskip("gguf")
+    cfg, files = tiny_files
+    path = files[("f32", "normal")]
+    r = gguf.GGUFReader(str(path))
+    mine = synth.read_gguf(path)
+    names = [t.name for t in r.tensors]
+    assert names == [n for n, _, _ in synth.tensor_specs(synth.ModelConfig.of(cfg))]
+    for t in r.tensors:
+        a = np.asarray(t.data).reshape(mine[t.name].shape)
+        assert np.array_equal(a, mine[t.name])
+        dims, ty, data = pkg.gguf_tensor(path, t.name)
+        assert dims == [int(d) for d in t.shape] and ty == 0
+        assert np.array_equal(data.view(np.float32).reshape(mine[t.name].shape), mine[t.name])
+    f = r.fields
+    assert int(f["qwen3-asr.text.hidden_size"].parts[-1][0]) == cfg["hidden"]
+
+
+def test_read_config(pkg, tiny_files):
+    cfg, files = tiny_files
+    got = pkg.read_gguf_config(files[("bf16", "one_plus")])
+    for k in ("n_layers", "hidden", "n_heads", "n_kv_heads", "head_dim", "intermediate", "vocab"):
+        assert got[k] == cfg[k]
+    assert got["rope_theta"] == pytest.approx(cfg["rope_theta"])
+
+
+def test_expected_tensor_set(synth):
+    """612 tensors for 0.6B with the audio tower (native-model.cpp:299-330); the text part is 3 + 11 per layer."""
+    specs = synth.tensor_specs(synth.ModelConfig.of(synth.QWEN3_ASR_0_6B))
+    assert len(specs) == 3 + 11 * 28
+    shapes = dict((n, s) for n, s, _ in specs)
+    assert shapes["text.blk.0.attn_q.weight"] == (2048, 1024)      # GGML ne {1024, 2048}
+    assert shapes["text.blk.27.ffn_down.weight"] == (1024, 3072)
+    assert shapes["text.output.weight"] == (151936, 1024)
+
+
+def test_bf16_rounding_is_rne(synth):
+    a = np.array([1.0, 1.00390625, 1.005859375, -3.14159, 65504.0], np.float32)
+    r = synth.bf16_round(a)
+    # ties-to-even: 1 + 2^-8 is halfway between 1 and 1 + 2^-7 -> 1.0
+    assert r[0] == 1.0 and r[1] == 1.0 and r[2] == np.float32(1.0078125)
+    assert (r.view(np.uint32) & 0xFFFF).max() == 0
+
+
+@pytest.mark.parametrize("damage", ["magic", "truncated", "offset", "version"])
+def test_reader_rejects_damaged_files(pkg, tiny_files, tmp_path, damage):
+    cfg, files = tiny_files
+    data = bytearray(files[("f32", "normal")].read_bytes())
+    if damage == "magic":
+        data[0:4] = b"GGUX"
+    elif damage == "truncated":
+        data = data[: len(data) // 2]
+    elif damage == "version":
+        data[4:8] = struct.pack("<I", 9)
+    else:
+        # point the first tensor's offset far beyond the end of the file
+        r = __import__("gguf").GGUFReader(str(files[("f32", "normal")]))
+        off = r.tensors[0].field.offset
+        field = r.tensors[0].field
+        # the offset is the last part of the tensor-info field
+        pos = off + sum(p.nbytes for p in field.parts[:-1])
+        data[pos:pos + 8] = struct.pack("<Q", 1 << 40)
+    p = tmp_path / f"bad_{damage}.gguf"
+    p.write_bytes(bytes(data))
+    with pytest.raises(pkg.QkvError) as ei:
+        pkg.gguf_tensor(p, "text.token_embd.weight")
+    assert ei.value.code in (6, 7)

@@ -1,0 +1,228 @@
+"""GPU parity of the KV-cache operators through the C ABI (device pointers):
+K1 append bit-exact against the oracle given the same projections, page
+gather bit-exact, K2 decode attention against the oracle over page
+boundaries, split rows and permuted page tables, and the microbench step."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+D, HQ, HKV = 128, 16, 8
+QKV = (HQ + 2 * HKV) * D
+
+
+def bf16_bits(a: np.ndarray) -> np.ndarray:
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32)
+    return (((u + 0x7FFF + ((u >> 16) & 1)) >> 16) & 0xFFFF).astype(np.uint16)
+
+
+def bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+def kv_handle(pkg, kv_dtype, n_layers=2, max_streams=8, max_context=4096, seed=0, pages=0):
+    rng = np.random.default_rng(99)
+    qn = (1.0 + 0.1 * rng.standard_normal((n_layers, D))).astype(np.float32)
+    kn = (1.0 + 0.1 * rng.standard_normal((n_layers, D))).astype(np.float32)
+    cfg = dict(n_layers=n_layers, hidden=256, n_heads=HQ, n_kv_heads=HKV, head_dim=D, intermediate=512, vocab=1000,
+               rope_theta=1.0e6, rms_norm_eps=1.0e-6)
+    rt = pkg.runtime_config(device=0, kv_dtype=kv_dtype, max_streams=max_streams, max_context=max_context,
+                            max_pages=pages, page_order_seed=seed)
+    return pkg.Decoder.kv_only(cfg, rt, qn, kn), qn, kn
+
+
+def dev_i32(a):
+    return torch.tensor(np.asarray(a, np.int32), device="cuda")
+
+
+def fill_stream(dec, layer, s, qkv_rows: np.ndarray, start: int = 0):
+    """Append rows to stream s at positions start.. (one launch)."""
+    n = qkv_rows.shape[0]
+    slots = dev_i32([s] * n)
+    pos = dev_i32(np.arange(start, start + n))
+    x = torch.tensor(qkv_rows, device="cuda")
+    q = torch.empty((n, HQ * D), device="cuda")
+    dec.kv_append(layer, n, slots.data_ptr(), pos.data_ptr(), x.data_ptr(), q.data_ptr())
+    torch.cuda.synchronize()
+    dec.sync()
+    return q.cpu().numpy()
+
+
+@pytest.mark.parametrize("kv_dtype", [0, 1])
+def test_append_bit_exact(pkg, checker, kv_dtype):
+    dec, qn, kn = kv_handle(pkg, kv_dtype, seed=5)
+    with dec:
+        rng = np.random.default_rng(1)
+        s = dec.open()
+        L = 1030
+        dec.extend(s, L)
+        positions = [0, 1, 14, 15, 16, 17, 31, 32, 100, 1000, 1029]
+        raw = rng.standard_normal((len(positions), QKV), dtype=np.float32) * 3.0
+        slots = dev_i32([s] * len(positions))
+        pos = dev_i32(positions)
+        x = torch.tensor(raw, device="cuda")
+        q = torch.empty((len(positions), HQ * D), device="cuda")
+        dec.kv_append(1, len(positions), slots.data_ptr(), pos.data_ptr(), x.data_ptr(), q.data_ptr())
+        torch.cuda.synchronize()
+        dec.sync()
+        k_all, v_all = dec.gather(1, s, kv_dtype)
+        qd = q.cpu().numpy()
+        for i, p in enumerate(positions):
+            oq, ok, ov = checker.append_qkv(raw[i], qn[1], kn[1], p)
+            assert np.array_equal(qd[i], oq), f"q row at position {p}"
+            if kv_dtype == 0:
+                assert np.array_equal(k_all[p], ok), f"K at position {p}"
+                assert np.array_equal(v_all[p], ov), f"V at position {p}"
+            else:
+                assert np.array_equal(k_all[p], bf16_bits(ok)), f"K at position {p}"
+                assert np.array_equal(v_all[p], bf16_bits(ov)), f"V at position {p}"
+
+
+@pytest.mark.parametrize("seed", [0, 77])
+def test_gather_roundtrip_permuted(pkg, checker, seed):
+    """Every token appended in one launch per stream reads back bit-exactly through
+    the page table, whatever the page order."""
+    dec, qn, kn = kv_handle(pkg, 0, seed=seed, max_streams=4)
+    with dec:
+        rng = np.random.default_rng(2)
+        for L in (1, 16, 17, 200):
+            s = dec.open()
+            raw = rng.standard_normal((L, QKV), dtype=np.float32)
+            dec.extend(s, L)
+            fill_stream(dec, 0, s, raw)
+            k, v = dec.gather(0, s, 0)
+            for t in range(L):
+                _, ok, ov = checker.append_qkv(raw[t], qn[0], kn[0], t)
+                assert np.array_equal(k[t], ok) and np.array_equal(v[t], ov)
+            if seed:
+                pages = dec.pages(s)
+                assert len(pages) == (L + 15) // 16
+            dec.close_stream(s)
+
+
+def attend_case(pkg, checker, kv_dtype, lens, seed=3, tol=2e-5):
+    dec, qn, kn = kv_handle(pkg, kv_dtype, seed=seed, max_streams=len(lens), max_context=max(lens) + 16)
+    with dec:
+        rng = np.random.default_rng(seed)
+        streams = []
+        for L in lens:
+            s = dec.open()
+            dec.extend(s, L)
+            fill_stream(dec, 0, s, rng.standard_normal((L, QKV), dtype=np.float32))
+            streams.append(s)
+        qv = rng.standard_normal((len(lens), HQ * D), dtype=np.float32)
+        q = torch.tensor(qv, device="cuda")
+        out = torch.empty_like(q)
+        dec.kv_attend(0, len(lens), dev_i32(streams).data_ptr(), dev_i32(lens).data_ptr(), q.data_ptr(),
+                      out.data_ptr())
+        torch.cuda.synchronize()
+        dec.sync()
+        got = out.cpu().numpy()
+        worst = 0.0
+        for i, s in enumerate(streams):
+            k, v = dec.gather(0, s, kv_dtype)
+            if kv_dtype == 1:
+                k, v = bits_to_f32(k), bits_to_f32(v)
+            want = checker.attend(qv[i], k, v)
+            err = np.max(np.abs(got[i] - want)) / max(np.max(np.abs(want)), 1e-6)
+            worst = max(worst, err)
+        assert worst < tol, worst
+        return worst
+
+
+@pytest.mark.parametrize("kv_dtype", [0, 1])
+def test_attention_page_boundaries(pkg, checker, kv_dtype):
+    attend_case(pkg, checker, kv_dtype, [1, 2, 15, 16, 17, 31, 32, 33])
+
+
+@pytest.mark.parametrize("kv_dtype", [0, 1])
+def test_attention_split_rows(pkg, checker, kv_dtype):
+    """One long row spread over every CTA plus short rows sharing CTAs (combine path)."""
+    attend_case(pkg, checker, kv_dtype, [4096, 5, 700, 64, 1, 2500])
+
+
+def test_attention_many_rows(pkg, checker):
+    rng = np.random.default_rng(4)
+    lens = rng.integers(1, 300, size=40).tolist()
+    attend_case(pkg, checker, 1, lens, seed=9)
+
+
+def test_attention_repeated_launches_reset_counters(pkg, checker):
+    """The split-row counters reset themselves: back-to-back launches agree."""
+    dec, qn, kn = kv_handle(pkg, 1, seed=1, max_streams=2, max_context=4096)
+    with dec:
+        rng = np.random.default_rng(8)
+        s = dec.open()
+        dec.extend(s, 3000)
+        fill_stream(dec, 0, s, rng.standard_normal((3000, QKV), dtype=np.float32))
+        q = torch.tensor(rng.standard_normal((1, HQ * D), dtype=np.float32), device="cuda")
+        outs = []
+        for _ in range(3):
+            out = torch.empty_like(q)
+            dec.kv_attend(0, 1, dev_i32([s]).data_ptr(), dev_i32([3000]).data_ptr(), q.data_ptr(), out.data_ptr())
+            torch.cuda.synchronize()
+            outs.append(out.cpu().numpy())
+        dec.sync()
+        assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[1], outs[2])
+
+
+def test_kv_step_matches_oracle(pkg, checker):
+    """The microbench step (append 1 token + attend, every layer) vs the oracle's batch leg."""
+    L_layers = 3
+    dec, qn, kn = kv_handle(pkg, 0, n_layers=L_layers, seed=13, max_streams=5, max_context=512)
+    with dec:
+        rng = np.random.default_rng(6)
+        lens0 = np.array([1, 15, 16, 40, 300], np.int32)
+        streams = [dec.open() for _ in lens0]
+        cap = 512
+        kcs = [np.zeros((L_layers, cap, 1024), np.float32) for _ in lens0]
+        vcs = [np.zeros((L_layers, cap, 1024), np.float32) for _ in lens0]
+        for i, (s, L) in enumerate(zip(streams, lens0)):
+            dec.extend(s, int(L))
+            for layer in range(L_layers):
+                rows = rng.standard_normal((int(L), QKV), dtype=np.float32)
+                fill_stream(dec, layer, s, rows)
+                k, v = dec.gather(layer, s, 0)
+                kcs[i][layer, :L] = k
+                vcs[i][layer, :L] = v
+        lens = lens0.copy()
+        for step in range(3):
+            qkv = rng.standard_normal((L_layers, len(streams), QKV), dtype=np.float32)
+            want = checker.kv_step_batch(qkv, qn, kn, kcs, vcs, lens)
+            x = torch.tensor(qkv, device="cuda")
+            out = torch.empty((L_layers, len(streams), HQ * D), device="cuda")
+            dec.kv_step(streams, x.data_ptr(), out.data_ptr())
+            torch.cuda.synchronize()
+            dec.sync()
+            np.testing.assert_allclose(out.cpu().numpy(), want, rtol=1e-4, atol=2e-5)
+        assert [dec.length(s) for s in streams] == (lens0 + 3).tolist()
+
+
+def test_kv_step_host_matches_device(pkg):
+    dec, qn, kn = kv_handle(pkg, 1, n_layers=2, seed=2, max_streams=3, max_context=256)
+    with dec:
+        rng = np.random.default_rng(12)
+        streams = [dec.open() for _ in range(3)]
+        for s, L in zip(streams, (10, 100, 33)):
+            dec.extend(s, L)
+        dec.fill_random(5)
+        qkv = rng.standard_normal((2, 3, QKV), dtype=np.float32)
+        out_h = np.zeros((2, 3, HQ * D), np.float32)
+        dec.kv_step_host(streams, qkv.ctypes.data, out_h.ctypes.data)
+        assert np.isfinite(out_h).all() and np.abs(out_h).max() > 0
+
+
+def test_device_error_on_bad_page_table_row(pkg):
+    """A row naming a stream that has no pages is reported, not faulted."""
+    dec, qn, kn = kv_handle(pkg, 1, seed=0, max_streams=2, max_context=64)
+    with dec:
+        s = dec.open()
+        q = torch.zeros((1, HQ * D), device="cuda")
+        out = torch.zeros_like(q)
+        dec.kv_attend(0, 1, dev_i32([s]).data_ptr(), dev_i32([20]).data_ptr(), q.data_ptr(), out.data_ptr())
+        torch.cuda.synchronize()
+        with pytest.raises(pkg.QkvError) as ei:
+            dec.sync()
+        assert ei.value.code == 5
+        dec.sync()   # the error word was cleared
