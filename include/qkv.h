@@ -7,10 +7,10 @@
  * owns one CUDA device: its weights, its paged KV pool and its stream table.
  * It is driven by one host thread at a time.  Multi-GPU = one handle per GPU.
  *
- * Every entry point whose arguments are host buffers synchronises the handle's
- * CUDA stream before it returns.  Entry points taking device pointers run on
- * the CUDA stream passed in (NULL = the handle's own stream) and do not
- * synchronise.
+ * Every entry point whose arguments are host buffers runs on the handle's own
+ * CUDA stream and synchronises it before it returns.  Entry points taking
+ * device pointers run on the CUDA stream passed in (NULL = the legacy default
+ * stream) and do not synchronise.
  *
  * Errors: a non-zero status; the message is kept per handle and read with
  * qkv_last_error().  Kernels never trap: device-side failures (a bounded wait
@@ -143,7 +143,9 @@ int qkv_generate(qkv_handle *h, const float *embeddings, int32_t tokens, int32_t
                  int32_t *stopped);
 
 /* ---- operator level: one layer's K/V append and decode attention ----
- * Device pointers; stream = cudaStream_t or NULL for the handle's stream.
+ * Device pointers; `stream` is the cudaStream_t to launch on (NULL = the CUDA
+ * legacy default stream, as in the CUDA runtime API).  Consecutive calls on a
+ * handle must use the same stream (its per-call row staging is stream-ordered).
  * Rows: slots[i] is an open stream id, positions[i] its token position. */
 
 /* K1: qkv[n][Hq*D + 2*Hkv*D] f32 (raw projections) -> QK-RMSNorm + NEOX RoPE;
@@ -188,7 +190,7 @@ int qkv_gather(qkv_handle *h, int32_t layer, int32_t stream_id, void *k_host, vo
 int qkv_stream_pages(const qkv_handle *h, int32_t stream_id, int32_t *pages_out, int32_t cap,
                      int32_t *n);
 
-/* Synchronise the handle's stream and surface any device error. */
+/* Synchronise the device and surface any device error. */
 int qkv_sync(qkv_handle *h);
 
 /* Device scratch / launch accounting of the last call (for benches). */

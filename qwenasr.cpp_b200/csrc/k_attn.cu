@@ -214,10 +214,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(AttendParams p
     __syncthreads();
 
     const int64_t T = row_start[n];
-    const int64_t G = gridDim.x;
+    // With fewer pages than CTAs, only the first T CTAs take a (one-page) range:
+    // every CTA in [0, G) then owns a non-empty range, which the per-row
+    // segment count c1 - c0 + 1 below relies on.
+    const int64_t G = T < static_cast<int64_t>(gridDim.x) ? T : static_cast<int64_t>(gridDim.x);
     const int64_t c = blockIdx.x;
+    if (c >= G) return;     // no pages for this CTA (nothing armed yet)
     const int64_t pb = c * T / G, pe = (c + 1) * T / G;
-    if (pb >= pe) return;   // no pages for this CTA (nothing armed yet)
     int r0 = 0;
     {
         int lo = 0, hi = n - 1;

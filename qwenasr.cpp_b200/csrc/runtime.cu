@@ -810,7 +810,7 @@ int qkv_kv_append(qkv_handle *h, int32_t layer, int32_t n, const int32_t *slots_
     if (layer < 0 || layer >= h->cfg.n_layers || n < 0 || (n > 0 && (!slots_dev || !positions_dev || !qkv_dev || !q_out_dev)))
         return fail(h, QKV_ERR_INVALID_ARG, "kv_append: bad layer or pointer");
     CK(cudaSetDevice(h->device));
-    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);   // NULL: the legacy default stream
     const qkv_handle::Layer &L = h->layers[static_cast<size_t>(layer)];
     AppendParams ap = append_params(h, layer, n, slots_dev, positions_dev, qkv_dev, q_out_dev, L.q_norm, L.k_norm);
     CK(launch_kv_append(ap, h->rt.kv_dtype, st));
@@ -825,7 +825,7 @@ int qkv_kv_attend(qkv_handle *h, int32_t layer, int32_t n, const int32_t *slots_
         (n > 0 && (!slots_dev || !lens_dev || !q_dev || !out_dev)))
         return fail(h, QKV_ERR_INVALID_ARG, "kv_attend: bad layer, row count or pointer");
     CK(cudaSetDevice(h->device));
-    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);   // NULL: the legacy default stream
     AttendParams at = attend_params(h, layer, n, slots_dev, lens_dev, q_dev, out_dev);
     CK(launch_decode_attn(at, h->rt.kv_dtype, false, h->num_sms, st));
     h->launches += 1;
@@ -839,7 +839,7 @@ int qkv_kv_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const float
     if (n > kAttnMaxRows) return fail(h, QKV_ERR_CAPACITY, "kv_step batch larger than 1024 rows");
     if (!qkv_dev || !out_dev) return fail(h, QKV_ERR_INVALID_ARG, "null device pointer");
     CK(cudaSetDevice(h->device));
-    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);   // NULL: the legacy default stream
     int *hs = row_stage(h), *hp = hs + n, *hl = hp + n;
     for (int i = 0; i < n; ++i) {
         const int len = stream_len(h, stream_ids[i]);
@@ -967,6 +967,7 @@ int qkv_stream_pages(const qkv_handle *h, int32_t stream_id, int32_t *pages_out,
 int qkv_sync(qkv_handle *h) {
     if (!h) return QKV_ERR_INVALID_ARG;
     CK(cudaSetDevice(h->device));
+    CK(cudaDeviceSynchronize());   // operator-level calls may run on any stream of this device
     return check_device_error(h);
 }
 

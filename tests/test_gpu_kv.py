@@ -114,8 +114,8 @@ def attend_case(pkg, checker, kv_dtype, lens, seed=3, tol=2e-5):
         qv = rng.standard_normal((len(lens), HQ * D), dtype=np.float32)
         q = torch.tensor(qv, device="cuda")
         out = torch.empty_like(q)
-        dec.kv_attend(0, len(lens), dev_i32(streams).data_ptr(), dev_i32(lens).data_ptr(), q.data_ptr(),
-                      out.data_ptr())
+        d_slots, d_lens = dev_i32(streams), dev_i32(lens)   # keep both alive until the kernel ran
+        dec.kv_attend(0, len(lens), d_slots.data_ptr(), d_lens.data_ptr(), q.data_ptr(), out.data_ptr())
         torch.cuda.synchronize()
         dec.sync()
         got = out.cpu().numpy()
@@ -157,10 +157,11 @@ def test_attention_repeated_launches_reset_counters(pkg, checker):
         dec.extend(s, 3000)
         fill_stream(dec, 0, s, rng.standard_normal((3000, QKV), dtype=np.float32))
         q = torch.tensor(rng.standard_normal((1, HQ * D), dtype=np.float32), device="cuda")
+        d_slots, d_lens = dev_i32([s]), dev_i32([3000])
         outs = []
         for _ in range(3):
             out = torch.empty_like(q)
-            dec.kv_attend(0, 1, dev_i32([s]).data_ptr(), dev_i32([3000]).data_ptr(), q.data_ptr(), out.data_ptr())
+            dec.kv_attend(0, 1, d_slots.data_ptr(), d_lens.data_ptr(), q.data_ptr(), out.data_ptr())
             torch.cuda.synchronize()
             outs.append(out.cpu().numpy())
         dec.sync()
@@ -220,7 +221,8 @@ def test_device_error_on_bad_page_table_row(pkg):
         s = dec.open()
         q = torch.zeros((1, HQ * D), device="cuda")
         out = torch.zeros_like(q)
-        dec.kv_attend(0, 1, dev_i32([s]).data_ptr(), dev_i32([20]).data_ptr(), q.data_ptr(), out.data_ptr())
+        d_slots, d_lens = dev_i32([s]), dev_i32([20])
+        dec.kv_attend(0, 1, d_slots.data_ptr(), d_lens.data_ptr(), q.data_ptr(), out.data_ptr())
         torch.cuda.synchronize()
         with pytest.raises(pkg.QkvError) as ei:
             dec.sync()
