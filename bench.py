@@ -203,6 +203,8 @@ def run_reference(args) -> int:
 def run_ours(args) -> int:
     import torch
 
+    global N_LAYERS
+    N_LAYERS = args.layers
     import __graft_entry__ as ge
     pkg = ge.load_package()
     rank, local, world, dist = dist_setup(args.gpus)
@@ -339,6 +341,8 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--layers", type=int, default=N_LAYERS,
+                    help="layers of cache (28 = the workload; fewer only for small profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
