@@ -196,6 +196,31 @@ int qkv_sync(qkv_handle *h);
 /* Device scratch / launch accounting of the last call (for benches). */
 int qkv_last_launches(const qkv_handle *h, int64_t *kernels);
 
+/* K2 decode attention for callers that may not allocate device memory: code
+ * embedded in a host framework that owns every device buffer through its own
+ * allocator and memory plan (a graph scheduler with pre-sized buffers, a
+ * server that budgets HBM up front), where a cudaMalloc or cudaFree behind the
+ * framework's back breaks its accounting or is not allowed.  This entry point
+ * has no counterpart in the reference.  The caller passes everything as device
+ * pointers: one layer's pool ([n_pages][2][8][16][128] elements of kv_dtype),
+ * its FP8 scales ([n_pages][2][8] f32, or NULL unless kv_dtype is FP8), the
+ * page table [max_streams][maxp], and per-row slots, lengths (tokens to
+ * attend over), queries [n][2048] f32 and outputs [n][2048] f32.  No call
+ * allocates: the kernel's scratch is a fixed ~3.5 MB array inside this
+ * library, which every GPU that loads the library holds until the process
+ * exits, and a call takes at most 256 rows (QKV_ERR_CAPACITY beyond).  The
+ * first call on each device, with that device current, looks up the array's
+ * device address and prepares the kernel; make that first call before any
+ * stream capture.  All calls share the one array, which keeps the last call's
+ * contents, so calls that overlap on the GPU (two streams, two host threads)
+ * race.  The call is asynchronous on `stream` (NULL = legacy default stream);
+ * rows that fail the kernel's bounds checks are skipped, not reported.  err
+ * (nullable) receives a message for a non-zero status. */
+int qkv_kv_attend_noalloc(const void *pool_layer, int32_t kv_dtype, const float *scales_layer,
+                          const int32_t *page_table, int32_t maxp, int32_t max_streams, int32_t n_pages,
+                          int32_t n, const int32_t *slots_dev, const int32_t *lens_dev, const float *q_dev,
+                          float *out_dev, void *stream, char *err, size_t err_len);
+
 /* Host-only GGUF probe (no GPU): shape / type of one tensor, and up to
  * cap_bytes of its raw data copied to data_out (nullable).  ne_out[4] gets
  * GGML ne (unused dims 1).  The loader checks of gguf-model.cpp:110-162 apply. */

@@ -27,6 +27,12 @@
 //   PV: lane owns dims [4*lane, 4*lane+4) of both heads.
 #include "kernels.h"
 
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
+#include "qkv.h"
+
 namespace qkv {
 
 namespace {
@@ -572,3 +578,122 @@ cudaError_t launch_decode_attn(const AttendParams &p, int kv_dtype, bool out_bf1
 }
 
 }  // namespace qkv
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of K2 for callers that may not allocate device
+// memory themselves: code embedded in a host framework that owns every device
+// buffer through its own allocator and memory plan (a GGML backend scheduler
+// with pre-sized buffers, an inference server that budgets HBM up front), where
+// a cudaMalloc/cudaFree behind the framework's back breaks its accounting or
+// is simply not permitted.  Such a caller passes its own KV pool, page table,
+// queries and output; the kernel's scratch (split-row partials, per-row merge
+// counters, the device error word) comes from the file-scope array below,
+// which every GPU that loads this library holds until the process exits.
+// ---------------------------------------------------------------------------
+namespace qkv {
+namespace {
+
+constexpr int kNoAllocMaxRows = 256;   // rows per call
+constexpr int kNoAllocMaxGrid = 160;   // CTAs per call (B200 has 148 SMs)
+constexpr size_t kNoAllocSlots = static_cast<size_t>(kNoAllocMaxRows + kNoAllocMaxGrid);
+constexpr size_t kNoAllocOBytes = kNoAllocSlots * kHq * kHeadDim * sizeof(float);   // 3.4 MB
+constexpr size_t kNoAllocMLBytes = kNoAllocSlots * kHq * 2 * sizeof(float);
+constexpr size_t kNoAllocCntBytes = static_cast<size_t>(kNoAllocMaxRows) * kHkv * sizeof(int);
+constexpr size_t kNoAllocBytes = kNoAllocOBytes + kNoAllocMLBytes + kNoAllocCntBytes + 256;
+
+// Host code must not use this name as an address: on the host it is only a
+// stand-in for the symbol.  The device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+uint8_t *g_noalloc_addr[kMaxDevices] = {};
+int g_noalloc_sms[kMaxDevices] = {};
+
+void noalloc_err(char *err, size_t len, const char *msg) {
+    if (err && len > 0) {
+        std::strncpy(err, msg, len - 1);
+        err[len - 1] = '\0';
+    }
+}
+
+// Once per device, with that device current: resolve the scratch array's
+// device address, opt the kernels into their shared-memory size, read the SM
+// count and clear the array.
+int noalloc_setup(int dev, char *err, size_t err_len) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_addr[dev]) return QKV_OK;
+    void *ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || !ptr) {
+        noalloc_err(err, err_len, "cudaGetSymbolAddress(g_noalloc_scratch) failed");
+        return QKV_ERR_CUDA;
+    }
+    int sms = 0;
+    if ((e = prepare_decode_attn()) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
+        (e = cudaMemset(ptr, 0, kNoAllocBytes)) != cudaSuccess || (e = cudaDeviceSynchronize()) != cudaSuccess) {
+        noalloc_err(err, err_len, cudaGetErrorString(e));
+        return QKV_ERR_CUDA;
+    }
+    g_noalloc_sms[dev] = sms;
+    g_noalloc_addr[dev] = static_cast<uint8_t *>(ptr);
+    return QKV_OK;
+}
+
+}  // namespace
+}  // namespace qkv
+
+extern "C" int qkv_kv_attend_noalloc(const void *pool_layer, int32_t kv_dtype, const float *scales_layer,
+                                     const int32_t *page_table, int32_t maxp, int32_t max_streams, int32_t n_pages,
+                                     int32_t n, const int32_t *slots_dev, const int32_t *lens_dev, const float *q_dev,
+                                     float *out_dev, void *stream, char *err, size_t err_len) {
+    using namespace qkv;
+    if (n < 0 || !pool_layer || !page_table || maxp <= 0 || max_streams <= 0 || n_pages <= 0 ||
+        (n > 0 && (!slots_dev || !lens_dev || !q_dev || !out_dev)) || kv_dtype < kKvF32 || kv_dtype > kKvFP8 ||
+        (kv_dtype == kKvFP8 && !scales_layer)) {
+        noalloc_err(err, err_len, "kv_attend_noalloc: bad argument");
+        return QKV_ERR_INVALID_ARG;
+    }
+    if (n > kNoAllocMaxRows) {
+        noalloc_err(err, err_len, "kv_attend_noalloc: more than 256 rows in one call (the fixed scratch limit)");
+        return QKV_ERR_CAPACITY;
+    }
+    if (n == 0) return QKV_OK;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        noalloc_err(err, err_len, "kv_attend_noalloc: no current CUDA device");
+        return QKV_ERR_NO_DEVICE;
+    }
+    int rc = noalloc_setup(dev, err, err_len);
+    if (rc != QKV_OK) return rc;
+    uint8_t *base = g_noalloc_addr[dev];
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    AttendParams p{};
+    p.n = n;
+    p.slots = slots_dev;
+    p.lens = lens_dev;
+    p.q = q_dev;
+    p.out = out_dev;
+    p.pool = pool_layer;
+    p.scales = scales_layer;
+    p.page_table = page_table;
+    p.maxp = maxp;
+    p.max_streams = max_streams;
+    p.n_pages = n_pages;
+    p.part_o = reinterpret_cast<float *>(base);
+    p.part_ml = reinterpret_cast<float *>(base + kNoAllocOBytes);
+    p.counters = reinterpret_cast<int *>(base + kNoAllocOBytes + kNoAllocMLBytes);
+    p.err = reinterpret_cast<DevError *>(base + kNoAllocOBytes + kNoAllocMLBytes + kNoAllocCntBytes);
+    p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(kHeadDim)));
+    // The merge counters must start at zero; a call that stopped early (bounded
+    // wait ran out) could have left some set.
+    cudaError_t e = cudaMemsetAsync(p.counters, 0, static_cast<size_t>(n) * kHkv * sizeof(int), st);
+    const int grid = g_noalloc_sms[dev] < kNoAllocMaxGrid ? g_noalloc_sms[dev] : kNoAllocMaxGrid;
+    if (e == cudaSuccess) e = launch_decode_attn(p, kv_dtype, false, grid, st);
+    if (e != cudaSuccess) {
+        noalloc_err(err, err_len, cudaGetErrorString(e));
+        return QKV_ERR_CUDA;
+    }
+    return QKV_OK;
+}
