@@ -123,21 +123,17 @@ def barrier(dist):
 
 
 def max_over_ranks(dist, v: float) -> float:
-    if dist is None:
-        return v
-    import torch
-    t = torch.tensor([v], device="cuda", dtype=torch.float64)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    import __graft_entry__ as ge
+    ge.load_package()
+    from qwenasr_cpp_b200 import shard
+    return shard.reduce_max(dist, v, device="cuda" if dist is not None else None)
 
 
 def sum_over_ranks(dist, v: float) -> float:
-    if dist is None:
-        return v
-    import torch
-    t = torch.tensor([v], device="cuda", dtype=torch.float64)
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
-    return float(t.item())
+    import __graft_entry__ as ge
+    ge.load_package()
+    from qwenasr_cpp_b200 import shard
+    return shard.reduce_sum(dist, v, device="cuda" if dist is not None else None)
 
 
 # ------------------------------------------------------------------ CPU legs

@@ -142,6 +142,12 @@ int qkv_generate(qkv_handle *h, const float *embeddings, int32_t tokens, int32_t
                  const int32_t *stop_ids, int32_t n_stop, int32_t *out_ids, int32_t *n_out,
                  int32_t *stopped);
 
+/* One decoder block over `tokens` rows at positions 0..tokens-1, no cache
+ * kept (a temporary stream is used and closed): x[tokens][hidden] f32 in,
+ * out[tokens][hidden] f32.  The single-layer parity probe, replacing
+ * qwenasr_text_layer_backend_forward (text-decoder.h:79-83, :1305-1390). */
+int qkv_layer_forward(qkv_handle *h, int32_t layer, int32_t tokens, const float *x, float *out);
+
 /* ---- operator level: one layer's K/V append and decode attention ----
  * Device pointers; `stream` is the cudaStream_t to launch on (NULL = the CUDA
  * legacy default stream, as in the CUDA runtime API).  Consecutive calls on a

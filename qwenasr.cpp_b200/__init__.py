@@ -63,6 +63,7 @@ SIGNATURES = {
     "qkv_prefill": (C.c_int, [_P, C.c_int32, _I32P, _I32P, _F32P, _I32P, _F32P]),
     "qkv_decode_step": (C.c_int, [_P, C.c_int32, _I32P, _I32P, _I32P, _F32P]),
     "qkv_generate": (C.c_int, [_P, _F32P, C.c_int32, C.c_int32, _I32P, C.c_int32, _I32P, _I32P, _I32P]),
+    "qkv_layer_forward": (C.c_int, [_P, C.c_int32, C.c_int32, _F32P, _F32P]),
     "qkv_kv_append": (C.c_int, [_P, C.c_int32, C.c_int32, _P, _P, _P, _P, _P]),
     "qkv_kv_attend": (C.c_int, [_P, C.c_int32, C.c_int32, _P, _P, _P, _P, _P]),
     "qkv_kv_step": (C.c_int, [_P, C.c_int32, _I32P, _P, _P, _P]),
@@ -263,6 +264,12 @@ class Decoder:
                                      _ptr(stop, C.c_int32), len(stop_ids), _ptr(out, C.c_int32), C.byref(n),
                                      C.byref(stopped)))
         return out[:n.value].copy(), bool(stopped.value)
+
+    def layer_forward(self, layer: int, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros_like(x)
+        self._check(lib.qkv_layer_forward(self.h, layer, x.shape[0], _ptr(x, C.c_float), _ptr(out, C.c_float)))
+        return out
 
     # ---- operator level (device pointers, ints) ----
     def kv_append(self, layer, n, slots_ptr, pos_ptr, qkv_ptr, q_out_ptr, stream=None):

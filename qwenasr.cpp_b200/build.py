@@ -21,11 +21,12 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "libqwenasr_b200.so"
+BIN = PKG / "bin"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
-          f"-I{ROOT / 'include'}", f"-I{CSRC}", "--expt-relaxed-constexpr"]
+          f"-I{ROOT / 'include'}", f"-I{CSRC}", f"-I{CSRC / 'adapter'}", "--expt-relaxed-constexpr"]
 
 
 def sources() -> list[Path]:
@@ -70,7 +71,22 @@ def build(clean: bool = False, verbose_ptxas: bool = False, jobs: int | None = N
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
     os.replace(tmp, LIB)
+    build_tools()
     return LIB
+
+
+def build_tools() -> None:
+    """CLI harnesses in csrc/tools, linked against the library (rpath $ORIGIN/..)."""
+    BIN.mkdir(exist_ok=True)
+    for src in sorted((CSRC / "tools").glob("*.cpp")):
+        exe = BIN / src.stem
+        if exe.exists() and exe.stat().st_mtime >= max(src.stat().st_mtime, LIB.stat().st_mtime):
+            continue
+        cmd = ["g++", "-O2", "-std=c++17", f"-I{ROOT / 'include'}", f"-I{CSRC}", f"-I{CSRC / 'adapter'}",
+               str(src), "-o", str(exe), f"-L{PKG}", "-lqwenasr_b200", "-Wl,-rpath,$ORIGIN/.."]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"tool build failed for {src.name}:\n{res.stdout}\n{res.stderr}")
 
 
 if __name__ == "__main__":

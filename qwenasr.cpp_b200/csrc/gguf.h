@@ -60,6 +60,7 @@ public:
     size_t alignment() const { return alignment_; }
     size_t data_offset() const { return data_offset_; }
     size_t file_size() const { return size_; }
+    const uint8_t *mapping() const { return map_; }
 
 private:
     int fd_ = -1;

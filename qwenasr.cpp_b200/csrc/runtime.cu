@@ -438,11 +438,13 @@ int head_and_argmax(qkv_handle *h, int n, const int *d_rows) {
 
 // All layers over `n` rows whose inputs are in h->x; decode rows attend with
 // K2, prompt rows with the causal prefill kernel.
-int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int *lens, bool prompt) {
+int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int *lens, bool prompt, int l0 = 0,
+               int l1 = -1) {
     const qkv_model_config &c = h->cfg;
     const bool bf = h->act_dtype == kActBF16;
     int rc;
-    for (int l = 0; l < c.n_layers; ++l) {
+    if (l1 < 0) l1 = c.n_layers;
+    for (int l = l0; l < l1; ++l) {
         const qkv_handle::Layer &L = h->layers[static_cast<size_t>(l)];
         CK(launch_rmsnorm(h->x, nullptr, n, c.hidden, L.attn_norm, c.rms_norm_eps, h->xn, h->act_dtype, h->stream));
         CK(launch_gemm(h->xn, h->act_dtype, L.w_qkv, h->w_dtype, h->qkv, n, kQkvDim, c.hidden, 0, h->stream));
@@ -766,6 +768,43 @@ int qkv_decode_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const i
     if ((rc = run_layers(h, n, ds, dp, dl, false))) return rc;
     if ((rc = head_and_argmax(h, n, nullptr))) return rc;
     return finish_ids(h, n, stream_ids, out_ids, out_logits);
+}
+
+int qkv_layer_forward(qkv_handle *h, int32_t layer, int32_t tokens, const float *x, float *out) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    if (!h->has_weights) return fail(h, QKV_ERR_STATE, "handle has no model weights");
+    if (layer < 0 || layer >= h->cfg.n_layers || tokens <= 0 || !x || !out)
+        return fail(h, QKV_ERR_INVALID_ARG, "layer_forward: bad layer, token count or pointer");
+    if (tokens > h->max_rows || tokens > h->rt.max_context) return fail(h, QKV_ERR_CAPACITY, "layer_forward: too many tokens");
+    CK(cudaSetDevice(h->device));
+    int32_t s = -1;
+    int rc = qkv_stream_open(h, &s);
+    if (rc) return rc;
+    int *hs = row_stage(h), *hp = hs + tokens;
+    for (int t = 0; t < tokens; ++t) {
+        hs[t] = s;
+        hp[t] = t;
+    }
+    rc = grow_streams(h, 1, &s, &tokens, h->stream);
+    if (rc == QKV_OK) rc = row_upload(h, hs, static_cast<size_t>(2 * tokens), h->stream);
+    if (rc == QKV_OK) {
+        const size_t bytes = static_cast<size_t>(tokens) * h->cfg.hidden * sizeof(float);
+        cudaError_t e = cudaMemcpyAsync(h->x, x, bytes, cudaMemcpyHostToDevice, h->stream);
+        if (e != cudaSuccess) rc = cuda_fail(h, e, "layer_forward upload");
+        if (rc == QKV_OK) rc = run_layers(h, tokens, h->d_rowbuf, h->d_rowbuf + tokens, nullptr, true, layer, layer + 1);
+        if (rc == QKV_OK) {
+            e = cudaMemcpyAsync(out, h->x, bytes, cudaMemcpyDeviceToHost, h->stream);
+            if (e != cudaSuccess) rc = cuda_fail(h, e, "layer_forward download");
+        }
+        if (rc == QKV_OK) rc = check_device_error(h);
+    }
+    const std::string keep = h->last_error;
+    const int rc2 = qkv_stream_close(h, s);
+    if (rc) {
+        h->last_error = keep;
+        return rc;
+    }
+    return rc2;
 }
 
 int qkv_generate(qkv_handle *h, const float *embeddings, int32_t tokens, int32_t max_new_tokens, const int32_t *stop_ids,

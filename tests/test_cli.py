@@ -1,0 +1,67 @@
+"""The decoder harness CLI (qwen-asr-text-decode) speaks the reference tool's
+key=value protocol (tools/qwen-asr-text-layer.cpp:487-517) and is driven here
+as a subprocess, the way the reference's benchmarks/check_text_*.py drive
+its binary.  GPU cases compare against the reference-scalar fixtures."""
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from conftest import rel_err
+
+ROOT = Path(__file__).resolve().parents[1]
+CLI = ROOT / "qwenasr.cpp_b200" / "bin" / "qwen-asr-text-decode"
+GOLDEN = ROOT / "tests" / "golden"
+
+
+def run(args):
+    p = subprocess.run([str(CLI), *map(str, args)], capture_output=True, text=True, timeout=600)
+    kv = dict(line.split("=", 1) for line in p.stdout.splitlines() if "=" in line)
+    return p.returncode, kv, p.stderr
+
+
+@pytest.fixture(scope="module")
+def case(tiny_files, tmp_path_factory):
+    cfg, files = tiny_files
+    g = np.load(GOLDEN / "tiny_one_plus.npz")
+    d = tmp_path_factory.mktemp("cli")
+    inp = d / "input.f32"
+    g["x"].astype(np.float32).tofile(inp)
+    return files[("f32", "one_plus")], inp, g, d
+
+
+def test_cli_usage_and_cpu_device_rejected(case):
+    path, inp, g, d = case
+    rc, kv, err = run([path, inp, "--generate", "2", "--device", "cpu"])
+    assert rc == 1 and "GPU only" in err
+    rc, kv, err = run([path])
+    assert rc == 2
+
+
+@pytest.mark.gpu
+def test_cli_generate_matches_reference(case):
+    path, inp, g, d = case
+    rc, kv, err = run([path, inp, "--generate", "16", "--no-stop"])
+    assert rc == 0, err
+    assert kv["mode"] == "generate" and kv["prompt_tokens"] == str(g["x"].shape[0])
+    assert [int(t) for t in kv["generated_ids"].split(",")] == g["ref_ids"].tolist()
+    rc, kv, err = run([path, inp, "--generate", "16", "--stop-ids", str(int(g["stop_id"]))])
+    assert rc == 0 and kv["stopped"] == "true"
+    assert [int(t) for t in kv["generated_ids"].split(",")] == g["ref_ids_stop"].tolist()
+
+
+@pytest.mark.gpu
+def test_cli_prefill_and_layer_outputs(case):
+    path, inp, g, d = case
+    out = d / "logits.f32"
+    rc, kv, err = run([path, inp, "--prefill", "--out", out])
+    assert rc == 0, err
+    logits = np.fromfile(out, np.float32)
+    assert rel_err(logits, g["ref_prefill_logits"]) < 1e-3
+    assert int(kv["top_id"]) == int(np.argmax(g["ref_prefill_logits"]))
+    out = d / "layer0.f32"
+    rc, kv, err = run([path, inp, "--layer", "0", "--out", out])
+    assert rc == 0, err
+    vals = np.fromfile(out, np.float32).reshape(g["ref_layer0"].shape)
+    assert rel_err(vals, g["ref_layer0"]) < 1e-4
