@@ -34,6 +34,10 @@ STREAMS_PER_GPU = 256
 CTX_LO, CTX_HI = 64, 4096
 WORKLOAD_SEED = 1004          # 1000 + config index
 METRIC = "decode tokens/s (KV append+GQA attn) & KV-read HBM GB/s vs 8 TB/s, 1-8 B200"
+# DRAM bytes (read + write) of one K2 launch on this workload, from the ncu
+# capture summarised in profiles/decode_attn_k2_config4.md (same 256 streams
+# and contexts; the capture held 2 layers of cache, a launch reads one).
+K2_NCU_TRAFFIC_BYTES = 1_017_933_000 + 5_662_720
 
 
 def peaks() -> dict:
@@ -313,7 +317,7 @@ def run_ours(args) -> int:
             "kv_read_gbs_step": round(kv_bytes_per_launch * N_LAYERS / (ms_max / args.steps / 1e3) / 1e9, 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved_gbs / pk["hbm_gbs"], 4), "frac_of_8tbs": round(achieved_gbs / 8000, 4),
-                         "traffic": None, "kernel": "decode_attn_kernel (K2)",
+                         "traffic": K2_NCU_TRAFFIC_BYTES, "kernel": "decode_attn_kernel (K2)",
                          "launch_ms": round(attn_ms, 4), "bytes_per_launch": kv_bytes_per_launch,
                          "peak_source": pk["source"]},
             "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s",
@@ -330,12 +334,80 @@ def run_ours(args) -> int:
     return 0
 
 
+def run_model(args) -> int:
+    """Config 2: 0.6B, bf16 weights + bf16 paged cache, 32 streams/GPU, prompts
+    U[100, 400] with 90% audio rows, greedy decode; value = decode tokens/s."""
+    import tempfile
+
+    import torch
+
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    synth = ge.load_synth()
+    rank, local, world, dist = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    cfg = dict(synth.QWEN3_ASR_0_6B)
+    n_streams = 32
+    steps = args.steps
+    tmpdir = Path(os.environ.get("QWENASR_BENCH_TMP", "/dev/shm" if Path("/dev/shm").is_dir() else tempfile.gettempdir()))
+    path = tmpdir / f"qwen3asr_0p6b_bf16_seed0_r{rank}.gguf"
+    t0 = time.perf_counter()
+    if not path.exists():
+        synth.write_gguf(path, cfg, seed=0, weights="bf16", norm_init="normal", tokenizer=False)
+    gen_s = time.perf_counter() - t0
+    embd = synth.read_gguf(path)["text.token_embd.weight"]
+    prompts = synth.config2_prompts(embd, n_streams, seed=1002, gpu=rank)
+    max_ctx = max(p.shape[0] for p in prompts) + args.warmup + steps + 8
+    rt = pkg.runtime_config(device=local, weight_dtype=pkg.BF16, kv_dtype=pkg.BF16, max_streams=n_streams,
+                            max_context=max_ctx, max_batch_tokens=sum(p.shape[0] for p in prompts),
+                            page_order_seed=1002 + rank)
+    dec = pkg.Decoder.from_gguf(path, rt, cfg)
+    streams = [dec.open() for _ in prompts]
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    dec.prefill(streams, prompts)
+    prefill_s = time.perf_counter() - t1
+    for _ in range(args.warmup):
+        dec.decode_step(streams)
+    launches0 = dec.launches()
+    sampler = ClockSampler(local)
+    barrier(dist)
+    with sampler:
+        t2 = time.perf_counter()
+        for _ in range(steps):
+            dec.decode_step(streams)
+        dt = time.perf_counter() - t2
+    launches = dec.launches() - launches0
+    dt_max = max_over_ranks(dist, dt)
+    tokens = sum_over_ranks(dist, float(n_streams * steps))
+    if rank == 0:
+        line = {
+            "metric": "greedy decode tokens/s (full 0.6B step: KV path + projections + LM head)",
+            "value": round(tokens / dt_max, 2), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": round(dt_max / steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config2: Qwen3-ASR-0.6B bf16 weights + bf16 paged KV, 32 streams/GPU, "
+                                   "prompts U[100,400] (90% audio rows), greedy decode",
+                       "prompt_tokens": int(sum(p.shape[0] for p in prompts)), "prefill_s": round(prefill_s, 3),
+                       "gguf_write_s": round(gen_s, 1)},
+            "e2e": {"value": round(tokens / dt_max, 2), "unit": "tokens/s", "h2d_bytes_per_step": n_streams * 4 * 4,
+                    "d2h_bytes_per_step": n_streams * 4, "note": "qkv_decode_step with host id buffers"},
+            "gpu_launches": int(launches), "clocks": sampler.summary()}
+        print(json.dumps(line), flush=True)
+    dec.close()
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=("kv", "model"), default="kv",
+                    help="kv: config 4 KV step (default); model: config 2 full greedy decode (0.6B bf16)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="layers of cache (28 = the workload; fewer only for small profiling captures)")
@@ -344,6 +416,8 @@ def main() -> int:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "model":
+        return run_model(args)
     return run_ours(args)
 
 

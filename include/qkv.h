@@ -165,6 +165,13 @@ int qkv_kv_append(qkv_handle *h, int32_t layer, int32_t n, const int32_t *slots_
 int qkv_kv_attend(qkv_handle *h, int32_t layer, int32_t n, const int32_t *slots_dev,
                   const int32_t *lens_dev, const float *q_dev, float *out_dev, void *stream);
 
+/* Operator: C[m][n] (+)= X[m][k] . W[n][k]^T on the tensor cores (tcgen05,
+ * bf16 X and W row-major, f32 C; k a multiple of 64).  accumulate = 0 stores,
+ * 1 adds into C.  The decoder's projections (text-decoder.cpp:371-373, 465,
+ * 469-472, 476-493).  Device pointers, current device, `stream` as above. */
+int qkv_gemm_bf16(const void *x, const void *w, float *c, int32_t m, int32_t n, int32_t k, int32_t accumulate,
+                  void *stream);
+
 /* One KV-cache step of the microbench: for each of the n streams append one
  * token and attend, for every layer.  qkv[n_layers][n][Hq*D+2*Hkv*D] f32,
  * out[n_layers][n][Hq*D] f32 (layer-major), device pointers; the streams'

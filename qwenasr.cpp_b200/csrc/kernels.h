@@ -94,6 +94,12 @@ cudaError_t launch_embed(const int *ids, int n, const void *embd, int w_dtype, i
 // epilogue 0: store, 1: accumulate into C (residual add).
 cudaError_t launch_gemm(const void *X, int x_dtype, const void *W, int w_dtype, float *C, int M, int N, int K,
                         int epilogue, cudaStream_t st);
+// tcgen05 path (bf16 X and W, K % 64 == 0): C (+)= X . W^T, split-K with f32
+// red.add when the tile grid is smaller than the SM count.
+cudaError_t prepare_gemm_tc();
+bool gemm_tc_supported(int M, int N, int K);
+cudaError_t launch_gemm_tc(const void *X, const void *W, float *C, int M, int N, int K, int accumulate, int num_sms,
+                           DevError *err, cudaStream_t st);
 // out[m][j] = silu(gu[m][j]) * gu[m][F + j]
 cudaError_t launch_swiglu(const float *gu, int M, int F, void *out, int out_dtype, cudaStream_t st);
 // GGUF tensor data (ggml type 0 f32, 1 f16, 30 bf16 passed as 2) -> weight dtype.

@@ -6,6 +6,7 @@
 #include <cmath>
 #include <cstring>
 #include <memory>
+#include <mutex>
 
 #include "gguf.h"
 
@@ -163,6 +164,7 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
     CK(cudaMemset(h->d_err, 0, sizeof(DevError)));
     CK(cudaMallocHost(&h->h_err, sizeof(DevError)));
     CK(prepare_decode_attn());
+    CK(prepare_gemm_tc());
     CK(cudaStreamSynchronize(h->stream));
     return QKV_OK;
 }
@@ -426,11 +428,19 @@ int layer_kv(qkv_handle *h, int layer, int n, const int *slots, const int *pos, 
     return QKV_OK;
 }
 
+// Projection C (+)= X . W^T: tcgen05 when activations and weights are bf16,
+// the SIMT kernel otherwise (f32 parity mode).
+cudaError_t gemm(qkv_handle *h, const void *X, const void *W, float *C, int M, int N, int K, int accumulate) {
+    if (h->act_dtype == kActBF16 && h->w_dtype == kActBF16 && gemm_tc_supported(M, N, K))
+        return launch_gemm_tc(X, W, C, M, N, K, accumulate, h->num_sms, h->d_err, h->stream);
+    return launch_gemm(X, h->act_dtype, W, h->w_dtype, C, M, N, K, accumulate, h->stream);
+}
+
 // Logits of the rows listed in d_rows (indices into x) -> ids (device), logits into h->logits.
 int head_and_argmax(qkv_handle *h, int n, const int *d_rows) {
     const qkv_model_config &c = h->cfg;
     CK(launch_rmsnorm(h->x, d_rows, n, c.hidden, h->out_norm, c.rms_norm_eps, h->xn, h->act_dtype, h->stream));
-    CK(launch_gemm(h->xn, h->act_dtype, h->w_out, h->w_dtype, h->logits, n, c.vocab, c.hidden, 0, h->stream));
+    CK(gemm(h, h->xn, h->w_out, h->logits, n, c.vocab, c.hidden, 0));
     CK(launch_argmax(h->logits, n, c.vocab, h->d_out_ids, h->stream));
     h->launches += 3;
     return QKV_OK;
@@ -447,7 +457,7 @@ int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int
     for (int l = l0; l < l1; ++l) {
         const qkv_handle::Layer &L = h->layers[static_cast<size_t>(l)];
         CK(launch_rmsnorm(h->x, nullptr, n, c.hidden, L.attn_norm, c.rms_norm_eps, h->xn, h->act_dtype, h->stream));
-        CK(launch_gemm(h->xn, h->act_dtype, L.w_qkv, h->w_dtype, h->qkv, n, kQkvDim, c.hidden, 0, h->stream));
+        CK(gemm(h, h->xn, L.w_qkv, h->qkv, n, kQkvDim, c.hidden, 0));
         if (!prompt) {
             if ((rc = layer_kv(h, l, n, slots, pos, lens, h->qkv, h->q, h->attn, bf, L.q_norm, L.k_norm, h->stream)))
                 return rc;
@@ -476,11 +486,11 @@ int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int
             CK(launch_prefill_attn(pp, h->rt.kv_dtype, bf, h->stream));
             h->launches += 2;
         }
-        CK(launch_gemm(h->attn, h->act_dtype, L.w_o, h->w_dtype, h->x, n, c.hidden, kQDim, 1, h->stream));
+        CK(gemm(h, h->attn, L.w_o, h->x, n, c.hidden, kQDim, 1));
         CK(launch_rmsnorm(h->x, nullptr, n, c.hidden, L.ffn_norm, c.rms_norm_eps, h->xn, h->act_dtype, h->stream));
-        CK(launch_gemm(h->xn, h->act_dtype, L.w_gu, h->w_dtype, h->gu, n, 2 * c.intermediate, c.hidden, 0, h->stream));
+        CK(gemm(h, h->xn, L.w_gu, h->gu, n, 2 * c.intermediate, c.hidden, 0));
         CK(launch_swiglu(h->gu, n, c.intermediate, h->act, h->act_dtype, h->stream));
-        CK(launch_gemm(h->act, h->act_dtype, L.w_down, h->w_dtype, h->x, n, c.hidden, c.intermediate, 1, h->stream));
+        CK(gemm(h, h->act, L.w_down, h->x, n, c.hidden, c.intermediate, 1));
         h->launches += 7;
     }
     return QKV_OK;
@@ -1014,6 +1024,23 @@ int qkv_last_launches(const qkv_handle *h, int64_t *kernels) {
     if (!h || !kernels) return QKV_ERR_INVALID_ARG;
     *kernels = h->launches;
     return QKV_OK;
+}
+
+int qkv_gemm_bf16(const void *x, const void *w, float *c, int32_t m, int32_t n, int32_t k, int32_t accumulate,
+                  void *stream) {
+    if (!x || !w || !c || m < 0 || n < 0 || k <= 0 || k % 64 != 0) return QKV_ERR_INVALID_ARG;
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return QKV_ERR_NO_DEVICE;
+    static std::once_flag once;
+    static cudaError_t prep = cudaSuccess;
+    std::call_once(once, [] { prep = prepare_gemm_tc(); });
+    if (prep != cudaSuccess) return QKV_ERR_CUDA;
+    if (!gemm_tc_supported(m, n, k)) return QKV_ERR_INVALID_ARG;
+    return launch_gemm_tc(x, w, c, m, n, k, accumulate ? 1 : 0, sms, nullptr, static_cast<cudaStream_t>(stream)) ==
+                   cudaSuccess
+               ? QKV_OK
+               : QKV_ERR_CUDA;
 }
 
 int qkv_gguf_tensor(const char *gguf_path, const char *name, int64_t *ne_out, int32_t *n_dims, int32_t *ggml_type,

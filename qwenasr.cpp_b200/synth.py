@@ -172,7 +172,7 @@ def write_gguf(path: str | Path, cfg: ModelConfig | dict, seed: int = 0, std: fl
         f.write(head + b"\0" * pad)
         for name, shape, kind in specs:
             a = _gen_tensor(rng, shape, kind, std, norm_init, weights == "bf16")
-            f.write(a.tobytes())
+            f.write(memoryview(np.ascontiguousarray(a)).cast("B"))
             f.write(b"\0" * ((-a.nbytes) % GGUF_ALIGN))
     return path
 
