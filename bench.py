@@ -346,17 +346,25 @@ def run_model(args) -> int:
     synth = ge.load_synth()
     rank, local, world, dist = dist_setup(args.gpus)
     torch.cuda.set_device(local)
-    cfg = dict(synth.QWEN3_ASR_0_6B)
-    n_streams = 32
+    big = args.workload == "model3"
+    cfg = dict(synth.QWEN3_ASR_1_7B if big else synth.QWEN3_ASR_0_6B)
+    n_streams = 64 if big else 32
     steps = args.steps
     tmpdir = Path(os.environ.get("QWENASR_BENCH_TMP", "/dev/shm" if Path("/dev/shm").is_dir() else tempfile.gettempdir()))
-    path = tmpdir / f"qwen3asr_0p6b_bf16_seed0_r{rank}.gguf"
+    path = tmpdir / f"qwen3asr_{'1p7b' if big else '0p6b'}_bf16_seed0_r{rank}.gguf"
     t0 = time.perf_counter()
     if not path.exists():
         synth.write_gguf(path, cfg, seed=0, weights="bf16", norm_init="normal", tokenizer=False)
     gen_s = time.perf_counter() - t0
     embd = synth.read_gguf(path)["text.token_embd.weight"]
-    prompts = synth.config2_prompts(embd, n_streams, seed=1002, gpu=rank)
+    if big:   # config 3: 390 audio rows + 20 text tokens per stream
+        prompts = []
+        for sidx in range(n_streams):
+            rng = np.random.default_rng(1003 * 1_000_003 + rank * 65_536 + sidx)
+            x, _ = synth.prompt_rows(embd, 410, rng, audio_rows=390, audio_start=9)
+            prompts.append(x)
+    else:
+        prompts = synth.config2_prompts(embd, n_streams, seed=1002, gpu=rank)
     max_ctx = max(p.shape[0] for p in prompts) + args.warmup + steps + 8
     rt = pkg.runtime_config(device=local, weight_dtype=pkg.BF16, kv_dtype=pkg.BF16, max_streams=n_streams,
                             max_context=max_ctx, max_batch_tokens=sum(p.shape[0] for p in prompts),
@@ -382,12 +390,14 @@ def run_model(args) -> int:
     tokens = sum_over_ranks(dist, float(n_streams * steps))
     if rank == 0:
         line = {
-            "metric": "greedy decode tokens/s (full 0.6B step: KV path + projections + LM head)",
+            "metric": f"greedy decode tokens/s (full {'1.7B' if big else '0.6B'} step: KV path + projections + LM head)",
             "value": round(tokens / dt_max, 2), "unit": "tokens/s", "n_gpus": world, "steps": steps,
             "warmup": args.warmup, "ms_per_step": round(dt_max / steps * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "config2: Qwen3-ASR-0.6B bf16 weights + bf16 paged KV, 32 streams/GPU, "
-                                   "prompts U[100,400] (90% audio rows), greedy decode",
+            "config": {"workload": ("config3: Qwen3-ASR-1.7B bf16 weights + bf16 paged KV, 64 streams/GPU, "
+                                    "390 audio rows + 20 text tokens, greedy decode") if big else
+                                   ("config2: Qwen3-ASR-0.6B bf16 weights + bf16 paged KV, 32 streams/GPU, "
+                                    "prompts U[100,400] (90% audio rows), greedy decode"),
                        "prompt_tokens": int(sum(p.shape[0] for p in prompts)), "prefill_s": round(prefill_s, 3),
                        "gguf_write_s": round(gen_s, 1)},
             "e2e": {"value": round(tokens / dt_max, 2), "unit": "tokens/s", "h2d_bytes_per_step": n_streams * 4 * 4,
@@ -406,8 +416,9 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("kv", "model"), default="kv",
-                    help="kv: config 4 KV step (default); model: config 2 full greedy decode (0.6B bf16)")
+    ap.add_argument("--workload", choices=("kv", "model", "model3"), default="kv",
+                    help="kv: config 4 KV step (default); model: config 2 full greedy decode (0.6B bf16, 32 "
+                         "streams); model3: config 3 (1.7B bf16, 64 streams, 390 audio + 20 text tokens)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="layers of cache (28 = the workload; fewer only for small profiling captures)")
@@ -416,7 +427,7 @@ def main() -> int:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
-    if args.workload == "model":
+    if args.workload in ("model", "model3"):
         return run_model(args)
     return run_ours(args)
 

@@ -258,13 +258,7 @@ cudaError_t launch_embed(const int *ids, int n, const void *embd, int w_dtype, i
 template <typename TX, typename TW>
 static cudaError_t gemm_t(const TX *X, const TW *W, float *C, int M, int N, int K, int epilogue, cudaStream_t st) {
     if (M <= 4) {
-        const size_t sm = static_cast<size_t>(M) * K * sizeof(float);
-        static_assert(sizeof(float) == 4, "");
-        if (sm > 48 * 1024) {
-            cudaError_t e = cudaFuncSetAttribute(gemv_kernel<TX, TW, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 static_cast<int>(sm));
-            if (e != cudaSuccess) return e;
-        }
+        const size_t sm = static_cast<size_t>(M) * K * sizeof(float);   // opted in by prepare_dense
         gemv_kernel<TX, TW, 4><<<(N + 7) / 8, 256, sm, st>>>(X, W, C, M, N, K, epilogue);
         return cudaGetLastError();
     }
@@ -289,18 +283,28 @@ static cudaError_t gemm_t(const TX *X, const TW *W, float *C, int M, int N, int 
     return cudaGetLastError();
 }
 
+cudaError_t prepare_dense(int max_k) {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+        sms > 0)
+        g_num_sms = sms;
+    const int sm = 4 * max_k * static_cast<int>(sizeof(float));
+    cudaError_t e;
+    if ((e = cudaFuncSetAttribute(gemv_kernel<float, float, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm)) != cudaSuccess)
+        return e;
+    if ((e = cudaFuncSetAttribute(gemv_kernel<__nv_bfloat16, __nv_bfloat16, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm)) !=
+        cudaSuccess)
+        return e;
+    if ((e = cudaFuncSetAttribute(gemv_kernel<float, __nv_bfloat16, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm)) !=
+        cudaSuccess)
+        return e;
+    return cudaFuncSetAttribute(gemv_kernel<__nv_bfloat16, float, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+}
+
 cudaError_t launch_gemm(const void *X, int x_dtype, const void *W, int w_dtype, float *C, int M, int N, int K,
                         int epilogue, cudaStream_t st) {
     if (M <= 0 || N <= 0) return cudaSuccess;
     if (K % BK != 0) return cudaErrorInvalidValue;
-    static bool sm_known = false;
-    if (!sm_known) {
-        int dev = 0, sms = 0;
-        if (cudaGetDevice(&dev) == cudaSuccess &&
-            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms > 0)
-            g_num_sms = sms;
-        sm_known = true;
-    }
     if (x_dtype == kActF32 && w_dtype == kActF32)
         return gemm_t(static_cast<const float *>(X), static_cast<const float *>(W), C, M, N, K, epilogue, st);
     if (x_dtype == kActBF16 && w_dtype == kActBF16)

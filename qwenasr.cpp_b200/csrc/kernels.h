@@ -100,6 +100,8 @@ cudaError_t prepare_gemm_tc();
 bool gemm_tc_supported(int M, int N, int K);
 cudaError_t launch_gemm_tc(const void *X, const void *W, float *C, int M, int N, int K, int accumulate, int num_sms,
                            DevError *err, cudaStream_t st);
+// Shared-memory opt-in of the dense kernels for rows up to max_k wide.
+cudaError_t prepare_dense(int max_k);
 // out[m][j] = silu(gu[m][j]) * gu[m][F + j]
 cudaError_t launch_swiglu(const float *gu, int M, int F, void *out, int out_dtype, cudaStream_t st);
 // GGUF tensor data (ggml type 0 f32, 1 f16, 30 bf16 passed as 2) -> weight dtype.

@@ -5,6 +5,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <functional>
 #include <memory>
 #include <mutex>
 
@@ -165,6 +166,8 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
     CK(cudaMallocHost(&h->h_err, sizeof(DevError)));
     CK(prepare_decode_attn());
     CK(prepare_gemm_tc());
+    CK(prepare_dense(std::max(c.hidden, std::max(c.intermediate, kQDim))));
+    (void)gemm_tc_supported(1, 1, 64);   // resolve the tensor-map encoder before any capture
     CK(cudaStreamSynchronize(h->stream));
     return QKV_OK;
 }
@@ -184,6 +187,8 @@ void destroy(qkv_handle *h) {
     cudaFree(h->d_rowbuf); cudaFree(h->d_out_ids); cudaFree(h->part_o); cudaFree(h->part_ml);
     cudaFree(h->counters); cudaFree(h->d_err);
     cudaFreeHost(h->h_page_table); cudaFreeHost(h->h_rowbuf); cudaFreeHost(h->h_out_ids); cudaFreeHost(h->h_err);
+    for (auto &kv : h->decode_graphs) cudaGraphExecDestroy(kv.second.exec);
+    for (auto &kv : h->kv_graphs) cudaGraphExecDestroy(kv.second.exec);
     for (auto &ev : h->row_ev) {
         if (ev) cudaEventDestroy(ev);
     }
@@ -357,6 +362,37 @@ int *row_stage(qkv_handle *h) {
 int row_upload(qkv_handle *h, const int *host, size_t count, cudaStream_t st) {
     CK(cudaMemcpyAsync(h->d_rowbuf, host, count * sizeof(int), cudaMemcpyHostToDevice, st));
     CK(cudaEventRecord(h->row_ev[h->row_slot], st));
+    return QKV_OK;
+}
+
+// Record `body` (kernel launches on h->stream) into a graph and instantiate it.
+int capture_graph(qkv_handle *h, const std::function<int()> &body, qkv_handle::Graph *out) {
+    const int64_t launches_before = h->launches;
+    CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+    const int rc = body();
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(h->stream, &g);
+    h->launches = launches_before;
+    if (rc != QKV_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return cuda_fail(h, e, "cudaStreamEndCapture");
+    size_t n_nodes = 0;
+    cudaGraphGetNodes(g, nullptr, &n_nodes);
+    std::vector<cudaGraphNode_t> nodes(n_nodes);
+    cudaGraphGetNodes(g, nodes.data(), &n_nodes);
+    int64_t kernels = 0;
+    for (cudaGraphNode_t nd : nodes) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels;
+    }
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ei = cudaGraphInstantiate(&exec, g, 0);
+    cudaGraphDestroy(g);
+    if (ei != cudaSuccess) return cuda_fail(h, ei, "cudaGraphInstantiate");
+    out->exec = exec;
+    out->kernels = kernels;
     return QKV_OK;
 }
 
@@ -773,10 +809,25 @@ int qkv_decode_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const i
     if ((rc = grow_streams(h, n, stream_ids, nullptr, h->stream))) return rc;
     int *ds = h->d_rowbuf, *dp = ds + n, *dl = dp + n, *di = dl + n;
     if ((rc = row_upload(h, hs, static_cast<size_t>(4 * n), h->stream))) return rc;
-    CK(launch_embed(di, n, h->embd, h->w_dtype, h->cfg.hidden, h->cfg.vocab, h->x, h->d_err, h->stream));
-    h->launches += 1;
-    if ((rc = run_layers(h, n, ds, dp, dl, false))) return rc;
-    if ((rc = head_and_argmax(h, n, nullptr))) return rc;
+    auto body = [&]() -> int {
+        CK(launch_embed(di, n, h->embd, h->w_dtype, h->cfg.hidden, h->cfg.vocab, h->x, h->d_err, h->stream));
+        h->launches += 1;
+        int r;
+        if ((r = run_layers(h, n, ds, dp, dl, false))) return r;
+        return head_and_argmax(h, n, nullptr);
+    };
+    if (h->use_graphs) {
+        auto it = h->decode_graphs.find(n);
+        if (it == h->decode_graphs.end()) {
+            qkv_handle::Graph g;
+            if ((rc = capture_graph(h, body, &g))) return rc;
+            it = h->decode_graphs.emplace(n, g).first;
+        }
+        CK(cudaGraphLaunch(it->second.exec, h->stream));
+        h->launches += it->second.kernels;
+    } else if ((rc = body())) {
+        return rc;
+    }
     return finish_ids(h, n, stream_ids, out_ids, out_logits);
 }
 
@@ -901,12 +952,31 @@ int qkv_kv_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const float
     int *ds = h->d_rowbuf, *dp = ds + n, *dl = dp + n;
     if ((rc = row_upload(h, hs, static_cast<size_t>(3 * n), st))) return rc;
     const size_t in_stride = static_cast<size_t>(n) * kQkvDim, out_stride = static_cast<size_t>(n) * kQDim;
-    for (int l = 0; l < h->cfg.n_layers; ++l) {
-        const qkv_handle::Layer &L = h->layers[static_cast<size_t>(l)];
-        if ((rc = layer_kv(h, l, n, ds, dp, dl, qkv_dev + in_stride * l, h->q, out_dev + out_stride * l, false, L.q_norm,
-                           L.k_norm, st)))
-            return rc;
+    auto body = [&](cudaStream_t on) -> int {
+        for (int l = 0; l < h->cfg.n_layers; ++l) {
+            const qkv_handle::Layer &L = h->layers[static_cast<size_t>(l)];
+            int r;
+            if ((r = layer_kv(h, l, n, ds, dp, dl, qkv_dev + in_stride * l, h->q, out_dev + out_stride * l, false,
+                              L.q_norm, L.k_norm, on)))
+                return r;
+        }
+        return QKV_OK;
+    };
+    if (!h->use_graphs) return body(st);
+    const auto key = std::make_tuple(n, static_cast<const void *>(qkv_dev), static_cast<const void *>(out_dev));
+    auto it = h->kv_graphs.find(key);
+    if (it == h->kv_graphs.end()) {
+        if (h->kv_graphs.size() >= 64) {
+            CK(cudaDeviceSynchronize());
+            for (auto &kv : h->kv_graphs) cudaGraphExecDestroy(kv.second.exec);
+            h->kv_graphs.clear();
+        }
+        qkv_handle::Graph g;
+        if ((rc = capture_graph(h, [&]() { return body(h->stream); }, &g))) return rc;
+        it = h->kv_graphs.emplace(key, g).first;
     }
+    CK(cudaGraphLaunch(it->second.exec, st));
+    h->launches += it->second.kernels;
     return QKV_OK;
 }
 

@@ -9,7 +9,9 @@
 
 #include <cuda_runtime.h>
 
+#include <map>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include "kernels.h"
@@ -75,6 +77,16 @@ struct qkv_handle {
 
     std::string last_error;
     int64_t launches = 0;
+
+    // Captured device work, replayed each call: decode step per batch size,
+    // microbench KV step per (batch size, qkv buffer, out buffer).
+    struct Graph {
+        cudaGraphExec_t exec = nullptr;
+        int64_t kernels = 0;
+    };
+    std::map<int, Graph> decode_graphs;
+    std::map<std::tuple<int, const void *, const void *>, Graph> kv_graphs;
+    bool use_graphs = true;
 };
 
 namespace qkv {
