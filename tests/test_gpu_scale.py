@@ -1,0 +1,89 @@
+"""Full-size parity: the Qwen3-ASR-0.6B architecture (28 layers, hidden 1024,
+vocab 151936) on seeded bf16-rounded N(0, 0.02) weights and config-1 prompts
+(160 tokens, 143 N(0,1) audio rows at positions 9..151).
+
+The CPU oracle (bit-exact with the reference's scalar path) runs the
+reference's cached greedy loop in spawned worker processes; the device path is
+teacher-forced with the oracle's ids so every step compares logits on an
+identical prefix.  Bars: f32 weights + f32 cache -> logits within 1e-3
+relative and identical greedy ids; bf16 weights + bf16 cache -> >= 99% greedy
+agreement with the max logit deviation printed."""
+import multiprocessing as mp
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from conftest import rel_err
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+N_PROMPTS = 2
+N_STEPS = 24
+
+
+def _oracle_job(args):
+    import sys
+    path, cfg, seed, n_steps, root = args
+    sys.path.insert(0, root)
+    import __graft_entry__ as ge
+    from oracle import oracle as checker
+    synth = ge.load_synth()
+    tensors = synth.read_gguf(path)
+    x = synth.config1_prompt(tensors["text.token_embd.weight"], seed=seed)
+    r = checker.OracleModel(cfg, tensors).generate(x, n_steps, want_logits=True)
+    return x, r["ids"], r["logits"]
+
+
+@pytest.fixture(scope="module")
+def scale_case(synth, tmp_path_factory):
+    cfg = dict(synth.QWEN3_ASR_0_6B)
+    path = synth.write_gguf(tmp_path_factory.mktemp("scale") / "qwen3asr_0p6b.gguf", cfg, seed=0, weights="bf16",
+                            tokenizer=False)
+    root = str(Path(__file__).resolve().parents[1])
+    with mp.get_context("spawn").Pool(N_PROMPTS) as pool:
+        refs = pool.map(_oracle_job, [(str(path), cfg, 1001 + i, N_STEPS, root) for i in range(N_PROMPTS)])
+    return cfg, path, refs
+
+
+def _teacher_forced(pkg, path, refs, w, kv):
+    rt = pkg.runtime_config(device=0, weight_dtype=w, kv_dtype=kv, max_streams=N_PROMPTS, max_context=256,
+                            max_batch_tokens=N_PROMPTS * 160)
+    worst, agree, total = 0.0, 0, 0
+    with pkg.Decoder.from_gguf(path, rt) as dec:
+        streams = [dec.open() for _ in refs]
+        ids, logits = dec.prefill(streams, [r[0] for r in refs], want_logits=True)
+        for step in range(N_STEPS):
+            for i, (_, ref_ids, ref_logits) in enumerate(refs):
+                worst = max(worst, rel_err(logits[i], ref_logits[step]))
+                agree += int(ids[i] == ref_ids[step])
+                total += 1
+            if step + 1 < N_STEPS:
+                ids, logits = dec.decode_step(streams, in_ids=[int(r[1][step]) for r in refs], want_logits=True)
+    return agree / total, worst
+
+
+def test_f32_full_size_logits_and_ids(pkg, scale_case):
+    cfg, path, refs = scale_case
+    agree, worst = _teacher_forced(pkg, path, refs, pkg.F32, pkg.F32)
+    print(f"0.6B f32: max relative logit deviation {worst:.3e}, greedy agreement {agree:.4f}")
+    assert worst < 1e-3 and agree == 1.0
+    rt = pkg.runtime_config(device=0, max_streams=1, max_context=256)
+    with pkg.Decoder.from_gguf(path, rt) as dec:      # the reference loop, free-running
+        ids, stopped = dec.generate(refs[0][0], N_STEPS)
+    assert ids.tolist() == refs[0][1].tolist()
+
+
+def test_bf16_full_size_agreement(pkg, scale_case):
+    cfg, path, refs = scale_case
+    agree, worst = _teacher_forced(pkg, path, refs, pkg.BF16, pkg.BF16)
+    print(f"0.6B bf16 weights+cache: greedy agreement {agree:.4f}, max relative logit deviation {worst:.3e}")
+    assert agree >= 0.99
+
+
+def test_fp8_full_size_deviation(pkg, scale_case):
+    cfg, path, refs = scale_case
+    agree, worst = _teacher_forced(pkg, path, refs, pkg.BF16, pkg.FP8)
+    print(f"0.6B bf16 weights + fp8 cache: greedy agreement {agree:.4f}, max relative logit deviation {worst:.3e}")
+    assert agree >= 0.9
