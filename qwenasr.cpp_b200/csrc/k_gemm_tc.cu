@@ -349,6 +349,10 @@ cudaError_t launch_bn(const void *X, const void *W, float *C, int M, int N, int 
 
 }  // namespace
 
+bool tc_tensor_map(CUtensorMap *out, const void *ptr, int rows, int K, int box_rows) {
+    return cached_map(out, ptr, rows, K, box_rows);
+}
+
 cudaError_t prepare_gemm_tc() {
     cudaError_t e;
     if ((e = prepare_bn<32>()) != cudaSuccess) return e;

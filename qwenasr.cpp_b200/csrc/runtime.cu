@@ -156,6 +156,9 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
     for (auto &ev : h->row_ev) CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
     CK(cudaMalloc(&h->d_out_ids, R * sizeof(int)));
     CK(cudaMallocHost(&h->h_out_ids, R * sizeof(int)));
+    h->max_items = (h->max_rows / 64 + h->rt.max_streams + 1) * kHkv;
+    CK(cudaMalloc(&h->d_items, static_cast<size_t>(h->max_items) * sizeof(int4)));
+    CK(cudaMallocHost(&h->h_items, static_cast<size_t>(h->max_items) * sizeof(int4)));
     const size_t slots = static_cast<size_t>(kAttnMaxRows + h->num_sms);
     CK(cudaMalloc(&h->part_o, slots * kHq * kHeadDim * sizeof(float)));
     CK(cudaMalloc(&h->part_ml, slots * kHq * 2 * sizeof(float)));
@@ -166,6 +169,7 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
     CK(cudaMallocHost(&h->h_err, sizeof(DevError)));
     CK(prepare_decode_attn());
     CK(prepare_gemm_tc());
+    CK(prepare_prefill_tc());
     CK(prepare_dense(std::max(c.hidden, std::max(c.intermediate, kQDim))));
     (void)gemm_tc_supported(1, 1, 64);   // resolve the tensor-map encoder before any capture
     CK(cudaStreamSynchronize(h->stream));
@@ -184,9 +188,9 @@ void destroy(qkv_handle *h) {
     cudaFree(h->pool); cudaFree(h->scales); cudaFree(h->d_page_table); cudaFree(h->d_rope);
     cudaFree(h->x); cudaFree(h->qkv); cudaFree(h->q); cudaFree(h->gu); cudaFree(h->logits);
     cudaFree(h->xn); cudaFree(h->attn); cudaFree(h->act); cudaFree(h->host_stage);
-    cudaFree(h->d_rowbuf); cudaFree(h->d_out_ids); cudaFree(h->part_o); cudaFree(h->part_ml);
+    cudaFree(h->d_rowbuf); cudaFree(h->d_out_ids); cudaFree(h->d_items); cudaFree(h->part_o); cudaFree(h->part_ml);
     cudaFree(h->counters); cudaFree(h->d_err);
-    cudaFreeHost(h->h_page_table); cudaFreeHost(h->h_rowbuf); cudaFreeHost(h->h_out_ids); cudaFreeHost(h->h_err);
+    cudaFreeHost(h->h_page_table); cudaFreeHost(h->h_items); cudaFreeHost(h->h_rowbuf); cudaFreeHost(h->h_out_ids); cudaFreeHost(h->h_err);
     for (auto &kv : h->decode_graphs) cudaGraphExecDestroy(kv.second.exec);
     for (auto &kv : h->kv_graphs) cudaGraphExecDestroy(kv.second.exec);
     for (auto &ev : h->row_ev) {
@@ -313,6 +317,25 @@ int stream_len(qkv_handle *h, int32_t s) {
     int32_t t = 0;
     h->pager->length(s, &t, nullptr);
     return t;
+}
+
+// Prefill attention items: per stream chunk of <= 64 consecutive prompt rows
+// (one stream each), per kv head.  Uploaded from pinned staging on the
+// handle's stream (prefill calls are synchronous, so the staging is free).
+int upload_items(qkv_handle *h, int n, const int32_t *lens, int *n_items) {
+    int k = 0, row = 0;
+    for (int i = 0; i < n; ++i) {
+        for (int q0 = 0; q0 < lens[i]; q0 += 64) {
+            for (int g = 0; g < kHkv; ++g) {
+                if (k >= h->max_items) return fail(h, QKV_ERR_CAPACITY, "too many prefill attention items");
+                h->h_items[k++] = make_int4(row + q0, std::min(64, lens[i] - q0), g, 0);
+            }
+        }
+        row += lens[i];
+    }
+    CK(cudaMemcpyAsync(h->d_items, h->h_items, static_cast<size_t>(k) * sizeof(int4), cudaMemcpyHostToDevice, h->stream));
+    *n_items = k;
+    return QKV_OK;
 }
 
 // Grow each row's stream by `tokens` (pages from the pager) and push changed
@@ -485,7 +508,7 @@ int head_and_argmax(qkv_handle *h, int n, const int *d_rows) {
 // All layers over `n` rows whose inputs are in h->x; decode rows attend with
 // K2, prompt rows with the causal prefill kernel.
 int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int *lens, bool prompt, int l0 = 0,
-               int l1 = -1) {
+               int l1 = -1, const int4 *items = nullptr, int n_items = 0) {
     const qkv_model_config &c = h->cfg;
     const bool bf = h->act_dtype == kActBF16;
     int rc;
@@ -519,7 +542,11 @@ int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int
             pp.n_pages = h->n_pages;
             pp.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(kHeadDim)));
             pp.err = h->d_err;
-            CK(launch_prefill_attn(pp, h->rt.kv_dtype, bf, h->stream));
+            if (h->rt.kv_dtype == kKvBF16 && items && n_items > 0) {
+                CK(launch_prefill_attn_tc(pp, items, n_items, bf, h->stream));
+            } else {
+                CK(launch_prefill_attn(pp, h->rt.kv_dtype, bf, h->stream));
+            }
             h->launches += 2;
         }
         CK(gemm(h, h->attn, L.w_o, h->x, n, c.hidden, kQDim, 1));
@@ -781,7 +808,9 @@ int qkv_prefill(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32
     if ((rc = row_upload(h, hs, static_cast<size_t>(2 * T + n), h->stream))) return rc;
     CK(cudaMemcpyAsync(h->x, embeddings, static_cast<size_t>(T) * h->cfg.hidden * sizeof(float), cudaMemcpyHostToDevice,
                        h->stream));
-    if ((rc = run_layers(h, T, ds, dp, nullptr, true))) return rc;
+    int n_items = 0;
+    if ((rc = upload_items(h, n, lens, &n_items))) return rc;
+    if ((rc = run_layers(h, T, ds, dp, nullptr, true, 0, -1, h->d_items, n_items))) return rc;
     if ((rc = head_and_argmax(h, n, dr))) return rc;
     return finish_ids(h, n, stream_ids, out_ids, out_logits);
 }
@@ -852,7 +881,11 @@ int qkv_layer_forward(qkv_handle *h, int32_t layer, int32_t tokens, const float 
         const size_t bytes = static_cast<size_t>(tokens) * h->cfg.hidden * sizeof(float);
         cudaError_t e = cudaMemcpyAsync(h->x, x, bytes, cudaMemcpyHostToDevice, h->stream);
         if (e != cudaSuccess) rc = cuda_fail(h, e, "layer_forward upload");
-        if (rc == QKV_OK) rc = run_layers(h, tokens, h->d_rowbuf, h->d_rowbuf + tokens, nullptr, true, layer, layer + 1);
+        int n_items = 0;
+        if (rc == QKV_OK) rc = upload_items(h, 1, &tokens, &n_items);
+        if (rc == QKV_OK)
+            rc = run_layers(h, tokens, h->d_rowbuf, h->d_rowbuf + tokens, nullptr, true, layer, layer + 1, h->d_items,
+                            n_items);
         if (rc == QKV_OK) {
             e = cudaMemcpyAsync(out, h->x, bytes, cudaMemcpyDeviceToHost, h->stream);
             if (e != cudaSuccess) rc = cuda_fail(h, e, "layer_forward download");

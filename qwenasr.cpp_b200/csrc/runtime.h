@@ -69,6 +69,9 @@ struct qkv_handle {
     int row_slot = 0;
     int *d_out_ids = nullptr;   // [max_rows]
     int *h_out_ids = nullptr;   // pinned
+    int4 *d_items = nullptr;    // prefill attention work items
+    int4 *h_items = nullptr;    // pinned
+    int max_items = 0;
     float *part_o = nullptr, *part_ml = nullptr;
     int *counters = nullptr;
     qkv::DevError *d_err = nullptr;

@@ -195,3 +195,36 @@ def test_stream_reuse_after_close(pkg, synth, checker, tiny_files):
             got = [int(dec.prefill([s], [x])[0])] + [int(dec.decode_step([s])[0]) for _ in range(4)]
             assert got == om.generate(x, 5)["ids"].tolist()
             dec.close_stream(s)
+
+
+@pytest.mark.parametrize("tokens", [1, 17, 64, 65, 130, 300])
+def test_bf16_prefill_attention_layer(pkg, synth, checker, tiny_files, tokens):
+    """The tensor-core prefill attention (bf16 cache) through one block vs the
+    reference's f32 block: prompt lengths around the 64-query item and the
+    128-key tile boundaries."""
+    cfg, files = tiny_files
+    path = files[("bf16", "one_plus")]
+    tensors = synth.read_gguf(path)
+    om = checker.OracleModel(cfg, tensors)
+    rng = np.random.default_rng(tokens)
+    x = rng.standard_normal((tokens, cfg["hidden"]), dtype=np.float32)
+    want, _, _ = om.layer_prefill(1, x)
+    with decoder(pkg, path, w=1, kv=1, streams=2, ctx=512) as dec:
+        got = dec.layer_forward(1, x)
+    err = rel_err(got - x, want - x)     # compare the block's update, not the residual carried through
+    assert err < 3e-2, err
+
+
+def test_bf16_prefill_logits_multi_stream(pkg, synth, checker, tiny_files):
+    """Ragged multi-stream prefill through the tensor-core attention vs the f32 reference."""
+    cfg, files = tiny_files
+    path = files[("bf16", "one_plus")]
+    tensors = synth.read_gguf(path)
+    om = checker.OracleModel(cfg, tensors)
+    xs = prompts(synth, tensors, 5, 300, lo=20, hi=200)
+    with decoder(pkg, path, w=1, kv=1, streams=5, ctx=256, batch_tokens=1024) as dec:
+        streams = [dec.open() for _ in xs]
+        ids, logits = dec.prefill(streams, xs, want_logits=True)
+    for i, x in enumerate(xs):
+        ref = om.prefill_logits(x)
+        assert rel_err(logits[i], ref) < 3e-2
