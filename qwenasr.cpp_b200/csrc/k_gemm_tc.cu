@@ -218,7 +218,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const bool have = bounded_wait(acc_full, 0);
         if (!have) report_error(p.err, kErrWaitTimeout, kWhereGemm, blockIdx.x, 1 << 20);
         tc_fence_after();
-        const bool valid_acc = have && nk > 0 && !*failed;
+        // Warp-uniform: tcgen05.ld is .sync.aligned, every lane of the warp must issue it.
+        const bool valid_acc = __all_sync(0xffffffffu, have && nk > 0 && !*failed);
         const bool atomic = p.accumulate || gridDim.z > 1;
 #pragma unroll 1
         for (int c = 0; c < BN; c += 8) {

@@ -298,12 +298,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         float m_run = -INFINITY, l_run = 0.0f, inv_l = 0.0f;
         for (int u = 0; u < n_uses; ++u) {
             const int pass = u / n_kt, kt = u % n_kt;
-            if (*failed || !mbar_wait(&bars->s_full, static_cast<uint32_t>(u) & 1u, kWaitLimitCycles)) break;
+            // Every exit decision is warp-uniform: the tcgen05.ld below is .sync.aligned.
+            bool go = !*failed && mbar_wait(&bars->s_full, static_cast<uint32_t>(u) & 1u, kWaitLimitCycles);
+            if (!__all_sync(0xffffffffu, go)) break;
             fence_after();
             if (pass == 1 && kt == 0) inv_l = 1.0f / l_run;
-            if (pass == 1 && kt > 0 &&
-                !mbar_wait(&bars->p_free, static_cast<uint32_t>(kt - 1) & 1u, kWaitLimitCycles))
-                break;
+            if (pass == 1 && kt > 0) {
+                go = mbar_wait(&bars->p_free, static_cast<uint32_t>(kt - 1) & 1u, kWaitLimitCycles);
+                if (!__all_sync(0xffffffffu, go)) break;
+            }
 #pragma unroll 1
             for (int ch = 0; ch < 4; ++ch) {
                 float s[32];
@@ -348,14 +351,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         // Epilogue: O row (128 dims) -> attention output of (query i, head 2g+h)
-        const bool done = n_uses > 0 && mbar_wait(&bars->o_done, 0, kWaitLimitCycles);
+        bool done = n_uses > 0 && mbar_wait(&bars->o_done, 0, kWaitLimitCycles) && !*failed;
+        done = __all_sync(0xffffffffu, done);   // warp-uniform: the whole warp loads TMEM, only real rows store
         fence_after();
-        if (done && !*failed && real) {
-            const size_t off = static_cast<size_t>(row0 + i) * kQDim + (2 * g + h) * kHeadDim;
+        if (done) {
+            const size_t off = static_cast<size_t>(row0 + (real ? i : 0)) * kQDim + (2 * g + h) * kHeadDim;
 #pragma unroll 1
             for (int ch = 0; ch < 4; ++ch) {
                 float o[32];
                 tmem_ld32(lane_addr + 128u + static_cast<uint32_t>(ch * 32), o);
+                if (!real) continue;
                 if (p.out_bf16) {
                     __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(p.out) + off + ch * 32;
 #pragma unroll
