@@ -44,6 +44,33 @@ template <> struct PageStore<uint8_t> {
     }
 };
 
+// Per-head RMSNorm (double mean square, as text-decoder.cpp:542-557) and NEOX
+// RoPE (:604-625) of the 8 dims a half-warp lane holds; lane l16 ^ 8 holds the
+// rotation partners.  Must be called by all 32 lanes of the warp.
+__device__ __forceinline__ void norm_rope8(float (&x)[8], const float *w8, const float2 *cs8, int l16, float eps) {
+    double ss = 0.0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss += static_cast<double>(x[j]) * x[j];
+#pragma unroll
+    for (int o = 8; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const double ms = ss / static_cast<double>(kHeadDim);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(ms), eps)));
+    float y[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y[j] = __fmul_rn(__fmul_rn(x[j], scale), w8[j]);
+    const bool lower = l16 < 8;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float other = __shfl_xor_sync(0xffffffffu, y[j], 8);
+        const float2 t = cs8[j];
+        if (lower) {  // row[i] = a*c - b*s   (a = own, b = partner)
+            x[j] = __fsub_rn(__fmul_rn(y[j], t.x), __fmul_rn(other, t.y));
+        } else {      // row[half+i] = b*c + a*s   (b = own, a = partner)
+            x[j] = __fadd_rn(__fmul_rn(y[j], t.x), __fmul_rn(other, t.y));
+        }
+    }
+}
+
 template <typename TC>
 __global__ void __launch_bounds__(512) kv_append_kernel(AppendParams p) {
     const int row = blockIdx.x;
@@ -62,9 +89,6 @@ __global__ void __launch_bounds__(512) kv_append_kernel(AppendParams p) {
         if (threadIdx.x == 0) report_error(p.err, page < 0 ? kErrPosition : kErrPageIndex, kWhereAppend, row, pos);
         return;
     }
-    // mode 1: only rows that open a page; mode 2: only the others (FP8 prefill
-    // runs both so a page's scale is set before its later tokens are stored).
-    if ((p.mode == 1 && (pos & (kPageTokens - 1)) != 0) || (p.mode == 2 && (pos & (kPageTokens - 1)) == 0)) return;
 
     int src_off;
     if (unit < kHq) src_off = unit * kHeadDim;
@@ -81,30 +105,9 @@ __global__ void __launch_bounds__(512) kv_append_kernel(AppendParams p) {
 
     // Warps 0-7 hold q units, 8-11 k units, 12-15 v units: the branch is warp-uniform.
     if (unit < kHq + kHkv) {
-        const float *w = (unit < kHq ? p.q_norm_w : p.k_norm_w) + l16 * 8;
-        double ss = 0.0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) ss += static_cast<double>(x[j]) * x[j];
-#pragma unroll
-        for (int o = 8; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const double ms = ss / static_cast<double>(kHeadDim);
-        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(ms), p.eps)));
-        float y[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) y[j] = __fmul_rn(__fmul_rn(x[j], scale), w[j]);
         // NEOX rotate-half: dim i (< 64) pairs with dim i + 64, held by lane l16 ^ 8.
-        const float2 *cs = p.rope + static_cast<size_t>(pos) * (kHeadDim / 2) + (l16 & 7) * 8;
-        const bool lower = l16 < 8;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float other = __shfl_xor_sync(0xffffffffu, y[j], 8);
-            const float2 t = cs[j];
-            if (lower) {  // row[i] = a*c - b*s   (a = own, b = partner)
-                x[j] = __fsub_rn(__fmul_rn(y[j], t.x), __fmul_rn(other, t.y));
-            } else {      // row[half+i] = b*c + a*s   (b = own, a = partner)
-                x[j] = __fadd_rn(__fmul_rn(y[j], t.x), __fmul_rn(other, t.y));
-            }
-        }
+        norm_rope8(x, (unit < kHq ? p.q_norm_w : p.k_norm_w) + l16 * 8,
+                   p.rope + static_cast<size_t>(pos) * (kHeadDim / 2) + (l16 & 7) * 8, l16, p.eps);
     }
 
     if (unit < kHq) {
@@ -118,24 +121,92 @@ __global__ void __launch_bounds__(512) kv_append_kernel(AppendParams p) {
     const int tok = pos & (kPageTokens - 1);
     float inv_scale = 1.0f;
     if constexpr (sizeof(TC) == 1) {
-        // FP8: the page's scale for (kv, head) is fixed by the first token
-        // written to the page (headroom x4 over its absolute maximum); later
-        // tokens saturate at +-448 * scale.
-        float amax = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(x[j]));
-#pragma unroll
-        for (int o = 8; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        float *sc = p.scales + (static_cast<size_t>(page) * 2 + kv) * kHkv + g;
-        if (tok == 0 && l16 == 0) *sc = fmaxf(amax * 4.0f / kE4m3Max, 1e-30f);
-        __syncwarp();
-        __threadfence_block();
-        inv_scale = 1.0f / *reinterpret_cast<volatile float *>(sc);
+        // FP8: the (page, kv, head) scale was settled for this batch by
+        // fp8_page_scale_kernel, which ran just before on the same stream.
+        inv_scale = 1.0f / p.scales[(static_cast<size_t>(page) * 2 + kv) * kHkv + g];
     }
     TC *pool = static_cast<TC *>(p.pool);
     TC *dst = pool + ((static_cast<size_t>(page) * 2 + kv) * kHkv + g) * (kPageTokens * kHeadDim) +
               tok * kHeadDim + l16 * 8;
     PageStore<TC>::put(dst, x, inv_scale);
+}
+
+// FP8 page scales.  One CTA per page touched by the batch (group = the
+// batch's consecutive rows of one stream inside one page), 16 half-warp units
+// = (K | V) x 8 kv heads.  Each unit takes the absolute maximum of its head
+// over the group's new tokens (K after norm + RoPE, V raw); if the page
+// already holds tokens and the new maximum fits the current scale the scale is
+// kept, otherwise the scale becomes amax / 448 x headroom (x2 while the page
+// will take more tokens) and the tokens already stored are re-quantised to
+// it.  K1 then stores the new tokens with the settled scale.
+__global__ void __launch_bounds__(256) fp8_page_scale_kernel(AppendParams p) {
+    // CTA per row; only the first row of each page group works (block-uniform exit).
+    const int row0 = blockIdx.x;
+    const int slot = p.slots[row0], pos0 = p.positions[row0];
+    if (row0 > 0 && p.slots[row0 - 1] == slot && p.positions[row0 - 1] == pos0 - 1 && (pos0 & (kPageTokens - 1)) != 0)
+        return;
+    if (slot < 0 || slot >= p.max_streams || pos0 < 0 || pos0 / kPageTokens >= p.maxp) return;   // K1 reports it
+    int cnt = 1;
+    while (row0 + cnt < p.n && cnt < kPageTokens && p.slots[row0 + cnt] == slot &&
+           p.positions[row0 + cnt] == pos0 + cnt && ((pos0 + cnt) & (kPageTokens - 1)) != 0)
+        ++cnt;
+    const int page = p.page_table[static_cast<size_t>(slot) * p.maxp + pos0 / kPageTokens];
+    const int tok0 = pos0 & (kPageTokens - 1);
+    const int unit = threadIdx.x >> 4, l16 = threadIdx.x & 15;   // unit 0..7 K heads, 8..15 V heads
+    const int kv = unit >> 3, g = unit & 7;
+    if (page < 0 || page >= p.n_pages) {
+        if (threadIdx.x == 0) report_error(p.err, kErrPageIndex, kWhereAppend, row0, page);
+        return;
+    }
+    float amax = 0.0f;
+    for (int r = 0; r < cnt; ++r) {
+        const int row = row0 + r;
+        const int pos = p.positions[row];
+        const int src_off = kQDim + kv * kKvDim + g * kHeadDim + l16 * 8;
+        const float *src = p.qkv + static_cast<size_t>(row) * kQkvDim + src_off;
+        float x[8];
+        const float4 a = reinterpret_cast<const float4 *>(src)[0];
+        const float4 b = reinterpret_cast<const float4 *>(src)[1];
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+        x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+        if (kv == 0) {   // warp-uniform: warps 0..3 hold K units
+            const int safe_pos = pos >= 0 && pos < p.rope_len ? pos : 0;
+            norm_rope8(x, p.k_norm_w + l16 * 8, p.rope + static_cast<size_t>(safe_pos) * (kHeadDim / 2) + (l16 & 7) * 8,
+                       l16, p.eps);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(x[j]));
+    }
+#pragma unroll
+    for (int o = 8; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    float *sc = p.scales + (static_cast<size_t>(page) * 2 + kv) * kHkv + g;
+    const float old_scale = *sc;
+    const bool has_old = tok0 > 0;
+    const bool fills_page = tok0 + cnt == kPageTokens;
+    if (has_old && amax <= kE4m3Max * old_scale) return;   // current scale still covers the new tokens
+    const float head = fills_page ? 1.0f : 2.0f;
+    const float new_scale = fmaxf(fmaxf(amax, has_old ? kE4m3Max * old_scale : 0.0f) * head / kE4m3Max, 1e-30f);
+    if (has_old) {
+        // re-quantise the tokens already in the page to the new scale
+        uint8_t *pool = static_cast<uint8_t *>(p.pool);
+        uint8_t *base = pool + ((static_cast<size_t>(page) * 2 + kv) * kHkv + g) * (kPageTokens * kHeadDim) + l16 * 8;
+        const float ratio = old_scale / new_scale;
+        for (int t = 0; t < tok0; ++t) {
+            uint2 w = *reinterpret_cast<uint2 *>(base + t * kHeadDim);
+            uint32_t lo = 0, hi = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 f = e4m3x2_to_f2(static_cast<uint16_t>(((j < 2 ? w.x : w.y) >> (16 * (j & 1))) & 0xffffu));
+                const uint32_t q0 = f_to_e4m3(f.x * ratio), q1 = f_to_e4m3(f.y * ratio);
+                const uint32_t pair = q0 | (q1 << 8);
+                if (j < 2) lo |= pair << (16 * j);
+                else hi |= pair << (16 * (j - 2));
+            }
+            *reinterpret_cast<uint2 *>(base + t * kHeadDim) = make_uint2(lo, hi);
+        }
+    }
+    __syncwarp();
+    if (l16 == 0) *sc = new_scale;
 }
 
 // Page gather: tokens [0, len) of one stream -> contiguous [len][Hkv*D] (K and V).
@@ -201,16 +272,28 @@ __global__ void page_fill_kernel(TC *pool, float *scales, const int *pages, int 
 
 }  // namespace
 
+cudaError_t launch_fp8_page_scale(const AppendParams &p, cudaStream_t st) {
+    if (p.n <= 0) return cudaSuccess;
+    fp8_page_scale_kernel<<<p.n, 256, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_kv_append(const AppendParams &p, int kv_dtype, cudaStream_t st) {
     if (p.n <= 0) return cudaSuccess;
     switch (kv_dtype) {
         case kKvF32: kv_append_kernel<float><<<p.n, 512, 0, st>>>(p); break;
         case kKvBF16: kv_append_kernel<__nv_bfloat16><<<p.n, 512, 0, st>>>(p); break;
-        case kKvFP8: kv_append_kernel<uint8_t><<<p.n, 512, 0, st>>>(p); break;
+        case kKvFP8: {
+            const cudaError_t e = launch_fp8_page_scale(p, st);
+            if (e != cudaSuccess) return e;
+            kv_append_kernel<uint8_t><<<p.n, 512, 0, st>>>(p);
+            break;
+        }
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
 }
+
 
 cudaError_t launch_page_gather(const void *pool, int kv_dtype, const int *pages, int n_pages_row, int len,
                                int n_pages, void *k_out, void *v_out, DevError *err, cudaStream_t st) {

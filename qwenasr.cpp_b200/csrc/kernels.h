@@ -32,7 +32,6 @@ struct AppendParams {
     int max_streams;
     int n_pages;
     float eps;
-    int mode;                  // 0 all rows, 1 page-opening rows only, 2 the others
     DevError *err;
 };
 
@@ -72,6 +71,9 @@ struct PrefillAttnParams {
 };
 
 cudaError_t launch_kv_append(const AppendParams &p, int kv_dtype, cudaStream_t st);
+// FP8 cache: settle each touched page's per-(kv, head) scale before K1 stores
+// (launch_kv_append runs it first for the FP8 cache).
+cudaError_t launch_fp8_page_scale(const AppendParams &p, cudaStream_t st);
 cudaError_t prepare_decode_attn();
 size_t attn_smem_bytes(int kv_dtype);
 cudaError_t launch_decode_attn(const AttendParams &p, int kv_dtype, bool out_bf16, int grid, cudaStream_t st);

@@ -449,7 +449,6 @@ AppendParams append_params(qkv_handle *h, int layer, int n, const int *slots, co
     p.max_streams = h->rt.max_streams;
     p.n_pages = h->n_pages;
     p.eps = h->cfg.rms_norm_eps;
-    p.mode = 0;
     p.err = h->d_err;
     return p;
 }
@@ -522,11 +521,6 @@ int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int
                 return rc;
         } else {
             AppendParams ap = append_params(h, l, n, slots, pos, h->qkv, h->q, L.q_norm, L.k_norm);
-            if (h->rt.kv_dtype == kKvFP8) {
-                ap.mode = 1;
-                CK(launch_kv_append(ap, h->rt.kv_dtype, h->stream));
-                ap.mode = 2;
-            }
             CK(launch_kv_append(ap, h->rt.kv_dtype, h->stream));
             PrefillAttnParams pp{};
             pp.n = n;

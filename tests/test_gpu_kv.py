@@ -228,3 +228,50 @@ def test_device_error_on_bad_page_table_row(pkg):
             dec.sync()
         assert ei.value.code == 5
         dec.sync()   # the error word was cleared
+
+
+def e4m3_to_f32(b: np.ndarray) -> np.ndarray:
+    b = b.astype(np.int32)
+    sign = np.where(b & 0x80, -1.0, 1.0)
+    e = (b >> 3) & 0xF
+    m = b & 0x7
+    val = np.where(e == 0, m / 8.0 * 2.0 ** -6, (1.0 + m / 8.0) * 2.0 ** (e - 7))
+    return (sign * val).astype(np.float32)
+
+
+@pytest.mark.parametrize("style", ["batch", "token_by_token"])
+def test_fp8_append_dequantises_within_e4m3_precision(pkg, checker, style):
+    """FP8 cache: every stored K/V element, dequantised with its page's
+    per-(kv, head) scale, is within 2^-4 of the page-head maximum of the
+    reference values, also when later tokens are 40x larger than the first
+    (the page scale grows and the stored tokens are re-quantised)."""
+    dec, qn, kn = kv_handle(pkg, 2, seed=3, max_streams=2, max_context=128)
+    with dec:
+        rng = np.random.default_rng(17)
+        L = 40
+        raw = rng.standard_normal((L, QKV), dtype=np.float32)
+        raw[5:11] *= 40.0          # a block of much larger rows inside page 0
+        raw[20] *= 40.0            # and one inside page 1
+        s = dec.open()
+        dec.extend(s, L)
+        if style == "batch":
+            fill_stream(dec, 0, s, raw)
+        else:
+            for t in range(L):
+                fill_stream(dec, 0, s, raw[t:t + 1], start=t)
+        k_b, v_b, scales = dec.gather(0, s, 2)
+        ref_k = np.zeros((L, 1024), np.float32)
+        ref_v = np.zeros((L, 1024), np.float32)
+        for t in range(L):
+            _, ok, ov = checker.append_qkv(raw[t], qn[0], kn[0], t)
+            ref_k[t], ref_v[t] = ok, ov
+        for t0 in range(0, L, 16):
+            pg = t0 // 16
+            rows = slice(t0, min(L, t0 + 16))
+            for kv, (got_b, ref) in enumerate(((k_b, ref_k), (v_b, ref_v))):
+                for g in range(8):
+                    cols = slice(g * 128, (g + 1) * 128)
+                    deq = e4m3_to_f32(got_b[rows, cols]) * scales[pg, kv, g]
+                    want = ref[rows, cols]
+                    bound = np.abs(want).max() * 2.0 ** -4
+                    assert np.abs(deq - want).max() <= bound, (style, pg, kv, g)
