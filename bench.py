@@ -410,15 +410,169 @@ def run_model(args) -> int:
     return 0
 
 
+def gguf_path(synth, cfg, name: str, rank: int) -> tuple[Path, float]:
+    import tempfile
+    tmpdir = Path(os.environ.get("QWENASR_BENCH_TMP", "/dev/shm" if Path("/dev/shm").is_dir() else tempfile.gettempdir()))
+    path = tmpdir / f"qwen3asr_{name}_bf16_seed0_r{rank}.gguf"
+    t0 = time.perf_counter()
+    if not path.exists():
+        synth.write_gguf(path, cfg, seed=0, weights="bf16", norm_init="normal", tokenizer=False)
+    return path, time.perf_counter() - t0
+
+
+def run_serve(args) -> int:
+    """Config 5: 1.7B, FP8-e4m3 paged cache (per-page-per-head scales), continuous
+    batching.  512 requests are admitted at start; each timed step first admits
+    Poisson(lambda) new requests (chunked prefill), then decodes one token for
+    every active stream, closes streams that reached their output length (pages
+    freed) and compacts the pool every 64 steps.  lambda = concurrency / mean
+    output length keeps ~512 streams in flight.  value = decoded tokens / wall
+    time of the timed steps (arrival prefills, closes and compaction included)."""
+    import torch
+
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    synth = ge.load_synth()
+    rank, local, world, dist = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    cfg = dict(synth.QWEN3_ASR_1_7B)
+    path, gen_s = gguf_path(synth, cfg, "1p7b", rank)
+    embd = synth.read_gguf(path)["text.token_embd.weight"]
+    conc = args.concurrency
+    rng = np.random.default_rng(1005 * 1_000_003 + rank * 65_536)
+    text_tokens, out_lo, out_hi = 20, 32, 512
+    lam = conc / ((out_lo + out_hi) / 2.0)
+    max_ctx = 780 + text_tokens + out_hi + 8
+    slots_cap = conc + 128
+    rt = pkg.runtime_config(device=local, weight_dtype=pkg.BF16, kv_dtype=pkg.FP8, max_streams=slots_cap,
+                            max_context=max_ctx, max_pages=slots_cap * ((max_ctx + 15) // 16),
+                            max_batch_tokens=32768, page_order_seed=1005 + rank)
+    dec = pkg.Decoder.from_gguf(path, rt, cfg)
+    active: dict[int, int] = {}
+
+    def admit(n_new: int) -> int:
+        reqs = []
+        for _ in range(n_new):
+            if len(active) + len(reqs) >= slots_cap:
+                break
+            audio = int(rng.integers(65, 781))
+            x, _ = synth.prompt_rows(embd, audio + text_tokens, rng, audio_rows=audio, audio_start=9)
+            reqs.append((x, int(rng.integers(out_lo, out_hi + 1))))
+        tokens = 0
+        i = 0
+        while i < len(reqs):   # chunked by the handle's prompt-token budget
+            chunk, budget = [], 0
+            while i < len(reqs) and budget + reqs[i][0].shape[0] <= 32768:
+                chunk.append(reqs[i])
+                budget += reqs[i][0].shape[0]
+                i += 1
+            streams = [dec.open() for _ in chunk]
+            dec.prefill(streams, [c[0] for c in chunk])
+            for s, (_, n_out) in zip(streams, chunk):
+                active[s] = n_out - 1      # the prefill produced the first token
+            tokens += budget
+        return tokens
+
+    t0 = time.perf_counter()
+    admit(conc)
+    fill_s = time.perf_counter() - t0
+    decoded = prefill_tokens = closed = moved = 0
+    conc_seen = []
+    sampler = ClockSampler(local)
+
+    def step(timed: bool):
+        nonlocal decoded, prefill_tokens, closed, moved
+        pt = admit(int(rng.poisson(lam)))
+        streams = list(active.keys())
+        dec.decode_step(streams)
+        for s in streams:
+            active[s] -= 1
+            if active[s] <= 0:
+                dec.close_stream(s)
+                del active[s]
+                closed += timed
+        if timed:
+            decoded += len(streams)
+            prefill_tokens += pt
+            conc_seen.append(len(streams))
+
+    for _ in range(args.warmup):
+        step(False)
+    barrier(dist)
+    with sampler:
+        t1 = time.perf_counter()
+        for k in range(args.steps):
+            step(True)
+            if (k + 1) % 64 == 0:
+                moved += dec.compact()
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t1
+    dt_max = max_over_ranks(dist, dt)
+    total = sum_over_ranks(dist, float(decoded))
+    free_pages, total_pages = dec.pool_stats()
+    dec.close()
+
+    # Deviation of the FP8 cache vs the bf16 cache: 8 config-5 prompts, the
+    # bf16-cache path's greedy ids teacher-force the FP8-cache path.
+    dev_line = None
+    if rank == 0:
+        drng = np.random.default_rng(4242)
+        prompts = []
+        for _ in range(8):
+            audio = int(drng.integers(65, 781))
+            x, _ = synth.prompt_rows(embd, audio + text_tokens, drng, audio_rows=audio, audio_start=9)
+            prompts.append(x)
+        n_steps = 32
+        outs = {}
+        for kvd in (pkg.BF16, pkg.FP8):
+            rt2 = pkg.runtime_config(device=local, weight_dtype=pkg.BF16, kv_dtype=kvd, max_streams=8,
+                                     max_context=max_ctx, max_batch_tokens=8 * 800)
+            with pkg.Decoder.from_gguf(path, rt2, cfg) as d2:
+                ss = [d2.open() for _ in prompts]
+                ids, lg = d2.prefill(ss, prompts, want_logits=True)
+                steps_ids, steps_lg = [ids], [lg]
+                for t in range(n_steps - 1):
+                    feed = outs[pkg.BF16][0][t] if kvd == pkg.FP8 else steps_ids[-1]
+                    ids, lg = d2.decode_step(ss, in_ids=feed, want_logits=True)
+                    steps_ids.append(ids)
+                    steps_lg.append(lg)
+                outs[kvd] = (steps_ids, steps_lg)
+        agree = np.mean([np.mean(a == b) for a, b in zip(outs[pkg.BF16][0], outs[pkg.FP8][0])])
+        rel = max(float(np.max(np.abs(a - b)) / np.max(np.abs(b))) for a, b in zip(outs[pkg.FP8][1], outs[pkg.BF16][1]))
+        dev_line = {"streams": 8, "steps": n_steps, "greedy_agreement_vs_bf16": round(float(agree), 4),
+                    "max_rel_logit_dev_vs_bf16": float(f"{rel:.3e}")}
+    if rank == 0:
+        line = {
+            "metric": "serving decode tokens/s (1.7B, FP8 KV cache, continuous batching)",
+            "value": round(total / dt_max, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt_max / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 weights, fp8-e4m3 KV", "data": "synthetic",
+            "config": {"workload": "config5: Qwen3-ASR-1.7B, FP8 paged KV (per-page-per-head scales), Poisson arrivals, "
+                                   "audio 65-780 rows + 20 text tokens, outputs 32-512 tokens",
+                       "target_concurrency": conc, "mean_concurrency": round(float(np.mean(conc_seen)), 1),
+                       "arrival_rate_per_step": round(lam, 3), "initial_fill_s": round(fill_s, 2),
+                       "prefill_tokens_timed": int(prefill_tokens), "streams_closed": int(closed),
+                       "pages_moved_by_compaction": int(moved), "free_pages_end": int(free_pages),
+                       "pool_pages": int(total_pages), "gguf_write_s": round(gen_s, 1)},
+            "fp8_deviation": dev_line,
+            "clocks": sampler.summary()}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("kv", "model", "model3"), default="kv",
+    ap.add_argument("--workload", choices=("kv", "model", "model3", "serve"), default="kv",
                     help="kv: config 4 KV step (default); model: config 2 full greedy decode (0.6B bf16, 32 "
-                         "streams); model3: config 3 (1.7B bf16, 64 streams, 390 audio + 20 text tokens)")
+                         "streams); model3: config 3 (1.7B bf16, 64 streams, 390 audio + 20 text tokens); "
+                         "serve: config 5 (1.7B, FP8 cache, 512 concurrent streams, Poisson arrivals)")
+    ap.add_argument("--concurrency", type=int, default=512, help="serve: target concurrent streams per GPU")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="layers of cache (28 = the workload; fewer only for small profiling captures)")
@@ -429,6 +583,8 @@ def main() -> int:
         return run_reference(args)
     if args.workload in ("model", "model3"):
         return run_model(args)
+    if args.workload == "serve":
+        return run_serve(args)
     return run_ours(args)
 
 
