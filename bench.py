@@ -218,7 +218,9 @@ def run_ours(args) -> int:
     qn, kn = qk_norm_weights()
     cfg = dict(n_layers=N_LAYERS, hidden=1024, n_heads=HQ, n_kv_heads=HKV, head_dim=D, intermediate=3072,
                vocab=151936, rope_theta=1.0e6, rms_norm_eps=1.0e-6)
-    rt = pkg.runtime_config(device=local, weight_dtype=pkg.F32, kv_dtype=pkg.BF16, max_streams=STREAMS_PER_GPU,
+    kvd = {"bf16": pkg.BF16, "fp8": pkg.FP8, "f32": pkg.F32}[args.kv_dtype]
+    elem = {"bf16": 2, "fp8": 1, "f32": 4}[args.kv_dtype]
+    rt = pkg.runtime_config(device=local, weight_dtype=pkg.F32, kv_dtype=kvd, max_streams=STREAMS_PER_GPU,
                             max_context=max_ctx, max_pages=pages, page_order_seed=WORKLOAD_SEED + rank)
     dec = pkg.Decoder.kv_only(cfg, rt, qn, kn)
     streams = [dec.open() for _ in range(STREAMS_PER_GPU)]
@@ -277,7 +279,9 @@ def run_ours(args) -> int:
     dec.sync()
     attn_ms = a0.elapsed_time(a1) / (n_rep * N_LAYERS)
     ctx_tokens = int(cur_lens.sum().item())
-    kv_bytes_per_launch = ctx_tokens * HKV * D * 2 * 2          # K and V, bf16, one layer
+    kv_bytes_per_launch = ctx_tokens * HKV * D * 2 * elem       # K and V, one layer
+    if elem == 1:
+        kv_bytes_per_launch += sum((dec.length(s) + 15) // 16 for s in streams) * 2 * HKV * 4   # FP8 scales
     achieved_gbs = kv_bytes_per_launch / (attn_ms / 1e3) / 1e9
 
     # e2e: the same step through the C ABI with pinned host buffers (copies in the timed region).
@@ -307,17 +311,18 @@ def run_ours(args) -> int:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.kv_dtype,
             "data": "synthetic",
             "config": {"workload": "config4: KV append + GQA decode attention, 28 layers, 256 streams/GPU, "
                                    "ctx log-uniform [64,4096], 16-token pages, permuted page table",
                        "streams_per_gpu": STREAMS_PER_GPU, "mean_ctx": round(mean_ctx, 1),
-                       "kv_cache": "bf16 paged", "parallelism": f"streams sharded x{world}, no collectives",
+                       "kv_cache": f"{args.kv_dtype} paged", "parallelism": f"streams sharded x{world}, no collectives",
                        "l2": "inputs larger than L2 (per-layer KV read ~1 GB >> 126 MB)"},
             "kv_read_gbs_step": round(kv_bytes_per_launch * N_LAYERS / (ms_max / args.steps / 1e3) / 1e9, 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved_gbs / pk["hbm_gbs"], 4), "frac_of_8tbs": round(achieved_gbs / 8000, 4),
-                         "traffic": K2_NCU_TRAFFIC_BYTES, "kernel": "decode_attn_kernel (K2)",
+                         "traffic": K2_NCU_TRAFFIC_BYTES if args.kv_dtype == "bf16" else None,
+                         "kernel": "decode_attn_kernel (K2)",
                          "launch_ms": round(attn_ms, 4), "bytes_per_launch": kv_bytes_per_launch,
                          "peak_source": pk["source"]},
             "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s",
@@ -573,6 +578,8 @@ def main() -> int:
                          "streams); model3: config 3 (1.7B bf16, 64 streams, 390 audio + 20 text tokens); "
                          "serve: config 5 (1.7B, FP8 cache, 512 concurrent streams, Poisson arrivals)")
     ap.add_argument("--concurrency", type=int, default=512, help="serve: target concurrent streams per GPU")
+    ap.add_argument("--kv-dtype", choices=("bf16", "fp8", "f32"), default="bf16",
+                    help="kv workload: cache dtype (bf16 is the config-4 workload)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="layers of cache (28 = the workload; fewer only for small profiling captures)")

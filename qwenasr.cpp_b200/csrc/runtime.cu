@@ -839,9 +839,18 @@ int qkv_decode_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const i
         if ((r = run_layers(h, n, ds, dp, dl, false))) return r;
         return head_and_argmax(h, n, nullptr);
     };
-    if (h->use_graphs) {
-        auto it = h->decode_graphs.find(n);
+    // Replay a captured graph for a steady batch; a batch whose size keeps
+    // changing (continuous batching) runs eagerly rather than capturing per size.
+    auto it = h->decode_graphs.find(n);
+    const bool steady = n == h->last_decode_n;
+    h->last_decode_n = n;
+    if (h->use_graphs && (it != h->decode_graphs.end() || steady)) {
         if (it == h->decode_graphs.end()) {
+            if (h->decode_graphs.size() >= 32) {
+                CK(cudaStreamSynchronize(h->stream));
+                for (auto &kv : h->decode_graphs) cudaGraphExecDestroy(kv.second.exec);
+                h->decode_graphs.clear();
+            }
             qkv_handle::Graph g;
             if ((rc = capture_graph(h, body, &g))) return rc;
             it = h->decode_graphs.emplace(n, g).first;

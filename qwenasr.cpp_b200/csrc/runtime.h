@@ -90,6 +90,7 @@ struct qkv_handle {
     std::map<int, Graph> decode_graphs;
     std::map<std::tuple<int, const void *, const void *>, Graph> kv_graphs;
     bool use_graphs = true;
+    int last_decode_n = -1;   // a graph is captured only for a batch size seen twice in a row
 };
 
 namespace qkv {
