@@ -455,14 +455,21 @@ def run_serve(args) -> int:
     dec = pkg.Decoder.from_gguf(path, rt, cfg)
     active: dict[int, int] = {}
 
-    def admit(n_new: int) -> int:
+    def make_request():
+        audio = int(rng.integers(65, 781))
+        x, _ = synth.prompt_rows(embd, audio + text_tokens, rng, audio_rows=audio, audio_start=9)
+        return x, int(rng.integers(out_lo, out_hi + 1))
+
+    # Requests are synthesised before any timing: per step a Poisson count of arrivals.
+    arrivals = [[make_request() for _ in range(int(rng.poisson(lam)))] for _ in range(args.warmup + args.steps)]
+    phase = {"prefill_s": 0.0, "decode_s": 0.0, "close_s": 0.0, "compact_s": 0.0}
+
+    def admit(pending) -> int:
         reqs = []
-        for _ in range(n_new):
+        for r in pending:
             if len(active) + len(reqs) >= slots_cap:
                 break
-            audio = int(rng.integers(65, 781))
-            x, _ = synth.prompt_rows(embd, audio + text_tokens, rng, audio_rows=audio, audio_start=9)
-            reqs.append((x, int(rng.integers(out_lo, out_hi + 1))))
+            reqs.append(r)
         tokens = 0
         i = 0
         while i < len(reqs):   # chunked by the handle's prompt-token budget
@@ -479,37 +486,46 @@ def run_serve(args) -> int:
         return tokens
 
     t0 = time.perf_counter()
-    admit(conc)
+    admit([make_request() for _ in range(conc)])
     fill_s = time.perf_counter() - t0
     decoded = prefill_tokens = closed = moved = 0
     conc_seen = []
     sampler = ClockSampler(local)
 
-    def step(timed: bool):
+    def step(k: int, timed: bool):
         nonlocal decoded, prefill_tokens, closed, moved
-        pt = admit(int(rng.poisson(lam)))
+        ta = time.perf_counter()
+        pt = admit(arrivals[k])
+        tb = time.perf_counter()
         streams = list(active.keys())
         dec.decode_step(streams)
+        tc = time.perf_counter()
         for s in streams:
             active[s] -= 1
             if active[s] <= 0:
                 dec.close_stream(s)
                 del active[s]
                 closed += timed
+        td = time.perf_counter()
         if timed:
             decoded += len(streams)
             prefill_tokens += pt
             conc_seen.append(len(streams))
+            phase["prefill_s"] += tb - ta
+            phase["decode_s"] += tc - tb
+            phase["close_s"] += td - tc
 
-    for _ in range(args.warmup):
-        step(False)
+    for k in range(args.warmup):
+        step(k, False)
     barrier(dist)
     with sampler:
         t1 = time.perf_counter()
         for k in range(args.steps):
-            step(True)
+            step(args.warmup + k, True)
             if (k + 1) % 64 == 0:
+                tc0 = time.perf_counter()
                 moved += dec.compact()
+                phase["compact_s"] += time.perf_counter() - tc0
         torch.cuda.synchronize()
         dt = time.perf_counter() - t1
     dt_max = max_over_ranks(dist, dt)
@@ -558,7 +574,8 @@ def run_serve(args) -> int:
                        "arrival_rate_per_step": round(lam, 3), "initial_fill_s": round(fill_s, 2),
                        "prefill_tokens_timed": int(prefill_tokens), "streams_closed": int(closed),
                        "pages_moved_by_compaction": int(moved), "free_pages_end": int(free_pages),
-                       "pool_pages": int(total_pages), "gguf_write_s": round(gen_s, 1)},
+                       "pool_pages": int(total_pages), "gguf_write_s": round(gen_s, 1),
+                       "phase_s": {k: round(v, 3) for k, v in phase.items()}},
             "fp8_deviation": dev_line,
             "clocks": sampler.summary()}
         print(json.dumps(line), flush=True)

@@ -13,8 +13,16 @@
 // index is unique per segment) and the last of its segments to finish (per kv
 // head, atomic counter) merges them.  Counters reset themselves.
 //
-// CTA = 8 consumer warps (warp g <-> kv head g, serving q heads 2g and 2g+1)
-// + 1 producer warp.  The producer streams each page chunk (all 8 heads, K and
+// CTA = HALVES x 8 consumer warps + 1 producer warp.  Consumer warp g (and,
+// with HALVES = 2, warp g + 8) serves kv head g (q heads 2g and 2g+1).  With
+// two halves, the warps of a head take alternate chunks of the ring, each with
+// its own online-softmax state; at the end of a segment warp g + 8 hands
+// (m, l, O) to warp g through shared memory (bounded flag waits) and warp g
+// merges.  The e4m3 cache uses two halves: a dequant per element on top of the
+// bf16 work needs twice the loads, conversions and FMA chains in flight per SM
+// to keep up with HBM.  A stage must always be consumed by the same half (a
+// warp that skipped a phase of a stage's mbarrier could otherwise see the
+// parity of the phase before it), so NS is a multiple of HALVES.  The producer streams each page chunk (all 8 heads, K and
 // V) into an NS-stage shared-memory ring with cp.async.bulk (no tensor map,
 // no multicast), completion on mbarriers.  Every wait is bounded.
 //
@@ -38,12 +46,12 @@ namespace qkv {
 namespace {
 
 template <typename TC> struct AttnTraits;
-template <> struct AttnTraits<__nv_bfloat16> { static constexpr int CH = 16, NS = 3; };
-template <> struct AttnTraits<float> { static constexpr int CH = 8, NS = 3; };
-template <> struct AttnTraits<uint8_t> { static constexpr int CH = 16, NS = 6; };
+template <> struct AttnTraits<__nv_bfloat16> { static constexpr int CH = 16, NS = 3, HALVES = 1; };
+template <> struct AttnTraits<float> { static constexpr int CH = 8, NS = 3, HALVES = 1; };
+template <> struct AttnTraits<uint8_t> { static constexpr int CH = 16, NS = 6, HALVES = 2; };
 
-constexpr int kConsumers = 8;
-constexpr int kThreads = (kConsumers + 1) * 32;
+template <typename TC> __host__ __device__ constexpr int consumers() { return kHkv * AttnTraits<TC>::HALVES; }
+template <typename TC> __host__ __device__ constexpr int threads() { return (consumers<TC>() + 1) * 32; }
 
 template <typename TC> __host__ __device__ constexpr uint32_t stage_bytes() {
     return 2u * kHkv * AttnTraits<TC>::CH * kHeadDim * sizeof(TC);
@@ -52,9 +60,12 @@ template <typename TC> __host__ __device__ constexpr size_t smem_bytes() {
     return static_cast<size_t>(AttnTraits<TC>::NS) * stage_bytes<TC>()    // stages
            + 2 * AttnTraits<TC>::NS * sizeof(uint64_t)                      // full/empty barriers
            + AttnTraits<TC>::NS * 2 * kHkv * sizeof(float)                  // fp8 scales per stage
-           + kConsumers * 2 * AttnTraits<TC>::CH * sizeof(float)            // p exchange (16B aligned)
+           + consumers<TC>() * 2 * AttnTraits<TC>::CH * sizeof(float)       // p exchange (16B aligned)
+           + kHkv * 32 * 8 * sizeof(float)                                  // half-warp O hand-over
+           + kHkv * 4 * sizeof(float)                                       // half-warp (m, l) hand-over
            + (kAttnMaxRows + 1) * sizeof(int)                               // row page prefix
-           + 16 * sizeof(int);                                              // scan scratch + abort flag
+           + 32 * sizeof(int)                                               // scan scratch + abort flag
+           + 2 * kHkv * sizeof(int);                                        // hand-over seq / ack flags
 }
 
 // Load 16 bytes of cache elements as floats.
@@ -146,10 +157,26 @@ __device__ __forceinline__ bool stage_wait(uint64_t *bar, uint32_t parity, volat
     return true;
 }
 
+// Bounded wait until *flag == want (a shared-memory hand-over between two
+// warps of the CTA); false on timeout or when another warp set the abort flag.
+__device__ __forceinline__ bool flag_wait(volatile int *flag, int want, volatile int *abort_flag) {
+    if (*flag == want) return true;
+    const long long t0 = clock64();
+    while (*flag != want) {
+        if (*abort_flag) return false;
+        if (clock64() - t0 > kWaitLimitCycles) return false;
+    }
+    return true;
+}
+
 template <typename TC, typename TOut>
-__global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(AttendParams p) {
+__global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendParams p) {
     constexpr int CH = AttnTraits<TC>::CH;
     constexpr int NS = AttnTraits<TC>::NS;
+    constexpr int kHalves = AttnTraits<TC>::HALVES;
+    constexpr int kConsumers = consumers<TC>();
+    constexpr int kThreads = threads<TC>();
+    static_assert(NS % kHalves == 0, "each stage must be consumed by one half");
     constexpr int CPP = kPageTokens / CH;          // chunks per page
     constexpr int HALF = kHkv * CH * kHeadDim;      // elements of K (or V) in a stage
     constexpr int TPQ = CH / 4;                     // tokens per quarter-warp
@@ -166,9 +193,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(AttendParams p
     uint64_t *empty = full + NS;
     float *sscale = reinterpret_cast<float *>(empty + NS);
     float *pbuf = sscale + NS * 2 * kHkv;                                  // [kConsumers][2*CH]
-    int *row_start = reinterpret_cast<int *>(pbuf + kConsumers * 2 * CH);  // [kAttnMaxRows + 1]
-    int *scan = row_start + kAttnMaxRows + 1;       // [0..9] warp totals, [12] abort flag
-    volatile int *abort_flag = scan + 12;
+    float *xo = pbuf + kConsumers * 2 * CH;                                // [kHkv][32 lanes][8]
+    float *xml = xo + kHkv * 32 * 8;                                       // [kHkv][m_a, l_a, m_b, l_b]
+    int *row_start = reinterpret_cast<int *>(xml + kHkv * 4);             // [kAttnMaxRows + 1]
+    int *scan = row_start + kAttnMaxRows + 1;       // [0..16] warp totals, [24] abort flag
+    volatile int *abort_flag = scan + 24;
+    volatile int *xseq = scan + 32;                 // [kHkv] segments handed over by warp g + 8
+    volatile int *xack = xseq + kHkv;               // [kHkv] segments merged by warp g
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n = p.n;
@@ -200,9 +231,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(AttendParams p
     if (lane == 31) scan[warp] = incl;
     if (tid == 0) {
         *abort_flag = 0;
+        for (int k = 0; k < kHkv; ++k) xseq[k] = xack[k] = 0;
         for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumers);
+            mbar_init(&empty[s], kHkv);     // one arrival per kv head: the warp that took the chunk
         }
         fence_mbar_init();
     }
@@ -335,8 +367,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(AttendParams p
         return;
     }
 
-    // ================= consumer warps: warp g <-> kv head g =================
-    const int g = warp;
+    // ============ consumer warps: warps g and g + 8 <-> kv head g ============
+    const int g = warp % kHkv;
+    const int half = warp / kHkv;                   // takes the chunks with iter % 2 == half
     const int qt = lane >> 3, j = lane & 7;
     const int k_idx = j >> KSHIFT;
     const int my_head = k_idx & 1;                   // which of the two q heads this lane's score is
@@ -345,6 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(AttendParams p
     TOut *out = static_cast<TOut *>(p.out);
 
     int iter = 0;
+    int nseg = 0;                                   // segments finished (both halves count alike)
     int r = r0;
     int64_t gp = pb;
     bool abort = false;
@@ -380,6 +414,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(AttendParams p
         for (int jp = j0; jp < j1 && !abort; ++jp) {
 #pragma unroll 1
             for (int cp = 0; cp < CPP; ++cp) {
+                if (iter % kHalves != half) {   // the partner warp takes this chunk
+                    ++iter;
+                    continue;
+                }
                 const int s = iter % NS;
                 const uint32_t ph = static_cast<uint32_t>(iter / NS) & 1u;
                 if (!stage_wait(&full[s], ph, abort_flag)) {
@@ -475,8 +513,58 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(AttendParams p
         if (abort) break;
 
         // ---- segment end ----
-        const float m_a = __shfl_sync(0xffffffffu, m_run, 0), m_b = __shfl_sync(0xffffffffu, m_run, HB);
-        const float l_a = __shfl_sync(0xffffffffu, l_run, 0), l_b = __shfl_sync(0xffffffffu, l_run, HB);
+        float m_a = __shfl_sync(0xffffffffu, m_run, 0), m_b = __shfl_sync(0xffffffffu, m_run, HB);
+        float l_a = __shfl_sync(0xffffffffu, l_run, 0), l_b = __shfl_sync(0xffffffffu, l_run, HB);
+        if constexpr (kHalves > 1) {
+            float *xol = xo + (g * 32 + lane) * 8;
+            if (half == 1) {
+                // Hand (m, l, O) to warp g once it has merged the previous segment.
+                if (!flag_wait(&xack[g], nseg, abort_flag)) {
+                    if (lane == 0) {
+                        report_error(p.err, kErrWaitTimeout, kWhereAttend, static_cast<int>(c), -1000 - nseg);
+                        *abort_flag = 1;
+                    }
+                    break;
+                }
+                *reinterpret_cast<float4 *>(xol) = make_float4(oa[0], oa[1], oa[2], oa[3]);
+                *reinterpret_cast<float4 *>(xol + 4) = make_float4(ob[0], ob[1], ob[2], ob[3]);
+                if (lane == 0) {
+                    xml[g * 4 + 0] = m_a; xml[g * 4 + 1] = l_a; xml[g * 4 + 2] = m_b; xml[g * 4 + 3] = l_b;
+                }
+                __threadfence_block();
+                __syncwarp();
+                if (lane == 0) xseq[g] = nseg + 1;
+                ++nseg;
+                gp = rs + j1;
+                continue;
+            }
+            if (!flag_wait(&xseq[g], nseg + 1, abort_flag)) {
+                if (lane == 0) {
+                    report_error(p.err, kErrWaitTimeout, kWhereAttend, static_cast<int>(c), -2000 - nseg);
+                    *abort_flag = 1;
+                }
+                break;
+            }
+            __threadfence_block();
+            const float4 xa = *reinterpret_cast<const float4 *>(xol);
+            const float4 xb = *reinterpret_cast<const float4 *>(xol + 4);
+            const float m1a = xml[g * 4 + 0], l1a = xml[g * 4 + 1], m1b = xml[g * 4 + 2], l1b = xml[g * 4 + 3];
+            __syncwarp();
+            if (lane == 0) xack[g] = nseg + 1;
+            const float Ma = fmaxf(m_a, m1a), Mb = fmaxf(m_b, m1b);
+            // A half that took no chunk of this segment has m = -inf: its weight is 0.
+            const float s0a = m_a == -INFINITY ? 0.f : exp2f(m_a - Ma), s1a = m1a == -INFINITY ? 0.f : exp2f(m1a - Ma);
+            const float s0b = m_b == -INFINITY ? 0.f : exp2f(m_b - Mb), s1b = m1b == -INFINITY ? 0.f : exp2f(m1b - Mb);
+            oa[0] = oa[0] * s0a + xa.x * s1a; oa[1] = oa[1] * s0a + xa.y * s1a;
+            oa[2] = oa[2] * s0a + xa.z * s1a; oa[3] = oa[3] * s0a + xa.w * s1a;
+            ob[0] = ob[0] * s0b + xb.x * s1b; ob[1] = ob[1] * s0b + xb.y * s1b;
+            ob[2] = ob[2] * s0b + xb.z * s1b; ob[3] = ob[3] * s0b + xb.w * s1b;
+            l_a = l_a * s0a + l1a * s1a;
+            l_b = l_b * s0b + l1b * s1b;
+            m_a = Ma;
+            m_b = Mb;
+        }
+        ++nseg;
         const int64_t c0 = cta_of_page(rs, T, G);
         const int64_t c1 = cta_of_page(re - 1, T, G);
         TOut *orow = out + static_cast<size_t>(r) * kQDim + (2 * g) * kHeadDim + 4 * lane;
@@ -539,7 +627,7 @@ template <typename TC, typename TOut> cudaError_t prepare_t() {
 }
 
 template <typename TC, typename TOut> cudaError_t launch_t(const AttendParams &p, int grid, cudaStream_t st) {
-    decode_attn_kernel<TC, TOut><<<grid, kThreads, smem_bytes<TC>(), st>>>(p);
+    decode_attn_kernel<TC, TOut><<<grid, threads<TC>(), smem_bytes<TC>(), st>>>(p);
     return cudaGetLastError();
 }
 

@@ -121,7 +121,11 @@ def attend_case(pkg, checker, kv_dtype, lens, seed=3, tol=2e-5):
         got = out.cpu().numpy()
         worst = 0.0
         for i, s in enumerate(streams):
-            k, v = dec.gather(0, s, kv_dtype)
+            got_kv = dec.gather(0, s, kv_dtype)
+            if kv_dtype == 2:
+                k, v = fp8_dequant(*got_kv)
+            else:
+                k, v = got_kv
             if kv_dtype == 1:
                 k, v = bits_to_f32(k), bits_to_f32(v)
             want = checker.attend(qv[i], k, v)
@@ -146,6 +150,22 @@ def test_attention_many_rows(pkg, checker):
     rng = np.random.default_rng(4)
     lens = rng.integers(1, 300, size=40).tolist()
     attend_case(pkg, checker, 1, lens, seed=9)
+
+
+@pytest.mark.parametrize("kv_dtype", [0, 1, 2])
+def test_attention_many_rows_multi_segment(pkg, checker, kv_dtype):
+    """200 rows, ~3800 pages: every CTA's page range spans several rows, so
+    each CTA runs several segments back to back (for the e4m3 cache, each one
+    ends in the hand-over between the two warps of a kv head)."""
+    rng = np.random.default_rng(21)
+    lens = rng.integers(1, 600, size=200).tolist()
+    attend_case(pkg, checker, kv_dtype, lens, seed=11)
+
+
+@pytest.mark.parametrize("lens", [[1, 2, 15, 16, 17, 31, 32, 33], [4096, 5, 700, 64, 1, 2500]])
+def test_attention_fp8_against_dequantised_cache(pkg, checker, lens):
+    """e4m3 cache: K2 equals exact attention over the dequantised cache."""
+    attend_case(pkg, checker, 2, lens)
 
 
 def test_attention_repeated_launches_reset_counters(pkg, checker):
@@ -237,6 +257,15 @@ def e4m3_to_f32(b: np.ndarray) -> np.ndarray:
     m = b & 0x7
     val = np.where(e == 0, m / 8.0 * 2.0 ** -6, (1.0 + m / 8.0) * 2.0 ** (e - 7))
     return (sign * val).astype(np.float32)
+
+
+def fp8_dequant(k_b, v_b, scales):
+    """(tokens, 1024) e4m3 bytes + (pages, 2, 8) scales -> f32 K and V."""
+    L = k_b.shape[0]
+    pg = np.arange(L) // 16
+    k = e4m3_to_f32(k_b).reshape(L, 8, 128) * scales[pg, 0, :, None]
+    v = e4m3_to_f32(v_b).reshape(L, 8, 128) * scales[pg, 1, :, None]
+    return k.reshape(L, 1024).astype(np.float32), v.reshape(L, 1024).astype(np.float32)
 
 
 @pytest.mark.parametrize("style", ["batch", "token_by_token"])
