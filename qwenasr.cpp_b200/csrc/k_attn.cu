@@ -108,12 +108,6 @@ template <> __device__ __forceinline__ float4 load4<__nv_bfloat16>(const __nv_bf
     const uint2 w = *reinterpret_cast<const uint2 *>(p);
     return make_float4(bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y));
 }
-template <> __device__ __forceinline__ float4 load4<uint8_t>(const uint8_t *p) {
-    const uint32_t w = *reinterpret_cast<const uint32_t *>(p);
-    const float2 a = e4m3x2_to_f2(static_cast<uint16_t>(w & 0xffffu));
-    const float2 b = e4m3x2_to_f2(static_cast<uint16_t>(w >> 16));
-    return make_float4(a.x, a.y, b.x, b.y);
-}
 
 template <typename TOut> __device__ __forceinline__ void store4(TOut *p, float4 v);
 template <> __device__ __forceinline__ void store4<float>(float *p, float4 v) {
@@ -408,6 +402,15 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
                 }
             }
         }
+        // e4m3 cache: q as f16 pairs for the mixed-precision dot (f16 x f16 -> f32).
+        uint32_t qa2[kFp8 ? 8 : 1], qb2[kFp8 ? 8 : 1];
+        if constexpr (kFp8) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                qa2[i] = pack_h2(qa[2 * i], qa[2 * i + 1]);
+                qb2[i] = pack_h2(qb[2 * i], qb[2 * i + 1]);
+            }
+        }
         float m_run = -INFINITY, l_run = 0.0f;
         float oa[4] = {0.f, 0.f, 0.f, 0.f}, ob[4] = {0.f, 0.f, 0.f, 0.f};
 
@@ -444,14 +447,29 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
                     for (int t = 0; t < TPQ; ++t) {
                         const TC *krow = kst + (qt * TPQ + t) * kHeadDim;
                         float acc_a = 0.f, acc_b = 0.f;
+                        if constexpr (kFp8) {
+                            // 16 e4m3 -> 8 f16x2 (exact), two mixed-precision FMAs per pair and head.
+                            const uint4 w = *reinterpret_cast<const uint4 *>(krow + j * 16);
+                            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-                        for (int cc = 0; cc < NC; ++cc) {
-                            float kv[E];
-                            Chunk16<TC>::load(krow + (j + 8 * cc) * E, kv);
+                            for (int k = 0; k < 4; ++k) {
+                                const uint32_t x = e4m3x2_to_h2(static_cast<uint16_t>(ws[k] & 0xffffu));
+                                const uint32_t y = e4m3x2_to_h2(static_cast<uint16_t>(ws[k] >> 16));
+                                dot2_f16_f32(acc_a, qa2[2 * k], x);
+                                dot2_f16_f32(acc_a, qa2[2 * k + 1], y);
+                                dot2_f16_f32(acc_b, qb2[2 * k], x);
+                                dot2_f16_f32(acc_b, qb2[2 * k + 1], y);
+                            }
+                        } else {
 #pragma unroll
-                            for (int e = 0; e < E; ++e) {
-                                acc_a = fmaf(qa[cc * E + e], kv[e], acc_a);
-                                acc_b = fmaf(qb[cc * E + e], kv[e], acc_b);
+                            for (int cc = 0; cc < NC; ++cc) {
+                                float kv[E];
+                                Chunk16<TC>::load(krow + (j + 8 * cc) * E, kv);
+#pragma unroll
+                                for (int e = 0; e < E; ++e) {
+                                    acc_a = fmaf(qa[cc * E + e], kv[e], acc_a);
+                                    acc_b = fmaf(qb[cc * E + e], kv[e], acc_b);
+                                }
                             }
                         }
                         part[2 * t + 0] = acc_a;
@@ -476,31 +494,69 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
                     }
                     l_run = l_run * alpha + ps;
                     m_run = m_new;
-                    my_p[my_head * CH + my_tok] = pv * sv;
+                    if constexpr (kFp8) {
+                        reinterpret_cast<__half *>(my_p)[my_head * CH + my_tok] = __float2half_rn(pv);
+                    } else {
+                        my_p[my_head * CH + my_tok] = pv;
+                    }
                     const float al_a = __shfl_sync(0xffffffffu, alpha, 0);
                     const float al_b = __shfl_sync(0xffffffffu, alpha, HB);
                     __syncwarp();
                     // ---- PV ----
+                    if constexpr (kFp8) {
+                        // p (f16) x V (e4m3 -> f16x2, exact) accumulated in f32 for this
+                        // chunk (= one page), then scaled by the page's V scale once.
+                        float xa[4] = {0.f, 0.f, 0.f, 0.f}, xb[4] = {0.f, 0.f, 0.f, 0.f};
+                        const uint16_t *phalf = reinterpret_cast<const uint16_t *>(my_p);
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        oa[e] *= al_a;
-                        ob[e] *= al_b;
-                    }
+                        for (int t4 = 0; t4 < CH; t4 += 4) {
+                            const uint2 pa = *reinterpret_cast<const uint2 *>(phalf + t4);
+                            const uint2 pb = *reinterpret_cast<const uint2 *>(phalf + CH + t4);
 #pragma unroll
-                    for (int t4 = 0; t4 < CH; t4 += 4) {
-                        const float4 pa4 = *reinterpret_cast<const float4 *>(my_p + t4);
-                        const float4 pb4 = *reinterpret_cast<const float4 *>(my_p + CH + t4);
-                        const float pa[4] = {pa4.x, pa4.y, pa4.z, pa4.w};
-                        const float pbv[4] = {pb4.x, pb4.y, pb4.z, pb4.w};
+                            for (int u = 0; u < 4; ++u) {
+                                const int t = t4 + u;
+                                if (t < nvalid) {
+                                    const uint32_t w = *reinterpret_cast<const uint32_t *>(vst + t * kHeadDim + 4 * lane);
+                                    const uint32_t x = e4m3x2_to_h2(static_cast<uint16_t>(w & 0xffffu));
+                                    const uint32_t y = e4m3x2_to_h2(static_cast<uint16_t>(w >> 16));
+                                    const uint32_t wa = u < 2 ? pa.x : pa.y, wb = u < 2 ? pb.x : pb.y;
+                                    if (u & 1) {
+                                        axpy2_f16_f32<1>(xa[0], xa[1], x, wa); axpy2_f16_f32<1>(xa[2], xa[3], y, wa);
+                                        axpy2_f16_f32<1>(xb[0], xb[1], x, wb); axpy2_f16_f32<1>(xb[2], xb[3], y, wb);
+                                    } else {
+                                        axpy2_f16_f32<0>(xa[0], xa[1], x, wa); axpy2_f16_f32<0>(xa[2], xa[3], y, wa);
+                                        axpy2_f16_f32<0>(xb[0], xb[1], x, wb); axpy2_f16_f32<0>(xb[2], xb[3], y, wb);
+                                    }
+                                }
+                            }
+                        }
 #pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const int t = t4 + u;
-                            if (t < nvalid) {
-                                const float4 v = load4<TC>(vst + t * kHeadDim + 4 * lane);
-                                oa[0] = fmaf(pa[u], v.x, oa[0]); oa[1] = fmaf(pa[u], v.y, oa[1]);
-                                oa[2] = fmaf(pa[u], v.z, oa[2]); oa[3] = fmaf(pa[u], v.w, oa[3]);
-                                ob[0] = fmaf(pbv[u], v.x, ob[0]); ob[1] = fmaf(pbv[u], v.y, ob[1]);
-                                ob[2] = fmaf(pbv[u], v.z, ob[2]); ob[3] = fmaf(pbv[u], v.w, ob[3]);
+                        for (int e = 0; e < 4; ++e) {
+                            oa[e] = fmaf(sv, xa[e], oa[e] * al_a);
+                            ob[e] = fmaf(sv, xb[e], ob[e] * al_b);
+                        }
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            oa[e] *= al_a;
+                            ob[e] *= al_b;
+                        }
+#pragma unroll
+                        for (int t4 = 0; t4 < CH; t4 += 4) {
+                            const float4 pa4 = *reinterpret_cast<const float4 *>(my_p + t4);
+                            const float4 pb4 = *reinterpret_cast<const float4 *>(my_p + CH + t4);
+                            const float pa[4] = {pa4.x, pa4.y, pa4.z, pa4.w};
+                            const float pbv[4] = {pb4.x, pb4.y, pb4.z, pb4.w};
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                const int t = t4 + u;
+                                if (t < nvalid) {
+                                    const float4 v = load4<TC>(vst + t * kHeadDim + 4 * lane);
+                                    oa[0] = fmaf(pa[u], v.x, oa[0]); oa[1] = fmaf(pa[u], v.y, oa[1]);
+                                    oa[2] = fmaf(pa[u], v.z, oa[2]); oa[3] = fmaf(pa[u], v.w, oa[3]);
+                                    ob[0] = fmaf(pbv[u], v.x, ob[0]); ob[1] = fmaf(pbv[u], v.y, ob[1]);
+                                    ob[2] = fmaf(pbv[u], v.z, ob[2]); ob[3] = fmaf(pbv[u], v.w, ob[3]);
+                                }
                             }
                         }
                     }

@@ -4,9 +4,11 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <string.h>
 
 namespace qkv {
 
@@ -64,6 +66,38 @@ __device__ __forceinline__ float2 e4m3x2_to_f2(uint16_t v) {
     const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(v), __NV_E4M3);
     const __half2 hh = *reinterpret_cast<const __half2 *>(&h);
     return __half22float2(hh);
+}
+// Two e4m3 bytes (low byte first) -> f16x2 bits (low half = low byte); exact.
+__device__ __forceinline__ uint32_t e4m3x2_to_h2(uint16_t v) {
+    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(v), __NV_E4M3);
+    uint32_t bits;
+    memcpy(&bits, &h, sizeof(bits));
+    return bits;
+}
+// acc += lo(a) * lo(b) + hi(a) * hi(b): f16 operands, products exact in f32,
+// f32 accumulation (PTX fma.rn.f32.f16, sm_100).
+__device__ __forceinline__ void dot2_f16_f32(float &acc, uint32_t a, uint32_t b) {
+    asm("{\n\t.reg .f16 al, ah, bl, bh;\n\tmov.b32 {al, ah}, %1;\n\tmov.b32 {bl, bh}, %2;\n\t"
+        "fma.rn.f32.f16 %0, al, bl, %0;\n\tfma.rn.f32.f16 %0, ah, bh, %0;\n\t}"
+        : "+f"(acc) : "r"(a), "r"(b));
+}
+// acc0 += lo(v) * p, acc1 += hi(v) * p with p = half H (0 low, 1 high) of pw.
+template <int H> __device__ __forceinline__ void axpy2_f16_f32(float &acc0, float &acc1, uint32_t v, uint32_t pw) {
+    if constexpr (H == 0) {
+        asm("{\n\t.reg .f16 vl, vh, pl, ph;\n\tmov.b32 {vl, vh}, %2;\n\tmov.b32 {pl, ph}, %3;\n\t"
+            "fma.rn.f32.f16 %0, vl, pl, %0;\n\tfma.rn.f32.f16 %1, vh, pl, %1;\n\t}"
+            : "+f"(acc0), "+f"(acc1) : "r"(v), "r"(pw));
+    } else {
+        asm("{\n\t.reg .f16 vl, vh, pl, ph;\n\tmov.b32 {vl, vh}, %2;\n\tmov.b32 {pl, ph}, %3;\n\t"
+            "fma.rn.f32.f16 %0, vl, ph, %0;\n\tfma.rn.f32.f16 %1, vh, ph, %1;\n\t}"
+            : "+f"(acc0), "+f"(acc1) : "r"(v), "r"(pw));
+    }
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    const __half2 v = __floats2half2_rn(lo, hi);
+    uint32_t bits;
+    memcpy(&bits, &v, sizeof(bits));
+    return bits;
 }
 __device__ __forceinline__ uint8_t f_to_e4m3(float v) {
     return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));

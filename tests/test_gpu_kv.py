@@ -101,7 +101,13 @@ def test_gather_roundtrip_permuted(pkg, checker, seed):
             dec.close_stream(s)
 
 
-def attend_case(pkg, checker, kv_dtype, lens, seed=3, tol=2e-5):
+def attend_case(pkg, checker, kv_dtype, lens, seed=3, tol=None):
+    """K2 against exact f32 attention over the cache as stored (bf16 widened,
+    e4m3 dequantised with its page scales).  f32/bf16: 2e-5 relative.  e4m3:
+    2e-3 relative, because K2 holds q and the softmax weights p as f16 for its
+    mixed-precision f16 x f16 -> f32 FMAs (2^-12 relative rounding each)."""
+    if tol is None:
+        tol = 2e-3 if kv_dtype == 2 else 2e-5
     dec, qn, kn = kv_handle(pkg, kv_dtype, seed=seed, max_streams=len(lens), max_context=max(lens) + 16)
     with dec:
         rng = np.random.default_rng(seed)
