@@ -6,9 +6,15 @@
 //
 // Swap-AB: the MMA's M side is 128 weight rows (output features) and its N
 // side is a tile of BN tokens, so a decode step's handful of tokens is a
-// legal N (16..256) while the weights stream through at full width.  Skinny
-// shapes split K across CTAs (grid.z) and accumulate with f32 red.add, so a
-// 1024-wide projection still puts ~150-300 CTAs on the memory system.
+// legal N (32..256) while the weights stream through at full width.
+//
+// Persistent: a grid of at most one CTA per SM walks the work units (weight
+// tile, token tile, K split) round-robin.  The TMA ring runs on across unit
+// boundaries, and the accumulator is double-buffered in TMEM (2 x BN columns)
+// so the epilogue of one unit overlaps the MMAs of the next.  Skinny shapes
+// split K over units and add with f32 red.add into a zeroed C; unsplit units
+// store (or read-add-write for accumulate), which keeps them deterministic.
+// The host picks BN and the split count with a small cost model.
 //
 // CTA = 6 warps: warp 0 TMA producer, warp 1 TMEM allocator + MMA issuer
 // (one thread), warps 2..5 epilogue (TMEM lane quadrant = warp % 4, one
@@ -33,15 +39,16 @@ template <int BN> struct TcTraits {
     static constexpr uint32_t kBBytes = BN * kBK * 2;
     static constexpr int NS = BN <= 32 ? 8 : BN <= 64 ? 8 : BN <= 128 ? 6 : 4;
     static constexpr uint32_t kStage = kABytes + kBBytes;
-    static constexpr int kCols = BN < 32 ? 32 : BN;  // TMEM columns (power of two >= 32)
+    static constexpr int kCols = 2 * BN;             // two accumulators (power of two, 64..512 columns)
     static constexpr size_t kSmem = 1024 /*align slack*/ + static_cast<size_t>(NS) * kStage + 256;
 };
 
 struct TcParams {
     int M, N, K;
     int ktiles_per_split;
+    int tiles_n, tiles_m, splits;   // units = tiles_n * tiles_m * splits, token tile fastest
     float *C;
-    int accumulate;   // 0: store (single split) / red.add into a zeroed C; 1: red.add into C
+    int accumulate;   // 0: store (one split) / red.add into a zeroed C; 1: add into C
     DevError *err;
 };
 
@@ -95,15 +102,18 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
-    uint32_t r[8];
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-                 : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+// 32 consecutive TMEM columns of this warp's 32 lanes; the caller waits (tcgen05.wait::ld).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
 }
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ bool bounded_wait(uint64_t *bar, uint32_t parity) {
     return mbar_wait(bar, parity, kWaitLimitCycles);
@@ -119,24 +129,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint8_t *tiles = smem;
     uint64_t *full = reinterpret_cast<uint64_t *>(tiles + static_cast<size_t>(T::NS) * T::kStage);
     uint64_t *empty = full + T::NS;
-    uint64_t *acc_full = empty + T::NS;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
+    uint64_t *acc_full = empty + T::NS;      // [2] MMA -> epilogue
+    uint64_t *acc_empty = acc_full + 2;      // [2] epilogue -> MMA
+    uint64_t *mma_done = acc_empty + 2;      // MMA thread's own drain
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
     volatile int *failed = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * kBM;
-    const int m0 = blockIdx.y * BN;
     const int ktiles = p.K / kBK;
-    const int kt0 = blockIdx.z * p.ktiles_per_split;
-    const int kt1 = min(ktiles, kt0 + p.ktiles_per_split);
-    const int nk = kt1 > kt0 ? kt1 - kt0 : 0;
+    const int units = p.tiles_n * p.tiles_m * p.splits;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < T::NS; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(acc_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        mbar_init(mma_done, 1);
         *failed = 0;
         fence_mbar_init();
     }
@@ -151,29 +163,48 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // unit u -> token tile (fastest), weight tile, K split
+    auto unit_coords = [&](int u, int &n0, int &m0, int &kt0, int &nk) {
+        const int tm = u % p.tiles_m;
+        const int rest = u / p.tiles_m;
+        const int tn = rest % p.tiles_n;
+        const int sp = rest / p.tiles_n;
+        n0 = tn * kBM;
+        m0 = tm * BN;
+        kt0 = sp * p.ktiles_per_split;
+        const int kt1 = min(ktiles, kt0 + p.ktiles_per_split);
+        nk = kt1 > kt0 ? kt1 - kt0 : 0;
+    };
+
     if (warp == 0) {
-        if (lane == 0 && nk > 0) {
+        if (lane == 0) {
             const uint64_t pol_w = l2_evict_first_policy();
             const uint64_t pol_x = l2_evict_last_policy();
-            int issued = 0;
-            for (int i = 0; i < nk; ++i) {
-                const int s = i % T::NS;
-                const uint32_t ph = static_cast<uint32_t>(i / T::NS) & 1u;
-                if (*failed || !bounded_wait(&empty[s], ph ^ 1u)) {
-                    report_error(p.err, kErrWaitTimeout, kWhereGemm, blockIdx.x, i);
-                    *failed = 1;
-                    break;
+            int it = 0;
+            bool bad = false;
+            for (int u = blockIdx.x; u < units && !bad; u += gridDim.x) {
+                int n0, m0, kt0, nk;
+                unit_coords(u, n0, m0, kt0, nk);
+                for (int i = 0; i < nk; ++i) {
+                    const int s = it % T::NS;
+                    const uint32_t ph = static_cast<uint32_t>(it / T::NS) & 1u;
+                    if (*failed || !bounded_wait(&empty[s], ph ^ 1u)) {
+                        report_error(p.err, kErrWaitTimeout, kWhereGemm, blockIdx.x, it);
+                        *failed = 1;
+                        bad = true;
+                        break;
+                    }
+                    uint8_t *a = tiles + static_cast<size_t>(s) * T::kStage;
+                    uint8_t *b = a + kABytes;
+                    mbar_arrive_expect_tx(&full[s], T::kStage);
+                    const int kx = (kt0 + i) * kBK;
+                    tma_load_2d(a, &tmW, kx, n0, &full[s], pol_w);
+                    tma_load_2d(b, &tmX, kx, m0, &full[s], pol_x);
+                    ++it;
                 }
-                uint8_t *a = tiles + static_cast<size_t>(s) * T::kStage;
-                uint8_t *b = a + kABytes;
-                mbar_arrive_expect_tx(&full[s], T::kStage);
-                const int kx = (kt0 + i) * kBK;
-                tma_load_2d(a, &tmW, kx, n0, &full[s], pol_w);
-                tma_load_2d(b, &tmX, kx, m0, &full[s], pol_x);
-                ++issued;
             }
             // Drain: every tile this thread asked for has landed before the CTA can exit.
-            for (int i = issued > T::NS ? issued - T::NS : 0; i < issued; ++i) {
+            for (int i = it > T::NS ? it - T::NS : 0; i < it; ++i) {
                 if (!bounded_wait(&full[i % T::NS], static_cast<uint32_t>(i / T::NS) & 1u)) {
                     report_error(p.err, kErrWaitTimeout, kWhereGemm, blockIdx.x, -(1 << 21));
                     break;
@@ -183,63 +214,93 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             const uint32_t idesc = idesc_bf16<BN>();
-            int issued = 0;
-            for (int i = 0; i < nk; ++i) {
-                const int s = i % T::NS;
-                const uint32_t ph = static_cast<uint32_t>(i / T::NS) & 1u;
-                if (*failed || !bounded_wait(&full[s], ph)) {
-                    report_error(p.err, kErrWaitTimeout, kWhereGemm, blockIdx.x, -1 - i);
+            int it = 0, j = 0;
+            bool bad = false, any = false;
+            for (int u = blockIdx.x; u < units && !bad; u += gridDim.x, ++j) {
+                int n0, m0, kt0, nk;
+                unit_coords(u, n0, m0, kt0, nk);
+                const int b = j & 1;
+                if (*failed || !bounded_wait(&acc_empty[b], (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u)) {
+                    report_error(p.err, kErrWaitTimeout, kWhereGemm, blockIdx.x, -(1 << 22) - j);
                     *failed = 1;
                     break;
                 }
                 tc_fence_after();
-                const uint8_t *a = tiles + static_cast<size_t>(s) * T::kStage;
-                const uint8_t *b = a + kABytes;
-                const uint64_t da = smem_desc_sw128(a), db = smem_desc_sw128(b);
+                const uint32_t d = tmem + static_cast<uint32_t>(b * BN);
+                for (int i = 0; i < nk; ++i) {
+                    const int s = it % T::NS;
+                    const uint32_t ph = static_cast<uint32_t>(it / T::NS) & 1u;
+                    if (*failed || !bounded_wait(&full[s], ph)) {
+                        report_error(p.err, kErrWaitTimeout, kWhereGemm, blockIdx.x, -1 - it);
+                        *failed = 1;
+                        bad = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint8_t *a = tiles + static_cast<size_t>(s) * T::kStage;
+                    const uint8_t *bb = a + kABytes;
+                    const uint64_t da = smem_desc_sw128(a), db = smem_desc_sw128(bb);
 #pragma unroll
-                for (int kk = 0; kk < kBK / 16; ++kk) {
-                    // advance 16 bf16 = 32 bytes inside the swizzle atom (descriptor units of 16 B)
-                    mma_bf16(tmem, da + 2ull * kk, db + 2ull * kk, idesc, (i > 0 || kk > 0) ? 1 : 0);
+                    for (int kk = 0; kk < kBK / 16; ++kk) {
+                        // advance 16 bf16 = 32 bytes inside the swizzle atom (descriptor units of 16 B)
+                        mma_bf16(d, da + 2ull * kk, db + 2ull * kk, idesc, (i > 0 || kk > 0) ? 1 : 0);
+                    }
+                    mma_commit(&empty[s]);
+                    any = true;
+                    ++it;
                 }
-                mma_commit(&empty[s]);
-                ++issued;
+                if (bad) break;
+                mma_commit(&acc_full[b]);
             }
-            // acc_full completes only when every MMA this thread issued has finished,
-            // also on the failure path (TMEM is freed after the epilogue saw it).
-            if (issued > 0) mma_commit(acc_full);
-            else mbar_arrive(acc_full);
+            // Every MMA this thread issued has completed before TMEM can be freed.
+            if (any) {
+                mma_commit(mma_done);
+                if (!bounded_wait(mma_done, 0)) report_error(p.err, kErrWaitTimeout, kWhereGemm, blockIdx.x, -(1 << 23));
+            }
         }
         __syncwarp();
     } else {
-        // epilogue: warps 2..5, TMEM lanes 32*(warp%4) .. +31 = weight rows of this tile
+        // epilogue: warps 2..5, TMEM lanes 32*(warp%4) .. +31 = weight rows of the unit
         const int q = warp & 3;
-        const int row = 32 * q + lane;
-        const int n = n0 + row;
-        const bool have = bounded_wait(acc_full, 0);
-        if (!have) report_error(p.err, kErrWaitTimeout, kWhereGemm, blockIdx.x, 1 << 20);
-        tc_fence_after();
-        // Warp-uniform: tcgen05.ld is .sync.aligned, every lane of the warp must issue it.
-        const bool valid_acc = __all_sync(0xffffffffu, have && nk > 0 && !*failed);
-        const bool atomic = p.accumulate || gridDim.z > 1;
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 8) {
-            float v[8];
-            if (valid_acc) {
-                tmem_ld8(tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(c), v);
-            } else {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) v[j] = 0.0f;
+        int j = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
+            int n0, m0, kt0, nk;
+            unit_coords(u, n0, m0, kt0, nk);
+            const int b = j & 1;
+            const bool have = bounded_wait(&acc_full[b], static_cast<uint32_t>(j >> 1) & 1u);
+            tc_fence_after();
+            // Warp-uniform: tcgen05.ld is .sync.aligned, every lane of the warp must issue it.
+            if (!__all_sync(0xffffffffu, have && !*failed)) {
+                if (lane == 0) {
+                    report_error(p.err, kErrWaitTimeout, kWhereGemm, blockIdx.x, (1 << 20) + j);
+                    *failed = 1;
+                }
+                break;
             }
-            if (n < p.N) {
+            const int n = n0 + 32 * q + lane;
+            const bool split = p.splits > 1;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                uint32_t r[32];
+                tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(b * BN + c), r);
+                tmem_wait_ld();
+                if (c + 32 >= BN) {
+                    // accumulator b fully read: hand it back to the MMA thread
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[b]);
+                }
+                if (n < p.N) {
+                    float *dst = p.C + static_cast<size_t>(m0 + c) * p.N + n;
+                    const int mlim = p.M - (m0 + c);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int m = m0 + c + j;
-                    if (m < p.M) {
-                        float *dst = p.C + static_cast<size_t>(m) * p.N + n;
-                        if (atomic) {
-                            if (valid_acc) atomicAdd(dst, v[j]);
-                        } else {
-                            *dst = v[j];
+                    for (int jj = 0; jj < 32; ++jj) {
+                        if (jj < mlim) {
+                            const float v = __uint_as_float(r[jj]);
+                            float *dp = dst + static_cast<size_t>(jj) * p.N;
+                            if (split) atomicAdd(dp, v);
+                            else if (p.accumulate) *dp += v;
+                            else *dp = v;
                         }
                     }
                 }
@@ -323,29 +384,66 @@ template <int BN> cudaError_t prepare_bn() {
 }
 
 template <int BN>
-cudaError_t launch_bn(const void *X, const void *W, float *C, int M, int N, int K, int accumulate, int num_sms,
-                      DevError *err, cudaStream_t st) {
+cudaError_t launch_bn(const void *X, const void *W, float *C, int M, int N, int K, int accumulate, int splits,
+                      int num_sms, DevError *err, cudaStream_t st) {
     CUtensorMap tw, tx;
     if (!cached_map(&tw, W, N, K, kBM) || !cached_map(&tx, X, M, K, BN)) return cudaErrorInvalidValue;
     const int tiles_n = (N + kBM - 1) / kBM, tiles_m = (M + BN - 1) / BN;
     const int ktiles = K / kBK;
-    int splits = 1;
-    const int tiles = tiles_n * tiles_m;
-    if (tiles < num_sms) {
-        splits = (2 * num_sms + tiles - 1) / tiles;
-        const int max_splits = ktiles / 2 > 0 ? ktiles / 2 : 1;
-        if (splits > max_splits) splits = max_splits;
-    }
     const int kps = (ktiles + splits - 1) / splits;
-    splits = (ktiles + kps - 1) / kps;
+    splits = (ktiles + kps - 1) / kps;     // every split owns >= 1 k-tile
     if (splits > 1 && !accumulate) {
         cudaError_t e = cudaMemsetAsync(C, 0, static_cast<size_t>(M) * N * sizeof(float), st);
         if (e != cudaSuccess) return e;
     }
-    TcParams p{M, N, K, kps, C, accumulate, err};
-    dim3 grid(tiles_n, tiles_m, splits);
+    TcParams p{M, N, K, kps, tiles_n, tiles_m, splits, C, accumulate, err};
+    const int units = tiles_n * tiles_m * splits;
+    const int grid = units < num_sms ? units : num_sms;
     gemm_tc_kernel<BN><<<grid, kGemmThreads, TcTraits<BN>::kSmem, st>>>(tw, tx, p);
     return cudaGetLastError();
+}
+
+// Cost model for the tile width BN and the K split: per-SM time of one
+// k-tile = max(MMA time, operand bytes over a per-SM share of L2/HBM
+// bandwidth), times the k-tiles of the SM that gets the most units, plus a
+// fixed pipeline-fill/epilogue term per unit and a red.add term when split.
+struct GemmPlan {
+    int bn, splits;
+};
+
+GemmPlan plan_gemm(int M, int N, int K, int num_sms) {
+    const double kMmaPerSm = 1.45e15 / 148.0;       // dense bf16 flop/s per SM
+    const double kBytesPerSm = 110e9;               // operand ingest per SM (L2-served)
+    const double kHbm = 6.2e12;                     // whole-chip weight streaming
+    const double kFixed = 1.2e-6;                   // per-unit fill + epilogue tail
+    const int ktiles = K / kBK;
+    const int tiles_n = (N + kBM - 1) / kBM;
+    GemmPlan best{256, 1};
+    double best_t = 1e30;
+    for (int bn : {32, 64, 128, 256}) {
+        if (bn > 32 && (bn / 2) >= M) break;          // a narrower tile already covers all tokens
+        const int tiles_m = (M + bn - 1) / bn;
+        const int tiles = tiles_n * tiles_m;
+        const int max_split = ktiles < 32 ? ktiles : 32;
+        for (int sp = 1; sp <= max_split; ++sp) {
+            const int kps = (ktiles + sp - 1) / sp;
+            const int spr = (ktiles + kps - 1) / kps;
+            if (spr != sp) continue;
+            const long units = static_cast<long>(tiles) * sp;
+            const long waves = (units + num_sms - 1) / num_sms;
+            const double t_mma = 2.0 * kBM * bn * kBK / kMmaPerSm;
+            const double t_ld = (kBM * kBK * 2.0 + bn * kBK * 2.0) / kBytesPerSm;
+            double t = waves * (kps * (t_mma > t_ld ? t_mma : t_ld) + kFixed);
+            const double t_w = static_cast<double>(N) * K * 2.0 / kHbm;   // weights read from HBM once
+            if (t_w > t) t = t_w;
+            if (sp > 1) t += static_cast<double>(M) * N * 4.0 * sp / 2.0e12 + 1.0e-6;   // memset + red.add
+            if (t < best_t * 0.98) {
+                best_t = t;
+                best = {bn, sp};
+            }
+        }
+    }
+    return best;
 }
 
 }  // namespace
@@ -370,10 +468,13 @@ cudaError_t launch_gemm_tc(const void *X, const void *W, float *C, int M, int N,
                            DevError *err, cudaStream_t st) {
     if (M <= 0 || N <= 0) return cudaSuccess;
     if (K % kBK != 0) return cudaErrorInvalidValue;
-    if (M <= 32) return launch_bn<32>(X, W, C, M, N, K, accumulate, num_sms, err, st);
-    if (M <= 64) return launch_bn<64>(X, W, C, M, N, K, accumulate, num_sms, err, st);
-    if (M <= 128) return launch_bn<128>(X, W, C, M, N, K, accumulate, num_sms, err, st);
-    return launch_bn<256>(X, W, C, M, N, K, accumulate, num_sms, err, st);
+    const GemmPlan pl = plan_gemm(M, N, K, num_sms);
+    switch (pl.bn) {
+        case 32: return launch_bn<32>(X, W, C, M, N, K, accumulate, pl.splits, num_sms, err, st);
+        case 64: return launch_bn<64>(X, W, C, M, N, K, accumulate, pl.splits, num_sms, err, st);
+        case 128: return launch_bn<128>(X, W, C, M, N, K, accumulate, pl.splits, num_sms, err, st);
+        default: return launch_bn<256>(X, W, C, M, N, K, accumulate, pl.splits, num_sms, err, st);
+    }
 }
 
 }  // namespace qkv
