@@ -311,10 +311,11 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
                                 const size_t kbase = (static_cast<size_t>(page) * 2) * kPageHalfElems;
                                 const size_t vbase = kbase + kPageHalfElems;
                                 if constexpr (CH == kPageTokens) {
+                                    // K and V halves of a page are contiguous: one copy (a CTA
+                                    // issues bulk copies at a bounded rate, so bytes per copy count).
                                     constexpr uint32_t half_bytes = HALF * sizeof(TC);
                                     mbar_arrive_expect_tx(&full[s], 2 * half_bytes + (kFp8 ? 64u : 0u));
-                                    bulk_g2s(dst, pool + kbase, half_bytes, &full[s], pol);
-                                    bulk_g2s(dst + HALF, pool + vbase, half_bytes, &full[s], pol);
+                                    bulk_g2s(dst, pool + kbase, 2 * half_bytes, &full[s], pol);
                                     if constexpr (kFp8) {
                                         bulk_g2s(sscale + s * 2 * kHkv, p.scales + static_cast<size_t>(page) * 2 * kHkv,
                                                  64u, &full[s], pol);
