@@ -454,8 +454,8 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
                             const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
                             for (int k = 0; k < 4; ++k) {
-                                const uint32_t x = e4m3x2_to_h2(static_cast<uint16_t>(ws[k] & 0xffffu));
-                                const uint32_t y = e4m3x2_to_h2(static_cast<uint16_t>(ws[k] >> 16));
+                                uint32_t x, y;
+                                e4m3x4_to_h2x2(ws[k], x, y);
                                 dot2_f16_f32(acc_a, qa2[2 * k], x);
                                 dot2_f16_f32(acc_a, qa2[2 * k + 1], y);
                                 dot2_f16_f32(acc_b, qb2[2 * k], x);
@@ -509,26 +509,38 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
                         // chunk (= one page), then scaled by the page's V scale once.
                         float xa[4] = {0.f, 0.f, 0.f, 0.f}, xb[4] = {0.f, 0.f, 0.f, 0.f};
                         const uint16_t *phalf = reinterpret_cast<const uint16_t *>(my_p);
+                        // One token of V for this lane's 4 dims, both heads.
+                        auto pv_token = [&](int t, uint32_t wa, uint32_t wb, int hsel) {
+                            const uint32_t w = *reinterpret_cast<const uint32_t *>(vst + t * kHeadDim + 4 * lane);
+                            uint32_t x, y;
+                            e4m3x4_to_h2x2(w, x, y);
+                            if (hsel) {
+                                axpy2_f16_f32<1>(xa[0], xa[1], x, wa); axpy2_f16_f32<1>(xa[2], xa[3], y, wa);
+                                axpy2_f16_f32<1>(xb[0], xb[1], x, wb); axpy2_f16_f32<1>(xb[2], xb[3], y, wb);
+                            } else {
+                                axpy2_f16_f32<0>(xa[0], xa[1], x, wa); axpy2_f16_f32<0>(xa[2], xa[3], y, wa);
+                                axpy2_f16_f32<0>(xb[0], xb[1], x, wb); axpy2_f16_f32<0>(xb[2], xb[3], y, wb);
+                            }
+                        };
+                        if (nvalid == CH) {     // full page: no per-token guard
 #pragma unroll
-                        for (int t4 = 0; t4 < CH; t4 += 4) {
-                            const uint2 pa = *reinterpret_cast<const uint2 *>(phalf + t4);
-                            const uint2 pb = *reinterpret_cast<const uint2 *>(phalf + CH + t4);
+                            for (int t4 = 0; t4 < CH; t4 += 4) {
+                                const uint2 pa = *reinterpret_cast<const uint2 *>(phalf + t4);
+                                const uint2 pb = *reinterpret_cast<const uint2 *>(phalf + CH + t4);
+                                pv_token(t4 + 0, pa.x, pb.x, 0);
+                                pv_token(t4 + 1, pa.x, pb.x, 1);
+                                pv_token(t4 + 2, pa.y, pb.y, 0);
+                                pv_token(t4 + 3, pa.y, pb.y, 1);
+                            }
+                        } else {
 #pragma unroll
-                            for (int u = 0; u < 4; ++u) {
-                                const int t = t4 + u;
-                                if (t < nvalid) {
-                                    const uint32_t w = *reinterpret_cast<const uint32_t *>(vst + t * kHeadDim + 4 * lane);
-                                    const uint32_t x = e4m3x2_to_h2(static_cast<uint16_t>(w & 0xffffu));
-                                    const uint32_t y = e4m3x2_to_h2(static_cast<uint16_t>(w >> 16));
-                                    const uint32_t wa = u < 2 ? pa.x : pa.y, wb = u < 2 ? pb.x : pb.y;
-                                    if (u & 1) {
-                                        axpy2_f16_f32<1>(xa[0], xa[1], x, wa); axpy2_f16_f32<1>(xa[2], xa[3], y, wa);
-                                        axpy2_f16_f32<1>(xb[0], xb[1], x, wb); axpy2_f16_f32<1>(xb[2], xb[3], y, wb);
-                                    } else {
-                                        axpy2_f16_f32<0>(xa[0], xa[1], x, wa); axpy2_f16_f32<0>(xa[2], xa[3], y, wa);
-                                        axpy2_f16_f32<0>(xb[0], xb[1], x, wb); axpy2_f16_f32<0>(xb[2], xb[3], y, wb);
-                                    }
-                                }
+                            for (int t4 = 0; t4 < CH; t4 += 4) {
+                                const uint2 pa = *reinterpret_cast<const uint2 *>(phalf + t4);
+                                const uint2 pb = *reinterpret_cast<const uint2 *>(phalf + CH + t4);
+                                if (t4 + 0 < nvalid) pv_token(t4 + 0, pa.x, pb.x, 0);
+                                if (t4 + 1 < nvalid) pv_token(t4 + 1, pa.x, pb.x, 1);
+                                if (t4 + 2 < nvalid) pv_token(t4 + 2, pa.y, pb.y, 0);
+                                if (t4 + 3 < nvalid) pv_token(t4 + 3, pa.y, pb.y, 1);
                             }
                         }
 #pragma unroll

@@ -16,9 +16,11 @@
 // store (or read-add-write for accumulate), which keeps them deterministic.
 // The host picks BN and the split count with a small cost model.
 //
-// CTA = 6 warps: warp 0 TMA producer, warp 1 TMEM allocator + MMA issuer
-// (one thread), warps 2..5 epilogue (TMEM lane quadrant = warp % 4, one
-// weight row per thread).  Every mbarrier wait is bounded.
+// CTA = 7 warps: warp 0 TMA producer of the weight tiles, warp 6 TMA producer
+// of the token tiles (a warp issues TMA copies at a bounded rate, so two
+// issuing warps double the ingest of one CTA), warp 1 TMEM allocator + MMA
+// issuer (one thread), warps 2..5 epilogue (TMEM lane quadrant = warp % 4,
+// one weight row per thread).  Every mbarrier wait is bounded.
 #include "kernels.h"
 
 #include <cuda.h>
@@ -33,7 +35,8 @@ namespace {
 constexpr int kBK = 64;                           // K per stage: one 128-byte swizzle atom of bf16
 constexpr int kBM = 128;                          // weight rows per tile (MMA M)
 constexpr uint32_t kABytes = kBM * kBK * 2;       // 16 KB
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 224;
+constexpr int kProducerB = 6;                     // warp that loads the token tiles
 
 template <int BN> struct TcTraits {
     static constexpr uint32_t kBBytes = BN * kBK * 2;
@@ -141,7 +144,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < T::NS; ++s) {
-            mbar_init(&full[s], 1);
+            mbar_init(&full[s], 2);         // one arrive.expect_tx per producer warp
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -176,10 +179,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         nk = kt1 > kt0 ? kt1 - kt0 : 0;
     };
 
-    if (warp == 0) {
+    if (warp == 0 || warp == kProducerB) {
         if (lane == 0) {
-            const uint64_t pol_w = l2_evict_first_policy();
-            const uint64_t pol_x = l2_evict_last_policy();
+            const bool is_w = warp == 0;
+            const uint64_t pol = is_w ? l2_evict_first_policy() : l2_evict_last_policy();
+            const CUtensorMap *map = is_w ? &tmW : &tmX;
+            const uint32_t bytes = is_w ? kABytes : T::kBBytes;
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
             int it = 0;
             bool bad = false;
             for (int u = blockIdx.x; u < units && !bad; u += gridDim.x) {
@@ -194,12 +200,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         bad = true;
                         break;
                     }
-                    uint8_t *a = tiles + static_cast<size_t>(s) * T::kStage;
-                    uint8_t *b = a + kABytes;
-                    mbar_arrive_expect_tx(&full[s], T::kStage);
-                    const int kx = (kt0 + i) * kBK;
-                    tma_load_2d(a, &tmW, kx, n0, &full[s], pol_w);
-                    tma_load_2d(b, &tmX, kx, m0, &full[s], pol_x);
+                    uint8_t *dst = tiles + static_cast<size_t>(s) * T::kStage + (is_w ? 0u : kABytes);
+                    mbar_arrive_expect_tx(&full[s], bytes);
+                    tma_load_2d(dst, map, (kt0 + i) * kBK, is_w ? n0 : m0, &full[s], pol);
                     ++it;
                 }
             }

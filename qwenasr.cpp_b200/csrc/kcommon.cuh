@@ -74,6 +74,13 @@ __device__ __forceinline__ uint32_t e4m3x2_to_h2(uint16_t v) {
     memcpy(&bits, &h, sizeof(bits));
     return bits;
 }
+// Four e4m3 bytes -> two f16x2 words (bytes 0,1 -> lo2; bytes 2,3 -> hi2); exact.
+// The word is split into its 16-bit halves inside PTX (no shift/mask ops).
+__device__ __forceinline__ void e4m3x4_to_h2x2(uint32_t w, uint32_t &lo2, uint32_t &hi2) {
+    asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+        "cvt.rn.f16x2.e4m3x2 %0, l;\n\tcvt.rn.f16x2.e4m3x2 %1, h;\n\t}"
+        : "=r"(lo2), "=r"(hi2) : "r"(w));
+}
 // acc += lo(a) * lo(b) + hi(a) * hi(b): f16 operands, products exact in f32,
 // f32 accumulation (PTX fma.rn.f32.f16, sm_100).
 __device__ __forceinline__ void dot2_f16_f32(float &acc, uint32_t a, uint32_t b) {
