@@ -25,6 +25,8 @@
 
 #include <cuda.h>
 
+#include <cstdio>
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
@@ -406,24 +408,37 @@ cudaError_t launch_bn(const void *X, const void *W, float *C, int M, int N, int 
     return cudaGetLastError();
 }
 
-// Cost model for the tile width BN and the K split: per-SM time of one
-// k-tile = max(MMA time, operand bytes over a per-SM share of L2/HBM
-// bandwidth), times the k-tiles of the SM that gets the most units, plus a
-// fixed pipeline-fill/epilogue term per unit and a red.add term when split.
+// Cost model for the tile width BN and the K split.  One thread issues a
+// tcgen05.mma (M=128, K=16) about every 150 cycles whatever N is, so a
+// k-tile (4 MMAs) costs about the same for every BN and only N = 256 keeps
+// the tensor pipe busy; below that a k-tile is bounded by MMA issue, by the
+// operand bytes the two TMA warps bring in, and by the refill latency over
+// the ring depth.  Units run round-robin over the persistent CTAs; a split
+// adds red.add traffic into C (and a memset when not accumulating).
 struct GemmPlan {
     int bn, splits;
 };
 
+template <int BN> constexpr double ktile_seconds() {
+    constexpr double kClk = 1.9e9;
+    constexpr double t_mma = 4 * 150.0 / kClk;                                    // issue-bound MMAs
+    constexpr double t_ld = (kABytes + TcTraits<BN>::kBBytes) / 150e9;           // two TMA issuers
+    constexpr double t_lat = 1.3e-6 / (TcTraits<BN>::NS - 1);                     // refill latency / depth
+    return t_mma > t_ld ? (t_mma > t_lat ? t_mma : t_lat) : (t_ld > t_lat ? t_ld : t_lat);
+}
+
 GemmPlan plan_gemm(int M, int N, int K, int num_sms) {
-    const double kMmaPerSm = 1.45e15 / 148.0;       // dense bf16 flop/s per SM
-    const double kBytesPerSm = 110e9;               // operand ingest per SM (L2-served)
     const double kHbm = 6.2e12;                     // whole-chip weight streaming
-    const double kFixed = 1.2e-6;                   // per-unit fill + epilogue tail
+    const double kFixed = 1.5e-6;                   // per-unit fill + epilogue tail
+    const double kRed = 250e9;                      // f32 red.add per second, whole chip
     const int ktiles = K / kBK;
     const int tiles_n = (N + kBM - 1) / kBM;
+    const double tk[4] = {ktile_seconds<32>(), ktile_seconds<64>(), ktile_seconds<128>(), ktile_seconds<256>()};
     GemmPlan best{256, 1};
     double best_t = 1e30;
+    int bi = 0;
     for (int bn : {32, 64, 128, 256}) {
+        const int idx = bi++;
         if (bn > 32 && (bn / 2) >= M) break;          // a narrower tile already covers all tokens
         const int tiles_m = (M + bn - 1) / bn;
         const int tiles = tiles_n * tiles_m;
@@ -434,12 +449,10 @@ GemmPlan plan_gemm(int M, int N, int K, int num_sms) {
             if (spr != sp) continue;
             const long units = static_cast<long>(tiles) * sp;
             const long waves = (units + num_sms - 1) / num_sms;
-            const double t_mma = 2.0 * kBM * bn * kBK / kMmaPerSm;
-            const double t_ld = (kBM * kBK * 2.0 + bn * kBK * 2.0) / kBytesPerSm;
-            double t = waves * (kps * (t_mma > t_ld ? t_mma : t_ld) + kFixed);
+            double t = waves * (kps * tk[idx] + kFixed);
             const double t_w = static_cast<double>(N) * K * 2.0 / kHbm;   // weights read from HBM once
             if (t_w > t) t = t_w;
-            if (sp > 1) t += static_cast<double>(M) * N * 4.0 * sp / 2.0e12 + 1.0e-6;   // memset + red.add
+            if (sp > 1) t += static_cast<double>(M) * N * sp / kRed + 1.0e-6;   // red.add + memset
             if (t < best_t * 0.98) {
                 best_t = t;
                 best = {bn, sp};
@@ -471,7 +484,14 @@ cudaError_t launch_gemm_tc(const void *X, const void *W, float *C, int M, int N,
                            DevError *err, cudaStream_t st) {
     if (M <= 0 || N <= 0) return cudaSuccess;
     if (K % kBK != 0) return cudaErrorInvalidValue;
-    const GemmPlan pl = plan_gemm(M, N, K, num_sms);
+    GemmPlan pl = plan_gemm(M, N, K, num_sms);
+    // Tuning override: QWENASR_B200_GEMM_PLAN="bn,splits" forces the plan (sweeps).
+    static const char *forced = getenv("QWENASR_B200_GEMM_PLAN");
+    if (forced) {
+        int bn = 0, sp = 0;
+        if (sscanf(forced, "%d,%d", &bn, &sp) == 2 && (bn == 32 || bn == 64 || bn == 128 || bn == 256) && sp >= 1)
+            pl = {bn, sp};
+    }
     switch (pl.bn) {
         case 32: return launch_bn<32>(X, W, C, M, N, K, accumulate, pl.splits, num_sms, err, st);
         case 64: return launch_bn<64>(X, W, C, M, N, K, accumulate, pl.splits, num_sms, err, st);
