@@ -1,41 +1,49 @@
-// K3: causal prefill attention on the tensor cores (tcgen05 + TMEM), bf16 cache.
-// Replaces the prompt half of text-decoder.cpp:322-334 (QK^T, diag mask,
-// softmax, PV over the whole prompt) for the paged cache that K1 has just
-// filled (and the scalar twin :739-791).
+// K3: causal prefill attention on the tensor cores (tcgen05 + TMEM) over the
+// paged cache, bf16 or e4m3.  Replaces the prompt half of
+// text-decoder.cpp:322-334 (QK^T, diag mask, softmax, PV over the whole
+// prompt) for the paged cache that K1 has just filled (and the scalar twin
+// :739-791).
 //
 // One CTA per work item = (64 consecutive queries of one stream, kv head g).
 // GQA: the two q heads of kv head g share the item, so the MMA's M = 128 rows
 // are [64 queries of head 2g | 64 queries of head 2g+1] and every K/V tile is
-// fetched once for both.  Keys come in tiles of 128 (8 pages): a tensor map
-// over the pool ([pool rows][128] bf16, box 16 rows x 64 columns, 128-byte
-// swizzle) brings each page's K or V rows straight into the canonical UMMA
-// layouts — K as the K-major B operand of S = Q K^T, V as the MN-major B
-// operand of O += P V.
+// fetched once for both.  Keys come in tiles of 128 (8 pages).
+//
+// Operand staging: a warpgroup of 128 loader threads, one key row each, reads
+// the row straight from its page with 16-byte loads and writes it into the
+// canonical 128-byte-swizzled UMMA layout — K as the K-major B operand of
+// S = Q K^T, V as the MN-major B operand of O += P V.  (A page contributes
+// 16 scattered rows per head; one TMA copy per page and column block would be
+// bounded by the rate at which a thread can issue copies.)  For the e4m3 cache
+// the loader dequantises on the way (e4m3 -> f16 exactly, times the page's
+// per-(kv, head) scale in f16), and Q, P are f16 too; for bf16 everything is
+// bf16.  K and V tiles are double-buffered, S is double-buffered in TMEM.
 //
 // Two passes over the key tiles: pass 1 computes each row's running max and
 // sum from S (TMEM -> registers); pass 2 recomputes S, writes the normalised
-// P (bf16, swizzled) to shared memory and accumulates O = P V in TMEM, so O
-// never needs rescaling.  Roles: warp 0 TMA producer, warp 1 TMEM allocator +
-// MMA issuer, warps 2..5 = 128 softmax/epilogue threads (thread = TMEM lane =
-// one query row).  All waits bounded.
+// P (swizzled) to shared memory and accumulates O = P V in TMEM, so O never
+// needs rescaling.  In pass 2 the issuer puts S of tile t ahead of P V of
+// tile t-1, so the softmax of t overlaps the PV MMAs of t-1.
+//
+// Roles: warps 0..3 loaders, warps 4..7 softmax/epilogue (thread = TMEM lane
+// = one query row; lane quadrant = warp % 4), warp 8 TMEM allocator + MMA
+// issuer (one thread).  All waits bounded.
 #include "kernels.h"
 
-#include <cuda.h>
-
 namespace qkv {
-
-bool tc_tensor_map(CUtensorMap *out, const void *ptr, int rows, int K, int box_rows);
 
 namespace {
 
 constexpr int kQPerItem = 64;
 constexpr int kKeyTile = 128;
-constexpr int kPagesPerTile = kKeyTile / kPageTokens;     // 8
-constexpr uint32_t kBlkBytes = 128 * 128;                 // [128 rows][64 bf16], 16 KB
+constexpr uint32_t kBlkBytes = 128 * 128;                 // [128 rows][64 x 16-bit], 16 KB
 constexpr uint32_t kTileBytes = 2 * kBlkBytes;            // two 64-column blocks, 32 KB
-constexpr int kThreads = 192;
-constexpr size_t kSmem = 1024 + 4 * static_cast<size_t>(kTileBytes) + 256;
-constexpr uint32_t kTmemCols = 256;                       // S: cols [0,128), O: cols [128,256)
+constexpr int kMmaWarp = 8;
+constexpr int kThreads = 9 * 32;
+// Q, K[2], V[2], P tiles + barriers
+constexpr size_t kSmem = 1024 + 6 * static_cast<size_t>(kTileBytes) + 512;
+constexpr uint32_t kTmemCols = 512;                       // S0 [0,128), S1 [128,256), O [256,384)
+constexpr uint32_t kTmemO = 256;
 
 struct K3Params {
     const int4 *items;      // (row0, nq, g, 0)
@@ -44,6 +52,8 @@ struct K3Params {
     const float *q;         // [rows][2048] post-RoPE
     void *out;              // [rows][2048]
     int out_bf16;
+    const void *pool;
+    const float *scales;    // e4m3 cache: [pages][2][8]
     const int *page_table;
     int maxp;
     int max_streams;
@@ -51,14 +61,6 @@ struct K3Params {
     float scale_log2;
     DevError *err;
 };
-
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
 
 // Swizzled (128 B) operand descriptors, sm_100 version bit set.
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t addr) {
@@ -70,8 +72,12 @@ __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t addr) {
            (1ull << 46) | (2ull << 61);
 }
 
-constexpr uint32_t kIdescS = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
-constexpr uint32_t kIdescPV = kIdescS | (1u << 16);   // B (V) MN-major
+// Instruction descriptors: f32 accumulate, A and B both bf16 (bits 7, 10) or
+// both f16, M = 128, N = 128; PV takes B (V) MN-major (bit 16).
+template <bool F16> constexpr uint32_t idesc_s() {
+    return (1u << 4) | (F16 ? 0u : ((1u << 7) | (1u << 10))) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+}
+template <bool F16> constexpr uint32_t idesc_pv() { return idesc_s<F16>() | (1u << 16); }
 
 __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, int acc) {
     asm volatile(
@@ -108,16 +114,84 @@ __device__ __forceinline__ uint32_t swz(int r, int c) {
     return static_cast<uint32_t>(r) * 128u + (static_cast<uint32_t>(c ^ (r & 7)) << 4);
 }
 
+template <bool F16> __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    if constexpr (F16) return pack_h2(lo, hi);
+    else return pack_bf16x2(lo, hi);
+}
+
+__device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t s2) {
+    __half2 x, y;
+    memcpy(&x, &a, 4);
+    memcpy(&y, &s2, 4);
+    const __half2 z = __hmul2(x, y);
+    uint32_t r;
+    memcpy(&r, &z, 4);
+    return r;
+}
+
+// One key row (128 dims of page `page`, kv half `kv`, head g, token `tok`) into
+// row r of a swizzled [2 blocks][128 rows][64] 16-bit tile; a key past the
+// stream's length (`live` false) becomes a zero row, whatever its slot holds.
+template <typename TC>
+__device__ __forceinline__ void load_row(const K3Params &p, uint8_t *tile, int r, int page, int kv, int g, int tok,
+                                         bool live) {
+    if (!live) {
+#pragma unroll
+        for (int c = 0; c < 16; ++c) *reinterpret_cast<uint4 *>(tile + (c >> 3) * kBlkBytes + swz(r, c & 7)) = make_uint4(0, 0, 0, 0);
+        return;
+    }
+    const size_t row = ((static_cast<size_t>(page) * 2 + kv) * kHkv + g) * kPageTokens + tok;
+    if constexpr (sizeof(TC) == 2) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const __nv_bfloat16 *>(p.pool) + row * kHeadDim);
+        uint4 w[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) w[c] = __ldg(src + c);
+#pragma unroll
+        for (int c = 0; c < 16; ++c) *reinterpret_cast<uint4 *>(tile + (c >> 3) * kBlkBytes + swz(r, c & 7)) = w[c];
+    } else {
+        const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(p.pool) + row * kHeadDim);
+        const float sc = __ldg(p.scales + (static_cast<size_t>(page) * 2 + kv) * kHkv + g);
+        const uint32_t s2 = pack_h2(sc, sc);
+        uint4 w[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) w[c] = __ldg(src + c);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            // 16 e4m3 = dims 16c .. 16c+15 -> f16 chunks 2c (dims 16c..+7) and 2c+1
+            const uint32_t ws[4] = {w[c].x, w[c].y, w[c].z, w[c].w};
+            uint32_t h[8];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                uint32_t lo2, hi2;
+                e4m3x4_to_h2x2(ws[k], lo2, hi2);
+                h[2 * k] = hmul2_bits(lo2, s2);
+                h[2 * k + 1] = hmul2_bits(hi2, s2);
+            }
+            const int c0 = 2 * c, c1 = 2 * c + 1;
+            *reinterpret_cast<uint4 *>(tile + (c0 >> 3) * kBlkBytes + swz(r, c0 & 7)) = make_uint4(h[0], h[1], h[2], h[3]);
+            *reinterpret_cast<uint4 *>(tile + (c1 >> 3) * kBlkBytes + swz(r, c1 & 7)) = make_uint4(h[4], h[5], h[6], h[7]);
+        }
+    }
+}
+
 struct Bars {
-    uint64_t q_ready, k_full, k_empty, v_full, v_empty, s_full, s_free, p_full, p_free, o_done;
+    uint64_t q_ready, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_free[2], p_full, p_free, o_done;
 };
 
-__global__ void __launch_bounds__(kThreads, 1)
-    prefill_attn_tc_kernel(const __grid_constant__ CUtensorMap pool_map, K3Params p) {
+__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity) {
+    return mbar_wait(bar, parity, kWaitLimitCycles);
+}
+
+template <typename TC>
+__global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p) {
+    constexpr bool kF16 = sizeof(TC) == 1;   // e4m3 cache -> f16 operands
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *sQ = smem, *sK = smem + kTileBytes, *sV = smem + 2 * kTileBytes, *sP = smem + 3 * kTileBytes;
-    Bars *bars = reinterpret_cast<Bars *>(smem + 4 * kTileBytes);
+    uint8_t *sQ = smem;
+    uint8_t *const sK0 = smem + kTileBytes;         // K[b] = sK0 + b * kTileBytes
+    uint8_t *const sV0 = smem + 3 * kTileBytes;     // V[b] = sV0 + b * kTileBytes
+    uint8_t *sP = smem + 5 * kTileBytes;
+    Bars *bars = reinterpret_cast<Bars *>(smem + 6 * kTileBytes);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 1);
     volatile int *failed = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -129,16 +203,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int kv_len = pos0 + nq;
     const int n_kt = (kv_len + kKeyTile - 1) / kKeyTile;
     const int key_pages = (kv_len + kPageTokens - 1) / kPageTokens;
-    const bool item_ok = slot >= 0 && slot < p.max_streams && pos0 >= 0 && nq > 0 && key_pages <= p.maxp;
+    const bool item_ok = slot >= 0 && slot < p.max_streams && pos0 >= 0 && nq > 0 && nq <= kQPerItem &&
+                         key_pages <= p.maxp && g >= 0 && g < kHkv;
+    const int *pt = p.page_table + static_cast<size_t>(item_ok ? slot : 0) * p.maxp;
 
     if (threadIdx.x == 0) {
         mbar_init(&bars->q_ready, 128);
-        mbar_init(&bars->k_full, 1);
-        mbar_init(&bars->k_empty, 1);
-        mbar_init(&bars->v_full, 1);
-        mbar_init(&bars->v_empty, 1);
-        mbar_init(&bars->s_full, 1);
-        mbar_init(&bars->s_free, 128);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars->k_full[b], 128);
+            mbar_init(&bars->k_empty[b], 1);
+            mbar_init(&bars->v_full[b], 128);
+            mbar_init(&bars->v_empty[b], 1);
+            mbar_init(&bars->s_full[b], 1);
+            mbar_init(&bars->s_free[b], 128);
+        }
         mbar_init(&bars->p_full, 128);
         mbar_init(&bars->p_free, 1);
         mbar_init(&bars->o_done, 1);
@@ -146,7 +224,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!item_ok) report_error(p.err, kErrRowBounds, kWherePrefillAttn, row0, pos0);
         fence_mbar_init();
     }
-    if (warp == 1) {
+    if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(kTmemCols)
                      : "memory");
@@ -155,108 +233,108 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_before();
     __syncthreads();
     fence_after();
+    // Every page id of the item's keys, checked once by the whole CTA.
+    if (item_ok) {
+        for (int i = threadIdx.x; i < key_pages; i += kThreads) {
+            const int pg = pt[i];
+            if (pg < 0 || pg >= p.n_pages) {
+                report_error(p.err, kErrPageIndex, kWherePrefillAttn, row0, i);
+                *failed = 1;
+            }
+        }
+    }
+    __syncthreads();
     const uint32_t tmem = *tmem_slot;
     const int n_uses = *failed ? 0 : 2 * n_kt;
 
-    if (warp == 0) {
-        // ================= TMA producer =================
-        if (lane == 0 && n_uses > 0) {
-            const int *pt = p.page_table + static_cast<size_t>(slot) * p.maxp;
-            int k_issued = 0, v_issued = 0;
-            for (int u = 0; u < n_uses && !*failed; ++u) {
-                const int pass = u / n_kt, kt = u % n_kt;
-                int pages[kPagesPerTile];
-                bool bad = false;
-                for (int j = 0; j < kPagesPerTile; ++j) {
-                    const int pi = kt * kPagesPerTile + j;
-                    // Key slots past the stream's last page reuse its first page: finite
-                    // values, masked out of S, multiplied by P = 0 in P V.
-                    int pg = pt[pi < key_pages ? pi : 0];
-                    if (pg < 0 || pg >= p.n_pages) bad = true;
-                    pages[j] = pg;
-                }
-                if (bad) {
-                    report_error(p.err, kErrPageIndex, kWherePrefillAttn, row0, kt);
-                    *failed = 1;
-                    break;
-                }
-                if (!mbar_wait(&bars->k_empty, (static_cast<uint32_t>(u) & 1u) ^ 1u, kWaitLimitCycles)) {
-                    report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, row0, u);
-                    *failed = 1;
-                    break;
-                }
-                mbar_arrive_expect_tx(&bars->k_full, kTileBytes);
-                for (int j = 0; j < kPagesPerTile; ++j) {
-                    const int krow = ((pages[j] * 2 + 0) * kHkv + g) * kPageTokens;
-                    tma_load_2d(sK + j * 2048, &pool_map, 0, krow, &bars->k_full);
-                    tma_load_2d(sK + kBlkBytes + j * 2048, &pool_map, 64, krow, &bars->k_full);
-                }
-                ++k_issued;
-                if (pass == 1) {
-                    if (!mbar_wait(&bars->v_empty, (static_cast<uint32_t>(kt) & 1u) ^ 1u, kWaitLimitCycles)) {
-                        report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, row0, -u);
-                        *failed = 1;
-                        break;
-                    }
-                    mbar_arrive_expect_tx(&bars->v_full, kTileBytes);
-                    for (int j = 0; j < kPagesPerTile; ++j) {
-                        const int vrow = ((pages[j] * 2 + 1) * kHkv + g) * kPageTokens;
-                        tma_load_2d(sV + j * 2048, &pool_map, 0, vrow, &bars->v_full);
-                        tma_load_2d(sV + kBlkBytes + j * 2048, &pool_map, 64, vrow, &bars->v_full);
-                    }
-                    ++v_issued;
-                }
+    if (warp < 4) {
+        // ================= loaders: thread = key row of the tile =================
+        const int r = threadIdx.x;
+        for (int u = 0; u < n_uses; ++u) {
+            const int pass = u / n_kt, kt = u % n_kt;
+            const int key = kt * kKeyTile + r;
+            // Keys past the stream's length are zero rows (masked out of S,
+            // multiplied by P = 0 in P V); their page index is clamped.
+            const int pi = key / kPageTokens;
+            const int page = pt[pi < key_pages ? pi : 0];
+            const int tok = key % kPageTokens;
+            const int kb = u & 1;
+            if (*failed || !wait_bar(&bars->k_empty[kb], ((static_cast<uint32_t>(u) >> 1) & 1u) ^ 1u)) {
+                if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, row0, u);
+                *failed = 1;
+                break;
             }
-            // Drain the last loads of each buffer before the CTA may exit.
-            if (k_issued > 0) mbar_wait(&bars->k_full, static_cast<uint32_t>(k_issued - 1) & 1u, kWaitLimitCycles);
-            if (v_issued > 0) mbar_wait(&bars->v_full, static_cast<uint32_t>(v_issued - 1) & 1u, kWaitLimitCycles);
+            load_row<TC>(p, sK0 + kb * kTileBytes, r, page, 0, g, tok, key < kv_len);
+            fence_async_smem();
+            mbar_arrive(&bars->k_full[kb]);
+            if (pass == 1) {
+                const int vb = kt & 1;
+                if (*failed || !wait_bar(&bars->v_empty[vb], ((static_cast<uint32_t>(kt) >> 1) & 1u) ^ 1u)) {
+                    if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, row0, -u);
+                    *failed = 1;
+                    break;
+                }
+                load_row<TC>(p, sV0 + vb * kTileBytes, r, page, 1, g, tok, key < kv_len);
+                fence_async_smem();
+                mbar_arrive(&bars->v_full[vb]);
+            }
         }
-    } else if (warp == 1) {
+    } else if (warp == kMmaWarp) {
         // ================= MMA issuer =================
         if (lane == 0) {
             int issued = 0;
-            bool ok = n_uses > 0 && mbar_wait(&bars->q_ready, 0, kWaitLimitCycles);
+            bool ok = n_uses > 0 && wait_bar(&bars->q_ready, 0);
             if (n_uses > 0 && !ok) {
                 report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, row0, 1 << 20);
                 *failed = 1;
             }
-            const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP);
-            for (int u = 0; ok && u < n_uses; ++u) {
-                const int pass = u / n_kt, kt = u % n_kt;
-                if (!mbar_wait(&bars->k_full, static_cast<uint32_t>(u) & 1u, kWaitLimitCycles) ||
-                    (u > 0 && !mbar_wait(&bars->s_free, static_cast<uint32_t>(u - 1) & 1u, kWaitLimitCycles))) {
-                    ok = false;
-                    break;
-                }
+            const uint32_t aQ = smem_u32(sQ), aP = smem_u32(sP);
+            // P V of tile kt: P (K-major A, 16 keys per step), V rows (MN-major B, 2 KB per 16 rows).
+            auto issue_pv = [&](int kt) -> bool {
+                const int vb = kt & 1;
+                if (*failed || !wait_bar(&bars->v_full[vb], (static_cast<uint32_t>(kt) >> 1) & 1u) ||
+                    !wait_bar(&bars->p_full, static_cast<uint32_t>(kt) & 1u))
+                    return false;
                 fence_after();
+                const uint32_t aV = smem_u32(sV0 + vb * kTileBytes);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint32_t blk = static_cast<uint32_t>(kk >> 2) * kBlkBytes;
                     const uint64_t step = 2ull * static_cast<uint64_t>(kk & 3);
-                    mma(tmem, desc_kmajor(aQ + blk) + step, desc_kmajor(aK + blk) + step, kIdescS, kk > 0);
+                    mma(tmem + kTmemO, desc_kmajor(aP + blk) + step, desc_mnmajor(aV + static_cast<uint32_t>(kk) * 2048u),
+                        idesc_pv<kF16>(), (kt > 0 || kk > 0) ? 1 : 0);
                 }
                 ++issued;
-                commit(&bars->s_full);
-                commit(&bars->k_empty);
-                if (pass == 1) {
-                    if (!mbar_wait(&bars->v_full, static_cast<uint32_t>(kt) & 1u, kWaitLimitCycles) ||
-                        !mbar_wait(&bars->p_full, static_cast<uint32_t>(kt) & 1u, kWaitLimitCycles)) {
-                        ok = false;
-                        break;
-                    }
-                    fence_after();
+                commit(&bars->p_free);
+                commit(&bars->v_empty[vb]);
+                return true;
+            };
+            for (int u = 0; ok && u < n_uses; ++u) {
+                const int pass = u / n_kt, kt = u % n_kt;
+                const int kb = u & 1, sb = u & 1;
+                const uint32_t use = (static_cast<uint32_t>(u) >> 1) & 1u;
+                if (*failed || !wait_bar(&bars->k_full[kb], use) || !wait_bar(&bars->s_free[sb], use ^ 1u)) {
+                    ok = false;
+                    break;
+                }
+                fence_after();
+                const uint32_t aK = smem_u32(sK0 + kb * kTileBytes);
 #pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) {
-                        const uint32_t blk = static_cast<uint32_t>(kk >> 2) * kBlkBytes;
-                        const uint64_t step = 2ull * static_cast<uint64_t>(kk & 3);
-                        // 16 keys per step: P columns (K-major), V rows (MN-major, 2 KB per 16 rows)
-                        mma(tmem + 128, desc_kmajor(aP + blk) + step, desc_mnmajor(aV + static_cast<uint32_t>(kk) * 2048u),
-                            kIdescPV, (kt > 0 || kk > 0) ? 1 : 0);
-                    }
-                    commit(&bars->p_free);
-                    commit(&bars->v_empty);
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t blk = static_cast<uint32_t>(kk >> 2) * kBlkBytes;
+                    const uint64_t step = 2ull * static_cast<uint64_t>(kk & 3);
+                    mma(tmem + static_cast<uint32_t>(sb * 128), desc_kmajor(aQ + blk) + step,
+                        desc_kmajor(aK + blk) + step, idesc_s<kF16>(), kk > 0);
+                }
+                ++issued;
+                commit(&bars->s_full[sb]);
+                commit(&bars->k_empty[kb]);
+                if (pass == 1 && kt > 0 && !issue_pv(kt - 1)) {
+                    ok = false;
+                    break;
                 }
             }
+            if (ok && n_uses > 0 && !issue_pv(n_kt - 1)) ok = false;
             if (!ok && n_uses > 0) {
                 report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, row0, 1 << 21);
                 *failed = 1;
@@ -264,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // o_done completes when every issued MMA has, on the error path too.
             if (issued > 0) commit(&bars->o_done);
             else mbar_arrive(&bars->o_done);
-            mbar_wait(&bars->o_done, 0, kWaitLimitCycles);
+            wait_bar(&bars->o_done, 0);
         }
         __syncwarp();
     } else {
@@ -276,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int pos_r = pos0 + (real ? i : nq - 1);
         const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * quad) << 16);
         if (n_uses > 0) {
-            // Q row (scaled into the log2 domain, bf16, swizzled K-major)
+            // Q row, scaled into the log2 domain, swizzled K-major
             const float *qrow = p.q + static_cast<size_t>(row0 + (real ? i : 0)) * kQDim + (2 * g + h) * kHeadDim;
 #pragma unroll 1
             for (int c16 = 0; c16 < 16; ++c16) {
@@ -285,10 +363,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float4 a = reinterpret_cast<const float4 *>(qrow + c16 * 8)[0];
                     const float4 b = reinterpret_cast<const float4 *>(qrow + c16 * 8)[1];
                     const float s = p.scale_log2;
-                    w.x = pack_bf16x2(a.x * s, a.y * s);
-                    w.y = pack_bf16x2(a.z * s, a.w * s);
-                    w.z = pack_bf16x2(b.x * s, b.y * s);
-                    w.w = pack_bf16x2(b.z * s, b.w * s);
+                    w.x = pack2<kF16>(a.x * s, a.y * s);
+                    w.y = pack2<kF16>(a.z * s, a.w * s);
+                    w.z = pack2<kF16>(b.x * s, b.y * s);
+                    w.w = pack2<kF16>(b.z * s, b.w * s);
                 }
                 *reinterpret_cast<uint4 *>(sQ + (c16 >> 3) * kBlkBytes + swz(r, c16 & 7)) = w;
             }
@@ -298,19 +376,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         float m_run = -INFINITY, l_run = 0.0f, inv_l = 0.0f;
         for (int u = 0; u < n_uses; ++u) {
             const int pass = u / n_kt, kt = u % n_kt;
+            const int sb = u & 1;
             // Every exit decision is warp-uniform: the tcgen05.ld below is .sync.aligned.
-            bool go = !*failed && mbar_wait(&bars->s_full, static_cast<uint32_t>(u) & 1u, kWaitLimitCycles);
+            bool go = !*failed && wait_bar(&bars->s_full[sb], (static_cast<uint32_t>(u) >> 1) & 1u);
             if (!__all_sync(0xffffffffu, go)) break;
             fence_after();
             if (pass == 1 && kt == 0) inv_l = 1.0f / l_run;
-            if (pass == 1 && kt > 0) {
-                go = mbar_wait(&bars->p_free, static_cast<uint32_t>(kt - 1) & 1u, kWaitLimitCycles);
-                if (!__all_sync(0xffffffffu, go)) break;
-            }
-#pragma unroll 1
+            uint32_t packed[4][16];
+#pragma unroll
             for (int ch = 0; ch < 4; ++ch) {
                 float s[32];
-                tmem_ld32(lane_addr + static_cast<uint32_t>(ch * 32), s);
+                tmem_ld32(lane_addr + static_cast<uint32_t>(sb * 128 + ch * 32), s);
                 const int key0 = kt * kKeyTile + ch * 32;
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
@@ -329,29 +405,34 @@ __global__ void __launch_bounds__(kThreads, 1)
                         m_run = m_new;
                     }
                 } else {
-                    uint32_t packed[16];
 #pragma unroll
                     for (int j = 0; j < 16; ++j)
-                        packed[j] = pack_bf16x2(exp2f(s[2 * j] - m_run) * inv_l, exp2f(s[2 * j + 1] - m_run) * inv_l);
+                        packed[ch][j] = pack2<kF16>(exp2f(s[2 * j] - m_run) * inv_l, exp2f(s[2 * j + 1] - m_run) * inv_l);
+                }
+            }
+            // S buffer sb read out: the issuer may compute the next-but-one tile into it.
+            fence_before();
+            mbar_arrive(&bars->s_free[sb]);
+            if (pass == 1) {
+                go = !*failed && wait_bar(&bars->p_free, (static_cast<uint32_t>(kt) & 1u) ^ 1u);
+                if (!__all_sync(0xffffffffu, go)) break;
+#pragma unroll
+                for (int ch = 0; ch < 4; ++ch) {
                     // keys ch*32 .. +31 = 4 chunks of 8 in block ch >> 1
                     uint8_t *blk = sP + (ch >> 1) * kBlkBytes;
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
                         const int chunk = (ch & 1) * 4 + c;
                         *reinterpret_cast<uint4 *>(blk + swz(r, chunk)) =
-                            make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+                            make_uint4(packed[ch][4 * c], packed[ch][4 * c + 1], packed[ch][4 * c + 2], packed[ch][4 * c + 3]);
                     }
                 }
-            }
-            fence_before();
-            mbar_arrive(&bars->s_free);
-            if (pass == 1) {
                 fence_async_smem();
                 mbar_arrive(&bars->p_full);
             }
         }
         // Epilogue: O row (128 dims) -> attention output of (query i, head 2g+h)
-        bool done = n_uses > 0 && mbar_wait(&bars->o_done, 0, kWaitLimitCycles) && !*failed;
+        bool done = n_uses > 0 && wait_bar(&bars->o_done, 0) && !*failed;
         done = __all_sync(0xffffffffu, done);   // warp-uniform: the whole warp loads TMEM, only real rows store
         fence_after();
         if (done) {
@@ -359,7 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
             for (int ch = 0; ch < 4; ++ch) {
                 float o[32];
-                tmem_ld32(lane_addr + 128u + static_cast<uint32_t>(ch * 32), o);
+                tmem_ld32(lane_addr + kTmemO + static_cast<uint32_t>(ch * 32), o);
                 if (!real) continue;
                 if (p.out_bf16) {
                     __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(p.out) + off + ch * 32;
@@ -379,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == kMmaWarp) {
         fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
     }
@@ -388,17 +469,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace
 
 cudaError_t prepare_prefill_tc() {
-    return cudaFuncSetAttribute(prefill_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(prefill_attn_tc_kernel<__nv_bfloat16>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmem));
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(prefill_attn_tc_kernel<uint8_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(kSmem));
 }
 
-cudaError_t launch_prefill_attn_tc(const PrefillAttnParams &pp, const int4 *items, int n_items, bool out_bf16,
-                                   cudaStream_t st) {
+bool prefill_tc_supported(int kv_dtype) { return kv_dtype == kKvBF16 || kv_dtype == kKvFP8; }
+
+cudaError_t launch_prefill_attn_tc(const PrefillAttnParams &pp, int kv_dtype, const int4 *items, int n_items,
+                                   bool out_bf16, cudaStream_t st) {
     if (n_items <= 0) return cudaSuccess;
-    CUtensorMap map;
-    const long long rows = static_cast<long long>(pp.n_pages) * 2 * kHkv * kPageTokens;
-    if (rows > 0x7fffffffLL || !tc_tensor_map(&map, pp.pool, static_cast<int>(rows), kHeadDim, kPageTokens))
-        return cudaErrorInvalidValue;
+    if (!prefill_tc_supported(kv_dtype) || (kv_dtype == kKvFP8 && !pp.scales)) return cudaErrorInvalidValue;
     K3Params p{};
     p.items = items;
     p.slots = pp.slots;
@@ -406,13 +489,16 @@ cudaError_t launch_prefill_attn_tc(const PrefillAttnParams &pp, const int4 *item
     p.q = pp.q;
     p.out = pp.out;
     p.out_bf16 = out_bf16 ? 1 : 0;
+    p.pool = pp.pool;
+    p.scales = pp.scales;
     p.page_table = pp.page_table;
     p.maxp = pp.maxp;
     p.max_streams = pp.max_streams;
     p.n_pages = pp.n_pages;
     p.scale_log2 = pp.scale_log2;
     p.err = pp.err;
-    prefill_attn_tc_kernel<<<n_items, kThreads, kSmem, st>>>(map, p);
+    if (kv_dtype == kKvBF16) prefill_attn_tc_kernel<__nv_bfloat16><<<n_items, kThreads, kSmem, st>>>(p);
+    else prefill_attn_tc_kernel<uint8_t><<<n_items, kThreads, kSmem, st>>>(p);
     return cudaGetLastError();
 }
 

@@ -78,10 +78,11 @@ cudaError_t prepare_decode_attn();
 size_t attn_smem_bytes(int kv_dtype);
 cudaError_t launch_decode_attn(const AttendParams &p, int kv_dtype, bool out_bf16, int grid, cudaStream_t st);
 cudaError_t launch_prefill_attn(const PrefillAttnParams &p, int kv_dtype, bool out_bf16, cudaStream_t st);
-// K3 (bf16 cache): items = (first row, query count <= 64, kv head, 0), one CTA each.
+// K3 (bf16 or e4m3 cache): items = (first row, query count <= 64, kv head, 0), one CTA each.
 cudaError_t prepare_prefill_tc();
-cudaError_t launch_prefill_attn_tc(const PrefillAttnParams &p, const int4 *items, int n_items, bool out_bf16,
-                                   cudaStream_t st);
+bool prefill_tc_supported(int kv_dtype);
+cudaError_t launch_prefill_attn_tc(const PrefillAttnParams &p, int kv_dtype, const int4 *items, int n_items,
+                                   bool out_bf16, cudaStream_t st);
 cudaError_t launch_page_gather(const void *pool, int kv_dtype, const int *pages, int n_pages_row, int len,
                                int n_pages, void *k_out, void *v_out, DevError *err, cudaStream_t st);
 cudaError_t launch_page_copy(void *pool_layer, size_t page_bytes, const int *src, const int *dst, int n,

@@ -4,6 +4,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <memory>
@@ -170,6 +171,10 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
     CK(prepare_decode_attn());
     CK(prepare_gemm_tc());
     CK(prepare_prefill_tc());
+    {
+        const char *pa = getenv("QWENASR_B200_PREFILL_ATTN");
+        h->prefill_tc = !(pa && std::strcmp(pa, "cuda_core") == 0);
+    }
     CK(prepare_dense(std::max(c.hidden, std::max(c.intermediate, kQDim))));
     (void)gemm_tc_supported(1, 1, 64);   // resolve the tensor-map encoder before any capture
     CK(cudaStreamSynchronize(h->stream));
@@ -536,8 +541,8 @@ int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int
             pp.n_pages = h->n_pages;
             pp.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(kHeadDim)));
             pp.err = h->d_err;
-            if (h->rt.kv_dtype == kKvBF16 && items && n_items > 0) {
-                CK(launch_prefill_attn_tc(pp, items, n_items, bf, h->stream));
+            if (h->prefill_tc && prefill_tc_supported(h->rt.kv_dtype) && items && n_items > 0) {
+                CK(launch_prefill_attn_tc(pp, h->rt.kv_dtype, items, n_items, bf, h->stream));
             } else {
                 CK(launch_prefill_attn(pp, h->rt.kv_dtype, bf, h->stream));
             }

@@ -90,6 +90,10 @@ struct qkv_handle {
     std::map<int, Graph> decode_graphs;
     std::map<std::tuple<int, const void *, const void *>, Graph> kv_graphs;
     bool use_graphs = true;
+    // Prefill attention on the tensor cores (K3) for bf16/e4m3 caches; the
+    // environment variable QWENASR_B200_PREFILL_ATTN=cuda_core selects the
+    // CUDA-core kernel instead (a cross-check of the two device paths).
+    bool prefill_tc = true;
     int last_decode_n = -1;   // a graph is captured only for a batch size seen twice in a row
 };
 
