@@ -129,36 +129,48 @@ __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t s2) {
     return r;
 }
 
-// One key row (128 dims of page `page`, kv half `kv`, head g, token `tok`) into
-// row r of a swizzled [2 blocks][128 rows][64] 16-bit tile; a key past the
-// stream's length (`live` false) becomes a zero row, whatever its slot holds.
+// One key row (128 dims of page `page`, kv half `kv`, head g, token `tok`) in
+// registers: 16 x 16 B of bf16, or 8 x 16 B of e4m3 (+ its page scale).  A key
+// past the stream's length (`live` false) is not read and stores as zeros.
+template <typename TC> struct RowRegs {
+    static constexpr int kWords = sizeof(TC) == 2 ? 16 : 8;
+    uint4 w[kWords];
+    float scale;
+    bool live;
+};
+
 template <typename TC>
-__device__ __forceinline__ void load_row(const K3Params &p, uint8_t *tile, int r, int page, int kv, int g, int tok,
-                                         bool live) {
-    if (!live) {
+__device__ __forceinline__ void fetch_row(const K3Params &p, RowRegs<TC> &rr, int page, int kv, int g, int tok,
+                                          bool live) {
+    rr.live = live;
+    rr.scale = 1.0f;
+    if (!live) return;
+    const size_t row = ((static_cast<size_t>(page) * 2 + kv) * kHkv + g) * kPageTokens + tok;
+    const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(p.pool) + row * kHeadDim * sizeof(TC));
 #pragma unroll
-        for (int c = 0; c < 16; ++c) *reinterpret_cast<uint4 *>(tile + (c >> 3) * kBlkBytes + swz(r, c & 7)) = make_uint4(0, 0, 0, 0);
+    for (int c = 0; c < RowRegs<TC>::kWords; ++c) rr.w[c] = __ldg(src + c);
+    if constexpr (sizeof(TC) == 1) rr.scale = __ldg(p.scales + (static_cast<size_t>(page) * 2 + kv) * kHkv + g);
+}
+
+// Row r of a swizzled [2 blocks][128 rows][64] 16-bit tile (e4m3: dequantised
+// exactly to f16, then times the page scale in f16).
+template <typename TC>
+__device__ __forceinline__ void store_row(uint8_t *tile, int r, const RowRegs<TC> &rr) {
+    if (!rr.live) {
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+            *reinterpret_cast<uint4 *>(tile + (c >> 3) * kBlkBytes + swz(r, c & 7)) = make_uint4(0, 0, 0, 0);
         return;
     }
-    const size_t row = ((static_cast<size_t>(page) * 2 + kv) * kHkv + g) * kPageTokens + tok;
     if constexpr (sizeof(TC) == 2) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const __nv_bfloat16 *>(p.pool) + row * kHeadDim);
-        uint4 w[16];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) w[c] = __ldg(src + c);
-#pragma unroll
-        for (int c = 0; c < 16; ++c) *reinterpret_cast<uint4 *>(tile + (c >> 3) * kBlkBytes + swz(r, c & 7)) = w[c];
+        for (int c = 0; c < 16; ++c) *reinterpret_cast<uint4 *>(tile + (c >> 3) * kBlkBytes + swz(r, c & 7)) = rr.w[c];
     } else {
-        const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(p.pool) + row * kHeadDim);
-        const float sc = __ldg(p.scales + (static_cast<size_t>(page) * 2 + kv) * kHkv + g);
-        const uint32_t s2 = pack_h2(sc, sc);
-        uint4 w[8];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) w[c] = __ldg(src + c);
+        const uint32_t s2 = pack_h2(rr.scale, rr.scale);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
             // 16 e4m3 = dims 16c .. 16c+15 -> f16 chunks 2c (dims 16c..+7) and 2c+1
-            const uint32_t ws[4] = {w[c].x, w[c].y, w[c].z, w[c].w};
+            const uint32_t ws[4] = {rr.w[c].x, rr.w[c].y, rr.w[c].z, rr.w[c].w};
             uint32_t h[8];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -259,12 +271,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
             const int page = pt[pi < key_pages ? pi : 0];
             const int tok = key % kPageTokens;
             const int kb = u & 1;
+            // K (and, in pass 2, V) loads in flight together before either buffer is waited on.
+            RowRegs<TC> kr, vr;
+            fetch_row<TC>(p, kr, page, 0, g, tok, key < kv_len);
+            if (pass == 1) fetch_row<TC>(p, vr, page, 1, g, tok, key < kv_len);
             if (*failed || !wait_bar(&bars->k_empty[kb], ((static_cast<uint32_t>(u) >> 1) & 1u) ^ 1u)) {
                 if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, row0, u);
                 *failed = 1;
                 break;
             }
-            load_row<TC>(p, sK0 + kb * kTileBytes, r, page, 0, g, tok, key < kv_len);
+            store_row<TC>(sK0 + kb * kTileBytes, r, kr);
             fence_async_smem();
             mbar_arrive(&bars->k_full[kb]);
             if (pass == 1) {
@@ -274,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
                     *failed = 1;
                     break;
                 }
-                load_row<TC>(p, sV0 + vb * kTileBytes, r, page, 1, g, tok, key < kv_len);
+                store_row<TC>(sV0 + vb * kTileBytes, r, vr);
                 fence_async_smem();
                 mbar_arrive(&bars->v_full[vb]);
             }
@@ -355,20 +371,22 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
         const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * quad) << 16);
         if (n_uses > 0) {
             // Q row, scaled into the log2 domain, swizzled K-major
-            const float *qrow = p.q + static_cast<size_t>(row0 + (real ? i : 0)) * kQDim + (2 * g + h) * kHeadDim;
-#pragma unroll 1
-            for (int c16 = 0; c16 < 16; ++c16) {
-                uint4 w = make_uint4(0, 0, 0, 0);
-                if (real) {
-                    const float4 a = reinterpret_cast<const float4 *>(qrow + c16 * 8)[0];
-                    const float4 b = reinterpret_cast<const float4 *>(qrow + c16 * 8)[1];
-                    const float s = p.scale_log2;
-                    w.x = pack2<kF16>(a.x * s, a.y * s);
-                    w.y = pack2<kF16>(a.z * s, a.w * s);
-                    w.z = pack2<kF16>(b.x * s, b.y * s);
-                    w.w = pack2<kF16>(b.z * s, b.w * s);
+            const float4 *qrow = reinterpret_cast<const float4 *>(
+                p.q + static_cast<size_t>(row0 + (real ? i : 0)) * kQDim + (2 * g + h) * kHeadDim);
+            const float s = p.scale_log2;
+#pragma unroll
+            for (int half_q = 0; half_q < 2; ++half_q) {
+                // 64 dims per half: all 16 loads in flight before any is used
+                float4 a[16];
+#pragma unroll
+                for (int k = 0; k < 16; ++k) a[k] = real ? __ldg(qrow + half_q * 16 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const float4 x = a[2 * c], y = a[2 * c + 1];
+                    const uint4 w = make_uint4(pack2<kF16>(x.x * s, x.y * s), pack2<kF16>(x.z * s, x.w * s),
+                                               pack2<kF16>(y.x * s, y.y * s), pack2<kF16>(y.z * s, y.w * s));
+                    *reinterpret_cast<uint4 *>(sQ + half_q * kBlkBytes + swz(r, c)) = w;
                 }
-                *reinterpret_cast<uint4 *>(sQ + (c16 >> 3) * kBlkBytes + swz(r, c16 & 7)) = w;
             }
             fence_async_smem();
             mbar_arrive(&bars->q_ready);
