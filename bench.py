@@ -38,14 +38,19 @@ METRIC = "decode tokens/s (KV append+GQA attn) & KV-read HBM GB/s vs 8 TB/s, 1-8
 # capture summarised in profiles/decode_attn_k2_config4.md (same 256 streams
 # and contexts; the capture held 2 layers of cache, a launch reads one).
 K2_NCU_TRAFFIC_BYTES = 1_017_933_000 + 5_662_720
+# e4m3 cache (profiles/decode_attn_k2_fp8_config4.md): the capture's launch read
+# 511,785,472 + wrote 7,432,704 bytes for 505,640,384 algorithmic bytes (2-layer
+# run, fewer appended tokens); scaled to a full run's 520,350,080 algorithmic bytes.
+K2_FP8_NCU_TRAFFIC_BYTES = round((511_785_472 + 7_432_704) * 520_350_080 / 505_640_384)
 
 
 def peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d.get("bf16_tflops", 1590.0)),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
 def stream_lengths(rank: int) -> np.ndarray:
@@ -321,7 +326,7 @@ def run_ours(args) -> int:
             "kv_read_gbs_step": round(kv_bytes_per_launch * N_LAYERS / (ms_max / args.steps / 1e3) / 1e9, 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved_gbs / pk["hbm_gbs"], 4), "frac_of_8tbs": round(achieved_gbs / 8000, 4),
-                         "traffic": K2_NCU_TRAFFIC_BYTES if args.kv_dtype == "bf16" else None,
+                         "traffic": {"bf16": K2_NCU_TRAFFIC_BYTES, "fp8": K2_FP8_NCU_TRAFFIC_BYTES}.get(args.kv_dtype),
                          "kernel": "decode_attn_kernel (K2)",
                          "launch_ms": round(attn_ms, 4), "bytes_per_launch": kv_bytes_per_launch,
                          "peak_source": pk["source"]},
@@ -584,16 +589,175 @@ def run_serve(args) -> int:
     return 0
 
 
+
+# ------------------------------------------------------------------ operator legs
+
+PREFILL_STREAMS, PREFILL_TOKENS = 64, 410      # config 3's prompts: 390 audio rows + 20 text tokens
+
+
+def run_prefill_attn(args) -> int:
+    """K3 on its own: causal prefill attention over 28 layers of a paged cache
+    holding config-3 prompts (64 streams x 410 tokens per GPU), through
+    qkv_prefill_attend.  A step = one launch per layer (every layer's cache is
+    a different 107 MB block (bf16), so 28 of them exceed L2 between reuses).
+    value = useful attention TFLOP/s (QK^T and PV of the causal triangle, 16 q
+    heads, D = 128); roofline against the measured dense bf16 peak."""
+    import torch
+
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    rank, local, world, dist = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    n, P = PREFILL_STREAMS, PREFILL_TOKENS
+    qn, kn = qk_norm_weights()
+    cfg = dict(n_layers=N_LAYERS, hidden=1024, n_heads=HQ, n_kv_heads=HKV, head_dim=D, intermediate=3072,
+               vocab=151936, rope_theta=1.0e6, rms_norm_eps=1.0e-6)
+    kvd = {"bf16": pkg.BF16, "fp8": pkg.FP8, "f32": pkg.F32}[args.kv_dtype]
+    rt = pkg.runtime_config(device=local, weight_dtype=pkg.F32, kv_dtype=kvd, max_streams=n, max_context=P + 16,
+                            max_batch_tokens=n * P, page_order_seed=WORKLOAD_SEED + rank)
+    dec = pkg.Decoder.kv_only(cfg, rt, qn, kn)
+    streams = [dec.open() for _ in range(n)]
+    for s_ in streams:
+        dec.extend(s_, P)
+    dec.fill_random(WORKLOAD_SEED + rank)
+    g = torch.Generator(device=dev).manual_seed(WORKLOAD_SEED + rank)
+    q = torch.randn((n * P, HQ * D), device=dev, generator=g)
+    out = torch.empty_like(q)
+    st = torch.cuda.current_stream(dev)
+    lens = [P] * n
+
+    def step():
+        for layer in range(N_LAYERS):
+            dec.prefill_attend(layer, streams, lens, q.data_ptr(), out.data_ptr(), st.cuda_stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    dec.sync()
+    barrier(dist)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as sampler:
+        torch.cuda.synchronize(dev)
+        e0.record(st)
+        for _ in range(args.steps):
+            step()
+        e1.record(st)
+        torch.cuda.synchronize(dev)
+    dec.sync()
+    ms = max_over_ranks(dist, e0.elapsed_time(e1))
+    flops_launch = n * HQ * D * 4 * (P * (P + 1) / 2)
+    tflops = flops_launch * N_LAYERS * args.steps * world / (ms / 1e3) / 1e12
+    per_gpu = flops_launch * N_LAYERS * args.steps / (ms / 1e3) / 1e12
+    pk = peaks()
+    if rank == 0:
+        line = {
+            "metric": "prefill attention TFLOP/s (K3, causal, paged cache)", "value": round(tflops, 2),
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": args.kv_dtype + " cache", "data": "synthetic",
+            "config": {"workload": f"K3 over config-3 prompts: {n} streams x {P} tokens per GPU, 28 layers of "
+                                   f"{args.kv_dtype} paged cache, permuted pages, one launch per layer",
+                       "flops_per_launch": flops_launch},
+            "roofline": {"bound": "tensor", "achieved": round(per_gpu, 1), "peak": pk["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": round(per_gpu / pk["bf16_tflops"], 4), "traffic": None,
+                         "kernel": "prefill_attn_tc_kernel (K3)" if args.kv_dtype != "f32" else "prefill_attn_kernel",
+                         "launch_ms": round(ms / args.steps / N_LAYERS, 4), "peak_source": pk["source"]},
+            "gpu_launches": int(dec.launches()),
+            "clocks": sampler.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+GEMM_SHAPES = {   # name: (N, K) of the decoder projections (W [N][K])
+    "qkv_0.6B": (4096, 1024), "o_0.6B": (1024, 2048), "gate_up_0.6B": (6144, 1024), "down_0.6B": (1024, 3072),
+    "qkv_1.7B": (4096, 2048), "o_1.7B": (2048, 2048), "gate_up_1.7B": (12288, 2048), "down_1.7B": (2048, 6144),
+}
+
+
+def run_gemm(args) -> int:
+    """The tcgen05 projection GEMM (qkv_gemm_bf16) on every decoder projection
+    shape at a decode batch (M = 32, 64) and a prefill batch (M = 1024); each
+    shape is launched 20 times inside one CUDA graph over 4 weight copies.
+    value = FLOP-weighted TFLOP/s over all shapes."""
+    import torch
+
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    rank, local, world, dist = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    rows, tot_flop, tot_ms = [], 0.0, 0.0
+    reps = 20
+    for M in (32, 64, 1024):
+        for name, (N, K) in GEMM_SHAPES.items():
+            ws = [torch.randn(N, K, device=dev).to(torch.bfloat16) for _ in range(4)]
+            x = torch.randn(M, K, device=dev).to(torch.bfloat16)
+            c = torch.empty(M, N, device=dev)
+
+            def call(i, st):
+                rc = pkg.lib.qkv_gemm_bf16(x.data_ptr(), ws[i % 4].data_ptr(), c.data_ptr(), M, N, K, 0, st)
+                if rc != 0:
+                    raise RuntimeError(f"qkv_gemm_bf16 failed: {rc}")
+
+            for i in range(args.warmup):
+                call(i, torch.cuda.current_stream(dev).cuda_stream)
+            torch.cuda.synchronize(dev)
+            graph, side = torch.cuda.CUDAGraph(), torch.cuda.Stream(dev)
+            with torch.cuda.stream(side):
+                with torch.cuda.graph(graph, stream=side):
+                    for i in range(reps):
+                        call(i, side.cuda_stream)
+            graph.replay()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            ms = e0.elapsed_time(e1) / (args.steps * reps)
+            fl = 2.0 * M * N * K
+            tot_flop += fl
+            tot_ms += ms
+            rows.append({"M": M, "shape": name, "N": N, "K": K, "us": round(ms * 1e3, 2),
+                         "tflops": round(fl / (ms / 1e3) / 1e12, 1),
+                         "weight_gbs": round(N * K * 2 / (ms / 1e3) / 1e9, 1)})
+            del graph
+    pk = peaks()
+    value = tot_flop / (tot_ms / 1e3) / 1e12
+    if rank == 0:
+        line = {
+            "metric": "projection GEMM TFLOP/s (tcgen05, bf16 x bf16 -> f32)", "value": round(value, 2),
+            "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(tot_ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "decoder projections of 0.6B and 1.7B at M = 32, 64, 1024 tokens; "
+                                   "20 launches per CUDA graph, 4 weight copies", "shapes": rows},
+            "roofline": {"bound": "tensor", "achieved": round(value, 1), "peak": pk["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": round(value / pk["bf16_tflops"], 4), "traffic": None,
+                         "kernel": "gemm_tc_kernel", "peak_source": pk["source"]},
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("kv", "model", "model3", "serve"), default="kv",
+    ap.add_argument("--workload", choices=("kv", "model", "model3", "serve", "prefill", "gemm"), default="kv",
                     help="kv: config 4 KV step (default); model: config 2 full greedy decode (0.6B bf16, 32 "
                          "streams); model3: config 3 (1.7B bf16, 64 streams, 390 audio + 20 text tokens); "
-                         "serve: config 5 (1.7B, FP8 cache, 512 concurrent streams, Poisson arrivals)")
+                         "serve: config 5 (1.7B, FP8 cache, 512 concurrent streams, Poisson arrivals); "
+                         "prefill: K3 prefill attention over config-3 prompts (--kv-dtype bf16/fp8/f32); "
+                         "gemm: the tcgen05 projection GEMM on every decoder projection shape")
     ap.add_argument("--concurrency", type=int, default=512, help="serve: target concurrent streams per GPU")
     ap.add_argument("--kv-dtype", choices=("bf16", "fp8", "f32"), default="bf16",
                     help="kv workload: cache dtype (bf16 is the config-4 workload)")
@@ -609,6 +773,10 @@ def main() -> int:
         return run_model(args)
     if args.workload == "serve":
         return run_serve(args)
+    if args.workload == "prefill":
+        return run_prefill_attn(args)
+    if args.workload == "gemm":
+        return run_gemm(args)
     return run_ours(args)
 
 

@@ -172,6 +172,16 @@ int qkv_kv_attend(qkv_handle *h, int32_t layer, int32_t n, const int32_t *slots_
 int qkv_gemm_bf16(const void *x, const void *w, float *c, int32_t m, int32_t n, int32_t k, int32_t accumulate,
                   void *stream);
 
+/* Causal prefill attention over one layer's paged cache (K3 on tcgen05 for
+ * bf16/e4m3 caches, the CUDA-core kernel for f32): for each of the n streams
+ * the queries are its LAST lens[i] cached positions (the prompt rows just
+ * appended), attending to every key at or before their position.  q_dev
+ * [sum lens][Hq*D] f32 post-RoPE, rows in stream order; out_dev same shape f32.
+ * stream_ids / lens are host arrays.  The prompt half of
+ * text-decoder.cpp:322-334 (QK^T, diag mask, softmax, PV), as an operator. */
+int qkv_prefill_attend(qkv_handle *h, int32_t layer, int32_t n, const int32_t *stream_ids, const int32_t *lens,
+                       const float *q_dev, float *out_dev, void *stream);
+
 /* One KV-cache step of the microbench: for each of the n streams append one
  * token and attend, for every layer.  qkv[n_layers][n][Hq*D+2*Hkv*D] f32,
  * out[n_layers][n][Hq*D] f32 (layer-major), device pointers; the streams'

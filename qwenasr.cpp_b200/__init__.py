@@ -77,6 +77,7 @@ SIGNATURES = {
     "qkv_kv_attend_noalloc": (C.c_int, [_P, C.c_int32, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, _P,
                                         _P, _P, _P, C.c_char_p, C.c_size_t]),
     "qkv_gemm_bf16": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P]),
+    "qkv_prefill_attend": (C.c_int, [_P, C.c_int32, C.c_int32, _P, _P, _P, _P, _P]),
     "qkv_gguf_tensor": (C.c_int, [C.c_char_p, C.c_char_p, _I64P, _I32P, _I32P, _P, C.c_size_t, C.c_char_p,
                                   C.c_size_t]),
     "qkv_pager_create": (_P, [C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_uint32]),
@@ -278,6 +279,12 @@ class Decoder:
 
     def kv_attend(self, layer, n, slots_ptr, lens_ptr, q_ptr, out_ptr, stream=None):
         self._check(lib.qkv_kv_attend(self.h, layer, n, slots_ptr, lens_ptr, q_ptr, out_ptr, stream))
+
+    def prefill_attend(self, layer, streams, lens, q_ptr: int, out_ptr: int, stream=None):
+        """Causal attention of each stream's last lens[i] positions (device q/out pointers)."""
+        streams, lens = _i32(streams), _i32(lens)
+        self._check(lib.qkv_prefill_attend(self.h, layer, len(streams), _ptr(streams, C.c_int32),
+                                           _ptr(lens, C.c_int32), q_ptr, out_ptr, stream))
 
     def kv_step(self, streams, qkv_ptr: int, out_ptr: int, stream=None):
         streams = _i32(streams)

@@ -9,9 +9,10 @@
 // are [64 queries of head 2g | 64 queries of head 2g+1] and every K/V tile is
 // fetched once for both.  Keys come in tiles of 128 (8 pages).
 //
-// Operand staging: a warpgroup of 128 loader threads, one key row each, reads
-// the row straight from its page with 16-byte loads and writes it into the
-// canonical 128-byte-swizzled UMMA layout — K as the K-major B operand of
+// Operand staging: a warpgroup of 128 loader threads reads each tile's key rows
+// straight from their pages with coalesced 16-byte loads (16 lanes per bf16
+// row, 8 per e4m3 row) and writes them into the canonical 128-byte-swizzled
+// UMMA layout — K as the K-major B operand of
 // S = Q K^T, V as the MN-major B operand of O += P V.  (A page contributes
 // 16 scattered rows per head; one TMA copy per page and column block would be
 // bounded by the rate at which a thread can issue copies.)  For the e4m3 cache
@@ -38,11 +39,13 @@ constexpr int kQPerItem = 64;
 constexpr int kKeyTile = 128;
 constexpr uint32_t kBlkBytes = 128 * 128;                 // [128 rows][64 x 16-bit], 16 KB
 constexpr uint32_t kTileBytes = 2 * kBlkBytes;            // two 64-column blocks, 32 KB
-constexpr int kMmaWarp = 8;
-constexpr int kThreads = 9 * 32;
-// Q, K[2], V[2], P tiles + barriers
-constexpr size_t kSmem = 1024 + 6 * static_cast<size_t>(kTileBytes) + 512;
-constexpr uint32_t kTmemCols = 512;                       // S0 [0,128), S1 [128,256), O [256,384)
+constexpr int kSoftmaxWarp0 = 4;                          // warps 4..11: two softmax warpgroups
+constexpr int kMmaWarp = 12;
+constexpr int kThreads = 13 * 32;
+// Q, K[2], V[2], P tiles + (m, l) hand-over [2 item parities][2 halves][128 rows] + barriers
+constexpr size_t kMlBytes = 2 * 2 * 128 * sizeof(float2);
+constexpr size_t kSmem = 1024 + 6 * static_cast<size_t>(kTileBytes) + kMlBytes + 512;
+constexpr uint32_t kTmemCols = 512;                       // S0 [0,128), S1 [128,256), O0 [256,384), O1 [384,512)
 constexpr uint32_t kTmemO = 256;
 
 struct K3Params {
@@ -129,48 +132,105 @@ __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t s2) {
     return r;
 }
 
-// One key row (128 dims of page `page`, kv half `kv`, head g, token `tok`) in
-// registers: 16 x 16 B of bf16, or 8 x 16 B of e4m3 (+ its page scale).  A key
-// past the stream's length (`live` false) is not read and stores as zeros.
-template <typename TC> struct RowRegs {
-    static constexpr int kWords = sizeof(TC) == 2 ? 16 : 8;
-    uint4 w[kWords];
-    float scale;
-    bool live;
-};
-
-template <typename TC>
-__device__ __forceinline__ void fetch_row(const K3Params &p, RowRegs<TC> &rr, int page, int kv, int g, int tok,
-                                          bool live) {
-    rr.live = live;
-    rr.scale = 1.0f;
-    if (!live) return;
-    const size_t row = ((static_cast<size_t>(page) * 2 + kv) * kHkv + g) * kPageTokens + tok;
-    const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(p.pool) + row * kHeadDim * sizeof(TC));
-#pragma unroll
-    for (int c = 0; c < RowRegs<TC>::kWords; ++c) rr.w[c] = __ldg(src + c);
-    if constexpr (sizeof(TC) == 1) rr.scale = __ldg(p.scales + (static_cast<size_t>(page) * 2 + kv) * kHkv + g);
+// 16-byte asynchronous global -> shared copy (L2 only); src_bytes 0 writes zeros.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+// Arrive on `bar` once every cp.async this thread issued so far has landed.
+__device__ __forceinline__ void cp_async_arrive(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Row r of a swizzled [2 blocks][128 rows][64] 16-bit tile (e4m3: dequantised
+// Page ids of key tile kt's 8 pages (clamped past the stream's last page).
+__device__ __forceinline__ void tile_pages(const int *pt, int key_pages, int kt, int (&pg)[8]) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int pi = kt * 8 + k;
+        pg[k] = __ldg(pt + (pi < key_pages ? pi : 0));
+    }
+}
+
+// bf16 tile by cp.async, straight into the swizzled layout: thread t copies
+// 16-byte chunk t % 16 of rows t / 16 + 8m (row r0 + 8m lies in page m / 2);
+// dead keys are zero-filled by the copy itself.
+__device__ __forceinline__ bool copy_tile_async(const K3Params &p, uint8_t *tile, const int (&pg)[8], int kv_len, int kt,
+                                                int kv, int g, int t) {
+    const int c = t & 15, r0 = t >> 4;
+    bool ok = true;
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+        const int r = r0 + 8 * m;
+        const int key = kt * kKeyTile + r;
+        const bool live = key < kv_len;
+        const int page = pg[m >> 1];
+        const bool valid = page >= 0 && page < p.n_pages;
+        if (live && !valid) ok = false;
+        const size_t row = ((static_cast<size_t>(valid ? page : 0) * 2 + kv) * kHkv + g) * kPageTokens + key % kPageTokens;
+        const uint8_t *src = static_cast<const uint8_t *>(p.pool) + row * kHeadDim * 2 + c * 16;
+        cp_async16(tile + (c >> 3) * kBlkBytes + swz(r, c & 7), src, (live && valid) ? 16u : 0u);
+    }
+    return ok;
+}
+
+// Tile loading, coalesced: the 128 loader threads cover a tile's 128 key rows
+// chunk-wise — for bf16, thread t reads 16-byte chunk t % 16 of rows
+// t / 16 + 8m (m = 0..15), so 16 lanes read one 256-byte row; for e4m3, chunk
+// t % 8 of rows t / 8 + 16m (m = 0..7), 8 lanes per 128-byte row.  Keys past
+// the stream's length are not read and store as zeros.
+template <typename TC> struct TileRegs {
+    static constexpr int kChunks = sizeof(TC) == 2 ? 16 : 8;   // per row
+    static constexpr int kRows = 128 * kChunks / 128;          // rows per thread: 16 (bf16) or 8 (e4m3)
+    static constexpr int kStride = 128 / kRows;                // row step between a thread's rows
+    uint4 w[kRows];
+    float scale[sizeof(TC) == 1 ? kRows : 1];
+    uint32_t live;                                             // bit m: row m of this thread is a live key
+};
+
+// e4m3 tile into registers: thread t reads 16-byte chunk t % 8 of rows
+// t / 8 + 16m (row r0 + 16m lies in page m), with each row's page scale.
+template <typename TC>
+__device__ __forceinline__ bool fetch_tile(const K3Params &p, TileRegs<TC> &tr, const int (&pg)[8], int kv_len, int kt,
+                                           int kv, int g, int t) {
+    static_assert(sizeof(TC) == 1, "register path is the e4m3 cache's");
+    using TR = TileRegs<TC>;
+    const int c = t % TR::kChunks, r0 = t / TR::kChunks;
+    bool ok = true;
+    tr.live = 0;
+#pragma unroll
+    for (int m = 0; m < TR::kRows; ++m) {
+        const int key = kt * kKeyTile + r0 + TR::kStride * m;
+        const bool live = key < kv_len;
+        const bool valid = pg[m] >= 0 && pg[m] < p.n_pages;
+        if (live) tr.live |= 1u << m;
+        if (live && !valid) ok = false;
+        const int page = valid ? pg[m] : 0;
+        const size_t row = ((static_cast<size_t>(page) * 2 + kv) * kHkv + g) * kPageTokens + key % kPageTokens;
+        tr.w[m] = __ldg(reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(p.pool) + row * kHeadDim) + c);
+        tr.scale[m] = __ldg(p.scales + (static_cast<size_t>(page) * 2 + kv) * kHkv + g);
+    }
+#pragma unroll
+    for (int m = 0; m < TR::kRows; ++m) {
+        if (!((tr.live >> m) & 1u)) tr.w[m] = make_uint4(0, 0, 0, 0);
+    }
+    return ok;
+}
+
+// Into a swizzled [2 blocks][128 rows][64] 16-bit tile (e4m3: dequantised
 // exactly to f16, then times the page scale in f16).
 template <typename TC>
-__device__ __forceinline__ void store_row(uint8_t *tile, int r, const RowRegs<TC> &rr) {
-    if (!rr.live) {
+__device__ __forceinline__ void store_tile(uint8_t *tile, const TileRegs<TC> &tr, int t) {
+    using TR = TileRegs<TC>;
+    const int c = t % TR::kChunks, r0 = t / TR::kChunks;
 #pragma unroll
-        for (int c = 0; c < 16; ++c)
-            *reinterpret_cast<uint4 *>(tile + (c >> 3) * kBlkBytes + swz(r, c & 7)) = make_uint4(0, 0, 0, 0);
-        return;
-    }
-    if constexpr (sizeof(TC) == 2) {
-#pragma unroll
-        for (int c = 0; c < 16; ++c) *reinterpret_cast<uint4 *>(tile + (c >> 3) * kBlkBytes + swz(r, c & 7)) = rr.w[c];
-    } else {
-        const uint32_t s2 = pack_h2(rr.scale, rr.scale);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
+    for (int m = 0; m < TR::kRows; ++m) {
+        const int r = r0 + TR::kStride * m;
+        if constexpr (sizeof(TC) == 2) {
+            *reinterpret_cast<uint4 *>(tile + (c >> 3) * kBlkBytes + swz(r, c & 7)) = tr.w[m];
+        } else {
             // 16 e4m3 = dims 16c .. 16c+15 -> f16 chunks 2c (dims 16c..+7) and 2c+1
-            const uint32_t ws[4] = {rr.w[c].x, rr.w[c].y, rr.w[c].z, rr.w[c].w};
+            const uint32_t s2 = pack_h2(tr.scale[m], tr.scale[m]);
+            const uint32_t ws[4] = {tr.w[m].x, tr.w[m].y, tr.w[m].z, tr.w[m].w};
             uint32_t h[8];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -187,53 +247,81 @@ __device__ __forceinline__ void store_row(uint8_t *tile, int r, const RowRegs<TC
 }
 
 struct Bars {
-    uint64_t q_ready, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_free[2], p_full, p_free, o_done;
+    uint64_t q_full, q_empty, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_free[2];
+    uint64_t p_full, p_free, o_full[2], o_empty[2], ml_ready[2], mma_done;
 };
 
-__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity) {
-    return mbar_wait(bar, parity, kWaitLimitCycles);
+// Bounded wait that also gives up as soon as another role set the abort flag.
+__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile int *failed) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*failed) return false;
+        if (clock64() - t0 > kWaitLimitCycles) return false;
+    }
+    return true;
 }
 
+struct ItemInfo {
+    int row0, nq, g, slot, pos0, kv_len, n_kt, key_pages;
+    bool ok;
+};
+
+__device__ __forceinline__ ItemInfo item_info(const K3Params &p, int it) {
+    const int4 v = p.items[it];
+    ItemInfo f;
+    f.row0 = v.x;
+    f.nq = v.y;
+    f.g = v.z;
+    f.slot = p.slots[f.row0];
+    f.pos0 = p.positions[f.row0];
+    f.kv_len = f.pos0 + f.nq;
+    f.n_kt = (f.kv_len + kKeyTile - 1) / kKeyTile;
+    f.key_pages = (f.kv_len + kPageTokens - 1) / kPageTokens;
+    f.ok = f.slot >= 0 && f.slot < p.max_streams && f.pos0 >= 0 && f.nq > 0 && f.nq <= kQPerItem &&
+           f.key_pages <= p.maxp && f.g >= 0 && f.g < kHkv;
+    return f;
+}
+
+// Persistent: CTA c takes items c, c + G, c + 2G, ... (the host orders items
+// longest first).  Every barrier phase follows from per-role counters that
+// run on across items: item j uses Q and O buffers j & 1; K use and S use u
+// (global count) use K/S buffer u & 1; pass-2 tile v (global count) uses V
+// buffer v & 1 and the single P tile.
 template <typename TC>
-__global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p) {
+__global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p, int n_items) {
     constexpr bool kF16 = sizeof(TC) == 1;   // e4m3 cache -> f16 operands
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *sQ = smem;
-    uint8_t *const sK0 = smem + kTileBytes;         // K[b] = sK0 + b * kTileBytes
-    uint8_t *const sV0 = smem + 3 * kTileBytes;     // V[b] = sV0 + b * kTileBytes
-    uint8_t *sP = smem + 5 * kTileBytes;
-    Bars *bars = reinterpret_cast<Bars *>(smem + 6 * kTileBytes);
+    uint8_t *const sQ = smem;
+    uint8_t *const sK0 = smem + kTileBytes;          // K[b] = sK0 + b * kTileBytes
+    uint8_t *const sV0 = smem + 3 * kTileBytes;      // V[b]
+    uint8_t *const sP = smem + 5 * kTileBytes;
+    float2 *const ml = reinterpret_cast<float2 *>(smem + 6 * kTileBytes);   // [parity][half][row]
+    Bars *bars = reinterpret_cast<Bars *>(smem + 6 * kTileBytes + kMlBytes);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 1);
     volatile int *failed = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int4 item = p.items[blockIdx.x];
-    const int row0 = item.x, nq = item.y, g = item.z;
-    const int slot = p.slots[row0];
-    const int pos0 = p.positions[row0];
-    const int kv_len = pos0 + nq;
-    const int n_kt = (kv_len + kKeyTile - 1) / kKeyTile;
-    const int key_pages = (kv_len + kPageTokens - 1) / kPageTokens;
-    const bool item_ok = slot >= 0 && slot < p.max_streams && pos0 >= 0 && nq > 0 && nq <= kQPerItem &&
-                         key_pages <= p.maxp && g >= 0 && g < kHkv;
-    const int *pt = p.page_table + static_cast<size_t>(item_ok ? slot : 0) * p.maxp;
 
     if (threadIdx.x == 0) {
-        mbar_init(&bars->q_ready, 128);
+        mbar_init(&bars->q_full, 128);
+        mbar_init(&bars->q_empty, 1);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&bars->k_full[b], 128);
             mbar_init(&bars->k_empty[b], 1);
             mbar_init(&bars->v_full[b], 128);
             mbar_init(&bars->v_empty[b], 1);
             mbar_init(&bars->s_full[b], 1);
-            mbar_init(&bars->s_free[b], 128);
+            mbar_init(&bars->s_free[b], 256);
+            mbar_init(&bars->o_full[b], 1);
+            mbar_init(&bars->o_empty[b], 256);
+            mbar_init(&bars->ml_ready[b], 256);
         }
-        mbar_init(&bars->p_full, 128);
+        mbar_init(&bars->p_full, 256);
         mbar_init(&bars->p_free, 1);
-        mbar_init(&bars->o_done, 1);
-        *failed = item_ok ? 0 : 1;
-        if (!item_ok) report_error(p.err, kErrRowBounds, kWherePrefillAttn, row0, pos0);
+        mbar_init(&bars->mma_done, 1);
+        *failed = 0;
         fence_mbar_init();
     }
     if (warp == kMmaWarp) {
@@ -245,220 +333,320 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
     fence_before();
     __syncthreads();
     fence_after();
-    // Every page id of the item's keys, checked once by the whole CTA.
-    if (item_ok) {
-        for (int i = threadIdx.x; i < key_pages; i += kThreads) {
-            const int pg = pt[i];
-            if (pg < 0 || pg >= p.n_pages) {
-                report_error(p.err, kErrPageIndex, kWherePrefillAttn, row0, i);
-                *failed = 1;
-            }
-        }
-    }
-    __syncthreads();
     const uint32_t tmem = *tmem_slot;
-    const int n_uses = *failed ? 0 : 2 * n_kt;
 
     if (warp < 4) {
-        // ================= loaders: thread = key row of the tile =================
+        // ================= loaders: Q rows, then K/V tiles chunk-wise =================
         const int r = threadIdx.x;
-        for (int u = 0; u < n_uses; ++u) {
-            const int pass = u / n_kt, kt = u % n_kt;
-            const int key = kt * kKeyTile + r;
-            // Keys past the stream's length are zero rows (masked out of S,
-            // multiplied by P = 0 in P V); their page index is clamped.
-            const int pi = key / kPageTokens;
-            const int page = pt[pi < key_pages ? pi : 0];
-            const int tok = key % kPageTokens;
-            const int kb = u & 1;
-            // K (and, in pass 2, V) loads in flight together before either buffer is waited on.
-            RowRegs<TC> kr, vr;
-            fetch_row<TC>(p, kr, page, 0, g, tok, key < kv_len);
-            if (pass == 1) fetch_row<TC>(p, vr, page, 1, g, tok, key < kv_len);
-            if (*failed || !wait_bar(&bars->k_empty[kb], ((static_cast<uint32_t>(u) >> 1) & 1u) ^ 1u)) {
-                if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, row0, u);
+        uint32_t ku = 0, vu = 0, j = 0;
+        for (int it = blockIdx.x; it < n_items && !*failed; it += gridDim.x, ++j) {
+            const ItemInfo f = item_info(p, it);
+            if (!f.ok) {
+                if (r == 0) report_error(p.err, kErrRowBounds, kWherePrefillAttn, f.row0, f.pos0);
                 *failed = 1;
                 break;
             }
-            store_row<TC>(sK0 + kb * kTileBytes, r, kr);
-            fence_async_smem();
-            mbar_arrive(&bars->k_full[kb]);
-            if (pass == 1) {
-                const int vb = kt & 1;
-                if (*failed || !wait_bar(&bars->v_empty[vb], ((static_cast<uint32_t>(kt) >> 1) & 1u) ^ 1u)) {
-                    if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, row0, -u);
+            const int *pt = p.page_table + static_cast<size_t>(f.slot) * p.maxp;
+            {
+                // Q rows (head 2g + h, query i) -> row (h << 6) | i, scaled into the log2
+                // domain, swizzled K-major.  Warp w fills rows 32w .. 32w+31, one 512-byte
+                // f32 row per load instruction (lane = dims 4 lane .. 4 lane + 3).
+                if (!wait_bar(&bars->q_empty, (j & 1u) ^ 1u, failed)) {
+                    if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, f.row0, -3);
                     *failed = 1;
                     break;
                 }
-                store_row<TC>(sV0 + vb * kTileBytes, r, vr);
+                uint8_t *q_tile = sQ;
+                const float s = p.scale_log2;
+                const int ln = r & 31, w = r >> 5;
+#pragma unroll
+                for (int b8 = 0; b8 < 4; ++b8) {
+                    float4 a[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const int row = 32 * w + 8 * b8 + k, h = row >> 6, i = row & 63;
+                        a[k] = i < f.nq ? __ldg(reinterpret_cast<const float4 *>(
+                                              p.q + static_cast<size_t>(f.row0 + i) * kQDim + (2 * f.g + h) * kHeadDim) + ln)
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const int row = 32 * w + 8 * b8 + k;
+                        const uint2 v = make_uint2(pack2<kF16>(a[k].x * s, a[k].y * s), pack2<kF16>(a[k].z * s, a[k].w * s));
+                        // dims 4 ln .. +3: block ln >> 4, 16-byte chunk (ln >> 1) & 7, half ln & 1
+                        *reinterpret_cast<uint2 *>(q_tile + (ln >> 4) * kBlkBytes + swz(row, (ln >> 1) & 7) + 8 * (ln & 1)) = v;
+                    }
+                }
                 fence_async_smem();
-                mbar_arrive(&bars->v_full[vb]);
+                mbar_arrive(&bars->q_full);
             }
+            const int n_uses = 2 * f.n_kt;
+            bool bad = false;
+            int pg[8], pg_next[8];
+            tile_pages(pt, f.key_pages, 0, pg);
+            for (int u = 0; u < n_uses; ++u) {
+                const int pass = u / f.n_kt, kt = u % f.n_kt;
+                const uint32_t kb = ku & 1;
+                // next use's page ids in flight while this tile's copies are issued
+                if (u + 1 < n_uses) tile_pages(pt, f.key_pages, (u + 1) % f.n_kt, pg_next);
+                if constexpr (sizeof(TC) == 2) {
+                    // bf16: asynchronous copies; the loader runs ahead as far as the buffers allow.
+                    if (!wait_bar(&bars->k_empty[kb], ((ku >> 1) & 1u) ^ 1u, failed)) {
+                        if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, f.row0, u);
+                        *failed = 1;
+                        bad = true;
+                        break;
+                    }
+                    bool ok = copy_tile_async(p, sK0 + kb * kTileBytes, pg, f.kv_len, kt, 0, f.g, r);
+                    cp_async_arrive(&bars->k_full[kb]);
+                    ++ku;
+                    if (pass == 1) {
+                        const uint32_t vb = vu & 1;
+                        if (!wait_bar(&bars->v_empty[vb], ((vu >> 1) & 1u) ^ 1u, failed)) {
+                            if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, f.row0, -u);
+                            *failed = 1;
+                            bad = true;
+                            break;
+                        }
+                        ok = copy_tile_async(p, sV0 + vb * kTileBytes, pg, f.kv_len, kt, 1, f.g, r) && ok;
+                        cp_async_arrive(&bars->v_full[vb]);
+                        ++vu;
+                    }
+                    if (!ok) {
+                        report_error(p.err, kErrPageIndex, kWherePrefillAttn, f.row0, kt);
+                        *failed = 1;
+                        bad = true;
+                        break;
+                    }
+                } else {
+                    // e4m3: K (and, in pass 2, V) loads in flight together, dequantised on the way in.
+                    TileRegs<TC> kr, vr;
+                    bool ok = fetch_tile<TC>(p, kr, pg, f.kv_len, kt, 0, f.g, r);
+                    if (pass == 1) ok = fetch_tile<TC>(p, vr, pg, f.kv_len, kt, 1, f.g, r) && ok;
+                    if (!ok) {
+                        report_error(p.err, kErrPageIndex, kWherePrefillAttn, f.row0, kt);
+                        *failed = 1;
+                        bad = true;
+                        break;
+                    }
+                    if (!wait_bar(&bars->k_empty[kb], ((ku >> 1) & 1u) ^ 1u, failed)) {
+                        if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, f.row0, u);
+                        *failed = 1;
+                        bad = true;
+                        break;
+                    }
+                    store_tile<TC>(sK0 + kb * kTileBytes, kr, r);
+                    fence_async_smem();
+                    mbar_arrive(&bars->k_full[kb]);
+                    ++ku;
+                    if (pass == 1) {
+                        const uint32_t vb = vu & 1;
+                        if (!wait_bar(&bars->v_empty[vb], ((vu >> 1) & 1u) ^ 1u, failed)) {
+                            if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, f.row0, -u);
+                            *failed = 1;
+                            bad = true;
+                            break;
+                        }
+                        store_tile<TC>(sV0 + vb * kTileBytes, vr, r);
+                        fence_async_smem();
+                        mbar_arrive(&bars->v_full[vb]);
+                        ++vu;
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < 8; ++k) pg[k] = pg_next[k];
+            }
+            if (bad) break;
         }
+        if constexpr (sizeof(TC) == 2) asm volatile("cp.async.wait_all;" ::: "memory");   // no copy outlives the CTA
     } else if (warp == kMmaWarp) {
         // ================= MMA issuer =================
         if (lane == 0) {
-            int issued = 0;
-            bool ok = n_uses > 0 && wait_bar(&bars->q_ready, 0);
-            if (n_uses > 0 && !ok) {
-                report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, row0, 1 << 20);
-                *failed = 1;
-            }
-            const uint32_t aQ = smem_u32(sQ), aP = smem_u32(sP);
-            // P V of tile kt: P (K-major A, 16 keys per step), V rows (MN-major B, 2 KB per 16 rows).
-            auto issue_pv = [&](int kt) -> bool {
-                const int vb = kt & 1;
-                if (*failed || !wait_bar(&bars->v_full[vb], (static_cast<uint32_t>(kt) >> 1) & 1u) ||
-                    !wait_bar(&bars->p_full, static_cast<uint32_t>(kt) & 1u))
-                    return false;
-                fence_after();
-                const uint32_t aV = smem_u32(sV0 + vb * kTileBytes);
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t blk = static_cast<uint32_t>(kk >> 2) * kBlkBytes;
-                    const uint64_t step = 2ull * static_cast<uint64_t>(kk & 3);
-                    mma(tmem + kTmemO, desc_kmajor(aP + blk) + step, desc_mnmajor(aV + static_cast<uint32_t>(kk) * 2048u),
-                        idesc_pv<kF16>(), (kt > 0 || kk > 0) ? 1 : 0);
-                }
-                ++issued;
-                commit(&bars->p_free);
-                commit(&bars->v_empty[vb]);
-                return true;
-            };
-            for (int u = 0; ok && u < n_uses; ++u) {
-                const int pass = u / n_kt, kt = u % n_kt;
-                const int kb = u & 1, sb = u & 1;
-                const uint32_t use = (static_cast<uint32_t>(u) >> 1) & 1u;
-                if (*failed || !wait_bar(&bars->k_full[kb], use) || !wait_bar(&bars->s_free[sb], use ^ 1u)) {
+            bool ok = true, any = false;
+            uint32_t ku = 0, vu = 0, j = 0;
+            const uint32_t aP = smem_u32(sP);
+            for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++j) {
+                const ItemInfo f = item_info(p, it);
+                if (!f.ok) break;                  // the loaders report it
+                const uint32_t ob = j & 1;
+                const uint32_t aQ = smem_u32(sQ);
+                const uint32_t tO = tmem + kTmemO + ob * 128u;
+                if (!wait_bar(&bars->q_full, j & 1u, failed) ||
+                    !wait_bar(&bars->o_empty[ob], ((j >> 1) & 1u) ^ 1u, failed)) {
                     ok = false;
                     break;
                 }
-                fence_after();
-                const uint32_t aK = smem_u32(sK0 + kb * kTileBytes);
+                // P V of the item's pass-2 tile kt (global pass-2 count vu).
+                auto issue_pv = [&](int kt) -> bool {
+                    const uint32_t vb = vu & 1;
+                    if (!wait_bar(&bars->v_full[vb], (vu >> 1) & 1u, failed) ||
+                        !wait_bar(&bars->p_full, vu & 1u, failed))
+                        return false;
+                    fence_async_smem();
+                    fence_after();
+                    const uint32_t aV = smem_u32(sV0 + vb * kTileBytes);
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t blk = static_cast<uint32_t>(kk >> 2) * kBlkBytes;
-                    const uint64_t step = 2ull * static_cast<uint64_t>(kk & 3);
-                    mma(tmem + static_cast<uint32_t>(sb * 128), desc_kmajor(aQ + blk) + step,
-                        desc_kmajor(aK + blk) + step, idesc_s<kF16>(), kk > 0);
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint32_t blk = static_cast<uint32_t>(kk >> 2) * kBlkBytes;
+                        const uint64_t step = 2ull * static_cast<uint64_t>(kk & 3);
+                        // P (K-major A, 16 keys per step), V rows (MN-major B, 2 KB per 16 rows)
+                        mma(tO, desc_kmajor(aP + blk) + step, desc_mnmajor(aV + static_cast<uint32_t>(kk) * 2048u),
+                            idesc_pv<kF16>(), (kt > 0 || kk > 0) ? 1 : 0);
+                    }
+                    commit(&bars->p_free);
+                    commit(&bars->v_empty[vb]);
+                    ++vu;
+                    return true;
+                };
+                const int n_uses = 2 * f.n_kt;
+                for (int u = 0; u < n_uses; ++u) {
+                    const int pass = u / f.n_kt, kt = u % f.n_kt;
+                    const uint32_t kb = ku & 1, use = (ku >> 1) & 1u;
+                    if (!wait_bar(&bars->k_full[kb], use, failed) || !wait_bar(&bars->s_free[kb], use ^ 1u, failed)) {
+                        ok = false;
+                        break;
+                    }
+                    fence_async_smem();     // loader-written tile -> async proxy (tcgen05.mma operand)
+                    fence_after();
+                    const uint32_t aK = smem_u32(sK0 + kb * kTileBytes);
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint32_t blk = static_cast<uint32_t>(kk >> 2) * kBlkBytes;
+                        const uint64_t step = 2ull * static_cast<uint64_t>(kk & 3);
+                        mma(tmem + kb * 128u, desc_kmajor(aQ + blk) + step, desc_kmajor(aK + blk) + step,
+                            idesc_s<kF16>(), kk > 0);
+                    }
+                    any = true;
+                    commit(&bars->s_full[kb]);
+                    commit(&bars->k_empty[kb]);
+                    if (u == n_uses - 1) commit(&bars->q_empty);   // Q is read by S MMAs only
+                    ++ku;
+                    if (pass == 1 && kt > 0 && !issue_pv(kt - 1)) {
+                        ok = false;
+                        break;
+                    }
                 }
-                ++issued;
-                commit(&bars->s_full[sb]);
-                commit(&bars->k_empty[kb]);
-                if (pass == 1 && kt > 0 && !issue_pv(kt - 1)) {
+                if (!ok || !issue_pv(f.n_kt - 1)) {
                     ok = false;
                     break;
                 }
+                commit(&bars->o_full[ob]);
             }
-            if (ok && n_uses > 0 && !issue_pv(n_kt - 1)) ok = false;
-            if (!ok && n_uses > 0) {
-                report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, row0, 1 << 21);
+            if (!ok) {
+                if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, blockIdx.x, 1 << 21);
                 *failed = 1;
             }
-            // o_done completes when every issued MMA has, on the error path too.
-            if (issued > 0) commit(&bars->o_done);
-            else mbar_arrive(&bars->o_done);
-            wait_bar(&bars->o_done, 0);
+            // Every MMA this thread issued has completed before TMEM is freed (error path too).
+            if (any) {
+                commit(&bars->mma_done);
+                mbar_wait(&bars->mma_done, 0, kWaitLimitCycles);
+            }
         }
         __syncwarp();
     } else {
-        // ================= softmax / epilogue: thread = query row =================
+        // ============ softmax / epilogue: two warpgroups, thread = (query row, key half) ============
+        const int sg = (warp - kSoftmaxWarp0) >> 2;       // columns [64 sg, 64 sg + 64) of S, P and O
         const int quad = warp & 3;
         const int r = 32 * quad + lane;          // TMEM lane and MMA row
         const int h = r >> 6, i = r & 63;
-        const bool real = i < nq;
-        const int pos_r = pos0 + (real ? i : nq - 1);
         const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * quad) << 16);
-        if (n_uses > 0) {
-            // Q row, scaled into the log2 domain, swizzled K-major
-            const float4 *qrow = reinterpret_cast<const float4 *>(
-                p.q + static_cast<size_t>(row0 + (real ? i : 0)) * kQDim + (2 * g + h) * kHeadDim);
-            const float s = p.scale_log2;
-#pragma unroll
-            for (int half_q = 0; half_q < 2; ++half_q) {
-                // 64 dims per half: all 16 loads in flight before any is used
-                float4 a[16];
-#pragma unroll
-                for (int k = 0; k < 16; ++k) a[k] = real ? __ldg(qrow + half_q * 16 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const float4 x = a[2 * c], y = a[2 * c + 1];
-                    const uint4 w = make_uint4(pack2<kF16>(x.x * s, x.y * s), pack2<kF16>(x.z * s, x.w * s),
-                                               pack2<kF16>(y.x * s, y.y * s), pack2<kF16>(y.z * s, y.w * s));
-                    *reinterpret_cast<uint4 *>(sQ + half_q * kBlkBytes + swz(r, c)) = w;
-                }
-            }
-            fence_async_smem();
-            mbar_arrive(&bars->q_ready);
-        }
-        float m_run = -INFINITY, l_run = 0.0f, inv_l = 0.0f;
-        for (int u = 0; u < n_uses; ++u) {
-            const int pass = u / n_kt, kt = u % n_kt;
-            const int sb = u & 1;
-            // Every exit decision is warp-uniform: the tcgen05.ld below is .sync.aligned.
-            bool go = !*failed && wait_bar(&bars->s_full[sb], (static_cast<uint32_t>(u) >> 1) & 1u);
-            if (!__all_sync(0xffffffffu, go)) break;
-            fence_after();
-            if (pass == 1 && kt == 0) inv_l = 1.0f / l_run;
-            uint32_t packed[4][16];
-#pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
-                float s[32];
-                tmem_ld32(lane_addr + static_cast<uint32_t>(sb * 128 + ch * 32), s);
-                const int key0 = kt * kKeyTile + ch * 32;
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    if (key0 + j > pos_r) s[j] = -INFINITY;
-                }
-                if (pass == 0) {
-                    float cm = s[0];
-#pragma unroll
-                    for (int j = 1; j < 32; ++j) cm = fmaxf(cm, s[j]);
-                    const float m_new = fmaxf(m_run, cm);
-                    if (m_new != -INFINITY) {
-                        float acc = 0.0f;
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) acc += exp2f(s[j] - m_new);
-                        l_run = l_run * exp2f(m_run - m_new) + acc;
-                        m_run = m_new;
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        packed[ch][j] = pack2<kF16>(exp2f(s[2 * j] - m_run) * inv_l, exp2f(s[2 * j + 1] - m_run) * inv_l);
-                }
-            }
-            // S buffer sb read out: the issuer may compute the next-but-one tile into it.
-            fence_before();
-            mbar_arrive(&bars->s_free[sb]);
-            if (pass == 1) {
-                go = !*failed && wait_bar(&bars->p_free, (static_cast<uint32_t>(kt) & 1u) ^ 1u);
+        uint32_t su = 0, pu = 0, j = 0;
+        for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++j) {
+            const ItemInfo f = item_info(p, it);
+            if (!f.ok) break;                      // the loaders report it
+            const bool real = i < f.nq;
+            const int pos_r = f.pos0 + (real ? i : f.nq - 1);
+            const uint32_t ob = j & 1;
+            float m_run = -INFINITY, l_run = 0.0f, inv_l = 0.0f;
+            const int n_uses = 2 * f.n_kt;
+            bool go = true;
+            for (int u = 0; u < n_uses; ++u) {
+                const int pass = u / f.n_kt, kt = u % f.n_kt;
+                const uint32_t sb = su & 1;
+                // Every exit decision is warp-uniform: the tcgen05.ld below is .sync.aligned.
+                go = wait_bar(&bars->s_full[sb], (su >> 1) & 1u, failed);
                 if (!__all_sync(0xffffffffu, go)) break;
+                fence_after();
+                uint32_t packed[2][16];
 #pragma unroll
-                for (int ch = 0; ch < 4; ++ch) {
-                    // keys ch*32 .. +31 = 4 chunks of 8 in block ch >> 1
-                    uint8_t *blk = sP + (ch >> 1) * kBlkBytes;
+                for (int ch = 0; ch < 2; ++ch) {
+                    float s[32];
+                    tmem_ld32(lane_addr + sb * 128u + static_cast<uint32_t>(64 * sg + 32 * ch), s);
+                    const int key0 = kt * kKeyTile + 64 * sg + 32 * ch;
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        const int chunk = (ch & 1) * 4 + c;
-                        *reinterpret_cast<uint4 *>(blk + swz(r, chunk)) =
-                            make_uint4(packed[ch][4 * c], packed[ch][4 * c + 1], packed[ch][4 * c + 2], packed[ch][4 * c + 3]);
+                    for (int jj = 0; jj < 32; ++jj) {
+                        if (key0 + jj > pos_r) s[jj] = -INFINITY;
+                    }
+                    if (pass == 0) {
+                        float cm = s[0];
+#pragma unroll
+                        for (int jj = 1; jj < 32; ++jj) cm = fmaxf(cm, s[jj]);
+                        const float m_new = fmaxf(m_run, cm);
+                        if (m_new != -INFINITY) {
+                            float acc = 0.0f;
+#pragma unroll
+                            for (int jj = 0; jj < 32; ++jj) acc += exp2f(s[jj] - m_new);
+                            l_run = l_run * exp2f(m_run - m_new) + acc;
+                            m_run = m_new;
+                        }
+                    } else {
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj)
+                            packed[ch][jj] =
+                                pack2<kF16>(exp2f(s[2 * jj] - m_run) * inv_l, exp2f(s[2 * jj + 1] - m_run) * inv_l);
                     }
                 }
-                fence_async_smem();
-                mbar_arrive(&bars->p_full);
+                // S buffer read out: the issuer may compute the next-but-one tile into it.
+                fence_before();
+                mbar_arrive(&bars->s_free[sb]);
+                ++su;
+                if (pass == 0 && kt == f.n_kt - 1) {
+                    // Row statistics of the two key halves -> the row's max and 1 / sum.
+                    float2 *slot = ml + (static_cast<size_t>(j & 1) * 2) * 128;
+                    slot[sg * 128 + r] = make_float2(m_run, l_run);
+                    mbar_arrive(&bars->ml_ready[j & 1]);
+                    go = wait_bar(&bars->ml_ready[j & 1], (j >> 1) & 1u, failed);
+                    if (!__all_sync(0xffffffffu, go)) break;
+                    const float2 o2 = slot[(1 - sg) * 128 + r];
+                    const float M = fmaxf(m_run, o2.x);
+                    const float L = (m_run == -INFINITY ? 0.0f : l_run * exp2f(m_run - M)) +
+                                    (o2.x == -INFINITY ? 0.0f : o2.y * exp2f(o2.x - M));
+                    m_run = M;
+                    inv_l = 1.0f / L;
+                }
+                if (pass == 1) {
+                    go = wait_bar(&bars->p_free, (pu & 1u) ^ 1u, failed);
+                    if (!__all_sync(0xffffffffu, go)) break;
+                    // keys 64 sg .. +63 = block sg of P (8 chunks of 8 keys)
+                    uint8_t *blk = sP + sg * kBlkBytes;
+#pragma unroll
+                    for (int ch = 0; ch < 2; ++ch) {
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            *reinterpret_cast<uint4 *>(blk + swz(r, 4 * ch + c)) = make_uint4(
+                                packed[ch][4 * c], packed[ch][4 * c + 1], packed[ch][4 * c + 2], packed[ch][4 * c + 3]);
+                        }
+                    }
+                    fence_async_smem();
+                    mbar_arrive(&bars->p_full);
+                    ++pu;
+                }
             }
-        }
-        // Epilogue: O row (128 dims) -> attention output of (query i, head 2g+h)
-        bool done = n_uses > 0 && wait_bar(&bars->o_done, 0) && !*failed;
-        done = __all_sync(0xffffffffu, done);   // warp-uniform: the whole warp loads TMEM, only real rows store
-        fence_after();
-        if (done) {
-            const size_t off = static_cast<size_t>(row0 + (real ? i : 0)) * kQDim + (2 * g + h) * kHeadDim;
+            if (!__all_sync(0xffffffffu, go)) break;
+            // Epilogue: dims [64 sg, 64 sg + 64) of the O row -> attention output of (query i, head 2g+h)
+            go = wait_bar(&bars->o_full[ob], (j >> 1) & 1u, failed);
+            if (!__all_sync(0xffffffffu, go)) break;   // warp-uniform: the whole warp loads TMEM
+            fence_after();
+            const size_t off = static_cast<size_t>(f.row0 + (real ? i : 0)) * kQDim + (2 * f.g + h) * kHeadDim + 64 * sg;
 #pragma unroll 1
-            for (int ch = 0; ch < 4; ++ch) {
+            for (int ch = 0; ch < 2; ++ch) {
                 float o[32];
-                tmem_ld32(lane_addr + kTmemO + static_cast<uint32_t>(ch * 32), o);
+                tmem_ld32(lane_addr + kTmemO + ob * 128u + static_cast<uint32_t>(64 * sg + 32 * ch), o);
+                if (ch == 1) {
+                    // O buffer ob read out: item j + 2 may accumulate into it.
+                    fence_before();
+                    mbar_arrive(&bars->o_empty[ob]);
+                }
                 if (!real) continue;
                 if (p.out_bf16) {
                     __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(p.out) + off + ch * 32;
@@ -515,8 +703,13 @@ cudaError_t launch_prefill_attn_tc(const PrefillAttnParams &pp, int kv_dtype, co
     p.n_pages = pp.n_pages;
     p.scale_log2 = pp.scale_log2;
     p.err = pp.err;
-    if (kv_dtype == kKvBF16) prefill_attn_tc_kernel<__nv_bfloat16><<<n_items, kThreads, kSmem, st>>>(p);
-    else prefill_attn_tc_kernel<uint8_t><<<n_items, kThreads, kSmem, st>>>(p);
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    const int grid = n_items < sms ? n_items : sms;   // persistent: one CTA per SM walks the items
+    if (kv_dtype == kKvBF16) prefill_attn_tc_kernel<__nv_bfloat16><<<grid, kThreads, kSmem, st>>>(p, n_items);
+    else prefill_attn_tc_kernel<uint8_t><<<grid, kThreads, kSmem, st>>>(p, n_items);
     return cudaGetLastError();
 }
 

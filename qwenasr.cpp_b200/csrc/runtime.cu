@@ -9,6 +9,7 @@
 #include <functional>
 #include <memory>
 #include <mutex>
+#include <vector>
 
 #include "gguf.h"
 
@@ -155,6 +156,7 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
     CK(cudaMalloc(&h->d_rowbuf, 4 * R * sizeof(int)));
     CK(cudaMallocHost(&h->h_rowbuf, qkv_handle::kRowRing * 4 * R * sizeof(int)));
     for (auto &ev : h->row_ev) CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&h->items_ev, cudaEventDisableTiming));
     CK(cudaMalloc(&h->d_out_ids, R * sizeof(int)));
     CK(cudaMallocHost(&h->h_out_ids, R * sizeof(int)));
     h->max_items = (h->max_rows / 64 + h->rt.max_streams + 1) * kHkv;
@@ -201,6 +203,7 @@ void destroy(qkv_handle *h) {
     for (auto &ev : h->row_ev) {
         if (ev) cudaEventDestroy(ev);
     }
+    if (h->items_ev) cudaEventDestroy(h->items_ev);
     if (h->stream) cudaStreamDestroy(h->stream);
     delete h->pager;
     delete h;
@@ -327,18 +330,35 @@ int stream_len(qkv_handle *h, int32_t s) {
 // Prefill attention items: per stream chunk of <= 64 consecutive prompt rows
 // (one stream each), per kv head.  Uploaded from pinned staging on the
 // handle's stream (prefill calls are synchronous, so the staging is free).
-int upload_items(qkv_handle *h, int n, const int32_t *lens, int *n_items) {
+// Row index of stream i's first prompt row in a batch laid out stream by stream.
+static int t_first(int i, const int32_t *lens) {
+    int t = 0;
+    for (int k = 0; k < i; ++k) t += lens[k];
+    return t;
+}
+
+// Prefill attention work items (first row, queries <= 64, kv head), ordered by
+// the number of keys they attend to, longest first: K3's persistent CTAs take
+// items round-robin, so this balances them.  base[i] = the stream's position
+// of its first query row (nullptr: 0).
+int upload_items(qkv_handle *h, int n, const int32_t *lens, const int *base, int *n_items, cudaStream_t st) {
+    // h_items is rewritten only after the copy that last read it has run.
+    cudaEventSynchronize(h->items_ev);
     int k = 0, row = 0;
     for (int i = 0; i < n; ++i) {
         for (int q0 = 0; q0 < lens[i]; q0 += 64) {
+            const int nq = std::min(64, lens[i] - q0);
+            const int keys = (base ? base[i] : 0) + q0 + nq;
             for (int g = 0; g < kHkv; ++g) {
                 if (k >= h->max_items) return fail(h, QKV_ERR_CAPACITY, "too many prefill attention items");
-                h->h_items[k++] = make_int4(row + q0, std::min(64, lens[i] - q0), g, 0);
+                h->h_items[k++] = make_int4(row + q0, nq, g, keys);
             }
         }
         row += lens[i];
     }
-    CK(cudaMemcpyAsync(h->d_items, h->h_items, static_cast<size_t>(k) * sizeof(int4), cudaMemcpyHostToDevice, h->stream));
+    std::stable_sort(h->h_items, h->h_items + k, [](const int4 &a, const int4 &b) { return a.w > b.w; });
+    CK(cudaMemcpyAsync(h->d_items, h->h_items, static_cast<size_t>(k) * sizeof(int4), cudaMemcpyHostToDevice, st));
+    CK(cudaEventRecord(h->items_ev, st));
     *n_items = k;
     return QKV_OK;
 }
@@ -511,6 +531,30 @@ int head_and_argmax(qkv_handle *h, int n, const int *d_rows) {
 
 // All layers over `n` rows whose inputs are in h->x; decode rows attend with
 // K2, prompt rows with the causal prefill kernel.
+// Causal prefill attention over layer l's cache for n query rows (slots,
+// positions on the device): K3 on the tensor cores for bf16/e4m3 caches
+// (items = 64-query blocks per kv head), the CUDA-core kernel otherwise.
+cudaError_t prefill_attend(qkv_handle *h, int l, int n, const int *slots, const int *pos, const float *q, void *out,
+                           bool out_bf16, const int4 *items, int n_items, cudaStream_t st) {
+    PrefillAttnParams pp{};
+    pp.n = n;
+    pp.slots = slots;
+    pp.positions = pos;
+    pp.q = q;
+    pp.out = out;
+    pp.pool = static_cast<const uint8_t *>(h->pool) + h->pool_layer_bytes * static_cast<size_t>(l);
+    pp.scales = h->scales ? h->scales + h->scales_layer_elems * static_cast<size_t>(l) : nullptr;
+    pp.page_table = h->d_page_table;
+    pp.maxp = h->maxp;
+    pp.max_streams = h->rt.max_streams;
+    pp.n_pages = h->n_pages;
+    pp.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(kHeadDim)));
+    pp.err = h->d_err;
+    if (h->prefill_tc && prefill_tc_supported(h->rt.kv_dtype) && items && n_items > 0)
+        return launch_prefill_attn_tc(pp, h->rt.kv_dtype, items, n_items, out_bf16, st);
+    return launch_prefill_attn(pp, h->rt.kv_dtype, out_bf16, st);
+}
+
 int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int *lens, bool prompt, int l0 = 0,
                int l1 = -1, const int4 *items = nullptr, int n_items = 0) {
     const qkv_model_config &c = h->cfg;
@@ -527,25 +571,7 @@ int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int
         } else {
             AppendParams ap = append_params(h, l, n, slots, pos, h->qkv, h->q, L.q_norm, L.k_norm);
             CK(launch_kv_append(ap, h->rt.kv_dtype, h->stream));
-            PrefillAttnParams pp{};
-            pp.n = n;
-            pp.slots = slots;
-            pp.positions = pos;
-            pp.q = h->q;
-            pp.out = h->attn;
-            pp.pool = ap.pool;
-            pp.scales = ap.scales;
-            pp.page_table = h->d_page_table;
-            pp.maxp = h->maxp;
-            pp.max_streams = h->rt.max_streams;
-            pp.n_pages = h->n_pages;
-            pp.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(kHeadDim)));
-            pp.err = h->d_err;
-            if (h->prefill_tc && prefill_tc_supported(h->rt.kv_dtype) && items && n_items > 0) {
-                CK(launch_prefill_attn_tc(pp, h->rt.kv_dtype, items, n_items, bf, h->stream));
-            } else {
-                CK(launch_prefill_attn(pp, h->rt.kv_dtype, bf, h->stream));
-            }
+            CK(prefill_attend(h, l, n, slots, pos, h->q, h->attn, bf, items, n_items, h->stream));
             h->launches += 2;
         }
         CK(gemm(h, h->attn, L.w_o, h->x, n, c.hidden, kQDim, 1));
@@ -808,7 +834,9 @@ int qkv_prefill(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32
     CK(cudaMemcpyAsync(h->x, embeddings, static_cast<size_t>(T) * h->cfg.hidden * sizeof(float), cudaMemcpyHostToDevice,
                        h->stream));
     int n_items = 0;
-    if ((rc = upload_items(h, n, lens, &n_items))) return rc;
+    std::vector<int> base(static_cast<size_t>(n));
+    for (int i = 0; i < n; ++i) base[static_cast<size_t>(i)] = hp[t_first(i, lens)];
+    if ((rc = upload_items(h, n, lens, base.data(), &n_items, h->stream))) return rc;
     if ((rc = run_layers(h, T, ds, dp, nullptr, true, 0, -1, h->d_items, n_items))) return rc;
     if ((rc = head_and_argmax(h, n, dr))) return rc;
     return finish_ids(h, n, stream_ids, out_ids, out_logits);
@@ -890,7 +918,7 @@ int qkv_layer_forward(qkv_handle *h, int32_t layer, int32_t tokens, const float 
         cudaError_t e = cudaMemcpyAsync(h->x, x, bytes, cudaMemcpyHostToDevice, h->stream);
         if (e != cudaSuccess) rc = cuda_fail(h, e, "layer_forward upload");
         int n_items = 0;
-        if (rc == QKV_OK) rc = upload_items(h, 1, &tokens, &n_items);
+        if (rc == QKV_OK) rc = upload_items(h, 1, &tokens, nullptr, &n_items, h->stream);
         if (rc == QKV_OK)
             rc = run_layers(h, tokens, h->d_rowbuf, h->d_rowbuf + tokens, nullptr, true, layer, layer + 1, h->d_items,
                             n_items);
@@ -969,6 +997,43 @@ int qkv_kv_attend(qkv_handle *h, int32_t layer, int32_t n, const int32_t *slots_
     cudaStream_t st = static_cast<cudaStream_t>(stream);   // NULL: the legacy default stream
     AttendParams at = attend_params(h, layer, n, slots_dev, lens_dev, q_dev, out_dev);
     CK(launch_decode_attn(at, h->rt.kv_dtype, false, h->num_sms, st));
+    h->launches += 1;
+    return QKV_OK;
+}
+
+int qkv_prefill_attend(qkv_handle *h, int32_t layer, int32_t n, const int32_t *stream_ids, const int32_t *lens,
+                       const float *q_dev, float *out_dev, void *stream) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    if (layer < 0 || layer >= h->cfg.n_layers || n < 0 || (n > 0 && (!stream_ids || !lens || !q_dev || !out_dev)))
+        return fail(h, QKV_ERR_INVALID_ARG, "prefill_attend: bad layer, count or pointer");
+    int rc;
+    if ((rc = check_streams(h, n, stream_ids))) return rc;
+    int64_t total = 0;
+    for (int i = 0; i < n; ++i) {
+        if (lens[i] <= 0 || lens[i] > stream_len(h, stream_ids[i]))
+            return fail(h, QKV_ERR_INVALID_ARG, "prefill_attend: query count must be in 1..stream length");
+        total += lens[i];
+    }
+    if (total > h->max_rows) return fail(h, QKV_ERR_CAPACITY, "prefill_attend rows exceed max_batch_tokens");
+    if (total == 0) return QKV_OK;
+    CK(cudaSetDevice(h->device));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);   // NULL: the legacy default stream
+    const int T = static_cast<int>(total);
+    int *hs = row_stage(h), *hp = hs + T;
+    int t = 0;
+    for (int i = 0; i < n; ++i) {
+        const int base = stream_len(h, stream_ids[i]) - lens[i];
+        for (int k = 0; k < lens[i]; ++k, ++t) {
+            hs[t] = stream_ids[i];
+            hp[t] = base + k;
+        }
+    }
+    if ((rc = row_upload(h, hs, static_cast<size_t>(2 * T), st))) return rc;
+    int n_items = 0;
+    std::vector<int> base(static_cast<size_t>(n));
+    for (int i = 0; i < n; ++i) base[static_cast<size_t>(i)] = stream_len(h, stream_ids[i]) - lens[i];
+    if ((rc = upload_items(h, n, lens, base.data(), &n_items, st))) return rc;
+    CK(prefill_attend(h, layer, T, h->d_rowbuf, h->d_rowbuf + T, q_dev, out_dev, false, h->d_items, n_items, st));
     h->launches += 1;
     return QKV_OK;
 }

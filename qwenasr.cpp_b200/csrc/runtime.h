@@ -66,6 +66,7 @@ struct qkv_handle {
     int *h_rowbuf = nullptr;    // pinned staging, kRowRing slots of [4][max_rows]
     static constexpr int kRowRing = 4;
     cudaEvent_t row_ev[kRowRing] = {};   // recorded after the copy out of each slot
+    cudaEvent_t items_ev = nullptr;      // recorded after the copy out of h_items
     int row_slot = 0;
     int *d_out_ids = nullptr;   // [max_rows]
     int *h_out_ids = nullptr;   // pinned

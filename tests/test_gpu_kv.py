@@ -21,14 +21,14 @@ def bits_to_f32(b: np.ndarray) -> np.ndarray:
     return (b.astype(np.uint32) << 16).view(np.float32)
 
 
-def kv_handle(pkg, kv_dtype, n_layers=2, max_streams=8, max_context=4096, seed=0, pages=0):
+def kv_handle(pkg, kv_dtype, n_layers=2, max_streams=8, max_context=4096, seed=0, pages=0, batch_tokens=0):
     rng = np.random.default_rng(99)
     qn = (1.0 + 0.1 * rng.standard_normal((n_layers, D))).astype(np.float32)
     kn = (1.0 + 0.1 * rng.standard_normal((n_layers, D))).astype(np.float32)
     cfg = dict(n_layers=n_layers, hidden=256, n_heads=HQ, n_kv_heads=HKV, head_dim=D, intermediate=512, vocab=1000,
                rope_theta=1.0e6, rms_norm_eps=1.0e-6)
     rt = pkg.runtime_config(device=0, kv_dtype=kv_dtype, max_streams=max_streams, max_context=max_context,
-                            max_pages=pages, page_order_seed=seed)
+                            max_pages=pages, max_batch_tokens=batch_tokens, page_order_seed=seed)
     return pkg.Decoder.kv_only(cfg, rt, qn, kn), qn, kn
 
 
@@ -310,3 +310,47 @@ def test_fp8_append_dequantises_within_e4m3_precision(pkg, checker, style):
                     want = ref[rows, cols]
                     bound = np.abs(want).max() * 2.0 ** -4
                     assert np.abs(deq - want).max() <= bound, (style, pg, kv, g)
+
+
+@pytest.mark.parametrize("kv_dtype", [0, 1, 2])
+def test_prefill_attention_operator(pkg, checker, kv_dtype):
+    """qkv_prefill_attend (K3 on tcgen05 for bf16/e4m3, CUDA cores for f32)
+    against exact causal attention over the cache as stored: ragged streams,
+    whole prompts and the tail of a longer stream (a continued prefill, queries
+    at positions 200..299).  f32: 2e-5 relative; bf16/e4m3: 2e-2, because K3
+    rounds Q and P to its 16-bit operand type (and e4m3 K/V times their scale
+    to f16)."""
+    lens_total = [1, 17, 64, 65, 130, 300, 410]
+    q_lens = [1, 17, 64, 65, 130, 100, 410]
+    dec, qn, kn = kv_handle(pkg, kv_dtype, seed=5, max_streams=len(lens_total), max_context=512, batch_tokens=1024)
+    with dec:
+        rng = np.random.default_rng(23)
+        streams = []
+        for L in lens_total:
+            s = dec.open()
+            dec.extend(s, L)
+            fill_stream(dec, 0, s, rng.standard_normal((L, QKV), dtype=np.float32))
+            streams.append(s)
+        n_rows = sum(q_lens)
+        qv = rng.standard_normal((n_rows, HQ * D), dtype=np.float32)
+        q = torch.tensor(qv, device="cuda")
+        out = torch.full_like(q, float("nan"))
+        dec.prefill_attend(0, streams, q_lens, q.data_ptr(), out.data_ptr())
+        torch.cuda.synchronize()
+        dec.sync()
+        got = out.cpu().numpy()
+        worst, row = 0.0, 0
+        for s, L, nq in zip(streams, lens_total, q_lens):
+            kv_got = dec.gather(0, s, kv_dtype)
+            k, v = fp8_dequant(*kv_got) if kv_dtype == 2 else kv_got
+            if kv_dtype == 1:
+                k, v = bits_to_f32(k), bits_to_f32(v)
+            for j in range(nq):
+                pos = L - nq + j
+                want = checker.attend(qv[row], k[:pos + 1], v[:pos + 1])
+                err = np.max(np.abs(got[row] - want)) / max(np.max(np.abs(want)), 1e-6)
+                worst = max(worst, err)
+                row += 1
+        tol = 2e-5 if kv_dtype == 0 else 2e-2
+        print(f"kv={kv_dtype}: prefill attention max relative error {worst:.3e}")
+        assert worst < tol, worst
