@@ -73,6 +73,8 @@ __device__ __forceinline__ void norm_rope8(float (&x)[8], const float *w8, const
 
 template <typename TC>
 __global__ void __launch_bounds__(512) kv_append_kernel(AppendParams p) {
+    pdl_trigger();
+    pdl_wait();   // everything below reads or writes memory of earlier kernels
     const int row = blockIdx.x;
     const int unit = threadIdx.x >> 4;      // 0..31
     const int l16 = threadIdx.x & 15;
@@ -140,6 +142,8 @@ __global__ void __launch_bounds__(512) kv_append_kernel(AppendParams p) {
 // will take more tokens) and the tokens already stored are re-quantised to
 // it.  K1 then stores the new tokens with the settled scale.
 __global__ void __launch_bounds__(256) fp8_page_scale_kernel(AppendParams p) {
+    pdl_trigger();
+    pdl_wait();   // everything below reads or writes memory of earlier kernels
     // CTA per row; only the first row of each page group works (block-uniform exit).
     const int row0 = blockIdx.x;
     const int slot = p.slots[row0], pos0 = p.positions[row0];
@@ -274,20 +278,18 @@ __global__ void page_fill_kernel(TC *pool, float *scales, const int *pages, int 
 
 cudaError_t launch_fp8_page_scale(const AppendParams &p, cudaStream_t st) {
     if (p.n <= 0) return cudaSuccess;
-    fp8_page_scale_kernel<<<p.n, 256, 0, st>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(fp8_page_scale_kernel, dim3(p.n), dim3(256), 0, st, p);
 }
 
 cudaError_t launch_kv_append(const AppendParams &p, int kv_dtype, cudaStream_t st) {
     if (p.n <= 0) return cudaSuccess;
     switch (kv_dtype) {
-        case kKvF32: kv_append_kernel<float><<<p.n, 512, 0, st>>>(p); break;
-        case kKvBF16: kv_append_kernel<__nv_bfloat16><<<p.n, 512, 0, st>>>(p); break;
+        case kKvF32: return launch_pdl(kv_append_kernel<float>, dim3(p.n), dim3(512), 0, st, p);
+        case kKvBF16: return launch_pdl(kv_append_kernel<__nv_bfloat16>, dim3(p.n), dim3(512), 0, st, p);
         case kKvFP8: {
             const cudaError_t e = launch_fp8_page_scale(p, st);
             if (e != cudaSuccess) return e;
-            kv_append_kernel<uint8_t><<<p.n, 512, 0, st>>>(p);
-            break;
+            return launch_pdl(kv_append_kernel<uint8_t>, dim3(p.n), dim3(512), 0, st, p);
         }
         default: return cudaErrorInvalidValue;
     }

@@ -165,6 +165,8 @@ __device__ __forceinline__ bool flag_wait(volatile int *flag, int want, volatile
 
 template <typename TC, typename TOut>
 __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendParams p) {
+    pdl_trigger();
+    pdl_wait();   // everything below reads or writes memory of earlier kernels
     constexpr int CH = AttnTraits<TC>::CH;
     constexpr int NS = AttnTraits<TC>::NS;
     constexpr int kHalves = AttnTraits<TC>::HALVES;
@@ -696,8 +698,7 @@ template <typename TC, typename TOut> cudaError_t prepare_t() {
 }
 
 template <typename TC, typename TOut> cudaError_t launch_t(const AttendParams &p, int grid, cudaStream_t st) {
-    decode_attn_kernel<TC, TOut><<<grid, threads<TC>(), smem_bytes<TC>(), st>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(decode_attn_kernel<TC, TOut>, dim3(grid), dim3(threads<TC>()), smem_bytes<TC>(), st, p);
 }
 
 }  // namespace

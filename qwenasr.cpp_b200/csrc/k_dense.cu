@@ -17,6 +17,8 @@ template <> __device__ __forceinline__ void put<__nv_bfloat16>(__nv_bfloat16 *p,
 template <typename TOut>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const int *rows, int hidden, const float *w,
                                                       float eps, TOut *out) {
+    pdl_trigger();
+    pdl_wait();   // everything below reads or writes memory of earlier kernels
     const int r = blockIdx.x;
     const float *xr = x + static_cast<size_t>(rows ? rows[r] : r) * hidden;
     double ss = 0.0;
@@ -41,6 +43,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const int 
 
 template <typename TW>
 __global__ void embed_kernel(const int *ids, const TW *embd, int hidden, int vocab, float *x, DevError *err) {
+    pdl_trigger();
+    pdl_wait();   // everything below reads or writes memory of earlier kernels
     const int r = blockIdx.x;
     const int id = ids[r];
     if (id < 0 || id >= vocab) {
@@ -69,6 +73,8 @@ constexpr int BM = 64, BN = 64, BK = 16, PAD = 4;
 template <typename TX, typename TW>
 __global__ void __launch_bounds__(256) gemm_simt_kernel(const TX *X, const TW *W, float *C, int M, int N, int K,
                                                         int k_per_split, int atomic_out) {
+    pdl_trigger();
+    pdl_wait();   // everything below reads or writes memory of earlier kernels
     __shared__ __align__(16) float As[BK][BM + PAD];
     __shared__ __align__(16) float Bs[BK][BN + PAD];
     const int tid = threadIdx.x;
@@ -127,6 +133,8 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const TX *X, const TW *W
 template <typename TX, typename TW, int MM>
 __global__ void __launch_bounds__(256) gemv_kernel(const TX *X, const TW *W, float *C, int M, int N, int K,
                                                    int accumulate) {
+    pdl_trigger();
+    pdl_wait();   // everything below reads or writes memory of earlier kernels
     extern __shared__ __align__(16) float xs[];   // [MM][K]
     for (int e = threadIdx.x * 4; e < M * K; e += blockDim.x * 4) {
         const float4 v = ld4<TX>(X + e);
@@ -169,6 +177,8 @@ __global__ void __launch_bounds__(256) gemv_kernel(const TX *X, const TW *W, flo
 
 template <typename TOut>
 __global__ void swiglu_kernel(const float *gu, int M, int F, TOut *out) {
+    pdl_trigger();
+    pdl_wait();   // everything below reads or writes memory of earlier kernels
     const size_t total = static_cast<size_t>(M) * F;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -182,6 +192,8 @@ __global__ void swiglu_kernel(const float *gu, int M, int F, TOut *out) {
 
 // Block per row; ties keep the smaller index (strict '>' scan from 0); NaN never wins.
 __global__ void __launch_bounds__(1024) argmax_kernel(const float *logits, int V, int *ids) {
+    pdl_trigger();
+    pdl_wait();   // everything below reads or writes memory of earlier kernels
     const float *row = logits + static_cast<size_t>(blockIdx.x) * V;
     float best = -INFINITY;
     int idx = -1;
@@ -242,25 +254,27 @@ cudaError_t launch_convert(const void *src, int src_ggml_type, void *dst, int ds
 cudaError_t launch_rmsnorm(const float *x, const int *rows, int n, int hidden, const float *w, float eps, void *out,
                            int out_dtype, cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
-    if (out_dtype == kActF32) rmsnorm_kernel<float><<<n, 256, 0, st>>>(x, rows, hidden, w, eps, static_cast<float *>(out));
-    else rmsnorm_kernel<__nv_bfloat16><<<n, 256, 0, st>>>(x, rows, hidden, w, eps, static_cast<__nv_bfloat16 *>(out));
-    return cudaGetLastError();
+    if (out_dtype == kActF32)
+        return launch_pdl(rmsnorm_kernel<float>, dim3(n), dim3(256), 0, st, x, rows, hidden, w, eps, static_cast<float *>(out));
+    return launch_pdl(rmsnorm_kernel<__nv_bfloat16>, dim3(n), dim3(256), 0, st, x, rows, hidden, w, eps,
+                      static_cast<__nv_bfloat16 *>(out));
 }
 
 cudaError_t launch_embed(const int *ids, int n, const void *embd, int w_dtype, int hidden, int vocab, float *x,
                          DevError *err, cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
-    if (w_dtype == kActF32) embed_kernel<float><<<n, 256, 0, st>>>(ids, static_cast<const float *>(embd), hidden, vocab, x, err);
-    else embed_kernel<__nv_bfloat16><<<n, 256, 0, st>>>(ids, static_cast<const __nv_bfloat16 *>(embd), hidden, vocab, x, err);
-    return cudaGetLastError();
+    if (w_dtype == kActF32)
+        return launch_pdl(embed_kernel<float>, dim3(n), dim3(256), 0, st, ids, static_cast<const float *>(embd), hidden, vocab,
+                          x, err);
+    return launch_pdl(embed_kernel<__nv_bfloat16>, dim3(n), dim3(256), 0, st, ids,
+                      static_cast<const __nv_bfloat16 *>(embd), hidden, vocab, x, err);
 }
 
 template <typename TX, typename TW>
 static cudaError_t gemm_t(const TX *X, const TW *W, float *C, int M, int N, int K, int epilogue, cudaStream_t st) {
     if (M <= 4) {
         const size_t sm = static_cast<size_t>(M) * K * sizeof(float);   // opted in by prepare_dense
-        gemv_kernel<TX, TW, 4><<<(N + 7) / 8, 256, sm, st>>>(X, W, C, M, N, K, epilogue);
-        return cudaGetLastError();
+        return launch_pdl(gemv_kernel<TX, TW, 4>, dim3((N + 7) / 8), dim3(256), sm, st, X, W, C, M, N, K, epilogue);
     }
     const int tm = (M + BM - 1) / BM, tn = (N + BN - 1) / BN;
     int splits = 1;
@@ -279,8 +293,7 @@ static cudaError_t gemm_t(const TX *X, const TW *W, float *C, int M, int N, int 
         if (e != cudaSuccess) return e;
     }
     dim3 grid(tn, tm, splits);
-    gemm_simt_kernel<TX, TW><<<grid, 256, 0, st>>>(X, W, C, M, N, K, kps, atomic ? 1 : 0);
-    return cudaGetLastError();
+    return launch_pdl(gemm_simt_kernel<TX, TW>, grid, dim3(256), 0, st, X, W, C, M, N, K, kps, atomic ? 1 : 0);
 }
 
 cudaError_t prepare_dense(int max_k) {
@@ -318,15 +331,15 @@ cudaError_t launch_swiglu(const float *gu, int M, int F, void *out, int out_dtyp
     if (M <= 0) return cudaSuccess;
     const size_t total = static_cast<size_t>(M) * F;
     const int blocks = static_cast<int>((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
-    if (out_dtype == kActF32) swiglu_kernel<float><<<blocks, 256, 0, st>>>(gu, M, F, static_cast<float *>(out));
-    else swiglu_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(gu, M, F, static_cast<__nv_bfloat16 *>(out));
-    return cudaGetLastError();
+    if (out_dtype == kActF32)
+        return launch_pdl(swiglu_kernel<float>, dim3(blocks), dim3(256), 0, st, gu, M, F, static_cast<float *>(out));
+    return launch_pdl(swiglu_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, st, gu, M, F,
+                      static_cast<__nv_bfloat16 *>(out));
 }
 
 cudaError_t launch_argmax(const float *logits, int M, int V, int *ids, cudaStream_t st) {
     if (M <= 0) return cudaSuccess;
-    argmax_kernel<<<M, 1024, 0, st>>>(logits, V, ids);
-    return cudaGetLastError();
+    return launch_pdl(argmax_kernel, dim3(M), dim3(1024), 0, st, logits, V, ids);
 }
 
 }  // namespace qkv

@@ -16,11 +16,13 @@
 // store (or read-add-write for accumulate), which keeps them deterministic.
 // The host picks BN and the split count with a small cost model.
 //
-// CTA = 7 warps: warp 0 TMA producer of the weight tiles, warp 6 TMA producer
+// CTA = 8 warps: warp 0 TMA producer of the weight tiles, warp 6 TMA producer
 // of the token tiles (a warp issues TMA copies at a bounded rate, so two
-// issuing warps double the ingest of one CTA), warp 1 TMEM allocator + MMA
-// issuer (one thread), warps 2..5 epilogue (TMEM lane quadrant = warp % 4,
-// one weight row per thread).  Every mbarrier wait is bounded.
+// issuing warps double the ingest of one CTA), warp 7 prefetches weight tiles
+// into L2 a bounded distance ahead of warp 0 (so its loads are L2 hits and the
+// ring's refill latency shrinks), warp 1 TMEM allocator + MMA issuer (one
+// thread), warps 2..5 epilogue (TMEM lane quadrant = warp % 4, one weight row
+// per thread).  Every wait is bounded.
 #include "kernels.h"
 
 #include <cuda.h>
@@ -37,8 +39,9 @@ namespace {
 constexpr int kBK = 64;                           // K per stage: one 128-byte swizzle atom of bf16
 constexpr int kBM = 128;                          // weight rows per tile (MMA M)
 constexpr uint32_t kABytes = kBM * kBK * 2;       // 16 KB
-constexpr int kGemmThreads = 224;
+constexpr int kGemmThreads = 256;
 constexpr int kProducerB = 6;                     // warp that loads the token tiles
+constexpr int kPrefetchW = 7;                     // warp that prefetches weight tiles into L2
 
 template <int BN> struct TcTraits {
     static constexpr uint32_t kBBytes = BN * kBK * 2;
@@ -139,10 +142,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t *mma_done = acc_empty + 2;      // MMA thread's own drain
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
     volatile int *failed = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    volatile int *w_issued = failed + 1;     // weight tiles warp 0 has issued (prefetch distance)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ktiles = p.K / kBK;
     const int units = p.tiles_n * p.tiles_m * p.splits;
+    // The next kernel may start its own set-up now.  Weight tiles depend on no
+    // earlier kernel, so their producer starts before pdl_wait; the token-tile
+    // producer and the epilogue wait for the previous kernel first.
+    pdl_trigger();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < T::NS; ++s) {
@@ -155,6 +163,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         mbar_init(mma_done, 1);
         *failed = 0;
+        *w_issued = 0;
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -184,6 +193,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (warp == 0 || warp == kProducerB) {
         if (lane == 0) {
             const bool is_w = warp == 0;
+            if (!is_w) pdl_wait();
             const uint64_t pol = is_w ? l2_evict_first_policy() : l2_evict_last_policy();
             const CUtensorMap *map = is_w ? &tmW : &tmX;
             const uint32_t bytes = is_w ? kABytes : T::kBBytes;
@@ -206,6 +216,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     mbar_arrive_expect_tx(&full[s], bytes);
                     tma_load_2d(dst, map, (kt0 + i) * kBK, is_w ? n0 : m0, &full[s], pol);
                     ++it;
+                    if (is_w) *w_issued = it;
                 }
             }
             // Drain: every tile this thread asked for has landed before the CTA can exit.
@@ -213,6 +224,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if (!bounded_wait(&full[i % T::NS], static_cast<uint32_t>(i / T::NS) & 1u)) {
                     report_error(p.err, kErrWaitTimeout, kWhereGemm, blockIdx.x, -(1 << 21));
                     break;
+                }
+            }
+        }
+    } else if (warp == kPrefetchW) {
+        if (lane == 0) {
+            // Weight tiles into L2, at most kAhead tiles ahead of the weight producer.
+            constexpr int kAhead = 2 * T::NS;
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
+            int pit = 0;
+            bool stop = false;
+            for (int u = blockIdx.x; u < units && !stop; u += gridDim.x) {
+                int n0, m0, kt0, nk;
+                unit_coords(u, n0, m0, kt0, nk);
+                for (int i = 0; i < nk; ++i, ++pit) {
+                    if (pit >= kAhead) {
+                        const long long t0 = clock64();
+                        while (pit - *w_issued >= kAhead) {
+                            if (*failed || clock64() - t0 > kWaitLimitCycles) {
+                                stop = true;
+                                break;
+                            }
+                        }
+                        if (stop) break;
+                    }
+                    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                                     reinterpret_cast<uint64_t>(&tmW)),
+                                 "r"((kt0 + i) * kBK), "r"(n0)
+                                 : "memory");
                 }
             }
         }
@@ -266,6 +305,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         __syncwarp();
     } else {
         // epilogue: warps 2..5, TMEM lanes 32*(warp%4) .. +31 = weight rows of the unit
+        pdl_wait();
         const int q = warp & 3;
         int j = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
@@ -404,8 +444,7 @@ cudaError_t launch_bn(const void *X, const void *W, float *C, int M, int N, int 
     TcParams p{M, N, K, kps, tiles_n, tiles_m, splits, C, accumulate, err};
     const int units = tiles_n * tiles_m * splits;
     const int grid = units < num_sms ? units : num_sms;
-    gemm_tc_kernel<BN><<<grid, kGemmThreads, TcTraits<BN>::kSmem, st>>>(tw, tx, p);
-    return cudaGetLastError();
+    return launch_pdl(gemm_tc_kernel<BN>, dim3(grid), dim3(kGemmThreads), TcTraits<BN>::kSmem, st, tw, tx, p);
 }
 
 // Cost model for the tile width BN and the K split.  One thread issues a

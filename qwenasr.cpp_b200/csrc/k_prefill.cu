@@ -59,6 +59,8 @@ template <> __device__ __forceinline__ void store_o4<__nv_bfloat16>(__nv_bfloat1
 
 template <typename TC, typename TOut>
 __global__ void __launch_bounds__(256) prefill_attn_kernel(PrefillAttnParams p) {
+    pdl_trigger();
+    pdl_wait();   // everything below reads or writes memory of earlier kernels
     __shared__ __align__(16) float qs[kHkv][2][kHeadDim];
     const int row = blockIdx.x;
     const int g = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -154,16 +156,16 @@ cudaError_t launch_prefill_attn(const PrefillAttnParams &p, int kv_dtype, bool o
     if (p.n <= 0) return cudaSuccess;
     switch (kv_dtype) {
         case kKvF32:
-            if (out_bf16) prefill_attn_kernel<float, __nv_bfloat16><<<p.n, 256, 0, st>>>(p);
-            else prefill_attn_kernel<float, float><<<p.n, 256, 0, st>>>(p);
+            if (out_bf16) return launch_pdl(prefill_attn_kernel<float, __nv_bfloat16>, dim3(p.n), dim3(256), 0, st, p);
+            else return launch_pdl(prefill_attn_kernel<float, float>, dim3(p.n), dim3(256), 0, st, p);
             break;
         case kKvBF16:
-            if (out_bf16) prefill_attn_kernel<__nv_bfloat16, __nv_bfloat16><<<p.n, 256, 0, st>>>(p);
-            else prefill_attn_kernel<__nv_bfloat16, float><<<p.n, 256, 0, st>>>(p);
+            if (out_bf16) return launch_pdl(prefill_attn_kernel<__nv_bfloat16, __nv_bfloat16>, dim3(p.n), dim3(256), 0, st, p);
+            else return launch_pdl(prefill_attn_kernel<__nv_bfloat16, float>, dim3(p.n), dim3(256), 0, st, p);
             break;
         case kKvFP8:
-            if (out_bf16) prefill_attn_kernel<uint8_t, __nv_bfloat16><<<p.n, 256, 0, st>>>(p);
-            else prefill_attn_kernel<uint8_t, float><<<p.n, 256, 0, st>>>(p);
+            if (out_bf16) return launch_pdl(prefill_attn_kernel<uint8_t, __nv_bfloat16>, dim3(p.n), dim3(256), 0, st, p);
+            else return launch_pdl(prefill_attn_kernel<uint8_t, float>, dim3(p.n), dim3(256), 0, st, p);
             break;
         default: return cudaErrorInvalidValue;
     }

@@ -303,6 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
     volatile int *failed = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_trigger();
 
     if (threadIdx.x == 0) {
         mbar_init(&bars->q_full, 128);
@@ -334,6 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
     __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();   // items, q rows and the pages come from earlier kernels and copies
 
     if (warp < 4) {
         // ================= loaders: Q rows, then K/V tiles chunk-wise =================
@@ -708,9 +710,9 @@ cudaError_t launch_prefill_attn_tc(const PrefillAttnParams &pp, int kv_dtype, co
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
     const int grid = n_items < sms ? n_items : sms;   // persistent: one CTA per SM walks the items
-    if (kv_dtype == kKvBF16) prefill_attn_tc_kernel<__nv_bfloat16><<<grid, kThreads, kSmem, st>>>(p, n_items);
-    else prefill_attn_tc_kernel<uint8_t><<<grid, kThreads, kSmem, st>>>(p, n_items);
-    return cudaGetLastError();
+    if (kv_dtype == kKvBF16)
+        return launch_pdl(prefill_attn_tc_kernel<__nv_bfloat16>, dim3(grid), dim3(kThreads), kSmem, st, p, n_items);
+    return launch_pdl(prefill_attn_tc_kernel<uint8_t>, dim3(grid), dim3(kThreads), kSmem, st, p, n_items);
 }
 
 }  // namespace qkv

@@ -174,6 +174,15 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     return pol;
 }
 
+// Programmatic dependent launch.  A kernel launched with it may start while the
+// previous kernel of the stream is still running: pdl_trigger lets the next
+// kernel start early, and pdl_wait blocks until the previous kernel has
+// completed and its memory is visible (it returns at once for a normal launch).
+// Every kernel below calls pdl_wait before its first access to memory that an
+// earlier kernel of the stream wrote or reads.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Cycle budget for any single wait before it is treated as a hang (~2 s at 1.9 GHz).
 constexpr long long kWaitLimitCycles = 4000000000ll;
 

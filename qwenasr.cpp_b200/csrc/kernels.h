@@ -3,10 +3,41 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <cstdlib>
+#include <cstring>
+#include <utility>
 
 #include "kcommon.cuh"
 
 namespace qkv {
+
+// Programmatic dependent launch of the step kernels (on unless the
+// environment sets QWENASR_B200_PDL=0, read once per process).
+inline bool pdl_enabled() {
+    static const bool on = [] {
+        const char *v = std::getenv("QWENASR_B200_PDL");
+        return !(v && std::strcmp(v, "0") == 0);
+    }();
+    return on;
+}
+
+// Launch `kernel` allowing it to start while the stream's previous kernel
+// finishes (the kernel must pdl_wait before touching that kernel's memory).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args &&...args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 enum KvDtype { kKvF32 = 0, kKvBF16 = 1, kKvFP8 = 2 };
 enum ActDtype { kActF32 = 0, kActBF16 = 1 };
