@@ -182,9 +182,12 @@ __global__ void swiglu_kernel(const float *gu, int M, int F, TOut *out) {
     const size_t total = static_cast<size_t>(M) * F;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        // gu rows hold gate and up interleaved in blocks of 64 features:
+        // [gate 64t..64t+63 | up 64t..64t+63] for t = 0 .. F/64 - 1.
         const size_t m = i / F, jf = i % F;
-        const float g = gu[m * 2 * F + jf];
-        const float u = gu[m * 2 * F + F + jf];
+        const size_t col = (jf >> 6) * 128 + (jf & 63);
+        const float g = gu[m * 2 * F + col];
+        const float u = gu[m * 2 * F + col + 64];
         const float s = g / (1.0f + expf(-g));
         put<TOut>(out + i, s * u);
     }

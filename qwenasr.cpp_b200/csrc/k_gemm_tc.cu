@@ -48,7 +48,8 @@ template <int BN> struct TcTraits {
     static constexpr int NS = BN <= 32 ? 8 : BN <= 64 ? 8 : BN <= 128 ? 6 : 4;
     static constexpr uint32_t kStage = kABytes + kBBytes;
     static constexpr int kCols = 2 * BN;             // two accumulators (power of two, 64..512 columns)
-    static constexpr size_t kSmem = 1024 /*align slack*/ + static_cast<size_t>(NS) * kStage + 256;
+    static constexpr size_t kXchBytes = 32 * 64 * sizeof(float);   // fused SwiGLU hand-over [32 tokens][64 rows]
+    static constexpr size_t kSmem = 1024 /*align slack*/ + static_cast<size_t>(NS) * kStage + kXchBytes + 256;
 };
 
 struct TcParams {
@@ -57,6 +58,10 @@ struct TcParams {
     int tiles_n, tiles_m, splits;   // units = tiles_n * tiles_m * splits, token tile fastest
     float *C;
     int accumulate;   // 0: store (one split) / red.add into a zeroed C; 1: add into C
+    // Fused SwiGLU (act != nullptr, one split): W holds gate and up rows
+    // interleaved in 64-row blocks, so weight tile t = [gate f 64t..64t+63 |
+    // up f 64t..64t+63]; act[M][N/2] (bf16) = silu(gate) * up, C is unused.
+    __nv_bfloat16 *act;
     DevError *err;
 };
 
@@ -135,12 +140,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // 1024-byte alignment for the swizzled tiles.
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *tiles = smem;
-    uint64_t *full = reinterpret_cast<uint64_t *>(tiles + static_cast<size_t>(T::NS) * T::kStage);
+    float *xch = reinterpret_cast<float *>(tiles + static_cast<size_t>(T::NS) * T::kStage);   // [32][64]
+    uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(xch) + T::kXchBytes);
     uint64_t *empty = full + T::NS;
     uint64_t *acc_full = empty + T::NS;      // [2] MMA -> epilogue
     uint64_t *acc_empty = acc_full + 2;      // [2] epilogue -> MMA
     uint64_t *mma_done = acc_empty + 2;      // MMA thread's own drain
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
+    uint64_t *xfull = mma_done + 1;          // fused SwiGLU: both halves written to xch
+    uint64_t *xempty = xfull + 1;            // fused SwiGLU: xch read by both sides
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(xempty + 1);
     volatile int *failed = reinterpret_cast<volatile int *>(tmem_slot + 1);
     volatile int *w_issued = failed + 1;     // weight tiles warp 0 has issued (prefetch distance)
 
@@ -162,6 +170,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_init(&acc_empty[b], 4);
         }
         mbar_init(mma_done, 1);
+        mbar_init(xfull, 128);
+        mbar_init(xempty, 128);
         *failed = 0;
         *w_issued = 0;
         fence_mbar_init();
@@ -308,6 +318,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         pdl_wait();
         const int q = warp & 3;
         int j = 0;
+        uint32_t xc = 0;       // fused SwiGLU chunks exchanged (xfull / xempty phase)
         for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
             int n0, m0, kt0, nk;
             unit_coords(u, n0, m0, kt0, nk);
@@ -324,6 +335,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             const int n = n0 + 32 * q + lane;
             const bool split = p.splits > 1;
+            const bool fused = p.act != nullptr;
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
                 uint32_t r[32];
@@ -334,6 +346,57 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&acc_empty[b]);
+                }
+                if (fused) {
+                    // Rows 0..63 (warps q = 0, 1) are gate features, rows 64..127 (q = 2, 3)
+                    // the matching up features.  Each side hands the other the half of the
+                    // chunk's 32 tokens that the other finishes: gate warps finish tokens
+                    // 0..15, up warps tokens 16..31 (xch rows 0..15 carry up values, rows
+                    // 16..31 gate values).
+                    const uint32_t ph = static_cast<uint32_t>(xc) & 1u;
+                    const int rr = 32 * (q & 1) + lane;            // feature within the tile's 64
+                    const bool gate = q < 2;
+                    // Warp-uniform decisions: the next tcgen05.ld is .sync.aligned.
+                    if (!__all_sync(0xffffffffu, !*failed && bounded_wait(xempty, ph ^ 1u))) {
+                        if (lane == 0) report_error(p.err, kErrWaitTimeout, kWhereGemm, blockIdx.x, -(1 << 24));
+                        *failed = 1;
+                        break;
+                    }
+                    // gate warps pass tokens 16..31, up warps pass tokens 0..15 (register
+                    // indices stay compile-time in both branches)
+                    if (gate) {
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj) xch[(16 + jj) * 64 + rr] = __uint_as_float(r[16 + jj]);
+                    } else {
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj) xch[jj * 64 + rr] = __uint_as_float(r[jj]);
+                    }
+                    mbar_arrive(xfull);
+                    if (!__all_sync(0xffffffffu, !*failed && bounded_wait(xfull, ph))) {
+                        if (lane == 0) report_error(p.err, kErrWaitTimeout, kWhereGemm, blockIdx.x, -(1 << 25));
+                        *failed = 1;
+                        break;
+                    }
+                    const int F = p.N >> 1;
+                    const int f = (n0 >> 1) + rr;
+                    const int mlim = p.M - (m0 + c);
+                    auto finish = [&](int t, float g, float u) {
+                        if (t < mlim && f < F) {
+                            const float sl = g * __frcp_rn(1.0f + __expf(-g));
+                            p.act[static_cast<size_t>(m0 + c + t) * F + f] = __float2bfloat16_rn(sl * u);
+                        }
+                    };
+                    if (gate) {
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj) finish(jj, __uint_as_float(r[jj]), xch[jj * 64 + rr]);
+                    } else {
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj)
+                            finish(16 + jj, xch[(16 + jj) * 64 + rr], __uint_as_float(r[16 + jj]));
+                    }
+                    mbar_arrive(xempty);
+                    ++xc;
+                    continue;
                 }
                 if (n < p.N) {
                     float *dst = p.C + static_cast<size_t>(m0 + c) * p.N + n;
@@ -430,18 +493,19 @@ template <int BN> cudaError_t prepare_bn() {
 
 template <int BN>
 cudaError_t launch_bn(const void *X, const void *W, float *C, int M, int N, int K, int accumulate, int splits,
-                      int num_sms, DevError *err, cudaStream_t st) {
+                      int num_sms, DevError *err, cudaStream_t st, __nv_bfloat16 *act = nullptr) {
     CUtensorMap tw, tx;
     if (!cached_map(&tw, W, N, K, kBM) || !cached_map(&tx, X, M, K, BN)) return cudaErrorInvalidValue;
     const int tiles_n = (N + kBM - 1) / kBM, tiles_m = (M + BN - 1) / BN;
     const int ktiles = K / kBK;
     const int kps = (ktiles + splits - 1) / splits;
     splits = (ktiles + kps - 1) / kps;     // every split owns >= 1 k-tile
+    if (act && splits != 1) return cudaErrorInvalidValue;
     if (splits > 1 && !accumulate) {
         cudaError_t e = cudaMemsetAsync(C, 0, static_cast<size_t>(M) * N * sizeof(float), st);
         if (e != cudaSuccess) return e;
     }
-    TcParams p{M, N, K, kps, tiles_n, tiles_m, splits, C, accumulate, err};
+    TcParams p{M, N, K, kps, tiles_n, tiles_m, splits, C, accumulate, act, err};
     const int units = tiles_n * tiles_m * splits;
     const int grid = units < num_sms ? units : num_sms;
     return launch_pdl(gemm_tc_kernel<BN>, dim3(grid), dim3(kGemmThreads), TcTraits<BN>::kSmem, st, tw, tx, p);
@@ -466,7 +530,7 @@ template <int BN> constexpr double ktile_seconds() {
     return t_mma > t_ld ? (t_mma > t_lat ? t_mma : t_lat) : (t_ld > t_lat ? t_ld : t_lat);
 }
 
-GemmPlan plan_gemm(int M, int N, int K, int num_sms) {
+GemmPlan plan_gemm(int M, int N, int K, int num_sms, bool no_split = false) {
     const double kHbm = 6.2e12;                     // whole-chip weight streaming
     const double kFixed = 1.5e-6;                   // per-unit fill + epilogue tail
     const double kRed = 250e9;                      // f32 red.add per second, whole chip
@@ -481,7 +545,7 @@ GemmPlan plan_gemm(int M, int N, int K, int num_sms) {
         if (bn > 32 && (bn / 2) >= M) break;          // a narrower tile already covers all tokens
         const int tiles_m = (M + bn - 1) / bn;
         const int tiles = tiles_n * tiles_m;
-        const int max_split = ktiles < 32 ? ktiles : 32;
+        const int max_split = no_split ? 1 : (ktiles < 32 ? ktiles : 32);
         for (int sp = 1; sp <= max_split; ++sp) {
             const int kps = (ktiles + sp - 1) / sp;
             const int spr = (ktiles + kps - 1) / kps;
@@ -536,6 +600,29 @@ cudaError_t launch_gemm_tc(const void *X, const void *W, float *C, int M, int N,
         case 64: return launch_bn<64>(X, W, C, M, N, K, accumulate, pl.splits, num_sms, err, st);
         case 128: return launch_bn<128>(X, W, C, M, N, K, accumulate, pl.splits, num_sms, err, st);
         default: return launch_bn<256>(X, W, C, M, N, K, accumulate, pl.splits, num_sms, err, st);
+    }
+}
+
+bool gemm_tc_swiglu_pays(int M, int N2, int K, int num_sms) {
+    // The SwiGLU epilogue is hidden behind the next unit's MMAs only when every
+    // CTA takes at least two work units.
+    if (K % kBK != 0 || N2 % kBM != 0) return false;
+    const GemmPlan pl = plan_gemm(M, N2, K, num_sms, true);
+    const long units = static_cast<long>(N2 / kBM) * ((M + pl.bn - 1) / pl.bn);
+    return units >= 2L * num_sms;
+}
+
+cudaError_t launch_gemm_tc_swiglu(const void *X, const void *W, void *act, int M, int N2, int K, int num_sms,
+                                  DevError *err, cudaStream_t st) {
+    if (M <= 0 || N2 <= 0) return cudaSuccess;
+    if (K % kBK != 0 || N2 % kBM != 0) return cudaErrorInvalidValue;
+    GemmPlan pl = plan_gemm(M, N2, K, num_sms, true);
+    __nv_bfloat16 *a = static_cast<__nv_bfloat16 *>(act);
+    switch (pl.bn) {
+        case 32: return launch_bn<32>(X, W, nullptr, M, N2, K, 0, 1, num_sms, err, st, a);
+        case 64: return launch_bn<64>(X, W, nullptr, M, N2, K, 0, 1, num_sms, err, st, a);
+        case 128: return launch_bn<128>(X, W, nullptr, M, N2, K, 0, 1, num_sms, err, st, a);
+        default: return launch_bn<256>(X, W, nullptr, M, N2, K, 0, 1, num_sms, err, st, a);
     }
 }
 

@@ -136,6 +136,11 @@ cudaError_t launch_gemm(const void *X, int x_dtype, const void *W, int w_dtype, 
 // red.add when the tile grid is smaller than the SM count.
 cudaError_t prepare_gemm_tc();
 bool gemm_tc_supported(int M, int N, int K);
+// act[M][N2/2] (bf16) = silu(gate) * up of X . W^T, W = gate/up rows
+// interleaved in 64-row blocks (N2 % 128 == 0); one K split.
+cudaError_t launch_gemm_tc_swiglu(const void *X, const void *W, void *act, int M, int N2, int K, int num_sms,
+                                  DevError *err, cudaStream_t st);
+bool gemm_tc_swiglu_pays(int M, int N2, int K, int num_sms);
 cudaError_t launch_gemm_tc(const void *X, const void *W, float *C, int M, int N, int K, int accumulate, int num_sms,
                            DevError *err, cudaStream_t st);
 // Shared-memory opt-in of the dense kernels for rows up to max_k wide.

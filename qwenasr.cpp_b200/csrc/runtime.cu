@@ -57,8 +57,8 @@ int validate_model(const qkv_model_config &c, std::string *e) {
              std::to_string(c.head_dim) + "/" + std::to_string(c.n_heads) + "/" + std::to_string(c.n_kv_heads) + ")";
         return QKV_ERR_INVALID_ARG;
     }
-    if (c.hidden % 16 != 0 || c.intermediate % 16 != 0) {
-        *e = "model config: hidden and intermediate must be multiples of 16";
+    if (c.hidden % 16 != 0 || c.intermediate % 64 != 0) {
+        *e = "model config: hidden must be a multiple of 16 and intermediate a multiple of 64";
         return QKV_ERR_INVALID_ARG;
     }
     if (!(c.rope_theta > 0.0f) || !(c.rms_norm_eps >= 0.0f)) {
@@ -176,6 +176,8 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
     {
         const char *pa = getenv("QWENASR_B200_PREFILL_ATTN");
         h->prefill_tc = !(pa && std::strcmp(pa, "cuda_core") == 0);
+        const char *fs = getenv("QWENASR_B200_FUSED_SWIGLU");
+        h->fused_swiglu = !(fs && std::strcmp(fs, "0") == 0);
     }
     CK(prepare_dense(std::max(c.hidden, std::max(c.intermediate, kQDim))));
     (void)gemm_tc_supported(1, 1, 64);   // resolve the tensor-map encoder before any capture
@@ -252,6 +254,11 @@ int load_weights(qkv_handle *h, const GgufFile &f) {
     const int64_t H = c.hidden, QD = kQDim, KD = kKvDim, F = c.intermediate, V = c.vocab, D = kHeadDim;
     const size_t we = h->w_elem;
     Uploader up{h};
+    struct DevBuf {
+        void *p = nullptr;
+        ~DevBuf() { cudaFree(p); }
+    } gu_buf;                                   // gate | up as read, before interleaving
+    void *&gu_tmp = gu_buf.p;
     h->layers.resize(static_cast<size_t>(c.n_layers));
     int rc;
     for (int l = 0; l < c.n_layers; ++l) {
@@ -277,16 +284,27 @@ int load_weights(qkv_handle *h, const GgufFile &f) {
         CK(cudaMalloc(&L.w_qkv, static_cast<size_t>(QD + 2 * KD) * H * we));
         CK(cudaMalloc(&L.w_o, static_cast<size_t>(H) * QD * we));
         CK(cudaMalloc(&L.w_gu, static_cast<size_t>(2 * F) * H * we));
+        if (!gu_tmp) CK(cudaMalloc(&gu_tmp, static_cast<size_t>(2 * F) * H * we));
         CK(cudaMalloc(&L.w_down, static_cast<size_t>(H) * F * we));
         if ((rc = up.put(an, L.attn_norm, kActF32, 0)) || (rc = up.put(fn, L.ffn_norm, kActF32, 0)) ||
             (rc = up.put(qn, L.q_norm, kActF32, 0)) || (rc = up.put(kn, L.k_norm, kActF32, 0)) ||
             (rc = up.put(wq, L.w_qkv, h->w_dtype, 0)) ||
             (rc = up.put(wk, L.w_qkv, h->w_dtype, static_cast<size_t>(QD) * H)) ||
             (rc = up.put(wv, L.w_qkv, h->w_dtype, static_cast<size_t>(QD + KD) * H)) ||
-            (rc = up.put(wo, L.w_o, h->w_dtype, 0)) || (rc = up.put(wg, L.w_gu, h->w_dtype, 0)) ||
-            (rc = up.put(wu, L.w_gu, h->w_dtype, static_cast<size_t>(F) * H)) ||
+            (rc = up.put(wo, L.w_o, h->w_dtype, 0)) || (rc = up.put(wg, gu_tmp, h->w_dtype, 0)) ||
+            (rc = up.put(wu, gu_tmp, h->w_dtype, static_cast<size_t>(F) * H)) ||
             (rc = up.put(wd, L.w_down, h->w_dtype, 0)))
             return rc;
+        // gate | up -> 64-row blocks interleaved: rows [128t, 128t+64) = gate features
+        // 64t.., rows [128t+64, 128t+128) = the matching up features (the layout the
+        // fused SwiGLU epilogue of the projection GEMM and the SwiGLU kernel read).
+        const size_t blk = static_cast<size_t>(64) * H * we;
+        CK(cudaMemcpy2DAsync(L.w_gu, 2 * blk, gu_tmp, blk, blk, static_cast<size_t>(F / 64), cudaMemcpyDeviceToDevice,
+                             h->stream));
+        CK(cudaMemcpy2DAsync(static_cast<uint8_t *>(L.w_gu) + blk, 2 * blk,
+                             static_cast<const uint8_t *>(gu_tmp) + static_cast<size_t>(F) * H * we, blk, blk,
+                             static_cast<size_t>(F / 64), cudaMemcpyDeviceToDevice, h->stream));
+        CK(cudaStreamSynchronize(h->stream));
     }
     const GgufTensor *te, *on, *ow;
     if ((rc = find_tensor(h, f, "text.token_embd.weight", {H, V}, &te)) ||
@@ -576,10 +594,19 @@ int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int
         }
         CK(gemm(h, h->attn, L.w_o, h->x, n, c.hidden, kQDim, 1));
         CK(launch_rmsnorm(h->x, nullptr, n, c.hidden, L.ffn_norm, c.rms_norm_eps, h->xn, h->act_dtype, h->stream));
-        CK(gemm(h, h->xn, L.w_gu, h->gu, n, 2 * c.intermediate, c.hidden, 0));
-        CK(launch_swiglu(h->gu, n, c.intermediate, h->act, h->act_dtype, h->stream));
+        const bool fused = h->fused_swiglu && h->act_dtype == kActBF16 && h->w_dtype == kActBF16 &&
+                           gemm_tc_supported(n, 2 * c.intermediate, c.hidden) &&
+                           gemm_tc_swiglu_pays(n, 2 * c.intermediate, c.hidden, h->num_sms);
+        if (fused) {
+            // gate/up projection with SwiGLU in its epilogue: act (bf16) straight from TMEM
+            CK(launch_gemm_tc_swiglu(h->xn, L.w_gu, h->act, n, 2 * c.intermediate, c.hidden, h->num_sms, h->d_err,
+                                     h->stream));
+        } else {
+            CK(gemm(h, h->xn, L.w_gu, h->gu, n, 2 * c.intermediate, c.hidden, 0));
+            CK(launch_swiglu(h->gu, n, c.intermediate, h->act, h->act_dtype, h->stream));
+        }
         CK(gemm(h, h->act, L.w_down, h->x, n, c.hidden, c.intermediate, 1));
-        h->launches += 7;
+        h->launches += fused ? 6 : 7;
     }
     return QKV_OK;
 }

@@ -95,6 +95,9 @@ struct qkv_handle {
     // environment variable QWENASR_B200_PREFILL_ATTN=cuda_core selects the
     // CUDA-core kernel instead (a cross-check of the two device paths).
     bool prefill_tc = true;
+    // SwiGLU in the gate/up GEMM's epilogue where each CTA gets >= 2 work
+    // units (QWENASR_B200_FUSED_SWIGLU=0: the separate SwiGLU kernel).
+    bool fused_swiglu = true;
     int last_decode_n = -1;   // a graph is captured only for a batch size seen twice in a row
 };
 
