@@ -20,15 +20,17 @@
 // per-(kv, head) scale in f16), and Q, P are f16 too; for bf16 everything is
 // bf16.  K and V tiles are double-buffered, S is double-buffered in TMEM.
 //
-// Two passes over the key tiles: pass 1 computes each row's running max and
-// sum from S (TMEM -> registers); pass 2 recomputes S, writes the normalised
-// P (swizzled) to shared memory and accumulates O = P V in TMEM, so O never
-// needs rescaling.  In pass 2 the issuer puts S of tile t ahead of P V of
-// tile t-1, so the softmax of t overlaps the PV MMAs of t-1.
+// One pass over the key tiles with an online softmax: the issuer puts S of
+// tile t + 1 ahead of P V of tile t, so the softmax of a tile overlaps the
+// MMAs around it.  P is written unnormalised against a per-row reference max;
+// the reference moves (and O, l are rescaled in place in TMEM) only when a
+// tile's max exceeds it by more than 2^8, so P stays within [0, 256] and most
+// tiles need no correction; O is divided by the row sum in the epilogue.
 //
-// Roles: warps 0..3 loaders, warps 4..7 softmax/epilogue (thread = TMEM lane
-// = one query row; lane quadrant = warp % 4), warp 8 TMEM allocator + MMA
-// issuer (one thread).  All waits bounded.
+// Roles: warps 0..3 loaders, warps 4..11 softmax/epilogue in two warpgroups
+// that split each row's key columns (thread = TMEM lane = one query row; lane
+// quadrant = warp % 4), warp 12 TMEM allocator + MMA issuer (one thread).
+// All waits bounded.
 #include "kernels.h"
 
 namespace qkv {
@@ -42,8 +44,10 @@ constexpr uint32_t kTileBytes = 2 * kBlkBytes;            // two 64-column block
 constexpr int kSoftmaxWarp0 = 4;                          // warps 4..11: two softmax warpgroups
 constexpr int kMmaWarp = 12;
 constexpr int kThreads = 13 * 32;
-// Q, K[2], V[2], P tiles + (m, l) hand-over [2 item parities][2 halves][128 rows] + barriers
-constexpr size_t kMlBytes = 2 * 2 * 128 * sizeof(float2);
+// Q, K[2], V[2], P tiles + row-max hand-over [2 S buffers][2 halves][128 rows]
+// + row-sum hand-over [2 item parities][2 halves][128 rows] + barriers
+constexpr size_t kMlBytes = 2 * 2 * 2 * 128 * sizeof(float);
+constexpr float kRescaleLog2 = 8.0f;                       // P <= 2^8 between reference moves
 constexpr size_t kSmem = 1024 + 6 * static_cast<size_t>(kTileBytes) + kMlBytes + 512;
 constexpr uint32_t kTmemCols = 512;                       // S0 [0,128), S1 [128,256), O0 [256,384), O1 [384,512)
 constexpr uint32_t kTmemO = 256;
@@ -97,8 +101,9 @@ __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::aft
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
+// 32 consecutive TMEM columns of this thread's lane; the values are usable
+// after tmem_wait_ld().
+__device__ __forceinline__ void tmem_ld32_issue(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
         "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
@@ -107,9 +112,43 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    tmem_ld32_issue(taddr, r);
+    tmem_wait_ld();
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 32 consecutive TMEM columns of this thread's lane; ordered by tmem_wait_st().
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 2^x by the SFU's approximate instruction (PTX ex2.approx.ftz.f32): denormal
+// results flush to zero, 2^-inf = 0.  P is rounded to 16 bits right after, so
+// neither the approximation nor the flush is visible in it.
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 // Byte offset of 16-byte chunk c (0..7) of row r inside a 128B-swizzled block.
@@ -183,12 +222,11 @@ template <typename TC> struct TileRegs {
     static constexpr int kRows = 128 * kChunks / 128;          // rows per thread: 16 (bf16) or 8 (e4m3)
     static constexpr int kStride = 128 / kRows;                // row step between a thread's rows
     uint4 w[kRows];
-    float scale[sizeof(TC) == 1 ? kRows : 1];
     uint32_t live;                                             // bit m: row m of this thread is a live key
 };
 
 // e4m3 tile into registers: thread t reads 16-byte chunk t % 8 of rows
-// t / 8 + 16m (row r0 + 16m lies in page m), with each row's page scale.
+// t / 8 + 16m (row r0 + 16m lies in page m).
 template <typename TC>
 __device__ __forceinline__ bool fetch_tile(const K3Params &p, TileRegs<TC> &tr, const int (&pg)[8], int kv_len, int kt,
                                            int kv, int g, int t) {
@@ -207,7 +245,6 @@ __device__ __forceinline__ bool fetch_tile(const K3Params &p, TileRegs<TC> &tr, 
         const int page = valid ? pg[m] : 0;
         const size_t row = ((static_cast<size_t>(page) * 2 + kv) * kHkv + g) * kPageTokens + key % kPageTokens;
         tr.w[m] = __ldg(reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(p.pool) + row * kHeadDim) + c);
-        tr.scale[m] = __ldg(p.scales + (static_cast<size_t>(page) * 2 + kv) * kHkv + g);
     }
 #pragma unroll
     for (int m = 0; m < TR::kRows; ++m) {
@@ -217,9 +254,11 @@ __device__ __forceinline__ bool fetch_tile(const K3Params &p, TileRegs<TC> &tr, 
 }
 
 // Into a swizzled [2 blocks][128 rows][64] 16-bit tile (e4m3: dequantised
-// exactly to f16, then times the page scale in f16).
+// exactly to f16, then times the page's (kv, g) scale in f16, read here so it
+// does not occupy registers while the loader waits for the buffer).
 template <typename TC>
-__device__ __forceinline__ void store_tile(uint8_t *tile, const TileRegs<TC> &tr, int t) {
+__device__ __forceinline__ void store_tile(const K3Params &p, uint8_t *tile, const TileRegs<TC> &tr, const int (&pg)[8],
+                                           int kv, int g, int t) {
     using TR = TileRegs<TC>;
     const int c = t % TR::kChunks, r0 = t / TR::kChunks;
 #pragma unroll
@@ -229,7 +268,9 @@ __device__ __forceinline__ void store_tile(uint8_t *tile, const TileRegs<TC> &tr
             *reinterpret_cast<uint4 *>(tile + (c >> 3) * kBlkBytes + swz(r, c & 7)) = tr.w[m];
         } else {
             // 16 e4m3 = dims 16c .. 16c+15 -> f16 chunks 2c (dims 16c..+7) and 2c+1
-            const uint32_t s2 = pack_h2(tr.scale[m], tr.scale[m]);
+            const bool valid = pg[m] >= 0 && pg[m] < p.n_pages;
+            const float sc = __ldg(p.scales + (static_cast<size_t>(valid ? pg[m] : 0) * 2 + kv) * kHkv + g);
+            const uint32_t s2 = pack_h2(sc, sc);
             const uint32_t ws[4] = {tr.w[m].x, tr.w[m].y, tr.w[m].z, tr.w[m].w};
             uint32_t h[8];
 #pragma unroll
@@ -248,7 +289,7 @@ __device__ __forceinline__ void store_tile(uint8_t *tile, const TileRegs<TC> &tr
 
 struct Bars {
     uint64_t q_full, q_empty, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_free[2];
-    uint64_t p_full, p_free, o_full[2], o_empty[2], ml_ready[2], mma_done;
+    uint64_t p_full, p_free, o_full[2], o_empty[2], mx_ready[2], l_ready[2], mma_done;
 };
 
 // Bounded wait that also gives up as soon as another role set the abort flag.
@@ -285,10 +326,11 @@ __device__ __forceinline__ ItemInfo item_info(const K3Params &p, int it) {
 
 // Persistent: CTA c takes items c, c + G, c + 2G, ... (the host orders items
 // longest first).  Every barrier phase follows from per-role counters that
-// run on across items: item j uses Q and O buffers j & 1; K use and S use u
-// (global count) use K/S buffer u & 1; pass-2 tile v (global count) uses V
-// buffer v & 1 and the single P tile.
+// run on across items: item j uses the Q tile and O buffer j & 1; key tile u
+// (global count) uses K, V, S and row-max buffers u & 1 and the single P tile.
 template <typename TC>
+// 13 warps: the SM's four sub-partitions hold up to 4 of them each, which caps
+// a thread at 128 registers.
 __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p, int n_items) {
     constexpr bool kF16 = sizeof(TC) == 1;   // e4m3 cache -> f16 operands
     extern __shared__ uint8_t smem_raw[];
@@ -297,7 +339,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
     uint8_t *const sK0 = smem + kTileBytes;          // K[b] = sK0 + b * kTileBytes
     uint8_t *const sV0 = smem + 3 * kTileBytes;      // V[b]
     uint8_t *const sP = smem + 5 * kTileBytes;
-    float2 *const ml = reinterpret_cast<float2 *>(smem + 6 * kTileBytes);   // [parity][half][row]
+    float *const xm = reinterpret_cast<float *>(smem + 6 * kTileBytes);     // tile row max [S buffer][half][row]
+    float *const xl = xm + 2 * 2 * 128;                                      // row sums [item parity][half][row]
     Bars *bars = reinterpret_cast<Bars *>(smem + 6 * kTileBytes + kMlBytes);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 1);
     volatile int *failed = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -317,7 +360,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
             mbar_init(&bars->s_free[b], 256);
             mbar_init(&bars->o_full[b], 1);
             mbar_init(&bars->o_empty[b], 256);
-            mbar_init(&bars->ml_ready[b], 256);
+            mbar_init(&bars->mx_ready[b], 256);
+            mbar_init(&bars->l_ready[b], 256);
         }
         mbar_init(&bars->p_full, 256);
         mbar_init(&bars->p_free, 1);
@@ -340,7 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
     if (warp < 4) {
         // ================= loaders: Q rows, then K/V tiles chunk-wise =================
         const int r = threadIdx.x;
-        uint32_t ku = 0, vu = 0, j = 0;
+        uint32_t ku = 0, j = 0;
         for (int it = blockIdx.x; it < n_items && !*failed; it += gridDim.x, ++j) {
             const ItemInfo f = item_info(p, it);
             if (!f.ok) {
@@ -382,38 +426,32 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
                 fence_async_smem();
                 mbar_arrive(&bars->q_full);
             }
-            const int n_uses = 2 * f.n_kt;
             bool bad = false;
             int pg[8], pg_next[8];
             tile_pages(pt, f.key_pages, 0, pg);
-            for (int u = 0; u < n_uses; ++u) {
-                const int pass = u / f.n_kt, kt = u % f.n_kt;
-                const uint32_t kb = ku & 1;
-                // next use's page ids in flight while this tile's copies are issued
-                if (u + 1 < n_uses) tile_pages(pt, f.key_pages, (u + 1) % f.n_kt, pg_next);
+            for (int kt = 0; kt < f.n_kt; ++kt) {
+                const uint32_t kb = ku & 1, par = ((ku >> 1) & 1u) ^ 1u;
+                // next tile's page ids in flight while this tile's copies are issued
+                if (kt + 1 < f.n_kt) tile_pages(pt, f.key_pages, kt + 1, pg_next);
                 if constexpr (sizeof(TC) == 2) {
                     // bf16: asynchronous copies; the loader runs ahead as far as the buffers allow.
-                    if (!wait_bar(&bars->k_empty[kb], ((ku >> 1) & 1u) ^ 1u, failed)) {
-                        if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, f.row0, u);
+                    if (!wait_bar(&bars->k_empty[kb], par, failed)) {
+                        if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, f.row0, kt);
                         *failed = 1;
                         bad = true;
                         break;
                     }
                     bool ok = copy_tile_async(p, sK0 + kb * kTileBytes, pg, f.kv_len, kt, 0, f.g, r);
                     cp_async_arrive(&bars->k_full[kb]);
-                    ++ku;
-                    if (pass == 1) {
-                        const uint32_t vb = vu & 1;
-                        if (!wait_bar(&bars->v_empty[vb], ((vu >> 1) & 1u) ^ 1u, failed)) {
-                            if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, f.row0, -u);
-                            *failed = 1;
-                            bad = true;
-                            break;
-                        }
-                        ok = copy_tile_async(p, sV0 + vb * kTileBytes, pg, f.kv_len, kt, 1, f.g, r) && ok;
-                        cp_async_arrive(&bars->v_full[vb]);
-                        ++vu;
+                    if (!wait_bar(&bars->v_empty[kb], par, failed)) {
+                        if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, f.row0, -1 - kt);
+                        *failed = 1;
+                        bad = true;
+                        break;
                     }
+                    ok = copy_tile_async(p, sV0 + kb * kTileBytes, pg, f.kv_len, kt, 1, f.g, r) && ok;
+                    cp_async_arrive(&bars->v_full[kb]);
+                    ++ku;
                     if (!ok) {
                         report_error(p.err, kErrPageIndex, kWherePrefillAttn, f.row0, kt);
                         *failed = 1;
@@ -421,39 +459,35 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
                         break;
                     }
                 } else {
-                    // e4m3: K (and, in pass 2, V) loads in flight together, dequantised on the way in.
+                    // e4m3: K and V loads in flight together, dequantised on the way in.
                     TileRegs<TC> kr, vr;
                     bool ok = fetch_tile<TC>(p, kr, pg, f.kv_len, kt, 0, f.g, r);
-                    if (pass == 1) ok = fetch_tile<TC>(p, vr, pg, f.kv_len, kt, 1, f.g, r) && ok;
+                    ok = fetch_tile<TC>(p, vr, pg, f.kv_len, kt, 1, f.g, r) && ok;
                     if (!ok) {
                         report_error(p.err, kErrPageIndex, kWherePrefillAttn, f.row0, kt);
                         *failed = 1;
                         bad = true;
                         break;
                     }
-                    if (!wait_bar(&bars->k_empty[kb], ((ku >> 1) & 1u) ^ 1u, failed)) {
-                        if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, f.row0, u);
+                    if (!wait_bar(&bars->k_empty[kb], par, failed)) {
+                        if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, f.row0, kt);
                         *failed = 1;
                         bad = true;
                         break;
                     }
-                    store_tile<TC>(sK0 + kb * kTileBytes, kr, r);
+                    store_tile<TC>(p, sK0 + kb * kTileBytes, kr, pg, 0, f.g, r);
                     fence_async_smem();
                     mbar_arrive(&bars->k_full[kb]);
-                    ++ku;
-                    if (pass == 1) {
-                        const uint32_t vb = vu & 1;
-                        if (!wait_bar(&bars->v_empty[vb], ((vu >> 1) & 1u) ^ 1u, failed)) {
-                            if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, f.row0, -u);
-                            *failed = 1;
-                            bad = true;
-                            break;
-                        }
-                        store_tile<TC>(sV0 + vb * kTileBytes, vr, r);
-                        fence_async_smem();
-                        mbar_arrive(&bars->v_full[vb]);
-                        ++vu;
+                    if (!wait_bar(&bars->v_empty[kb], par, failed)) {
+                        if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, f.row0, -1 - kt);
+                        *failed = 1;
+                        bad = true;
+                        break;
                     }
+                    store_tile<TC>(p, sV0 + kb * kTileBytes, vr, pg, 1, f.g, r);
+                    fence_async_smem();
+                    mbar_arrive(&bars->v_full[kb]);
+                    ++ku;
                 }
 #pragma unroll
                 for (int k = 0; k < 8; ++k) pg[k] = pg_next[k];
@@ -465,7 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
         // ================= MMA issuer =================
         if (lane == 0) {
             bool ok = true, any = false;
-            uint32_t ku = 0, vu = 0, j = 0;
+            uint32_t ku = 0, j = 0;
             const uint32_t aP = smem_u32(sP);
             for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++j) {
                 const ItemInfo f = item_info(p, it);
@@ -478,11 +512,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
                     ok = false;
                     break;
                 }
-                // P V of the item's pass-2 tile kt (global pass-2 count vu).
-                auto issue_pv = [&](int kt) -> bool {
-                    const uint32_t vb = vu & 1;
-                    if (!wait_bar(&bars->v_full[vb], (vu >> 1) & 1u, failed) ||
-                        !wait_bar(&bars->p_full, vu & 1u, failed))
+                // P V of key tile kt (global tile count u): P from the softmax, V buffer u & 1.
+                auto issue_pv = [&](int kt, uint32_t u) -> bool {
+                    const uint32_t vb = u & 1;
+                    if (!wait_bar(&bars->v_full[vb], (u >> 1) & 1u, failed) || !wait_bar(&bars->p_full, u & 1u, failed))
                         return false;
                     fence_async_smem();
                     fence_after();
@@ -497,12 +530,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
                     }
                     commit(&bars->p_free);
                     commit(&bars->v_empty[vb]);
-                    ++vu;
                     return true;
                 };
-                const int n_uses = 2 * f.n_kt;
-                for (int u = 0; u < n_uses; ++u) {
-                    const int pass = u / f.n_kt, kt = u % f.n_kt;
+                for (int kt = 0; kt < f.n_kt; ++kt) {
                     const uint32_t kb = ku & 1, use = (ku >> 1) & 1u;
                     if (!wait_bar(&bars->k_full[kb], use, failed) || !wait_bar(&bars->s_free[kb], use ^ 1u, failed)) {
                         ok = false;
@@ -521,14 +551,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
                     any = true;
                     commit(&bars->s_full[kb]);
                     commit(&bars->k_empty[kb]);
-                    if (u == n_uses - 1) commit(&bars->q_empty);   // Q is read by S MMAs only
+                    if (kt == f.n_kt - 1) commit(&bars->q_empty);   // Q is read by S MMAs only
                     ++ku;
-                    if (pass == 1 && kt > 0 && !issue_pv(kt - 1)) {
+                    if (kt > 0 && !issue_pv(kt - 1, ku - 2)) {
                         ok = false;
                         break;
                     }
                 }
-                if (!ok || !issue_pv(f.n_kt - 1)) {
+                if (!ok || !issue_pv(f.n_kt - 1, ku - 1)) {
                     ok = false;
                     break;
                 }
@@ -552,89 +582,99 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
         const int r = 32 * quad + lane;          // TMEM lane and MMA row
         const int h = r >> 6, i = r & 63;
         const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * quad) << 16);
-        uint32_t su = 0, pu = 0, j = 0;
+        uint32_t su = 0, j = 0;
         for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++j) {
             const ItemInfo f = item_info(p, it);
             if (!f.ok) break;                      // the loaders report it
             const bool real = i < f.nq;
             const int pos_r = f.pos0 + (real ? i : f.nq - 1);
             const uint32_t ob = j & 1;
-            float m_run = -INFINITY, l_run = 0.0f, inv_l = 0.0f;
-            const int n_uses = 2 * f.n_kt;
+            const uint32_t tO = lane_addr + kTmemO + ob * 128u + static_cast<uint32_t>(64 * sg);
+            // m_ref: the row's reference max (log2 domain) shared by both halves; l_run: this half's sum.
+            float m_ref = -INFINITY, l_run = 0.0f;
             bool go = true;
-            for (int u = 0; u < n_uses; ++u) {
-                const int pass = u / f.n_kt, kt = u % f.n_kt;
-                const uint32_t sb = su & 1;
-                // Every exit decision is warp-uniform: the tcgen05.ld below is .sync.aligned.
-                go = wait_bar(&bars->s_full[sb], (su >> 1) & 1u, failed);
+            for (int kt = 0; kt < f.n_kt; ++kt) {
+                const uint32_t sb = su & 1, par = (su >> 1) & 1u;
+                // Every exit decision is warp-uniform: tcgen05.ld / st are .sync.aligned.
+                go = wait_bar(&bars->s_full[sb], par, failed);
                 if (!__all_sync(0xffffffffu, go)) break;
                 fence_after();
-                uint32_t packed[2][16];
-#pragma unroll
-                for (int ch = 0; ch < 2; ++ch) {
-                    float s[32];
-                    tmem_ld32(lane_addr + sb * 128u + static_cast<uint32_t>(64 * sg + 32 * ch), s);
-                    const int key0 = kt * kKeyTile + 64 * sg + 32 * ch;
-#pragma unroll
-                    for (int jj = 0; jj < 32; ++jj) {
-                        if (key0 + jj > pos_r) s[jj] = -INFINITY;
-                    }
-                    if (pass == 0) {
-                        float cm = s[0];
-#pragma unroll
-                        for (int jj = 1; jj < 32; ++jj) cm = fmaxf(cm, s[jj]);
-                        const float m_new = fmaxf(m_run, cm);
-                        if (m_new != -INFINITY) {
-                            float acc = 0.0f;
-#pragma unroll
-                            for (int jj = 0; jj < 32; ++jj) acc += exp2f(s[jj] - m_new);
-                            l_run = l_run * exp2f(m_run - m_new) + acc;
-                            m_run = m_new;
-                        }
-                    } else {
-#pragma unroll
-                        for (int jj = 0; jj < 16; ++jj)
-                            packed[ch][jj] =
-                                pack2<kF16>(exp2f(s[2 * jj] - m_run) * inv_l, exp2f(s[2 * jj + 1] - m_run) * inv_l);
-                    }
-                }
+                uint32_t sr[2][32];
+                tmem_ld32_issue(lane_addr + sb * 128u + static_cast<uint32_t>(64 * sg), sr[0]);
+                tmem_ld32_issue(lane_addr + sb * 128u + static_cast<uint32_t>(64 * sg + 32), sr[1]);
+                tmem_wait_ld();
                 // S buffer read out: the issuer may compute the next-but-one tile into it.
                 fence_before();
                 mbar_arrive(&bars->s_free[sb]);
-                ++su;
-                if (pass == 0 && kt == f.n_kt - 1) {
-                    // Row statistics of the two key halves -> the row's max and 1 / sum.
-                    float2 *slot = ml + (static_cast<size_t>(j & 1) * 2) * 128;
-                    slot[sg * 128 + r] = make_float2(m_run, l_run);
-                    mbar_arrive(&bars->ml_ready[j & 1]);
-                    go = wait_bar(&bars->ml_ready[j & 1], (j >> 1) & 1u, failed);
-                    if (!__all_sync(0xffffffffu, go)) break;
-                    const float2 o2 = slot[(1 - sg) * 128 + r];
-                    const float M = fmaxf(m_run, o2.x);
-                    const float L = (m_run == -INFINITY ? 0.0f : l_run * exp2f(m_run - M)) +
-                                    (o2.x == -INFINITY ? 0.0f : o2.y * exp2f(o2.x - M));
-                    m_run = M;
-                    inv_l = 1.0f / L;
-                }
-                if (pass == 1) {
-                    go = wait_bar(&bars->p_free, (pu & 1u) ^ 1u, failed);
-                    if (!__all_sync(0xffffffffu, go)) break;
-                    // keys 64 sg .. +63 = block sg of P (8 chunks of 8 keys)
-                    uint8_t *blk = sP + sg * kBlkBytes;
+                float sv[64];
+                const int key0 = kt * kKeyTile + 64 * sg;
+                float tm = -INFINITY;
 #pragma unroll
+                for (int jj = 0; jj < 64; ++jj) {
+                    sv[jj] = key0 + jj > pos_r ? -INFINITY : __uint_as_float(sr[jj >> 5][jj & 31]);
+                    tm = fmaxf(tm, sv[jj]);
+                }
+                // Tile max of the row over both halves.
+                xm[(sb * 2 + sg) * 128 + r] = tm;
+                mbar_arrive(&bars->mx_ready[sb]);
+                go = wait_bar(&bars->mx_ready[sb], par, failed);
+                if (!__all_sync(0xffffffffu, go)) break;
+                tm = fmaxf(tm, xm[(sb * 2 + (1 - sg)) * 128 + r]);
+                // Key 0 is in tile 0 and never masked, so m_ref is finite from tile 0 on.
+                float alpha = 1.0f;
+                bool rescale = false;
+                if (kt == 0) {
+                    m_ref = tm;
+                } else if (tm > m_ref + kRescaleLog2) {
+                    alpha = ex2_approx(m_ref - tm);
+                    m_ref = tm;
+                    l_run *= alpha;
+                    rescale = true;
+                }
+                uint32_t packed[32];
+                float acc = 0.0f;
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) {
+                    const float e0 = ex2_approx(sv[2 * jj] - m_ref), e1 = ex2_approx(sv[2 * jj + 1] - m_ref);
+                    acc += e0 + e1;
+                    packed[jj] = pack2<kF16>(e0, e1);
+                }
+                l_run += acc;
+                // P V of the previous tile has completed: the P tile is free and O is at rest
+                // (P V of this tile waits for P).
+                go = wait_bar(&bars->p_free, (su & 1u) ^ 1u, failed);
+                if (!__all_sync(0xffffffffu, go)) break;
+                if (__any_sync(0xffffffffu, rescale)) {
+                    fence_after();
+#pragma unroll 1
                     for (int ch = 0; ch < 2; ++ch) {
+                        float o[32];
+                        tmem_ld32(tO + 32u * ch, o);
 #pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            *reinterpret_cast<uint4 *>(blk + swz(r, 4 * ch + c)) = make_uint4(
-                                packed[ch][4 * c], packed[ch][4 * c + 1], packed[ch][4 * c + 2], packed[ch][4 * c + 3]);
-                        }
+                        for (int c = 0; c < 32; ++c) o[c] *= alpha;
+                        tmem_st32(tO + 32u * ch, o);
                     }
-                    fence_async_smem();
-                    mbar_arrive(&bars->p_full);
-                    ++pu;
+                    tmem_wait_st();
                 }
+                // keys 64 sg .. +63 = block sg of P (8 chunks of 8 keys)
+                uint8_t *blk = sP + sg * kBlkBytes;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    *reinterpret_cast<uint4 *>(blk + swz(r, c)) =
+                        make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+                }
+                fence_async_smem();
+                fence_before();
+                mbar_arrive(&bars->p_full);
+                ++su;
             }
             if (!__all_sync(0xffffffffu, go)) break;
+            // Row sum over both halves.
+            xl[((j & 1) * 2 + sg) * 128 + r] = l_run;
+            mbar_arrive(&bars->l_ready[j & 1]);
+            go = wait_bar(&bars->l_ready[j & 1], (j >> 1) & 1u, failed);
+            if (!__all_sync(0xffffffffu, go)) break;
+            const float inv_l = 1.0f / (l_run + xl[((j & 1) * 2 + (1 - sg)) * 128 + r]);
             // Epilogue: dims [64 sg, 64 sg + 64) of the O row -> attention output of (query i, head 2g+h)
             go = wait_bar(&bars->o_full[ob], (j >> 1) & 1u, failed);
             if (!__all_sync(0xffffffffu, go)) break;   // warp-uniform: the whole warp loads TMEM
@@ -650,6 +690,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
                     mbar_arrive(&bars->o_empty[ob]);
                 }
                 if (!real) continue;
+#pragma unroll
+                for (int c = 0; c < 32; ++c) o[c] *= inv_l;
                 if (p.out_bf16) {
                     __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(p.out) + off + ch * 32;
 #pragma unroll
