@@ -598,7 +598,8 @@ PREFILL_STREAMS, PREFILL_TOKENS = 64, 410      # config 3's prompts: 390 audio r
 def run_prefill_attn(args) -> int:
     """K3 on its own: causal prefill attention over 28 layers of a paged cache
     holding config-3 prompts (64 streams x 410 tokens per GPU), through
-    qkv_prefill_attend.  A step = one launch per layer (every layer's cache is
+    qkv_prefill_attend_q16 (queries in the kernel's operand form, as the fused
+    append writes them in a prefill).  A step = one launch per layer (every layer's cache is
     a different 107 MB block (bf16), so 28 of them exceed L2 between reuses).
     value = useful attention TFLOP/s (QK^T and PV of the causal triangle, 16 q
     heads, D = 128); roofline against the measured dense bf16 peak."""
@@ -626,10 +627,16 @@ def run_prefill_attn(args) -> int:
     out = torch.empty_like(q)
     st = torch.cuda.current_stream(dev)
     lens = [P] * n
+    q_scale = float(np.float32(1.4426950408889634 / np.sqrt(float(D))))
+    q16 = (q * q_scale).to(torch.float16 if args.kv_dtype == "fp8" else torch.bfloat16)
+    tc = args.kv_dtype != "f32"
 
     def step():
         for layer in range(N_LAYERS):
-            dec.prefill_attend(layer, streams, lens, q.data_ptr(), out.data_ptr(), st.cuda_stream)
+            if tc:
+                dec.prefill_attend_q16(layer, streams, lens, q16.data_ptr(), out.data_ptr(), st.cuda_stream)
+            else:
+                dec.prefill_attend(layer, streams, lens, q.data_ptr(), out.data_ptr(), st.cuda_stream)
 
     for _ in range(args.warmup):
         step()

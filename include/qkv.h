@@ -182,6 +182,14 @@ int qkv_gemm_bf16(const void *x, const void *w, float *c, int32_t m, int32_t n, 
 int qkv_prefill_attend(qkv_handle *h, int32_t layer, int32_t n, const int32_t *stream_ids, const int32_t *lens,
                        const float *q_dev, float *out_dev, void *stream);
 
+/* qkv_prefill_attend with the queries already in the tensor-core kernel's
+ * operand form, as the fused append writes them for prompt rows: q16_dev
+ * [sum lens][Hq*D] = q x log2(e) / sqrt(D) rounded to bf16 (bf16 cache) or f16
+ * (e4m3 cache).  Saves the f32 -> 16-bit pass over q.  QKV_ERR_STATE for an
+ * f32 cache or with the CUDA-core prefill kernel selected. */
+int qkv_prefill_attend_q16(qkv_handle *h, int32_t layer, int32_t n, const int32_t *stream_ids, const int32_t *lens,
+                           const void *q16_dev, float *out_dev, void *stream);
+
 /* One KV-cache step of the microbench: for each of the n streams append one
  * token and attend, for every layer.  qkv[n_layers][n][Hq*D+2*Hkv*D] f32,
  * out[n_layers][n][Hq*D] f32 (layer-major), device pointers; the streams'

@@ -78,6 +78,7 @@ SIGNATURES = {
                                         _P, _P, _P, C.c_char_p, C.c_size_t]),
     "qkv_gemm_bf16": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P]),
     "qkv_prefill_attend": (C.c_int, [_P, C.c_int32, C.c_int32, _P, _P, _P, _P, _P]),
+    "qkv_prefill_attend_q16": (C.c_int, [_P, C.c_int32, C.c_int32, _P, _P, _P, _P, _P]),
     "qkv_gguf_tensor": (C.c_int, [C.c_char_p, C.c_char_p, _I64P, _I32P, _I32P, _P, C.c_size_t, C.c_char_p,
                                   C.c_size_t]),
     "qkv_pager_create": (_P, [C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_uint32]),
@@ -285,6 +286,12 @@ class Decoder:
         streams, lens = _i32(streams), _i32(lens)
         self._check(lib.qkv_prefill_attend(self.h, layer, len(streams), _ptr(streams, C.c_int32),
                                            _ptr(lens, C.c_int32), q_ptr, out_ptr, stream))
+
+    def prefill_attend_q16(self, layer, streams, lens, q16_ptr: int, out_ptr: int, stream=None):
+        """prefill_attend with q16 = bf16 (f16 for an e4m3 cache) of q * log2(e) / sqrt(128)."""
+        streams, lens = _i32(streams), _i32(lens)
+        self._check(lib.qkv_prefill_attend_q16(self.h, layer, len(streams), _ptr(streams, C.c_int32),
+                                               _ptr(lens, C.c_int32), q16_ptr, out_ptr, stream))
 
     def kv_step(self, streams, qkv_ptr: int, out_ptr: int, stream=None):
         streams = _i32(streams)

@@ -1,6 +1,7 @@
 // K1: fused K/V append.  One CTA per token row; 32 half-warp units, each
 // holding 8 contiguous dims of one head (16 lanes x 8 = 128):
-//   units  0..15  q heads  -> per-head RMSNorm -> NEOX RoPE -> q_out (f32)
+//   units  0..15  q heads  -> per-head RMSNorm -> NEOX RoPE -> q_out (f32) and/or
+//                  q16_out (x scale, bf16/f16: the prefill kernel's Q operand)
 //   units 16..23  k heads  -> per-head RMSNorm -> NEOX RoPE -> K page slot
 //   units 24..31  v heads  -> raw                           -> V page slot
 // Replaces text-decoder.cpp:375-433 (reshape, ggml_rms_norm * q/k_norm,
@@ -113,9 +114,22 @@ __global__ void __launch_bounds__(512) kv_append_kernel(AppendParams p) {
     }
 
     if (unit < kHq) {
-        float *dst = p.q_out + static_cast<size_t>(row) * kQDim + unit * kHeadDim + l16 * 8;
-        reinterpret_cast<float4 *>(dst)[0] = make_float4(x[0], x[1], x[2], x[3]);
-        reinterpret_cast<float4 *>(dst)[1] = make_float4(x[4], x[5], x[6], x[7]);
+        const size_t off = static_cast<size_t>(row) * kQDim + unit * kHeadDim + l16 * 8;
+        if (p.q16_out) {
+            // Prefill rows for K3: q x scale rounded once to the MMA operand type.
+            const float s = p.q16_scale;
+            uint4 w;
+            if (p.q16_f16) w = make_uint4(pack_h2(x[0] * s, x[1] * s), pack_h2(x[2] * s, x[3] * s),
+                                          pack_h2(x[4] * s, x[5] * s), pack_h2(x[6] * s, x[7] * s));
+            else w = make_uint4(pack_bf16x2(x[0] * s, x[1] * s), pack_bf16x2(x[2] * s, x[3] * s),
+                                pack_bf16x2(x[4] * s, x[5] * s), pack_bf16x2(x[6] * s, x[7] * s));
+            *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.q16_out) + off) = w;
+        }
+        if (p.q_out) {
+            float *dst = p.q_out + off;
+            reinterpret_cast<float4 *>(dst)[0] = make_float4(x[0], x[1], x[2], x[3]);
+            reinterpret_cast<float4 *>(dst)[1] = make_float4(x[4], x[5], x[6], x[7]);
+        }
         return;
     }
     const int kv = unit < kHq + kHkv ? 0 : 1;

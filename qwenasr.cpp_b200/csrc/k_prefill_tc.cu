@@ -44,11 +44,14 @@ constexpr uint32_t kTileBytes = 2 * kBlkBytes;            // two 64-column block
 constexpr int kSoftmaxWarp0 = 4;                          // warps 4..11: two softmax warpgroups
 constexpr int kMmaWarp = 12;
 constexpr int kThreads = 13 * 32;
-// Q, K[2], V[2], P tiles + row-max hand-over [2 S buffers][2 halves][128 rows]
-// + row-sum hand-over [2 item parities][2 halves][128 rows] + barriers
-constexpr size_t kMlBytes = 2 * 2 * 2 * 128 * sizeof(float);
+// Shared memory from a 1024-byte boundary: Q[2], K[2], V[2], P tiles, then the
+// row hand-over ring [2 slots][2 halves][128 rows] of floats, the barriers,
+// the TMEM address and the abort flag.
+constexpr size_t kTiles = 7;
+constexpr size_t kXBytes = 2 * 2 * 128 * sizeof(float);
+constexpr size_t kTailBytes = kXBytes + 256;
+constexpr size_t kSmemNeed = kTiles * static_cast<size_t>(kTileBytes) + kTailBytes;
 constexpr float kRescaleLog2 = 8.0f;                       // P <= 2^8 between reference moves
-constexpr size_t kSmem = 1024 + 6 * static_cast<size_t>(kTileBytes) + kMlBytes + 512;
 constexpr uint32_t kTmemCols = 512;                       // S0 [0,128), S1 [128,256), O0 [256,384), O1 [384,512)
 constexpr uint32_t kTmemO = 256;
 
@@ -56,7 +59,7 @@ struct K3Params {
     const int4 *items;      // (row0, nq, g, 0)
     const int *slots;
     const int *positions;
-    const float *q;         // [rows][2048] post-RoPE
+    const uint16_t *q16;    // [rows][2048] post-RoPE q x scale_log2, bf16 (f16 for e4m3)
     void *out;              // [rows][2048]
     int out_bf16;
     const void *pool;
@@ -65,7 +68,6 @@ struct K3Params {
     int maxp;
     int max_streams;
     int n_pages;
-    float scale_log2;
     DevError *err;
 };
 
@@ -288,9 +290,10 @@ __device__ __forceinline__ void store_tile(const K3Params &p, uint8_t *tile, con
 }
 
 struct Bars {
-    uint64_t q_full, q_empty, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_free[2];
-    uint64_t p_full, p_free, o_full[2], o_empty[2], mx_ready[2], l_ready[2], mma_done;
+    uint64_t q_full[2], q_empty[2], k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_free[2];
+    uint64_t p_full, p_free, o_full[2], o_empty[2], x_ready[2], mma_done;
 };
+static_assert(sizeof(Bars) + 2 * sizeof(uint32_t) <= kTailBytes - kXBytes, "tail of the shared-memory layout");
 
 // Bounded wait that also gives up as soon as another role set the abort flag.
 __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile int *failed) {
@@ -327,31 +330,39 @@ __device__ __forceinline__ ItemInfo item_info(const K3Params &p, int it) {
 // Persistent: CTA c takes items c, c + G, c + 2G, ... (the host orders items
 // longest first).  Every barrier phase follows from per-role counters that
 // run on across items: item j uses the Q tile and O buffer j & 1; key tile u
-// (global count) uses K, V, S and row-max buffers u & 1 and the single P tile.
-template <typename TC>
+// (global count) uses K, V and S buffers u & 1 and the single P tile; the
+// softmax threads' x-th row hand-over (each tile's max, each item's sum) uses
+// ring slot x & 1.
 // 13 warps: the SM's four sub-partitions hold up to 4 of them each, which caps
 // a thread at 128 registers.
+template <typename TC>
 __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p, int n_items) {
     constexpr bool kF16 = sizeof(TC) == 1;   // e4m3 cache -> f16 operands
     extern __shared__ uint8_t smem_raw[];
+    pdl_trigger();
+    // The tiles need a 1024-byte boundary; the layout must fit the launch's allocation.
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *const sQ = smem;
-    uint8_t *const sK0 = smem + kTileBytes;          // K[b] = sK0 + b * kTileBytes
-    uint8_t *const sV0 = smem + 3 * kTileBytes;      // V[b]
-    uint8_t *const sP = smem + 5 * kTileBytes;
-    float *const xm = reinterpret_cast<float *>(smem + 6 * kTileBytes);     // tile row max [S buffer][half][row]
-    float *const xl = xm + 2 * 2 * 128;                                      // row sums [item parity][half][row]
-    Bars *bars = reinterpret_cast<Bars *>(smem + 6 * kTileBytes + kMlBytes);
+    uint32_t dyn_bytes;
+    asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn_bytes));
+    if (static_cast<size_t>(smem - smem_raw) + kSmemNeed > dyn_bytes) {
+        if (threadIdx.x == 0) report_error(p.err, kErrRowBounds, kWherePrefillAttn, -1, static_cast<int>(dyn_bytes));
+        return;
+    }
+    uint8_t *const sQ0 = smem;                       // Q[b] = sQ0 + b * kTileBytes
+    uint8_t *const sK0 = smem + 2 * kTileBytes;      // K[b]
+    uint8_t *const sV0 = smem + 4 * kTileBytes;      // V[b]
+    uint8_t *const sP = smem + 6 * kTileBytes;
+    float *const xr = reinterpret_cast<float *>(smem + kTiles * kTileBytes);   // row hand-over [slot][half][row]
+    Bars *bars = reinterpret_cast<Bars *>(smem + kTiles * kTileBytes + kXBytes);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 1);
     volatile int *failed = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    pdl_trigger();
 
     if (threadIdx.x == 0) {
-        mbar_init(&bars->q_full, 128);
-        mbar_init(&bars->q_empty, 1);
         for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars->q_full[b], 128);
+            mbar_init(&bars->q_empty[b], 1);
             mbar_init(&bars->k_full[b], 128);
             mbar_init(&bars->k_empty[b], 1);
             mbar_init(&bars->v_full[b], 128);
@@ -360,8 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
             mbar_init(&bars->s_free[b], 256);
             mbar_init(&bars->o_full[b], 1);
             mbar_init(&bars->o_empty[b], 256);
-            mbar_init(&bars->mx_ready[b], 256);
-            mbar_init(&bars->l_ready[b], 256);
+            mbar_init(&bars->x_ready[b], 256);
         }
         mbar_init(&bars->p_full, 256);
         mbar_init(&bars->p_free, 1);
@@ -394,37 +404,26 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
             }
             const int *pt = p.page_table + static_cast<size_t>(f.slot) * p.maxp;
             {
-                // Q rows (head 2g + h, query i) -> row (h << 6) | i, scaled into the log2
-                // domain, swizzled K-major.  Warp w fills rows 32w .. 32w+31, one 512-byte
-                // f32 row per load instruction (lane = dims 4 lane .. 4 lane + 3).
-                if (!wait_bar(&bars->q_empty, (j & 1u) ^ 1u, failed)) {
-                    if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, f.row0, -3);
+                // Q rows (head 2g + h, query i) -> tile row (h << 6) | i, swizzled K-major,
+                // by cp.async like a key tile: thread t copies 16-byte chunk t % 16 of rows
+                // t / 16 + 8m; rows past the item's queries are zero-filled.
+                const uint32_t qb = j & 1;
+                if (!wait_bar(&bars->q_empty[qb], ((j >> 1) & 1u) ^ 1u, failed)) {
+                    if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, f.row0, -(1 << 20));
                     *failed = 1;
                     break;
                 }
-                uint8_t *q_tile = sQ;
-                const float s = p.scale_log2;
-                const int ln = r & 31, w = r >> 5;
+                uint8_t *q_tile = sQ0 + qb * kTileBytes;
+                const int c = r & 15;
 #pragma unroll
-                for (int b8 = 0; b8 < 4; ++b8) {
-                    float4 a[8];
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        const int row = 32 * w + 8 * b8 + k, h = row >> 6, i = row & 63;
-                        a[k] = i < f.nq ? __ldg(reinterpret_cast<const float4 *>(
-                                              p.q + static_cast<size_t>(f.row0 + i) * kQDim + (2 * f.g + h) * kHeadDim) + ln)
-                                        : make_float4(0.f, 0.f, 0.f, 0.f);
-                    }
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        const int row = 32 * w + 8 * b8 + k;
-                        const uint2 v = make_uint2(pack2<kF16>(a[k].x * s, a[k].y * s), pack2<kF16>(a[k].z * s, a[k].w * s));
-                        // dims 4 ln .. +3: block ln >> 4, 16-byte chunk (ln >> 1) & 7, half ln & 1
-                        *reinterpret_cast<uint2 *>(q_tile + (ln >> 4) * kBlkBytes + swz(row, (ln >> 1) & 7) + 8 * (ln & 1)) = v;
-                    }
+                for (int m = 0; m < 16; ++m) {
+                    const int row = (r >> 4) + 8 * m, h = row >> 6, i = row & 63;
+                    const bool live = i < f.nq;
+                    const uint16_t *src =
+                        p.q16 + static_cast<size_t>(f.row0 + (live ? i : 0)) * kQDim + (2 * f.g + h) * kHeadDim + 8 * c;
+                    cp_async16(q_tile + (c >> 3) * kBlkBytes + swz(row, c & 7), src, live ? 16u : 0u);
                 }
-                fence_async_smem();
-                mbar_arrive(&bars->q_full);
+                cp_async_arrive(&bars->q_full[qb]);
             }
             bool bad = false;
             int pg[8], pg_next[8];
@@ -505,9 +504,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
                 const ItemInfo f = item_info(p, it);
                 if (!f.ok) break;                  // the loaders report it
                 const uint32_t ob = j & 1;
-                const uint32_t aQ = smem_u32(sQ);
+                const uint32_t aQ = smem_u32(sQ0 + ob * kTileBytes);
                 const uint32_t tO = tmem + kTmemO + ob * 128u;
-                if (!wait_bar(&bars->q_full, j & 1u, failed) ||
+                if (!wait_bar(&bars->q_full[ob], (j >> 1) & 1u, failed) ||
                     !wait_bar(&bars->o_empty[ob], ((j >> 1) & 1u) ^ 1u, failed)) {
                     ok = false;
                     break;
@@ -551,7 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
                     any = true;
                     commit(&bars->s_full[kb]);
                     commit(&bars->k_empty[kb]);
-                    if (kt == f.n_kt - 1) commit(&bars->q_empty);   // Q is read by S MMAs only
+                    if (kt == f.n_kt - 1) commit(&bars->q_empty[ob]);   // Q is read by S MMAs only
                     ++ku;
                     if (kt > 0 && !issue_pv(kt - 1, ku - 2)) {
                         ok = false;
@@ -582,7 +581,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
         const int r = 32 * quad + lane;          // TMEM lane and MMA row
         const int h = r >> 6, i = r & 63;
         const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * quad) << 16);
-        uint32_t su = 0, j = 0;
+        uint32_t su = 0, xu = 0, j = 0;
+        // Row hand-over with the other half: publish v, return the other half's value.
+        auto exchange = [&](float v, float &other) -> bool {
+            const uint32_t xs = xu & 1;
+            xr[(xs * 2 + sg) * 128 + r] = v;
+            mbar_arrive(&bars->x_ready[xs]);
+            const bool ok = wait_bar(&bars->x_ready[xs], (xu >> 1) & 1u, failed);
+            other = xr[(xs * 2 + (1 - sg)) * 128 + r];
+            ++xu;
+            return ok;
+        };
         for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++j) {
             const ItemInfo f = item_info(p, it);
             if (!f.ok) break;                      // the loaders report it
@@ -615,11 +624,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
                     tm = fmaxf(tm, sv[jj]);
                 }
                 // Tile max of the row over both halves.
-                xm[(sb * 2 + sg) * 128 + r] = tm;
-                mbar_arrive(&bars->mx_ready[sb]);
-                go = wait_bar(&bars->mx_ready[sb], par, failed);
+                float tm_other;
+                go = exchange(tm, tm_other);
                 if (!__all_sync(0xffffffffu, go)) break;
-                tm = fmaxf(tm, xm[(sb * 2 + (1 - sg)) * 128 + r]);
+                tm = fmaxf(tm, tm_other);
                 // Key 0 is in tile 0 and never masked, so m_ref is finite from tile 0 on.
                 float alpha = 1.0f;
                 bool rescale = false;
@@ -670,11 +678,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
             }
             if (!__all_sync(0xffffffffu, go)) break;
             // Row sum over both halves.
-            xl[((j & 1) * 2 + sg) * 128 + r] = l_run;
-            mbar_arrive(&bars->l_ready[j & 1]);
-            go = wait_bar(&bars->l_ready[j & 1], (j >> 1) & 1u, failed);
+            float l_other;
+            go = exchange(l_run, l_other);
             if (!__all_sync(0xffffffffu, go)) break;
-            const float inv_l = 1.0f / (l_run + xl[((j & 1) * 2 + (1 - sg)) * 128 + r]);
+            const float inv_l = 1.0f / (l_run + l_other);
             // Epilogue: dims [64 sg, 64 sg + 64) of the O row -> attention output of (query i, head 2g+h)
             go = wait_bar(&bars->o_full[ob], (j >> 1) & 1u, failed);
             if (!__all_sync(0xffffffffu, go)) break;   // warp-uniform: the whole warp loads TMEM
@@ -716,27 +723,69 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
     }
 }
 
+// Rows of q (f32) x scale rounded to the 16-bit operand type; 8 elements per thread.
+__global__ void q_to16_kernel(const float *__restrict__ q, size_t n8, float scale, int f16, uint16_t *out) {
+    pdl_trigger();
+    pdl_wait();
+    for (size_t t = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; t < n8;
+         t += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const float4 a = reinterpret_cast<const float4 *>(q)[2 * t];
+        const float4 b = reinterpret_cast<const float4 *>(q)[2 * t + 1];
+        const float s = scale;
+        uint4 w;
+        if (f16) w = make_uint4(pack_h2(a.x * s, a.y * s), pack_h2(a.z * s, a.w * s), pack_h2(b.x * s, b.y * s),
+                                pack_h2(b.z * s, b.w * s));
+        else w = make_uint4(pack_bf16x2(a.x * s, a.y * s), pack_bf16x2(a.z * s, a.w * s),
+                            pack_bf16x2(b.x * s, b.y * s), pack_bf16x2(b.z * s, b.w * s));
+        reinterpret_cast<uint4 *>(out)[t] = w;
+    }
+}
+
+// Dynamic shared memory of a K3 launch: the layout plus room to reach a
+// 1024-byte boundary, capped at the device's per-block maximum (the kernel
+// checks that its layout fits what it was given).
+cudaError_t k3_smem_bytes(size_t *bytes) {
+    int dev = 0, optin = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return e;
+    const size_t want = kSmemNeed + 1023;
+    *bytes = want < static_cast<size_t>(optin) ? want : static_cast<size_t>(optin);
+    return cudaSuccess;
+}
+
 }  // namespace
 
 cudaError_t prepare_prefill_tc() {
-    cudaError_t e = cudaFuncSetAttribute(prefill_attn_tc_kernel<__nv_bfloat16>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmem));
+    size_t smem = 0;
+    cudaError_t e = k3_smem_bytes(&smem);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(prefill_attn_tc_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(prefill_attn_tc_kernel<uint8_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(kSmem));
+                                static_cast<int>(smem));
 }
 
 bool prefill_tc_supported(int kv_dtype) { return kv_dtype == kKvBF16 || kv_dtype == kKvFP8; }
 
+cudaError_t launch_q_to16(const float *q, int n, float scale, bool f16, void *out, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    const size_t n8 = static_cast<size_t>(n) * kQDim / 8;
+    const size_t blocks = (n8 + 255) / 256;
+    return launch_pdl(q_to16_kernel, dim3(static_cast<unsigned>(blocks < 4096 ? blocks : 4096)), dim3(256), 0, st, q,
+                      n8, scale, f16 ? 1 : 0, static_cast<uint16_t *>(out));
+}
+
 cudaError_t launch_prefill_attn_tc(const PrefillAttnParams &pp, int kv_dtype, const int4 *items, int n_items,
                                    bool out_bf16, cudaStream_t st) {
     if (n_items <= 0) return cudaSuccess;
-    if (!prefill_tc_supported(kv_dtype) || (kv_dtype == kKvFP8 && !pp.scales)) return cudaErrorInvalidValue;
+    if (!prefill_tc_supported(kv_dtype) || (kv_dtype == kKvFP8 && !pp.scales) || !pp.q16) return cudaErrorInvalidValue;
     K3Params p{};
     p.items = items;
     p.slots = pp.slots;
     p.positions = pp.positions;
-    p.q = pp.q;
+    p.q16 = static_cast<const uint16_t *>(pp.q16);
     p.out = pp.out;
     p.out_bf16 = out_bf16 ? 1 : 0;
     p.pool = pp.pool;
@@ -745,16 +794,17 @@ cudaError_t launch_prefill_attn_tc(const PrefillAttnParams &pp, int kv_dtype, co
     p.maxp = pp.maxp;
     p.max_streams = pp.max_streams;
     p.n_pages = pp.n_pages;
-    p.scale_log2 = pp.scale_log2;
     p.err = pp.err;
     int dev = 0, sms = 0;
+    size_t smem = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess) e = k3_smem_bytes(&smem);
     if (e != cudaSuccess) return e;
     const int grid = n_items < sms ? n_items : sms;   // persistent: one CTA per SM walks the items
     if (kv_dtype == kKvBF16)
-        return launch_pdl(prefill_attn_tc_kernel<__nv_bfloat16>, dim3(grid), dim3(kThreads), kSmem, st, p, n_items);
-    return launch_pdl(prefill_attn_tc_kernel<uint8_t>, dim3(grid), dim3(kThreads), kSmem, st, p, n_items);
+        return launch_pdl(prefill_attn_tc_kernel<__nv_bfloat16>, dim3(grid), dim3(kThreads), smem, st, p, n_items);
+    return launch_pdl(prefill_attn_tc_kernel<uint8_t>, dim3(grid), dim3(kThreads), smem, st, p, n_items);
 }
 
 }  // namespace qkv

@@ -51,7 +51,10 @@ struct AppendParams {
     const int *slots;          // [n] stream ids (page-table rows)
     const int *positions;      // [n] token position of each row
     const float *qkv;          // [n][kQkvDim] raw projections
-    float *q_out;              // [n][kQDim]
+    float *q_out;              // [n][kQDim] f32, or null
+    void *q16_out;             // [n][kQDim] 16-bit q x q16_scale (K3's Q operand), or null
+    float q16_scale;
+    int q16_f16;               // 1: f16 (e4m3 cache), 0: bf16
     const float *q_norm_w;     // [kHeadDim]
     const float *k_norm_w;     // [kHeadDim]
     const float2 *rope;        // [rope_len][kHeadDim/2] (cos, sin)
@@ -89,7 +92,8 @@ struct PrefillAttnParams {
     int n;                     // query rows
     const int *slots;          // [n]
     const int *positions;      // [n] query position; keys are [0, position]
-    const float *q;            // [n][kQDim]
+    const float *q;            // [n][kQDim] (CUDA-core kernel)
+    const void *q16;           // [n][kQDim] q x scale_log2 in bf16 (f16 for e4m3), for K3
     void *out;                 // [n][kQDim] f32 or bf16
     const void *pool;
     const float *scales;
@@ -114,6 +118,8 @@ cudaError_t prepare_prefill_tc();
 bool prefill_tc_supported(int kv_dtype);
 cudaError_t launch_prefill_attn_tc(const PrefillAttnParams &p, int kv_dtype, const int4 *items, int n_items,
                                    bool out_bf16, cudaStream_t st);
+// q (f32, [n][kQDim]) x scale rounded to bf16 (f16 if `f16`): K3's Q operand for callers that hold f32 q.
+cudaError_t launch_q_to16(const float *q, int n, float scale, bool f16, void *out, cudaStream_t st);
 cudaError_t launch_page_gather(const void *pool, int kv_dtype, const int *pages, int n_pages_row, int len,
                                int n_pages, void *k_out, void *v_out, DevError *err, cudaStream_t st);
 cudaError_t launch_page_copy(void *pool_layer, size_t page_bytes, const int *src, const int *dst, int n,

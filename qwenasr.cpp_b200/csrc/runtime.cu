@@ -473,6 +473,9 @@ int check_streams(qkv_handle *h, int n, const int32_t *streams) {
     return QKV_OK;
 }
 
+// Softmax scale folded into q: 1 / sqrt(head dim) in the log2 domain.
+float attn_scale_log2() { return static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(kHeadDim))); }
+
 AppendParams append_params(qkv_handle *h, int layer, int n, const int *slots, const int *pos, const float *qkv,
                            float *q_out, const float *qn, const float *kn) {
     AppendParams p{};
@@ -513,7 +516,7 @@ AttendParams attend_params(qkv_handle *h, int layer, int n, const int *slots, co
     p.part_o = h->part_o;
     p.part_ml = h->part_ml;
     p.counters = h->counters;
-    p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(kHeadDim)));
+    p.scale_log2 = attn_scale_log2();
     p.err = h->d_err;
     return p;
 }
@@ -549,16 +552,25 @@ int head_and_argmax(qkv_handle *h, int n, const int *d_rows) {
 
 // All layers over `n` rows whose inputs are in h->x; decode rows attend with
 // K2, prompt rows with the causal prefill kernel.
+// K3 (tensor cores) serves bf16 and e4m3 caches when items are given.
+bool prefill_on_tc(const qkv_handle *h, const int4 *items, int n_items) {
+    return h->prefill_tc && prefill_tc_supported(h->rt.kv_dtype) && items && n_items > 0;
+}
+
 // Causal prefill attention over layer l's cache for n query rows (slots,
 // positions on the device): K3 on the tensor cores for bf16/e4m3 caches
 // (items = 64-query blocks per kv head), the CUDA-core kernel otherwise.
-cudaError_t prefill_attend(qkv_handle *h, int l, int n, const int *slots, const int *pos, const float *q, void *out,
-                           bool out_bf16, const int4 *items, int n_items, cudaStream_t st) {
+// K3 reads q16 (q x scale in its operand type, as K1 writes it for prompt
+// rows); when q16 is null, q is converted into it first, into h->q's storage
+// behind q (q itself must then not be h->q).
+cudaError_t prefill_attend(qkv_handle *h, int l, int n, const int *slots, const int *pos, const float *q,
+                           const void *q16, void *out, bool out_bf16, const int4 *items, int n_items, cudaStream_t st) {
     PrefillAttnParams pp{};
     pp.n = n;
     pp.slots = slots;
     pp.positions = pos;
     pp.q = q;
+    pp.q16 = q16;
     pp.out = out;
     pp.pool = static_cast<const uint8_t *>(h->pool) + h->pool_layer_bytes * static_cast<size_t>(l);
     pp.scales = h->scales ? h->scales + h->scales_layer_elems * static_cast<size_t>(l) : nullptr;
@@ -566,10 +578,16 @@ cudaError_t prefill_attend(qkv_handle *h, int l, int n, const int *slots, const 
     pp.maxp = h->maxp;
     pp.max_streams = h->rt.max_streams;
     pp.n_pages = h->n_pages;
-    pp.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(kHeadDim)));
+    pp.scale_log2 = attn_scale_log2();
     pp.err = h->d_err;
-    if (h->prefill_tc && prefill_tc_supported(h->rt.kv_dtype) && items && n_items > 0)
+    if (prefill_on_tc(h, items, n_items)) {
+        if (!pp.q16) {
+            cudaError_t e = launch_q_to16(q, n, pp.scale_log2, h->rt.kv_dtype == kKvFP8, h->q, st);
+            if (e != cudaSuccess) return e;
+            pp.q16 = h->q;
+        }
         return launch_prefill_attn_tc(pp, h->rt.kv_dtype, items, n_items, out_bf16, st);
+    }
     return launch_prefill_attn(pp, h->rt.kv_dtype, out_bf16, st);
 }
 
@@ -587,9 +605,16 @@ int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int
             if ((rc = layer_kv(h, l, n, slots, pos, lens, h->qkv, h->q, h->attn, bf, L.q_norm, L.k_norm, h->stream)))
                 return rc;
         } else {
-            AppendParams ap = append_params(h, l, n, slots, pos, h->qkv, h->q, L.q_norm, L.k_norm);
+            // K3 takes q from K1 already scaled and rounded to its operand type.
+            const bool tc = prefill_on_tc(h, items, n_items);
+            AppendParams ap = append_params(h, l, n, slots, pos, h->qkv, tc ? nullptr : h->q, L.q_norm, L.k_norm);
+            if (tc) {
+                ap.q16_out = h->q;
+                ap.q16_scale = attn_scale_log2();
+                ap.q16_f16 = h->rt.kv_dtype == kKvFP8 ? 1 : 0;
+            }
             CK(launch_kv_append(ap, h->rt.kv_dtype, h->stream));
-            CK(prefill_attend(h, l, n, slots, pos, h->q, h->attn, bf, items, n_items, h->stream));
+            CK(prefill_attend(h, l, n, slots, pos, h->q, tc ? h->q : nullptr, h->attn, bf, items, n_items, h->stream));
             h->launches += 2;
         }
         CK(gemm(h, h->attn, L.w_o, h->x, n, c.hidden, kQDim, 1));
@@ -1028,11 +1053,15 @@ int qkv_kv_attend(qkv_handle *h, int32_t layer, int32_t n, const int32_t *slots_
     return QKV_OK;
 }
 
-int qkv_prefill_attend(qkv_handle *h, int32_t layer, int32_t n, const int32_t *stream_ids, const int32_t *lens,
-                       const float *q_dev, float *out_dev, void *stream) {
+// Shared body of the two prefill-attention operators: exactly one of q (f32)
+// and q16 (K3's operand form) is given.
+static int prefill_attend_op(qkv_handle *h, int32_t layer, int32_t n, const int32_t *stream_ids, const int32_t *lens,
+                      const float *q, const void *q16, float *out, void *stream) {
     if (!h) return QKV_ERR_INVALID_ARG;
-    if (layer < 0 || layer >= h->cfg.n_layers || n < 0 || (n > 0 && (!stream_ids || !lens || !q_dev || !out_dev)))
+    if (layer < 0 || layer >= h->cfg.n_layers || n < 0 || (n > 0 && (!stream_ids || !lens || !(q || q16) || !out)))
         return fail(h, QKV_ERR_INVALID_ARG, "prefill_attend: bad layer, count or pointer");
+    if (q16 && !(h->prefill_tc && prefill_tc_supported(h->rt.kv_dtype)))
+        return fail(h, QKV_ERR_STATE, "prefill_attend_q16: needs a bf16 or e4m3 cache with the tensor-core kernel");
     int rc;
     if ((rc = check_streams(h, n, stream_ids))) return rc;
     int64_t total = 0;
@@ -1060,9 +1089,19 @@ int qkv_prefill_attend(qkv_handle *h, int32_t layer, int32_t n, const int32_t *s
     std::vector<int> base(static_cast<size_t>(n));
     for (int i = 0; i < n; ++i) base[static_cast<size_t>(i)] = stream_len(h, stream_ids[i]) - lens[i];
     if ((rc = upload_items(h, n, lens, base.data(), &n_items, st))) return rc;
-    CK(prefill_attend(h, layer, T, h->d_rowbuf, h->d_rowbuf + T, q_dev, out_dev, false, h->d_items, n_items, st));
-    h->launches += 1;
+    CK(prefill_attend(h, layer, T, h->d_rowbuf, h->d_rowbuf + T, q, q16, out, false, h->d_items, n_items, st));
+    h->launches += (!q16 && prefill_on_tc(h, h->d_items, n_items)) ? 2 : 1;
     return QKV_OK;
+}
+
+int qkv_prefill_attend(qkv_handle *h, int32_t layer, int32_t n, const int32_t *stream_ids, const int32_t *lens,
+                       const float *q_dev, float *out_dev, void *stream) {
+    return prefill_attend_op(h, layer, n, stream_ids, lens, q_dev, nullptr, out_dev, stream);
+}
+
+int qkv_prefill_attend_q16(qkv_handle *h, int32_t layer, int32_t n, const int32_t *stream_ids, const int32_t *lens,
+                           const void *q16_dev, float *out_dev, void *stream) {
+    return prefill_attend_op(h, layer, n, stream_ids, lens, nullptr, q16_dev, out_dev, stream);
 }
 
 int qkv_kv_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const float *qkv_dev, float *out_dev, void *stream) {

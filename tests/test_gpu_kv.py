@@ -354,3 +354,38 @@ def test_prefill_attention_operator(pkg, checker, kv_dtype):
         tol = 2e-5 if kv_dtype == 0 else 2e-2
         print(f"kv={kv_dtype}: prefill attention max relative error {worst:.3e}")
         assert worst < tol, worst
+
+
+@pytest.mark.parametrize("kv_dtype", [0, 1, 2])
+def test_prefill_attention_q16_entry(pkg, kv_dtype):
+    """qkv_prefill_attend_q16 with q already scaled and rounded (torch's
+    round-to-nearest, as the fused append and the f32 entry's conversion do)
+    gives bit-identical output to qkv_prefill_attend; an f32 cache (CUDA-core
+    kernel, no 16-bit operand form) is refused with QKV_ERR_STATE."""
+    lens_total = [5, 64, 129, 300]
+    q_lens = [5, 64, 129, 77]
+    dec, _, _ = kv_handle(pkg, kv_dtype, seed=9, max_streams=len(lens_total), max_context=512, batch_tokens=1024)
+    with dec:
+        rng = np.random.default_rng(31)
+        streams = []
+        for L in lens_total:
+            s = dec.open()
+            dec.extend(s, L)
+            fill_stream(dec, 0, s, rng.standard_normal((L, QKV), dtype=np.float32))
+            streams.append(s)
+        q = torch.tensor(rng.standard_normal((sum(q_lens), HQ * D), dtype=np.float32), device="cuda")
+        scale = np.float32(1.4426950408889634 / np.sqrt(128.0))
+        q16 = (q * float(scale)).to(torch.float16 if kv_dtype == 2 else torch.bfloat16)
+        out_q16 = torch.full_like(q, float("nan"))
+        if kv_dtype == 0:
+            with pytest.raises(pkg.QkvError) as ei:
+                dec.prefill_attend_q16(0, streams, q_lens, q16.data_ptr(), out_q16.data_ptr())
+            assert "STATE" in str(ei.value)
+            return
+        out = torch.full_like(q, float("nan"))
+        dec.prefill_attend(0, streams, q_lens, q.data_ptr(), out.data_ptr())
+        dec.prefill_attend_q16(0, streams, q_lens, q16.data_ptr(), out_q16.data_ptr())
+        torch.cuda.synchronize()
+        dec.sync()
+        assert torch.isfinite(out).all()
+        assert torch.equal(out, out_q16)
