@@ -55,7 +55,8 @@ template <int BN> struct TcTraits {
 struct TcParams {
     int M, N, K;
     int ktiles_per_split;
-    int tiles_n, tiles_m, splits;   // units = tiles_n * tiles_m * splits, token tile fastest
+    int tiles_n, tiles_m, splits;   // units = tiles_n * tiles_m * splits
+    int w_fastest;                  // unit order: 1 weight tile fastest, 0 token tile fastest
     float *C;
     int accumulate;   // 0: store (one split) / red.add into a zeroed C; 1: add into C
     // Fused SwiGLU (act != nullptr, one split): W holds gate and up rows
@@ -187,12 +188,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    // unit u -> token tile (fastest), weight tile, K split
+    // unit u -> (token tile, weight tile) in the launch's order, then K split
     auto unit_coords = [&](int u, int &n0, int &m0, int &kt0, int &nk) {
-        const int tm = u % p.tiles_m;
-        const int rest = u / p.tiles_m;
-        const int tn = rest % p.tiles_n;
-        const int sp = rest / p.tiles_n;
+        const int tiles = p.tiles_m * p.tiles_n;
+        const int sp = u / tiles;
+        const int t = u - sp * tiles;
+        const int tm = p.w_fastest ? t / p.tiles_n : t % p.tiles_m;
+        const int tn = p.w_fastest ? t % p.tiles_n : t / p.tiles_m;
         n0 = tn * kBM;
         m0 = tm * BN;
         kt0 = sp * p.ktiles_per_split;
@@ -204,7 +206,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (lane == 0) {
             const bool is_w = warp == 0;
             if (!is_w) pdl_wait();
-            const uint64_t pol = is_w ? l2_evict_first_policy() : l2_evict_last_policy();
+            // The operand that every wave of units re-reads stays in L2 (evict_last): the
+            // token tiles when they run fastest, the weights when they do.
+            const bool keep = is_w == (p.w_fastest != 0);
+            const uint64_t pol = keep ? l2_evict_last_policy() : l2_evict_first_policy();
             const CUtensorMap *map = is_w ? &tmW : &tmX;
             const uint32_t bytes = is_w ? kABytes : T::kBBytes;
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -491,6 +496,15 @@ template <int BN> cudaError_t prepare_bn() {
                                 static_cast<int>(TcTraits<BN>::kSmem));
 }
 
+// Unit order: weight tiles fastest once the token operand outgrows a share of
+// L2 (the weights, <= 50 MB for every decoder projection, then stay resident
+// while the token tiles stream once); token tiles fastest otherwise.
+bool weight_fastest(int M, int K, int tiles_m) {
+    static const char *forced = getenv("QWENASR_B200_GEMM_ORDER");
+    if (forced && (forced[0] == 'w' || forced[0] == 't')) return forced[0] == 'w' && tiles_m > 1;
+    return tiles_m > 1 && static_cast<double>(M) * K * 2.0 > 32.0e6;
+}
+
 template <int BN>
 cudaError_t launch_bn(const void *X, const void *W, float *C, int M, int N, int K, int accumulate, int splits,
                       int num_sms, DevError *err, cudaStream_t st, __nv_bfloat16 *act = nullptr) {
@@ -505,7 +519,7 @@ cudaError_t launch_bn(const void *X, const void *W, float *C, int M, int N, int 
         cudaError_t e = cudaMemsetAsync(C, 0, static_cast<size_t>(M) * N * sizeof(float), st);
         if (e != cudaSuccess) return e;
     }
-    TcParams p{M, N, K, kps, tiles_n, tiles_m, splits, C, accumulate, act, err};
+    TcParams p{M, N, K, kps, tiles_n, tiles_m, splits, weight_fastest(M, K, tiles_m) ? 1 : 0, C, accumulate, act, err};
     const int units = tiles_n * tiles_m * splits;
     const int grid = units < num_sms ? units : num_sms;
     return launch_pdl(gemm_tc_kernel<BN>, dim3(grid), dim3(kGemmThreads), TcTraits<BN>::kSmem, st, tw, tx, p);

@@ -21,7 +21,8 @@
 // bf16.  K and V tiles are double-buffered, S is double-buffered in TMEM.
 //
 // One pass over the key tiles with an online softmax: the issuer puts S of
-// tile t + 1 ahead of P V of tile t, so the softmax of a tile overlaps the
+// tile t + 1 ahead of P V of tile t (across items too: the next item's first S
+// goes ahead of this item's last P V), so the softmax of a tile overlaps the
 // MMAs around it.  P is written unnormalised against a per-row reference max;
 // the reference moves (and O, l are rescaled in place in TMEM) only when a
 // tile's max exceeds it by more than 2^8, so P stays within [0, 256] and most
@@ -500,37 +501,49 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
             bool ok = true, any = false;
             uint32_t ku = 0, j = 0;
             const uint32_t aP = smem_u32(sP);
+            // P V of a tile is issued after S of the next tile in the CTA's stream,
+            // the next item's first tile included, so S is ready when the softmax
+            // threads come back from an item's epilogue.
+            struct Pending {
+                bool live;
+                bool last;        // the item's last key tile: O is complete after it
+                int kt;
+                uint32_t u, ob, j;
+            } pend{false, false, 0, 0, 0, 0};
+            auto issue_pv = [&]() -> bool {
+                if (!pend.live) return true;
+                const uint32_t vb = pend.u & 1;
+                // O buffer ob is free once item j - 2's epilogue has read it.
+                if (pend.kt == 0 && !wait_bar(&bars->o_empty[pend.ob], ((pend.j >> 1) & 1u) ^ 1u, failed)) return false;
+                if (!wait_bar(&bars->v_full[vb], (pend.u >> 1) & 1u, failed) || !wait_bar(&bars->p_full, pend.u & 1u, failed))
+                    return false;
+                fence_async_smem();
+                fence_after();
+                const uint32_t aV = smem_u32(sV0 + vb * kTileBytes);
+                const uint32_t tO = tmem + kTmemO + pend.ob * 128u;
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t blk = static_cast<uint32_t>(kk >> 2) * kBlkBytes;
+                    const uint64_t step = 2ull * static_cast<uint64_t>(kk & 3);
+                    // P (K-major A, 16 keys per step), V rows (MN-major B, 2 KB per 16 rows)
+                    mma(tO, desc_kmajor(aP + blk) + step, desc_mnmajor(aV + static_cast<uint32_t>(kk) * 2048u),
+                        idesc_pv<kF16>(), (pend.kt > 0 || kk > 0) ? 1 : 0);
+                }
+                commit(&bars->p_free);
+                commit(&bars->v_empty[vb]);
+                if (pend.last) commit(&bars->o_full[pend.ob]);
+                pend.live = false;
+                return true;
+            };
             for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++j) {
                 const ItemInfo f = item_info(p, it);
                 if (!f.ok) break;                  // the loaders report it
-                const uint32_t ob = j & 1;
-                const uint32_t aQ = smem_u32(sQ0 + ob * kTileBytes);
-                const uint32_t tO = tmem + kTmemO + ob * 128u;
-                if (!wait_bar(&bars->q_full[ob], (j >> 1) & 1u, failed) ||
-                    !wait_bar(&bars->o_empty[ob], ((j >> 1) & 1u) ^ 1u, failed)) {
+                const uint32_t qb = j & 1;
+                const uint32_t aQ = smem_u32(sQ0 + qb * kTileBytes);
+                if (!wait_bar(&bars->q_full[qb], (j >> 1) & 1u, failed)) {
                     ok = false;
                     break;
                 }
-                // P V of key tile kt (global tile count u): P from the softmax, V buffer u & 1.
-                auto issue_pv = [&](int kt, uint32_t u) -> bool {
-                    const uint32_t vb = u & 1;
-                    if (!wait_bar(&bars->v_full[vb], (u >> 1) & 1u, failed) || !wait_bar(&bars->p_full, u & 1u, failed))
-                        return false;
-                    fence_async_smem();
-                    fence_after();
-                    const uint32_t aV = smem_u32(sV0 + vb * kTileBytes);
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) {
-                        const uint32_t blk = static_cast<uint32_t>(kk >> 2) * kBlkBytes;
-                        const uint64_t step = 2ull * static_cast<uint64_t>(kk & 3);
-                        // P (K-major A, 16 keys per step), V rows (MN-major B, 2 KB per 16 rows)
-                        mma(tO, desc_kmajor(aP + blk) + step, desc_mnmajor(aV + static_cast<uint32_t>(kk) * 2048u),
-                            idesc_pv<kF16>(), (kt > 0 || kk > 0) ? 1 : 0);
-                    }
-                    commit(&bars->p_free);
-                    commit(&bars->v_empty[vb]);
-                    return true;
-                };
                 for (int kt = 0; kt < f.n_kt; ++kt) {
                     const uint32_t kb = ku & 1, use = (ku >> 1) & 1u;
                     if (!wait_bar(&bars->k_full[kb], use, failed) || !wait_bar(&bars->s_free[kb], use ^ 1u, failed)) {
@@ -550,19 +563,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(K3Params p
                     any = true;
                     commit(&bars->s_full[kb]);
                     commit(&bars->k_empty[kb]);
-                    if (kt == f.n_kt - 1) commit(&bars->q_empty[ob]);   // Q is read by S MMAs only
+                    if (kt == f.n_kt - 1) commit(&bars->q_empty[qb]);   // Q is read by S MMAs only
                     ++ku;
-                    if (kt > 0 && !issue_pv(kt - 1, ku - 2)) {
+                    if (!issue_pv()) {
                         ok = false;
                         break;
                     }
+                    pend = Pending{true, kt == f.n_kt - 1, kt, ku - 1, qb, j};
                 }
-                if (!ok || !issue_pv(f.n_kt - 1, ku - 1)) {
-                    ok = false;
-                    break;
-                }
-                commit(&bars->o_full[ob]);
             }
+            if (ok && !issue_pv()) ok = false;
             if (!ok) {
                 if (!*failed) report_error(p.err, kErrWaitTimeout, kWherePrefillAttn, blockIdx.x, 1 << 21);
                 *failed = 1;
