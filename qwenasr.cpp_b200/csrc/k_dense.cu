@@ -14,15 +14,45 @@ template <typename T> __device__ __forceinline__ void put(T *p, float v);
 template <> __device__ __forceinline__ void put<float>(float *p, float v) { *p = v; }
 template <> __device__ __forceinline__ void put<__nv_bfloat16>(__nv_bfloat16 *p, float v) { *p = __float2bfloat16_rn(v); }
 
+// Four outputs from a float4 (one 16-byte f32 or 8-byte bf16 store).
+template <typename T> __device__ __forceinline__ void put4(T *p, float4 v);
+template <> __device__ __forceinline__ void put4<float>(float *p, float4 v) { *reinterpret_cast<float4 *>(p) = v; }
+template <> __device__ __forceinline__ void put4<__nv_bfloat16>(__nv_bfloat16 *p, float4 v) {
+    *reinterpret_cast<uint2 *>(p) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+}
+
+// RMSNorm of one row per CTA (mean square accumulated in double, as the
+// scalar path does).  Rows whose width is a multiple of 4 and at most
+// 256 x 4 x kVec, with 16-byte aligned x and w, stay in registers between the
+// two passes (one read of x, 16-byte loads); others take the element loop.
 template <typename TOut>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const int *rows, int hidden, const float *w,
                                                       float eps, TOut *out) {
+    constexpr int kVec = 4;
     pdl_trigger();
     pdl_wait();   // everything below reads or writes memory of earlier kernels
     const int r = blockIdx.x;
     const float *xr = x + static_cast<size_t>(rows ? rows[r] : r) * hidden;
+    TOut *o = out + static_cast<size_t>(r) * hidden;
+    const bool vec = (hidden & 3) == 0 && hidden <= 256 * 4 * kVec &&
+                     ((reinterpret_cast<uintptr_t>(xr) | reinterpret_cast<uintptr_t>(w)) & 15u) == 0 &&
+                     (reinterpret_cast<uintptr_t>(o) & (4 * sizeof(TOut) - 1)) == 0;
+    const int n4 = hidden >> 2;
+    float4 v[kVec];
     double ss = 0.0;
-    for (int i = threadIdx.x; i < hidden; i += blockDim.x) ss += static_cast<double>(xr[i]) * xr[i];
+    if (vec) {
+#pragma unroll
+        for (int k = 0; k < kVec; ++k) {
+            const int i4 = threadIdx.x + 256 * k;
+            v[k] = i4 < n4 ? reinterpret_cast<const float4 *>(xr)[i4] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < kVec; ++k)
+            ss += static_cast<double>(v[k].x) * v[k].x + static_cast<double>(v[k].y) * v[k].y +
+                  static_cast<double>(v[k].z) * v[k].z + static_cast<double>(v[k].w) * v[k].w;
+    } else {
+        for (int i = threadIdx.x; i < hidden; i += blockDim.x) ss += static_cast<double>(xr[i]) * xr[i];
+    }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     __shared__ double part[8];
@@ -37,8 +67,21 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const int 
     }
     __syncthreads();
     const float scale = s_scale;
-    TOut *o = out + static_cast<size_t>(r) * hidden;
-    for (int i = threadIdx.x; i < hidden; i += blockDim.x) put<TOut>(o + i, __fmul_rn(__fmul_rn(xr[i], scale), w[i]));
+    if (vec) {
+#pragma unroll
+        for (int k = 0; k < kVec; ++k) {
+            const int i4 = threadIdx.x + 256 * k;
+            if (i4 < n4) {
+                const float4 wv = reinterpret_cast<const float4 *>(w)[i4];
+                put4<TOut>(o + 4 * i4, make_float4(__fmul_rn(__fmul_rn(v[k].x, scale), wv.x),
+                                                   __fmul_rn(__fmul_rn(v[k].y, scale), wv.y),
+                                                   __fmul_rn(__fmul_rn(v[k].z, scale), wv.z),
+                                                   __fmul_rn(__fmul_rn(v[k].w, scale), wv.w)));
+            }
+        }
+    } else {
+        for (int i = threadIdx.x; i < hidden; i += blockDim.x) put<TOut>(o + i, __fmul_rn(__fmul_rn(xr[i], scale), w[i]));
+    }
 }
 
 template <typename TW>

@@ -406,14 +406,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if (n < p.N) {
                     float *dst = p.C + static_cast<size_t>(m0 + c) * p.N + n;
                     const int mlim = p.M - (m0 + c);
+                    if (!split && p.accumulate) {
+                        // Read the chunk's 32 C values first (one memory latency, not 32:
+                        // the compiler cannot tell that the strided addresses differ).
+                        float old[32];
 #pragma unroll
-                    for (int jj = 0; jj < 32; ++jj) {
-                        if (jj < mlim) {
-                            const float v = __uint_as_float(r[jj]);
-                            float *dp = dst + static_cast<size_t>(jj) * p.N;
-                            if (split) atomicAdd(dp, v);
-                            else if (p.accumulate) *dp += v;
-                            else *dp = v;
+                        for (int jj = 0; jj < 32; ++jj)
+                            old[jj] = jj < mlim ? dst[static_cast<size_t>(jj) * p.N] : 0.0f;
+#pragma unroll
+                        for (int jj = 0; jj < 32; ++jj)
+                            if (jj < mlim) dst[static_cast<size_t>(jj) * p.N] = old[jj] + __uint_as_float(r[jj]);
+                    } else {
+#pragma unroll
+                        for (int jj = 0; jj < 32; ++jj) {
+                            if (jj < mlim) {
+                                const float v = __uint_as_float(r[jj]);
+                                float *dp = dst + static_cast<size_t>(jj) * p.N;
+                                if (split) atomicAdd(dp, v);
+                                else *dp = v;
+                            }
                         }
                     }
                 }
