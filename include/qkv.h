@@ -127,6 +127,15 @@ int qkv_compact(qkv_handle *h, int64_t *moved);
 int qkv_prefill(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *lens,
                 const float *embeddings, int32_t *out_ids, float *out_logits);
 
+/* qkv_prefill with each stream's prompt rows in a block of its own:
+ * embeddings[i] points to lens[i] x hidden f32 host values, so a caller that
+ * holds one array per request need not first copy them into one block.  The
+ * rows reach the device through the handle's pinned chunks, filled by several
+ * host threads (as in qkv_prefill).  The same operation as the prefill half of
+ * text_decoder_backend_cached_logits (text-decoder.cpp:1641-1755). */
+int qkv_prefill_rows(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *lens,
+                     const float *const *embeddings, int32_t *out_ids, float *out_logits);
+
 /* One greedy decode step for n streams: embed in_ids (NULL = each stream's
  * last greedy id kept on the device), run all layers appending one token per
  * stream, and write the next greedy ids to out_ids[n] (first maximum, as

@@ -61,6 +61,7 @@ SIGNATURES = {
     "qkv_pool_stats": (C.c_int, [_P, _I64P, _I64P]),
     "qkv_compact": (C.c_int, [_P, _I64P]),
     "qkv_prefill": (C.c_int, [_P, C.c_int32, _I32P, _I32P, _F32P, _I32P, _F32P]),
+    "qkv_prefill_rows": (C.c_int, [_P, C.c_int32, _I32P, _I32P, _P, _I32P, _F32P]),
     "qkv_decode_step": (C.c_int, [_P, C.c_int32, _I32P, _I32P, _I32P, _F32P]),
     "qkv_generate": (C.c_int, [_P, _F32P, C.c_int32, C.c_int32, _I32P, C.c_int32, _I32P, _I32P, _I32P]),
     "qkv_layer_forward": (C.c_int, [_P, C.c_int32, C.c_int32, _F32P, _F32P]),
@@ -240,12 +241,14 @@ class Decoder:
     def prefill(self, streams, prompts: list[np.ndarray], want_logits=False):
         streams = _i32(streams)
         lens = _i32([p.shape[0] for p in prompts])
-        emb = np.ascontiguousarray(np.concatenate(prompts, axis=0), np.float32)
+        # one block per stream (no concatenation); each must be C-contiguous f32
+        blocks = [np.ascontiguousarray(p, np.float32) for p in prompts]
+        ptrs = (C.c_void_p * max(len(blocks), 1))(*[b.ctypes.data for b in blocks])
         ids = np.zeros(len(streams), np.int32)
         logits = np.zeros((len(streams), self.cfg["vocab"]), np.float32) if want_logits else None
-        self._check(lib.qkv_prefill(self.h, len(streams), _ptr(streams, C.c_int32), _ptr(lens, C.c_int32),
-                                    _ptr(emb, C.c_float), _ptr(ids, C.c_int32),
-                                    _ptr(logits, C.c_float) if want_logits else None))
+        self._check(lib.qkv_prefill_rows(self.h, len(streams), _ptr(streams, C.c_int32), _ptr(lens, C.c_int32),
+                                         ptrs, _ptr(ids, C.c_int32),
+                                         _ptr(logits, C.c_float) if want_logits else None))
         return (ids, logits) if want_logits else ids
 
     def decode_step(self, streams, in_ids=None, want_logits=False):

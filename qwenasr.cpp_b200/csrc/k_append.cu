@@ -177,23 +177,32 @@ __global__ void __launch_bounds__(256) fp8_page_scale_kernel(AppendParams p) {
         return;
     }
     float amax = 0.0f;
-    for (int r = 0; r < cnt; ++r) {
-        const int row = row0 + r;
-        const int pos = p.positions[row];
-        const int src_off = kQDim + kv * kKvDim + g * kHeadDim + l16 * 8;
-        const float *src = p.qkv + static_cast<size_t>(row) * kQkvDim + src_off;
-        float x[8];
-        const float4 a = reinterpret_cast<const float4 *>(src)[0];
-        const float4 b = reinterpret_cast<const float4 *>(src)[1];
-        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
-        x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-        if (kv == 0) {   // warp-uniform: warps 0..3 hold K units
-            const int safe_pos = pos >= 0 && pos < p.rope_len ? pos : 0;
-            norm_rope8(x, p.k_norm_w + l16 * 8, p.rope + static_cast<size_t>(safe_pos) * (kHeadDim / 2) + (l16 & 7) * 8,
-                       l16, p.eps);
+    // The group's rows hold positions pos0 .. pos0 + cnt - 1.  Rows are loaded
+    // four at a time before any is normalised (a batch past the group's end
+    // repeats its last row, which leaves the maximum unchanged).
+    const int src_off = kQDim + kv * kKvDim + g * kHeadDim + l16 * 8;
+    for (int r0 = 0; r0 < cnt; r0 += 4) {
+        float x[4][8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int r = r0 + k < cnt ? r0 + k : cnt - 1;
+            const float *src = p.qkv + static_cast<size_t>(row0 + r) * kQkvDim + src_off;
+            const float4 a = reinterpret_cast<const float4 *>(src)[0];
+            const float4 b = reinterpret_cast<const float4 *>(src)[1];
+            x[k][0] = a.x; x[k][1] = a.y; x[k][2] = a.z; x[k][3] = a.w;
+            x[k][4] = b.x; x[k][5] = b.y; x[k][6] = b.z; x[k][7] = b.w;
         }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(x[j]));
+        for (int k = 0; k < 4; ++k) {
+            if (kv == 0) {   // warp-uniform: warps 0..3 hold K units
+                const int pos = pos0 + (r0 + k < cnt ? r0 + k : cnt - 1);
+                const int safe_pos = pos < p.rope_len ? pos : 0;
+                norm_rope8(x[k], p.k_norm_w + l16 * 8,
+                           p.rope + static_cast<size_t>(safe_pos) * (kHeadDim / 2) + (l16 & 7) * 8, l16, p.eps);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(x[k][j]));
+        }
     }
 #pragma unroll
     for (int o = 8; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));

@@ -9,6 +9,7 @@
 #include <functional>
 #include <memory>
 #include <mutex>
+#include <thread>
 #include <vector>
 
 #include "gguf.h"
@@ -159,6 +160,12 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
     CK(cudaEventCreateWithFlags(&h->items_ev, cudaEventDisableTiming));
     CK(cudaMalloc(&h->d_out_ids, R * sizeof(int)));
     CK(cudaMallocHost(&h->h_out_ids, R * sizeof(int)));
+    if (with_model_scratch) {
+        for (int i = 0; i < qkv_handle::kEmbRing; ++i) {
+            CK(cudaMallocHost(&h->h_emb[i], qkv_handle::kEmbChunkBytes));
+            CK(cudaEventCreateWithFlags(&h->emb_ev[i], cudaEventDisableTiming));
+        }
+    }
     h->max_items = (h->max_rows / 64 + h->rt.max_streams + 1) * kHkv;
     CK(cudaMalloc(&h->d_items, static_cast<size_t>(h->max_items) * sizeof(int4)));
     CK(cudaMallocHost(&h->h_items, static_cast<size_t>(h->max_items) * sizeof(int4)));
@@ -200,6 +207,10 @@ void destroy(qkv_handle *h) {
     cudaFree(h->d_rowbuf); cudaFree(h->d_out_ids); cudaFree(h->d_items); cudaFree(h->part_o); cudaFree(h->part_ml);
     cudaFree(h->counters); cudaFree(h->d_err);
     cudaFreeHost(h->h_page_table); cudaFreeHost(h->h_items); cudaFreeHost(h->h_rowbuf); cudaFreeHost(h->h_out_ids); cudaFreeHost(h->h_err);
+    for (int i = 0; i < qkv_handle::kEmbRing; ++i) {
+        cudaFreeHost(h->h_emb[i]);
+        if (h->emb_ev[i]) cudaEventDestroy(h->emb_ev[i]);
+    }
     for (auto &kv : h->decode_graphs) cudaGraphExecDestroy(kv.second.exec);
     for (auto &kv : h->kv_graphs) cudaGraphExecDestroy(kv.second.exec);
     for (auto &ev : h->row_ev) {
@@ -428,6 +439,72 @@ int *row_stage(qkv_handle *h) {
 int row_upload(qkv_handle *h, const int *host, size_t count, cudaStream_t st) {
     CK(cudaMemcpyAsync(h->d_rowbuf, host, count * sizeof(int), cudaMemcpyHostToDevice, st));
     CK(cudaEventRecord(h->row_ev[h->row_slot], st));
+    return QKV_OK;
+}
+
+// Prompt rows (stream i: rows[i], lens[i] rows of `row_floats` f32, host
+// memory) -> dst (device, rows back to back) through the pinned chunk ring.
+// Each chunk is filled by up to kFillThreads threads (byte ranges of equal
+// size, across row-block boundaries) and sent with one asynchronous copy, so
+// the fill of one chunk overlaps the copy of the other.
+int upload_prompt_rows(qkv_handle *h, float *dst, int n, const float *const *rows, const int32_t *lens,
+                       int row_floats, cudaStream_t st) {
+    constexpr int kFillThreads = 8;
+    constexpr size_t kBytesPerThread = size_t(1) << 20;
+    const size_t row_bytes = static_cast<size_t>(row_floats) * sizeof(float);
+    if (row_bytes == 0 || row_bytes > qkv_handle::kEmbChunkBytes || !h->h_emb[0])
+        return fail(h, QKV_ERR_STATE, "prompt staging: no pinned chunks or rows wider than a chunk");
+    struct Seg {
+        const uint8_t *src;
+        size_t bytes, off;   // off: byte offset inside the chunk
+    };
+    std::vector<Seg> segs;
+    size_t dst_off = 0;   // bytes of dst written so far
+    int i = 0;
+    size_t in_row = 0;    // bytes of stream i already taken
+    while (i < n) {
+        // gather up to one chunk of whole rows (at least one row)
+        segs.clear();
+        size_t fill = 0;
+        while (i < n) {
+            const size_t total_i = static_cast<size_t>(lens[i]) * row_bytes;
+            const size_t room = (qkv_handle::kEmbChunkBytes - fill) / row_bytes * row_bytes;
+            if (room == 0) break;
+            const size_t take = std::min(total_i - in_row, room);
+            if (take > 0) segs.push_back({reinterpret_cast<const uint8_t *>(rows[i]) + in_row, take, fill});
+            fill += take;
+            in_row += take;
+            if (in_row == total_i) {
+                ++i;
+                in_row = 0;
+            }
+        }
+        if (fill == 0) break;
+        const int slot = h->emb_slot;
+        h->emb_slot = (slot + 1) % qkv_handle::kEmbRing;
+        CK(cudaEventSynchronize(h->emb_ev[slot]));
+        uint8_t *chunk = reinterpret_cast<uint8_t *>(h->h_emb[slot]);
+        auto copy_range = [&](size_t lo, size_t hi) {   // chunk bytes [lo, hi)
+            for (const Seg &g : segs) {
+                const size_t a = std::max(lo, g.off), b = std::min(hi, g.off + g.bytes);
+                if (a < b) std::memcpy(chunk + a, g.src + (a - g.off), b - a);
+            }
+        };
+        const int nt = static_cast<int>(std::min<size_t>(kFillThreads, std::max<size_t>(1, fill / kBytesPerThread)));
+        if (nt == 1) {
+            copy_range(0, fill);
+        } else {
+            std::vector<std::thread> pool;
+            const size_t per = (fill + nt - 1) / nt;
+            for (int t = 1; t < nt; ++t)
+                pool.emplace_back(copy_range, std::min(fill, per * t), std::min(fill, per * (t + 1)));
+            copy_range(0, std::min(fill, per));
+            for (auto &th : pool) th.join();
+        }
+        CK(cudaMemcpyAsync(reinterpret_cast<uint8_t *>(dst) + dst_off, chunk, fill, cudaMemcpyHostToDevice, st));
+        CK(cudaEventRecord(h->emb_ev[slot], st));
+        dst_off += fill;
+    }
     return QKV_OK;
 }
 
@@ -853,11 +930,10 @@ int qkv_compact(qkv_handle *h, int64_t *moved) {
     return QKV_OK;
 }
 
-int qkv_prefill(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *lens, const float *embeddings,
-                int32_t *out_ids, float *out_logits) {
-    if (!h) return QKV_ERR_INVALID_ARG;
-    if (!h->has_weights) return fail(h, QKV_ERR_STATE, "handle has no model weights");
-    if (!lens || !embeddings) return fail(h, QKV_ERR_INVALID_ARG, "null lens or embeddings");
+// Shared body of qkv_prefill (one contiguous embedding block) and
+// qkv_prefill_rows (one block per stream): rows[i] = stream i's prompt rows.
+static int prefill_impl(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *lens,
+                        const float *const *rows, int32_t *out_ids, float *out_logits) {
     int rc;
     if ((rc = check_streams(h, n, stream_ids))) return rc;
     int64_t total = 0;
@@ -883,8 +959,7 @@ int qkv_prefill(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32
     if ((rc = grow_streams(h, n, stream_ids, lens, h->stream))) return rc;
     int *ds = h->d_rowbuf, *dp = ds + T, *dr = dp + T;
     if ((rc = row_upload(h, hs, static_cast<size_t>(2 * T + n), h->stream))) return rc;
-    CK(cudaMemcpyAsync(h->x, embeddings, static_cast<size_t>(T) * h->cfg.hidden * sizeof(float), cudaMemcpyHostToDevice,
-                       h->stream));
+    if ((rc = upload_prompt_rows(h, h->x, n, rows, lens, h->cfg.hidden, h->stream))) return rc;
     int n_items = 0;
     std::vector<int> base(static_cast<size_t>(n));
     for (int i = 0; i < n; ++i) base[static_cast<size_t>(i)] = hp[t_first(i, lens)];
@@ -892,6 +967,31 @@ int qkv_prefill(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32
     if ((rc = run_layers(h, T, ds, dp, nullptr, true, 0, -1, h->d_items, n_items))) return rc;
     if ((rc = head_and_argmax(h, n, dr))) return rc;
     return finish_ids(h, n, stream_ids, out_ids, out_logits);
+}
+
+int qkv_prefill(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *lens, const float *embeddings,
+                int32_t *out_ids, float *out_logits) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    if (!h->has_weights) return fail(h, QKV_ERR_STATE, "handle has no model weights");
+    if (!lens || !embeddings) return fail(h, QKV_ERR_INVALID_ARG, "null lens or embeddings");
+    if (n < 0) return fail(h, QKV_ERR_INVALID_ARG, "negative stream count");
+    std::vector<const float *> rows(static_cast<size_t>(n));
+    size_t off = 0;
+    for (int i = 0; i < n; ++i) {
+        rows[static_cast<size_t>(i)] = embeddings + off;
+        off += static_cast<size_t>(lens[i] > 0 ? lens[i] : 0) * h->cfg.hidden;
+    }
+    return prefill_impl(h, n, stream_ids, lens, rows.data(), out_ids, out_logits);
+}
+
+int qkv_prefill_rows(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *lens,
+                     const float *const *embeddings, int32_t *out_ids, float *out_logits) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    if (!h->has_weights) return fail(h, QKV_ERR_STATE, "handle has no model weights");
+    if (!lens || !embeddings) return fail(h, QKV_ERR_INVALID_ARG, "null lens or embeddings");
+    for (int i = 0; i < n; ++i)
+        if (!embeddings[i]) return fail(h, QKV_ERR_INVALID_ARG, "null embedding rows for a stream");
+    return prefill_impl(h, n, stream_ids, lens, embeddings, out_ids, out_logits);
 }
 
 int qkv_decode_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *in_ids, int32_t *out_ids,

@@ -68,6 +68,14 @@ struct qkv_handle {
     cudaEvent_t row_ev[kRowRing] = {};   // recorded after the copy out of each slot
     cudaEvent_t items_ev = nullptr;      // recorded after the copy out of h_items
     int row_slot = 0;
+    // Prompt embeddings go to the device through kEmbRing pinned chunks of
+    // kEmbChunkBytes: host threads fill a chunk, one asynchronous copy moves
+    // it, and a chunk is refilled only after its copy has run (its event).
+    static constexpr int kEmbRing = 2;
+    static constexpr size_t kEmbChunkBytes = size_t(16) << 20;
+    float *h_emb[kEmbRing] = {};
+    cudaEvent_t emb_ev[kEmbRing] = {};
+    int emb_slot = 0;
     int *d_out_ids = nullptr;   // [max_rows]
     int *h_out_ids = nullptr;   // pinned
     int4 *d_items = nullptr;    // prefill attention work items

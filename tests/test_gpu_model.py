@@ -257,3 +257,34 @@ def test_bf16_prefill_logits_multi_stream(pkg, synth, checker, tiny_files):
     for i, x in enumerate(xs):
         ref = om.prefill_logits(x)
         assert rel_err(logits[i], ref) < 3e-2
+
+
+def test_prefill_rows_entry_matches_contiguous(pkg, synth, tiny_files):
+    """qkv_prefill_rows (one host block per stream, what Decoder.prefill
+    passes) and qkv_prefill (one contiguous block) give identical ids and
+    logits.  40 prompts of 700-1300 rows x 1 KB span several of the handle's
+    16 MB pinned staging chunks, with streams split across chunk edges."""
+    import ctypes as C
+    cfg, files = tiny_files
+    path = files[("bf16", "one_plus")]
+    tensors = synth.read_gguf(path)
+    xs = prompts(synth, tensors, 40, 900, lo=700, hi=1300)
+    total = sum(x.shape[0] for x in xs)
+    assert total * cfg["hidden"] * 4 > 2 * (16 << 20)
+    with decoder(pkg, path, w=1, kv=1, streams=80, ctx=1400, batch_tokens=total) as dec:
+        s_rows = [dec.open() for _ in xs]
+        ids_rows, logits_rows = dec.prefill(s_rows, xs, want_logits=True)
+        for s in s_rows:
+            dec.close_stream(s)
+        s_cat = np.array([dec.open() for _ in xs], np.int32)
+        lens = np.array([x.shape[0] for x in xs], np.int32)
+        emb = np.ascontiguousarray(np.concatenate(xs, axis=0), np.float32)
+        ids_cat = np.zeros(len(xs), np.int32)
+        logits_cat = np.zeros((len(xs), dec.cfg["vocab"]), np.float32)
+        i32 = C.POINTER(C.c_int32)
+        f32 = C.POINTER(C.c_float)
+        rc = pkg.lib.qkv_prefill(dec.h, len(xs), s_cat.ctypes.data_as(i32), lens.ctypes.data_as(i32),
+                                 emb.ctypes.data_as(f32), ids_cat.ctypes.data_as(i32), logits_cat.ctypes.data_as(f32))
+        assert rc == 0
+    assert np.array_equal(ids_rows, ids_cat)
+    assert np.array_equal(logits_rows, logits_cat)
