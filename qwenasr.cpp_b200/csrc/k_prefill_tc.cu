@@ -328,8 +328,9 @@ __device__ __forceinline__ ItemInfo item_info(const K3Params &p, int it) {
     return f;
 }
 
-// Persistent: CTA c takes items c, c + G, c + 2G, ... (the host orders items
-// longest first).  Every barrier phase follows from per-role counters that
+// Persistent: CTA c takes items c, c + G, c + 2G, ... (the host puts the
+// items of one (stream, kv head) pair back to back, longest first, so a pair's
+// query blocks run together on neighbouring CTAs and share its K/V in L2).  Every barrier phase follows from per-role counters that
 // run on across items: item j uses the Q tile and O buffer j & 1; key tile u
 // (global count) uses K, V and S buffers u & 1 and the single P tile; the
 // softmax threads' x-th row hand-over (each tile's max, each item's sum) uses

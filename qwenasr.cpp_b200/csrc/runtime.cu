@@ -373,19 +373,47 @@ static int t_first(int i, const int32_t *lens) {
 int upload_items(qkv_handle *h, int n, const int32_t *lens, const int *base, int *n_items, cudaStream_t st) {
     // h_items is rewritten only after the copy that last read it has run.
     cudaEventSynchronize(h->items_ev);
-    int k = 0, row = 0;
+    // Item order (the persistent K3 CTAs take items round-robin): the items of
+    // one (stream, kv head) pair back to back, longest first, pairs of the
+    // longest streams first.  A pair's query blocks then run at the same time
+    // on neighbouring CTAs and share its K/V tiles through L2, and each CTA
+    // still sees every block length in turn.  QWENASR_B200_K3_ORDER=lpt keeps
+    // the plain longest-first order over all items (the earlier schedule).
+    static const bool lpt = [] {
+        const char *e = std::getenv("QWENASR_B200_K3_ORDER");
+        return e && std::strcmp(e, "lpt") == 0;
+    }();
+    struct Tagged {
+        int total, stream, g;
+        int4 it;
+    };
+    std::vector<Tagged> v;
+    int row = 0;
     for (int i = 0; i < n; ++i) {
+        const int total = (base ? base[i] : 0) + lens[i];
         for (int q0 = 0; q0 < lens[i]; q0 += 64) {
             const int nq = std::min(64, lens[i] - q0);
             const int keys = (base ? base[i] : 0) + q0 + nq;
             for (int g = 0; g < kHkv; ++g) {
-                if (k >= h->max_items) return fail(h, QKV_ERR_CAPACITY, "too many prefill attention items");
-                h->h_items[k++] = make_int4(row + q0, nq, g, keys);
+                if (static_cast<int>(v.size()) >= h->max_items)
+                    return fail(h, QKV_ERR_CAPACITY, "too many prefill attention items");
+                v.push_back({total, i, g, make_int4(row + q0, nq, g, keys)});
             }
         }
         row += lens[i];
     }
-    std::stable_sort(h->h_items, h->h_items + k, [](const int4 &a, const int4 &b) { return a.w > b.w; });
+    if (lpt) {
+        std::stable_sort(v.begin(), v.end(), [](const Tagged &a, const Tagged &b) { return a.it.w > b.it.w; });
+    } else {
+        std::stable_sort(v.begin(), v.end(), [](const Tagged &a, const Tagged &b) {
+            if (a.total != b.total) return a.total > b.total;
+            if (a.stream != b.stream) return a.stream < b.stream;
+            if (a.g != b.g) return a.g < b.g;
+            return a.it.w > b.it.w;
+        });
+    }
+    const int k = static_cast<int>(v.size());
+    for (int j = 0; j < k; ++j) h->h_items[j] = v[static_cast<size_t>(j)].it;
     CK(cudaMemcpyAsync(h->d_items, h->h_items, static_cast<size_t>(k) * sizeof(int4), cudaMemcpyHostToDevice, st));
     CK(cudaEventRecord(h->items_ev, st));
     *n_items = k;
