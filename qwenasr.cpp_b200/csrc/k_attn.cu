@@ -166,7 +166,11 @@ __device__ __forceinline__ bool flag_wait(volatile int *flag, int want, volatile
 template <typename TC, typename TOut>
 __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendParams p) {
     pdl_trigger();
-    pdl_wait();   // everything below reads or writes memory of earlier kernels
+    // With p.early the set-up below (row arrays, page table: host copies that
+    // finished before the preceding kernels) and the copies of pages other
+    // than a row's last run before the grid dependency wait; the producer waits
+    // before a row's last page, the consumers before q and the merge scratch.
+    if (!p.early) pdl_wait();
     constexpr int CH = AttnTraits<TC>::CH;
     constexpr int NS = AttnTraits<TC>::NS;
     constexpr int kHalves = AttnTraits<TC>::HALVES;
@@ -271,11 +275,13 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
         const TC *pool = static_cast<const TC *>(p.pool);
         int iter = 0;
         bool abort = false;
+        bool waited = !p.early;
         int r = r0;
         int64_t gp = pb;
         while (gp < pe && !abort) {
             while (row_start[r + 1] <= gp) ++r;
             const int rs = row_start[r];
+            const int row_pages = row_start[r + 1] - rs;
             const int j0 = static_cast<int>(gp - rs);
             const int j1 = static_cast<int>((pe < row_start[r + 1] ? pe : row_start[r + 1]) - rs);
             const int slot = p.slots[r];
@@ -300,6 +306,10 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
                 const int cntp = (j1 - jb) < 32 ? (j1 - jb) : 32;
                 for (int k = 0; k < cntp && !abort; ++k) {
                     const int page = __shfl_sync(0xffffffffu, pid, k);
+                    if (!waited && jb + k == row_pages - 1) {
+                        pdl_wait();   // the row's last page holds this step's token
+                        waited = true;
+                    }
 #pragma unroll 1
                     for (int cp = 0; cp < CPP; ++cp) {
                         const int s = iter % NS;
@@ -374,6 +384,7 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
     float *my_p = pbuf + warp * (2 * CH);
     TOut *out = static_cast<TOut *>(p.out);
 
+    if (p.early) pdl_wait();   // q and the merge scratch come from the preceding kernels
     int iter = 0;
     int nseg = 0;                                   // segments finished (both halves count alike)
     int r = r0;

@@ -86,6 +86,12 @@ struct AttendParams {
     int *counters;             // [n][kHkv], zero between launches
     float scale_log2;          // log2(e) / sqrt(head_dim)
     DevError *err;
+    // 1: the kernel(s) just before this launch on the stream wrote only each
+    // row's LAST page (one new token per row: K1, the e4m3 page-scale pass),
+    // and the row arrays and page table came from copies that finished before
+    // them, so K2 may set up and stream the other pages before its grid
+    // dependency wait.  0: everything waits (any caller).
+    int early;
 };
 
 struct PrefillAttnParams {

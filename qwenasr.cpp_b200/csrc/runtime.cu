@@ -632,6 +632,7 @@ int layer_kv(qkv_handle *h, int layer, int n, const int *slots, const int *pos, 
     AppendParams ap = append_params(h, layer, n, slots, pos, qkv, q, qn, kn);
     CK(launch_kv_append(ap, h->rt.kv_dtype, st));
     AttendParams at = attend_params(h, layer, n, slots, lens, q, out);
+    at.early = 1;   // K1 just appended one token per row (see AttendParams::early)
     CK(launch_decode_attn(at, h->rt.kv_dtype, out_bf16, h->num_sms, st));
     h->launches += 2;
     return QKV_OK;
