@@ -217,6 +217,11 @@ void destroy(qkv_handle *h) {
         if (ev) cudaEventDestroy(ev);
     }
     if (h->items_ev) cudaEventDestroy(h->items_ev);
+    for (cudaEvent_t ev : h->ev_in) cudaEventDestroy(ev);
+    for (cudaEvent_t ev : h->ev_done) cudaEventDestroy(ev);
+    if (h->ev_tail) cudaEventDestroy(h->ev_tail);
+    if (h->copy_in) cudaStreamDestroy(h->copy_in);
+    if (h->copy_out) cudaStreamDestroy(h->copy_out);
     if (h->stream) cudaStreamDestroy(h->stream);
     delete h->pager;
     delete h;
@@ -1281,27 +1286,79 @@ int qkv_kv_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const float
     return QKV_OK;
 }
 
+// Host-buffer KV step, pipelined by layer: layer l's inputs go up on
+// copy_in while earlier layers compute, layer l's kernels wait only for its own
+// inputs, and its outputs come back on copy_out as soon as its attention has
+// run, so PCIe traffic in both directions overlaps the kernels.
 int qkv_kv_step_host(qkv_handle *h, int32_t n, const int32_t *stream_ids, const float *qkv_host, float *out_host) {
     if (!h) return QKV_ERR_INVALID_ARG;
     if (!qkv_host || !out_host || n <= 0) return fail(h, QKV_ERR_INVALID_ARG, "null host pointer or empty batch");
+    int rc;
+    if ((rc = check_streams(h, n, stream_ids))) return rc;
+    if (n > kAttnMaxRows) return fail(h, QKV_ERR_CAPACITY, "kv_step batch larger than 1024 rows");
     CK(cudaSetDevice(h->device));
-    const size_t in_elems = static_cast<size_t>(h->cfg.n_layers) * n * kQkvDim;
-    const size_t out_elems = static_cast<size_t>(h->cfg.n_layers) * n * kQDim;
+    const int L = h->cfg.n_layers;
+    const size_t in_stride = static_cast<size_t>(n) * kQkvDim, out_stride = static_cast<size_t>(n) * kQDim;
+    const size_t in_elems = in_stride * L, out_elems = out_stride * L;
     const size_t need = (in_elems + out_elems) * sizeof(float);
     if (need > h->host_stage_bytes) {   // device staging, grown on demand and kept
-        CK(cudaStreamSynchronize(h->stream));
+        CK(cudaDeviceSynchronize());
         cudaFree(h->host_stage);
         h->host_stage = nullptr;
         h->host_stage_bytes = 0;
         CK(cudaMalloc(&h->host_stage, need));
         h->host_stage_bytes = need;
     }
-    float *stage = h->host_stage;
-    CK(cudaMemcpyAsync(stage, qkv_host, in_elems * sizeof(float), cudaMemcpyHostToDevice, h->stream));
-    int rc = qkv_kv_step(h, n, stream_ids, stage, stage + in_elems, h->stream);
-    if (rc == QKV_OK) {
-        CK(cudaMemcpyAsync(out_host, stage + in_elems, out_elems * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+    if (!h->copy_in) {
+        CK(cudaStreamCreateWithFlags(&h->copy_in, cudaStreamNonBlocking));
+        CK(cudaStreamCreateWithFlags(&h->copy_out, cudaStreamNonBlocking));
+        CK(cudaEventCreateWithFlags(&h->ev_tail, cudaEventDisableTiming));
     }
+    while (static_cast<int>(h->ev_in.size()) < L) {
+        cudaEvent_t a = nullptr, b = nullptr;
+        CK(cudaEventCreateWithFlags(&a, cudaEventDisableTiming));
+        CK(cudaEventCreateWithFlags(&b, cudaEventDisableTiming));
+        h->ev_in.push_back(a);
+        h->ev_done.push_back(b);
+    }
+    float *stage_in = h->host_stage, *stage_out = h->host_stage + in_elems;
+    // Rows: as qkv_kv_step (one appended token per stream).
+    int *hs = row_stage(h), *hp = hs + n, *hl = hp + n;
+    for (int i = 0; i < n; ++i) {
+        const int len = stream_len(h, stream_ids[i]);
+        if (len + 1 > h->rt.max_context) return fail(h, QKV_ERR_CAPACITY, "stream reached max_context");
+        hs[i] = stream_ids[i];
+        hp[i] = len;
+        hl[i] = len + 1;
+    }
+    if ((rc = grow_streams(h, n, stream_ids, nullptr, h->stream))) return rc;
+    int *ds = h->d_rowbuf, *dp = ds + n, *dl = dp + n;
+    if ((rc = row_upload(h, hs, static_cast<size_t>(3 * n), h->stream))) return rc;
+    // The staging is free once the work queued so far on h->stream has run
+    // (earlier calls' kernels and output copies end there).
+    CK(cudaEventRecord(h->ev_tail, h->stream));
+    CK(cudaStreamWaitEvent(h->copy_in, h->ev_tail, 0));
+    for (int l = 0; l < L; ++l) {
+        CK(cudaMemcpyAsync(stage_in + in_stride * l, qkv_host + in_stride * l, in_stride * sizeof(float),
+                           cudaMemcpyHostToDevice, h->copy_in));
+        CK(cudaEventRecord(h->ev_in[static_cast<size_t>(l)], h->copy_in));
+    }
+    for (int l = 0; l < L; ++l) {
+        const qkv_handle::Layer &Ly = h->layers[static_cast<size_t>(l)];
+        CK(cudaStreamWaitEvent(h->stream, h->ev_in[static_cast<size_t>(l)], 0));
+        if ((rc = layer_kv(h, l, n, ds, dp, dl, stage_in + in_stride * l, h->q, stage_out + out_stride * l, false,
+                           Ly.q_norm, Ly.k_norm, h->stream)))
+            break;
+        CK(cudaEventRecord(h->ev_done[static_cast<size_t>(l)], h->stream));
+        CK(cudaStreamWaitEvent(h->copy_out, h->ev_done[static_cast<size_t>(l)], 0));
+        CK(cudaMemcpyAsync(out_host + out_stride * l, stage_out + out_stride * l, out_stride * sizeof(float),
+                           cudaMemcpyDeviceToHost, h->copy_out));
+    }
+    // Every copy of this call has run before the status read below returns.
+    CK(cudaEventRecord(h->ev_tail, h->copy_out));
+    CK(cudaStreamWaitEvent(h->stream, h->ev_tail, 0));
+    CK(cudaEventRecord(h->ev_tail, h->copy_in));
+    CK(cudaStreamWaitEvent(h->stream, h->ev_tail, 0));
     const int rc2 = check_device_error(h);
     return rc ? rc : rc2;
 }

@@ -76,6 +76,11 @@ struct qkv_handle {
     float *h_emb[kEmbRing] = {};
     cudaEvent_t emb_ev[kEmbRing] = {};
     int emb_slot = 0;
+    // qkv_kv_step_host's per-layer pipeline: inputs go up on copy_in, outputs
+    // come back on copy_out, one event per layer each way (created on first use).
+    cudaStream_t copy_in = nullptr, copy_out = nullptr;
+    std::vector<cudaEvent_t> ev_in, ev_done;
+    cudaEvent_t ev_tail = nullptr;
     int *d_out_ids = nullptr;   // [max_rows]
     int *h_out_ids = nullptr;   // pinned
     int4 *d_items = nullptr;    // prefill attention work items

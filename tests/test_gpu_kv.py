@@ -226,18 +226,46 @@ def test_kv_step_matches_oracle(pkg, checker):
         assert [dec.length(s) for s in streams] == (lens0 + 3).tolist()
 
 
-def test_kv_step_host_matches_device(pkg):
-    dec, qn, kn = kv_handle(pkg, 1, n_layers=2, seed=2, max_streams=3, max_context=256)
-    with dec:
-        rng = np.random.default_rng(12)
-        streams = [dec.open() for _ in range(3)]
-        for s, L in zip(streams, (10, 100, 33)):
-            dec.extend(s, L)
-        dec.fill_random(5)
-        qkv = rng.standard_normal((2, 3, QKV), dtype=np.float32)
-        out_h = np.zeros((2, 3, HQ * D), np.float32)
-        dec.kv_step_host(streams, qkv.ctypes.data, out_h.ctypes.data)
-        assert np.isfinite(out_h).all() and np.abs(out_h).max() > 0
+@pytest.mark.parametrize("kv_dtype", [1, 2])
+def test_kv_step_host_matches_device(pkg, kv_dtype):
+    """qkv_kv_step_host (host buffers; copies pipelined by layer on two copy
+    streams) gives bit-identical output to qkv_kv_step on device buffers, over
+    two consecutive steps (the device staging is reused) with pinned and with
+    pageable host buffers."""
+    lens = (10, 100, 33, 700, 1, 16, 17, 250)
+    results = {}
+    for mode in ("device", "pinned", "pageable"):
+        dec, qn, kn = kv_handle(pkg, kv_dtype, n_layers=4, seed=2, max_streams=8, max_context=1024)
+        with dec:
+            streams = [dec.open() for _ in lens]
+            for s, L in zip(streams, lens):
+                dec.extend(s, L)
+            dec.fill_random(5)
+            rng = np.random.default_rng(12)
+            outs = []
+            for _ in range(2):
+                qkv = rng.standard_normal((4, len(lens), QKV), dtype=np.float32)
+                if mode == "device":
+                    dq = torch.from_numpy(qkv).cuda()
+                    do = torch.zeros((4, len(lens), HQ * D), device="cuda")
+                    dec.kv_step(streams, dq.data_ptr(), do.data_ptr())
+                    torch.cuda.synchronize()
+                    dec.sync()
+                    outs.append(do.cpu().numpy())
+                elif mode == "pinned":
+                    hq = torch.from_numpy(qkv).pin_memory()
+                    ho = torch.zeros((4, len(lens), HQ * D)).pin_memory()
+                    dec.kv_step_host(streams, hq.data_ptr(), ho.data_ptr())
+                    outs.append(ho.numpy().copy())
+                else:
+                    out_h = np.zeros((4, len(lens), HQ * D), np.float32)
+                    dec.kv_step_host(streams, qkv.ctypes.data, out_h.ctypes.data)
+                    outs.append(out_h)
+            results[mode] = outs
+    for step in range(2):
+        assert np.isfinite(results["device"][step]).all() and np.abs(results["device"][step]).max() > 0
+        assert np.array_equal(results["device"][step], results["pinned"][step])
+        assert np.array_equal(results["device"][step], results["pageable"][step])
 
 
 def test_device_error_on_bad_page_table_row(pkg):
