@@ -136,6 +136,29 @@ int qkv_prefill(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32
 int qkv_prefill_rows(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *lens,
                      const float *const *embeddings, int32_t *out_ids, float *out_logits);
 
+/* Decoder input on the device: the embedding lookup and audio-row splice of
+ * qwenasr_decoder_input_from_audio (src/decoder-input.cpp:64-98), after the
+ * prompt (src/tokenizer.cpp:529-549) has been tokenised by the caller.  For n
+ * prompts of lens[i] ids each (ids: sum lens int32, host), row t of the
+ * output is the embedding row of ids[t], or, where ids[t] == audio_token_id,
+ * the prompt's next audio row: audio[i] points to audio_tokens[i] x hidden
+ * f32 values, in host memory, or in device memory when audio_on_device (as
+ * an audio encoder on the GPU leaves them).  The same checks and messages as
+ * the reference, in its order (QKV_ERR_INVALID_ARG): an id outside the
+ * embedding table, more placeholders than audio rows, a count that differs.
+ * x_dev: sum lens x hidden f32 (device), written on `stream`.  The embedding
+ * rows are the handle's table (bf16-rounded in bf16 weight mode). */
+int qkv_decoder_input(qkv_handle *h, int32_t n, const int32_t *lens, const int32_t *ids,
+                      const float *const *audio, const int32_t *audio_tokens, int32_t audio_on_device,
+                      int32_t audio_token_id, float *x_dev, void *stream);
+
+/* qkv_prefill with the prompt rows built on the device by qkv_decoder_input
+ * (arguments as there): only the ids and the audio rows cross to the device,
+ * and nothing does when the audio rows are already there. */
+int qkv_prefill_ids(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *lens, const int32_t *ids,
+                    const float *const *audio, const int32_t *audio_tokens, int32_t audio_on_device,
+                    int32_t audio_token_id, int32_t *out_ids, float *out_logits);
+
 /* One greedy decode step for n streams: embed in_ids (NULL = each stream's
  * last greedy id kept on the device), run all layers appending one token per
  * stream, and write the next greedy ids to out_ids[n] (first maximum, as

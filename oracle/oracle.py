@@ -74,6 +74,7 @@ def lib():
         L.oracle_rope_cos_sin.argtypes = [C.c_int, C.c_int, C.c_int, C.c_float, _F, _F]
         L.oracle_argmax.argtypes = [_F, C.c_int]
         L.oracle_argmax.restype = C.c_int32
+        L.oracle_decoder_input.argtypes = [_I, C.c_int, _F, C.c_int, C.c_int, _F, C.c_int, C.c_int32, _F]
     return _lib
 
 
@@ -88,6 +89,8 @@ def ref_lib():
         _ref.ref_generate_cached.argtypes = [C.c_char_p, P, _F, C.c_int, C.c_int, _I, C.c_int, _I, _I, _I]
         _ref.ref_generate_greedy.argtypes = [C.c_char_p, P, _F, C.c_int, C.c_int, _I, _I]
         _ref.ref_layer_forward.argtypes = [C.c_char_p, P, C.c_int, _F, C.c_int, _F]
+        _ref.ref_decoder_input.argtypes = [C.c_char_p, C.c_int, C.c_int, _F, C.c_int, C.c_char_p, C.c_char_p, C.c_int,
+                                           _I, _F, C.POINTER(C.c_int)]
         _ref.ref_last_error.restype = C.c_char_p
     return _ref
 
@@ -261,3 +264,32 @@ class RefModel:
         out = np.zeros_like(x)
         self._chk(ref_lib().ref_layer_forward(self.path, C.byref(self.c), layer, _f(x), x.shape[0], _f(out)))
         return out
+
+
+def decoder_input(ids: np.ndarray, embd: np.ndarray, audio: np.ndarray, audio_token_id: int):
+    """(status, rows): the reference's splice (src/decoder-input.cpp:64-98);
+    status 0 ok, 1 id out of range, 2 more placeholders than audio rows,
+    3 placeholder count differs from the audio rows."""
+    ids = np.ascontiguousarray(ids, np.int32)
+    embd = np.ascontiguousarray(embd, np.float32)
+    audio = np.ascontiguousarray(audio, np.float32).reshape(-1, embd.shape[1])
+    out = np.zeros((ids.shape[0], embd.shape[1]), np.float32)
+    rc = lib().oracle_decoder_input(_i(ids), ids.shape[0], _f(embd), embd.shape[0], embd.shape[1], _f(audio),
+                                    audio.shape[0], int(audio_token_id), _f(out))
+    return rc, out
+
+
+def ref_decoder_input(gguf: str, audio: np.ndarray, audio_token_id: int, system_text: str = "",
+                      language: str = "", max_tokens: int = 8192):
+    """The reference's own qwenasr_decoder_input_from_audio on `gguf` (its
+    prompt template, tokenizer and splice): (status, ids, rows, message)."""
+    audio = np.ascontiguousarray(audio, np.float32)
+    ids = np.zeros(max_tokens, np.int32)
+    rows = np.zeros((max_tokens, audio.shape[1]), np.float32)
+    t = C.c_int(0)
+    rc = ref_lib().ref_decoder_input(str(gguf).encode(), audio.shape[0], audio.shape[1], _f(audio), int(audio_token_id),
+                                     system_text.encode(), language.encode(), max_tokens, _i(ids), _f(rows),
+                                     C.byref(t))
+    msg = ref_lib().ref_last_error().decode() if rc else ""
+    n = t.value if rc == 0 else 0
+    return rc, ids[:n].copy(), rows[:n].copy(), msg

@@ -457,3 +457,22 @@ int oracle_kv_step_batch(int n_streams, int n_layers, const float *qkv, const fl
     (void)n_threads;
     return 0;
 }
+
+/* src/decoder-input.cpp:64-98 (qwenasr_decoder_input_from_audio, after the
+ * prompt is tokenised): embedding copy, then the audio row over it. */
+int oracle_decoder_input(const int32_t *ids, int tokens, const float *embd, int vocab, int hidden,
+                         const float *audio, int audio_tokens, int32_t audio_token_id, float *out) {
+    int audio_positions = 0;
+    for (int t = 0; t < tokens; ++t) {
+        const int32_t id = ids[t];
+        if (id < 0 || id >= vocab) return 1;
+        float *dst = out + (size_t)t * hidden;
+        memcpy(dst, embd + (size_t)id * hidden, (size_t)hidden * sizeof(float));
+        if (id == audio_token_id) {
+            if (audio_positions >= audio_tokens) return 2;
+            memcpy(dst, audio + (size_t)audio_positions * hidden, (size_t)hidden * sizeof(float));
+            ++audio_positions;
+        }
+    }
+    return audio_positions == audio_tokens ? 0 : 3;
+}

@@ -113,6 +113,14 @@ void oracle_attend(const float *q, const float *k_cache, const float *v_cache, i
  * q_norm_w / k_norm_w: [n_layers][head_dim]; caches: per stream s a pointer to
  * [n_layers][capacity[s]][Hkv*D] for K and for V; lens: tokens already cached
  * (incremented); out: [n_layers][n_streams][Hq*D]. */
+/* Decoder input (src/decoder-input.cpp:64-98): row t of out = embedding row
+ * ids[t]; a row whose id is audio_token_id takes the next audio row instead
+ * (in order).  Checks as the reference does, in its order: 1 = an id outside
+ * [0, vocab), 2 = more placeholders than audio rows, 3 = fewer (the counts
+ * differ at the end); 0 = ok.  embd [vocab][hidden], audio [audio_tokens][hidden]. */
+int oracle_decoder_input(const int32_t *ids, int tokens, const float *embd, int vocab, int hidden,
+                         const float *audio, int audio_tokens, int32_t audio_token_id, float *out);
+
 int oracle_kv_step_batch(int n_streams, int n_layers, const float *qkv, const float *q_norm_w,
                          const float *k_norm_w, float *const *k_caches, float *const *v_caches,
                          const int *capacity, int *lens, int n_heads, int n_kv_heads, int head_dim,

@@ -24,6 +24,12 @@ struct gguf_context {
     std::vector<std::string> names;
     std::vector<size_t> offsets;
     size_t data_offset = 0;
+    // metadata: every key, with its u32 value (scalar u32 keys) and its
+    // strings (string arrays); other values are skipped
+    std::vector<std::string> keys;
+    std::vector<uint32_t> u32;
+    std::vector<std::vector<std::string>> strs;
+    std::vector<size_t> arr_n;
 };
 
 static size_t type_size(ggml_type t) {
@@ -197,25 +203,35 @@ gguf_context *gguf_init_from_file(const char *fname, gguf_init_params params) {
     const uint64_t n_kv = r.get<uint64_t>();
     if (!r.ok || version < 2 || version > 3) { std::fclose(f); return nullptr; }
     size_t alignment = 32;
+    gguf_context *g = new gguf_context();
     for (uint64_t i = 0; i < n_kv && r.ok; ++i) {
         const std::string key = r.str();
         const uint32_t t = r.get<uint32_t>();
+        uint32_t u = 0;
+        size_t an = 0;
+        std::vector<std::string> strs;
         if (t == 8) {
             r.str();
         } else if (t == 9) {
             const uint32_t at = r.get<uint32_t>();
             const uint64_t n = r.get<uint64_t>();
-            if (at == 8) { for (uint64_t k = 0; k < n && r.ok; ++k) r.str(); }
+            an = static_cast<size_t>(n);
+            if (at == 8) { for (uint64_t k = 0; k < n && r.ok; ++k) strs.push_back(r.str()); }
             else if (scalar_bytes(at)) r.skip(n * scalar_bytes(at));
             else r.ok = false;
+        } else if (t == 4) {
+            u = r.get<uint32_t>();
+            if (key == "general.alignment") alignment = u;
         } else if (scalar_bytes(t)) {
-            if (key == "general.alignment" && t == 4) alignment = r.get<uint32_t>();
-            else r.skip(scalar_bytes(t));
+            r.skip(scalar_bytes(t));
         } else {
             r.ok = false;
         }
+        g->keys.push_back(key);
+        g->u32.push_back(u);
+        g->strs.push_back(std::move(strs));
+        g->arr_n.push_back(an);
     }
-    gguf_context *g = new gguf_context();
     ggml_context *meta = ggml_init({0, nullptr, true});
     for (uint64_t i = 0; i < n_tensors && r.ok; ++i) {
         const std::string name = r.str();
@@ -252,6 +268,24 @@ size_t gguf_get_tensor_offset(const gguf_context *ctx, int64_t id) {
     return (ctx && id >= 0 && id < static_cast<int64_t>(ctx->offsets.size())) ? ctx->offsets[static_cast<size_t>(id)] : 0;
 }
 size_t gguf_get_data_offset(const gguf_context *ctx) { return ctx ? ctx->data_offset : 0; }
+int64_t gguf_find_key(const gguf_context *ctx, const char *key) {
+    if (!ctx || !key) return -1;
+    for (size_t i = 0; i < ctx->keys.size(); ++i) {
+        if (ctx->keys[i] == key) return static_cast<int64_t>(i);
+    }
+    return -1;
+}
+uint32_t gguf_get_val_u32(const gguf_context *ctx, int64_t id) {
+    return (ctx && id >= 0 && id < static_cast<int64_t>(ctx->u32.size())) ? ctx->u32[static_cast<size_t>(id)] : 0;
+}
+size_t gguf_get_arr_n(const gguf_context *ctx, int64_t id) {
+    return (ctx && id >= 0 && id < static_cast<int64_t>(ctx->arr_n.size())) ? ctx->arr_n[static_cast<size_t>(id)] : 0;
+}
+const char *gguf_get_arr_str(const gguf_context *ctx, int64_t id, size_t i) {
+    if (!ctx || id < 0 || id >= static_cast<int64_t>(ctx->strs.size())) return nullptr;
+    const auto &v = ctx->strs[static_cast<size_t>(id)];
+    return i < v.size() ? v[i].c_str() : nullptr;
+}
 int64_t gguf_find_tensor(const gguf_context *ctx, const char *name) {
     if (!ctx || !name) return -1;
     for (size_t i = 0; i < ctx->names.size(); ++i) {

@@ -1,13 +1,16 @@
 // Test infrastructure: extern "C" entry points into the reference's own
-// scalar text-decoder functions (src/text-decoder.h), for ctypes.  Each call
+// scalar text-decoder functions (src/text-decoder.h) and its decoder-input
+// assembly (src/decoder-input.h, with src/tokenizer.cpp), for ctypes.  Each call
 // opens the GGUF with the reference's loader (src/gguf-model.cpp) and runs
 // the reference function unchanged.
 #include <cstring>
 #include <string>
 #include <vector>
 
+#include "decoder-input.h"
 #include "gguf-model.h"
 #include "text-decoder.h"
+#include "tokenizer.h"
 
 namespace {
 std::string g_error;
@@ -91,4 +94,42 @@ int ref_layer_forward(const char *gguf, const Cfg *c, int layer, const float *x,
     return ok ? 0 : 2;
 }
 
+// qwenasr_decoder_input_from_audio (decoder-input.cpp:26-101): prompt template
+// + tokenizer (from the same GGUF) + embedding rows with the audio rows
+// spliced in.  out_ids / out_values must hold max_tokens rows; *tokens gets
+// the prompt length (also when it exceeds max_tokens, with return 3).
+int ref_decoder_input(const char *gguf, int audio_tokens, int hidden, const float *audio_values, int audio_token_id,
+                      const char *system_text, const char *language, int max_tokens, int32_t *out_ids,
+                      float *out_values, int *tokens) {
+    QwenAsrGgufModel model;
+    if (!qwenasr_gguf_model_open(gguf, &model, &g_error)) return 1;
+    QwenAsrTokenizer tok;
+    if (!qwenasr_tokenizer_load_gguf(gguf, &tok, &g_error)) {
+        qwenasr_gguf_model_close(&model);
+        return 1;
+    }
+    QwenAsrAudioEncoderOutput audio;
+    audio.tokens = audio_tokens;
+    audio.hidden = hidden;
+    audio.values.assign(audio_values, audio_values + static_cast<size_t>(audio_tokens) * hidden);
+    QwenAsrDecoderInputOutput out;
+    const bool ok = qwenasr_decoder_input_from_audio(model, tok, audio, audio_token_id, system_text, language, &out,
+                                                     &g_error);
+    qwenasr_gguf_model_close(&model);
+    if (!ok) return 2;
+    *tokens = out.tokens;
+    if (out.tokens > max_tokens) return 3;
+    for (int i = 0; i < out.tokens; ++i) out_ids[i] = out.input_ids[static_cast<size_t>(i)];
+    std::memcpy(out_values, out.values.data(), out.values.size() * sizeof(float));
+    return 0;
+}
+
 }  // extern "C"
+
+// The reference's GGML audio encoder is not built here (GGML is an empty
+// submodule in its tree); decoder-input.cpp names it, so this stub fails.
+bool qwenasr_audio_encoder_forward_ggml(const QwenAsrGgufModel &, const QwenAsrFeatures &, int, int, int, int,
+                                        QwenAsrAudioEncoderOutput *, std::string *error) {
+    if (error) *error = "GGML audio encoder unavailable in the test harness";
+    return false;
+}

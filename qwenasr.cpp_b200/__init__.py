@@ -62,6 +62,9 @@ SIGNATURES = {
     "qkv_compact": (C.c_int, [_P, _I64P]),
     "qkv_prefill": (C.c_int, [_P, C.c_int32, _I32P, _I32P, _F32P, _I32P, _F32P]),
     "qkv_prefill_rows": (C.c_int, [_P, C.c_int32, _I32P, _I32P, _P, _I32P, _F32P]),
+    "qkv_decoder_input": (C.c_int, [_P, C.c_int32, _I32P, _I32P, _P, _I32P, C.c_int32, C.c_int32, _P, _P]),
+    "qkv_prefill_ids": (C.c_int, [_P, C.c_int32, _I32P, _I32P, _I32P, _P, _I32P, C.c_int32, C.c_int32, _I32P,
+                                  _F32P]),
     "qkv_decode_step": (C.c_int, [_P, C.c_int32, _I32P, _I32P, _I32P, _F32P]),
     "qkv_generate": (C.c_int, [_P, _F32P, C.c_int32, C.c_int32, _I32P, C.c_int32, _I32P, _I32P, _I32P]),
     "qkv_layer_forward": (C.c_int, [_P, C.c_int32, C.c_int32, _F32P, _F32P]),
@@ -250,6 +253,56 @@ class Decoder:
                                          ptrs, _ptr(ids, C.c_int32),
                                          _ptr(logits, C.c_float) if want_logits else None))
         return (ids, logits) if want_logits else ids
+
+    @staticmethod
+    def _audio_table(audio, n):
+        """(pointer table, per-prompt row counts, on_device, keep-alive) for a
+        list of per-prompt audio blocks: numpy arrays (host) or torch CUDA
+        tensors (device), None for a prompt without audio rows."""
+        on_dev = any(a is not None and not isinstance(a, np.ndarray) for a in audio)
+        keep, ptrs, counts = [], [], []
+        for a in audio:
+            if a is None:
+                ptrs.append(None)
+                counts.append(0)
+            elif isinstance(a, np.ndarray):
+                if on_dev:
+                    raise ValueError("audio blocks must all be host arrays or all device tensors")
+                b = np.ascontiguousarray(a, np.float32)
+                keep.append(b)
+                ptrs.append(b.ctypes.data)
+                counts.append(b.shape[0])
+            else:
+                if not (a.is_cuda and a.is_contiguous() and str(a.dtype) == "torch.float32"):
+                    raise ValueError("device audio blocks must be contiguous float32 CUDA tensors")
+                ptrs.append(a.data_ptr())
+                counts.append(a.shape[0])
+        table = (C.c_void_p * max(n, 1))(*ptrs)
+        return table, _i32(counts), on_dev, keep
+
+    def decoder_input(self, lens, ids, audio, audio_token_id: int, x_ptr: int, stream=None):
+        """Prompt rows on the device from ids + audio rows (qkv_decoder_input): x_ptr receives sum(lens) x hidden f32."""
+        lens = _i32(lens)
+        ids = _i32(np.concatenate([np.asarray(i, np.int32) for i in ids]) if isinstance(ids, (list, tuple)) else ids)
+        table, counts, on_dev, keep = self._audio_table(audio, len(lens))
+        self._check(lib.qkv_decoder_input(self.h, len(lens), _ptr(lens, C.c_int32), _ptr(ids, C.c_int32), table,
+                                          _ptr(counts, C.c_int32), int(on_dev), int(audio_token_id), x_ptr, stream))
+
+    def prefill_ids(self, streams, ids, audio, audio_token_id: int, want_logits=False):
+        """prefill with the prompt rows built on the device (qkv_prefill_ids):
+        ids = one int array per prompt, audio = one block per prompt (host
+        arrays or CUDA tensors, None for none)."""
+        streams = _i32(streams)
+        lens = _i32([len(i) for i in ids])
+        flat = _i32(np.concatenate([np.asarray(i, np.int32) for i in ids]))
+        table, counts, on_dev, keep = self._audio_table(audio, len(streams))
+        out = np.zeros(len(streams), np.int32)
+        logits = np.zeros((len(streams), self.cfg["vocab"]), np.float32) if want_logits else None
+        self._check(lib.qkv_prefill_ids(self.h, len(streams), _ptr(streams, C.c_int32), _ptr(lens, C.c_int32),
+                                        _ptr(flat, C.c_int32), table, _ptr(counts, C.c_int32), int(on_dev),
+                                        int(audio_token_id), _ptr(out, C.c_int32),
+                                        _ptr(logits, C.c_float) if want_logits else None))
+        return (out, logits) if want_logits else out
 
     def decode_step(self, streams, in_ids=None, want_logits=False):
         streams = _i32(streams)

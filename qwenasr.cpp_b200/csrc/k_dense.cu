@@ -101,6 +101,35 @@ __global__ void embed_kernel(const int *ids, const TW *embd, int hidden, int voc
     }
 }
 
+// Decoder input (the device side of src/decoder-input.cpp:64-98): row t is
+// the embedding row of ids[t], or, where src[t] >= 0, audio row src[t]
+// (rows[src[t]] points at its hidden f32 values).  One CTA per row, 16-byte
+// copies when hidden is a multiple of 4; ids and src were checked on the host.
+template <typename TW>
+__global__ void decoder_input_kernel(const int *ids, const int *src, const TW *embd, int hidden,
+                                     const float *const *rows, float *x) {
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.x;
+    float *dst = x + static_cast<size_t>(t) * hidden;
+    const int a = src[t];
+    if (a >= 0) {
+        const float *s = rows[a];
+        if ((hidden & 3) == 0 && (reinterpret_cast<uintptr_t>(s) & 15) == 0) {
+            for (int i = threadIdx.x; i < (hidden >> 2); i += blockDim.x)
+                reinterpret_cast<float4 *>(dst)[i] = reinterpret_cast<const float4 *>(s)[i];
+        } else {
+            for (int i = threadIdx.x; i < hidden; i += blockDim.x) dst[i] = s[i];
+        }
+        return;
+    }
+    const TW *e = embd + static_cast<size_t>(ids[t]) * hidden;
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+        if constexpr (sizeof(TW) == 4) dst[i] = e[i];
+        else dst[i] = __bfloat162float(e[i]);
+    }
+}
+
 // Four consecutive elements -> float4.
 template <typename T> __device__ __forceinline__ float4 ld4(const T *p);
 template <> __device__ __forceinline__ float4 ld4<float>(const float *p) { return *reinterpret_cast<const float4 *>(p); }
@@ -304,6 +333,16 @@ cudaError_t launch_rmsnorm(const float *x, const int *rows, int n, int hidden, c
         return launch_pdl(rmsnorm_kernel<float>, dim3(n), dim3(256), 0, st, x, rows, hidden, w, eps, static_cast<float *>(out));
     return launch_pdl(rmsnorm_kernel<__nv_bfloat16>, dim3(n), dim3(256), 0, st, x, rows, hidden, w, eps,
                       static_cast<__nv_bfloat16 *>(out));
+}
+
+cudaError_t launch_decoder_input(const int *ids, const int *src, int n, const void *embd, int w_dtype, int hidden,
+                                 const float *const *rows, float *x, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    if (w_dtype == kActF32)
+        return launch_pdl(decoder_input_kernel<float>, dim3(n), dim3(256), 0, st, ids, src,
+                          static_cast<const float *>(embd), hidden, rows, x);
+    return launch_pdl(decoder_input_kernel<__nv_bfloat16>, dim3(n), dim3(256), 0, st, ids, src,
+                      static_cast<const __nv_bfloat16 *>(embd), hidden, rows, x);
 }
 
 cudaError_t launch_embed(const int *ids, int n, const void *embd, int w_dtype, int hidden, int vocab, float *x,

@@ -138,6 +138,9 @@ cudaError_t launch_page_fill(void *pool_layer, float *scales_layer, int kv_dtype
 cudaError_t launch_rmsnorm(const float *x, const int *rows, int n, int hidden, const float *w, float eps,
                            void *out, int out_dtype, cudaStream_t st);
 // x[r] = embd[ids[r]] as f32
+// Prompt rows from ids: embedding row of ids[t], or audio row rows[src[t]] where src[t] >= 0.
+cudaError_t launch_decoder_input(const int *ids, const int *src, int n, const void *embd, int w_dtype, int hidden,
+                                 const float *const *rows, float *x, cudaStream_t st);
 cudaError_t launch_embed(const int *ids, int n, const void *embd, int w_dtype, int hidden, int vocab, float *x,
                          DevError *err, cudaStream_t st);
 // C[m][n] (+)= sum_k X[m][k] * W[n][k];  X: act dtype, W: weight dtype, C f32.

@@ -161,6 +161,11 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
     CK(cudaMalloc(&h->d_out_ids, R * sizeof(int)));
     CK(cudaMallocHost(&h->h_out_ids, R * sizeof(int)));
     if (with_model_scratch) {
+        CK(cudaMallocHost(&h->h_dec, 2 * R * sizeof(int)));
+        CK(cudaMalloc(&h->d_dec, 2 * R * sizeof(int)));
+        CK(cudaMallocHost(reinterpret_cast<void **>(&h->h_rowptr), R * sizeof(float *)));
+        CK(cudaMalloc(reinterpret_cast<void **>(&h->d_rowptr), R * sizeof(float *)));
+        CK(cudaEventCreateWithFlags(&h->dec_ev, cudaEventDisableTiming));
         for (int i = 0; i < qkv_handle::kEmbRing; ++i) {
             CK(cudaMallocHost(&h->h_emb[i], qkv_handle::kEmbChunkBytes));
             CK(cudaEventCreateWithFlags(&h->emb_ev[i], cudaEventDisableTiming));
@@ -207,6 +212,8 @@ void destroy(qkv_handle *h) {
     cudaFree(h->d_rowbuf); cudaFree(h->d_out_ids); cudaFree(h->d_items); cudaFree(h->part_o); cudaFree(h->part_ml);
     cudaFree(h->counters); cudaFree(h->d_err);
     cudaFreeHost(h->h_page_table); cudaFreeHost(h->h_items); cudaFreeHost(h->h_rowbuf); cudaFreeHost(h->h_out_ids); cudaFreeHost(h->h_err);
+    cudaFreeHost(h->h_dec); cudaFree(h->d_dec); cudaFreeHost(h->h_rowptr); cudaFree(h->d_rowptr);
+    if (h->dec_ev) cudaEventDestroy(h->dec_ev);
     for (int i = 0; i < qkv_handle::kEmbRing; ++i) {
         cudaFreeHost(h->h_emb[i]);
         if (h->emb_ev[i]) cudaEventDestroy(h->emb_ev[i]);
@@ -964,10 +971,99 @@ int qkv_compact(qkv_handle *h, int64_t *moved) {
     return QKV_OK;
 }
 
+// Decoder input from prompt ids (the device side of
+// src/decoder-input.cpp:64-98).  Checks, per stream and in the reference's
+// order: every id inside the embedding table, no more placeholders than the
+// stream's audio rows, and as many.  Then row t of x is the embedding row of
+// ids[t], or the stream's next audio row where ids[t] == audio_token_id.
+// Audio rows in host memory go up through the pinned chunks into h->qkv
+// (free until the first projection of a prefill writes it); rows already on
+// the device are read where they are.
+static int decoder_input_check(qkv_handle *h, int n, const int32_t *lens, const int32_t *ids,
+                               const int32_t *audio_tokens, int32_t audio_token_id) {
+    if (!lens || !ids || !audio_tokens) return fail(h, QKV_ERR_INVALID_ARG, "null lens, ids or audio_tokens");
+    if (audio_token_id < 0) return fail(h, QKV_ERR_INVALID_ARG, "invalid decoder input configuration");
+    size_t t = 0;
+    for (int i = 0; i < n; ++i) {
+        if (lens[i] <= 0) return fail(h, QKV_ERR_INVALID_ARG, "prompt length must be positive");
+        if (audio_tokens[i] < 0) return fail(h, QKV_ERR_INVALID_ARG, "invalid native audio encoder output");
+        int audio_positions = 0;
+        for (int k = 0; k < lens[i]; ++k, ++t) {
+            const int32_t id = ids[t];
+            if (id < 0 || id >= h->cfg.vocab)
+                return fail(h, QKV_ERR_INVALID_ARG, "decoder input token id is out of embedding range");
+            if (id == audio_token_id) {
+                if (audio_positions >= audio_tokens[i])
+                    return fail(h, QKV_ERR_INVALID_ARG, "prompt has more audio placeholders than audio encoder outputs");
+                ++audio_positions;
+            }
+        }
+        if (audio_positions != audio_tokens[i])
+            return fail(h, QKV_ERR_INVALID_ARG, "audio placeholder count does not match audio encoder output count");
+    }
+    return QKV_OK;
+}
+
+static int decoder_input_run(qkv_handle *h, int n, const int32_t *lens, const int32_t *ids,
+                             const float *const *audio, const int32_t *audio_tokens, bool audio_on_device,
+                             int32_t audio_token_id, float *x, cudaStream_t st) {
+    const int H = h->cfg.hidden;
+    int T = 0, A = 0;
+    for (int i = 0; i < n; ++i) {
+        T += lens[i];
+        A += audio_tokens[i];
+        if (audio_tokens[i] > 0 && (!audio || !audio[i]))
+            return fail(h, QKV_ERR_INVALID_ARG, "null audio rows for a stream with audio placeholders");
+    }
+    if (T > h->max_rows) return fail(h, QKV_ERR_CAPACITY, "prompt tokens exceed max_batch_tokens");
+    if (A > 0 && !audio_on_device && H > kQkvDim)
+        return fail(h, QKV_ERR_STATE, "audio staging: hidden wider than the projection scratch");
+    CK(cudaEventSynchronize(h->dec_ev));   // the pinned staging is free again
+    int *hid = h->h_dec, *hsrc = h->h_dec + T;
+    const float **hptr = h->h_rowptr;
+    int t = 0, a = 0;
+    for (int i = 0; i < n; ++i) {
+        int k_audio = 0;
+        for (int k = 0; k < lens[i]; ++k, ++t) {
+            hid[t] = ids[t];
+            if (ids[t] == audio_token_id) {
+                hsrc[t] = a;
+                hptr[a] = audio_on_device ? audio[i] + static_cast<size_t>(k_audio) * H
+                                          : h->qkv + static_cast<size_t>(a) * H;
+                ++a;
+                ++k_audio;
+            } else {
+                hsrc[t] = -1;
+            }
+        }
+    }
+    int rc;
+    if (A > 0 && !audio_on_device) {
+        std::vector<const float *> blocks;
+        std::vector<int32_t> counts;
+        for (int i = 0; i < n; ++i) {
+            if (audio_tokens[i] > 0) {
+                blocks.push_back(audio[i]);
+                counts.push_back(audio_tokens[i]);
+            }
+        }
+        if ((rc = upload_prompt_rows(h, h->qkv, static_cast<int>(blocks.size()), blocks.data(), counts.data(), H, st)))
+            return rc;
+    }
+    CK(cudaMemcpyAsync(h->d_dec, h->h_dec, 2 * static_cast<size_t>(T) * sizeof(int), cudaMemcpyHostToDevice, st));
+    if (A > 0)
+        CK(cudaMemcpyAsync(h->d_rowptr, h->h_rowptr, static_cast<size_t>(A) * sizeof(float *), cudaMemcpyHostToDevice,
+                           st));
+    CK(cudaEventRecord(h->dec_ev, st));
+    CK(launch_decoder_input(h->d_dec, h->d_dec + T, T, h->embd, h->w_dtype, H, h->d_rowptr, x, st));
+    h->launches += 1;
+    return QKV_OK;
+}
+
 // Shared body of qkv_prefill (one contiguous embedding block) and
 // qkv_prefill_rows (one block per stream): rows[i] = stream i's prompt rows.
 static int prefill_impl(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *lens,
-                        const float *const *rows, int32_t *out_ids, float *out_logits) {
+                        const std::function<int()> &fill_x, int32_t *out_ids, float *out_logits) {
     int rc;
     if ((rc = check_streams(h, n, stream_ids))) return rc;
     int64_t total = 0;
@@ -993,7 +1089,7 @@ static int prefill_impl(qkv_handle *h, int32_t n, const int32_t *stream_ids, con
     if ((rc = grow_streams(h, n, stream_ids, lens, h->stream))) return rc;
     int *ds = h->d_rowbuf, *dp = ds + T, *dr = dp + T;
     if ((rc = row_upload(h, hs, static_cast<size_t>(2 * T + n), h->stream))) return rc;
-    if ((rc = upload_prompt_rows(h, h->x, n, rows, lens, h->cfg.hidden, h->stream))) return rc;
+    if ((rc = fill_x())) return rc;
     int n_items = 0;
     std::vector<int> base(static_cast<size_t>(n));
     for (int i = 0; i < n; ++i) base[static_cast<size_t>(i)] = hp[t_first(i, lens)];
@@ -1015,7 +1111,9 @@ int qkv_prefill(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32
         rows[static_cast<size_t>(i)] = embeddings + off;
         off += static_cast<size_t>(lens[i] > 0 ? lens[i] : 0) * h->cfg.hidden;
     }
-    return prefill_impl(h, n, stream_ids, lens, rows.data(), out_ids, out_logits);
+    return prefill_impl(h, n, stream_ids, lens,
+                        [&]() { return upload_prompt_rows(h, h->x, n, rows.data(), lens, h->cfg.hidden, h->stream); },
+                        out_ids, out_logits);
 }
 
 int qkv_prefill_rows(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *lens,
@@ -1025,7 +1123,38 @@ int qkv_prefill_rows(qkv_handle *h, int32_t n, const int32_t *stream_ids, const 
     if (!lens || !embeddings) return fail(h, QKV_ERR_INVALID_ARG, "null lens or embeddings");
     for (int i = 0; i < n; ++i)
         if (!embeddings[i]) return fail(h, QKV_ERR_INVALID_ARG, "null embedding rows for a stream");
-    return prefill_impl(h, n, stream_ids, lens, embeddings, out_ids, out_logits);
+    return prefill_impl(h, n, stream_ids, lens,
+                        [&]() { return upload_prompt_rows(h, h->x, n, embeddings, lens, h->cfg.hidden, h->stream); },
+                        out_ids, out_logits);
+}
+
+int qkv_prefill_ids(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *lens, const int32_t *ids,
+                    const float *const *audio, const int32_t *audio_tokens, int32_t audio_on_device,
+                    int32_t audio_token_id, int32_t *out_ids, float *out_logits) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    if (!h->has_weights) return fail(h, QKV_ERR_STATE, "handle has no model weights");
+    if (n < 0) return fail(h, QKV_ERR_INVALID_ARG, "negative stream count");
+    int rc;
+    if ((rc = decoder_input_check(h, n, lens, ids, audio_tokens, audio_token_id))) return rc;
+    return prefill_impl(h, n, stream_ids, lens,
+                        [&]() {
+                            return decoder_input_run(h, n, lens, ids, audio, audio_tokens, audio_on_device != 0,
+                                                     audio_token_id, h->x, h->stream);
+                        },
+                        out_ids, out_logits);
+}
+
+int qkv_decoder_input(qkv_handle *h, int32_t n, const int32_t *lens, const int32_t *ids, const float *const *audio,
+                      const int32_t *audio_tokens, int32_t audio_on_device, int32_t audio_token_id, float *x_dev,
+                      void *stream) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    if (!h->has_weights) return fail(h, QKV_ERR_STATE, "handle has no model weights");
+    if (n < 0 || !x_dev) return fail(h, QKV_ERR_INVALID_ARG, "negative stream count or null output");
+    int rc;
+    if ((rc = decoder_input_check(h, n, lens, ids, audio_tokens, audio_token_id))) return rc;
+    CK(cudaSetDevice(h->device));
+    return decoder_input_run(h, n, lens, ids, audio, audio_tokens, audio_on_device != 0, audio_token_id, x_dev,
+                             static_cast<cudaStream_t>(stream));
 }
 
 int qkv_decode_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *in_ids, int32_t *out_ids,

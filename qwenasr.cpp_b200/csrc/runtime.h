@@ -76,6 +76,12 @@ struct qkv_handle {
     float *h_emb[kEmbRing] = {};
     cudaEvent_t emb_ev[kEmbRing] = {};
     int emb_slot = 0;
+    // Decoder input from ids: pinned / device staging of [ids | row source]
+    // ([2][max_rows] int32) and of the audio-row pointer table ([max_rows]),
+    // rewritten only after the copies that last read them have run (dec_ev).
+    int *h_dec = nullptr, *d_dec = nullptr;
+    const float **h_rowptr = nullptr, **d_rowptr = nullptr;
+    cudaEvent_t dec_ev = nullptr;
     // qkv_kv_step_host's per-layer pipeline: inputs go up on copy_in, outputs
     // come back on copy_out, one event per layer each way (created on first use).
     cudaStream_t copy_in = nullptr, copy_out = nullptr;

@@ -33,6 +33,30 @@ TINY = dict(n_layers=2, hidden=256, n_heads=16, n_kv_heads=8, head_dim=128,
 TOKEN_IDS = dict(endoftext=151643, im_start=151644, im_end=151645, audio=151676,
                  audio_start=151669, audio_end=151670, asr_text=151704)
 
+# Byte-level tokenizer for small synthetic vocabularies: ids 0..255 are the
+# 256 byte symbols, the special tokens follow, so a prompt built from the ASR
+# template tokenises inside a 1000-row embedding table.
+BYTE_TOKEN_IDS = dict(endoftext=256, im_start=257, im_end=258, audio_start=259, audio_end=260, audio=261,
+                      asr_text=262)
+SPECIAL_STRINGS = dict(endoftext="<|endoftext|>", im_start="<|im_start|>", im_end="<|im_end|>",
+                       audio_start="<|audio_start|>", audio_end="<|audio_end|>", audio="<|audio_pad|>",
+                       asr_text="<asr_text>")
+
+
+def byte_symbols() -> list[str]:
+    """The byte-level BPE alphabet: byte b -> one printable character (the
+    published GPT-2 mapping: printable Latin-1 bytes map to themselves, the
+    other 68 bytes to code points 256, 257, ... in byte order)."""
+    keep = list(range(0x21, 0x7F)) + list(range(0xA1, 0xAD)) + list(range(0xAE, 0x100))
+    table, extra = {}, 0
+    for b in range(256):
+        if b in keep:
+            table[b] = chr(b)
+        else:
+            table[b] = chr(256 + extra)
+            extra += 1
+    return [table[b] for b in range(256)]
+
 
 @dataclass
 class ModelConfig:
@@ -104,7 +128,10 @@ def _kv_arr_i32(key: str, items: np.ndarray) -> bytes:
     return struct.pack("<Q", len(k)) + k + struct.pack("<IIQ", 9, 5, len(items)) + items.astype("<i4").tobytes()
 
 
-def metadata(cfg: ModelConfig, name: str, tokenizer: bool) -> list[bytes]:
+def metadata(cfg: ModelConfig, name: str, tokenizer: bool | str) -> list[bytes]:
+    """tokenizer: False (none), True (placeholder vocabulary with the real
+    Qwen special-token ids) or "bytes" (byte-level vocabulary, BYTE_TOKEN_IDS)."""
+    ids = BYTE_TOKEN_IDS if tokenizer == "bytes" else TOKEN_IDS
     kv = [_kv_str("general.architecture", "qwen3-asr"), _kv_str("general.name", name),
           _kv_str("qwen3-asr.arch", "qwen3-asr"), _kv_u32("general.alignment", GGUF_ALIGN),
           _kv_u32("qwen3-asr.audio.sample_rate", 16000), _kv_u32("qwen3-asr.audio.num_mel_bins", 128),
@@ -119,20 +146,27 @@ def metadata(cfg: ModelConfig, name: str, tokenizer: bool) -> list[bytes]:
           _kv_u32("qwen3-asr.text.head_dim", cfg.head_dim),
           _kv_f32("qwen3-asr.text.rope_theta", cfg.rope_theta),
           _kv_f32("qwen3-asr.text.rms_norm_eps", cfg.rms_norm_eps),
-          _kv_u32("qwen3-asr.token.audio_token_id", TOKEN_IDS["audio"]),
-          _kv_u32("qwen3-asr.token.audio_start_token_id", TOKEN_IDS["audio_start"]),
-          _kv_u32("qwen3-asr.token.audio_end_token_id", TOKEN_IDS["audio_end"])]
+          _kv_u32("qwen3-asr.token.audio_token_id", ids["audio"]),
+          _kv_u32("qwen3-asr.token.audio_start_token_id", ids["audio_start"]),
+          _kv_u32("qwen3-asr.token.audio_end_token_id", ids["audio_end"])]
+    if tokenizer == "bytes":
+        n = max(cfg.vocab, ids["asr_text"] + 1)
+        tokens = byte_symbols() + [f"<t{i}>" for i in range(256, n)]
+        for k, i in ids.items():
+            tokens[i] = SPECIAL_STRINGS[k]
+    else:
+        n = max(cfg.vocab, ids["asr_text"] + 1)
+        tokens = [f"<t{i}>" for i in range(n)]
     if tokenizer:
-        n = max(cfg.vocab, TOKEN_IDS["asr_text"] + 1)
         kv += [_kv_str("tokenizer.ggml.model", "gpt2"),
-               _kv_arr_str("tokenizer.ggml.tokens", [f"<t{i}>" for i in range(n)]),
+               _kv_arr_str("tokenizer.ggml.tokens", tokens),
                _kv_arr_i32("tokenizer.ggml.token_type", np.ones(n, np.int32)),
                _kv_arr_str("tokenizer.ggml.merges", []),
-               _kv_u32("tokenizer.ggml.eos_token_id", TOKEN_IDS["im_end"]),
-               _kv_u32("qwen3-asr.token.endoftext_token_id", TOKEN_IDS["endoftext"]),
-               _kv_u32("qwen3-asr.token.im_start_token_id", TOKEN_IDS["im_start"]),
-               _kv_u32("qwen3-asr.token.im_end_token_id", TOKEN_IDS["im_end"]),
-               _kv_u32("qwen3-asr.token.asr_text_token_id", TOKEN_IDS["asr_text"])]
+               _kv_u32("tokenizer.ggml.eos_token_id", ids["im_end"]),
+               _kv_u32("qwen3-asr.token.endoftext_token_id", ids["endoftext"]),
+               _kv_u32("qwen3-asr.token.im_start_token_id", ids["im_start"]),
+               _kv_u32("qwen3-asr.token.im_end_token_id", ids["im_end"]),
+               _kv_u32("qwen3-asr.token.asr_text_token_id", ids["asr_text"])]
     return kv
 
 
@@ -145,7 +179,7 @@ def _gen_tensor(rng: np.random.Generator, shape, kind: str, std: float, norm_ini
 
 
 def write_gguf(path: str | Path, cfg: ModelConfig | dict, seed: int = 0, std: float = 0.02,
-               weights: str = "f32", norm_init: str = "normal", tokenizer: bool = True) -> Path:
+               weights: str = "f32", norm_init: str = "normal", tokenizer: bool | str = True) -> Path:
     """Write a random-init text-decoder GGUF; returns the path.
 
     weights: "f32" (plain N(0,std) floats) or "bf16" (bf16-rounded, stored f32).

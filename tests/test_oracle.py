@@ -105,3 +105,70 @@ def test_rope_table_formula(checker):
         c, s = checker.rope_cos_sin(pos, i)
         inv = math.exp(-math.log(1.0e6) * (2 * i) / 128.0)
         assert c == np.float32(math.cos(pos * inv)) and s == np.float32(math.sin(pos * inv))
+
+
+# ---- decoder input (src/decoder-input.cpp:64-98) ----
+
+def _digest(a):
+    import hashlib
+    return hashlib.sha256(np.ascontiguousarray(a, np.float32).tobytes()).hexdigest()
+
+
+@pytest.fixture(scope="module")
+def dec_input(synth, tmp_path_factory):
+    """The decoder-input fixture (the reference's own assembly, see
+    tests/golden/make_decoder_input_golden.py) with the tiny model's table."""
+    g = np.load(GOLDEN / "decoder_input.npz")
+    path = synth.write_gguf(tmp_path_factory.mktemp("di") / "m.gguf", dict(synth.TINY), seed=0, weights="f32",
+                            norm_init="one_plus", tokenizer="bytes")
+    embd = np.array(synth.read_gguf(path)["text.token_embd.weight"])
+    assert _digest(embd) == str(g["embd_sha256"]), "synthetic weight generator drifted from the fixture"
+    return g, embd, path
+
+
+def test_decoder_input_bit_exact(dec_input, checker):
+    g, embd, _ = dec_input
+    aid = int(g["audio_token_id"])
+    for k in range(3):
+        rc, rows = checker.decoder_input(g[f"ids_{k}"], embd, g[f"audio_{k}"], aid)
+        assert rc == 0
+        assert _digest(rows) == str(g[f"rows_sha256_{k}"])
+    rc, rows = checker.decoder_input(g["ids_0"], embd, g["audio_0"], aid)
+    assert np.array_equal(rows, g["rows_0"])
+
+
+def test_decoder_input_error_order(dec_input, checker):
+    """The reference's checks in its order: 1 id outside the table, 2 more
+    placeholders than audio rows (seen while scanning), 3 a count that differs
+    at the end.  (The reference reports 2 as "prompt has more audio
+    placeholders ..." and 3 as "audio placeholder count does not match ...",
+    the two messages the fixture recorded from its own failures.)"""
+    g, embd, _ = dec_input
+    aid = int(g["audio_token_id"])
+    ids, audio = g["ids_0"], g["audio_0"]
+    assert checker.decoder_input(ids, embd, audio[:4], aid)[0] == 2
+    assert checker.decoder_input(ids, embd, np.concatenate([audio, audio[:1]]), aid)[0] == 3
+    bad = ids.copy()
+    bad[1] = embd.shape[0]
+    assert checker.decoder_input(bad, embd, audio, aid)[0] == 1
+    bad[1] = -1
+    assert checker.decoder_input(bad, embd, audio, aid)[0] == 1
+    # an out-of-range id after a surplus placeholder: the placeholder is seen first
+    extra = np.concatenate([ids[:1], [aid] * 6, [embd.shape[0]]]).astype(np.int32)
+    assert checker.decoder_input(extra, embd, audio, aid)[0] == 2
+    assert "more audio placeholders" in str(g["error_0"])
+    assert "count does not match" in str(g["error_1"])
+
+
+def test_decoder_input_reference_live(dec_input, checker):
+    """With the reference tree built here (oracle/_ref), its assembly still
+    gives the fixture."""
+    if not checker.ref_available():
+        pytest.skip("oracle/_ref not built")
+    g, _, path = dec_input
+    for k in range(3):
+        rc, ids, rows, msg = checker.ref_decoder_input(str(path), g[f"audio_{k}"], int(g["audio_token_id"]),
+                                                       str(g[f"system_{k}"]), str(g[f"language_{k}"]))
+        assert rc == 0, msg
+        assert np.array_equal(ids, g[f"ids_{k}"])
+        assert _digest(rows) == str(g[f"rows_sha256_{k}"])
