@@ -136,6 +136,18 @@ int qkv_prefill(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32
 int qkv_prefill_rows(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *lens,
                      const float *const *embeddings, int32_t *out_ids, float *out_logits);
 
+/* Audio projector on the device (src/audio-encoder.cpp:848-856, the stage
+ * between the audio encoder and the decoder input): rows of the encoder's
+ * output, audio_dev [n][Ha] f32 (device), go through LayerNorm (eps 1e-5,
+ * weight and bias) -> audio.proj.0 + bias -> erf GELU -> audio.proj.1 + bias
+ * into out_dev [n][hidden] f32 (device), on `stream`; the result can go to
+ * qkv_prefill_ids / qkv_decoder_input with audio_on_device = 1.  Needs the
+ * audio.post_norm / audio.proj tensors in the model file (QKV_ERR_STATE when
+ * absent; qkv_audio_projector_width gives Ha, 0 without them).  Uses the
+ * handle's prefill scratch: do not overlap it with other calls on the handle. */
+int qkv_audio_project(qkv_handle *h, int32_t n, const float *audio_dev, float *out_dev, void *stream);
+int qkv_audio_projector_width(const qkv_handle *h, int32_t *width);
+
 /* Decoder input on the device: the embedding lookup and audio-row splice of
  * qwenasr_decoder_input_from_audio (src/decoder-input.cpp:64-98), after the
  * prompt (src/tokenizer.cpp:529-549) has been tokenised by the caller.  For n

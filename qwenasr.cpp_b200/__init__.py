@@ -63,6 +63,8 @@ SIGNATURES = {
     "qkv_prefill": (C.c_int, [_P, C.c_int32, _I32P, _I32P, _F32P, _I32P, _F32P]),
     "qkv_prefill_rows": (C.c_int, [_P, C.c_int32, _I32P, _I32P, _P, _I32P, _F32P]),
     "qkv_decoder_input": (C.c_int, [_P, C.c_int32, _I32P, _I32P, _P, _I32P, C.c_int32, C.c_int32, _P, _P]),
+    "qkv_audio_project": (C.c_int, [_P, C.c_int32, _P, _P, _P]),
+    "qkv_audio_projector_width": (C.c_int, [_P, _I32P]),
     "qkv_prefill_ids": (C.c_int, [_P, C.c_int32, _I32P, _I32P, _I32P, _P, _I32P, C.c_int32, C.c_int32, _I32P,
                                   _F32P]),
     "qkv_decode_step": (C.c_int, [_P, C.c_int32, _I32P, _I32P, _I32P, _F32P]),
@@ -279,6 +281,17 @@ class Decoder:
                 counts.append(a.shape[0])
         table = (C.c_void_p * max(n, 1))(*ptrs)
         return table, _i32(counts), on_dev, keep
+
+    def audio_projector_width(self) -> int:
+        """Width of the audio encoder rows the projector takes (0: the file has no projector)."""
+        w = np.zeros(1, np.int32)
+        self._check(lib.qkv_audio_projector_width(self.h, _ptr(w, C.c_int32)))
+        return int(w[0])
+
+    def audio_project(self, n: int, audio_ptr: int, out_ptr: int, stream=None):
+        """Audio projector on the device (qkv_audio_project): n rows of width
+        audio_projector_width() -> n decoder rows (device pointers, f32)."""
+        self._check(lib.qkv_audio_project(self.h, n, audio_ptr, out_ptr, stream))
 
     def decoder_input(self, lens, ids, audio, audio_token_id: int, x_ptr: int, stream=None):
         """Prompt rows on the device from ids + audio rows (qkv_decoder_input): x_ptr receives sum(lens) x hidden f32."""

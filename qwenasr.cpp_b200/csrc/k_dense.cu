@@ -4,6 +4,8 @@
 // the first-maximum argmax of the greedy loop (:2266-2274).
 #include "kernels.h"
 
+#include <algorithm>
+
 #include <cuda_fp16.h>
 
 namespace qkv {
@@ -98,6 +100,67 @@ __global__ void embed_kernel(const int *ids, const TW *embd, int hidden, int voc
     for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
         if constexpr (sizeof(TW) == 4) x[static_cast<size_t>(r) * hidden + i] = src[i];
         else x[static_cast<size_t>(r) * hidden + i] = __bfloat162float(src[i]);
+    }
+}
+
+// Audio projector LayerNorm (audio-encoder.cpp:399-407 / 851: mean and
+// variance over the row, eps 1e-5, times weight plus bias), one CTA per row;
+// mean and variance accumulated in double, two passes over the row.
+template <typename TOut>
+__global__ void __launch_bounds__(256) layernorm_kernel(const float *x, int width, const float *w, const float *b,
+                                                        float eps, TOut *out) {
+    pdl_trigger();
+    pdl_wait();
+    const int r = blockIdx.x;
+    const float *xr = x + static_cast<size_t>(r) * width;
+    __shared__ double part[8];
+    __shared__ float s_mean, s_scale;
+    double acc = 0.0;
+    for (int i = threadIdx.x; i < width; i += blockDim.x) acc += xr[i];
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) t += part[k];
+        s_mean = static_cast<float>(t / width);
+    }
+    __syncthreads();
+    const float mean = s_mean;
+    acc = 0.0;
+    for (int i = threadIdx.x; i < width; i += blockDim.x) {
+        const double d = static_cast<double>(xr[i]) - mean;
+        acc += d * d;
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) t += part[k];
+        s_scale = static_cast<float>(1.0 / sqrt(t / width + static_cast<double>(eps)));
+    }
+    __syncthreads();
+    const float scale = s_scale;
+    TOut *o = out + static_cast<size_t>(r) * width;
+    for (int i = threadIdx.x; i < width; i += blockDim.x) put<TOut>(o + i, (xr[i] - mean) * scale * w[i] + b[i]);
+}
+
+// out[r][j] = act(c[r][j] + bias[j]) with act = GELU (erf form,
+// 0.5 x (1 + erf(x / sqrt 2)), as the projector's ggml_gelu_erf) or identity.
+template <typename TOut>
+__global__ void bias_act_kernel(const float *c, const float *bias, int n, int width, int gelu, TOut *out) {
+    pdl_trigger();
+    pdl_wait();
+    const size_t total = static_cast<size_t>(n) * width;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        float v = c[i] + bias[i % width];
+        if (gelu) v = 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+        put<TOut>(out + i, v);
     }
 }
 
@@ -333,6 +396,28 @@ cudaError_t launch_rmsnorm(const float *x, const int *rows, int n, int hidden, c
         return launch_pdl(rmsnorm_kernel<float>, dim3(n), dim3(256), 0, st, x, rows, hidden, w, eps, static_cast<float *>(out));
     return launch_pdl(rmsnorm_kernel<__nv_bfloat16>, dim3(n), dim3(256), 0, st, x, rows, hidden, w, eps,
                       static_cast<__nv_bfloat16 *>(out));
+}
+
+cudaError_t launch_layernorm(const float *x, int n, int width, const float *w, const float *b, float eps, void *out,
+                             int out_dtype, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    if (out_dtype == kActF32)
+        return launch_pdl(layernorm_kernel<float>, dim3(n), dim3(256), 0, st, x, width, w, b, eps,
+                          static_cast<float *>(out));
+    return launch_pdl(layernorm_kernel<__nv_bfloat16>, dim3(n), dim3(256), 0, st, x, width, w, b, eps,
+                      static_cast<__nv_bfloat16 *>(out));
+}
+
+cudaError_t launch_bias_act(const float *c, const float *bias, int n, int width, bool gelu, void *out, int out_dtype,
+                            cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    const size_t total = static_cast<size_t>(n) * width;
+    const unsigned blocks = static_cast<unsigned>(std::min<size_t>((total + 255) / 256, 65535));
+    if (out_dtype == kActF32)
+        return launch_pdl(bias_act_kernel<float>, dim3(blocks), dim3(256), 0, st, c, bias, n, width, gelu ? 1 : 0,
+                          static_cast<float *>(out));
+    return launch_pdl(bias_act_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, st, c, bias, n, width,
+                      gelu ? 1 : 0, static_cast<__nv_bfloat16 *>(out));
 }
 
 cudaError_t launch_decoder_input(const int *ids, const int *src, int n, const void *embd, int w_dtype, int hidden,

@@ -138,6 +138,12 @@ cudaError_t launch_page_fill(void *pool_layer, float *scales_layer, int kv_dtype
 cudaError_t launch_rmsnorm(const float *x, const int *rows, int n, int hidden, const float *w, float eps,
                            void *out, int out_dtype, cudaStream_t st);
 // x[r] = embd[ids[r]] as f32
+// Audio projector pieces: LayerNorm (weight, bias) of f32 rows into `out_dtype`;
+// out = act(c + bias) (act = erf GELU or identity) into `out_dtype`.
+cudaError_t launch_layernorm(const float *x, int n, int width, const float *w, const float *b, float eps, void *out,
+                             int out_dtype, cudaStream_t st);
+cudaError_t launch_bias_act(const float *c, const float *bias, int n, int width, bool gelu, void *out, int out_dtype,
+                            cudaStream_t st);
 // Prompt rows from ids: embedding row of ids[t], or audio row rows[src[t]] where src[t] >= 0.
 cudaError_t launch_decoder_input(const int *ids, const int *src, int n, const void *embd, int w_dtype, int hidden,
                                  const float *const *rows, float *x, cudaStream_t st);

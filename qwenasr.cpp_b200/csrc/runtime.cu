@@ -206,6 +206,8 @@ void destroy(qkv_handle *h) {
         cudaFree(L.w_qkv); cudaFree(L.w_o); cudaFree(L.w_gu); cudaFree(L.w_down);
     }
     cudaFree(h->embd); cudaFree(h->w_out); cudaFree(h->out_norm);
+    cudaFree(h->ap_norm_w); cudaFree(h->ap_norm_b); cudaFree(h->ap_w0); cudaFree(h->ap_b0); cudaFree(h->ap_w1);
+    cudaFree(h->ap_b1);
     cudaFree(h->pool); cudaFree(h->scales); cudaFree(h->d_page_table); cudaFree(h->d_rope);
     cudaFree(h->x); cudaFree(h->qkv); cudaFree(h->q); cudaFree(h->gu); cudaFree(h->logits);
     cudaFree(h->xn); cudaFree(h->attn); cudaFree(h->act); cudaFree(h->host_stage);
@@ -340,6 +342,31 @@ int load_weights(qkv_handle *h, const GgufFile &f) {
     if ((rc = up.put(te, h->embd, h->w_dtype, 0)) || (rc = up.put(ow, h->w_out, h->w_dtype, 0)) ||
         (rc = up.put(on, h->out_norm, kActF32, 0)))
         return rc;
+    // Audio projector, when the file has it (names and shapes of
+    // audio-encoder.cpp:776-790; GGML ne = [in, out]).
+    if (const GgufTensor *pw0 = f.find("audio.post_norm.weight")) {
+        const int64_t A = pw0->ne.size() == 1 ? pw0->ne[0] : 0;
+        if (A <= 0 || A % 64 != 0) return fail(h, QKV_ERR_FORMAT, "audio projector width must be a multiple of 64");
+        const GgufTensor *pw, *pb, *w0, *b0, *w1, *b1;
+        if ((rc = find_tensor(h, f, "audio.post_norm.weight", {A}, &pw)) ||
+            (rc = find_tensor(h, f, "audio.post_norm.bias", {A}, &pb)) ||
+            (rc = find_tensor(h, f, "audio.proj.0.weight", {A, A}, &w0)) ||
+            (rc = find_tensor(h, f, "audio.proj.0.bias", {A}, &b0)) ||
+            (rc = find_tensor(h, f, "audio.proj.1.weight", {A, H}, &w1)) ||
+            (rc = find_tensor(h, f, "audio.proj.1.bias", {H}, &b1)))
+            return rc;
+        CK(cudaMalloc(&h->ap_norm_w, A * sizeof(float)));
+        CK(cudaMalloc(&h->ap_norm_b, A * sizeof(float)));
+        CK(cudaMalloc(&h->ap_w0, static_cast<size_t>(A) * A * we));
+        CK(cudaMalloc(&h->ap_b0, A * sizeof(float)));
+        CK(cudaMalloc(&h->ap_w1, static_cast<size_t>(H) * A * we));
+        CK(cudaMalloc(&h->ap_b1, H * sizeof(float)));
+        if ((rc = up.put(pw, h->ap_norm_w, kActF32, 0)) || (rc = up.put(pb, h->ap_norm_b, kActF32, 0)) ||
+            (rc = up.put(w0, h->ap_w0, h->w_dtype, 0)) || (rc = up.put(b0, h->ap_b0, kActF32, 0)) ||
+            (rc = up.put(w1, h->ap_w1, h->w_dtype, 0)) || (rc = up.put(b1, h->ap_b1, kActF32, 0)))
+            return rc;
+        h->audio_hidden = static_cast<int>(A);
+    }
     h->has_weights = true;
     return QKV_OK;
 }
@@ -1142,6 +1169,41 @@ int qkv_prefill_ids(qkv_handle *h, int32_t n, const int32_t *stream_ids, const i
                                                      audio_token_id, h->x, h->stream);
                         },
                         out_ids, out_logits);
+}
+
+int qkv_audio_projector_width(const qkv_handle *h, int32_t *width) {
+    if (!h || !width) return QKV_ERR_INVALID_ARG;
+    *width = h->audio_hidden;
+    return QKV_OK;
+}
+
+// Audio projector (audio-encoder.cpp:848-856): LayerNorm -> proj0 + bias ->
+// erf GELU -> proj1 + bias, rows of the audio encoder's output (device) to
+// decoder-width rows (device).  Intermediates live in the handle's prefill
+// scratch: LayerNorm output in act, proj0 sums in gu, GELU output in xn.
+int qkv_audio_project(qkv_handle *h, int32_t n, const float *audio_dev, float *out_dev, void *stream) {
+    if (!h) return QKV_ERR_INVALID_ARG;
+    if (!h->has_weights || h->audio_hidden <= 0) return fail(h, QKV_ERR_STATE, "the model file has no audio projector");
+    if (n < 0 || (n > 0 && (!audio_dev || !out_dev))) return fail(h, QKV_ERR_INVALID_ARG, "bad row count or pointer");
+    if (n == 0) return QKV_OK;
+    const int A = h->audio_hidden, H = h->cfg.hidden;
+    if (n > h->max_rows) return fail(h, QKV_ERR_CAPACITY, "audio rows exceed max_batch_tokens");
+    if (A > h->cfg.intermediate || A > H)
+        return fail(h, QKV_ERR_STATE, "audio projector wider than the handle's row scratch");
+    CK(cudaSetDevice(h->device));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const cudaStream_t saved = h->stream;   // the GEMM helper launches on h->stream
+    h->stream = st;
+    int rc = QKV_OK;
+    cudaError_t e = launch_layernorm(audio_dev, n, A, h->ap_norm_w, h->ap_norm_b, 1.0e-5f, h->act, h->act_dtype, st);
+    if (e == cudaSuccess) e = gemm(h, h->act, h->ap_w0, h->gu, n, A, A, 0);
+    if (e == cudaSuccess) e = launch_bias_act(h->gu, h->ap_b0, n, A, true, h->xn, h->act_dtype, st);
+    if (e == cudaSuccess) e = gemm(h, h->xn, h->ap_w1, out_dev, n, H, A, 0);
+    if (e == cudaSuccess) e = launch_bias_act(out_dev, h->ap_b1, n, H, false, out_dev, kActF32, st);
+    h->stream = saved;
+    if (e != cudaSuccess) rc = cuda_fail(h, e, "audio projector");
+    else h->launches += 5;
+    return rc;
 }
 
 int qkv_decoder_input(qkv_handle *h, int32_t n, const int32_t *lens, const int32_t *ids, const float *const *audio,

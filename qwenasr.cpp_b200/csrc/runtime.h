@@ -41,6 +41,11 @@ struct qkv_handle {
     void *embd = nullptr;      // [V][H]
     void *w_out = nullptr;     // [V][H]
     float *out_norm = nullptr; // [H]
+    // Audio projector (optional in the GGUF): LayerNorm [Ha] weight/bias, proj0
+    // [Ha][Ha] + bias, proj1 [H][Ha] + bias (weights in the weight dtype).
+    int audio_hidden = 0;
+    float *ap_norm_w = nullptr, *ap_norm_b = nullptr, *ap_b0 = nullptr, *ap_b1 = nullptr;
+    void *ap_w0 = nullptr, *ap_w1 = nullptr;
 
     // KV pool
     void *pool = nullptr;

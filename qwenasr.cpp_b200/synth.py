@@ -75,8 +75,11 @@ class ModelConfig:
         return ModelConfig(**d)
 
 
-def tensor_specs(cfg: ModelConfig) -> list[tuple[str, tuple[int, ...], str]]:
-    """(name, numpy shape = reversed GGML ne, kind) in file order."""
+def tensor_specs(cfg: ModelConfig, audio_hidden: int = 0) -> list[tuple[str, tuple[int, ...], str]]:
+    """(name, numpy shape = reversed GGML ne, kind) in file order.  With
+    audio_hidden > 0 the audio projector follows the text tensors (names and
+    shapes of convert.py:145-150 and audio-encoder.cpp:776-790: LayerNorm
+    weight and bias [Ha], proj.0 [Ha][Ha] + bias, proj.1 [H][Ha] + bias)."""
     H, F, V, D = cfg.hidden, cfg.intermediate, cfg.vocab, cfg.head_dim
     q, kv = cfg.n_heads * D, cfg.n_kv_heads * D
     out = [("text.token_embd.weight", (V, H), "w"),
@@ -90,6 +93,11 @@ def tensor_specs(cfg: ModelConfig) -> list[tuple[str, tuple[int, ...], str]]:
                 (p + "attn_q_norm.weight", (D,), "norm"), (p + "attn_k_norm.weight", (D,), "norm"),
                 (p + "ffn_gate.weight", (F, H), "w"), (p + "ffn_up.weight", (F, H), "w"),
                 (p + "ffn_down.weight", (H, F), "w")]
+    if audio_hidden:
+        A = audio_hidden
+        out += [("audio.post_norm.weight", (A,), "norm"), ("audio.post_norm.bias", (A,), "w"),
+                ("audio.proj.0.weight", (A, A), "w"), ("audio.proj.0.bias", (A,), "w"),
+                ("audio.proj.1.weight", (H, A), "w"), ("audio.proj.1.bias", (H,), "w")]
     return out
 
 
@@ -179,16 +187,18 @@ def _gen_tensor(rng: np.random.Generator, shape, kind: str, std: float, norm_ini
 
 
 def write_gguf(path: str | Path, cfg: ModelConfig | dict, seed: int = 0, std: float = 0.02,
-               weights: str = "f32", norm_init: str = "normal", tokenizer: bool | str = True) -> Path:
+               weights: str = "f32", norm_init: str = "normal", tokenizer: bool | str = True,
+               audio_hidden: int = 0) -> Path:
     """Write a random-init text-decoder GGUF; returns the path.
 
     weights: "f32" (plain N(0,std) floats) or "bf16" (bf16-rounded, stored f32).
     norm_init: "normal" -> norm weights ~ N(0,std) like every other tensor;
                "one_plus" -> 1 + N(0,std) (a trained-like scale).
+    audio_hidden: > 0 adds the audio projector tensors (tensor_specs).
     """
     cfg = ModelConfig.of(cfg) if isinstance(cfg, dict) else cfg
     path = Path(path)
-    specs = tensor_specs(cfg)
+    specs = tensor_specs(cfg, audio_hidden)
     kv = metadata(cfg, f"qwen3-asr-synthetic-{cfg.hidden}", tokenizer)
     infos = []
     offset = 0

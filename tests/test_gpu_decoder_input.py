@@ -134,3 +134,86 @@ def test_decoder_input_errors(pkg, golden, files):
         assert dec.length(s) == 0
         ids_out = dec.prefill_ids([s], [ids], [audio], aid)   # the handle is still usable
         assert ids_out.shape == (1,)
+
+
+# ---- audio projector (src/audio-encoder.cpp:848-856) ----
+
+@pytest.fixture(scope="module")
+def proj_files(synth, tmp_path_factory):
+    d = tmp_path_factory.mktemp("proj")
+    return {w: synth.write_gguf(d / f"tiny_proj_{w}.gguf", dict(synth.TINY), seed=3, weights=w, norm_init="one_plus",
+                                tokenizer="bytes", audio_hidden=256) for w in ("f32", "bf16")}
+
+
+def torch_projector(t, x):
+    """The reference's PyTorch restatement of the projector
+    (benchmarks/check_decoder_input.py:113-123), in float64."""
+    import torch.nn.functional as F
+    g = {k: torch.tensor(np.array(t[k]), dtype=torch.float64) for k in t if k.startswith("audio.")}
+    y = F.layer_norm(x, (x.shape[-1],), g["audio.post_norm.weight"], g["audio.post_norm.bias"], eps=1e-5)
+    y = F.linear(y, g["audio.proj.0.weight"], g["audio.proj.0.bias"])
+    y = F.gelu(y)
+    return F.linear(y, g["audio.proj.1.weight"], g["audio.proj.1.bias"])
+
+
+@pytest.mark.parametrize("w", ["f32", "bf16"])
+def test_audio_projector_matches_torch(pkg, synth, proj_files, w):
+    """f32 weights: within 1e-5 of the float64 restatement (max |diff| / max
+    |ref|); bf16 weights and activations: within 2e-2."""
+    t = synth.read_gguf(proj_files[w])
+    rng = np.random.default_rng(41)
+    enc = rng.standard_normal((300, 256)).astype(np.float32)
+    want = torch_projector(t, torch.tensor(enc, dtype=torch.float64)).numpy()
+    with decoder(pkg, proj_files[w], pkg.F32 if w == "f32" else pkg.BF16) as dec:
+        assert dec.audio_projector_width() == 256
+        x = torch.tensor(enc, device="cuda")
+        out = torch.full((300, 256), float("nan"), device="cuda")
+        for _ in range(2):
+            dec.audio_project(300, x.data_ptr(), out.data_ptr())
+            torch.cuda.synchronize()
+            dec.sync()
+            got = out.cpu().numpy().astype(np.float64)
+            err = np.abs(got - want).max() / np.abs(want).max()
+            assert err < (1e-5 if w == "f32" else 2e-2), err
+
+
+def test_prefill_from_projected_audio(pkg, synth, checker, golden, proj_files):
+    """Audio encoder rows -> projector (device) -> decoder input (device) ->
+    prefill, against prefill of rows spliced on the host from the torch
+    projector's output: identical greedy ids, logits within the f32 parity bar
+    of 1e-3 (the projected rows themselves differ from the float64
+    restatement by ~1e-5, which two decoder layers amplify; measured 2.7e-4)."""
+    t = synth.read_gguf(proj_files["f32"])
+    embd = np.array(t["text.token_embd.weight"])
+    aid = int(golden["audio_token_id"])
+    cs = cases(golden)
+    rng = np.random.default_rng(43)
+    encs = [rng.standard_normal((a.shape[0], 256)).astype(np.float32) for _, a in cs]
+    with decoder(pkg, proj_files["f32"], pkg.F32, streams=8) as dec:
+        projected = []
+        for e in encs:
+            o = torch.empty((e.shape[0], 256), device="cuda")
+            dec.audio_project(e.shape[0], torch.tensor(e, device="cuda").data_ptr(), o.data_ptr())
+            projected.append(o)
+        torch.cuda.synchronize()
+        s1 = [dec.open() for _ in cs]
+        ids1, lg1 = dec.prefill_ids(s1, [i for i, _ in cs], projected, aid, want_logits=True)
+        rows = []
+        for (i, _), e in zip(cs, encs):
+            p = torch_projector(t, torch.tensor(e, dtype=torch.float64)).numpy().astype(np.float32)
+            rc, r = checker.decoder_input(i, embd, p, aid)
+            assert rc == 0
+            rows.append(r)
+        s2 = [dec.open() for _ in cs]
+        ids2, lg2 = dec.prefill(s2, rows, want_logits=True)
+    assert np.array_equal(ids1, ids2)
+    assert rel_err(lg1, lg2) < 1e-3
+
+
+def test_audio_projector_absent(pkg, files):
+    with decoder(pkg, files["f32"], pkg.F32) as dec:
+        assert dec.audio_projector_width() == 0
+        x = torch.zeros((4, 256), device="cuda")
+        with pytest.raises(pkg.QkvError) as ei:
+            dec.audio_project(4, x.data_ptr(), x.data_ptr())
+        assert "no audio projector" in str(ei.value)
