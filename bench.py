@@ -361,10 +361,12 @@ def run_model(args) -> int:
     n_streams = 64 if big else 32
     steps = args.steps
     tmpdir = Path(os.environ.get("QWENASR_BENCH_TMP", "/dev/shm" if Path("/dev/shm").is_dir() else tempfile.gettempdir()))
-    path = tmpdir / f"qwen3asr_{'1p7b' if big else '0p6b'}_bf16_seed0_r{rank}.gguf"
+    audio_hidden = 896 if big else 0   # config 3 also runs the audio projector (encoder width 896)
+    path = tmpdir / f"qwen3asr_{'1p7b' if big else '0p6b'}_bf16_seed0{'_ap' if big else ''}_r{rank}.gguf"
     t0 = time.perf_counter()
     if not path.exists():
-        synth.write_gguf(path, cfg, seed=0, weights="bf16", norm_init="normal", tokenizer=False)
+        synth.write_gguf(path, cfg, seed=0, weights="bf16", norm_init="normal", tokenizer=False,
+                         audio_hidden=audio_hidden)
     gen_s = time.perf_counter() - t0
     embd = synth.read_gguf(path)["text.token_embd.weight"]
     prompt_ids = []
@@ -430,8 +432,32 @@ def run_model(args) -> int:
 
         rows_s = min(timed(lambda ss: dec.prefill(ss, prompts)) for _ in range(2))
         ids_s = min(timed(lambda ss: dec.prefill_ids(ss, ids_l, audio_l, aid)) for _ in range(2))
+        # From audio-encoder rows on the device: projector, then the same prefill.
+        # All streams' encoder rows in one block, projected by one call.
+        gdev = torch.Generator(device=torch.device("cuda", local)).manual_seed(1003 + rank)
+        n_enc = 390 * len(prompts)
+        enc = torch.randn((n_enc, audio_hidden), device=torch.device("cuda", local), generator=gdev)
+        proj = torch.empty((n_enc, cfg["hidden"]), device=torch.device("cuda", local))
+        proj_l = [proj[390 * k:390 * (k + 1)] for k in range(len(prompts))]
+
+        def project():
+            dec.audio_project(n_enc, enc.data_ptr(), proj.data_ptr())
+
+        project()
+        torch.cuda.synchronize()
+        pe0, pe1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        pe0.record()
+        project()
+        pe1.record()
+        torch.cuda.synchronize()
+        proj_ms = pe0.elapsed_time(pe1)
+        enc_s = min(timed(lambda ss: (project(), dec.prefill_ids(ss, ids_l, proj_l, aid))) for _ in range(2))
         T = int(sum(p.shape[0] for p in prompts))
         prefill_cmp = {"prefill_warm_rows_s": round(rows_s, 4), "prefill_warm_ids_device_audio_s": round(ids_s, 4),
+                       "prefill_warm_from_encoder_rows_s": round(enc_s, 4),
+                       "audio_projector_ms": round(proj_ms, 3),
+                       "audio_projector_tflops": round(n_enc * 2.0 * audio_hidden *
+                                       (audio_hidden + cfg["hidden"]) / (proj_ms / 1e3) / 1e12, 1),
                        "prefill_h2d_bytes_rows": T * cfg["hidden"] * 4, "prefill_h2d_bytes_ids": T * 4}
         streams = []
     if rank == 0:
