@@ -30,6 +30,7 @@ extern "C" {
 #define QKV_ABI_VERSION 1
 
 typedef struct qkv_handle qkv_handle;
+typedef struct qkv_tokenizer qkv_tokenizer;
 typedef struct qkv_pager qkv_pager;
 
 enum qkv_status {
@@ -301,6 +302,21 @@ int qkv_kv_attend_noalloc(const void *pool_layer, int32_t kv_dtype, const float 
  * GGML ne (unused dims 1).  The loader checks of gguf-model.cpp:110-162 apply. */
 int qkv_gguf_tensor(const char *gguf_path, const char *name, int64_t *ne_out, int32_t *n_dims, int32_t *ggml_type,
                     void *data_out, size_t cap_bytes, char *err, size_t err_len);
+
+/* ---- host-only detokenisation (no GPU) ----
+ * The step after the greedy loop: qwenasr_tokenizer_decode (src/tokenizer.cpp:
+ * 482-527).  qkv_tokenizer_open reads the byte-level BPE vocabulary and the
+ * seven special-token ids from a model file's metadata (the keys and checks
+ * of qwenasr_tokenizer_load_gguf, :306-372; QKV_ERR_FORMAT with the
+ * reference's message when incomplete).  qkv_tokenizer_decode writes the bytes
+ * of ids[0..n) (out-of-range ids skipped; the special tokens too when
+ * skip_special) to out, *len = their count; QKV_ERR_CAPACITY when they do not
+ * fit in cap (*len still tells how many).  A token whose last UTF-8 sequence
+ * is cut short is read up to its end (the reference reads past it). */
+int qkv_tokenizer_open(const char *gguf_path, qkv_tokenizer **out, char *err, size_t err_len);
+int qkv_tokenizer_decode(const qkv_tokenizer *t, const int32_t *ids, int32_t n, int32_t skip_special, char *out,
+                         size_t cap, size_t *len);
+void qkv_tokenizer_close(qkv_tokenizer *t);
 
 /* ---- host-only page allocator (no GPU needed; used inside every handle) ----
  * Pages hold page_tokens tokens of every layer's K and V for one stream. */

@@ -91,6 +91,8 @@ def ref_lib():
         _ref.ref_layer_forward.argtypes = [C.c_char_p, P, C.c_int, _F, C.c_int, _F]
         _ref.ref_decoder_input.argtypes = [C.c_char_p, C.c_int, C.c_int, _F, C.c_int, C.c_char_p, C.c_char_p, C.c_int,
                                            _I, _F, C.POINTER(C.c_int)]
+        _ref.ref_tokenizer_decode.argtypes = [C.c_char_p, _I, C.c_int, C.c_int, C.c_char_p, C.c_int,
+                                              C.POINTER(C.c_int)]
         _ref.ref_last_error.restype = C.c_char_p
     return _ref
 
@@ -293,3 +295,16 @@ def ref_decoder_input(gguf: str, audio: np.ndarray, audio_token_id: int, system_
     msg = ref_lib().ref_last_error().decode() if rc else ""
     n = t.value if rc == 0 else 0
     return rc, ids[:n].copy(), rows[:n].copy(), msg
+
+
+def ref_tokenizer_decode(gguf: str, ids, skip_special: bool = True) -> bytes:
+    """The reference's own qwenasr_tokenizer_decode on `gguf`'s tokenizer."""
+    ids = np.ascontiguousarray(ids, np.int32)
+    cap = 64 + 32 * ids.shape[0]
+    buf = C.create_string_buffer(cap)
+    n = C.c_int(0)
+    rc = ref_lib().ref_tokenizer_decode(str(gguf).encode(), _i(ids), ids.shape[0], int(skip_special), buf, cap,
+                                        C.byref(n))
+    if rc != 0:
+        raise RuntimeError(f"ref_tokenizer_decode failed ({rc}): {ref_lib().ref_last_error().decode()}")
+    return buf.raw[:n.value]

@@ -124,6 +124,18 @@ int ref_decoder_input(const char *gguf, int audio_tokens, int hidden, const floa
     return 0;
 }
 
+// qwenasr_tokenizer_decode (tokenizer.cpp:482-527) with the tokenizer of `gguf`:
+// bytes into out (cap), *len = their count (return 3 when they do not fit).
+int ref_tokenizer_decode(const char *gguf, const int32_t *ids, int n, int skip_special, char *out, int cap, int *len) {
+    QwenAsrTokenizer tok;
+    if (!qwenasr_tokenizer_load_gguf(gguf, &tok, &g_error)) return 1;
+    const std::string s = qwenasr_tokenizer_decode(tok, std::vector<int32_t>(ids, ids + n), skip_special != 0);
+    *len = static_cast<int>(s.size());
+    if (static_cast<int>(s.size()) > cap) return 3;
+    std::memcpy(out, s.data(), s.size());
+    return 0;
+}
+
 }  // extern "C"
 
 // The reference's GGML audio encoder is not built here (GGML is an empty

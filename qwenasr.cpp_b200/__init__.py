@@ -17,6 +17,7 @@ PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "libqwenasr_b200.so"
 
 QKV_OK = 0
+QKV_ERR_CAPACITY = 3
 STATUS = {0: "QKV_OK", 1: "QKV_ERR_INVALID_ARG", 2: "QKV_ERR_OUT_OF_PAGES", 3: "QKV_ERR_CAPACITY",
           4: "QKV_ERR_CUDA", 5: "QKV_ERR_DEVICE", 6: "QKV_ERR_IO", 7: "QKV_ERR_FORMAT", 8: "QKV_ERR_STATE",
           9: "QKV_ERR_NO_DEVICE"}
@@ -85,6 +86,10 @@ SIGNATURES = {
     "qkv_gemm_bf16": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P]),
     "qkv_prefill_attend": (C.c_int, [_P, C.c_int32, C.c_int32, _P, _P, _P, _P, _P]),
     "qkv_prefill_attend_q16": (C.c_int, [_P, C.c_int32, C.c_int32, _P, _P, _P, _P, _P]),
+    "qkv_tokenizer_open": (C.c_int, [C.c_char_p, C.POINTER(C.c_void_p), C.c_char_p, C.c_size_t]),
+    "qkv_tokenizer_decode": (C.c_int, [_P, _I32P, C.c_int32, C.c_int32, C.c_char_p, C.c_size_t,
+                                       C.POINTER(C.c_size_t)]),
+    "qkv_tokenizer_close": (None, [_P]),
     "qkv_gguf_tensor": (C.c_int, [C.c_char_p, C.c_char_p, _I64P, _I32P, _I32P, _P, C.c_size_t, C.c_char_p,
                                   C.c_size_t]),
     "qkv_pager_create": (_P, [C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_uint32]),
@@ -140,6 +145,44 @@ def read_gguf_config(path) -> dict:
     if rc != QKV_OK:
         raise QkvError(rc, err.value.decode())
     return {f: getattr(cfg, f) for f, _ in ModelConfig._fields_}
+
+
+class Tokenizer:
+    """Detokeniser of a model file's byte-level BPE vocabulary (host only):
+    Tokenizer(path).decode(ids, skip_special=True) -> bytes."""
+
+    def __init__(self, path):
+        h = C.c_void_p()
+        err = C.create_string_buffer(512)
+        rc = lib.qkv_tokenizer_open(str(path).encode(), C.byref(h), err, 512)
+        if rc != QKV_OK:
+            raise QkvError(rc, err.value.decode())
+        self.h = h
+
+    def decode(self, ids, skip_special: bool = True) -> bytes:
+        ids = _i32(ids)
+        n = C.c_size_t(0)
+        buf = C.create_string_buffer(max(16 * len(ids), 64))
+        rc = lib.qkv_tokenizer_decode(self.h, _ptr(ids, C.c_int32), len(ids), int(skip_special), buf, len(buf),
+                                      C.byref(n))
+        if rc == QKV_ERR_CAPACITY:
+            buf = C.create_string_buffer(n.value)
+            rc = lib.qkv_tokenizer_decode(self.h, _ptr(ids, C.c_int32), len(ids), int(skip_special), buf,
+                                          len(buf), C.byref(n))
+        if rc != QKV_OK:
+            raise QkvError(rc, "tokenizer decode failed")
+        return buf.raw[:n.value]
+
+    def close(self):
+        if self.h:
+            lib.qkv_tokenizer_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def gguf_tensor(path, name: str, want_data: bool = True):

@@ -99,7 +99,9 @@ bool read_value(Cursor &c, uint32_t type, GgufValue *v) {
             v->arr_n = c.get<uint64_t>();
             if (!c.ok) return false;
             if (v->arr_type == kString) {
-                for (uint64_t k = 0; k < v->arr_n && c.ok; ++k) c.string(nullptr);
+                if (v->arr_n > c.size - c.pos) return false;   // each string takes at least 8 bytes
+                v->strs.resize(static_cast<size_t>(v->arr_n));
+                for (uint64_t k = 0; k < v->arr_n && c.ok; ++k) c.string(&v->strs[static_cast<size_t>(k)]);
             } else {
                 const size_t es = scalar_size(v->arr_type);
                 if (es == 0) return false;  // nested arrays are not used by GGUF writers here

@@ -36,6 +36,7 @@ struct GgufValue {
     std::string s;
     uint32_t arr_type = 0;
     uint64_t arr_n = 0;
+    std::vector<std::string> strs;   // string arrays (tokenizer vocabulary and merges)
 };
 
 class GgufFile {

@@ -22,6 +22,7 @@ import numpy as np
 
 GGUF_ALIGN = 32
 GGML_F32 = 0
+GGML_BF16 = 30
 
 QWEN3_ASR_0_6B = dict(n_layers=28, hidden=1024, n_heads=16, n_kv_heads=8, head_dim=128,
                       intermediate=3072, vocab=151936, rope_theta=1.0e6, rms_norm_eps=1.0e-6)
@@ -188,26 +189,33 @@ def _gen_tensor(rng: np.random.Generator, shape, kind: str, std: float, norm_ini
 
 def write_gguf(path: str | Path, cfg: ModelConfig | dict, seed: int = 0, std: float = 0.02,
                weights: str = "f32", norm_init: str = "normal", tokenizer: bool | str = True,
-               audio_hidden: int = 0) -> Path:
+               audio_hidden: int = 0, storage: str = "f32") -> Path:
     """Write a random-init text-decoder GGUF; returns the path.
 
     weights: "f32" (plain N(0,std) floats) or "bf16" (bf16-rounded, stored f32).
     norm_init: "normal" -> norm weights ~ N(0,std) like every other tensor;
                "one_plus" -> 1 + N(0,std) (a trained-like scale).
     audio_hidden: > 0 adds the audio projector tensors (tensor_specs).
+    storage: "f32" (GGML type 0, as the reference's converter writes) or
+             "bf16" (GGML type 30: the bf16-rounded values' upper 16 bits).
     """
+    if storage not in ("f32", "bf16"):
+        raise ValueError(storage)
+    if storage == "bf16":
+        weights = "bf16"
     cfg = ModelConfig.of(cfg) if isinstance(cfg, dict) else cfg
     path = Path(path)
     specs = tensor_specs(cfg, audio_hidden)
     kv = metadata(cfg, f"qwen3-asr-synthetic-{cfg.hidden}", tokenizer)
     infos = []
     offset = 0
+    es, gtype = (4, GGML_F32) if storage == "f32" else (2, GGML_BF16)
     for name, shape, _ in specs:
-        nb = int(np.prod(shape)) * 4
+        nb = int(np.prod(shape)) * es
         ne = tuple(reversed(shape))
         nm = name.encode()
         infos.append(struct.pack("<Q", len(nm)) + nm + struct.pack("<I", len(ne)) +
-                     b"".join(struct.pack("<Q", d) for d in ne) + struct.pack("<IQ", GGML_F32, offset))
+                     b"".join(struct.pack("<Q", d) for d in ne) + struct.pack("<IQ", gtype, offset))
         offset += (nb + GGUF_ALIGN - 1) // GGUF_ALIGN * GGUF_ALIGN
     head = b"GGUF" + struct.pack("<IQQ", 3, len(specs), len(kv)) + b"".join(kv) + b"".join(infos)
     pad = (-len(head)) % GGUF_ALIGN
@@ -216,6 +224,8 @@ def write_gguf(path: str | Path, cfg: ModelConfig | dict, seed: int = 0, std: fl
         f.write(head + b"\0" * pad)
         for name, shape, kind in specs:
             a = _gen_tensor(rng, shape, kind, std, norm_init, weights == "bf16")
+            if storage == "bf16":
+                a = (np.ascontiguousarray(a).view(np.uint32) >> np.uint32(16)).astype(np.uint16)
             f.write(memoryview(np.ascontiguousarray(a)).cast("B"))
             f.write(b"\0" * ((-a.nbytes) % GGUF_ALIGN))
     return path
@@ -224,7 +234,8 @@ def write_gguf(path: str | Path, cfg: ModelConfig | dict, seed: int = 0, std: fl
 # ---- minimal reader (for building prompts and for the oracle) ----
 
 def read_gguf(path: str | Path) -> dict[str, np.ndarray]:
-    """name -> read-only float32 memmap array (numpy shape = reversed ne)."""
+    """name -> float32 array (numpy shape = reversed ne): a read-only memmap
+    for f32 tensors, a widened copy for bf16 ones."""
     path = Path(path)
     buf = np.memmap(path, dtype=np.uint8, mode="r")
     pos = 0
@@ -280,10 +291,14 @@ def read_gguf(path: str | Path) -> dict[str, np.ndarray]:
     data0 = (pos + align - 1) // align * align
     out = {}
     for name, ne, t, off in infos:
-        if t != GGML_F32:
-            raise ValueError(f"{name}: only f32 tensors are read here")
         shape = tuple(reversed(ne))
-        out[name] = np.ndarray(shape, dtype=np.float32, buffer=buf, offset=data0 + off)
+        if t == GGML_F32:
+            out[name] = np.ndarray(shape, dtype=np.float32, buffer=buf, offset=data0 + off)
+        elif t == GGML_BF16:   # widened to f32 (a copy)
+            bits = np.ndarray(shape, dtype=np.uint16, buffer=buf, offset=data0 + off)
+            out[name] = (bits.astype(np.uint32) << np.uint32(16)).view(np.float32)
+        else:
+            raise ValueError(f"{name}: only f32 and bf16 tensors are read here")
     return out
 
 

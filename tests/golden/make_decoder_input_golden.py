@@ -12,7 +12,10 @@ tokens sit at ids 256..262, inside the 1000-row embedding table.
 
 Recorded per case: the prompt ids, the audio rows, a SHA-256 of the
 reference's output rows (f32 bytes) and, for the smallest case, the rows
-themselves; for the reference's own failure cases, its error message.
+themselves; for the reference's own failure cases, its error message.  Also
+detokenisation known answers: the bytes qwenasr_tokenizer_decode
+(src/tokenizer.cpp:482-527) gives for a few id sequences, with and without
+skipping the special tokens.
 
     python tests/golden/make_decoder_input_golden.py
 """
@@ -78,6 +81,14 @@ def main() -> None:
             assert rc != 0
             out[f"error_{k}"] = np.array(msg)
             print(f"error case {k}: {msg}")
+        detok = [out["ids_1"],
+                 np.array([300, 10, 32, 1000, -5, 257, 65, 0xC3, 0xA9, 999, 262], np.int32),
+                 np.arange(0, 1000, dtype=np.int32)]
+        for k, ids in enumerate(detok):
+            out[f"detok_ids_{k}"] = ids
+            for skip in (0, 1):
+                out[f"detok_bytes_{k}_{skip}"] = np.frombuffer(
+                    checker.ref_tokenizer_decode(str(path), ids, bool(skip)), np.uint8).copy()
     np.savez_compressed(HERE / "decoder_input.npz", **out)
     print("wrote", HERE / "decoder_input.npz")
 

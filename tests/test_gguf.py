@@ -89,3 +89,19 @@ def test_reader_rejects_damaged_files(pkg, tiny_files, tmp_path, damage):
     with pytest.raises(pkg.QkvError) as ei:
         pkg.gguf_tensor(p, "text.token_embd.weight")
     assert ei.value.code in (6, 7)
+
+
+def test_bf16_typed_file(pkg, synth, tmp_path):
+    """A file whose tensors are stored as GGML bf16 (type 30): the library's
+    reader (range checks of gguf-model.cpp:110-162) returns, per tensor, the
+    upper 16 bits of the f32 file of the same bf16-rounded values."""
+    a = synth.write_gguf(tmp_path / "f32.gguf", dict(synth.TINY), seed=0, weights="bf16", norm_init="one_plus",
+                         tokenizer=False)
+    b = synth.write_gguf(tmp_path / "bf16.gguf", dict(synth.TINY), seed=0, norm_init="one_plus", tokenizer=False,
+                         storage="bf16")
+    ta = synth.read_gguf(a)
+    for name in ("text.token_embd.weight", "text.blk.1.ffn_down.weight", "text.blk.0.attn_q_norm.weight"):
+        dims, ty, data = pkg.gguf_tensor(b, name)
+        assert ty == 30 and dims == list(reversed(ta[name].shape))
+        want = (np.ascontiguousarray(ta[name]).view(np.uint32) >> np.uint32(16)).astype(np.uint16)
+        assert np.array_equal(data.view(np.uint16).reshape(want.shape), want)

@@ -288,3 +288,23 @@ def test_prefill_rows_entry_matches_contiguous(pkg, synth, tiny_files):
         assert rc == 0
     assert np.array_equal(ids_rows, ids_cat)
     assert np.array_equal(logits_rows, logits_cat)
+
+
+@pytest.mark.parametrize("w", [0, 1])
+def test_bf16_typed_file_loads_like_f32_file(pkg, synth, tmp_path, w):
+    """The same bf16-rounded weights stored as f32 (as the reference's
+    converter writes) and as GGML bf16: identical greedy ids, logits within
+    the parity bars (f32 1e-3, bf16 1e-2): two prefills of one file already
+    differ by up to ~1.5e-4 (f32) / 2.4e-3 (bf16) because split-K sums are
+    atomic, while a wrong conversion would be off by orders of magnitude."""
+    a = synth.write_gguf(tmp_path / "f32.gguf", dict(synth.TINY), seed=0, weights="bf16", norm_init="one_plus",
+                         tokenizer=False)
+    b = synth.write_gguf(tmp_path / "bf16.gguf", dict(synth.TINY), seed=0, norm_init="one_plus", tokenizer=False,
+                         storage="bf16")
+    xs = prompts(synth, synth.read_gguf(a), 3, 500, lo=40, hi=120)
+    out = []
+    for path in (a, b):
+        with decoder(pkg, path, w=w, kv=1, streams=3, ctx=256, batch_tokens=512) as dec:
+            out.append(dec.prefill([dec.open() for _ in xs], xs, want_logits=True))
+    assert np.array_equal(out[0][0], out[1][0])
+    assert rel_err(out[0][1], out[1][1]) < (1e-3 if w == 0 else 1e-2)

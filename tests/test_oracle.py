@@ -172,3 +172,37 @@ def test_decoder_input_reference_live(dec_input, checker):
         assert rc == 0, msg
         assert np.array_equal(ids, g[f"ids_{k}"])
         assert _digest(rows) == str(g[f"rows_sha256_{k}"])
+
+
+# ---- detokenisation (src/tokenizer.cpp:482-527) ----
+
+def test_detokenize_matches_reference_known_answers(pkg, dec_input):
+    """qkv_tokenizer_decode against the bytes the reference's own
+    qwenasr_tokenizer_decode gave (fixture), with and without skipping the
+    special tokens: prompt ids, out-of-range and negative ids, every id."""
+    g, _, path = dec_input
+    tok = pkg.Tokenizer(path)
+    for k in range(3):
+        ids = g[f"detok_ids_{k}"]
+        for skip in (0, 1):
+            assert tok.decode(ids, bool(skip)) == g[f"detok_bytes_{k}_{skip}"].tobytes()
+    tok.close()
+
+
+def test_detokenize_reference_live(pkg, dec_input, checker):
+    if not checker.ref_available():
+        pytest.skip("oracle/_ref not built")
+    _, _, path = dec_input
+    tok = pkg.Tokenizer(path)
+    rng = np.random.default_rng(7)
+    for _ in range(20):
+        ids = rng.integers(-3, 1003, size=int(rng.integers(0, 300))).astype(np.int32)
+        for skip in (False, True):
+            assert tok.decode(ids, skip) == checker.ref_tokenizer_decode(str(path), ids, skip)
+
+
+def test_tokenizer_open_errors(pkg, synth, tmp_path):
+    p = synth.write_gguf(tmp_path / "none.gguf", dict(synth.TINY), seed=0, tokenizer=False)
+    with pytest.raises(pkg.QkvError) as ei:
+        pkg.Tokenizer(p)
+    assert "incomplete" in str(ei.value)
