@@ -303,7 +303,7 @@ int qkv_kv_attend_noalloc(const void *pool_layer, int32_t kv_dtype, const float 
 int qkv_gguf_tensor(const char *gguf_path, const char *name, int64_t *ne_out, int32_t *n_dims, int32_t *ggml_type,
                     void *data_out, size_t cap_bytes, char *err, size_t err_len);
 
-/* ---- host-only detokenisation (no GPU) ----
+/* ---- host-only tokenizer: ASR prompt ids and detokenisation (no GPU) ----
  * The step after the greedy loop: qwenasr_tokenizer_decode (src/tokenizer.cpp:
  * 482-527).  qkv_tokenizer_open reads the byte-level BPE vocabulary and the
  * seven special-token ids from a model file's metadata (the keys and checks
@@ -316,6 +316,17 @@ int qkv_gguf_tensor(const char *gguf_path, const char *name, int64_t *ne_out, in
 int qkv_tokenizer_open(const char *gguf_path, qkv_tokenizer **out, char *err, size_t err_len);
 int qkv_tokenizer_decode(const qkv_tokenizer *t, const int32_t *ids, int32_t n, int32_t skip_special, char *out,
                          size_t cap, size_t *len);
+/* Encoding, as qwenasr_tokenizer_encode (src/tokenizer.cpp:438-480): the ids
+ * of text[0..text_len) (plus the end-of-sequence id when add_eos) into
+ * ids[0..cap), *n = their count (QKV_ERR_CAPACITY when more than cap; *n
+ * still tells how many).  qkv_asr_prompt_ids encodes the ASR prompt of
+ * qwenasr_build_asr_prompt (:529-549): system text, audio_tokens audio
+ * placeholders, and the language line when language is non-empty; its ids go
+ * to qkv_prefill_ids together with the audio rows. */
+int qkv_tokenizer_encode(const qkv_tokenizer *t, const char *text, size_t text_len, int32_t add_eos, int32_t *ids,
+                         size_t cap, size_t *n);
+int qkv_asr_prompt_ids(const qkv_tokenizer *t, int32_t audio_tokens, const char *system_text, const char *language,
+                       int32_t *ids, size_t cap, size_t *n);
 void qkv_tokenizer_close(qkv_tokenizer *t);
 
 /* ---- host-only page allocator (no GPU needed; used inside every handle) ----

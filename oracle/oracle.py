@@ -93,6 +93,8 @@ def ref_lib():
                                            _I, _F, C.POINTER(C.c_int)]
         _ref.ref_tokenizer_decode.argtypes = [C.c_char_p, _I, C.c_int, C.c_int, C.c_char_p, C.c_int,
                                               C.POINTER(C.c_int)]
+        _ref.ref_tokenizer_encode.argtypes = [C.c_char_p, C.c_char_p, C.c_int, C.c_int, _I, C.c_int,
+                                              C.POINTER(C.c_int)]
         _ref.ref_last_error.restype = C.c_char_p
     return _ref
 
@@ -308,3 +310,15 @@ def ref_tokenizer_decode(gguf: str, ids, skip_special: bool = True) -> bytes:
     if rc != 0:
         raise RuntimeError(f"ref_tokenizer_decode failed ({rc}): {ref_lib().ref_last_error().decode()}")
     return buf.raw[:n.value]
+
+
+def ref_tokenizer_encode(gguf: str, text, add_eos: bool = False) -> np.ndarray:
+    """The reference's own qwenasr_tokenizer_encode on `gguf`'s tokenizer."""
+    b = text.encode() if isinstance(text, str) else bytes(text)
+    cap = 16 + 2 * len(b)
+    ids = np.zeros(cap, np.int32)
+    n = C.c_int(0)
+    rc = ref_lib().ref_tokenizer_encode(str(gguf).encode(), b, len(b), int(add_eos), _i(ids), cap, C.byref(n))
+    if rc != 0:
+        raise RuntimeError(f"ref_tokenizer_encode failed ({rc}): {ref_lib().ref_last_error().decode()}")
+    return ids[:n.value].copy()

@@ -136,6 +136,19 @@ int ref_tokenizer_decode(const char *gguf, const int32_t *ids, int n, int skip_s
     return 0;
 }
 
+// qwenasr_tokenizer_encode (tokenizer.cpp:438-480) with the tokenizer of `gguf`.
+int ref_tokenizer_encode(const char *gguf, const char *text, int text_len, int add_eos, int32_t *ids, int cap,
+                         int *n) {
+    QwenAsrTokenizer tok;
+    if (!qwenasr_tokenizer_load_gguf(gguf, &tok, &g_error)) return 1;
+    const std::vector<int32_t> v = qwenasr_tokenizer_encode(tok, std::string(text, static_cast<size_t>(text_len)),
+                                                            add_eos != 0);
+    *n = static_cast<int>(v.size());
+    if (*n > cap) return 3;
+    for (int i = 0; i < *n; ++i) ids[i] = v[static_cast<size_t>(i)];
+    return 0;
+}
+
 }  // extern "C"
 
 // The reference's GGML audio encoder is not built here (GGML is an empty

@@ -90,6 +90,10 @@ SIGNATURES = {
     "qkv_tokenizer_decode": (C.c_int, [_P, _I32P, C.c_int32, C.c_int32, C.c_char_p, C.c_size_t,
                                        C.POINTER(C.c_size_t)]),
     "qkv_tokenizer_close": (None, [_P]),
+    "qkv_tokenizer_encode": (C.c_int, [_P, C.c_char_p, C.c_size_t, C.c_int32, _I32P, C.c_size_t,
+                                       C.POINTER(C.c_size_t)]),
+    "qkv_asr_prompt_ids": (C.c_int, [_P, C.c_int32, C.c_char_p, C.c_char_p, _I32P, C.c_size_t,
+                                     C.POINTER(C.c_size_t)]),
     "qkv_gguf_tensor": (C.c_int, [C.c_char_p, C.c_char_p, _I64P, _I32P, _I32P, _P, C.c_size_t, C.c_char_p,
                                   C.c_size_t]),
     "qkv_pager_create": (_P, [C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_uint32]),
@@ -172,6 +176,29 @@ class Tokenizer:
         if rc != QKV_OK:
             raise QkvError(rc, "tokenizer decode failed")
         return buf.raw[:n.value]
+
+    def _ids(self, call):
+        n = C.c_size_t(0)
+        out = np.zeros(256, np.int32)
+        rc = call(out, n)
+        if rc == QKV_ERR_CAPACITY:
+            out = np.zeros(n.value, np.int32)
+            rc = call(out, n)
+        if rc != QKV_OK:
+            raise QkvError(rc, "tokenizer encode failed")
+        return out[:n.value].copy()
+
+    def encode(self, text, add_eos: bool = False) -> np.ndarray:
+        """Ids of text (str or bytes), as qwenasr_tokenizer_encode."""
+        b = text.encode() if isinstance(text, str) else bytes(text)
+        return self._ids(lambda out, n: lib.qkv_tokenizer_encode(self.h, b, len(b), int(add_eos),
+                                                                 _ptr(out, C.c_int32), len(out), C.byref(n)))
+
+    def asr_prompt_ids(self, audio_tokens: int, system_text: str = "", language: str = "") -> np.ndarray:
+        """Ids of the ASR prompt (qwenasr_build_asr_prompt, then encoded)."""
+        return self._ids(lambda out, n: lib.qkv_asr_prompt_ids(self.h, int(audio_tokens), system_text.encode(),
+                                                               language.encode(), _ptr(out, C.c_int32), len(out),
+                                                               C.byref(n)))
 
     def close(self):
         if self.h:

@@ -44,6 +44,41 @@ SPECIAL_STRINGS = dict(endoftext="<|endoftext|>", im_start="<|im_start|>", im_en
                        asr_text="<asr_text>")
 
 
+BPE_SAMPLE = ("You transcribe speech. Be exact. The quick brown fox jumps over the lazy dog; the dog "
+              "sleeps. language English German French system user assistant transcription of the audio "
+              "that follows, with punctuation and numbers like 2024 or 3.14, isn't it? We're there.\n")
+
+
+def byte_merges(n_merges: int = 200) -> list[tuple[str, str]]:
+    """A small byte-level BPE merge table learned from BPE_SAMPLE (most
+    frequent adjacent pair first, ties broken by the pair's text), so the
+    synthetic tokenizer exercises the merge path.  Words carry their leading
+    space, as the byte-level pre-tokeniser keeps it."""
+    sym = byte_symbols()
+    words = []
+    for i, w in enumerate(BPE_SAMPLE.split(" ")):
+        text = (" " if i else "") + w
+        words.append([sym[b] for b in text.encode()])
+    merges = []
+    for _ in range(n_merges):
+        counts: dict[tuple[str, str], int] = {}
+        for w in words:
+            for a, b in zip(w, w[1:]):
+                counts[(a, b)] = counts.get((a, b), 0) + 1
+        if not counts:
+            break
+        best = min(counts, key=lambda k: (-counts[k], k))
+        merges.append(best)
+        for w in words:
+            i = 0
+            while i + 1 < len(w):
+                if (w[i], w[i + 1]) == best:
+                    w[i:i + 2] = [w[i] + w[i + 1]]
+                else:
+                    i += 1
+    return merges
+
+
 def byte_symbols() -> list[str]:
     """The byte-level BPE alphabet: byte b -> one printable character (the
     published GPT-2 mapping: printable Latin-1 bytes map to themselves, the
@@ -158,11 +193,20 @@ def metadata(cfg: ModelConfig, name: str, tokenizer: bool | str) -> list[bytes]:
           _kv_u32("qwen3-asr.token.audio_token_id", ids["audio"]),
           _kv_u32("qwen3-asr.token.audio_start_token_id", ids["audio_start"]),
           _kv_u32("qwen3-asr.token.audio_end_token_id", ids["audio_end"])]
+    merges: list[str] = []
     if tokenizer == "bytes":
         n = max(cfg.vocab, ids["asr_text"] + 1)
         tokens = byte_symbols() + [f"<t{i}>" for i in range(256, n)]
         for k, i in ids.items():
             tokens[i] = SPECIAL_STRINGS[k]
+        # merged tokens right after the special ids (as many as fit)
+        nxt = max(ids.values()) + 1
+        for a, b in byte_merges():
+            if nxt >= n:
+                break
+            tokens[nxt] = a + b
+            merges.append(f"{a} {b}")
+            nxt += 1
     else:
         n = max(cfg.vocab, ids["asr_text"] + 1)
         tokens = [f"<t{i}>" for i in range(n)]
@@ -170,7 +214,7 @@ def metadata(cfg: ModelConfig, name: str, tokenizer: bool | str) -> list[bytes]:
         kv += [_kv_str("tokenizer.ggml.model", "gpt2"),
                _kv_arr_str("tokenizer.ggml.tokens", tokens),
                _kv_arr_i32("tokenizer.ggml.token_type", np.ones(n, np.int32)),
-               _kv_arr_str("tokenizer.ggml.merges", []),
+               _kv_arr_str("tokenizer.ggml.merges", merges),
                _kv_u32("tokenizer.ggml.eos_token_id", ids["im_end"]),
                _kv_u32("qwen3-asr.token.endoftext_token_id", ids["endoftext"]),
                _kv_u32("qwen3-asr.token.im_start_token_id", ids["im_start"]),

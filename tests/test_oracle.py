@@ -206,3 +206,31 @@ def test_tokenizer_open_errors(pkg, synth, tmp_path):
     with pytest.raises(pkg.QkvError) as ei:
         pkg.Tokenizer(p)
     assert "incomplete" in str(ei.value)
+
+
+# ---- tokenizer encode and the ASR prompt (src/tokenizer.cpp:438-480, 529-549) ----
+
+def test_asr_prompt_ids_match_reference(pkg, dec_input):
+    """qkv_asr_prompt_ids gives the ids the reference's own template +
+    encoder gave for the fixture's prompts (system text, language, audio
+    placeholders; the synthetic tokenizer has a learned merge table)."""
+    g, _, path = dec_input
+    tok = pkg.Tokenizer(path)
+    a = [5, 37, 130]
+    for k in range(3):
+        ids = tok.asr_prompt_ids(a[k], str(g[f"system_{k}"]), str(g[f"language_{k}"]))
+        assert ids.tolist() == g[f"ids_{k}"].tolist()
+
+
+def test_encode_reference_live(pkg, dec_input, checker):
+    if not checker.ref_available():
+        pytest.skip("oracle/_ref not built")
+    _, _, path = dec_input
+    tok = pkg.Tokenizer(path)
+    rng = np.random.default_rng(11)
+    pieces = ["the", " quick", "isn't", "'LL", " 3.14", "\n\n", "  ", "\t", "Grüße", "日本", "<|im_end|>",
+              "<|audio_pad|>", "<asr_text>", "!?", "speech", " We're", "\r\n", "x", "2024", " ", "é"]
+    for _ in range(40):
+        text = "".join(rng.choice(pieces, size=int(rng.integers(0, 30))))
+        for eos in (False, True):
+            assert tok.encode(text, eos).tolist() == checker.ref_tokenizer_encode(str(path), text, eos).tolist()
