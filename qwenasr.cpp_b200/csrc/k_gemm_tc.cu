@@ -507,6 +507,18 @@ template <int BN> cudaError_t prepare_bn() {
                                 static_cast<int>(TcTraits<BN>::kSmem));
 }
 
+// Zeroes C before a K-split GEMM adds its partial sums into it.  A kernel
+// rather than a memset, so the launch chain (programmatic dependent launch)
+// is not broken: the GEMM behind it starts and streams its weights while this
+// and the kernels before it finish.
+__global__ void zero_f32_kernel(float4 *c, size_t n4) {
+    pdl_trigger();
+    pdl_wait();   // earlier kernels may still read C
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        c[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
 // Unit order: weight tiles fastest once the token operand outgrows a share of
 // L2 (the weights, <= 50 MB for every decoder projection, then stay resident
 // while the token tiles stream once); token tiles fastest otherwise.
@@ -527,7 +539,15 @@ cudaError_t launch_bn(const void *X, const void *W, float *C, int M, int N, int 
     splits = (ktiles + kps - 1) / kps;     // every split owns >= 1 k-tile
     if (act && splits != 1) return cudaErrorInvalidValue;
     if (splits > 1 && !accumulate) {
-        cudaError_t e = cudaMemsetAsync(C, 0, static_cast<size_t>(M) * N * sizeof(float), st);
+        const size_t n = static_cast<size_t>(M) * N;
+        cudaError_t e;
+        if (n % 4 == 0 && (reinterpret_cast<uintptr_t>(C) & 15) == 0) {
+            const size_t blocks = (n / 4 + 255) / 256;
+            e = launch_pdl(zero_f32_kernel, dim3(static_cast<unsigned>(blocks < 1184 ? blocks : 1184)), dim3(256), 0,
+                           st, reinterpret_cast<float4 *>(C), n / 4);
+        } else {
+            e = cudaMemsetAsync(C, 0, n * sizeof(float), st);
+        }
         if (e != cudaSuccess) return e;
     }
     TcParams p{M, N, K, kps, tiles_n, tiles_m, splits, weight_fastest(M, K, tiles_m) ? 1 : 0, C, accumulate, act, err};
@@ -608,10 +628,8 @@ bool gemm_tc_supported(int M, int N, int K) {
     return M > 0 && N > 0 && K > 0 && K % kBK == 0 && encoder() != nullptr;
 }
 
-cudaError_t launch_gemm_tc(const void *X, const void *W, float *C, int M, int N, int K, int accumulate, int num_sms,
-                           DevError *err, cudaStream_t st) {
-    if (M <= 0 || N <= 0) return cudaSuccess;
-    if (K % kBK != 0) return cudaErrorInvalidValue;
+namespace {
+GemmPlan choose_plan(int M, int N, int K, int num_sms) {
     GemmPlan pl = plan_gemm(M, N, K, num_sms);
     // Tuning override: QWENASR_B200_GEMM_PLAN="bn,splits" forces the plan (sweeps).
     static const char *forced = getenv("QWENASR_B200_GEMM_PLAN");
@@ -620,6 +638,24 @@ cudaError_t launch_gemm_tc(const void *X, const void *W, float *C, int M, int N,
         if (sscanf(forced, "%d,%d", &bn, &sp) == 2 && (bn == 32 || bn == 64 || bn == 128 || bn == 256) && sp >= 1)
             pl = {bn, sp};
     }
+    return pl;
+}
+}  // namespace
+
+int gemm_tc_kernels(int M, int N, int K, int accumulate, int num_sms) {
+    if (M <= 0 || N <= 0 || K % kBK != 0) return 0;
+    const GemmPlan pl = choose_plan(M, N, K, num_sms);
+    const int ktiles = K / kBK;
+    const int kps = (ktiles + pl.splits - 1) / pl.splits;
+    const int splits = (ktiles + kps - 1) / kps;
+    return (splits > 1 && !accumulate) ? 2 : 1;
+}
+
+cudaError_t launch_gemm_tc(const void *X, const void *W, float *C, int M, int N, int K, int accumulate, int num_sms,
+                           DevError *err, cudaStream_t st) {
+    if (M <= 0 || N <= 0) return cudaSuccess;
+    if (K % kBK != 0) return cudaErrorInvalidValue;
+    const GemmPlan pl = choose_plan(M, N, K, num_sms);
     switch (pl.bn) {
         case 32: return launch_bn<32>(X, W, C, M, N, K, accumulate, pl.splits, num_sms, err, st);
         case 64: return launch_bn<64>(X, W, C, M, N, K, accumulate, pl.splits, num_sms, err, st);

@@ -162,6 +162,8 @@ bool gemm_tc_supported(int M, int N, int K);
 cudaError_t launch_gemm_tc_swiglu(const void *X, const void *W, void *act, int M, int N2, int K, int num_sms,
                                   DevError *err, cudaStream_t st);
 bool gemm_tc_swiglu_pays(int M, int N2, int K, int num_sms);
+// Kernels one launch_gemm_tc call launches: 2 when a K split first zeroes C.
+int gemm_tc_kernels(int M, int N, int K, int accumulate, int num_sms);
 cudaError_t launch_gemm_tc(const void *X, const void *W, float *C, int M, int N, int K, int accumulate, int num_sms,
                            DevError *err, cudaStream_t st);
 // Shared-memory opt-in of the dense kernels for rows up to max_k wide.

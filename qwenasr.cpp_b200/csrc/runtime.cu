@@ -680,8 +680,10 @@ int layer_kv(qkv_handle *h, int layer, int n, const int *slots, const int *pos, 
 // Projection C (+)= X . W^T: tcgen05 when activations and weights are bf16,
 // the SIMT kernel otherwise (f32 parity mode).
 cudaError_t gemm(qkv_handle *h, const void *X, const void *W, float *C, int M, int N, int K, int accumulate) {
-    if (h->act_dtype == kActBF16 && h->w_dtype == kActBF16 && gemm_tc_supported(M, N, K))
+    if (h->act_dtype == kActBF16 && h->w_dtype == kActBF16 && gemm_tc_supported(M, N, K)) {
+        h->launches += gemm_tc_kernels(M, N, K, accumulate, h->num_sms) - 1;   // the zeroing kernel, if any
         return launch_gemm_tc(X, W, C, M, N, K, accumulate, h->num_sms, h->d_err, h->stream);
+    }
     return launch_gemm(X, h->act_dtype, W, h->w_dtype, C, M, N, K, accumulate, h->stream);
 }
 
