@@ -328,27 +328,29 @@ __global__ void swiglu_kernel(const float *gu, int M, int F, TOut *out) {
     }
 }
 
-// Block per row; ties keep the smaller index (strict '>' scan from 0); NaN never wins.
-__global__ void __launch_bounds__(1024) argmax_kernel(const float *logits, int V, int *ids) {
-    pdl_trigger();
-    pdl_wait();   // everything below reads or writes memory of earlier kernels
-    const float *row = logits + static_cast<size_t>(blockIdx.x) * V;
-    float best = -INFINITY;
-    int idx = -1;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        const float v = row[i];
-        if (v > best) { best = v; idx = i; }
+// Split argmax: CTA (r, s) scans slice s of row r (16-byte loads when the
+// row allows them) and writes its (max, index) partial; the last CTA of the
+// row to finish (per-row counter, which it resets) merges the partials in
+// slice order.  The first maximum wins (ties keep the smaller index); NaN never wins.
+__device__ __forceinline__ void take_max(float v, int i, float &best, int &idx) {
+    if (v > best || (v == best && i >= 0 && (idx < 0 || i < idx))) {
+        best = v;
+        idx = i;
     }
-    __shared__ float sb[32];
-    __shared__ int si[32];
+}
+
+__device__ __forceinline__ void block_max(float &best, int &idx, float *sb, int *si) {
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) {
         const float ob = __shfl_xor_sync(0xffffffffu, best, o);
         const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-        if (ob > best || (ob == best && oi >= 0 && (idx < 0 || oi < idx))) { best = ob; idx = oi; }
+        take_max(ob, oi, best, idx);
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) { sb[warp] = best; si[warp] = idx; }
+    if (lane == 0) {
+        sb[warp] = best;
+        si[warp] = idx;
+    }
     __syncthreads();
     if (warp == 0) {
         const int nw = blockDim.x >> 5;
@@ -358,10 +360,60 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *logits, int V
         for (int o = 16; o >= 1; o >>= 1) {
             const float ob = __shfl_xor_sync(0xffffffffu, best, o);
             const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-            if (ob > best || (ob == best && oi >= 0 && (idx < 0 || oi < idx))) { best = ob; idx = oi; }
+            take_max(ob, oi, best, idx);
         }
-        if (lane == 0) ids[blockIdx.x] = idx;
     }
+}
+
+__global__ void __launch_bounds__(512) argmax_split_kernel(const float *logits, int V, int S, float *part_v,
+                                                           int *part_i, int *counters, int *ids) {
+    pdl_trigger();
+    pdl_wait();   // everything below reads or writes memory of earlier kernels
+    const int r = blockIdx.x, sl = blockIdx.y;
+    const float *row = logits + static_cast<size_t>(r) * V;
+    float best = -INFINITY;
+    int idx = -1;
+    if ((V & 3) == 0 && (reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+        const int v4 = V >> 2, ch = (v4 + S - 1) / S;
+        const int lo = sl * ch, hi = min(v4, lo + ch);
+        for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+            const float4 q = reinterpret_cast<const float4 *>(row)[i];
+            if (q.x > best) { best = q.x; idx = 4 * i; }
+            if (q.y > best) { best = q.y; idx = 4 * i + 1; }
+            if (q.z > best) { best = q.z; idx = 4 * i + 2; }
+            if (q.w > best) { best = q.w; idx = 4 * i + 3; }
+        }
+    } else {
+        const int ch = (V + S - 1) / S;
+        const int lo = sl * ch, hi = min(V, lo + ch);
+        for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+            const float v = row[i];
+            if (v > best) { best = v; idx = i; }
+        }
+    }
+    __shared__ float sb[32];
+    __shared__ int si[32];
+    __shared__ int last;
+    block_max(best, idx, sb, si);
+    if (threadIdx.x == 0) {
+        if (S == 1) {
+            ids[r] = idx;
+            last = 0;
+        } else {
+            part_v[r * S + sl] = best;
+            part_i[r * S + sl] = idx;
+            __threadfence();
+            last = atomicAdd(&counters[r], 1) == S - 1;
+        }
+    }
+    __syncthreads();
+    if (!last || threadIdx.x != 0) return;
+    __threadfence();
+    float b = -INFINITY;
+    int bi = -1;
+    for (int k = 0; k < S; ++k) take_max(__ldcg(part_v + r * S + k), __ldcg(part_i + r * S + k), b, bi);
+    ids[r] = bi;
+    counters[r] = 0;
 }
 
 // GGUF tensor bytes (f32 / f16 / bf16) -> device weight dtype (f32 / bf16, RNE).
@@ -507,9 +559,15 @@ cudaError_t launch_swiglu(const float *gu, int M, int F, void *out, int out_dtyp
                       static_cast<__nv_bfloat16 *>(out));
 }
 
-cudaError_t launch_argmax(const float *logits, int M, int V, int *ids, cudaStream_t st) {
+cudaError_t launch_argmax_split(const float *logits, int M, int V, int *ids, float *part_v, int *part_i,
+                                int *counters, int max_slices, int num_sms, cudaStream_t st) {
     if (M <= 0) return cudaSuccess;
-    return launch_pdl(argmax_kernel, dim3(M), dim3(1024), 0, st, logits, V, ids);
+    int S = (2 * num_sms + M - 1) / M;
+    if (S > max_slices) S = max_slices;
+    if (S > (V + 4095) / 4096) S = (V + 4095) / 4096;   // slices of at least ~4K logits
+    if (S < 1) S = 1;
+    return launch_pdl(argmax_split_kernel, dim3(M, S), dim3(512), 0, st, logits, V, S, part_v, part_i, counters,
+                      ids);
 }
 
 }  // namespace qkv

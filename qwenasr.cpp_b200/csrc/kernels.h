@@ -173,6 +173,10 @@ cudaError_t launch_swiglu(const float *gu, int M, int F, void *out, int out_dtyp
 // GGUF tensor data (ggml type 0 f32, 1 f16, 30 bf16 passed as 2) -> weight dtype.
 cudaError_t launch_convert(const void *src, int src_ggml_type, void *dst, int dst_dtype, size_t n, cudaStream_t st);
 // ids[m] = first index of the maximum of logits[m][0..V)
-cudaError_t launch_argmax(const float *logits, int M, int V, int *ids, cudaStream_t st);
+// Row argmax (the first maximum; NaN never wins) with each row split over up
+// to max_slices CTAs (grid about two waves); part_v / part_i [M][max_slices]
+// scratch, counters [M] zero between launches (the kernel resets them).
+cudaError_t launch_argmax_split(const float *logits, int M, int V, int *ids, float *part_v, int *part_i,
+                                int *counters, int max_slices, int num_sms, cudaStream_t st);
 
 }  // namespace qkv

@@ -153,6 +153,11 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
         CK(cudaMalloc(&h->gu, R * 2 * c.intermediate * sizeof(float)));
         CK(cudaMalloc(&h->act, R * c.intermediate * act));
         CK(cudaMalloc(&h->logits, static_cast<size_t>(h->rt.max_streams) * c.vocab * sizeof(float)));
+        const size_t ms = static_cast<size_t>(h->rt.max_streams);
+        CK(cudaMalloc(&h->am_v, ms * qkv_handle::kArgmaxSlices * sizeof(float)));
+        CK(cudaMalloc(&h->am_i, ms * qkv_handle::kArgmaxSlices * sizeof(int)));
+        CK(cudaMalloc(&h->am_cnt, ms * sizeof(int)));
+        CK(cudaMemset(h->am_cnt, 0, ms * sizeof(int)));
     }
     CK(cudaMalloc(&h->d_rowbuf, 4 * R * sizeof(int)));
     CK(cudaMallocHost(&h->h_rowbuf, qkv_handle::kRowRing * 4 * R * sizeof(int)));
@@ -210,6 +215,7 @@ void destroy(qkv_handle *h) {
     cudaFree(h->ap_b1);
     cudaFree(h->pool); cudaFree(h->scales); cudaFree(h->d_page_table); cudaFree(h->d_rope);
     cudaFree(h->x); cudaFree(h->qkv); cudaFree(h->q); cudaFree(h->gu); cudaFree(h->logits);
+    cudaFree(h->am_v); cudaFree(h->am_i); cudaFree(h->am_cnt);
     cudaFree(h->xn); cudaFree(h->attn); cudaFree(h->act); cudaFree(h->host_stage);
     cudaFree(h->d_rowbuf); cudaFree(h->d_out_ids); cudaFree(h->d_items); cudaFree(h->part_o); cudaFree(h->part_ml);
     cudaFree(h->counters); cudaFree(h->d_err);
@@ -692,7 +698,8 @@ int head_and_argmax(qkv_handle *h, int n, const int *d_rows) {
     const qkv_model_config &c = h->cfg;
     CK(launch_rmsnorm(h->x, d_rows, n, c.hidden, h->out_norm, c.rms_norm_eps, h->xn, h->act_dtype, h->stream));
     CK(gemm(h, h->xn, h->w_out, h->logits, n, c.vocab, c.hidden, 0));
-    CK(launch_argmax(h->logits, n, c.vocab, h->d_out_ids, h->stream));
+    CK(launch_argmax_split(h->logits, n, c.vocab, h->d_out_ids, h->am_v, h->am_i, h->am_cnt,
+                           qkv_handle::kArgmaxSlices, h->num_sms, h->stream));
     h->launches += 3;
     return QKV_OK;
 }

@@ -92,6 +92,10 @@ struct qkv_handle {
     cudaStream_t copy_in = nullptr, copy_out = nullptr;
     std::vector<cudaEvent_t> ev_in, ev_done;
     cudaEvent_t ev_tail = nullptr;
+    // split argmax scratch: partials [max_streams][kArgmaxSlices], per-row counters (zero between launches)
+    static constexpr int kArgmaxSlices = 16;
+    float *am_v = nullptr;
+    int *am_i = nullptr, *am_cnt = nullptr;
     int *d_out_ids = nullptr;   // [max_rows]
     int *h_out_ids = nullptr;   // pinned
     int4 *d_items = nullptr;    // prefill attention work items

@@ -308,3 +308,21 @@ def test_bf16_typed_file_loads_like_f32_file(pkg, synth, tmp_path, w):
             out.append(dec.prefill([dec.open() for _ in xs], xs, want_logits=True))
     assert np.array_equal(out[0][0], out[1][0])
     assert rel_err(out[0][1], out[1][1]) < (1e-3 if w == 0 else 1e-2)
+
+
+@pytest.mark.parametrize("n", [4, 40])
+def test_argmax_first_maximum_over_split_rows(pkg, synth, tmp_path, n):
+    """The device argmax (rows split over several CTAs for a 20000-word
+    vocabulary) returns the first maximum of the logits it also returns, for
+    the prefill and two decode steps."""
+    cfg = dict(synth.TINY, vocab=20000)
+    path = synth.write_gguf(tmp_path / "v20k.gguf", cfg, seed=4, weights="bf16", norm_init="one_plus",
+                            tokenizer=False)
+    xs = prompts(synth, synth.read_gguf(path), n, 600, lo=10, hi=60)
+    with decoder(pkg, path, w=1, kv=1, streams=n, ctx=128, batch_tokens=n * 64) as dec:
+        s = [dec.open() for _ in xs]
+        ids, logits = dec.prefill(s, xs, want_logits=True)
+        assert np.array_equal(ids, np.argmax(logits, axis=1))
+        for _ in range(2):
+            ids, logits = dec.decode_step(s, want_logits=True)
+            assert np.array_equal(ids, np.argmax(logits, axis=1))
