@@ -17,6 +17,7 @@
 #include <vector>
 
 #include "gguf.h"
+#include "qkv.h"
 #include "text-decoder.h"
 
 namespace {
@@ -43,6 +44,47 @@ bool read_f32(const std::string &path, std::vector<float> *out, std::string *err
     in.seekg(0);
     in.read(reinterpret_cast<char *>(out->data()), n);
     return static_cast<bool>(in);
+}
+
+// The reference tool's text_json value: the text in double quotes with
+// backslash, quote, \n, \r, \t escaped and other bytes below 0x20 as \u00xx.
+std::string json_escape(const std::string &text) {
+    static const char hex[] = "0123456789abcdef";
+    std::string out = "\"";
+    for (const unsigned char c : text) {
+        if (c == '\\') out += "\\\\";
+        else if (c == '"') out += "\\\"";
+        else if (c == '\n') out += "\\n";
+        else if (c == '\r') out += "\\r";
+        else if (c == '\t') out += "\\t";
+        else if (c < 0x20) {
+            out += "\\u00";
+            out.push_back(hex[c >> 4]);
+            out.push_back(hex[c & 0x0F]);
+        } else {
+            out.push_back(static_cast<char>(c));
+        }
+    }
+    return out + "\"";
+}
+
+// Generated ids -> text with the model file's tokenizer (special tokens
+// skipped, as the reference tool decodes); false when the file has none.
+bool detokenize(const std::string &model_path, const std::vector<int32_t> &ids, std::string *text) {
+    qkv_tokenizer *tok = nullptr;
+    char err[256];
+    if (qkv_tokenizer_open(model_path.c_str(), &tok, err, sizeof err) != QKV_OK) return false;
+    size_t n = 0;
+    std::string buf(ids.size() * 16 + 64, '\0');
+    int rc = qkv_tokenizer_decode(tok, ids.data(), static_cast<int32_t>(ids.size()), 1, &buf[0], buf.size(), &n);
+    if (rc == QKV_ERR_CAPACITY) {
+        buf.assign(n, '\0');
+        rc = qkv_tokenizer_decode(tok, ids.data(), static_cast<int32_t>(ids.size()), 1, &buf[0], buf.size(), &n);
+    }
+    qkv_tokenizer_close(tok);
+    if (rc != QKV_OK) return false;
+    text->assign(buf.data(), n);
+    return true;
 }
 
 bool write_f32(const std::string &path, const std::vector<float> &v, std::string *err) {
@@ -173,6 +215,15 @@ int main(int argc, char **argv) {
         std::cout << "generated_ids=";
         for (size_t i = 0; i < out.generated_ids.size(); ++i) std::cout << (i ? "," : "") << out.generated_ids[i];
         std::cout << "\n";
+        std::string text;
+        if (detokenize(model_path, out.generated_ids, &text)) {   // the model file has a tokenizer
+            if (!out_path.empty()) {
+                std::ofstream o(out_path, std::ios::binary);
+                o.write(text.data(), static_cast<std::streamsize>(text.size()));
+                if (!o) { std::cerr << "cannot write " << out_path << "\n"; return 1; }
+            }
+            std::cout << "text_json=" << json_escape(text) << "\n";
+        }
         return 0;
     }
     if (prefill) {

@@ -65,3 +65,45 @@ def test_cli_prefill_and_layer_outputs(case):
     assert rc == 0, err
     vals = np.fromfile(out, np.float32).reshape(g["ref_layer0"].shape)
     assert rel_err(vals, g["ref_layer0"]) < 1e-4
+
+
+def json_escape(b: bytes) -> bytes:
+    """The reference tool's text_json escaping (tools/qwen-asr-text-layer.cpp:66-91)."""
+    out = bytearray(b'"')
+    for c in b:
+        if c == 0x5C:
+            out += b"\\\\"
+        elif c == 0x22:
+            out += b'\\"'
+        elif c == 0x0A:
+            out += b"\\n"
+        elif c == 0x0D:
+            out += b"\\r"
+        elif c == 0x09:
+            out += b"\\t"
+        elif c < 0x20:
+            out += b"\\u00%02x" % c
+        else:
+            out.append(c)
+    return bytes(out + b'"')
+
+
+@pytest.mark.gpu
+def test_cli_generate_prints_text(case, synth, pkg, tmp_path):
+    """With a tokenizer in the model file, --generate also prints text_json
+    (the detokenised ids, special tokens skipped) and writes the text to
+    --out, as the reference tool does (:478-517).  Same tensors as the golden
+    model, so the ids are the reference's."""
+    _, inp, g, _ = case
+    model = synth.write_gguf(tmp_path / "bytes.gguf", dict(synth.TINY), seed=0, weights="f32", norm_init="one_plus",
+                             tokenizer="bytes")
+    out = tmp_path / "text.bin"
+    p = subprocess.run([str(CLI), str(model), str(inp), "--generate", "16", "--no-stop", "--out", str(out)],
+                       capture_output=True, timeout=600)
+    assert p.returncode == 0, p.stderr
+    kv = dict(line.split(b"=", 1) for line in p.stdout.splitlines() if b"=" in line)
+    ids = [int(t) for t in kv[b"generated_ids"].split(b",")]
+    assert ids == g["ref_ids"].tolist()
+    text = pkg.Tokenizer(model).decode(ids, True)
+    assert out.read_bytes() == text
+    assert kv[b"text_json"] == json_escape(text)
