@@ -64,6 +64,7 @@ def build(clean: bool = False, verbose_ptxas: bool = False, jobs: int | None = N
         objs = list(ex.map(lambda s: compile_one(s, hdr, verbose_ptxas), srcs))
     newest = max(o.stat().st_mtime for o in objs)
     if LIB.exists() and LIB.stat().st_mtime >= newest and not clean:
+        build_tools()   # a tool's own source may have changed
         return LIB
     tmp = LIB.with_suffix(".so.tmp")
     cmd = [NVCC, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lpthread"]
