@@ -818,10 +818,12 @@ def run_gemm(args) -> int:
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    # Each step appends a token to every stream, so a long run drifts the
-    # workload away from its definition (config 4: contexts log-uniform in
-    # [64, 4096], mean ~970): 20 steps move it by ~2 %, 100 steps by ~10 %.
-    ap.add_argument("--steps", type=int, default=20)
+    # Each step appends a token to every stream, so a long config-4 run drifts
+    # the workload away from its definition (contexts log-uniform in [64, 4096],
+    # mean ~970): 20 steps move it by ~2 %, 100 steps by ~10 %.  Serving
+    # compacts the pool every 64 steps, so it times at least that many.
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default: 20 for the config-4 KV step, 64 for serve, 100 otherwise)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=("kv", "model", "model3", "serve", "prefill", "gemm"), default="kv",
@@ -837,6 +839,8 @@ def main() -> int:
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="layers of cache (28 = the workload; fewer only for small profiling captures)")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = {"kv": 20, "serve": 64}.get(args.workload, 100)
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.impl == "reference":
