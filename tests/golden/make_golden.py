@@ -13,7 +13,7 @@ Two independent sources of truth, both the reference's own code:
 The weights are the seeded tiny model of qwenasr.cpp_b200/synth.py; the file
 records a checksum of them so a change of the generator is caught.
 
-    python tests/golden/make_golden.py [--ref-root /root/reference]
+    python tests/golden/make_golden.py [--ref-root PATH-OF-THE-REFERENCE-TREE]
 """
 from __future__ import annotations
 
