@@ -234,3 +234,30 @@ def test_encode_reference_live(pkg, dec_input, checker):
         text = "".join(rng.choice(pieces, size=int(rng.integers(0, 30))))
         for eos in (False, True):
             assert tok.encode(text, eos).tolist() == checker.ref_tokenizer_encode(str(path), text, eos).tolist()
+
+
+def test_tokenizer_capi_contract(pkg, dec_input):
+    """QKV_ERR_CAPACITY with the needed count when the output is too small,
+    then success with that count; bad arguments are refused; add_eos appends
+    the file's end-of-sequence id."""
+    import ctypes as C
+    _, _, path = dec_input
+    tok = pkg.Tokenizer(path)
+    lib = pkg.lib
+    text = b"You transcribe speech."
+    ids = np.zeros(2, np.int32)
+    n = C.c_size_t(0)
+    i32 = C.POINTER(C.c_int32)
+    rc = lib.qkv_tokenizer_encode(tok.h, text, len(text), 0, ids.ctypes.data_as(i32), 2, C.byref(n))
+    assert rc == pkg.QKV_ERR_CAPACITY and n.value > 2
+    big = np.zeros(n.value, np.int32)
+    rc = lib.qkv_tokenizer_encode(tok.h, text, len(text), 0, big.ctypes.data_as(i32), n.value, C.byref(n))
+    assert rc == 0 and big.tolist() == tok.encode(text).tolist()
+    eos = tok.encode(text, add_eos=True)
+    assert eos[:-1].tolist() == big.tolist() and eos[-1] == 258   # im_end, the synthetic file's eos id
+    out = C.create_string_buffer(1)
+    rc = lib.qkv_tokenizer_decode(tok.h, big.ctypes.data_as(i32), len(big), 1, out, 1, C.byref(n))
+    assert rc == pkg.QKV_ERR_CAPACITY and n.value == len(tok.decode(big))
+    assert lib.qkv_tokenizer_encode(None, text, len(text), 0, big.ctypes.data_as(i32), 8, C.byref(n)) == 1
+    assert lib.qkv_asr_prompt_ids(tok.h, 2, b"", b"", None, 0, None) == 1
+    tok.close()
