@@ -217,3 +217,39 @@ def test_audio_projector_absent(pkg, files):
         with pytest.raises(pkg.QkvError) as ei:
             dec.audio_project(4, x.data_ptr(), x.data_ptr())
         assert "no audio projector" in str(ei.value)
+
+
+def test_prompt_to_text_pipeline(pkg, synth, checker, proj_files):
+    """The whole text side, as a user runs it: prompt ids from the model
+    file's tokenizer (the reference's template and encoder), audio-encoder rows
+    through the projector on the device, the decoder input on the device,
+    prefill from ids, greedy decode, detokenisation.  f32 weights: the ids
+    equal the oracle's greedy ids for the same prompt rows (built from the
+    projector's output), and the text is their detokenisation."""
+    path = proj_files["f32"]
+    t = synth.read_gguf(path)
+    cfg = dict(synth.TINY)
+    tok = pkg.Tokenizer(path)
+    aid = synth.BYTE_TOKEN_IDS["audio"]
+    n_audio, steps = 40, 8
+    prompt = tok.asr_prompt_ids(n_audio, "You transcribe speech.", "English")
+    enc = np.random.default_rng(47).standard_normal((n_audio, 256)).astype(np.float32)
+    rt = pkg.runtime_config(device=0, weight_dtype=pkg.F32, kv_dtype=pkg.F32, max_streams=2, max_context=256,
+                            max_batch_tokens=256)
+    with pkg.Decoder.from_gguf(path, rt) as dec:   # f32 weights and cache: the oracle's arithmetic
+        e = torch.tensor(enc, device="cuda")
+        rows = torch.empty((n_audio, 256), device="cuda")
+        dec.audio_project(n_audio, e.data_ptr(), rows.data_ptr())
+        torch.cuda.synchronize()
+        s = dec.open()
+        ids = [int(dec.prefill_ids([s], [prompt], [rows], aid)[0])]
+        for _ in range(steps - 1):
+            ids.append(int(dec.decode_step([s])[0]))
+        projected = rows.cpu().numpy()
+    rc, x = checker.decoder_input(prompt, np.array(t["text.token_embd.weight"]), projected, aid)
+    assert rc == 0
+    want = checker.OracleModel(cfg, t).generate(x, steps)["ids"]
+    assert ids == want.tolist()
+    # the text: detokenisation of the ids (pinned to the reference's decoder by the CPU tests)
+    text = tok.decode(np.array(ids, np.int32))
+    assert isinstance(text, bytes) and len(text) > 0
