@@ -43,7 +43,8 @@ enum qkv_status {
     QKV_ERR_IO = 6,            /* file could not be opened / mapped */
     QKV_ERR_FORMAT = 7,        /* GGUF parse error, missing tensor, shape or type mismatch */
     QKV_ERR_STATE = 8,         /* call not valid in the current state */
-    QKV_ERR_NO_DEVICE = 9      /* no CUDA device / wrong architecture */
+    QKV_ERR_NO_DEVICE = 9,     /* no CUDA device / wrong architecture */
+    QKV_ERR_HOST_MEMORY = 10   /* a host table or string did not fit in host memory */
 };
 
 enum qkv_dtype {

@@ -20,7 +20,7 @@ QKV_OK = 0
 QKV_ERR_CAPACITY = 3
 STATUS = {0: "QKV_OK", 1: "QKV_ERR_INVALID_ARG", 2: "QKV_ERR_OUT_OF_PAGES", 3: "QKV_ERR_CAPACITY",
           4: "QKV_ERR_CUDA", 5: "QKV_ERR_DEVICE", 6: "QKV_ERR_IO", 7: "QKV_ERR_FORMAT", 8: "QKV_ERR_STATE",
-          9: "QKV_ERR_NO_DEVICE"}
+          9: "QKV_ERR_NO_DEVICE", 10: "QKV_ERR_HOST_MEMORY"}
 F32, BF16, FP8 = 0, 1, 2
 
 

@@ -20,6 +20,8 @@
 #include <cctype>
 #include <climits>
 #include <cstring>
+#include <exception>
+#include <memory>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -218,15 +220,20 @@ int emit_ids(const std::vector<int32_t> &v, int32_t *out, size_t cap, size_t *n)
     return QKV_OK;
 }
 
-}  // namespace
-
-extern "C" {
-
-int qkv_tokenizer_open(const char *gguf_path, qkv_tokenizer **out, char *err, size_t err_len) {
-    if (!gguf_path || !out) {
-        set_err(err, err_len, "qkv_tokenizer_open: null path or out");
-        return QKV_ERR_INVALID_ARG;
+// The C entry points return a status.  Their tables and strings are sized by
+// the caller's input (a long text, a prompt with many audio placeholders) or
+// the file's vocabulary; an allocation failure there becomes a status instead
+// of an exception crossing the C ABI.  A distinct status, so that it is not
+// mistaken for the capacity protocol's "give me a larger buffer".
+template <typename F> int no_throw(F &&body) {
+    try {
+        return body();
+    } catch (const std::exception &) {
+        return QKV_ERR_HOST_MEMORY;
     }
+}
+
+int open_tokenizer(const char *gguf_path, qkv_tokenizer **out, char *err, size_t err_len) {
     qkv::GgufFile f;
     std::string e;
     int rc = f.open(gguf_path, &e);
@@ -240,7 +247,7 @@ int qkv_tokenizer_open(const char *gguf_path, qkv_tokenizer **out, char *err, si
         set_err(err, err_len, "GGUF tokenizer metadata is incomplete");
         return QKV_ERR_FORMAT;
     }
-    auto *t = new qkv_tokenizer();
+    auto t = std::make_unique<qkv_tokenizer>();
     t->id_to_token = tokens->strs;
     t->special.assign(t->id_to_token.size(), 0);
     for (size_t i = 0; i < t->id_to_token.size(); ++i) t->vocab[t->id_to_token[i]] = static_cast<int32_t>(i);
@@ -258,12 +265,10 @@ int qkv_tokenizer_open(const char *gguf_path, qkv_tokenizer **out, char *err, si
         uint32_t id = 0;
         if (!f.get_u32(k, &id)) {
             set_err(err, err_len, std::string("missing tokenizer special key: ") + k);
-            delete t;
             return QKV_ERR_FORMAT;
         }
         if (id >= t->special.size()) {
             set_err(err, err_len, std::string("tokenizer special id out of range for key: ") + k);
-            delete t;
             return QKV_ERR_FORMAT;
         }
         t->special[id] = 1;
@@ -282,56 +287,77 @@ int qkv_tokenizer_open(const char *gguf_path, qkv_tokenizer **out, char *err, si
         t->symbol[b] = utf8(printable ? b : 256 + extra++);
         t->byte_of[t->symbol[b]] = static_cast<unsigned char>(b);
     }
-    *out = t;
+    *out = t.release();
     return QKV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int qkv_tokenizer_open(const char *gguf_path, qkv_tokenizer **out, char *err, size_t err_len) {
+    if (!gguf_path || !out) {
+        set_err(err, err_len, "qkv_tokenizer_open: null path or out");
+        return QKV_ERR_INVALID_ARG;
+    }
+    try {
+        return open_tokenizer(gguf_path, out, err, err_len);
+    } catch (const std::exception &) {
+        set_err(err, err_len, "tokenizer tables do not fit in host memory");
+        return QKV_ERR_HOST_MEMORY;
+    }
 }
 
 int qkv_tokenizer_decode(const qkv_tokenizer *t, const int32_t *ids, int32_t n, int32_t skip_special, char *out,
                          size_t cap, size_t *len) {
     if (!t || (n > 0 && !ids) || !len) return QKV_ERR_INVALID_ARG;
-    std::string s;
-    for (int32_t k = 0; k < n; ++k) {
-        const int32_t id = ids[k];
-        if (id < 0 || static_cast<size_t>(id) >= t->id_to_token.size()) continue;
-        if (skip_special && t->special[static_cast<size_t>(id)]) continue;
-        const std::string &tok = t->id_to_token[static_cast<size_t>(id)];
-        const int L = static_cast<int>(tok.size());
-        for (int pos = 0; pos < L;) {
-            const int adv = piece_len(static_cast<unsigned char>(tok[static_cast<size_t>(pos)]), L - pos);
-            const std::string piece = tok.substr(static_cast<size_t>(pos), static_cast<size_t>(adv));
-            const auto it = t->byte_of.find(piece);
-            if (it != t->byte_of.end()) s.push_back(static_cast<char>(it->second));
-            else s += piece;
-            pos += adv;
+    return no_throw([&] {
+        std::string s;
+        for (int32_t k = 0; k < n; ++k) {
+            const int32_t id = ids[k];
+            if (id < 0 || static_cast<size_t>(id) >= t->id_to_token.size()) continue;
+            if (skip_special && t->special[static_cast<size_t>(id)]) continue;
+            const std::string &tok = t->id_to_token[static_cast<size_t>(id)];
+            const int L = static_cast<int>(tok.size());
+            for (int pos = 0; pos < L;) {
+                const int adv = piece_len(static_cast<unsigned char>(tok[static_cast<size_t>(pos)]), L - pos);
+                const std::string piece = tok.substr(static_cast<size_t>(pos), static_cast<size_t>(adv));
+                const auto it = t->byte_of.find(piece);
+                if (it != t->byte_of.end()) s.push_back(static_cast<char>(it->second));
+                else s += piece;
+                pos += adv;
+            }
         }
-    }
-    *len = s.size();
-    if (s.size() > cap || (s.size() > 0 && !out)) return QKV_ERR_CAPACITY;
-    if (!s.empty()) std::memcpy(out, s.data(), s.size());
-    return QKV_OK;
+        *len = s.size();
+        if (s.size() > cap || (s.size() > 0 && !out)) return QKV_ERR_CAPACITY;
+        if (!s.empty()) std::memcpy(out, s.data(), s.size());
+        return QKV_OK;
+    });
 }
 
 int qkv_tokenizer_encode(const qkv_tokenizer *t, const char *text, size_t text_len, int32_t add_eos, int32_t *ids,
                          size_t cap, size_t *n) {
     if (!t || (text_len > 0 && !text) || !n) return QKV_ERR_INVALID_ARG;
-    return emit_ids(encode(t, std::string(text ? text : "", text_len), add_eos != 0), ids, cap, n);
+    return no_throw([&] { return emit_ids(encode(t, std::string(text ? text : "", text_len), add_eos != 0), ids, cap, n); });
 }
 
 int qkv_asr_prompt_ids(const qkv_tokenizer *t, int32_t audio_tokens, const char *system_text, const char *language,
                        int32_t *ids, size_t cap, size_t *n) {
     if (!t || !n) return QKV_ERR_INVALID_ARG;
-    // the template of src/tokenizer.cpp:529-549
-    std::string p = "<|im_start|>system\n";
-    p += system_text ? system_text : "";
-    p += "<|im_end|>\n<|im_start|>user\n<|audio_start|>";
-    for (int32_t i = 0; i < audio_tokens; ++i) p += "<|audio_pad|>";
-    p += "<|audio_end|><|im_end|>\n<|im_start|>assistant\n";
-    if (language && language[0]) {
-        p += "language ";
-        p += language;
-        p += "<asr_text>";
-    }
-    return emit_ids(encode(t, p, false), ids, cap, n);
+    return no_throw([&] {
+        // the template of src/tokenizer.cpp:529-549
+        std::string p = "<|im_start|>system\n";
+        p += system_text ? system_text : "";
+        p += "<|im_end|>\n<|im_start|>user\n<|audio_start|>";
+        for (int32_t i = 0; i < audio_tokens; ++i) p += "<|audio_pad|>";
+        p += "<|audio_end|><|im_end|>\n<|im_start|>assistant\n";
+        if (language && language[0]) {
+            p += "language ";
+            p += language;
+            p += "<asr_text>";
+        }
+        return emit_ids(encode(t, p, false), ids, cap, n);
+    });
 }
 
 void qkv_tokenizer_close(qkv_tokenizer *t) { delete t; }

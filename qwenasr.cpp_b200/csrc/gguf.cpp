@@ -2,11 +2,13 @@
 
 #include <cerrno>
 #include <cstring>
+#include <exception>
 #include <fcntl.h>
 #include <limits>
 #include <sys/mman.h>
 #include <sys/stat.h>
 #include <unistd.h>
+#include <utility>
 
 #include "qkv.h"
 
@@ -99,7 +101,7 @@ bool read_value(Cursor &c, uint32_t type, GgufValue *v) {
             v->arr_n = c.get<uint64_t>();
             if (!c.ok) return false;
             if (v->arr_type == kString) {
-                if (v->arr_n > c.size - c.pos) return false;   // each string takes at least 8 bytes
+                if (v->arr_n > (c.size - c.pos) / 8) return false;   // each string takes at least 8 bytes
                 v->strs.resize(static_cast<size_t>(v->arr_n));
                 for (uint64_t k = 0; k < v->arr_n && c.ok; ++k) c.string(&v->strs[static_cast<size_t>(k)]);
             } else {
@@ -125,12 +127,28 @@ void GgufFile::close() {
     map_ = nullptr;
     fd_ = -1;
     size_ = 0;
+    version_ = 0;
+    alignment_ = 32;
+    data_offset_ = 0;
     tensors_.clear();
     by_name_.clear();
     kv_.clear();
 }
 
 int GgufFile::open(const char *path, std::string *err) {
+    // The metadata tables are sized by counts read from the file; a file whose
+    // counts fit its size but not host memory fails here instead of throwing
+    // through the C entry points that call this.
+    try {
+        return parse(path, err);
+    } catch (const std::exception &ex) {
+        close();
+        if (err) *err = std::string("gguf: metadata does not fit in host memory (") + ex.what() + ")";
+        return QKV_ERR_HOST_MEMORY;
+    }
+}
+
+int GgufFile::parse(const char *path, std::string *err) {
     close();
     if (!path) {
         if (err) *err = "gguf: path is null";
@@ -189,7 +207,7 @@ int GgufFile::open(const char *path, std::string *err) {
             close();
             return QKV_ERR_FORMAT;
         }
-        kv_[key] = v;
+        kv_[key] = std::move(v);
     }
     auto al = kv_.find("general.alignment");
     if (al != kv_.end()) {

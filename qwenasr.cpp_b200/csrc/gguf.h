@@ -64,6 +64,8 @@ public:
     const uint8_t *mapping() const { return map_; }
 
 private:
+    int parse(const char *path, std::string *err);
+
     int fd_ = -1;
     const uint8_t *map_ = nullptr;
     size_t size_ = 0;

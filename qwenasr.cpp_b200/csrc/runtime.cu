@@ -6,6 +6,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <exception>
 #include <functional>
 #include <memory>
 #include <mutex>
@@ -25,6 +26,18 @@ int fail(qkv_handle *h, int code, const std::string &msg) {
 
 int cuda_fail(qkv_handle *h, cudaError_t e, const char *what) {
     return fail(h, QKV_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// Handle set-up sizes host tables (the RoPE table, page tables, the pager's
+// lists) from the runtime config: a config that passes the checks but does
+// not fit in host memory fails with a status instead of an exception
+// crossing the C ABI.
+template <typename F> int host_alloc_guard(qkv_handle *h, F &&body) {
+    try {
+        return body();
+    } catch (const std::exception &ex) {
+        return fail(h, QKV_ERR_HOST_MEMORY, std::string("host allocation failed during set-up: ") + ex.what());
+    }
 }
 
 }  // namespace qkv
@@ -878,7 +891,8 @@ int qkv_create(const char *gguf_path, const qkv_model_config *cfg, const qkv_run
     h->w_dtype = rt->weight_dtype == QKV_BF16 ? kActBF16 : kActF32;
     h->act_dtype = h->w_dtype;
     h->w_elem = h->w_dtype == kActBF16 ? 2 : 4;
-    if ((rc = setup_common(h, true)) || (rc = load_weights(h, f))) {
+    if ((rc = host_alloc_guard(h, [&] { return setup_common(h, true); })) ||
+        (rc = host_alloc_guard(h, [&] { return load_weights(h, f); }))) {
         set_err(err, err_len, h->last_error);
         destroy(h);
         return rc;
@@ -905,7 +919,7 @@ int qkv_create_kv_only(const qkv_model_config *cfg, const qkv_runtime_config *rt
     h->rt = *rt;
     h->w_dtype = kActF32;
     h->act_dtype = kActF32;
-    if ((rc = setup_common(h, false))) {
+    if ((rc = host_alloc_guard(h, [&] { return setup_common(h, false); }))) {
         set_err(err, err_len, h->last_error);
         destroy(h);
         return rc;

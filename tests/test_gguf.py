@@ -105,3 +105,43 @@ def test_bf16_typed_file(pkg, synth, tmp_path):
         assert ty == 30 and dims == list(reversed(ta[name].shape))
         want = (np.ascontiguousarray(ta[name]).view(np.uint32) >> np.uint32(16)).astype(np.uint16)
         assert np.array_equal(data.view(np.uint16).reshape(want.shape), want)
+
+
+def _string_array_file(path, count: int, payload: bytes):
+    """A GGUF v3 file with no tensors and one key: tokenizer.ggml.tokens, a
+    string array that claims `count` entries followed by `payload`."""
+    key = b"tokenizer.ggml.tokens"
+    head = b"GGUF" + struct.pack("<IQQ", 3, 0, 1)
+    kv = struct.pack("<Q", len(key)) + key + struct.pack("<IIQ", 9, 8, count)
+    path.write_bytes(head + kv + payload)
+    return path
+
+
+@pytest.mark.parametrize("case", ["huge_count", "count_past_end", "string_past_end"])
+def test_reader_bounds_string_array_counts(pkg, tmp_path, case):
+    """A string-array count larger than the rest of the file can hold (every
+    entry takes at least its 8-byte length) is a format error found before
+    any table is sized from it; a count that fits but whose strings run past
+    the end is one too.  Neither may surface as an exception or an
+    allocation of the claimed size."""
+    entry = struct.pack("<Q", 2) + b"ab"
+    if case == "string_past_end":
+        count, payload = 2, entry + struct.pack("<Q", 100) + b"ab"    # the second string claims 100 bytes
+    else:
+        count, payload = (1 << 40) if case == "huge_count" else 3, entry * 2   # 2 entries present, 20 bytes
+    p = _string_array_file(tmp_path / "strs.gguf", count, payload)
+    with pytest.raises(pkg.QkvError) as ei:
+        pkg.Tokenizer(p)
+    assert ei.value.code == 7, ei.value
+    assert "tokenizer.ggml.tokens" in str(ei.value)
+
+
+def test_reader_accepts_exact_string_array(pkg, tmp_path):
+    """The same file with the count it holds parses; the tokenizer then
+    reports the missing merges key, which shows that the array was read."""
+    entry = struct.pack("<Q", 2) + b"ab"
+    p = _string_array_file(tmp_path / "strs.gguf", 2, entry * 2)
+    with pytest.raises(pkg.QkvError) as ei:
+        pkg.Tokenizer(p)
+    assert ei.value.code == 7
+    assert "incomplete" in str(ei.value)
