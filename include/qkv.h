@@ -331,7 +331,9 @@ int qkv_asr_prompt_ids(const qkv_tokenizer *t, int32_t audio_tokens, const char 
 void qkv_tokenizer_close(qkv_tokenizer *t);
 
 /* ---- host-only page allocator (no GPU needed; used inside every handle) ----
- * Pages hold page_tokens tokens of every layer's K and V for one stream. */
+ * Pages hold page_tokens tokens of every layer's K and V for one stream.
+ * qkv_pager_create returns NULL on a bad argument (n_pages outside 1..2^30)
+ * or when its free list does not fit in host memory. */
 qkv_pager *qkv_pager_create(int64_t n_pages, int32_t page_tokens, int32_t max_streams,
                             int32_t max_pages_per_stream, uint32_t seed);
 void qkv_pager_destroy(qkv_pager *p);

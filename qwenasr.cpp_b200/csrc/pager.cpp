@@ -101,6 +101,10 @@ int Pager::append(int32_t s, int32_t tokens, std::vector<int32_t> *added, std::s
         }
         return QKV_ERR_OUT_OF_PAGES;
     }
+    if (extra > 0) {   // reserve first: a page never leaves the free list without landing in the stream
+        st.pages.reserve(static_cast<size_t>(need));
+        if (added) added->reserve(added->size() + static_cast<size_t>(extra));
+    }
     for (int64_t i = 0; i < extra; ++i) {
         const int32_t p = free_.back();
         free_.pop_back();
@@ -131,6 +135,11 @@ void Pager::compact(std::vector<int32_t> *src, std::vector<int32_t> *dst) {
         if (p < live) low_free.push_back(p);
     }
     std::sort(low_free.begin(), low_free.end());
+    // Every move fills one low free page, so the lists never outgrow
+    // low_free: reserving them here means nothing below allocates, and an
+    // allocation failure leaves the pager as it was.
+    if (src) src->reserve(src->size() + low_free.size());
+    if (dst) dst->reserve(dst->size() + low_free.size());
     size_t next = 0;
     for (Stream &st : streams_) {
         if (!st.open) continue;

@@ -1647,7 +1647,7 @@ int qkv_gather(qkv_handle *h, int32_t layer, int32_t stream_id, void *k_host, vo
 }
 
 int qkv_stream_pages(const qkv_handle *h, int32_t stream_id, int32_t *pages_out, int32_t cap, int32_t *n) {
-    if (!h || !n) return QKV_ERR_INVALID_ARG;
+    if (!h || !n || (cap > 0 && !pages_out)) return QKV_ERR_INVALID_ARG;
     const std::vector<int32_t> *pg = h->pager->pages(stream_id);
     if (!pg) return QKV_ERR_INVALID_ARG;
     *n = static_cast<int32_t>(pg->size());
@@ -1715,7 +1715,11 @@ qkv_pager *qkv_pager_create(int64_t n_pages, int32_t page_tokens, int32_t max_st
                             uint32_t seed) {
     if (n_pages <= 0 || n_pages > (int64_t{1} << 30) || page_tokens <= 0 || max_streams <= 0 || max_pages_per_stream <= 0)
         return nullptr;
-    return reinterpret_cast<qkv_pager *>(new Pager(n_pages, page_tokens, max_streams, max_pages_per_stream, seed));
+    try {
+        return reinterpret_cast<qkv_pager *>(new Pager(n_pages, page_tokens, max_streams, max_pages_per_stream, seed));
+    } catch (const std::exception &) {
+        return nullptr;   // the free list (4 bytes a page) does not fit in host memory
+    }
 }
 void qkv_pager_destroy(qkv_pager *p) { delete reinterpret_cast<Pager *>(p); }
 int qkv_pager_open(qkv_pager *p, int32_t *stream_id) {
@@ -1726,16 +1730,21 @@ int qkv_pager_close(qkv_pager *p, int32_t stream_id) {
 }
 int qkv_pager_append(qkv_pager *p, int32_t stream_id, int32_t tokens, int32_t *new_pages) {
     if (!p) return QKV_ERR_INVALID_ARG;
-    std::vector<int32_t> added;
-    const int rc = reinterpret_cast<Pager *>(p)->append(stream_id, tokens, &added, nullptr);
-    if (new_pages) *new_pages = rc == QKV_OK ? static_cast<int32_t>(added.size()) : 0;
-    return rc;
+    if (new_pages) *new_pages = 0;
+    try {
+        std::vector<int32_t> added;
+        const int rc = reinterpret_cast<Pager *>(p)->append(stream_id, tokens, &added, nullptr);
+        if (new_pages && rc == QKV_OK) *new_pages = static_cast<int32_t>(added.size());
+        return rc;
+    } catch (const std::exception &) {
+        return QKV_ERR_HOST_MEMORY;
+    }
 }
 int qkv_pager_length(const qkv_pager *p, int32_t stream_id, int32_t *tokens) {
     return p ? reinterpret_cast<const Pager *>(p)->length(stream_id, tokens, nullptr) : QKV_ERR_INVALID_ARG;
 }
 int qkv_pager_pages(const qkv_pager *p, int32_t stream_id, int32_t *pages_out, int32_t cap, int32_t *n) {
-    if (!p || !n) return QKV_ERR_INVALID_ARG;
+    if (!p || !n || (cap > 0 && !pages_out)) return QKV_ERR_INVALID_ARG;
     const std::vector<int32_t> *pg = reinterpret_cast<const Pager *>(p)->pages(stream_id);
     if (!pg) return QKV_ERR_INVALID_ARG;
     *n = static_cast<int32_t>(pg->size());
@@ -1746,7 +1755,11 @@ int64_t qkv_pager_free_pages(const qkv_pager *p) { return p ? reinterpret_cast<c
 int qkv_pager_compact(qkv_pager *p, int32_t *src, int32_t *dst, int64_t cap, int64_t *n_moves) {
     if (!p) return QKV_ERR_INVALID_ARG;
     std::vector<int32_t> s, d;
-    reinterpret_cast<Pager *>(p)->compact(&s, &d);
+    try {
+        reinterpret_cast<Pager *>(p)->compact(&s, &d);
+    } catch (const std::exception &) {
+        return QKV_ERR_HOST_MEMORY;
+    }
     if (n_moves) *n_moves = static_cast<int64_t>(s.size());
     for (int64_t i = 0; i < cap && i < static_cast<int64_t>(s.size()); ++i) {
         if (src) src[i] = s[static_cast<size_t>(i)];

@@ -110,3 +110,19 @@ def test_randomized_soak(pkg):
         if step % 100 == 0:
             assert p.check() == 0
     assert p.check() == 0
+
+
+def test_c_abi_argument_checks(pkg):
+    """qkv_pager_pages rejects a null output with a positive capacity (a
+    count-only query passes cap 0 and may pass NULL); qkv_pager_create returns
+    NULL outside 1..2^30 pages."""
+    import ctypes as C
+    p = pkg.Pager(16, 16, 2, 8)
+    s = p.open()
+    p.append(s, 40)
+    n = C.c_int32(-1)
+    assert pkg.lib.qkv_pager_pages(p.p, s, None, 4, C.byref(n)) == 1    # QKV_ERR_INVALID_ARG
+    assert pkg.lib.qkv_pager_pages(p.p, s, None, 0, C.byref(n)) == 0 and n.value == 3
+    assert not pkg.lib.qkv_pager_create(0, 16, 2, 8, 0)
+    assert not pkg.lib.qkv_pager_create((1 << 30) + 1, 16, 2, 8, 0)
+    assert p.check() == 0
