@@ -28,6 +28,19 @@ int cuda_fail(qkv_handle *h, cudaError_t e, const char *what) {
     return fail(h, QKV_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
+// Owner of a temporary device buffer of a host-driven call (the compaction
+// move list, the fill list, a gather target): freed on every return path,
+// including the early returns of a failed CUDA call.
+struct DeviceTemp {
+    void *p = nullptr;
+    DeviceTemp() = default;
+    DeviceTemp(const DeviceTemp &) = delete;
+    DeviceTemp &operator=(const DeviceTemp &) = delete;
+    ~DeviceTemp() {
+        if (p) cudaFree(p);
+    }
+};
+
 // Handle set-up sizes host tables (the RoPE table, page tables, the pager's
 // lists) from the runtime config: a config that passes the checks but does
 // not fit in host memory fails with a status instead of an exception
@@ -993,8 +1006,9 @@ int qkv_compact(qkv_handle *h, int64_t *moved) {
     h->pager->compact(&src, &dst);
     if (moved) *moved = static_cast<int64_t>(src.size());
     if (!src.empty()) {
-        int *d_moves = nullptr;
-        CK(cudaMalloc(&d_moves, 2 * src.size() * sizeof(int)));
+        DeviceTemp moves;
+        CK(cudaMalloc(&moves.p, 2 * src.size() * sizeof(int)));
+        int *d_moves = static_cast<int *>(moves.p);
         CK(cudaMemcpy(d_moves, src.data(), src.size() * sizeof(int), cudaMemcpyHostToDevice));
         CK(cudaMemcpy(d_moves + src.size(), dst.data(), dst.size() * sizeof(int), cudaMemcpyHostToDevice));
         for (int l = 0; l < h->cfg.n_layers; ++l) {
@@ -1006,7 +1020,6 @@ int qkv_compact(qkv_handle *h, int64_t *moved) {
             }
         }
         CK(cudaStreamSynchronize(h->stream));
-        cudaFree(d_moves);
     }
     // Rewrite the whole page table from the pager.
     std::fill(h->h_page_table, h->h_page_table + static_cast<size_t>(h->rt.max_streams) * h->maxp, -1);
@@ -1347,6 +1360,7 @@ int qkv_generate(qkv_handle *h, const float *embeddings, int32_t tokens, int32_t
     if (static_cast<int64_t>(tokens) + max_new_tokens > h->rt.max_context)
         return fail(h, QKV_ERR_CAPACITY, "generation exceeds KV-cache capacity");
     if (max_new_tokens == 0) return QKV_OK;
+    if (!out_ids || (n_stop > 0 && !stop_ids)) return fail(h, QKV_ERR_INVALID_ARG, "out_ids or stop_ids is null");
     int32_t s = -1;
     int rc = qkv_stream_open(h, &s);
     if (rc) return rc;
@@ -1599,8 +1613,9 @@ int qkv_fill_random(qkv_handle *h, uint64_t seed) {
         if (pg) pages.insert(pages.end(), pg->begin(), pg->end());
     }
     if (pages.empty()) return QKV_OK;
-    int *d = nullptr;
-    CK(cudaMalloc(&d, pages.size() * sizeof(int)));
+    DeviceTemp list;
+    CK(cudaMalloc(&list.p, pages.size() * sizeof(int)));
+    int *d = static_cast<int *>(list.p);
     CK(cudaMemcpy(d, pages.data(), pages.size() * sizeof(int), cudaMemcpyHostToDevice));
     for (int l = 0; l < h->cfg.n_layers; ++l) {
         CK(launch_page_fill(static_cast<uint8_t *>(h->pool) + h->pool_layer_bytes * static_cast<size_t>(l),
@@ -1609,7 +1624,6 @@ int qkv_fill_random(qkv_handle *h, uint64_t seed) {
                             h->stream));
     }
     CK(cudaStreamSynchronize(h->stream));
-    cudaFree(d);
     return QKV_OK;
 }
 
@@ -1624,8 +1638,9 @@ int qkv_gather(qkv_handle *h, int32_t layer, int32_t stream_id, void *k_host, vo
     if (len == 0) return QKV_OK;
     const size_t eb = kv_elem_bytes(h->rt.kv_dtype);
     const size_t bytes = static_cast<size_t>(len) * kKvDim * eb;
-    uint8_t *d = nullptr;
-    CK(cudaMalloc(&d, 2 * bytes + pg->size() * sizeof(int)));
+    DeviceTemp target;
+    CK(cudaMalloc(&target.p, 2 * bytes + pg->size() * sizeof(int)));
+    uint8_t *d = static_cast<uint8_t *>(target.p);
     int *dpages = reinterpret_cast<int *>(d + 2 * bytes);
     CK(cudaMemcpy(dpages, pg->data(), pg->size() * sizeof(int), cudaMemcpyHostToDevice));
     CK(launch_page_gather(static_cast<uint8_t *>(h->pool) + h->pool_layer_bytes * static_cast<size_t>(layer),
@@ -1641,9 +1656,7 @@ int qkv_gather(qkv_handle *h, int32_t layer, int32_t stream_id, void *k_host, vo
                                2 * kHkv * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
         }
     }
-    const int rc = check_device_error(h);
-    cudaFree(d);
-    return rc;
+    return check_device_error(h);
 }
 
 int qkv_stream_pages(const qkv_handle *h, int32_t stream_id, int32_t *pages_out, int32_t cap, int32_t *n) {
