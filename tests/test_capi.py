@@ -25,6 +25,16 @@ def test_every_declared_symbol_is_exported(pkg):
     assert set(syms) <= set(pkg.SIGNATURES), sorted(set(syms) - set(pkg.SIGNATURES))
 
 
+def test_status_codes_agree_with_header(pkg):
+    """The Python status names are the header's enum, value for value."""
+    text = (ROOT / "include" / "qkv.h").read_text()
+    body = re.search(r"enum qkv_status \{(.*?)\};", text, flags=re.S).group(1)
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    header = {int(v): k for k, v in re.findall(r"(QKV_[A-Z_]+)\s*=\s*(\d+)", body)}
+    assert header == pkg.STATUS
+    assert header[pkg.QKV_ERR_CAPACITY] == "QKV_ERR_CAPACITY"
+
+
 def test_create_without_device_fails_cleanly(pkg, tiny_files):
     import torch
     if torch.cuda.is_available():
