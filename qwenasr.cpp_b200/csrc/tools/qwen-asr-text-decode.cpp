@@ -6,11 +6,17 @@
 //
 //   qwen-asr-text-decode MODEL.gguf INPUT.f32 [--generate N | --prefill | --layer L]
 //                        [--out PATH] [--device auto|gpu|cpu] [--stop-ids a,b,..] [--no-stop]
+//                        [--kv-dtype f32|bf16|fp8] [--weights f32|bf16] [--page-size 16] [--gpu N]
 // INPUT.f32 = raw float32 [tokens][hidden] (audio rows already spliced in).
+// The B200 options pick the cache element type (f32 keeps the reference's
+// numerics), the device weight type, and the GPU; the paged cache has
+// 16-token pages only.  They set the backend's QWENASR_B200_KV /
+// QWENASR_B200_WEIGHTS / QWENASR_B200_DEVICE switches for this process.
 #include <chrono>
 #include <cstdio>
 #include <cstdlib>
 #include <fstream>
+#include <initializer_list>
 #include <iostream>
 #include <sstream>
 #include <string>
@@ -25,7 +31,8 @@ namespace {
 int usage(const char *argv0) {
     std::cerr << "usage: " << argv0
               << " MODEL.gguf INPUT.f32 [--generate N | --prefill | --layer L] [--out PATH]"
-                 " [--device auto|gpu|cpu] [--stop-ids a,b] [--no-stop]\n";
+                 " [--device auto|gpu|cpu] [--stop-ids a,b] [--no-stop]"
+                 " [--kv-dtype f32|bf16|fp8] [--weights f32|bf16] [--page-size 16] [--gpu N]\n";
     return 2;
 }
 
@@ -97,6 +104,18 @@ bool write_f32(const std::string &path, const std::vector<float> &v, std::string
     return true;
 }
 
+// The element type a backend switch selects, as the backend reads it: one of
+// `other`, else f32 (unset, empty or unrecognised values keep f32).
+std::string switch_value(const char *name, std::initializer_list<const char *> other) {
+    const char *v = std::getenv(name);
+    if (v) {
+        for (const char *o : other) {
+            if (std::string(v) == o) return o;
+        }
+    }
+    return "f32";
+}
+
 double ms_since(std::chrono::steady_clock::time_point t0) {
     return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
 }
@@ -110,6 +129,7 @@ int main(int argc, char **argv) {
     bool prefill = false, no_stop = false, have_stop = false;
     std::vector<int32_t> stop_ids;
     QwenAsrGgmlDevice device = qwenasr_ggml_device_auto();
+    std::string kv_dtype, weights, gpu;
     for (int i = 1; i < argc; ++i) {
         const std::string a = argv[i];
         auto need = [&](const char *what) -> const char * {
@@ -143,12 +163,34 @@ int main(int argc, char **argv) {
             std::string tok;
             while (std::getline(ss, tok, ',')) if (!tok.empty()) stop_ids.push_back(static_cast<int32_t>(std::atoi(tok.c_str())));
             have_stop = true;
+        } else if (a == "--kv-dtype") {
+            kv_dtype = need("f32, bf16 or fp8");
+            if (kv_dtype != "f32" && kv_dtype != "bf16" && kv_dtype != "fp8") {
+                std::cerr << "--kv-dtype must be f32, bf16 or fp8\n";
+                return 2;
+            }
+        } else if (a == "--weights") {
+            weights = need("f32 or bf16");
+            if (weights != "f32" && weights != "bf16") { std::cerr << "--weights must be f32 or bf16\n"; return 2; }
+        } else if (a == "--page-size") {
+            if (std::string(need("16")) != "16") { std::cerr << "--page-size: the paged cache has 16-token pages only\n"; return 2; }
+        } else if (a == "--gpu") {
+            char *end = nullptr;
+            const long v = std::strtol(need("a device ordinal"), &end, 10);
+            if (!end || *end || v < 0 || v > 255) { std::cerr << "--gpu requires a device ordinal 0..255\n"; return 2; }
+            gpu = std::to_string(v);
         } else if (a == "--threads") need("a positive integer");   // accepted for CLI compatibility
         else if (model_path.empty()) model_path = a;
         else if (input_path.empty()) input_path = a;
         else { std::cerr << "too many positional arguments\n"; return 2; }
     }
     if (prefill && generate >= 0) { std::cerr << "--prefill and --generate are mutually exclusive\n"; return 2; }
+    // A flag overrides the switch; without one the switch (or its f32 default) stands.
+    if (!kv_dtype.empty()) setenv("QWENASR_B200_KV", kv_dtype.c_str(), 1);
+    if (!weights.empty()) setenv("QWENASR_B200_WEIGHTS", weights.c_str(), 1);
+    if (!gpu.empty()) setenv("QWENASR_B200_DEVICE", gpu.c_str(), 1);
+    const std::string kv_shown = switch_value("QWENASR_B200_KV", {"bf16", "fp8"});
+    const std::string weights_shown = switch_value("QWENASR_B200_WEIGHTS", {"bf16"});
 
     const auto t_init = std::chrono::steady_clock::now();
     QwenAsrGgufModel model;
@@ -185,6 +227,9 @@ int main(int argc, char **argv) {
     std::cout << "layers=" << L << "\n";
     std::cout << "prompt_tokens=" << input.tokens << "\n";
     std::cout << "hidden=" << H << "\n";
+    std::cout << "kv_dtype=" << kv_shown << "\n";
+    std::cout << "weights=" << weights_shown << "\n";
+    std::cout << "page_tokens=16\n";
 
     if (generate >= 0) {
         const auto t0 = std::chrono::steady_clock::now();
@@ -211,6 +256,8 @@ int main(int argc, char **argv) {
         std::cout << "vocab=" << out.vocab << "\n";
         std::cout << "requested_tokens=" << generate << "\n";
         std::cout << "generated_tokens=" << out.generated_ids.size() << "\n";
+        std::cout << "tokens_per_s=" << (generate_ms > 0 ? 1e3 * static_cast<double>(out.generated_ids.size()) / generate_ms : 0.0)
+                  << "\n";
         std::cout << "stopped=" << (out.stopped ? "true" : "false") << "\n";
         std::cout << "generated_ids=";
         for (size_t i = 0; i < out.generated_ids.size(); ++i) std::cout << (i ? "," : "") << out.generated_ids[i];

@@ -39,16 +39,42 @@ def test_cli_usage_and_cpu_device_rejected(case):
     assert rc == 2
 
 
+@pytest.mark.parametrize("flags,msg", [(["--kv-dtype", "int8"], "--kv-dtype"), (["--weights", "fp8"], "--weights"),
+                                       (["--page-size", "32"], "16-token pages"), (["--gpu", "x"], "--gpu")])
+def test_cli_rejects_bad_b200_options(case, flags, msg):
+    """The B200 options are checked before any file or device is touched."""
+    path, inp, g, d = case
+    rc, kv, err = run([path, inp, "--generate", "2", *flags])
+    assert rc == 2 and msg in err, err
+
+
 @pytest.mark.gpu
 def test_cli_generate_matches_reference(case):
     path, inp, g, d = case
     rc, kv, err = run([path, inp, "--generate", "16", "--no-stop"])
     assert rc == 0, err
     assert kv["mode"] == "generate" and kv["prompt_tokens"] == str(g["x"].shape[0])
+    assert kv["kv_dtype"] == "f32" and kv["weights"] == "f32" and kv["page_tokens"] == "16"
+    assert float(kv["tokens_per_s"]) > 0
     assert [int(t) for t in kv["generated_ids"].split(",")] == g["ref_ids"].tolist()
     rc, kv, err = run([path, inp, "--generate", "16", "--stop-ids", str(int(g["stop_id"]))])
     assert rc == 0 and kv["stopped"] == "true"
     assert [int(t) for t in kv["generated_ids"].split(",")] == g["ref_ids_stop"].tolist()
+
+
+@pytest.mark.gpu
+def test_cli_b200_options(case):
+    """--kv-dtype / --weights / --page-size / --gpu reach the backend: an e4m3
+    cache with bf16 weights generates the requested count of in-vocabulary
+    ids.  (Agreement with the reference's ids at these types is measured by
+    the model tests; this tiny model's top-1 margin is too small to pin.)"""
+    path, inp, g, d = case
+    rc, kv, err = run([path, inp, "--generate", "16", "--no-stop", "--kv-dtype", "fp8", "--weights", "bf16",
+                       "--page-size", "16", "--gpu", "0"])
+    assert rc == 0, err
+    assert kv["kv_dtype"] == "fp8" and kv["weights"] == "bf16"
+    ids = [int(t) for t in kv["generated_ids"].split(",")]
+    assert len(ids) == 16 and all(0 <= t < int(kv["vocab"]) for t in ids)
 
 
 @pytest.mark.gpu
