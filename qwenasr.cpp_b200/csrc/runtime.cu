@@ -13,6 +13,8 @@
 #include <thread>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "gguf.h"
 
 using qkv::DevError;
@@ -27,6 +29,16 @@ int fail(qkv_handle *h, int code, const std::string &msg) {
 int cuda_fail(qkv_handle *h, cudaError_t e, const char *what) {
     return fail(h, QKV_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
+
+// An NVTX range around a C entry point, so a profiler's timeline (and ncu's
+// --nvtx filters) can pick out prefill, decode and the operator steps; a
+// load and a branch when no tool is attached.
+struct TraceRange {
+    explicit TraceRange(const char *name) { nvtxRangePushA(name); }
+    ~TraceRange() { nvtxRangePop(); }
+    TraceRange(const TraceRange &) = delete;
+    TraceRange &operator=(const TraceRange &) = delete;
+};
 
 // Owner of a temporary device buffer of a host-driven call (the compaction
 // move list, the fill list, a gather target): freed on every return path,
@@ -876,6 +888,7 @@ int qkv_read_gguf_config(const char *gguf_path, qkv_model_config *cfg, char *err
 
 int qkv_create(const char *gguf_path, const qkv_model_config *cfg, const qkv_runtime_config *rt, qkv_handle **out,
                char *err, size_t err_len) {
+    const TraceRange trace("qkv_create");
     if (!out || !rt) {
         set_err(err, err_len, "out or rt is null");
         return QKV_ERR_INVALID_ARG;
@@ -999,6 +1012,7 @@ int qkv_pool_stats(const qkv_handle *h, int64_t *free_pages, int64_t *total_page
 }
 
 int qkv_compact(qkv_handle *h, int64_t *moved) {
+    const TraceRange trace("qkv_compact");
     if (!h) return QKV_ERR_INVALID_ARG;
     CK(cudaSetDevice(h->device));
     CK(cudaStreamSynchronize(h->stream));
@@ -1164,6 +1178,7 @@ static int prefill_impl(qkv_handle *h, int32_t n, const int32_t *stream_ids, con
 
 int qkv_prefill(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *lens, const float *embeddings,
                 int32_t *out_ids, float *out_logits) {
+    const TraceRange trace("qkv_prefill");
     if (!h) return QKV_ERR_INVALID_ARG;
     if (!h->has_weights) return fail(h, QKV_ERR_STATE, "handle has no model weights");
     if (!lens || !embeddings) return fail(h, QKV_ERR_INVALID_ARG, "null lens or embeddings");
@@ -1181,6 +1196,7 @@ int qkv_prefill(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32
 
 int qkv_prefill_rows(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *lens,
                      const float *const *embeddings, int32_t *out_ids, float *out_logits) {
+    const TraceRange trace("qkv_prefill_rows");
     if (!h) return QKV_ERR_INVALID_ARG;
     if (!h->has_weights) return fail(h, QKV_ERR_STATE, "handle has no model weights");
     if (!lens || !embeddings) return fail(h, QKV_ERR_INVALID_ARG, "null lens or embeddings");
@@ -1194,6 +1210,7 @@ int qkv_prefill_rows(qkv_handle *h, int32_t n, const int32_t *stream_ids, const 
 int qkv_prefill_ids(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *lens, const int32_t *ids,
                     const float *const *audio, const int32_t *audio_tokens, int32_t audio_on_device,
                     int32_t audio_token_id, int32_t *out_ids, float *out_logits) {
+    const TraceRange trace("qkv_prefill_ids");
     if (!h) return QKV_ERR_INVALID_ARG;
     if (!h->has_weights) return fail(h, QKV_ERR_STATE, "handle has no model weights");
     if (n < 0) return fail(h, QKV_ERR_INVALID_ARG, "negative stream count");
@@ -1218,6 +1235,7 @@ int qkv_audio_projector_width(const qkv_handle *h, int32_t *width) {
 // decoder-width rows (device).  Intermediates live in the handle's prefill
 // scratch: LayerNorm output in act, proj0 sums in gu, GELU output in xn.
 int qkv_audio_project(qkv_handle *h, int32_t n, const float *audio_dev, float *out_dev, void *stream) {
+    const TraceRange trace("qkv_audio_project");
     if (!h) return QKV_ERR_INVALID_ARG;
     if (!h->has_weights || h->audio_hidden <= 0) return fail(h, QKV_ERR_STATE, "the model file has no audio projector");
     if (n < 0 || (n > 0 && (!audio_dev || !out_dev))) return fail(h, QKV_ERR_INVALID_ARG, "bad row count or pointer");
@@ -1245,6 +1263,7 @@ int qkv_audio_project(qkv_handle *h, int32_t n, const float *audio_dev, float *o
 int qkv_decoder_input(qkv_handle *h, int32_t n, const int32_t *lens, const int32_t *ids, const float *const *audio,
                       const int32_t *audio_tokens, int32_t audio_on_device, int32_t audio_token_id, float *x_dev,
                       void *stream) {
+    const TraceRange trace("qkv_decoder_input");
     if (!h) return QKV_ERR_INVALID_ARG;
     if (!h->has_weights) return fail(h, QKV_ERR_STATE, "handle has no model weights");
     if (n < 0 || !x_dev) return fail(h, QKV_ERR_INVALID_ARG, "negative stream count or null output");
@@ -1257,6 +1276,7 @@ int qkv_decoder_input(qkv_handle *h, int32_t n, const int32_t *lens, const int32
 
 int qkv_decode_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const int32_t *in_ids, int32_t *out_ids,
                     float *out_logits) {
+    const TraceRange trace("qkv_decode_step");
     if (!h) return QKV_ERR_INVALID_ARG;
     if (!h->has_weights) return fail(h, QKV_ERR_STATE, "handle has no model weights");
     int rc;
@@ -1310,6 +1330,7 @@ int qkv_decode_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const i
 }
 
 int qkv_layer_forward(qkv_handle *h, int32_t layer, int32_t tokens, const float *x, float *out) {
+    const TraceRange trace("qkv_layer_forward");
     if (!h) return QKV_ERR_INVALID_ARG;
     if (!h->has_weights) return fail(h, QKV_ERR_STATE, "handle has no model weights");
     if (layer < 0 || layer >= h->cfg.n_layers || tokens <= 0 || !x || !out)
@@ -1352,6 +1373,7 @@ int qkv_layer_forward(qkv_handle *h, int32_t layer, int32_t tokens, const float 
 
 int qkv_generate(qkv_handle *h, const float *embeddings, int32_t tokens, int32_t max_new_tokens, const int32_t *stop_ids,
                  int32_t n_stop, int32_t *out_ids, int32_t *n_out, int32_t *stopped) {
+    const TraceRange trace("qkv_generate");
     if (!h) return QKV_ERR_INVALID_ARG;
     if (n_out) *n_out = 0;
     if (stopped) *stopped = 0;
@@ -1467,6 +1489,7 @@ int qkv_prefill_attend_q16(qkv_handle *h, int32_t layer, int32_t n, const int32_
 }
 
 int qkv_kv_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const float *qkv_dev, float *out_dev, void *stream) {
+    const TraceRange trace("qkv_kv_step");
     if (!h) return QKV_ERR_INVALID_ARG;
     int rc;
     if ((rc = check_streams(h, n, stream_ids))) return rc;
@@ -1519,6 +1542,7 @@ int qkv_kv_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const float
 // inputs, and its outputs come back on copy_out as soon as its attention has
 // run, so PCIe traffic in both directions overlaps the kernels.
 int qkv_kv_step_host(qkv_handle *h, int32_t n, const int32_t *stream_ids, const float *qkv_host, float *out_host) {
+    const TraceRange trace("qkv_kv_step_host");
     if (!h) return QKV_ERR_INVALID_ARG;
     if (!qkv_host || !out_host || n <= 0) return fail(h, QKV_ERR_INVALID_ARG, "null host pointer or empty batch");
     int rc;
