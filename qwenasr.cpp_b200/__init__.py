@@ -268,9 +268,16 @@ class Decoder:
         return d
 
     def close(self):
-        if self.h:
+        if getattr(self, "h", None):
             lib.qkv_destroy(self.h)
             self.h = None
+
+    def __del__(self):
+        # A handle dropped without close() still returns its pool and weights.
+        try:
+            self.close()
+        except Exception:
+            pass
 
     def __enter__(self):
         return self
