@@ -25,7 +25,7 @@ BIN = PKG / "bin"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
+COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall,-Wextra,-Wshadow",
           f"-I{ROOT / 'include'}", f"-I{CSRC}", f"-I{CSRC / 'adapter'}", "--expt-relaxed-constexpr"]
 
 

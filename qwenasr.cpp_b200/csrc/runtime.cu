@@ -1318,7 +1318,8 @@ int qkv_decode_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const i
                 h->decode_graphs.clear();
             }
             qkv_handle::Graph g;
-            if ((rc = capture_graph(h, body, &g))) return rc;
+            rc = capture_graph(h, body, &g);
+            if (rc) return rc;
             it = h->decode_graphs.emplace(n, g).first;
         }
         CK(cudaGraphLaunch(it->second.exec, h->stream));
@@ -1529,7 +1530,8 @@ int qkv_kv_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const float
             h->kv_graphs.clear();
         }
         qkv_handle::Graph g;
-        if ((rc = capture_graph(h, [&]() { return body(h->stream); }, &g))) return rc;
+        rc = capture_graph(h, [&]() { return body(h->stream); }, &g);
+        if (rc) return rc;
         it = h->kv_graphs.emplace(key, g).first;
     }
     CK(cudaGraphLaunch(it->second.exec, st));
