@@ -86,6 +86,25 @@ int code_point(const char *s, int left, int *adv) {
     return cp;
 }
 
+// The reference's reading of a segment (src/tokenizer.cpp:71-96 inside the
+// loops of :140-262): the code point at s takes the whole length its lead
+// byte announces, even where the segment ends sooner, and a chunk is cut with
+// that length.  Past the end the reference reads the segment's string
+// terminator (zero) and, for a sequence short by two or three bytes, the
+// bytes after it, which were zero in its runs here.  pre_tokenize therefore
+// reads a copy of the segment followed by three zero bytes: a sequence cut
+// off at a segment's end gives a chunk ending in zero bytes, byte-level
+// encoded like any other byte, as the reference does.
+int code_point_padded(const char *s, int *adv) {
+    const unsigned char c = static_cast<unsigned char>(s[0]);
+    const int n = piece_len(c, 4);
+    *adv = n;
+    if (n == 1) return c;
+    int cp = n == 2 ? (c & 0x1F) : n == 3 ? (c & 0x0F) : (c & 0x07);
+    for (int k = 1; k < n; ++k) cp = (cp << 6) | (static_cast<unsigned char>(s[k]) & 0x3F);
+    return cp;
+}
+
 bool is_letter(int cp) {
     if ((cp >= 'A' && cp <= 'Z') || (cp >= 'a' && cp <= 'z')) return true;
     if (cp < 0x80) return false;
@@ -99,12 +118,13 @@ bool is_space(int cp) { return cp == ' ' || cp == '\t' || cp == 0x0B || cp == 0x
 
 std::vector<std::string> pre_tokenize(const std::string &text) {
     std::vector<std::string> chunks;
-    const char *s = text.data();
+    const std::string padded = text + std::string(3, '\0');   // reads and chunks may run 3 bytes past the end
+    const char *s = padded.data();
     const int len = static_cast<int>(text.size());
     auto run = [&](int i, bool (*keep)(int)) {   // end of the run of `keep` code points from i
         while (i < len) {
             int a = 0;
-            if (!keep(code_point(s + i, len - i, &a))) break;
+            if (!keep(code_point_padded(s + i, &a))) break;
             i += a;
         }
         return i;
@@ -112,7 +132,7 @@ std::vector<std::string> pre_tokenize(const std::string &text) {
     int i = 0;
     while (i < len) {
         int adv = 0;
-        const int cp = code_point(s + i, len - i, &adv);
+        const int cp = code_point_padded(s + i, &adv);
         if (cp == '\'' && i + adv < len) {
             static const char *suffixes[] = {"ll", "re", "ve", "s", "t", "m", "d"};
             const char *rest = s + i + adv;
@@ -134,7 +154,7 @@ std::vector<std::string> pre_tokenize(const std::string &text) {
         }
         if (is_space(cp) && i + adv < len) {
             int a2 = 0;
-            if (is_letter(code_point(s + i + adv, len - i - adv, &a2))) {
+            if (is_letter(code_point_padded(s + i + adv, &a2))) {
                 const int end = run(i + adv + a2, is_letter);
                 chunks.emplace_back(s + i, static_cast<size_t>(end - i));
                 i = end;

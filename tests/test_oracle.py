@@ -261,3 +261,38 @@ def test_tokenizer_capi_contract(pkg, dec_input):
     assert lib.qkv_tokenizer_encode(None, text, len(text), 0, big.ctypes.data_as(i32), 8, C.byref(n)) == 1
     assert lib.qkv_asr_prompt_ids(tok.h, 2, b"", b"", None, 0, None) == 1
     tok.close()
+
+
+def test_encode_reference_live_bytes(pkg, dec_input, checker):
+    """Byte strings at the edges of the pre-tokeniser's classes, against the
+    reference's own encoder: other whitespace (VT, FF, NBSP, ideographic
+    space), non-ASCII digits and letters, invalid UTF-8 (lone continuation
+    bytes, truncated sequences, 0xFF), contractions in other cases and
+    fragments of the special tokens.
+
+    A sequence cut off at the end of a segment (the text's end, or just
+    before a special token) makes the reference read past the segment: one
+    missing byte reads its string terminator, a zero byte, which ends up in
+    the ids; two or three missing bytes read memory after the terminator,
+    whose contents are not defined.  So every truncated piece here is short
+    by one byte at most, whatever follows it."""
+    if not checker.ref_available():
+        pytest.skip("oracle/_ref not built")
+    _, _, path = dec_input
+    tok = pkg.Tokenizer(path)
+    rng = np.random.default_rng(23)
+    pieces = [b"a", b"Z", b" ", b"   ", b"\t", b"\x0b", b"\x0c", b"\n", b"\r", b"\r\n\n", b"\xc2\xa0", b"\xe3\x80\x80",
+              b"0", b"42", b"\xd9\xa3", b"\xef\xbc\x91", b"\xc3\xa9", b"\xce\xb1\xce\xb2", b"\xe4\xb8\xad\xe6\x96\x87",
+              b"\xf0\x9f\x98\x80", b"\xff", b"\xc3", b"\x80", b"\xe4\xb8", b"\xf0\x9f\x98", b"'s", b"'S", b"'LL", b"'", b"''",
+              b"'ve", b" 'm", b"<|im_", b"end|>", b"<|im_end|>", b"<|audio_pad|><|audio_pad|>", b"<asr_text>",
+              b"<", b"|>", b"!!", b"...", b"-", b"_", b"#", b"\x01", b"\x7f"]
+    known = [b"\xc3", b"a\xc3", b"\xe4\xb8", b"x\xf0\x9f\x98", b"\xc3<|im_end|>", b"ab\xe4\xb8<asr_text>x",
+             b" \xce", b"\t\xc3"]
+    for text in known:
+        assert tok.encode(text, False).tolist() == checker.ref_tokenizer_encode(str(path), text, False).tolist(), text
+    assert 0 in tok.encode(b"a\xc3", False).tolist()     # the terminator's zero byte, as the reference
+    for _ in range(120):
+        text = b"".join(pieces[int(i)] for i in rng.integers(0, len(pieces), size=int(rng.integers(0, 40))))
+        want = checker.ref_tokenizer_encode(str(path), text, False)
+        got = tok.encode(text, False)
+        assert got.tolist() == want.tolist(), text
