@@ -340,8 +340,12 @@ int qkv_tokenizer_decode(const qkv_tokenizer *t, const int32_t *ids, int32_t n, 
             const std::string &tok = t->id_to_token[static_cast<size_t>(id)];
             const int L = static_cast<int>(tok.size());
             for (int pos = 0; pos < L;) {
-                const int adv = piece_len(static_cast<unsigned char>(tok[static_cast<size_t>(pos)]), L - pos);
-                const std::string piece = tok.substr(static_cast<size_t>(pos), static_cast<size_t>(adv));
+                // A piece is the sequence the lead byte announces; one cut off at
+                // the token's end runs on into zero bytes, as the reference's
+                // piece does (it reads the token's terminator: :513-516).
+                const int adv = piece_len(static_cast<unsigned char>(tok[static_cast<size_t>(pos)]), 4);
+                std::string piece = tok.substr(static_cast<size_t>(pos), static_cast<size_t>(adv));
+                piece.resize(static_cast<size_t>(adv), '\0');
                 const auto it = t->byte_of.find(piece);
                 if (it != t->byte_of.end()) s.push_back(static_cast<char>(it->second));
                 else s += piece;

@@ -201,6 +201,33 @@ def test_detokenize_reference_live(pkg, dec_input, checker):
             assert tok.decode(ids, skip) == checker.ref_tokenizer_decode(str(path), ids, skip)
 
 
+def test_detokenize_malformed_vocabulary_reference_live(pkg, dec_input, checker, tmp_path):
+    """Vocabulary entries that are not byte-symbol strings (invalid UTF-8,
+    a sequence cut off by the token's end), patched into a copy of the model
+    file in place of filler tokens of the same length: decoding them matches
+    the reference's own decoder, which reads a cut-off sequence on into the
+    token's zero terminator.  Cut-offs are one byte short, the case where
+    that read is defined."""
+    if not checker.ref_available():
+        pytest.skip("oracle/_ref not built")
+    _, _, path = dec_input
+    data = bytearray(Path(path).read_bytes())
+    patches = {900: b"abcde\xc3", 901: b"abcd\xe4\xb8", 902: b"\xf0\x9f\x98xyz", 903: b"\xff\x80ab\xc2\xa0",
+               904: b"\xc4\x80abc\xc3", 905: b"\xe4\xb8\xadxy\xce"}
+    for tid, new in patches.items():
+        old = f"<t{tid}>".encode()
+        assert len(new) == len(old) and data.count(old) == 1
+        data[data.index(old):data.index(old) + len(old)] = new
+    bad = tmp_path / "malformed_vocab.gguf"
+    bad.write_bytes(bytes(data))
+    tok = pkg.Tokenizer(bad)
+    ids = np.array([900, 901, 902, 903, 904, 905, 97, 900, 259, 905], np.int32)
+    for skip in (False, True):
+        want = checker.ref_tokenizer_decode(str(bad), ids, skip)
+        assert tok.decode(ids, skip) == want
+        assert tok.decode(ids[:1], skip) == b"abcde\xc3\x00"   # the terminator's zero byte, as the reference
+
+
 def test_tokenizer_open_errors(pkg, synth, tmp_path):
     p = synth.write_gguf(tmp_path / "none.gguf", dict(synth.TINY), seed=0, tokenizer=False)
     with pytest.raises(pkg.QkvError) as ei:
