@@ -291,11 +291,15 @@ int open_tokenizer(const char *gguf_path, qkv_tokenizer **out, char *err, size_t
             set_err(err, err_len, std::string("tokenizer special id out of range for key: ") + k);
             return QKV_ERR_FORMAT;
         }
-        t->special[id] = 1;
+        // A special joins the list (and is skipped by decode) unless its token
+        // is empty or already listed under an earlier key, as :265-281 keep it.
         const std::string &tok = t->id_to_token[id];
         bool seen = tok.empty();
         for (const auto &sp : t->specials) seen = seen || sp.first == tok;
-        if (!seen) t->specials.emplace_back(tok, static_cast<int32_t>(id));
+        if (!seen) {
+            t->specials.emplace_back(tok, static_cast<int32_t>(id));
+            t->special[id] = 1;
+        }
     }
     std::sort(t->specials.begin(), t->specials.end(), [](const auto &a, const auto &b) {
         return a.first.size() != b.first.size() ? a.first.size() > b.first.size() : a.first < b.first;

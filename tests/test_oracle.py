@@ -228,6 +228,41 @@ def test_detokenize_malformed_vocabulary_reference_live(pkg, dec_input, checker,
         assert tok.decode(ids[:1], skip) == b"abcde\xc3\x00"   # the terminator's zero byte, as the reference
 
 
+def test_special_list_edge_cases_reference_live(pkg, synth, checker, tmp_path):
+    """Special-token keys whose token strings repeat an earlier key's, or are
+    empty: the reference lists a special only once and never an empty one,
+    and decode skips only listed ids.  A tokenizer-only file (no tensors)
+    written with the gguf package's writer; ids and bytes match the
+    reference's own encoder and decoder."""
+    if not checker.ref_available():
+        pytest.skip("oracle/_ref not built")
+    gguf = pytest.importorskip("gguf")
+    tokens = synth.byte_symbols() + ["<|endoftext|>", "<|im_start|>", "<|im_end|>", "<|audio_start|>",
+                                     "<|audio_end|>", "<|audio_pad|>", "<asr_text>", "<|im_end|>", "", "ab"]
+    keys = {"endoftext": 256, "im_start": 257, "im_end": 258, "audio_start": 259,
+            "audio_end": 263,        # the same string as im_end, under a later key
+            "audio": 261, "asr_text": 264}   # an empty token
+    p = tmp_path / "specials.gguf"
+    w = gguf.GGUFWriter(str(p), "qwen3-asr")
+    w.add_array("tokenizer.ggml.tokens", tokens)
+    w.add_array("tokenizer.ggml.merges", ["a b"])
+    w.add_uint32("tokenizer.ggml.eos_token_id", 258)
+    for k, v in keys.items():
+        w.add_uint32(f"qwen3-asr.token.{k}_token_id", v)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    tok = pkg.Tokenizer(p)
+    ids = np.array([258, 263, 264, 97, 262, 265, 256, 260], np.int32)
+    for skip in (False, True):
+        assert tok.decode(ids, skip) == checker.ref_tokenizer_decode(str(p), ids, skip), skip
+    assert tok.decode(np.array([263, 264], np.int32), True) == b"<|im_end|>"   # 263 is not listed, 264 is empty
+    for text in (b"x<|im_end|>y", b"<asr_text>ab<|audio_pad|>", b"ab ab", b"<|audio_end|>"):
+        for eos in (False, True):
+            assert tok.encode(text, eos).tolist() == checker.ref_tokenizer_encode(str(p), text, eos).tolist(), text
+
+
 def test_tokenizer_open_errors(pkg, synth, tmp_path):
     p = synth.write_gguf(tmp_path / "none.gguf", dict(synth.TINY), seed=0, tokenizer=False)
     with pytest.raises(pkg.QkvError) as ei:
