@@ -116,6 +116,26 @@ std::string switch_value(const char *name, std::initializer_list<const char *> o
     return "f32";
 }
 
+// min / max / mean of an output, as the reference tool prints them for its
+// prefill logits and layer rows (the mean summed in double).
+struct Summary {
+    float min = 0.f, max = 0.f;
+    double mean = 0.0;
+};
+Summary summarize(const std::vector<float> &v) {
+    Summary s;
+    if (v.empty()) return s;
+    s.min = s.max = v[0];
+    double sum = 0.0;
+    for (const float x : v) {
+        s.min = x < s.min ? x : s.min;
+        s.max = x > s.max ? x : s.max;
+        sum += x;
+    }
+    s.mean = sum / static_cast<double>(v.size());
+    return s;
+}
+
 double ms_since(std::chrono::steady_clock::time_point t0) {
     return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
 }
@@ -129,7 +149,7 @@ int main(int argc, char **argv) {
     bool prefill = false, no_stop = false, have_stop = false;
     std::vector<int32_t> stop_ids;
     QwenAsrGgmlDevice device = qwenasr_ggml_device_auto();
-    std::string kv_dtype, weights, gpu;
+    std::string kv_dtype, weights, gpu, threads = "1";
     for (int i = 1; i < argc; ++i) {
         const std::string a = argv[i];
         auto need = [&](const char *what) -> const char * {
@@ -179,7 +199,7 @@ int main(int argc, char **argv) {
             const long v = std::strtol(need("a device ordinal"), &end, 10);
             if (!end || *end || v < 0 || v > 255) { std::cerr << "--gpu requires a device ordinal 0..255\n"; return 2; }
             gpu = std::to_string(v);
-        } else if (a == "--threads") need("a positive integer");   // accepted for CLI compatibility
+        } else if (a == "--threads") threads = need("a positive integer");   // accepted and echoed; the GPU path has no host threads to size
         else if (model_path.empty()) model_path = a;
         else if (input_path.empty()) input_path = a;
         else { std::cerr << "too many positional arguments\n"; return 2; }
@@ -214,16 +234,22 @@ int main(int argc, char **argv) {
     }
     if (no_stop) stop_ids.clear();
 
+    const double init_ms = ms_since(t_init);
+    // decoder_input_ms: the reference tool assembles the decoder input from
+    // audio here; this harness reads the assembled rows from INPUT.f32.
+    const auto t_input = std::chrono::steady_clock::now();
     QwenAsrDecoderInputOutput input;
     if (!read_f32(input_path, &input.values, &error)) { std::cerr << error << "\n"; return 1; }
     if (input.values.size() % H != 0) { std::cerr << "input size is not a multiple of hidden\n"; return 1; }
     input.hidden = static_cast<int>(H);
     input.tokens = static_cast<int>(input.values.size() / H);
-    const double init_ms = ms_since(t_init);
+    const double decoder_input_ms = ms_since(t_input);
 
     std::cout << "backend=b200\n";
     std::cout << "device=" << qwenasr_ggml_device_name(device) << "\n";
+    std::cout << "threads=" << threads << "\n";
     std::cout << "init_ms=" << init_ms << "\n";
+    std::cout << "decoder_input_ms=" << decoder_input_ms << "\n";
     std::cout << "layers=" << L << "\n";
     std::cout << "prompt_tokens=" << input.tokens << "\n";
     std::cout << "hidden=" << H << "\n";
@@ -292,11 +318,18 @@ int main(int argc, char **argv) {
         int top = 0;
         for (int i = 1; i < out.vocab; ++i) if (out.logits[static_cast<size_t>(i)] > out.logits[static_cast<size_t>(top)]) top = i;
         if (!out_path.empty() && !write_f32(out_path, out.logits, &error)) { std::cerr << error << "\n"; return 1; }
+        const Summary sm = summarize(out.logits);
         std::cout << "mode=prefill\n";
         std::cout << "text_init_ms=" << text_init_ms << "\n";
         std::cout << "prefill_ms=" << prefill_ms << "\n";
+        std::cout << "tokens=" << out.tokens << "\n";
         std::cout << "vocab=" << out.vocab << "\n";
+        std::cout << "values=" << out.logits.size() << "\n";
         std::cout << "top_id=" << top << "\n";
+        std::cout << "top_logit=" << out.logits[static_cast<size_t>(top)] << "\n";
+        std::cout << "min=" << sm.min << "\n";
+        std::cout << "max=" << sm.max << "\n";
+        std::cout << "mean=" << sm.mean << "\n";
         return 0;
     }
     QwenAsrTextLayerBackend *b = nullptr;
@@ -312,9 +345,14 @@ int main(int argc, char **argv) {
     qwenasr_text_layer_backend_free(b);
     if (!ok) { std::cerr << error << "\n"; return 1; }
     if (!out_path.empty() && !write_f32(out_path, out.values, &error)) { std::cerr << error << "\n"; return 1; }
+    const Summary sm = summarize(out.values);
     std::cout << "mode=layer\n";
+    std::cout << "text_layer_ms=" << layer_ms << "\n";
     std::cout << "layer=" << layer << "\n";
-    std::cout << "layer_ms=" << layer_ms << "\n";
     std::cout << "tokens=" << out.tokens << "\n";
+    std::cout << "values=" << out.values.size() << "\n";
+    std::cout << "min=" << sm.min << "\n";
+    std::cout << "max=" << sm.max << "\n";
+    std::cout << "mean=" << sm.mean << "\n";
     return 0;
 }

@@ -55,7 +55,7 @@ def test_cli_generate_matches_reference(case):
     assert rc == 0, err
     assert kv["mode"] == "generate" and kv["prompt_tokens"] == str(g["x"].shape[0])
     assert kv["kv_dtype"] == "f32" and kv["weights"] == "f32" and kv["page_tokens"] == "16"
-    assert float(kv["tokens_per_s"]) > 0
+    assert float(kv["tokens_per_s"]) > 0 and float(kv["decoder_input_ms"]) >= 0   # keys the reference's benches read
     assert [int(t) for t in kv["generated_ids"].split(",")] == g["ref_ids"].tolist()
     rc, kv, err = run([path, inp, "--generate", "16", "--stop-ids", str(int(g["stop_id"]))])
     assert rc == 0 and kv["stopped"] == "true"
@@ -86,11 +86,21 @@ def test_cli_prefill_and_layer_outputs(case):
     logits = np.fromfile(out, np.float32)
     assert rel_err(logits, g["ref_prefill_logits"]) < 1e-3
     assert int(kv["top_id"]) == int(np.argmax(g["ref_prefill_logits"]))
+    # the reference tool's prefill keys (tools/qwen-asr-text-layer.cpp:603-625)
+    assert int(kv["tokens"]) == g["x"].shape[0] and int(kv["values"]) == logits.size
+    assert float(kv["top_logit"]) == pytest.approx(float(logits.max()), rel=1e-5)
+    assert float(kv["min"]) == pytest.approx(float(logits.min()), rel=1e-5)
+    assert float(kv["max"]) == pytest.approx(float(logits.max()), rel=1e-5)
+    assert float(kv["mean"]) == pytest.approx(float(logits.astype(np.float64).mean()), rel=1e-4, abs=1e-6)
+    assert float(kv["decoder_input_ms"]) >= 0 and kv["threads"] == "1"
     out = d / "layer0.f32"
-    rc, kv, err = run([path, inp, "--layer", "0", "--out", out])
+    rc, kv, err = run([path, inp, "--layer", "0", "--out", out, "--threads", "8"])
     assert rc == 0, err
     vals = np.fromfile(out, np.float32).reshape(g["ref_layer0"].shape)
     assert rel_err(vals, g["ref_layer0"]) < 1e-4
+    # the reference tool's layer keys (:715-735)
+    assert float(kv["text_layer_ms"]) > 0 and int(kv["values"]) == vals.size and kv["threads"] == "8"
+    assert float(kv["max"]) == pytest.approx(float(vals.max()), rel=1e-5)
 
 
 def json_escape(b: bytes) -> bytes:
