@@ -263,6 +263,31 @@ def test_special_list_edge_cases_reference_live(pkg, synth, checker, tmp_path):
             assert tok.encode(text, eos).tolist() == checker.ref_tokenizer_encode(str(p), text, eos).tolist(), text
 
 
+def test_asr_prompt_ids_reference_live(pkg, dec_input, checker):
+    """qkv_asr_prompt_ids against the ids the reference's own decoder-input
+    assembly builds (qwenasr_build_asr_prompt + qwenasr_tokenizer_encode,
+    reached through qwenasr_decoder_input_from_audio) for random system
+    texts (special-token strings inside them included), languages and
+    audio counts."""
+    if not checker.ref_available():
+        pytest.skip("oracle/_ref not built")
+    g, embd, path = dec_input
+    tok = pkg.Tokenizer(path)
+    aid = int(g["audio_token_id"])
+    rng = np.random.default_rng(31)
+    pieces = ["You", " are", " a", " helpful", " assistant", ".", "\n", "  ", "'s", "42", "é", "中文", "<|im_end|>",
+              "<|im_start|>", "<asr_text>", "language", " ", "\t", "!"]
+    languages = ["", "English", "Chinese", "日本語", "x<asr_text>", " German", "fr-FR"]
+    for _ in range(40):
+        system = "".join(rng.choice(pieces, size=int(rng.integers(0, 12))))
+        language = str(rng.choice(languages))
+        n_audio = int(rng.integers(0, 40))
+        rc, ref_ids, _, msg = checker.ref_decoder_input(str(path), np.zeros((n_audio, embd.shape[1]), np.float32), aid,
+                                                       system, language)
+        assert rc == 0, msg
+        assert tok.asr_prompt_ids(n_audio, system, language).tolist() == ref_ids.tolist(), (system, language)
+
+
 def test_tokenizer_open_errors(pkg, synth, tmp_path):
     p = synth.write_gguf(tmp_path / "none.gguf", dict(synth.TINY), seed=0, tokenizer=False)
     with pytest.raises(pkg.QkvError) as ei:
