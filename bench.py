@@ -147,19 +147,30 @@ def sum_over_ranks(dist, v: float) -> float:
 
 # ------------------------------------------------------------------ CPU legs
 
-def cpu_kv_sample(lens: np.ndarray, n_streams: int, steps: int, threads: int):
+def config4(kv_dtype: str, world: int, mean_ctx: float) -> dict:
+    """The config of the default workload's line, shared by both arms."""
+    return {"workload": "config4: KV append + GQA decode attention, 28 layers, 256 streams/GPU, "
+                        "ctx log-uniform [64,4096], 16-token pages, permuted page table",
+            "streams_per_gpu": STREAMS_PER_GPU, "mean_ctx": round(mean_ctx, 1),
+            "kv_cache": f"{kv_dtype} paged", "parallelism": f"streams sharded x{world}, no collectives",
+            "l2": "inputs larger than L2 (per-layer KV read ~1 GB >> 126 MB)"}
+
+
+def cpu_kv_sample(lens: np.ndarray, n_streams: int, steps: int, threads: int, warmup: int = 1):
     """Time the reference arithmetic (oracle port, bit-exact with the reference's
-    scalar path) on the first n_streams streams of this GPU's workload."""
+    scalar path) on the first n_streams streams of this GPU's workload, after
+    `warmup` untimed steps."""
     from oracle import oracle as checker
 
     sel = lens[:n_streams]
     rng = np.random.default_rng(7)
     # Cache contents: a random block tiled over the context (values do not change
     # the arithmetic's cost; filling GBs with fresh random numbers would dominate).
-    block = rng.standard_normal((2, CTX_HI + steps + 2, HKV * D), dtype=np.float32)
+    appends = warmup + steps                      # every step, warm-up included, appends one token per stream
+    block = rng.standard_normal((2, CTX_HI + appends + 2, HKV * D), dtype=np.float32)
     kcs, vcs = [], []
     for L in sel:
-        cap = int(L) + steps + 2
+        cap = int(L) + appends + 2
         k = np.empty((N_LAYERS, cap, HKV * D), np.float32)
         v = np.empty((N_LAYERS, cap, HKV * D), np.float32)
         k[:] = block[0, :cap]
@@ -169,7 +180,8 @@ def cpu_kv_sample(lens: np.ndarray, n_streams: int, steps: int, threads: int):
     qn, kn = qk_norm_weights()
     cur = sel.astype(np.int32).copy()
     qkv = rng.standard_normal((N_LAYERS, len(sel), QKV), dtype=np.float32)
-    checker.kv_step_batch(qkv, qn, kn, kcs, vcs, cur, threads=threads)   # warm-up (page-in)
+    for _ in range(warmup):   # untimed (the first pages the cache in)
+        checker.kv_step_batch(qkv, qn, kn, kcs, vcs, cur, threads=threads)
     t0 = time.perf_counter()
     for _ in range(steps):
         checker.kv_step_batch(qkv, qn, kn, kcs, vcs, cur, threads=threads)
@@ -186,17 +198,18 @@ def run_reference(args) -> int:
     threads = os.cpu_count() or 1
     lens = stream_lengths(0)
     n = min(STREAMS_PER_GPU, 16)
-    value, dt = cpu_kv_sample(lens, n, max(args.steps, 1), threads)
+    value, dt = cpu_kv_sample(lens, n, max(args.steps, 1), threads, warmup=max(args.warmup, 1))
     per_step_ms = dt / max(args.steps, 1) * 1e3
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step_ms, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config4 KV append+GQA decode attention step, 28 layers, log-uniform ctx [64,4096]",
-                   "streams_sampled": int(n), "cache": "f32 contiguous (reference layout)"},
+        "config": config4(args.kv_dtype, args.gpus, float(lens.mean())),
         "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"{n} streams x {args.steps} steps of the GPU-0 workload (oracle/qkv_oracle.c, "
-                                   f"bit-exact with the reference scalar path), OpenMP over streams"},
+                         "sample": f"{n} of the {STREAMS_PER_GPU} streams of GPU 0 x {args.steps} steps "
+                                   f"(after {max(args.warmup, 1)} untimed), in the reference's layout and arithmetic "
+                                   f"(f32 contiguous cache; oracle/qkv_oracle.c, bit-exact with the reference scalar "
+                                   f"path), OpenMP over streams"},
         "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -318,11 +331,7 @@ def run_ours(args) -> int:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.kv_dtype,
             "data": "synthetic",
-            "config": {"workload": "config4: KV append + GQA decode attention, 28 layers, 256 streams/GPU, "
-                                   "ctx log-uniform [64,4096], 16-token pages, permuted page table",
-                       "streams_per_gpu": STREAMS_PER_GPU, "mean_ctx": round(mean_ctx, 1),
-                       "kv_cache": f"{args.kv_dtype} paged", "parallelism": f"streams sharded x{world}, no collectives",
-                       "l2": "inputs larger than L2 (per-layer KV read ~1 GB >> 126 MB)"},
+            "config": config4(args.kv_dtype, world, mean_ctx),
             "kv_read_gbs_step": round(kv_bytes_per_launch * N_LAYERS / (ms_max / args.steps / 1e3) / 1e9, 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved_gbs / pk["hbm_gbs"], 4), "frac_of_8tbs": round(achieved_gbs / 8000, 4),
