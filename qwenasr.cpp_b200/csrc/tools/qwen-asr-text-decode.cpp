@@ -7,6 +7,8 @@
 //   qwen-asr-text-decode MODEL.gguf INPUT.f32 [--generate N | --prefill | --layer L]
 //                        [--out PATH] [--device auto|gpu|cpu] [--stop-ids a,b,..] [--no-stop]
 //                        [--kv-dtype f32|bf16|fp8] [--weights f32|bf16] [--page-size 16] [--gpu N]
+//                        (the reference tool's --threads, --backend, --audio-backend, --kv-cache,
+//                         --language and --system are accepted; see main)
 // INPUT.f32 = raw float32 [tokens][hidden] (audio rows already spliced in).
 // The B200 options pick the cache element type (f32 keeps the reference's
 // numerics), the device weight type, and the GPU; the paged cache has
@@ -200,6 +202,21 @@ int main(int argc, char **argv) {
             if (!end || *end || v < 0 || v > 255) { std::cerr << "--gpu requires a device ordinal 0..255\n"; return 2; }
             gpu = std::to_string(v);
         } else if (a == "--threads") threads = need("a positive integer");   // accepted and echoed; the GPU path has no host threads to size
+        // The reference tool's other flags, accepted so its scripts run unchanged:
+        // the text backend is always this library's, generation always uses the
+        // KV cache, and the prompt options shape a decoder input that arrives
+        // ready-made in INPUT.f32.
+        else if (a == "--backend") {
+            const std::string v = need("scalar, ggml, or sched");
+            if (v != "scalar" && v != "ggml" && v != "sched") { std::cerr << "--backend requires scalar, ggml, or sched\n"; return 2; }
+        } else if (a == "--audio-backend") {
+            const std::string v = need("ggml or sched");
+            if (v != "ggml" && v != "sched") { std::cerr << "--audio-backend requires ggml or sched\n"; return 2; }
+        } else if (a == "--kv-cache") {
+        } else if (a == "--language" || a == "--system") {
+            need("a value");
+            std::cerr << "note: " << a << " is ignored: INPUT.f32 already holds the assembled prompt rows\n";
+        }
         else if (model_path.empty()) model_path = a;
         else if (input_path.empty()) input_path = a;
         else { std::cerr << "too many positional arguments\n"; return 2; }

@@ -39,6 +39,20 @@ def test_cli_usage_and_cpu_device_rejected(case):
     assert rc == 2
 
 
+def test_cli_accepts_reference_flags(case):
+    """The reference tool's flags parse (the run then stops at the CPU-device
+    check, after parsing); bad backend values exit 2 with its messages."""
+    path, inp, g, d = case
+    rc, kv, err = run([path, inp, "--generate", "2", "--threads", "8", "--backend", "sched", "--audio-backend", "ggml",
+                       "--kv-cache", "--language", "English", "--system", "x", "--device", "cpu"])
+    assert rc == 1 and "GPU only" in err, err
+    assert "--language is ignored" in err and "--system is ignored" in err
+    rc, kv, err = run([path, inp, "--backend", "gpu"])
+    assert rc == 2 and "--backend requires scalar, ggml, or sched" in err
+    rc, kv, err = run([path, inp, "--audio-backend", "x"])
+    assert rc == 2 and "--audio-backend requires ggml or sched" in err
+
+
 @pytest.mark.parametrize("flags,msg", [(["--kv-dtype", "int8"], "--kv-dtype"), (["--weights", "fp8"], "--weights"),
                                        (["--page-size", "32"], "16-token pages"), (["--gpu", "x"], "--gpu")])
 def test_cli_rejects_bad_b200_options(case, flags, msg):
