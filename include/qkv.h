@@ -91,7 +91,9 @@ int qkv_read_gguf_config(const char *gguf_path, qkv_model_config *cfg, char *err
  * (text-decoder.h:85-116, text-decoder.cpp:1476-1639).  cfg may be NULL, in
  * which case it is read from the file.  Tensors must be F32, F16 or BF16 with
  * the reference's names and shapes (text-decoder.cpp:191-228, 523-537).  The
- * file is not needed after the call returns. */
+ * file is not needed after the call returns.  QKV_ERR_HOST_MEMORY when the
+ * host tables a runtime config asks for do not fit in host memory (as for
+ * qkv_create_kv_only). */
 int qkv_create(const char *gguf_path, const qkv_model_config *cfg, const qkv_runtime_config *rt,
                qkv_handle **out, char *err, size_t err_len);
 
@@ -312,8 +314,11 @@ int qkv_gguf_tensor(const char *gguf_path, const char *name, int64_t *ne_out, in
  * reference's message when incomplete).  qkv_tokenizer_decode writes the bytes
  * of ids[0..n) (out-of-range ids skipped; the special tokens too when
  * skip_special) to out, *len = their count; QKV_ERR_CAPACITY when they do not
- * fit in cap (*len still tells how many).  A token whose last UTF-8 sequence
- * is cut short is read up to its end (the reference reads past it). */
+ * fit in cap (*len still tells how many).  A malformed token whose last UTF-8
+ * sequence is cut short yields that sequence followed by zero bytes, as the
+ * reference's read runs on into the token's terminator.  Every tokenizer
+ * entry returns QKV_ERR_HOST_MEMORY when its tables or output do not fit in
+ * host memory. */
 int qkv_tokenizer_open(const char *gguf_path, qkv_tokenizer **out, char *err, size_t err_len);
 int qkv_tokenizer_decode(const qkv_tokenizer *t, const int32_t *ids, int32_t n, int32_t skip_special, char *out,
                          size_t cap, size_t *len);
@@ -323,7 +328,10 @@ int qkv_tokenizer_decode(const qkv_tokenizer *t, const int32_t *ids, int32_t n, 
  * still tells how many).  qkv_asr_prompt_ids encodes the ASR prompt of
  * qwenasr_build_asr_prompt (:529-549): system text, audio_tokens audio
  * placeholders, and the language line when language is non-empty; its ids go
- * to qkv_prefill_ids together with the audio rows. */
+ * to qkv_prefill_ids together with the audio rows.  As in the reference, a
+ * UTF-8 sequence cut off at the end of a segment (the text's end, or just
+ * before a special token) is read to its announced length: the missing
+ * bytes encode as zero bytes. */
 int qkv_tokenizer_encode(const qkv_tokenizer *t, const char *text, size_t text_len, int32_t add_eos, int32_t *ids,
                          size_t cap, size_t *n);
 int qkv_asr_prompt_ids(const qkv_tokenizer *t, int32_t audio_tokens, const char *system_text, const char *language,
