@@ -15,7 +15,9 @@
 // space-or-tab run of one followed by letters; a letter run; one digit; a
 // newline run; a space run; a run of anything else); byte-map each chunk and
 // merge the adjacent pair of lowest rank until none is in the table; look the
-// pieces up (pieces not in the vocabulary are dropped).
+// pieces up (pieces not in the vocabulary are dropped).  A UTF-8 sequence cut
+// off at a segment's end is read to its announced length, into zero bytes,
+// as the reference reads it (code_point_padded).
 #include <algorithm>
 #include <cctype>
 #include <climits>
