@@ -19,7 +19,8 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "_build" / "libqkv_oracle.so"
 REF_SO = HERE / "_ref" / "libqwenasr_ref.so"
-REF_SRC = Path(os.environ.get("QWENASR_REF_SRC", "/root/reference/src"))
+# The reference checkout's src/ beside this repository unless QWENASR_REF_SRC names another.
+REF_SRC = Path(os.environ.get("QWENASR_REF_SRC", str(HERE.parent.parent / "reference" / "src")))
 
 _F = C.POINTER(C.c_float)
 _I = C.POINTER(C.c_int32)

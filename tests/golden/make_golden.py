@@ -77,7 +77,8 @@ def torch_reference(ref_root: Path, cfg: dict, tensors: dict, x: np.ndarray, n_n
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref-root", type=Path, default=Path("/root/reference"))
+    ap.add_argument("--ref-root", type=Path, default=HERE.parents[2] / "reference",
+                    help="reference checkout (default: beside this repository)")
     ap.add_argument("--out", type=Path, default=HERE)
     a = ap.parse_args()
     synth = ge.load_synth()
