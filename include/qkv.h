@@ -269,6 +269,17 @@ int qkv_gather(qkv_handle *h, int32_t layer, int32_t stream_id, void *k_host, vo
 int qkv_stream_pages(const qkv_handle *h, int32_t stream_id, int32_t *pages_out, int32_t cap,
                      int32_t *n);
 
+/* Test of the failure path of the kernels' bounded waits (the reference has
+ * no device code; its counterpart is the status checking of
+ * text-decoder.cpp:1740-1746).  Launches, on the handle's stream, one CTA that
+ * runs the kernels' own bounded waits (the decode-attention stage and
+ * hand-over waits, the mbarrier wait of the GEMM and prefill attention) on
+ * events nothing completes, each giving up after limit_cycles SM clock cycles
+ * (1 .. 4e9, the kernels' own limit) and recording a "bounded wait ran out"
+ * device error.  Returns QKV_OK once launched; the next qkv_sync reports
+ * QKV_ERR_DEVICE and clears the error, and the handle stays usable. */
+int qkv_debug_wait_timeout(qkv_handle *h, int64_t limit_cycles);
+
 /* Synchronise the device and surface any device error. */
 int qkv_sync(qkv_handle *h);
 
@@ -292,9 +303,13 @@ int qkv_last_launches(const qkv_handle *h, int64_t *kernels);
  * device address and prepares the kernel; make that first call before any
  * stream capture.  All calls share the one array, which keeps the last call's
  * contents, so calls that overlap on the GPU (two streams, two host threads)
- * race.  The call is asynchronous on `stream` (NULL = legacy default stream);
- * rows that fail the kernel's bounds checks are skipped, not reported.  err
- * (nullable) receives a message for a non-zero status. */
+ * race.  The call is asynchronous on `stream` (NULL = legacy default stream)
+ * and its status covers the argument checks and the launch only: device-side
+ * errors are not reported.  A row that fails the kernel's bounds checks (a
+ * slot, length or page id out of range), and any row left when one of the
+ * kernel's bounded waits runs out (~2 s), keeps whatever its output held
+ * before the call; fill the output with NaN first where that must be seen.
+ * err (nullable) receives a message for a non-zero status. */
 int qkv_kv_attend_noalloc(const void *pool_layer, int32_t kv_dtype, const float *scales_layer,
                           const int32_t *page_table, int32_t maxp, int32_t max_streams, int32_t n_pages,
                           int32_t n, const int32_t *slots_dev, const int32_t *lens_dev, const float *q_dev,

@@ -80,6 +80,7 @@ SIGNATURES = {
     "qkv_gather": (C.c_int, [_P, C.c_int32, C.c_int32, _P, _P, _F32P]),
     "qkv_stream_pages": (C.c_int, [_P, C.c_int32, _I32P, C.c_int32, _I32P]),
     "qkv_sync": (C.c_int, [_P]),
+    "qkv_debug_wait_timeout": (C.c_int, [_P, C.c_int64]),
     "qkv_last_launches": (C.c_int, [_P, _I64P]),
     "qkv_kv_attend_noalloc": (C.c_int, [_P, C.c_int32, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, _P,
                                         _P, _P, _P, C.c_char_p, C.c_size_t]),

@@ -141,26 +141,55 @@ __device__ __forceinline__ int64_t cta_of_page(int64_t pg, int64_t total, int64_
 }
 
 // Bounded wait that also gives up when another role raised the abort flag.
-__device__ __forceinline__ bool stage_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+__device__ __forceinline__ bool stage_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                           long long limit = kWaitLimitCycles) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
         if (*abort_flag) return false;
-        if (clock64() - t0 > kWaitLimitCycles) return false;
+        if (clock64() - t0 > limit) return false;
     }
     return true;
 }
 
 // Bounded wait until *flag == want (a shared-memory hand-over between two
 // warps of the CTA); false on timeout or when another warp set the abort flag.
-__device__ __forceinline__ bool flag_wait(volatile int *flag, int want, volatile int *abort_flag) {
+__device__ __forceinline__ bool flag_wait(volatile int *flag, int want, volatile int *abort_flag,
+                                          long long limit = kWaitLimitCycles) {
     if (*flag == want) return true;
     const long long t0 = clock64();
     while (*flag != want) {
         if (*abort_flag) return false;
-        if (clock64() - t0 > kWaitLimitCycles) return false;
+        if (clock64() - t0 > limit) return false;
     }
     return true;
+}
+
+// Wait probe: runs the bounded waits the kernels use against events that
+// never come, with a caller-given short limit, so a test can see a wait run
+// out and be reported through the device error word while the context stays
+// usable.  Warp 0 waits on an mbarrier that expects one arrival nobody makes
+// (K2's stage wait, then the plain mbarrier wait of the GEMM and K3); warp 1
+// waits on a shared flag nobody sets (K2's hand-over wait).  Nothing is in
+// flight when a wait gives up, so the CTA simply returns.
+__global__ void __launch_bounds__(64) wait_probe_kernel(DevError *err, long long limit) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int flag, never;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        flag = 0;
+        never = 0;
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (lane != 0) return;
+    if (warp == 0) {
+        if (!stage_wait(&bar, 0u, &never, limit)) report_error(err, kErrWaitTimeout, kWhereProbe, 0, 0);
+        if (!mbar_wait(&bar, 0u, limit)) report_error(err, kErrWaitTimeout, kWhereProbe, 1, 0);
+    } else {
+        if (!flag_wait(&flag, 1, &never, limit)) report_error(err, kErrWaitTimeout, kWhereProbe, 2, 0);
+    }
 }
 
 template <typename TC, typename TOut>
@@ -746,6 +775,11 @@ cudaError_t launch_decode_attn(const AttendParams &p, int kv_dtype, bool out_bf1
     }
 }
 
+cudaError_t launch_wait_probe(DevError *err, long long limit_cycles, cudaStream_t st) {
+    wait_probe_kernel<<<1, 64, 0, st>>>(err, limit_cycles);
+    return cudaGetLastError();
+}
+
 }  // namespace qkv
 
 // ---------------------------------------------------------------------------
@@ -855,9 +889,12 @@ extern "C" int qkv_kv_attend_noalloc(const void *pool_layer, int32_t kv_dtype, c
     p.counters = reinterpret_cast<int *>(base + kNoAllocOBytes + kNoAllocMLBytes);
     p.err = reinterpret_cast<DevError *>(base + kNoAllocOBytes + kNoAllocMLBytes + kNoAllocCntBytes);
     p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(kHeadDim)));
-    // The merge counters must start at zero; a call that stopped early (bounded
-    // wait ran out) could have left some set.
-    cudaError_t e = cudaMemsetAsync(p.counters, 0, static_cast<size_t>(n) * kHkv * sizeof(int), st);
+    // The merge counters must start at zero (a call that stopped early, when a
+    // bounded wait ran out, could have left some set), and the error word
+    // directly after them is cleared too, so no earlier call's error stays
+    // latched in the shared array.  This entry never reads the word back: a
+    // read would need a synchronisation the caller has not asked for.
+    cudaError_t e = cudaMemsetAsync(p.counters, 0, kNoAllocCntBytes + sizeof(DevError), st);
     const int grid = g_noalloc_sms[dev] < kNoAllocMaxGrid ? g_noalloc_sms[dev] : kNoAllocMaxGrid;
     if (e == cudaSuccess) e = launch_decode_attn(p, kv_dtype, false, grid, st);
     if (e != cudaSuccess) {

@@ -31,7 +31,7 @@ struct DevError {
 };
 enum DevErrCode { kErrPageIndex = 1, kErrWaitTimeout = 2, kErrPosition = 3, kErrRowBounds = 4 };
 enum DevErrWhere { kWhereAppend = 1, kWhereAttend = 2, kWherePrefillAttn = 3, kWhereGather = 4,
-                   kWhereEmbed = 5, kWhereGemm = 6 };
+                   kWhereEmbed = 5, kWhereGemm = 6, kWhereProbe = 7 };
 
 __device__ __forceinline__ void report_error(DevError *e, int code, int where, int a, int b) {
     if (e && atomicCAS(&e->code, 0, code) == 0) {

@@ -118,6 +118,9 @@ cudaError_t launch_fp8_page_scale(const AppendParams &p, cudaStream_t st);
 cudaError_t prepare_decode_attn();
 size_t attn_smem_bytes(int kv_dtype);
 cudaError_t launch_decode_attn(const AttendParams &p, int kv_dtype, bool out_bf16, int grid, cudaStream_t st);
+// Test of the bounded waits: one CTA whose waits (K2's stage and hand-over
+// waits, the plain mbarrier wait) run out after limit_cycles and report it.
+cudaError_t launch_wait_probe(DevError *err, long long limit_cycles, cudaStream_t st);
 cudaError_t launch_prefill_attn(const PrefillAttnParams &p, int kv_dtype, bool out_bf16, cudaStream_t st);
 // K3 (bf16 or e4m3 cache): items = (first row, query count <= 64, kv head, 0), one CTA each.
 cudaError_t prepare_prefill_tc();

@@ -1694,6 +1694,14 @@ int qkv_stream_pages(const qkv_handle *h, int32_t stream_id, int32_t *pages_out,
     return QKV_OK;
 }
 
+int qkv_debug_wait_timeout(qkv_handle *h, int64_t limit_cycles) {
+    if (!h || limit_cycles < 1 || limit_cycles > qkv::kWaitLimitCycles) return QKV_ERR_INVALID_ARG;
+    CK(cudaSetDevice(h->device));
+    CK(launch_wait_probe(h->d_err, static_cast<long long>(limit_cycles), h->stream));
+    ++h->launches;
+    return QKV_OK;
+}
+
 int qkv_sync(qkv_handle *h) {
     if (!h) return QKV_ERR_INVALID_ARG;
     CK(cudaSetDevice(h->device));

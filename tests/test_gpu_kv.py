@@ -284,6 +284,41 @@ def test_device_error_on_bad_page_table_row(pkg):
         dec.sync()   # the error word was cleared
 
 
+def test_bounded_wait_runs_out_and_is_reported(pkg, checker):
+    """The kernels' bounded waits (K2's mbarrier stage wait and its hand-over
+    flag wait, the plain mbarrier wait of the GEMM and K3), run by a probe on
+    events nothing completes with a short limit (1e5 cycles, ~50 us), give up,
+    record "bounded wait ran out" and return: the next sync reports
+    QKV_ERR_DEVICE, clears it, and a normal decode attention on the same
+    handle then runs and matches the oracle."""
+    dec, qn, kn = kv_handle(pkg, pkg.F32, n_layers=1, max_streams=2, max_context=64)
+    rng = np.random.default_rng(5)
+    with dec:
+        s = dec.open()
+        L = 40
+        dec.extend(s, L)
+        rows = rng.standard_normal((L, QKV), dtype=np.float32)
+        fill_stream(dec, 0, s, rows)
+        dec.sync()
+        assert pkg.lib.qkv_debug_wait_timeout(dec.h, 100_000) == 0
+        with pytest.raises(pkg.QkvError) as ei:
+            dec.sync()
+        assert ei.value.code == 5 and "bounded wait ran out" in str(ei.value)
+        dec.sync()   # reported once, then cleared
+        assert pkg.lib.qkv_debug_wait_timeout(dec.h, 0) != 0   # limits outside 1 .. 4e9 are refused
+        q = rng.standard_normal((1, HQ * D), dtype=np.float32)
+        d_q = torch.tensor(q, device="cuda")
+        out = torch.zeros_like(d_q)
+        d_slots, d_lens = dev_i32([s]), dev_i32([L])
+        dec.kv_attend(0, 1, d_slots.data_ptr(), d_lens.data_ptr(), d_q.data_ptr(), out.data_ptr())
+        torch.cuda.synchronize()
+        dec.sync()
+        k, v = dec.gather(0, s, pkg.F32)
+        want = checker.attend(q[0], k, v)
+        got = out.cpu().numpy()[0]
+        assert np.max(np.abs(got - want)) / np.max(np.abs(want)) < 2e-5
+
+
 def e4m3_to_f32(b: np.ndarray) -> np.ndarray:
     b = b.astype(np.int32)
     sign = np.where(b & 0x80, -1.0, 1.0)

@@ -5,9 +5,11 @@ vocab 151936) on seeded bf16-rounded N(0, 0.02) weights and config-1 prompts
 The CPU oracle (bit-exact with the reference's scalar path) runs the
 reference's cached greedy loop in spawned worker processes; the device path is
 teacher-forced with the oracle's ids so every step compares logits on an
-identical prefix.  Bars: f32 weights + f32 cache -> logits within 1e-3
-relative and identical greedy ids; bf16 weights + bf16 cache -> >= 99% greedy
-agreement with the max logit deviation printed."""
+identical prefix.  8 prompts x 64 steps = 512 compared positions.  Bars: f32
+weights + f32 cache -> logits within 1e-3 relative and identical greedy ids;
+bf16 weights + bf16 cache -> >= 99% greedy agreement with the max logit
+deviation printed, and for every flipped position the oracle's top-2 margin
+(relative to the row's max |logit|) next to the device's deviation there."""
 import multiprocessing as mp
 from pathlib import Path
 
@@ -19,8 +21,8 @@ from conftest import rel_err
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
-N_PROMPTS = 2
-N_STEPS = 24
+N_PROMPTS = 8
+N_STEPS = 64
 
 
 def _oracle_job(args):
@@ -51,16 +53,24 @@ def _teacher_forced(pkg, path, refs, w, kv):
     rt = pkg.runtime_config(device=0, weight_dtype=w, kv_dtype=kv, max_streams=N_PROMPTS, max_context=256,
                             max_batch_tokens=N_PROMPTS * 160)
     worst, agree, total = 0.0, 0, 0
+    flips = []
     with pkg.Decoder.from_gguf(path, rt) as dec:
         streams = [dec.open() for _ in refs]
         ids, logits = dec.prefill(streams, [r[0] for r in refs], want_logits=True)
         for step in range(N_STEPS):
             for i, (_, ref_ids, ref_logits) in enumerate(refs):
-                worst = max(worst, rel_err(logits[i], ref_logits[step]))
+                dev = rel_err(logits[i], ref_logits[step])
+                worst = max(worst, dev)
                 agree += int(ids[i] == ref_ids[step])
                 total += 1
+                if ids[i] != ref_ids[step]:
+                    r = ref_logits[step]
+                    top2 = np.sort(r)[-2:]
+                    flips.append((i, step, float((top2[1] - top2[0]) / np.max(np.abs(r))), dev))
             if step + 1 < N_STEPS:
                 ids, logits = dec.decode_step(streams, in_ids=[int(r[1][step]) for r in refs], want_logits=True)
+    for i, step, margin, dev in flips:
+        print(f"  flip: prompt {i} step {step}: oracle top-2 margin {margin:.2e}, deviation there {dev:.2e}")
     return agree / total, worst
 
 
@@ -86,4 +96,4 @@ def test_fp8_full_size_deviation(pkg, scale_case):
     cfg, path, refs = scale_case
     agree, worst = _teacher_forced(pkg, path, refs, pkg.BF16, pkg.FP8)
     print(f"0.6B bf16 weights + fp8 cache: greedy agreement {agree:.4f}, max relative logit deviation {worst:.3e}")
-    assert agree >= 0.9
+    assert agree >= 0.95

@@ -23,7 +23,10 @@ def _i32(a):
     return torch.tensor(np.asarray(a, np.int32), device="cuda")
 
 
-def test_noalloc_attention_matches_handle_path(pkg):
+@pytest.mark.parametrize("kv", ["bf16", "f32", "fp8"])
+def test_noalloc_attention_matches_handle_path(pkg, kv):
+    kv_dtype = {"bf16": pkg.BF16, "f32": pkg.F32, "fp8": pkg.FP8}[kv]
+    elem = {"bf16": np.uint16, "f32": np.float32, "fp8": np.uint8}[kv]
     rng = np.random.default_rng(21)
     n_layers = 1
     qn = (1.0 + 0.1 * rng.standard_normal((n_layers, D))).astype(np.float32)
@@ -31,7 +34,7 @@ def test_noalloc_attention_matches_handle_path(pkg):
     cfg = dict(n_layers=n_layers, hidden=256, n_heads=HQ, n_kv_heads=HKV, head_dim=D, intermediate=512,
                vocab=1000, rope_theta=1.0e6, rms_norm_eps=1.0e-6)
     lens = [37, 300, 1200, 16, 1, 2049]
-    rt = pkg.runtime_config(device=0, kv_dtype=pkg.BF16, max_streams=len(lens), max_context=2100,
+    rt = pkg.runtime_config(device=0, kv_dtype=kv_dtype, max_streams=len(lens), max_context=2100,
                             page_order_seed=4)
     with pkg.Decoder.kv_only(cfg, rt, qn, kn) as dec:
         streams = []
@@ -51,17 +54,19 @@ def test_noalloc_attention_matches_handle_path(pkg):
         dec.kv_attend(0, len(lens), d_slots.data_ptr(), d_lens.data_ptr(), q.data_ptr(), want.data_ptr())
         torch.cuda.synchronize()
         dec.sync()
-        gathered = [dec.gather(0, s, pkg.BF16) for s in streams]
+        gathered = [dec.gather(0, s, kv_dtype) for s in streams]
 
     # The caller's own pool: same pages, reversed-permuted page ids.
     need = [(L + PT - 1) // PT for L in lens]
     n_pages = sum(need) + 3
     maxp = max(need)
     order = rng.permutation(n_pages)
-    pool = np.zeros((n_pages, 2, HKV, PT, D), np.uint16)
+    pool = np.zeros((n_pages, 2, HKV, PT, D), elem)
+    scales = np.ones((n_pages, 2, HKV), np.float32)
     table = np.full((len(lens), maxp), -1, np.int32)
     nxt = 0
-    for i, (L, (k, v)) in enumerate(zip(lens, gathered)):
+    for i, (L, got) in enumerate(zip(lens, gathered)):
+        k, v = got[0], got[1]
         for j in range(need[i]):
             page = int(order[nxt])
             nxt += 1
@@ -69,21 +74,27 @@ def test_noalloc_attention_matches_handle_path(pkg):
             t0, t1 = j * PT, min(L, (j + 1) * PT)
             pool[page, 0, :, : t1 - t0, :] = k[t0:t1].reshape(t1 - t0, HKV, D).transpose(1, 0, 2)
             pool[page, 1, :, : t1 - t0, :] = v[t0:t1].reshape(t1 - t0, HKV, D).transpose(1, 0, 2)
-    d_pool = torch.tensor(pool.view(np.int16), device="cuda")
+            if kv == "fp8":
+                scales[page] = got[2][j]
+    view = {"bf16": np.int16, "f32": np.float32, "fp8": np.uint8}[kv]
+    d_pool = torch.tensor(pool.view(view), device="cuda")
+    d_scales = torch.tensor(scales, device="cuda") if kv == "fp8" else None
     d_table = torch.tensor(table, device="cuda")
     d_rows = _i32(np.arange(len(lens)))
     err = C.create_string_buffer(256)
     outs = []
     for _ in range(2):   # two calls in a row share (and reuse) the fixed scratch
         out = torch.full_like(q, float("nan"))
-        rc = pkg.lib.qkv_kv_attend_noalloc(d_pool.data_ptr(), pkg.BF16, None, d_table.data_ptr(), maxp, len(lens),
+        rc = pkg.lib.qkv_kv_attend_noalloc(d_pool.data_ptr(), kv_dtype,
+                                           d_scales.data_ptr() if d_scales is not None else None,
+                                           d_table.data_ptr(), maxp, len(lens),
                                            n_pages, len(lens), d_rows.data_ptr(), d_lens.data_ptr(), q.data_ptr(),
                                            out.data_ptr(), None, err, 256)
         assert rc == 0, err.value.decode()
         torch.cuda.synchronize()
         outs.append(out.cpu().numpy())
     ref = want.cpu().numpy()
-    for got in outs:
+    for got in outs:   # the same kernel on the same bytes: equal up to the split-row merge order
         rel = np.max(np.abs(got - ref)) / np.max(np.abs(ref))
         assert rel < 2e-5, rel
 
