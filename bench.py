@@ -54,8 +54,45 @@ def peaks() -> dict:
 
 
 def stream_lengths(rank: int) -> np.ndarray:
+    """The seeded contexts of GPU `rank`'s 256 streams (log-uniform [64, 4096])."""
     rng = np.random.default_rng(WORKLOAD_SEED * 1_000_003 + rank * 65_536)
     return np.exp(rng.uniform(np.log(CTX_LO), np.log(CTX_HI), size=STREAMS_PER_GPU)).astype(np.int64).clip(CTX_LO, CTX_HI)
+
+
+def box_lengths(rank: int, world: int) -> np.ndarray:
+    """Whole-box workload: one seeded set of world x 256 streams (the union of
+    every GPU's seeded contexts), partitioned over the ranks by greedy LPT on
+    each stream's per-step KV read (its context length), 256 streams per rank
+    (shard.lpt_partition).  world = 1 gives stream_lengths(0) unchanged."""
+    if world == 1:
+        return stream_lengths(0)
+    import __graft_entry__ as ge
+    ge.load_package()
+    from qwenasr_cpp_b200 import shard
+    pool = np.concatenate([stream_lengths(g) for g in range(world)])
+    parts = shard.lpt_partition(pool, world, cap=STREAMS_PER_GPU)
+    return pool[np.asarray(parts[rank], dtype=np.int64)]
+
+
+def bind_numa(gpu: int) -> str | None:
+    """Pin this process to the host cores of its GPU's NUMA node (before any
+    pinned host buffer is allocated, so those pages land on that node).
+    Best effort: returns the node, or None where the topology is not exposed."""
+    try:
+        import torch
+        pr = torch.cuda.get_device_properties(gpu)
+        bus = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        node = int(Path(f"/sys/bus/pci/devices/{bus}/numa_node").read_text().strip())
+        if node < 0:
+            return None
+        cpus = set()
+        for part in Path(f"/sys/devices/system/node/node{node}/cpulist").read_text().strip().split(","):
+            a, _, b = part.partition("-")
+            cpus.update(range(int(a), int(b or a) + 1))
+        os.sched_setaffinity(0, cpus)
+        return f"node{node}"
+    except Exception:
+        return None
 
 
 def qk_norm_weights(seed: int = 0):
@@ -152,7 +189,10 @@ def config4(kv_dtype: str, world: int, mean_ctx: float) -> dict:
     return {"workload": "config4: KV append + GQA decode attention, 28 layers, 256 streams/GPU, "
                         "ctx log-uniform [64,4096], 16-token pages, permuted page table",
             "streams_per_gpu": STREAMS_PER_GPU, "mean_ctx": round(mean_ctx, 1),
-            "kv_cache": f"{kv_dtype} paged", "parallelism": f"streams sharded x{world}, no collectives",
+            "kv_cache": f"{kv_dtype} paged",
+            "parallelism": (f"streams sharded x{world}, no collectives" if world == 1 else
+                            f"one seeded set of {world}x{STREAMS_PER_GPU} streams, LPT-partitioned on per-step KV "
+                            f"read ({STREAMS_PER_GPU} per GPU), no collectives"),
             "l2": "inputs larger than L2 (per-layer KV read ~1 GB >> 126 MB)"}
 
 
@@ -242,16 +282,17 @@ def run_ours(args) -> int:
     rank, local, world, dist = dist_setup(args.gpus)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    numa = bind_numa(local) if world > 1 else None
 
-    lens = stream_lengths(rank)
+    lens = box_lengths(rank, world)
     total_steps = args.warmup + args.steps + 2 + 8    # + kernel-timing pass + e2e pass
     max_ctx = int(lens.max()) + total_steps + 16
     pages = int(sum((int(L) + total_steps + 15) // 16 for L in lens)) + 64
     qn, kn = qk_norm_weights()
     cfg = dict(n_layers=N_LAYERS, hidden=1024, n_heads=HQ, n_kv_heads=HKV, head_dim=D, intermediate=3072,
                vocab=151936, rope_theta=1.0e6, rms_norm_eps=1.0e-6)
-    kvd = {"bf16": pkg.BF16, "fp8": pkg.FP8, "f32": pkg.F32}[args.kv_dtype]
-    elem = {"bf16": 2, "fp8": 1, "f32": 4}[args.kv_dtype]
+    kvd = {"bf16": pkg.BF16, "fp8": pkg.FP8, "e4i8": pkg.E4I8, "f32": pkg.F32}[args.kv_dtype]
+    elem = {"bf16": 2, "fp8": 1, "e4i8": 1, "f32": 4}[args.kv_dtype]
     rt = pkg.runtime_config(device=local, weight_dtype=pkg.F32, kv_dtype=kvd, max_streams=STREAMS_PER_GPU,
                             max_context=max_ctx, max_pages=pages, page_order_seed=WORKLOAD_SEED + rank)
     dec = pkg.Decoder.kv_only(cfg, rt, qn, kn)
@@ -315,6 +356,7 @@ def run_ours(args) -> int:
     if elem == 1:
         kv_bytes_per_launch += sum((dec.length(s) + 15) // 16 for s in streams) * 2 * HKV * 4   # FP8 scales
     achieved_gbs = kv_bytes_per_launch / (attn_ms / 1e3) / 1e9
+    probe = read_probe(pkg, dec, streams, elem, st, attn_ms)
 
     # e2e: the same step through the C ABI with pinned host buffers (copies in the timed region).
     e2e_steps = 4
@@ -325,8 +367,18 @@ def run_ours(args) -> int:
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
         dec.kv_step_host(streams, h_qkv.data_ptr(), h_out.data_ptr())
-    e2e_s = max_over_ranks(dist, time.perf_counter() - t0)
+    box_mean = sum_over_ranks(dist, float(lens.sum())) / (world * STREAMS_PER_GPU)
+    e2e_rank_s = time.perf_counter() - t0
+    e2e_s = max_over_ranks(dist, e2e_rank_s)
     e2e_value = sum_over_ranks(dist, float(STREAMS_PER_GPU * e2e_steps)) / e2e_s
+    per_rank = [STREAMS_PER_GPU * e2e_steps / e2e_rank_s]
+    k2_frac_ranks = [achieved_gbs / peaks()["hbm_gbs"]]
+    if dist is not None:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, (per_rank[0], k2_frac_ranks[0], numa))
+        per_rank = [g[0] for g in gathered]
+        k2_frac_ranks = [g[1] for g in gathered]
+        numa_ranks = [g[2] for g in gathered]
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -341,7 +393,7 @@ def run_ours(args) -> int:
 
     pk = peaks()
     if rank == 0:
-        mean_ctx = float(lens.mean())   # the configured contexts, before any step (as the reference arm)
+        mean_ctx = box_mean   # the configured contexts, before any step (as the reference arm)
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
@@ -354,16 +406,107 @@ def run_ours(args) -> int:
                          "traffic": {"bf16": K2_NCU_TRAFFIC_BYTES, "fp8": K2_FP8_NCU_TRAFFIC_BYTES}.get(args.kv_dtype),
                          "kernel": "decode_attn_kernel (K2)",
                          "launch_ms": round(attn_ms, 4), "bytes_per_launch": kv_bytes_per_launch,
-                         "peak_source": pk["source"]},
+                         "peak_source": pk["source"], "read_probe": probe,
+                         "frac_per_rank": [round(v, 4) for v in k2_frac_ranks]},
             "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s",
-                    "h2d_bytes_per_step": int(qkv.numel() * 4), "d2h_bytes_per_step": int(out.numel() * 4)},
+                    "h2d_bytes_per_step": int(qkv.numel() * 4), "d2h_bytes_per_step": int(out.numel() * 4),
+                    "per_rank": [round(v, 1) for v in per_rank]},
             "gpu_launches": int(launches),
             "clocks": sampler.summary(),
         }
+        if world > 1:
+            line["numa_per_rank"] = numa_ranks
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
     dec.close()
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+def read_probe(pkg, dec, streams, elem: int, st, attn_ms: float | None, reps: int = 2) -> dict | None:
+    """The read ceiling of K2's access pattern on this workload: the same
+    pages of every stream (K2's order), the same persistent grid and page
+    split, one bulk copy per page into shared memory, nothing computed
+    (qkv_page_read_probe), one launch per layer, timed with CUDA events on
+    the launching stream.  k2_time_frac = probe time / K2 time over the same
+    pages (1.0 = K2 streams as fast as a pure read of its pages)."""
+    import torch
+    if elem > 2:
+        return None
+    plist = np.concatenate([dec.pages(s) for s in streams]).astype(np.int32)
+    d_pages = torch.tensor(plist, device=torch.device("cuda", torch.cuda.current_device()))
+    page_bytes = 2 * HKV * 16 * D * elem
+    sp = st.cuda_stream
+    for layer in range(N_LAYERS):   # warm (one pass)
+        rc = pkg.lib.qkv_page_read_probe(dec.h, layer, len(plist), d_pages.data_ptr(), sp)
+        if rc != 0:
+            raise RuntimeError(f"qkv_page_read_probe failed: {rc}")
+    torch.cuda.synchronize()
+    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b0.record(st)
+    for _ in range(reps):
+        for layer in range(N_LAYERS):
+            pkg.lib.qkv_page_read_probe(dec.h, layer, len(plist), d_pages.data_ptr(), sp)
+    b1.record(st)
+    torch.cuda.synchronize()
+    dec.sync()
+    ms = b0.elapsed_time(b1) / (reps * N_LAYERS)
+    gbs = len(plist) * page_bytes / (ms / 1e3) / 1e9
+    out = {"gbs": round(gbs, 1), "launch_ms": round(ms, 4), "pages": int(len(plist)), "page_bytes": page_bytes,
+           "frac_of_copy_peak": round(gbs / peaks()["hbm_gbs"], 4)}
+    if attn_ms:
+        out["k2_time_frac"] = round(ms / attn_ms, 4)
+    return out
+
+
+def run_readprobe(args) -> int:
+    """--workload readprobe: the read ceiling of K2's page stream on the
+    config-4 cache (same streams, contexts, page permutation and dtype as the
+    default line; nothing is appended).  value = page bytes read per second,
+    whole job (sum over ranks of bytes, max over ranks of time)."""
+    import torch
+
+    global N_LAYERS
+    N_LAYERS = args.layers
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    rank, local, world, dist = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    lens = stream_lengths(rank)
+    qn, kn = qk_norm_weights()
+    cfg = dict(n_layers=N_LAYERS, hidden=1024, n_heads=HQ, n_kv_heads=HKV, head_dim=D, intermediate=3072,
+               vocab=151936, rope_theta=1.0e6, rms_norm_eps=1.0e-6)
+    kvd = {"bf16": pkg.BF16, "fp8": pkg.FP8, "e4i8": pkg.E4I8}[args.kv_dtype]
+    elem = 2 if args.kv_dtype == "bf16" else 1
+    rt = pkg.runtime_config(device=local, weight_dtype=pkg.F32, kv_dtype=kvd, max_streams=STREAMS_PER_GPU,
+                            max_context=int(lens.max()) + 16, max_pages=int(sum((int(L) + 15) // 16 for L in lens)) + 64,
+                            page_order_seed=WORKLOAD_SEED + rank)
+    with pkg.Decoder.kv_only(cfg, rt, qn, kn) as dec:
+        streams = [dec.open() for _ in range(STREAMS_PER_GPU)]
+        for s, L in zip(streams, lens):
+            dec.extend(s, int(L))
+        dec.fill_random(WORKLOAD_SEED + rank)
+        st = torch.cuda.current_stream()
+        sampler = ClockSampler(local)
+        barrier(dist)
+        with sampler:
+            probe = read_probe(pkg, dec, streams, elem, st, None, reps=max(args.steps, 1))
+        barrier(dist)
+    ms = max_over_ranks(dist, probe["launch_ms"])
+    total = sum_over_ranks(dist, float(probe["pages"] * probe["page_bytes"]))
+    if rank == 0:
+        gbs = total / (ms / 1e3) / 1e9
+        print(json.dumps({
+            "metric": "KV page-stream read GB/s (read probe of the decode-attention access pattern)",
+            "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": 1,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": args.kv_dtype, "data": "synthetic", "config": config4(args.kv_dtype, world, float(lens.mean())),
+            "roofline": {"bound": "hbm", "achieved": round(gbs / world, 1), "peak": peaks()["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / world / peaks()["hbm_gbs"], 4), "traffic": None,
+                         "kernel": "page_read_probe_kernel", "peak_source": peaks()["source"]},
+            "clocks": sampler.summary()}), flush=True)
     if dist is not None:
         dist.destroy_process_group()
     return 0
@@ -541,7 +684,8 @@ def run_serve(args) -> int:
     lam = conc / ((out_lo + out_hi) / 2.0)
     max_ctx = 780 + text_tokens + out_hi + 8
     slots_cap = conc + 128
-    rt = pkg.runtime_config(device=local, weight_dtype=pkg.BF16, kv_dtype=pkg.FP8, max_streams=slots_cap,
+    serve_kv = {"e4i8": pkg.E4I8, "fp8": pkg.FP8}[args.serve_kv]
+    rt = pkg.runtime_config(device=local, weight_dtype=pkg.BF16, kv_dtype=serve_kv, max_streams=slots_cap,
                             max_context=max_ctx, max_pages=slots_cap * ((max_ctx + 15) // 16),
                             max_batch_tokens=32768, page_order_seed=1005 + rank)
     dec = pkg.Decoder.from_gguf(path, rt, cfg)
@@ -625,8 +769,8 @@ def run_serve(args) -> int:
     free_pages, total_pages = dec.pool_stats()
     dec.close()
 
-    # Deviation of the FP8 cache vs the bf16 cache: 8 config-5 prompts, the
-    # bf16-cache path's greedy ids teacher-force the FP8-cache path.
+    # Deviation of the 8-bit caches vs the bf16 cache: 8 config-5 prompts, the
+    # bf16-cache path's greedy ids teacher-force the 8-bit-cache paths.
     dev_line = None
     if rank == 0:
         drng = np.random.default_rng(4242)
@@ -637,7 +781,7 @@ def run_serve(args) -> int:
             prompts.append(x)
         n_steps = 32
         outs = {}
-        for kvd in (pkg.BF16, pkg.FP8):
+        for kvd in (pkg.BF16, pkg.E4I8, pkg.FP8):
             rt2 = pkg.runtime_config(device=local, weight_dtype=pkg.BF16, kv_dtype=kvd, max_streams=8,
                                      max_context=max_ctx, max_batch_tokens=8 * 800)
             with pkg.Decoder.from_gguf(path, rt2, cfg) as d2:
@@ -645,30 +789,35 @@ def run_serve(args) -> int:
                 ids, lg = d2.prefill(ss, prompts, want_logits=True)
                 steps_ids, steps_lg = [ids], [lg]
                 for t in range(n_steps - 1):
-                    feed = outs[pkg.BF16][0][t] if kvd == pkg.FP8 else steps_ids[-1]
+                    feed = outs[pkg.BF16][0][t] if kvd != pkg.BF16 else steps_ids[-1]
                     ids, lg = d2.decode_step(ss, in_ids=feed, want_logits=True)
                     steps_ids.append(ids)
                     steps_lg.append(lg)
                 outs[kvd] = (steps_ids, steps_lg)
-        agree = np.mean([np.mean(a == b) for a, b in zip(outs[pkg.BF16][0], outs[pkg.FP8][0])])
-        rel = max(float(np.max(np.abs(a - b)) / np.max(np.abs(b))) for a, b in zip(outs[pkg.FP8][1], outs[pkg.BF16][1]))
-        dev_line = {"streams": 8, "steps": n_steps, "greedy_agreement_vs_bf16": round(float(agree), 4),
-                    "max_rel_logit_dev_vs_bf16": float(f"{rel:.3e}")}
+        dev_line = {"streams": 8, "steps": n_steps}
+        for name, kvd in (("e4i8", pkg.E4I8), ("fp8", pkg.FP8)):
+            agree = np.mean([np.mean(a == b) for a, b in zip(outs[pkg.BF16][0], outs[kvd][0])])
+            rel = max(float(np.max(np.abs(a - b)) / np.max(np.abs(b))) for a, b in zip(outs[kvd][1], outs[pkg.BF16][1]))
+            dev_line[name] = {"greedy_agreement_vs_bf16": round(float(agree), 4),
+                              "max_rel_logit_dev_vs_bf16": float(f"{rel:.3e}")}
     if rank == 0:
         line = {
-            "metric": "serving decode tokens/s (1.7B, FP8 KV cache, continuous batching)",
+            "metric": "serving decode tokens/s (1.7B, 8-bit KV cache, continuous batching)",
             "value": round(total / dt_max, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dt_max / args.steps * 1e3, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 weights, fp8-e4m3 KV", "data": "synthetic",
-            "config": {"workload": "config5: Qwen3-ASR-1.7B, FP8 paged KV (per-page-per-head scales), Poisson arrivals, "
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 weights, " + ("e4m3 K + int8 V" if args.serve_kv == "e4i8" else "e4m3 K and V") + " KV",
+            "data": "synthetic",
+            "config": {"workload": "config5: Qwen3-ASR-1.7B, 8-bit paged KV (per-page-per-head scales), Poisson arrivals, "
                                    "audio 65-780 rows + 20 text tokens, outputs 32-512 tokens",
+                       "kv_cache": args.serve_kv,
                        "target_concurrency": conc, "mean_concurrency": round(float(np.mean(conc_seen)), 1),
                        "arrival_rate_per_step": round(lam, 3), "initial_fill_s": round(fill_s, 2),
                        "prefill_tokens_timed": int(prefill_tokens), "streams_closed": int(closed),
                        "pages_moved_by_compaction": int(moved), "free_pages_end": int(free_pages),
                        "pool_pages": int(total_pages), "gguf_write_s": round(gen_s, 1),
                        "phase_s": {k: round(v, 3) for k, v in phase.items()}},
-            "fp8_deviation": dev_line,
+            "deviation_vs_bf16_cache": dev_line,
             "clocks": sampler.summary()}
         print(json.dumps(line), flush=True)
     if dist is not None:
@@ -701,7 +850,7 @@ def run_prefill_attn(args) -> int:
     qn, kn = qk_norm_weights()
     cfg = dict(n_layers=N_LAYERS, hidden=1024, n_heads=HQ, n_kv_heads=HKV, head_dim=D, intermediate=3072,
                vocab=151936, rope_theta=1.0e6, rms_norm_eps=1.0e-6)
-    kvd = {"bf16": pkg.BF16, "fp8": pkg.FP8, "f32": pkg.F32}[args.kv_dtype]
+    kvd = {"bf16": pkg.BF16, "fp8": pkg.FP8, "e4i8": pkg.E4I8, "f32": pkg.F32}[args.kv_dtype]
     rt = pkg.runtime_config(device=local, weight_dtype=pkg.F32, kv_dtype=kvd, max_streams=n, max_context=P + 16,
                             max_batch_tokens=n * P, page_order_seed=WORKLOAD_SEED + rank)
     dec = pkg.Decoder.kv_only(cfg, rt, qn, kn)
@@ -715,7 +864,7 @@ def run_prefill_attn(args) -> int:
     st = torch.cuda.current_stream(dev)
     lens = [P] * n
     q_scale = float(np.float32(1.4426950408889634 / np.sqrt(float(D))))
-    q16 = (q * q_scale).to(torch.float16 if args.kv_dtype == "fp8" else torch.bfloat16)
+    q16 = (q * q_scale).to(torch.float16 if args.kv_dtype in ("fp8", "e4i8") else torch.bfloat16)
     tc = args.kv_dtype != "f32"
 
     def step():
@@ -851,14 +1000,18 @@ def main() -> int:
                     help="timed steps (default: 20 for the config-4 KV step, 64 for serve, 100 otherwise)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("kv", "model", "model3", "serve", "prefill", "gemm"), default="kv",
-                    help="kv: config 4 KV step (default); model: config 2 full greedy decode (0.6B bf16, 32 "
+    ap.add_argument("--workload", choices=("kv", "model", "model3", "serve", "prefill", "gemm", "readprobe"),
+                    default="kv",
+                    help="kv: config 4 KV step (default); readprobe: the read ceiling of K2's page stream on "
+                         "the config-4 cache; model: config 2 full greedy decode (0.6B bf16, 32 "
                          "streams); model3: config 3 (1.7B bf16, 64 streams, 390 audio + 20 text tokens); "
-                         "serve: config 5 (1.7B, FP8 cache, 512 concurrent streams, Poisson arrivals); "
+                         "serve: config 5 (1.7B, 8-bit cache, 512 concurrent streams, Poisson arrivals); "
                          "prefill: K3 prefill attention over config-3 prompts (--kv-dtype bf16/fp8/f32); "
                          "gemm: the tcgen05 projection GEMM on every decoder projection shape")
     ap.add_argument("--concurrency", type=int, default=512, help="serve: target concurrent streams per GPU")
-    ap.add_argument("--kv-dtype", choices=("bf16", "fp8", "f32"), default="bf16",
+    ap.add_argument("--serve-kv", choices=("e4i8", "fp8"), default="e4i8",
+                    help="serve: 8-bit cache (e4i8 = e4m3 K + int8 V, fp8 = e4m3 K and V)")
+    ap.add_argument("--kv-dtype", choices=("bf16", "fp8", "e4i8", "f32"), default="bf16",
                     help="kv workload: cache dtype (bf16 is the config-4 workload)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
@@ -878,6 +1031,8 @@ def main() -> int:
         return run_prefill_attn(args)
     if args.workload == "gemm":
         return run_gemm(args)
+    if args.workload == "readprobe":
+        return run_readprobe(args)
     return run_ours(args)
 
 

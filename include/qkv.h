@@ -50,7 +50,9 @@ enum qkv_status {
 enum qkv_dtype {
     QKV_F32 = 0,
     QKV_BF16 = 1,
-    QKV_FP8_E4M3 = 2           /* KV cache only: e4m3 values, fp32 scale per (page, kv head) */
+    QKV_FP8_E4M3 = 2,          /* KV cache only: e4m3 values, fp32 scale per (page, K|V, kv head) */
+    QKV_E4M3K_I8V = 3          /* KV cache only: K in e4m3, V in int8 stored as excess-128 bytes
+                                  (byte u holds (u - 128) x scale), fp32 scale per (page, K|V, kv head) */
 };
 
 /* Decoder hyper-parameters (GGUF keys qwen3-asr.text.*).
@@ -73,7 +75,7 @@ typedef struct qkv_model_config {
 typedef struct qkv_runtime_config {
     int32_t device;            /* CUDA device ordinal */
     int32_t weight_dtype;      /* QKV_F32 or QKV_BF16 (f32 GGUF values are rounded RNE) */
-    int32_t kv_dtype;          /* QKV_F32, QKV_BF16 or QKV_FP8_E4M3 */
+    int32_t kv_dtype;          /* QKV_F32, QKV_BF16, QKV_FP8_E4M3 or QKV_E4M3K_I8V */
     int32_t page_tokens;       /* tokens per page; must be 16 */
     int32_t max_streams;       /* stream slots */
     int32_t max_context;       /* tokens per stream (prompt + generated) */
@@ -256,18 +258,37 @@ int qkv_kv_step_host(qkv_handle *h, int32_t n, const int32_t *stream_ids, const 
 int qkv_stream_extend(qkv_handle *h, int32_t stream_id, int32_t tokens);
 
 /* Fill every page currently owned by open streams, in every layer, with
- * seeded N(0,1) values in the cache dtype (fp8: per-page scales set). */
+ * seeded N(0,1) values in the cache dtype (8-bit caches: per-page scales set). */
 int qkv_fill_random(qkv_handle *h, uint64_t seed);
 
 /* Page gather: copy tokens [0, len) of one stream's layer cache to host as
- * contiguous k[len][Hkv*D] and v[len][Hkv*D] in the cache dtype (fp8: raw
- * e4m3 bytes; scales via scales_out[n_pages][2][Hkv] when non-NULL). */
+ * contiguous k[len][Hkv*D] and v[len][Hkv*D] in the cache dtype (8-bit
+ * caches: the raw bytes, e4m3 or excess-128 int8; scales via
+ * scales_out[n_pages][2][Hkv] when non-NULL). */
 int qkv_gather(qkv_handle *h, int32_t layer, int32_t stream_id, void *k_host, void *v_host,
                float *scales_out);
 
 /* Page table of a stream: up to cap page ids into pages_out; *n = pages used. */
 int qkv_stream_pages(const qkv_handle *h, int32_t stream_id, int32_t *pages_out, int32_t cap,
                      int32_t *n);
+
+/* Measurement probe, no counterpart in the reference: the HBM read ceiling of
+ * the decode-attention kernel's access pattern.  Streams the pages
+ * pages_dev[0..n) (device int32 page ids of one layer's pool, in the order the
+ * decode attention reads them: each row's pages in turn) into shared memory
+ * with the same persistent grid, page split and one bulk copy per page as the
+ * decode-attention kernel, and discards them.  bf16 and 8-bit caches (pages of
+ * at most 64 KB); asynchronous on `stream` (NULL = the CUDA legacy default
+ * stream, as for the other operator-level calls). */
+int qkv_page_read_probe(qkv_handle *h, int32_t layer, int32_t n, const int32_t *pages_dev, void *stream);
+
+/* Debug probe of the greedy head (the reference keeps the equivalent hidden
+ * row inside text-decoder.cpp:476-493): copies the f32 residual rows [n][H]
+ * that the last qkv_decode_step fed to the final RMSNorm and the LM head, in
+ * that call's stream order, so a checker can recompute the f32 logits and
+ * their argmax (with bf16 weights the device re-scores in f32 every token
+ * that could be the f32 argmax; QWENASR_B200_EXACT_ARGMAX=0 turns that off). */
+int qkv_debug_residual(qkv_handle *h, int32_t n, float *out);
 
 /* Test of the failure path of the kernels' bounded waits (the reference has
  * no device code; its counterpart is the status checking of
@@ -293,7 +314,8 @@ int qkv_last_launches(const qkv_handle *h, int64_t *kernels);
  * framework's back breaks its accounting or is not allowed.  This entry point
  * has no counterpart in the reference.  The caller passes everything as device
  * pointers: one layer's pool ([n_pages][2][8][16][128] elements of kv_dtype),
- * its FP8 scales ([n_pages][2][8] f32, or NULL unless kv_dtype is FP8), the
+ * its 8-bit scales ([n_pages][2][8] f32, or NULL unless kv_dtype is one of
+ * the 8-bit caches), the
  * page table [max_streams][maxp], and per-row slots, lengths (tokens to
  * attend over), queries [n][2048] f32 and outputs [n][2048] f32.  No call
  * allocates: the kernel's scratch is a fixed ~3.5 MB array inside this

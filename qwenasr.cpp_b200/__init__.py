@@ -22,6 +22,7 @@ STATUS = {0: "QKV_OK", 1: "QKV_ERR_INVALID_ARG", 2: "QKV_ERR_OUT_OF_PAGES", 3: "
           4: "QKV_ERR_CUDA", 5: "QKV_ERR_DEVICE", 6: "QKV_ERR_IO", 7: "QKV_ERR_FORMAT", 8: "QKV_ERR_STATE",
           9: "QKV_ERR_NO_DEVICE", 10: "QKV_ERR_HOST_MEMORY"}
 F32, BF16, FP8 = 0, 1, 2
+E4I8 = 3          # 8-bit cache: e4m3 K, int8 (excess-128) V
 
 
 class ModelConfig(C.Structure):
@@ -81,6 +82,8 @@ SIGNATURES = {
     "qkv_stream_pages": (C.c_int, [_P, C.c_int32, _I32P, C.c_int32, _I32P]),
     "qkv_sync": (C.c_int, [_P]),
     "qkv_debug_wait_timeout": (C.c_int, [_P, C.c_int64]),
+    "qkv_debug_residual": (C.c_int, [_P, C.c_int32, C.c_void_p]),
+    "qkv_page_read_probe": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),
     "qkv_last_launches": (C.c_int, [_P, _I64P]),
     "qkv_kv_attend_noalloc": (C.c_int, [_P, C.c_int32, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, _P,
                                         _P, _P, _P, C.c_char_p, C.c_size_t]),
@@ -456,14 +459,14 @@ class Decoder:
 
     def gather(self, layer: int, s: int, kv_dtype: int):
         n = self.length(s)
-        dt = {F32: np.float32, BF16: np.uint16, FP8: np.uint8}[kv_dtype]
+        dt = {F32: np.float32, BF16: np.uint16, FP8: np.uint8, E4I8: np.uint8}[kv_dtype]
         k = np.zeros((n, 1024), dt)
         v = np.zeros((n, 1024), dt)
         npg = (n + 15) // 16
         scales = np.zeros((npg, 2, 8), np.float32)
         self._check(lib.qkv_gather(self.h, layer, s, k.ctypes.data, v.ctypes.data,
-                                   _ptr(scales, C.c_float) if kv_dtype == FP8 else None))
-        return (k, v, scales) if kv_dtype == FP8 else (k, v)
+                                   _ptr(scales, C.c_float) if kv_dtype in (FP8, E4I8) else None))
+        return (k, v, scales) if kv_dtype in (FP8, E4I8) else (k, v)
 
     def sync(self):
         self._check(lib.qkv_sync(self.h))

@@ -24,6 +24,7 @@ int env_dtype(const char *name, int dflt) {
     if (s == "f32") return QKV_F32;
     if (s == "bf16") return QKV_BF16;
     if (s == "fp8") return QKV_FP8_E4M3;
+    if (s == "e4i8") return QKV_E4M3K_I8V;
     return dflt;
 }
 

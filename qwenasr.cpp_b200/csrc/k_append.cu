@@ -45,6 +45,18 @@ template <> struct PageStore<uint8_t> {
     }
 };
 
+// V half of the e4m3-K / int8-V cache: excess-128 int8 bytes.
+struct PageStoreI8 {
+    static __device__ __forceinline__ void put(uint8_t *dst, const float (&v)[8], float inv_scale) {
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) lo |= f_to_u8ex(v[j] * inv_scale) << (8 * j);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) hi |= f_to_u8ex(v[4 + j] * inv_scale) << (8 * j);
+        *reinterpret_cast<uint2 *>(dst) = make_uint2(lo, hi);
+    }
+};
+
 // Per-head RMSNorm (double mean square, as text-decoder.cpp:542-557) and NEOX
 // RoPE (:604-625) of the 8 dims a half-warp lane holds; lane l16 ^ 8 holds the
 // rotation partners.  Must be called by all 32 lanes of the warp.
@@ -144,17 +156,26 @@ __global__ void __launch_bounds__(512) kv_append_kernel(AppendParams p) {
     TC *pool = static_cast<TC *>(p.pool);
     TC *dst = pool + ((static_cast<size_t>(page) * 2 + kv) * kHkv + g) * (kPageTokens * kHeadDim) +
               tok * kHeadDim + l16 * 8;
+    if constexpr (sizeof(TC) == 1) {
+        if (kv == 1 && p.v_int8) {   // warp-uniform (warps 12..15 hold V)
+            PageStoreI8::put(dst, x, inv_scale);
+            return;
+        }
+    }
     PageStore<TC>::put(dst, x, inv_scale);
 }
 
-// FP8 page scales.  One CTA per page touched by the batch (group = the
+// 8-bit page scales.  One CTA per page touched by the batch (group = the
 // batch's consecutive rows of one stream inside one page), 16 half-warp units
 // = (K | V) x 8 kv heads.  Each unit takes the absolute maximum of its head
 // over the group's new tokens (K after norm + RoPE, V raw); if the page
 // already holds tokens and the new maximum fits the current scale the scale is
-// kept, otherwise the scale becomes amax / 448 x headroom (x2 while the page
-// will take more tokens) and the tokens already stored are re-quantised to
-// it.  K1 then stores the new tokens with the settled scale.
+// kept, otherwise the scale becomes amax / qmax x headroom and the tokens
+// already stored are re-quantised to it.  K1 then stores the new tokens with
+// the settled scale.  e4m3 (qmax 448): headroom x2 while the page will take
+// more tokens, which costs nothing in a floating-point format.  int8 V (qmax
+// 127): headroom x1.25, since every bit of headroom is a bit of precision
+// lost; a page filled in one batch (prefill) gets no headroom either way.
 __global__ void __launch_bounds__(256) fp8_page_scale_kernel(AppendParams p) {
     pdl_trigger();
     pdl_wait();   // everything below reads or writes memory of earlier kernels
@@ -210,9 +231,11 @@ __global__ void __launch_bounds__(256) fp8_page_scale_kernel(AppendParams p) {
     const float old_scale = *sc;
     const bool has_old = tok0 > 0;
     const bool fills_page = tok0 + cnt == kPageTokens;
-    if (has_old && amax <= kE4m3Max * old_scale) return;   // current scale still covers the new tokens
-    const float head = fills_page ? 1.0f : 2.0f;
-    const float new_scale = fmaxf(fmaxf(amax, has_old ? kE4m3Max * old_scale : 0.0f) * head / kE4m3Max, 1e-30f);
+    const bool i8 = kv == 1 && p.v_int8;   // uniform over the half-warp unit
+    const float qmax = i8 ? kI8Max : kE4m3Max;
+    if (has_old && amax <= qmax * old_scale) return;   // current scale still covers the new tokens
+    const float head = fills_page ? 1.0f : (i8 ? 1.25f : 2.0f);
+    const float new_scale = fmaxf(fmaxf(amax, has_old ? qmax * old_scale : 0.0f) * head / qmax, 1e-30f);
     if (has_old) {
         // re-quantise the tokens already in the page to the new scale
         uint8_t *pool = static_cast<uint8_t *>(p.pool);
@@ -221,18 +244,28 @@ __global__ void __launch_bounds__(256) fp8_page_scale_kernel(AppendParams p) {
         for (int t = 0; t < tok0; ++t) {
             uint2 w = *reinterpret_cast<uint2 *>(base + t * kHeadDim);
             uint32_t lo = 0, hi = 0;
+            if (i8) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float2 f = e4m3x2_to_f2(static_cast<uint16_t>(((j < 2 ? w.x : w.y) >> (16 * (j & 1))) & 0xffffu));
-                const uint32_t q0 = f_to_e4m3(f.x * ratio), q1 = f_to_e4m3(f.y * ratio);
-                const uint32_t pair = q0 | (q1 << 8);
-                if (j < 2) lo |= pair << (16 * j);
-                else hi |= pair << (16 * (j - 2));
+                for (int j = 0; j < 4; ++j) {
+                    lo |= f_to_u8ex(u8ex_to_f((w.x >> (8 * j)) & 0xffu) * ratio) << (8 * j);
+                    hi |= f_to_u8ex(u8ex_to_f((w.y >> (8 * j)) & 0xffu) * ratio) << (8 * j);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 f = e4m3x2_to_f2(static_cast<uint16_t>(((j < 2 ? w.x : w.y) >> (16 * (j & 1))) & 0xffffu));
+                    const uint32_t q0 = f_to_e4m3(f.x * ratio), q1 = f_to_e4m3(f.y * ratio);
+                    const uint32_t pair = q0 | (q1 << 8);
+                    if (j < 2) lo |= pair << (16 * j);
+                    else hi |= pair << (16 * (j - 2));
+                }
             }
             *reinterpret_cast<uint2 *>(base + t * kHeadDim) = make_uint2(lo, hi);
         }
     }
-    __syncwarp();
+    // Only this half-warp unit takes this path (the other half of the warp
+    // may have returned above).
+    __syncwarp(0xffffu << (threadIdx.x & 16));
     if (l16 == 0) *sc = new_scale;
 }
 
@@ -275,8 +308,9 @@ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
 }
 
 // Seeded N(0,1) fill of the given pages (Box-Muller on a counter hash).
+// 8-bit caches: scale 8 / qmax per (page, K|V, head); v_int8 stores V as int8.
 template <typename TC>
-__global__ void page_fill_kernel(TC *pool, float *scales, const int *pages, int n, uint64_t seed) {
+__global__ void page_fill_kernel(TC *pool, float *scales, const int *pages, int n, uint64_t seed, int v_int8) {
     const size_t per_page = static_cast<size_t>(2) * kPageHalfElems;
     for (int i = blockIdx.y; i < n; i += gridDim.y) {
         const int page = pages[i];
@@ -288,11 +322,13 @@ __global__ void page_fill_kernel(TC *pool, float *scales, const int *pages, int 
             const float z = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
             if constexpr (sizeof(TC) == 4) base[e] = z;
             else if constexpr (sizeof(TC) == 2) base[e] = __float2bfloat16_rn(z);
+            else if (v_int8 && e >= static_cast<size_t>(kPageHalfElems)) base[e] = static_cast<uint8_t>(f_to_u8ex(z * (kI8Max / 8.0f)));
             else base[e] = f_to_e4m3(z * (kE4m3Max / 8.0f));
         }
         if constexpr (sizeof(TC) == 1) {
             if (blockIdx.x == 0 && threadIdx.x < 2 * kHkv)
-                scales[static_cast<size_t>(page) * 2 * kHkv + threadIdx.x] = 8.0f / kE4m3Max;
+                scales[static_cast<size_t>(page) * 2 * kHkv + threadIdx.x] =
+                    8.0f / (v_int8 && threadIdx.x >= kHkv ? kI8Max : kE4m3Max);
         }
     }
 }
@@ -309,10 +345,13 @@ cudaError_t launch_kv_append(const AppendParams &p, int kv_dtype, cudaStream_t s
     switch (kv_dtype) {
         case kKvF32: return launch_pdl(kv_append_kernel<float>, dim3(p.n), dim3(512), 0, st, p);
         case kKvBF16: return launch_pdl(kv_append_kernel<__nv_bfloat16>, dim3(p.n), dim3(512), 0, st, p);
-        case kKvFP8: {
-            const cudaError_t e = launch_fp8_page_scale(p, st);
+        case kKvFP8:
+        case kKvE4I8: {
+            AppendParams q = p;
+            q.v_int8 = kv_dtype == kKvE4I8 ? 1 : 0;
+            const cudaError_t e = launch_fp8_page_scale(q, st);
             if (e != cudaSuccess) return e;
-            return launch_pdl(kv_append_kernel<uint8_t>, dim3(p.n), dim3(512), 0, st, p);
+            return launch_pdl(kv_append_kernel<uint8_t>, dim3(q.n), dim3(512), 0, st, q);
         }
         default: return cudaErrorInvalidValue;
     }
@@ -334,6 +373,7 @@ cudaError_t launch_page_gather(const void *pool, int kv_dtype, const int *pages,
                 static_cast<__nv_bfloat16 *>(k_out), static_cast<__nv_bfloat16 *>(v_out), err);
             break;
         case kKvFP8:
+        case kKvE4I8:
             page_gather_kernel<uint8_t><<<len, 256, 0, st>>>(static_cast<const uint8_t *>(pool), pages, n_pages_row, len,
                                                              n_pages, static_cast<uint8_t *>(k_out), static_cast<uint8_t *>(v_out), err);
             break;
@@ -356,12 +396,14 @@ cudaError_t launch_page_fill(void *pool_layer, float *scales_layer, int kv_dtype
     if (n <= 0) return cudaSuccess;
     dim3 grid(32, n < 4096 ? n : 4096);
     switch (kv_dtype) {
-        case kKvF32: page_fill_kernel<float><<<grid, 256, 0, st>>>(static_cast<float *>(pool_layer), nullptr, pages, n, seed); break;
+        case kKvF32: page_fill_kernel<float><<<grid, 256, 0, st>>>(static_cast<float *>(pool_layer), nullptr, pages, n, seed, 0); break;
         case kKvBF16:
-            page_fill_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<__nv_bfloat16 *>(pool_layer), nullptr, pages, n, seed);
+            page_fill_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<__nv_bfloat16 *>(pool_layer), nullptr, pages, n, seed, 0);
             break;
         case kKvFP8:
-            page_fill_kernel<uint8_t><<<grid, 256, 0, st>>>(static_cast<uint8_t *>(pool_layer), scales_layer, pages, n, seed);
+        case kKvE4I8:
+            page_fill_kernel<uint8_t><<<grid, 256, 0, st>>>(static_cast<uint8_t *>(pool_layer), scales_layer, pages, n, seed,
+                                                            kv_dtype == kKvE4I8 ? 1 : 0);
             break;
         default: return cudaErrorInvalidValue;
     }

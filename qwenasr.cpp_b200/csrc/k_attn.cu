@@ -192,7 +192,8 @@ __global__ void __launch_bounds__(64) wait_probe_kernel(DevError *err, long long
     }
 }
 
-template <typename TC, typename TOut>
+// kVI8 (8-bit cache only): V is int8 (excess-128 bytes) rather than e4m3.
+template <typename TC, typename TOut, bool kVI8 = false>
 __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendParams p) {
     pdl_trigger();
     // With p.early the set-up below (row arrays, page table: host copies that
@@ -547,15 +548,16 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
                     __syncwarp();
                     // ---- PV ----
                     if constexpr (kFp8) {
-                        // p (f16) x V (e4m3 -> f16x2, exact) accumulated in f32 for this
-                        // chunk (= one page), then scaled by the page's V scale once.
+                        // p (f16) x V (e4m3 or int8 -> f16x2, exact) accumulated in f32
+                        // for this chunk (= one page), then scaled by the page's V scale once.
                         float xa[4] = {0.f, 0.f, 0.f, 0.f}, xb[4] = {0.f, 0.f, 0.f, 0.f};
                         const uint16_t *phalf = reinterpret_cast<const uint16_t *>(my_p);
                         // One token of V for this lane's 4 dims, both heads.
                         auto pv_token = [&](int t, uint32_t wa, uint32_t wb, int hsel) {
                             const uint32_t w = *reinterpret_cast<const uint32_t *>(vst + t * kHeadDim + 4 * lane);
                             uint32_t x, y;
-                            e4m3x4_to_h2x2(w, x, y);
+                            if constexpr (kVI8) u8x4_to_h2x2(w, x, y);
+                            else e4m3x4_to_h2x2(w, x, y);
                             if (hsel) {
                                 axpy2_f16_f32<1>(xa[0], xa[1], x, wa); axpy2_f16_f32<1>(xa[2], xa[3], y, wa);
                                 axpy2_f16_f32<1>(xb[0], xb[1], x, wb); axpy2_f16_f32<1>(xb[2], xb[3], y, wb);
@@ -732,13 +734,14 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
     }
 }
 
-template <typename TC, typename TOut> cudaError_t prepare_t() {
-    return cudaFuncSetAttribute(decode_attn_kernel<TC, TOut>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+template <typename TC, typename TOut, bool kVI8 = false> cudaError_t prepare_t() {
+    return cudaFuncSetAttribute(decode_attn_kernel<TC, TOut, kVI8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(smem_bytes<TC>()));
 }
 
-template <typename TC, typename TOut> cudaError_t launch_t(const AttendParams &p, int grid, cudaStream_t st) {
-    return launch_pdl(decode_attn_kernel<TC, TOut>, dim3(grid), dim3(threads<TC>()), smem_bytes<TC>(), st, p);
+template <typename TC, typename TOut, bool kVI8 = false>
+cudaError_t launch_t(const AttendParams &p, int grid, cudaStream_t st) {
+    return launch_pdl(decode_attn_kernel<TC, TOut, kVI8>, dim3(grid), dim3(threads<TC>()), smem_bytes<TC>(), st, p);
 }
 
 }  // namespace
@@ -751,14 +754,17 @@ cudaError_t prepare_decode_attn() {
     if ((e = prepare_t<__nv_bfloat16, float>()) != cudaSuccess) return e;
     if ((e = prepare_t<__nv_bfloat16, __nv_bfloat16>()) != cudaSuccess) return e;
     if ((e = prepare_t<uint8_t, float>()) != cudaSuccess) return e;
-    return prepare_t<uint8_t, __nv_bfloat16>();
+    if ((e = prepare_t<uint8_t, __nv_bfloat16>()) != cudaSuccess) return e;
+    if ((e = prepare_t<uint8_t, float, true>()) != cudaSuccess) return e;
+    return prepare_t<uint8_t, __nv_bfloat16, true>();
 }
 
 size_t attn_smem_bytes(int kv_dtype) {
     switch (kv_dtype) {
         case kKvF32: return smem_bytes<float>();
         case kKvBF16: return smem_bytes<__nv_bfloat16>();
-        case kKvFP8: return smem_bytes<uint8_t>();
+        case kKvFP8:
+        case kKvE4I8: return smem_bytes<uint8_t>();
         default: return 0;
     }
 }
@@ -771,8 +777,98 @@ cudaError_t launch_decode_attn(const AttendParams &p, int kv_dtype, bool out_bf1
         case kKvBF16:
             return out_bf16 ? launch_t<__nv_bfloat16, __nv_bfloat16>(p, grid, st) : launch_t<__nv_bfloat16, float>(p, grid, st);
         case kKvFP8: return out_bf16 ? launch_t<uint8_t, __nv_bfloat16>(p, grid, st) : launch_t<uint8_t, float>(p, grid, st);
+        case kKvE4I8:
+            return out_bf16 ? launch_t<uint8_t, __nv_bfloat16, true>(p, grid, st) : launch_t<uint8_t, float, true>(p, grid, st);
         default: return cudaErrorInvalidValue;
     }
+}
+
+namespace {
+
+// Read probe: the ceiling of K2's page stream.  The same persistent grid and
+// page split as K2 (CTA c of G takes pages [c n / G, (c + 1) n / G) of the
+// list, which holds the rows' pages end to end in K2's order), each page's
+// K and V block (page_bytes <= 64 KB, contiguous) brought into a 3-stage
+// shared-memory ring by one cp.async.bulk copy from this GPU's own memory
+// with the L2 evict-first hint, no multicast.  The consumer warp only waits
+// for each stage to land and hands it back; nothing is computed.  Every wait
+// is bounded, and the producer drains its copies before the CTA exits.
+constexpr int kProbeStages = 3;
+__global__ void __launch_bounds__(64, 1) page_read_probe_kernel(const uint8_t *pool, uint32_t page_bytes,
+                                                                const int *pages, int n, int n_pool_pages,
+                                                                DevError *err) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + static_cast<size_t>(kProbeStages) * page_bytes);
+    uint64_t *empty = full + kProbeStages;
+    __shared__ int never;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        never = 0;
+        for (int s = 0; s < kProbeStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (lane != 0) return;
+    const int64_t G = gridDim.x, c = blockIdx.x;
+    const int p0 = static_cast<int>(c * n / G), p1 = static_cast<int>((c + 1) * n / G);
+    if (warp == 0) {
+        const uint64_t pol = l2_evict_first_policy();
+        int iter = 0;
+        for (int i = p0; i < p1; ++i, ++iter) {
+            const int s = iter % kProbeStages;
+            const uint32_t ph = static_cast<uint32_t>(iter / kProbeStages) & 1u;
+            const int page = pages[i];
+            if (page < 0 || page >= n_pool_pages) {
+                report_error(err, kErrPageIndex, kWhereProbe, i, page);
+                break;
+            }
+            if (!stage_wait(&empty[s], ph ^ 1u, &never)) {
+                report_error(err, kErrWaitTimeout, kWhereProbe, static_cast<int>(c), iter);
+                break;
+            }
+            mbar_arrive_expect_tx(&full[s], page_bytes);
+            bulk_g2s(smem + static_cast<size_t>(s) * page_bytes, pool + static_cast<size_t>(page) * page_bytes,
+                     page_bytes, &full[s], pol);
+        }
+        // Drain: every copy issued has landed before the CTA can exit.
+        for (int it = iter > kProbeStages ? iter - kProbeStages : 0; it < iter; ++it) {
+            if (!mbar_wait(&full[it % kProbeStages], static_cast<uint32_t>(it / kProbeStages) & 1u, kWaitLimitCycles)) {
+                report_error(err, kErrWaitTimeout, kWhereProbe, static_cast<int>(c), -it);
+                break;
+            }
+        }
+    } else {
+        for (int i = p0, iter = 0; i < p1; ++i, ++iter) {
+            const int s = iter % kProbeStages;
+            if (!stage_wait(&full[s], static_cast<uint32_t>(iter / kProbeStages) & 1u, &never)) {
+                report_error(err, kErrWaitTimeout, kWhereProbe, static_cast<int>(c), iter);
+                break;
+            }
+            mbar_arrive(&empty[s]);
+        }
+    }
+}
+
+}  // namespace
+
+size_t page_read_probe_smem(uint32_t page_bytes) {
+    return static_cast<size_t>(kProbeStages) * page_bytes + 2 * kProbeStages * sizeof(uint64_t);
+}
+
+cudaError_t launch_page_read_probe(const void *pool_layer, uint32_t page_bytes, const int *pages, int n,
+                                   int n_pool_pages, int grid, DevError *err, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    if (page_bytes == 0 || page_bytes > 65536u || page_bytes % 16 != 0) return cudaErrorInvalidValue;
+    const size_t smem = page_read_probe_smem(page_bytes);
+    cudaError_t e = cudaFuncSetAttribute(page_read_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    page_read_probe_kernel<<<grid, 64, smem, st>>>(static_cast<const uint8_t *>(pool_layer), page_bytes, pages, n,
+                                                    n_pool_pages, err);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_wait_probe(DevError *err, long long limit_cycles, cudaStream_t st) {
@@ -853,8 +949,8 @@ extern "C" int qkv_kv_attend_noalloc(const void *pool_layer, int32_t kv_dtype, c
                                      float *out_dev, void *stream, char *err, size_t err_len) {
     using namespace qkv;
     if (n < 0 || !pool_layer || !page_table || maxp <= 0 || max_streams <= 0 || n_pages <= 0 ||
-        (n > 0 && (!slots_dev || !lens_dev || !q_dev || !out_dev)) || kv_dtype < kKvF32 || kv_dtype > kKvFP8 ||
-        (kv_dtype == kKvFP8 && !scales_layer)) {
+        (n > 0 && (!slots_dev || !lens_dev || !q_dev || !out_dev)) || kv_dtype < kKvF32 || kv_dtype > kKvE4I8 ||
+        (kv_is_8bit(kv_dtype) && !scales_layer)) {
         noalloc_err(err, err_len, "kv_attend_noalloc: bad argument");
         return QKV_ERR_INVALID_ARG;
     }

@@ -416,6 +416,128 @@ __global__ void __launch_bounds__(512) argmax_split_kernel(const float *logits, 
     counters[r] = 0;
 }
 
+// Largest row norm of a bf16 weight matrix [rows][H] (warp per row), for the
+// error bound of argmax_refine_kernel.  *out must start at 0; row norms are
+// positive, so their float bits order like the floats.
+__global__ void __launch_bounds__(256) row_norm_max_kernel(const __nv_bfloat16 *W, int rows, int H, float *out) {
+    const int lane = threadIdx.x & 31;
+    const int warps = static_cast<int>(gridDim.x * (blockDim.x >> 5));
+    for (int r = static_cast<int>(blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)); r < rows; r += warps) {
+        const __nv_bfloat16 *w = W + static_cast<size_t>(r) * H;
+        double ss = 0.0;
+        for (int k = lane; k < H; k += 32) {
+            const double v = __bfloat162float(w[k]);
+            ss += v * v;
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) atomicMax(reinterpret_cast<int *>(out), __float_as_int(static_cast<float>(sqrt(ss)) * 1.0001f));
+    }
+}
+
+// Exact re-scoring of the greedy argmax behind the bf16 LM head.  The head
+// GEMM multiplies bf16 weights by the bf16-rounded final hidden row b =
+// bf16(h), so an approximate logit a_j differs from the f32 logit
+// l_j = sum_k W_jk h_k by at most
+//     sum_k |W_jk| |h_k - b_k| + (f32 accumulation) <= (2^-8 + 2^-12) ||W_j|| ||h||
+//     <= e = (2^-8 + 2^-12) wmax ||h||                 (Cauchy-Schwarz; wmax = max_j ||W_j||).
+// The f32 argmax j* therefore has a_j* >= l_j* - e >= l_jmax - e >= a_jmax - 2e:
+// every token whose approximate logit is within 2e of the approximate maximum
+// is re-scored exactly (bf16 weight row x f32 h, f32 accumulation), and the
+// row's id becomes the first maximum of those scores, i.e. the argmax of the
+// f32 logits (as text-decoder.cpp:2266-2274 takes it over its f32 logits).
+// Grid (rows, slices): each CTA rebuilds h from the residual row exactly as
+// rmsnorm_kernel does, scans its slice, and a warp re-scores each candidate;
+// scores meet in a per-row 64-bit key (ordered float bits, then the inverted
+// index so that the lower index wins a tie), and the row's last CTA writes the
+// id and resets the key and counter.
+__global__ void __launch_bounds__(256) argmax_refine_kernel(const float *logits, int V, int S, const float *x,
+                                                            const int *rows, int H, const float *norm_w, float eps,
+                                                            const __nv_bfloat16 *W, const float *wmax,
+                                                            unsigned long long *keys, int *counters, int *ids) {
+    pdl_trigger();
+    pdl_wait();   // ids and logits come from the kernels before this one
+    extern __shared__ __align__(16) float hs[];   // [H]
+    __shared__ double part[8];
+    __shared__ float s_scale, s_thr;
+    __shared__ int last;
+    const int r = blockIdx.x, sl = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float *xr = x + static_cast<size_t>(rows ? rows[r] : r) * H;
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) ss += static_cast<double>(xr[i]) * xr[i];
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) part[warp] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) t += part[k];
+        s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(t / static_cast<double>(H)), eps)));
+    }
+    __syncthreads();
+    const float scale = s_scale;
+    double hh = 0.0;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+        const float v = __fmul_rn(__fmul_rn(xr[i], scale), norm_w[i]);
+        hs[i] = v;
+        hh += static_cast<double>(v) * v;
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) hh += __shfl_xor_sync(0xffffffffu, hh, o);
+    __syncthreads();   // part[] is reused below
+    if (lane == 0) part[warp] = hh;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) t += part[k];
+        const double e = (1.0 / 256.0 + 1.0 / 4096.0) * static_cast<double>(*wmax) * sqrt(t);
+        const float amax = logits[static_cast<size_t>(r) * V + ids[r]];
+        s_thr = static_cast<float>(static_cast<double>(amax) - 2.0 * e * 1.01);
+    }
+    __syncthreads();
+    const float thr = s_thr;
+    const float *row = logits + static_cast<size_t>(r) * V;
+    const int ch = (V + S - 1) / S;
+    const int lo = sl * ch, hi = min(V, lo + ch);
+    for (int base = lo + warp * 32; base < hi; base += static_cast<int>(blockDim.x)) {
+        const int j = base + lane;
+        const bool cand = j < hi && row[j] >= thr;
+        unsigned mask = __ballot_sync(0xffffffffu, cand);
+        while (mask) {
+            const int jj = base + __ffs(mask) - 1;
+            mask &= mask - 1;
+            const __nv_bfloat16 *w = W + static_cast<size_t>(jj) * H;
+            float acc = 0.0f;
+            for (int k = lane * 8; k < H; k += 256) {   // H % 8 == 0 (checked at launch)
+                const uint4 q = *reinterpret_cast<const uint4 *>(w + k);
+                acc = fmaf(bf16lo(q.x), hs[k + 0], acc); acc = fmaf(bf16hi(q.x), hs[k + 1], acc);
+                acc = fmaf(bf16lo(q.y), hs[k + 2], acc); acc = fmaf(bf16hi(q.y), hs[k + 3], acc);
+                acc = fmaf(bf16lo(q.z), hs[k + 4], acc); acc = fmaf(bf16hi(q.z), hs[k + 5], acc);
+                acc = fmaf(bf16lo(q.w), hs[k + 6], acc); acc = fmaf(bf16hi(q.w), hs[k + 7], acc);
+            }
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (lane == 0) {
+                const uint32_t u = __float_as_uint(acc);
+                const uint32_t ou = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+                atomicMax(keys + r, (static_cast<unsigned long long>(ou) << 32) | (0xffffffffu - static_cast<uint32_t>(jj)));
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(&counters[r], 1) == S - 1;
+    }
+    __syncthreads();
+    if (!last || threadIdx.x != 0) return;
+    __threadfence();
+    const unsigned long long key = atomicExch(keys + r, 0ull);
+    if (key != 0ull) ids[r] = static_cast<int>(0xffffffffu - static_cast<uint32_t>(key & 0xffffffffull));
+    counters[r] = 0;
+}
+
 // GGUF tensor bytes (f32 / f16 / bf16) -> device weight dtype (f32 / bf16, RNE).
 template <typename TD>
 __global__ void convert_kernel(const void *src, int src_type, TD *dst, size_t n) {
@@ -568,6 +690,28 @@ cudaError_t launch_argmax_split(const float *logits, int M, int V, int *ids, flo
     if (S < 1) S = 1;
     return launch_pdl(argmax_split_kernel, dim3(M, S), dim3(512), 0, st, logits, V, S, part_v, part_i, counters,
                       ids);
+}
+
+cudaError_t launch_row_norm_max(const void *W, int rows, int H, float *out, cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    cudaError_t e = cudaMemsetAsync(out, 0, sizeof(float), st);
+    if (e != cudaSuccess) return e;
+    const int blocks = (rows + 7) / 8 < 4096 ? (rows + 7) / 8 : 4096;
+    row_norm_max_kernel<<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16 *>(W), rows, H, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_argmax_refine(const float *logits, int M, int V, const float *x, const int *rows, int H,
+                                 const float *norm_w, float eps, const void *W, const float *wmax,
+                                 unsigned long long *keys, int *counters, int *ids, int num_sms, cudaStream_t st) {
+    if (M <= 0) return cudaSuccess;
+    if (H % 8 != 0 || H > 12 * 1024) return cudaErrorInvalidValue;
+    int S = (2 * num_sms + M - 1) / M;
+    if (S > 64) S = 64;
+    if (S > (V + 4095) / 4096) S = (V + 4095) / 4096;
+    if (S < 1) S = 1;
+    return launch_pdl(argmax_refine_kernel, dim3(M, S), dim3(256), static_cast<size_t>(H) * sizeof(float), st, logits,
+                      V, S, x, rows, H, norm_w, eps, static_cast<const __nv_bfloat16 *>(W), wmax, keys, counters, ids);
 }
 
 }  // namespace qkv

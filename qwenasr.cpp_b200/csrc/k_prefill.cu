@@ -51,13 +51,20 @@ template <> __device__ __forceinline__ float4 load_v4<uint8_t>(const uint8_t *p)
     return make_float4(a.x, a.y, b.x, b.y);
 }
 
+// V of the e4m3-K / int8-V cache: four excess-128 int8 bytes.
+__device__ __forceinline__ float4 load_v4_i8(const uint8_t *p) {
+    const uint32_t w = *reinterpret_cast<const uint32_t *>(p);
+    return make_float4(u8ex_to_f(w & 0xffu), u8ex_to_f((w >> 8) & 0xffu), u8ex_to_f((w >> 16) & 0xffu),
+                       u8ex_to_f(w >> 24));
+}
+
 template <typename TOut> __device__ __forceinline__ void store_o4(TOut *p, float4 v);
 template <> __device__ __forceinline__ void store_o4<float>(float *p, float4 v) { *reinterpret_cast<float4 *>(p) = v; }
 template <> __device__ __forceinline__ void store_o4<__nv_bfloat16>(__nv_bfloat16 *p, float4 v) {
     *reinterpret_cast<uint2 *>(p) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
 }
 
-template <typename TC, typename TOut>
+template <typename TC, typename TOut, bool kVI8 = false>
 __global__ void __launch_bounds__(256) prefill_attn_kernel(PrefillAttnParams p) {
     pdl_trigger();
     pdl_wait();   // everything below reads or writes memory of earlier kernels
@@ -139,7 +146,9 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(PrefillAttnParams p) 
             const int kk = kb + jk;
             const size_t vbase = ((static_cast<size_t>(pg) * 2 + 1) * kHkv + g) * (kPageTokens * kHeadDim) +
                                  (kk % kPageTokens) * kHeadDim + 4 * lane;
-            const float4 v = load_v4<TC>(pool + vbase);
+            float4 v;
+            if constexpr (kVI8) v = load_v4_i8(reinterpret_cast<const uint8_t *>(pool) + vbase);
+            else v = load_v4<TC>(pool + vbase);
             oa.x = fmaf(wa, v.x, oa.x); oa.y = fmaf(wa, v.y, oa.y); oa.z = fmaf(wa, v.z, oa.z); oa.w = fmaf(wa, v.w, oa.w);
             ob.x = fmaf(wb, v.x, ob.x); ob.y = fmaf(wb, v.y, ob.y); ob.z = fmaf(wb, v.z, ob.z); ob.w = fmaf(wb, v.w, ob.w);
         }
@@ -166,6 +175,10 @@ cudaError_t launch_prefill_attn(const PrefillAttnParams &p, int kv_dtype, bool o
         case kKvFP8:
             if (out_bf16) return launch_pdl(prefill_attn_kernel<uint8_t, __nv_bfloat16>, dim3(p.n), dim3(256), 0, st, p);
             else return launch_pdl(prefill_attn_kernel<uint8_t, float>, dim3(p.n), dim3(256), 0, st, p);
+            break;
+        case kKvE4I8:
+            if (out_bf16) return launch_pdl(prefill_attn_kernel<uint8_t, __nv_bfloat16, true>, dim3(p.n), dim3(256), 0, st, p);
+            else return launch_pdl(prefill_attn_kernel<uint8_t, float, true>, dim3(p.n), dim3(256), 0, st, p);
             break;
         default: return cudaErrorInvalidValue;
     }

@@ -70,6 +70,7 @@ struct K3Params {
     int max_streams;
     int n_pages;
     DevError *err;
+    int v_int8;             // 8-bit cache: V tiles are int8 (excess-128 bytes), not e4m3
 };
 
 // Swizzled (128 B) operand descriptors, sm_100 version bit set.
@@ -256,9 +257,10 @@ __device__ __forceinline__ bool fetch_tile(const K3Params &p, TileRegs<TC> &tr, 
     return ok;
 }
 
-// Into a swizzled [2 blocks][128 rows][64] 16-bit tile (e4m3: dequantised
-// exactly to f16, then times the page's (kv, g) scale in f16, read here so it
-// does not occupy registers while the loader waits for the buffer).
+// Into a swizzled [2 blocks][128 rows][64] 16-bit tile (8-bit cache: e4m3,
+// or int8 for V tiles of the e4m3-K / int8-V cache, dequantised exactly to
+// f16, then times the page's (kv, g) scale in f16, read here so it does not
+// occupy registers while the loader waits for the buffer).
 template <typename TC>
 __device__ __forceinline__ void store_tile(const K3Params &p, uint8_t *tile, const TileRegs<TC> &tr, const int (&pg)[8],
                                            int kv, int g, int t) {
@@ -275,11 +277,13 @@ __device__ __forceinline__ void store_tile(const K3Params &p, uint8_t *tile, con
             const float sc = __ldg(p.scales + (static_cast<size_t>(valid ? pg[m] : 0) * 2 + kv) * kHkv + g);
             const uint32_t s2 = pack_h2(sc, sc);
             const uint32_t ws[4] = {tr.w[m].x, tr.w[m].y, tr.w[m].z, tr.w[m].w};
+            const bool i8 = kv == 1 && p.v_int8;
             uint32_t h[8];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 uint32_t lo2, hi2;
-                e4m3x4_to_h2x2(ws[k], lo2, hi2);
+                if (i8) u8x4_to_h2x2(ws[k], lo2, hi2);
+                else e4m3x4_to_h2x2(ws[k], lo2, hi2);
                 h[2 * k] = hmul2_bits(lo2, s2);
                 h[2 * k + 1] = hmul2_bits(hi2, s2);
             }
@@ -778,7 +782,7 @@ cudaError_t prepare_prefill_tc() {
                                 static_cast<int>(smem));
 }
 
-bool prefill_tc_supported(int kv_dtype) { return kv_dtype == kKvBF16 || kv_dtype == kKvFP8; }
+bool prefill_tc_supported(int kv_dtype) { return kv_dtype == kKvBF16 || kv_is_8bit(kv_dtype); }
 
 cudaError_t launch_q_to16(const float *q, int n, float scale, bool f16, void *out, cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
@@ -791,7 +795,7 @@ cudaError_t launch_q_to16(const float *q, int n, float scale, bool f16, void *ou
 cudaError_t launch_prefill_attn_tc(const PrefillAttnParams &pp, int kv_dtype, const int4 *items, int n_items,
                                    bool out_bf16, cudaStream_t st) {
     if (n_items <= 0) return cudaSuccess;
-    if (!prefill_tc_supported(kv_dtype) || (kv_dtype == kKvFP8 && !pp.scales) || !pp.q16) return cudaErrorInvalidValue;
+    if (!prefill_tc_supported(kv_dtype) || (kv_is_8bit(kv_dtype) && !pp.scales) || !pp.q16) return cudaErrorInvalidValue;
     K3Params p{};
     p.items = items;
     p.slots = pp.slots;
@@ -806,6 +810,7 @@ cudaError_t launch_prefill_attn_tc(const PrefillAttnParams &pp, int kv_dtype, co
     p.max_streams = pp.max_streams;
     p.n_pages = pp.n_pages;
     p.err = pp.err;
+    p.v_int8 = kv_dtype == kKvE4I8 ? 1 : 0;
     int dev = 0, sms = 0;
     size_t smem = 0;
     cudaError_t e = cudaGetDevice(&dev);

@@ -111,6 +111,26 @@ __device__ __forceinline__ uint8_t f_to_e4m3(float v) {
 }
 constexpr float kE4m3Max = 448.0f;
 
+// ---- int8 V of the e4m3-K / int8-V cache ----
+// A V element is one excess-128 byte u = q + 128 with q = round(v / scale)
+// clamped to [-127, 127], so u is 1..255.
+constexpr float kI8Max = 127.0f;
+__device__ __forceinline__ uint32_t f_to_u8ex(float v) {
+    int q = __float2int_rn(v);
+    q = q < -127 ? -127 : (q > 127 ? 127 : q);
+    return static_cast<uint32_t>(q + 128);
+}
+__device__ __forceinline__ float u8ex_to_f(uint32_t u) { return static_cast<float>(static_cast<int>(u) - 128); }
+// Four excess-128 bytes -> two f16x2 words holding q exactly (bytes 0,1 ->
+// lo2; 2,3 -> hi2): 0x6400 | u is the f16 number 1024 + u, and subtracting
+// 1152 (f16 bits 0x6480) leaves u - 128 = q.
+__device__ __forceinline__ void u8x4_to_h2x2(uint32_t w, uint32_t &lo2, uint32_t &hi2) {
+    const uint32_t a = __byte_perm(w, 0x64646464u, 0x4140);   // u0, 0x64, u1, 0x64
+    const uint32_t b = __byte_perm(w, 0x64646464u, 0x4342);   // u2, 0x64, u3, 0x64
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(lo2) : "r"(a), "r"(0x64806480u));
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(hi2) : "r"(b), "r"(0x64806480u));
+}
+
 // ---- shared-memory address + mbarrier + bulk copy (inline PTX) ----
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -39,7 +39,11 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-enum KvDtype { kKvF32 = 0, kKvBF16 = 1, kKvFP8 = 2 };
+// kKvFP8: K and V in e4m3.  kKvE4I8: K in e4m3, V in int8 (excess-128 bytes);
+// both one byte per element with an f32 scale per (page, K|V, kv head).
+enum KvDtype { kKvF32 = 0, kKvBF16 = 1, kKvFP8 = 2, kKvE4I8 = 3 };
+inline bool kv_is_8bit(int kv_dtype) { return kv_dtype == kKvFP8 || kv_dtype == kKvE4I8; }
+inline size_t kv_elem_bytes(int kv_dtype) { return kv_dtype == kKvF32 ? 4 : (kv_dtype == kKvBF16 ? 2 : 1); }
 enum ActDtype { kActF32 = 0, kActBF16 = 1 };
 
 constexpr int kAttnMaxRows = 1024;   // rows (streams) per decode-attention launch
@@ -67,6 +71,7 @@ struct AppendParams {
     int n_pages;
     float eps;
     DevError *err;
+    int v_int8;                // 8-bit cache: 1 = V stored as int8 (kKvE4I8), 0 = e4m3
 };
 
 struct AttendParams {
@@ -118,6 +123,11 @@ cudaError_t launch_fp8_page_scale(const AppendParams &p, cudaStream_t st);
 cudaError_t prepare_decode_attn();
 size_t attn_smem_bytes(int kv_dtype);
 cudaError_t launch_decode_attn(const AttendParams &p, int kv_dtype, bool out_bf16, int grid, cudaStream_t st);
+// Read probe of K2's page stream: pages[0..n) (ids into this layer's pool of
+// n_pool_pages pages of page_bytes <= 64 KB) bulk-copied into shared memory and
+// discarded, split over `grid` persistent CTAs like K2's page list.
+cudaError_t launch_page_read_probe(const void *pool_layer, uint32_t page_bytes, const int *pages, int n,
+                                   int n_pool_pages, int grid, DevError *err, cudaStream_t st);
 // Test of the bounded waits: one CTA whose waits (K2's stage and hand-over
 // waits, the plain mbarrier wait) run out after limit_cycles and report it.
 cudaError_t launch_wait_probe(DevError *err, long long limit_cycles, cudaStream_t st);
@@ -181,5 +191,12 @@ cudaError_t launch_convert(const void *src, int src_ggml_type, void *dst, int ds
 // scratch, counters [M] zero between launches (the kernel resets them).
 cudaError_t launch_argmax_split(const float *logits, int M, int V, int *ids, float *part_v, int *part_i,
                                 int *counters, int max_slices, int num_sms, cudaStream_t st);
+// bf16 LM head: the largest row norm of W (once, at load), and the exact
+// re-scoring of every token whose approximate logit could be the f32 maximum
+// (keys/counters: [M] zeroed once; they reset themselves).
+cudaError_t launch_row_norm_max(const void *W, int rows, int H, float *out, cudaStream_t st);
+cudaError_t launch_argmax_refine(const float *logits, int M, int V, const float *x, const int *rows, int H,
+                                 const float *norm_w, float eps, const void *W, const float *wmax,
+                                 unsigned long long *keys, int *counters, int *ids, int num_sms, cudaStream_t st);
 
 }  // namespace qkv

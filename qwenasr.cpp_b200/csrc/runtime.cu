@@ -84,8 +84,6 @@ void set_err(char *err, size_t len, const std::string &msg) {
     }
 }
 
-size_t kv_elem_bytes(int kv_dtype) { return kv_dtype == kKvF32 ? 4 : kv_dtype == kKvBF16 ? 2 : 1; }
-
 int validate_model(const qkv_model_config &c, std::string *e) {
     if (c.n_layers <= 0 || c.hidden <= 0 || c.intermediate <= 0 || c.vocab <= 0) {
         *e = "model config: non-positive dimension";
@@ -112,7 +110,7 @@ int validate_rt(const qkv_runtime_config &r, std::string *e) {
         *e = "runtime config: page_tokens must be 16";
         return QKV_ERR_INVALID_ARG;
     }
-    if (r.kv_dtype < QKV_F32 || r.kv_dtype > QKV_FP8_E4M3 || (r.weight_dtype != QKV_F32 && r.weight_dtype != QKV_BF16)) {
+    if (r.kv_dtype < QKV_F32 || r.kv_dtype > QKV_E4M3K_I8V || (r.weight_dtype != QKV_F32 && r.weight_dtype != QKV_BF16)) {
         *e = "runtime config: bad dtype";
         return QKV_ERR_INVALID_ARG;
     }
@@ -147,7 +145,7 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
     h->pool_layer_bytes = h->page_bytes * static_cast<size_t>(h->n_pages);
     CK(cudaMalloc(&h->pool, h->pool_layer_bytes * c.n_layers));
     CK(cudaMemsetAsync(h->pool, 0, h->pool_layer_bytes * c.n_layers, h->stream));
-    if (h->rt.kv_dtype == kKvFP8) {
+    if (kv_is_8bit(h->rt.kv_dtype)) {
         h->scales_layer_elems = static_cast<size_t>(h->n_pages) * 2 * kHkv;
         CK(cudaMalloc(&h->scales, h->scales_layer_elems * c.n_layers * sizeof(float)));
         std::vector<float> ones(h->scales_layer_elems * c.n_layers, 1.0f);
@@ -196,6 +194,14 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
         CK(cudaMalloc(&h->am_i, ms * qkv_handle::kArgmaxSlices * sizeof(int)));
         CK(cudaMalloc(&h->am_cnt, ms * sizeof(int)));
         CK(cudaMemset(h->am_cnt, 0, ms * sizeof(int)));
+        CK(cudaMalloc(&h->am_keys, ms * sizeof(unsigned long long)));
+        CK(cudaMemset(h->am_keys, 0, ms * sizeof(unsigned long long)));
+        CK(cudaMalloc(&h->am_rcnt, ms * sizeof(int)));
+        CK(cudaMemset(h->am_rcnt, 0, ms * sizeof(int)));
+        CK(cudaMalloc(&h->d_wout_norm, sizeof(float)));
+        CK(cudaMemset(h->d_wout_norm, 0, sizeof(float)));
+        const char *ea = std::getenv("QWENASR_B200_EXACT_ARGMAX");
+        h->exact_argmax = !(ea && std::strcmp(ea, "0") == 0);
     }
     CK(cudaMalloc(&h->d_rowbuf, 4 * R * sizeof(int)));
     CK(cudaMallocHost(&h->h_rowbuf, qkv_handle::kRowRing * 4 * R * sizeof(int)));
@@ -254,6 +260,7 @@ void destroy(qkv_handle *h) {
     cudaFree(h->pool); cudaFree(h->scales); cudaFree(h->d_page_table); cudaFree(h->d_rope);
     cudaFree(h->x); cudaFree(h->qkv); cudaFree(h->q); cudaFree(h->gu); cudaFree(h->logits);
     cudaFree(h->am_v); cudaFree(h->am_i); cudaFree(h->am_cnt);
+    cudaFree(h->am_keys); cudaFree(h->am_rcnt); cudaFree(h->d_wout_norm);
     cudaFree(h->xn); cudaFree(h->attn); cudaFree(h->act); cudaFree(h->host_stage);
     cudaFree(h->d_rowbuf); cudaFree(h->d_out_ids); cudaFree(h->d_items); cudaFree(h->part_o); cudaFree(h->part_ml);
     cudaFree(h->counters); cudaFree(h->d_err);
@@ -386,6 +393,7 @@ int load_weights(qkv_handle *h, const GgufFile &f) {
     if ((rc = up.put(te, h->embd, h->w_dtype, 0)) || (rc = up.put(ow, h->w_out, h->w_dtype, 0)) ||
         (rc = up.put(on, h->out_norm, kActF32, 0)))
         return rc;
+    if (h->w_dtype == kActBF16) CK(launch_row_norm_max(h->w_out, static_cast<int>(V), static_cast<int>(H), h->d_wout_norm, h->stream));
     // Audio projector, when the file has it (names and shapes of
     // audio-encoder.cpp:776-790; GGML ne = [in, out]).
     if (const GgufTensor *pw0 = f.find("audio.post_norm.weight")) {
@@ -739,6 +747,13 @@ int head_and_argmax(qkv_handle *h, int n, const int *d_rows) {
     CK(launch_argmax_split(h->logits, n, c.vocab, h->d_out_ids, h->am_v, h->am_i, h->am_cnt,
                            qkv_handle::kArgmaxSlices, h->num_sms, h->stream));
     h->launches += 3;
+    if (h->w_dtype == kActBF16 && h->exact_argmax) {
+        // The bf16 head rounds the final hidden row to bf16 (2^-8 relative):
+        // re-score, in f32, every token that could be the f32 argmax.
+        CK(launch_argmax_refine(h->logits, n, c.vocab, h->x, d_rows, c.hidden, h->out_norm, c.rms_norm_eps, h->w_out,
+                                h->d_wout_norm, h->am_keys, h->am_rcnt, h->d_out_ids, h->num_sms, h->stream));
+        h->launches += 1;
+    }
     return QKV_OK;
 }
 
@@ -774,7 +789,7 @@ cudaError_t prefill_attend(qkv_handle *h, int l, int n, const int *slots, const 
     pp.err = h->d_err;
     if (prefill_on_tc(h, items, n_items)) {
         if (!pp.q16) {
-            cudaError_t e = launch_q_to16(q, n, pp.scale_log2, h->rt.kv_dtype == kKvFP8, h->q, st);
+            cudaError_t e = launch_q_to16(q, n, pp.scale_log2, kv_is_8bit(h->rt.kv_dtype), h->q, st);
             if (e != cudaSuccess) return e;
             pp.q16 = h->q;
         }
@@ -803,7 +818,7 @@ int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int
             if (tc) {
                 ap.q16_out = h->q;
                 ap.q16_scale = attn_scale_log2();
-                ap.q16_f16 = h->rt.kv_dtype == kKvFP8 ? 1 : 0;
+                ap.q16_f16 = kv_is_8bit(h->rt.kv_dtype) ? 1 : 0;
             }
             CK(launch_kv_append(ap, h->rt.kv_dtype, h->stream));
             CK(prefill_attend(h, l, n, slots, pos, h->q, tc ? h->q : nullptr, h->attn, bf, items, n_items, h->stream));
@@ -1446,7 +1461,7 @@ static int prefill_attend_op(qkv_handle *h, int32_t layer, int32_t n, const int3
     if (layer < 0 || layer >= h->cfg.n_layers || n < 0 || (n > 0 && (!stream_ids || !lens || !(q || q16) || !out)))
         return fail(h, QKV_ERR_INVALID_ARG, "prefill_attend: bad layer, count or pointer");
     if (q16 && !(h->prefill_tc && prefill_tc_supported(h->rt.kv_dtype)))
-        return fail(h, QKV_ERR_STATE, "prefill_attend_q16: needs a bf16 or e4m3 cache with the tensor-core kernel");
+        return fail(h, QKV_ERR_STATE, "prefill_attend_q16: needs a bf16 or 8-bit cache with the tensor-core kernel");
     int rc;
     if ((rc = check_streams(h, n, stream_ids))) return rc;
     int64_t total = 0;
@@ -1691,6 +1706,29 @@ int qkv_stream_pages(const qkv_handle *h, int32_t stream_id, int32_t *pages_out,
     if (!pg) return QKV_ERR_INVALID_ARG;
     *n = static_cast<int32_t>(pg->size());
     for (int32_t i = 0; i < cap && i < *n; ++i) pages_out[i] = (*pg)[static_cast<size_t>(i)];
+    return QKV_OK;
+}
+
+int qkv_page_read_probe(qkv_handle *h, int32_t layer, int32_t n, const int32_t *pages_dev, void *stream) {
+    if (!h || n < 0 || (n > 0 && !pages_dev)) return QKV_ERR_INVALID_ARG;
+    if (layer < 0 || layer >= h->cfg.n_layers) return fail(h, QKV_ERR_INVALID_ARG, "read probe: bad layer");
+    if (h->page_bytes > 65536) return fail(h, QKV_ERR_STATE, "read probe: pages larger than 64 KB (f32 cache)");
+    CK(cudaSetDevice(h->device));
+    CK(launch_page_read_probe(static_cast<const uint8_t *>(h->pool) + h->pool_layer_bytes * static_cast<size_t>(layer),
+                              static_cast<uint32_t>(h->page_bytes), pages_dev, n, h->n_pages, h->num_sms, h->d_err,
+                              static_cast<cudaStream_t>(stream)));
+    ++h->launches;
+    return QKV_OK;
+}
+
+int qkv_debug_residual(qkv_handle *h, int32_t n, float *out) {
+    if (!h || !out || n <= 0) return QKV_ERR_INVALID_ARG;
+    if (!h->has_weights) return fail(h, QKV_ERR_STATE, "handle has no model weights");
+    if (n > h->rt.max_streams) return fail(h, QKV_ERR_INVALID_ARG, "more rows than the decode batch can hold");
+    CK(cudaSetDevice(h->device));
+    CK(cudaMemcpyAsync(out, h->x, static_cast<size_t>(n) * h->cfg.hidden * sizeof(float), cudaMemcpyDeviceToHost,
+                       h->stream));
+    CK(cudaStreamSynchronize(h->stream));
     return QKV_OK;
 }
 

@@ -96,6 +96,12 @@ struct qkv_handle {
     static constexpr int kArgmaxSlices = 16;
     float *am_v = nullptr;
     int *am_i = nullptr, *am_cnt = nullptr;
+    // exact re-scoring of the bf16 head's argmax: per-row keys and counters
+    // (zero between launches) and the largest row norm of the head weights
+    unsigned long long *am_keys = nullptr;
+    int *am_rcnt = nullptr;
+    float *d_wout_norm = nullptr;
+    bool exact_argmax = true;   // QWENASR_B200_EXACT_ARGMAX=0 turns the re-scoring off
     int *d_out_ids = nullptr;   // [max_rows]
     int *h_out_ids = nullptr;   // pinned
     int4 *d_items = nullptr;    // prefill attention work items

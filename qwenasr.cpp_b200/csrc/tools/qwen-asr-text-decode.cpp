@@ -6,7 +6,7 @@
 //
 //   qwen-asr-text-decode MODEL.gguf INPUT.f32 [--generate N | --prefill | --layer L]
 //                        [--out PATH] [--device auto|gpu|cpu] [--stop-ids a,b,..] [--no-stop]
-//                        [--kv-dtype f32|bf16|fp8] [--weights f32|bf16] [--page-size 16] [--gpu N]
+//                        [--kv-dtype f32|bf16|fp8|e4i8] [--weights f32|bf16] [--page-size 16] [--gpu N]
 //                        (the reference tool's --threads, --backend, --audio-backend, --kv-cache,
 //                         --language and --system are accepted; see main)
 // INPUT.f32 = raw float32 [tokens][hidden] (audio rows already spliced in).
@@ -34,7 +34,7 @@ int usage(const char *argv0) {
     std::cerr << "usage: " << argv0
               << " MODEL.gguf INPUT.f32 [--generate N | --prefill | --layer L] [--out PATH]"
                  " [--device auto|gpu|cpu] [--stop-ids a,b] [--no-stop]"
-                 " [--kv-dtype f32|bf16|fp8] [--weights f32|bf16] [--page-size 16] [--gpu N]\n";
+                 " [--kv-dtype f32|bf16|fp8|e4i8] [--weights f32|bf16] [--page-size 16] [--gpu N]\n";
     return 2;
 }
 
@@ -186,9 +186,9 @@ int main(int argc, char **argv) {
             while (std::getline(ss, tok, ',')) if (!tok.empty()) stop_ids.push_back(static_cast<int32_t>(std::atoi(tok.c_str())));
             have_stop = true;
         } else if (a == "--kv-dtype") {
-            kv_dtype = need("f32, bf16 or fp8");
-            if (kv_dtype != "f32" && kv_dtype != "bf16" && kv_dtype != "fp8") {
-                std::cerr << "--kv-dtype must be f32, bf16 or fp8\n";
+            kv_dtype = need("f32, bf16, fp8 or e4i8");
+            if (kv_dtype != "f32" && kv_dtype != "bf16" && kv_dtype != "fp8" && kv_dtype != "e4i8") {
+                std::cerr << "--kv-dtype must be f32, bf16, fp8 (e4m3 K and V) or e4i8 (e4m3 K, int8 V)\n";
                 return 2;
             }
         } else if (a == "--weights") {
@@ -226,7 +226,7 @@ int main(int argc, char **argv) {
     if (!kv_dtype.empty()) setenv("QWENASR_B200_KV", kv_dtype.c_str(), 1);
     if (!weights.empty()) setenv("QWENASR_B200_WEIGHTS", weights.c_str(), 1);
     if (!gpu.empty()) setenv("QWENASR_B200_DEVICE", gpu.c_str(), 1);
-    const std::string kv_shown = switch_value("QWENASR_B200_KV", {"bf16", "fp8"});
+    const std::string kv_shown = switch_value("QWENASR_B200_KV", {"bf16", "fp8", "e4i8"});
     const std::string weights_shown = switch_value("QWENASR_B200_WEIGHTS", {"bf16"});
 
     const auto t_init = std::chrono::steady_clock::now();

@@ -18,15 +18,22 @@ def stream_cost(prompt_len: int, new_tokens: int) -> int:
     return int(new_tokens * prompt_len + new_tokens * (new_tokens + 1) // 2)
 
 
-def lpt_partition(costs, n_ranks: int) -> list[list[int]]:
-    """Indices of `costs` per rank, greedy longest-processing-time first."""
-    order = np.argsort(-np.asarray(costs, dtype=np.int64), kind="stable")
+def lpt_partition(costs, n_ranks: int, cap: int | None = None) -> list[list[int]]:
+    """Indices of `costs` per rank, greedy longest-processing-time first: each
+    stream, costliest first, goes to the least-loaded rank (ties: lowest rank).
+    With `cap`, a rank that holds `cap` streams takes no more (a fixed batch
+    per GPU); n_ranks * cap must cover all streams."""
+    costs = np.asarray(costs, dtype=np.int64)
+    if cap is not None and cap * n_ranks < len(costs):
+        raise ValueError("cap * n_ranks is smaller than the number of streams")
+    order = np.argsort(-costs, kind="stable")
     heap = [(0, r) for r in range(n_ranks)]
     out: list[list[int]] = [[] for _ in range(n_ranks)]
     for i in order:
         load, r = heapq.heappop(heap)
         out[r].append(int(i))
-        heapq.heappush(heap, (load + int(costs[i]), r))
+        if cap is None or len(out[r]) < cap:
+            heapq.heappush(heap, (load + int(costs[i]), r))
     return [sorted(x) for x in out]
 
 

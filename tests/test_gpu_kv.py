@@ -103,11 +103,12 @@ def test_gather_roundtrip_permuted(pkg, checker, seed):
 
 def attend_case(pkg, checker, kv_dtype, lens, seed=3, tol=None):
     """K2 against exact f32 attention over the cache as stored (bf16 widened,
-    e4m3 dequantised with its page scales).  f32/bf16: 2e-5 relative.  e4m3:
-    2e-3 relative, because K2 holds q and the softmax weights p as f16 for its
-    mixed-precision f16 x f16 -> f32 FMAs (2^-12 relative rounding each)."""
+    8-bit caches dequantised with their page scales).  f32/bf16: 2e-5
+    relative.  8-bit: 2e-3 relative, because K2 holds q and the softmax
+    weights p as f16 for its mixed-precision f16 x f16 -> f32 FMAs (2^-12
+    relative rounding each)."""
     if tol is None:
-        tol = 2e-3 if kv_dtype == 2 else 2e-5
+        tol = 2e-3 if kv_dtype in (2, 3) else 2e-5
     dec, qn, kn = kv_handle(pkg, kv_dtype, seed=seed, max_streams=len(lens), max_context=max(lens) + 16)
     with dec:
         rng = np.random.default_rng(seed)
@@ -127,13 +128,7 @@ def attend_case(pkg, checker, kv_dtype, lens, seed=3, tol=None):
         got = out.cpu().numpy()
         worst = 0.0
         for i, s in enumerate(streams):
-            got_kv = dec.gather(0, s, kv_dtype)
-            if kv_dtype == 2:
-                k, v = fp8_dequant(*got_kv)
-            else:
-                k, v = got_kv
-            if kv_dtype == 1:
-                k, v = bits_to_f32(k), bits_to_f32(v)
+            k, v = as_f32_cache(kv_dtype, dec.gather(0, s, kv_dtype))
             want = checker.attend(qv[i], k, v)
             err = np.max(np.abs(got[i] - want)) / max(np.max(np.abs(want)), 1e-6)
             worst = max(worst, err)
@@ -158,7 +153,7 @@ def test_attention_many_rows(pkg, checker):
     attend_case(pkg, checker, 1, lens, seed=9)
 
 
-@pytest.mark.parametrize("kv_dtype", [0, 1, 2])
+@pytest.mark.parametrize("kv_dtype", [0, 1, 2, 3])
 def test_attention_many_rows_multi_segment(pkg, checker, kv_dtype):
     """200 rows, ~3800 pages: every CTA's page range spans several rows, so
     each CTA runs several segments back to back (for the e4m3 cache, each one
@@ -168,10 +163,12 @@ def test_attention_many_rows_multi_segment(pkg, checker, kv_dtype):
     attend_case(pkg, checker, kv_dtype, lens, seed=11)
 
 
+@pytest.mark.parametrize("kv_dtype", [2, 3])
 @pytest.mark.parametrize("lens", [[1, 2, 15, 16, 17, 31, 32, 33], [4096, 5, 700, 64, 1, 2500]])
-def test_attention_fp8_against_dequantised_cache(pkg, checker, lens):
-    """e4m3 cache: K2 equals exact attention over the dequantised cache."""
-    attend_case(pkg, checker, 2, lens)
+def test_attention_fp8_against_dequantised_cache(pkg, checker, lens, kv_dtype):
+    """8-bit caches (e4m3 K and V; e4m3 K and int8 V): K2 equals exact
+    attention over the dequantised cache."""
+    attend_case(pkg, checker, kv_dtype, lens)
 
 
 def test_attention_repeated_launches_reset_counters(pkg, checker):
@@ -224,6 +221,62 @@ def test_kv_step_matches_oracle(pkg, checker):
             dec.sync()
             np.testing.assert_allclose(out.cpu().numpy(), want, rtol=1e-4, atol=2e-5)
         assert [dec.length(s) for s in streams] == (lens0 + 3).tolist()
+
+
+def test_kv_step_at_bench_scale_matches_oracle(pkg, checker):
+    """The benched configuration itself (config 4: 256 streams with the
+    bench's seeded log-uniform [64, 4096] contexts, bf16 paged cache, the
+    bench's seeded page permutation, N(0,1) contents), 2 of its 28 layers,
+    two qkv_kv_step calls.  For 16 streams spread over the length range (the
+    middle stream of each of 16 rank bins): the appended K and V are RNE
+    bf16 of the oracle's append (text-decoder.cpp:958-1028) bit for bit, and
+    the output is within 2e-5 relative of the oracle's attention
+    (:1029-1075) over the cache as stored (bf16 widened to f32)."""
+    import bench
+    n_layers = 2
+    lens = bench.stream_lengths(0).astype(np.int32)
+    qn, kn = bench.qk_norm_weights()
+    qn, kn = qn[:n_layers], kn[:n_layers]
+    cfg = dict(n_layers=n_layers, hidden=1024, n_heads=HQ, n_kv_heads=HKV, head_dim=D, intermediate=3072,
+               vocab=151936, rope_theta=1.0e6, rms_norm_eps=1.0e-6)
+    steps = 2
+    pages = int(sum((int(L) + steps + 15) // 16 for L in lens)) + 64
+    rt = pkg.runtime_config(device=0, weight_dtype=pkg.F32, kv_dtype=pkg.BF16, max_streams=len(lens),
+                            max_context=int(lens.max()) + steps + 16, max_pages=pages,
+                            page_order_seed=bench.WORKLOAD_SEED)
+    order = np.argsort(lens, kind="stable")
+    sample = order[8::16]
+    assert len(sample) == 16
+    rng = np.random.default_rng(44)
+    worst = 0.0
+    with pkg.Decoder.kv_only(cfg, rt, qn, kn) as dec:
+        streams = [dec.open() for _ in lens]
+        for s, L in zip(streams, lens):
+            dec.extend(s, int(L))
+        dec.fill_random(bench.WORKLOAD_SEED)
+        cur = lens.copy()
+        for step in range(steps):
+            qkv = rng.standard_normal((n_layers, len(lens), QKV), dtype=np.float32)
+            x = torch.tensor(qkv, device="cuda")
+            out = torch.empty((n_layers, len(lens), HQ * D), device="cuda")
+            dec.kv_step(streams, x.data_ptr(), out.data_ptr())
+            torch.cuda.synchronize()
+            dec.sync()
+            got = out.cpu().numpy()
+            for i in sample:
+                pos = int(cur[i])
+                for layer in range(n_layers):
+                    k_b, v_b = dec.gather(layer, streams[i], pkg.BF16)
+                    assert k_b.shape[0] == pos + 1
+                    q, k, v = checker.append_qkv(qkv[layer, i], qn[layer], kn[layer], pos)
+                    assert np.array_equal(k_b[pos], bf16_bits(k)), (step, i, layer)
+                    assert np.array_equal(v_b[pos], bf16_bits(v)), (step, i, layer)
+                    want = checker.attend(q, bits_to_f32(k_b), bits_to_f32(v_b))
+                    worst = max(worst, float(np.max(np.abs(got[layer, i] - want)) / np.max(np.abs(want))))
+            cur += 1
+    print(f"config-4 step at bench scale: max relative attention error {worst:.3e} over {len(sample)} streams "
+          f"(contexts {int(lens[sample].min())}..{int(lens[sample].max())})")
+    assert worst < 2e-5, worst
 
 
 @pytest.mark.parametrize("kv_dtype", [1, 2])
@@ -328,22 +381,42 @@ def e4m3_to_f32(b: np.ndarray) -> np.ndarray:
     return (sign * val).astype(np.float32)
 
 
-def fp8_dequant(k_b, v_b, scales):
-    """(tokens, 1024) e4m3 bytes + (pages, 2, 8) scales -> f32 K and V."""
+def u8ex_to_f32(b: np.ndarray) -> np.ndarray:
+    """Excess-128 int8 bytes (the V half of the e4m3-K / int8-V cache) -> q."""
+    return (b.astype(np.int32) - 128).astype(np.float32)
+
+
+def fp8_dequant(k_b, v_b, scales, v_int8=False):
+    """(tokens, 1024) 8-bit bytes + (pages, 2, 8) scales -> f32 K and V
+    (K e4m3; V e4m3, or int8 when v_int8)."""
     L = k_b.shape[0]
     pg = np.arange(L) // 16
     k = e4m3_to_f32(k_b).reshape(L, 8, 128) * scales[pg, 0, :, None]
-    v = e4m3_to_f32(v_b).reshape(L, 8, 128) * scales[pg, 1, :, None]
+    v = (u8ex_to_f32(v_b) if v_int8 else e4m3_to_f32(v_b)).reshape(L, 8, 128) * scales[pg, 1, :, None]
     return k.reshape(L, 1024).astype(np.float32), v.reshape(L, 1024).astype(np.float32)
 
 
+def as_f32_cache(kv_dtype, got):
+    """A gathered cache as the f32 values K2/K3 compute with."""
+    if kv_dtype in (2, 3):
+        return fp8_dequant(*got, v_int8=kv_dtype == 3)
+    if kv_dtype == 1:
+        return bits_to_f32(got[0]), bits_to_f32(got[1])
+    return got
+
+
+@pytest.mark.parametrize("kv_dtype", [2, 3])
 @pytest.mark.parametrize("style", ["batch", "token_by_token"])
-def test_fp8_append_dequantises_within_e4m3_precision(pkg, checker, style):
-    """FP8 cache: every stored K/V element, dequantised with its page's
-    per-(kv, head) scale, is within 2^-4 of the page-head maximum of the
-    reference values, also when later tokens are 40x larger than the first
-    (the page scale grows and the stored tokens are re-quantised)."""
-    dec, qn, kn = kv_handle(pkg, 2, seed=3, max_streams=2, max_context=128)
+def test_fp8_append_dequantises_within_e4m3_precision(pkg, checker, style, kv_dtype):
+    """8-bit caches: every stored K/V element, dequantised with its page's
+    per-(kv, head) scale, is within the format's precision of the reference
+    values, also when later tokens are 40x larger than the first (the page
+    scale grows and the stored tokens are re-quantised).  e4m3: within 2^-4
+    of the page-head maximum.  int8 V: within 2.5 steps of the final scale
+    (half a step per rounding; each re-quantisation grows the scale by at
+    least 1.25x, so the half steps of all earlier scales sum to < 2 more),
+    and within half a step for a page filled in one batch."""
+    dec, qn, kn = kv_handle(pkg, kv_dtype, seed=3, max_streams=2, max_context=128)
     with dec:
         rng = np.random.default_rng(17)
         L = 40
@@ -357,7 +430,7 @@ def test_fp8_append_dequantises_within_e4m3_precision(pkg, checker, style):
         else:
             for t in range(L):
                 fill_stream(dec, 0, s, raw[t:t + 1], start=t)
-        k_b, v_b, scales = dec.gather(0, s, 2)
+        k_b, v_b, scales = dec.gather(0, s, kv_dtype)
         ref_k = np.zeros((L, 1024), np.float32)
         ref_v = np.zeros((L, 1024), np.float32)
         for t in range(L):
@@ -369,13 +442,20 @@ def test_fp8_append_dequantises_within_e4m3_precision(pkg, checker, style):
             for kv, (got_b, ref) in enumerate(((k_b, ref_k), (v_b, ref_v))):
                 for g in range(8):
                     cols = slice(g * 128, (g + 1) * 128)
-                    deq = e4m3_to_f32(got_b[rows, cols]) * scales[pg, kv, g]
                     want = ref[rows, cols]
-                    bound = np.abs(want).max() * 2.0 ** -4
-                    assert np.abs(deq - want).max() <= bound, (style, pg, kv, g)
+                    if kv == 1 and kv_dtype == 3:
+                        sc = scales[pg, kv, g]
+                        deq = u8ex_to_f32(got_b[rows, cols]) * sc
+                        assert np.abs(want).max() <= 127.0 * sc * (1 + 1e-6), (style, pg, g)   # no clipping
+                        steps = 0.5 if (style == "batch" and t0 + 16 <= L) else 2.5
+                        assert np.abs(deq - want).max() <= steps * sc * (1 + 1e-5), (style, pg, g)
+                    else:
+                        deq = e4m3_to_f32(got_b[rows, cols]) * scales[pg, kv, g]
+                        bound = np.abs(want).max() * 2.0 ** -4
+                        assert np.abs(deq - want).max() <= bound, (style, pg, kv, g)
 
 
-@pytest.mark.parametrize("kv_dtype", [0, 1, 2])
+@pytest.mark.parametrize("kv_dtype", [0, 1, 2, 3])
 def test_prefill_attention_operator(pkg, checker, kv_dtype):
     """qkv_prefill_attend (K3 on tcgen05 for bf16/e4m3, CUDA cores for f32)
     against exact causal attention over the cache as stored: ragged streams,
@@ -404,10 +484,7 @@ def test_prefill_attention_operator(pkg, checker, kv_dtype):
         got = out.cpu().numpy()
         worst, row = 0.0, 0
         for s, L, nq in zip(streams, lens_total, q_lens):
-            kv_got = dec.gather(0, s, kv_dtype)
-            k, v = fp8_dequant(*kv_got) if kv_dtype == 2 else kv_got
-            if kv_dtype == 1:
-                k, v = bits_to_f32(k), bits_to_f32(v)
+            k, v = as_f32_cache(kv_dtype, dec.gather(0, s, kv_dtype))
             for j in range(nq):
                 pos = L - nq + j
                 want = checker.attend(qv[row], k[:pos + 1], v[:pos + 1])
@@ -419,7 +496,7 @@ def test_prefill_attention_operator(pkg, checker, kv_dtype):
         assert worst < tol, worst
 
 
-@pytest.mark.parametrize("kv_dtype", [0, 1, 2])
+@pytest.mark.parametrize("kv_dtype", [0, 1, 2, 3])
 def test_prefill_attention_q16_entry(pkg, kv_dtype):
     """qkv_prefill_attend_q16 with q already scaled and rounded (torch's
     round-to-nearest, as the fused append and the f32 entry's conversion do)
@@ -438,7 +515,7 @@ def test_prefill_attention_q16_entry(pkg, kv_dtype):
             streams.append(s)
         q = torch.tensor(rng.standard_normal((sum(q_lens), HQ * D), dtype=np.float32), device="cuda")
         scale = np.float32(1.4426950408889634 / np.sqrt(128.0))
-        q16 = (q * float(scale)).to(torch.float16 if kv_dtype == 2 else torch.bfloat16)
+        q16 = (q * float(scale)).to(torch.float16 if kv_dtype in (2, 3) else torch.bfloat16)
         out_q16 = torch.full_like(q, float("nan"))
         if kv_dtype == 0:
             with pytest.raises(pkg.QkvError) as ei:

@@ -5,7 +5,9 @@ arithmetic: the committed fixtures (reference scalar C++) and the live oracle.
 Bars (from the task's north star):
   f32 weights + f32 cache: logits within 1e-3 relative, identical greedy ids;
   bf16 weights + bf16 cache: >= 99% teacher-forced greedy agreement, max logit
-  deviation reported; FP8 cache: deviation vs the bf16 cache reported."""
+  deviation reported (asserted at full size; this file's tiny model holds 98%);
+  8-bit caches: agreement and deviation reported, the e4m3-K / int8-V cache
+  held to the bf16 cache's bar, the all-e4m3 cache to a stated lower one."""
 from pathlib import Path
 
 import numpy as np
@@ -132,11 +134,20 @@ def test_bf16_agreement(pkg, synth, checker, tiny_files, norm):
     assert agree >= 0.98 and dev < 0.02, (agree, dev)
 
 
-def test_fp8_cache_deviation(pkg, synth, checker, tiny_files):
+@pytest.mark.parametrize("kv,bar", [(2, 0.90), (3, 0.93)])
+def test_fp8_cache_deviation(pkg, synth, checker, tiny_files, kv, bar):
+    """8-bit caches on the tiny model with trained-like norm weights (1 +
+    N(0, 0.02)): its attention is peaked, so the 8-bit K error moves the
+    softmax weights as much as the V error moves the output, and neither
+    8-bit cache reaches the bf16 cache's 99% here (measured 94% for both;
+    a float64 simulation gives 94.3% for e4m3 K and V, 96.2% for e4m3 K +
+    int8 V and 98.4% even for int8 K + bf16 V).  Stated deviations, held to
+    90% (e4m3 K and V) and 93% (e4m3 K + int8 V).  The 99% bar is asserted
+    at full size on the configured N(0, 0.02) model (test_gpu_scale.py)."""
     cfg, files = tiny_files
-    agree, dev = teacher_forced(pkg, synth, checker, files[("bf16", "one_plus")], 1, 2, n_streams=8, n_steps=64)
-    print(f"fp8 cache: teacher-forced agreement {agree:.4f}, max rel logit deviation {dev:.3e}")
-    assert agree >= 0.85, (agree, dev)   # e4m3 keeps 3 mantissa bits: a stated deviation, not a parity bar
+    agree, dev = teacher_forced(pkg, synth, checker, files[("bf16", "one_plus")], 1, kv, n_streams=8, n_steps=64)
+    print(f"8-bit cache kv={kv}: teacher-forced agreement {agree:.4f}, max rel logit deviation {dev:.3e}")
+    assert agree >= bar, (agree, dev)
 
 
 def test_out_of_pages_and_capacity_errors(pkg, synth, tiny_files):
@@ -218,7 +229,7 @@ def test_prefill_attention_layer(pkg, synth, checker, tiny_files, tokens, kv):
     assert err < (3e-2 if kv == 1 else 1e-1), err
 
 
-@pytest.mark.parametrize("kv", [1, 2])
+@pytest.mark.parametrize("kv", [1, 2, 3])
 def test_prefill_attention_tensor_cores_match_cuda_cores(pkg, synth, tiny_files, kv, monkeypatch):
     """Same cache, same prompts: K3 (tcgen05) and the CUDA-core prefill
     attention (f32 math over the exactly dequantised cache) agree.  K3 rounds
@@ -311,10 +322,12 @@ def test_bf16_typed_file_loads_like_f32_file(pkg, synth, tmp_path, w):
 
 
 @pytest.mark.parametrize("n", [4, 40])
-def test_argmax_first_maximum_over_split_rows(pkg, synth, tmp_path, n):
+def test_argmax_first_maximum_over_split_rows(pkg, synth, tmp_path, n, monkeypatch):
     """The device argmax (rows split over several CTAs for a 20000-word
     vocabulary) returns the first maximum of the logits it also returns, for
-    the prefill and two decode steps."""
+    the prefill and two decode steps (the f32 re-scoring of the bf16 head is
+    off here: it may pick a token whose bf16-input logit is not the largest)."""
+    monkeypatch.setenv("QWENASR_B200_EXACT_ARGMAX", "0")
     cfg = dict(synth.TINY, vocab=20000)
     path = synth.write_gguf(tmp_path / "v20k.gguf", cfg, seed=4, weights="bf16", norm_init="one_plus",
                             tokenizer=False)
@@ -326,3 +339,38 @@ def test_argmax_first_maximum_over_split_rows(pkg, synth, tmp_path, n):
         for _ in range(2):
             ids, logits = dec.decode_step(s, want_logits=True)
             assert np.array_equal(ids, np.argmax(logits, axis=1))
+
+
+def test_bf16_head_argmax_is_the_f32_argmax(pkg, synth, tmp_path, monkeypatch):
+    """bf16 weights: the LM head's GEMM rounds the final hidden row to bf16,
+    so its logits carry up to 2^-8 relative error; the device then re-scores
+    in f32 every token within the proven error bound of the maximum.  The ids
+    must equal the argmax of the f32 logits W . rmsnorm(x) computed here in
+    float64 from the step's own residual rows (qkv_debug_residual), at every
+    decode step; without the re-scoring some rows pick another token."""
+    import ctypes as C
+    cfg = dict(synth.TINY, vocab=20000)
+    path = synth.write_gguf(tmp_path / "v20k.gguf", cfg, seed=4, weights="bf16", norm_init="normal",
+                            tokenizer=False)
+    t = synth.read_gguf(path)
+    W = np.asarray(t["text.output.weight"], np.float64)
+    g = np.asarray(t["text.output_norm.weight"], np.float64)
+    n = 40
+    xs = prompts(synth, t, n, 610, lo=10, hi=60)
+    miss = {}
+    for exact in ("1", "0"):
+        monkeypatch.setenv("QWENASR_B200_EXACT_ARGMAX", exact)
+        miss[exact] = 0
+        with decoder(pkg, path, w=1, kv=1, streams=n, ctx=128, batch_tokens=n * 64) as dec:
+            s = [dec.open() for _ in xs]
+            dec.prefill(s, xs)
+            for _ in range(6):
+                ids = dec.decode_step(s)
+                x = np.zeros((n, cfg["hidden"]), np.float32)
+                assert pkg.lib.qkv_debug_residual(dec.h, n, x.ctypes.data) == 0
+                xd = x.astype(np.float64)
+                h = xd / np.sqrt((xd * xd).mean(axis=1, keepdims=True) + cfg["rms_norm_eps"]) * g
+                want = np.argmax(h @ W.T, axis=1)
+                miss[exact] += int(np.sum(np.asarray(ids) != want))
+    print(f"rows whose id differs from the f32 argmax: re-scored {miss['1']}, bf16 logits only {miss['0']} (of {6 * n})")
+    assert miss["1"] == 0

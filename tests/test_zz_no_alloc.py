@@ -23,10 +23,10 @@ def _i32(a):
     return torch.tensor(np.asarray(a, np.int32), device="cuda")
 
 
-@pytest.mark.parametrize("kv", ["bf16", "f32", "fp8"])
+@pytest.mark.parametrize("kv", ["bf16", "f32", "fp8", "e4i8"])
 def test_noalloc_attention_matches_handle_path(pkg, kv):
-    kv_dtype = {"bf16": pkg.BF16, "f32": pkg.F32, "fp8": pkg.FP8}[kv]
-    elem = {"bf16": np.uint16, "f32": np.float32, "fp8": np.uint8}[kv]
+    kv_dtype = {"bf16": pkg.BF16, "f32": pkg.F32, "fp8": pkg.FP8, "e4i8": pkg.E4I8}[kv]
+    elem = {"bf16": np.uint16, "f32": np.float32, "fp8": np.uint8, "e4i8": np.uint8}[kv]
     rng = np.random.default_rng(21)
     n_layers = 1
     qn = (1.0 + 0.1 * rng.standard_normal((n_layers, D))).astype(np.float32)
@@ -74,11 +74,11 @@ def test_noalloc_attention_matches_handle_path(pkg, kv):
             t0, t1 = j * PT, min(L, (j + 1) * PT)
             pool[page, 0, :, : t1 - t0, :] = k[t0:t1].reshape(t1 - t0, HKV, D).transpose(1, 0, 2)
             pool[page, 1, :, : t1 - t0, :] = v[t0:t1].reshape(t1 - t0, HKV, D).transpose(1, 0, 2)
-            if kv == "fp8":
+            if kv in ("fp8", "e4i8"):
                 scales[page] = got[2][j]
-    view = {"bf16": np.int16, "f32": np.float32, "fp8": np.uint8}[kv]
+    view = {"bf16": np.int16, "f32": np.float32, "fp8": np.uint8, "e4i8": np.uint8}[kv]
     d_pool = torch.tensor(pool.view(view), device="cuda")
-    d_scales = torch.tensor(scales, device="cuda") if kv == "fp8" else None
+    d_scales = torch.tensor(scales, device="cuda") if kv in ("fp8", "e4i8") else None
     d_table = torch.tensor(table, device="cuda")
     d_rows = _i32(np.arange(len(lens)))
     err = C.create_string_buffer(256)
