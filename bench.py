@@ -38,10 +38,6 @@ METRIC = "decode tokens/s (KV append+GQA attn) & KV-read HBM GB/s vs 8 TB/s, 1-8
 # capture summarised in profiles/decode_attn_k2_config4.md (same 256 streams
 # and contexts; the capture held 2 layers of cache, a launch reads one).
 K2_NCU_TRAFFIC_BYTES = 1_017_933_000 + 5_662_720
-# e4m3 cache (profiles/decode_attn_k2_fp8_config4.md): the capture's launch read
-# 511,785,472 + wrote 7,432,704 bytes for 505,640,384 algorithmic bytes (2-layer
-# run, fewer appended tokens); scaled to a full run's 520,350,080 algorithmic bytes.
-K2_FP8_NCU_TRAFFIC_BYTES = round((511_785_472 + 7_432_704) * 520_350_080 / 505_640_384)
 
 
 def peaks() -> dict:
@@ -103,7 +99,9 @@ def qk_norm_weights(seed: int = 0):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled during the timed
+    region: through NVML every 5 ms (read-only queries), else nvidia-smi
+    every 0.2 s."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -115,7 +113,36 @@ class ClockSampler:
         self._stop = threading.Event()
         self._t = None
 
+    def _nvml_handle(self):
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            pr = torch.cuda.get_device_properties(self.gpu)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return None, None
+
     def _run(self):
+        nv, h = self._nvml_handle()
+        self.source = "nvml 5 ms" if h is not None else "nvidia-smi 0.2 s"
+        if h is not None:
+            bits = [("hw_slowdown", nv.nvmlClocksEventReasonHwSlowdown),
+                    ("hw_thermal_slowdown", nv.nvmlClocksEventReasonHwThermalSlowdown),
+                    ("sw_thermal_slowdown", nv.nvmlClocksEventReasonSwThermalSlowdown),
+                    ("sw_power_cap", nv.nvmlClocksEventReasonSwPowerCap)]
+            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            while not self._stop.is_set():
+                try:
+                    sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                    rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.rows.append([str(self.gpu), str(sm), str(mx), "", hex(rs)] +
+                                     ["Active" if rs & b else "Not Active" for _, b in bits])
+                except Exception:
+                    pass
+                self._stop.wait(0.005)
+            return
         while not self._stop.is_set():
             try:
                 out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
@@ -144,7 +171,7 @@ class ClockSampler:
         reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 5 + i and "Active" in r[5 + i]
                           and "Not" not in r[5 + i]})
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+                "reasons": reasons, "samples": len(self.rows), "sampler": getattr(self, "source", None)}
 
 
 def dist_setup(n_gpus: int):
@@ -354,7 +381,7 @@ def run_ours(args) -> int:
     ctx_tokens = int(cur_lens.sum().item())
     kv_bytes_per_launch = ctx_tokens * HKV * D * 2 * elem       # K and V, one layer
     if elem == 1:
-        kv_bytes_per_launch += sum((dec.length(s) + 15) // 16 for s in streams) * 2 * HKV * 4   # FP8 scales
+        kv_bytes_per_launch += sum((dec.length(s) + 15) // 16 for s in streams) * 2 * HKV * 16 * 4   # 8-bit scales: one per (token, head) of K and V
     achieved_gbs = kv_bytes_per_launch / (attn_ms / 1e3) / 1e9
     probe = read_probe(pkg, dec, streams, elem, st, attn_ms)
 
@@ -403,7 +430,7 @@ def run_ours(args) -> int:
             "kv_read_gbs_step": round(kv_bytes_per_launch * N_LAYERS / (ms_max / args.steps / 1e3) / 1e9, 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved_gbs / pk["hbm_gbs"], 4), "frac_of_8tbs": round(achieved_gbs / 8000, 4),
-                         "traffic": {"bf16": K2_NCU_TRAFFIC_BYTES, "fp8": K2_FP8_NCU_TRAFFIC_BYTES}.get(args.kv_dtype),
+                         "traffic": {"bf16": K2_NCU_TRAFFIC_BYTES}.get(args.kv_dtype),
                          "kernel": "decode_attn_kernel (K2)",
                          "launch_ms": round(attn_ms, 4), "bytes_per_launch": kv_bytes_per_launch,
                          "peak_source": pk["source"], "read_probe": probe,
@@ -808,7 +835,7 @@ def run_serve(args) -> int:
             "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16 weights, " + ("e4m3 K + int8 V" if args.serve_kv == "e4i8" else "e4m3 K and V") + " KV",
             "data": "synthetic",
-            "config": {"workload": "config5: Qwen3-ASR-1.7B, 8-bit paged KV (per-page-per-head scales), Poisson arrivals, "
+            "config": {"workload": "config5: Qwen3-ASR-1.7B, 8-bit paged KV (f32 scale per stored token and head), Poisson arrivals, "
                                    "audio 65-780 rows + 20 text tokens, outputs 32-512 tokens",
                        "kv_cache": args.serve_kv,
                        "target_concurrency": conc, "mean_concurrency": round(float(np.mean(conc_seen)), 1),

@@ -50,9 +50,10 @@ enum qkv_status {
 enum qkv_dtype {
     QKV_F32 = 0,
     QKV_BF16 = 1,
-    QKV_FP8_E4M3 = 2,          /* KV cache only: e4m3 values, fp32 scale per (page, K|V, kv head) */
+    QKV_FP8_E4M3 = 2,          /* KV cache only: e4m3 values; fp32 scale per stored (token, kv head)
+                                  vector of K and of V: [n_pages][2][8][16], value = code x scale */
     QKV_E4M3K_I8V = 3          /* KV cache only: K in e4m3, V in int8 stored as excess-128 bytes
-                                  (byte u holds (u - 128) x scale), fp32 scale per (page, K|V, kv head) */
+                                  (byte u holds (u - 128) x scale); scales as for QKV_FP8_E4M3 */
 };
 
 /* Decoder hyper-parameters (GGUF keys qwen3-asr.text.*).
@@ -264,7 +265,7 @@ int qkv_fill_random(qkv_handle *h, uint64_t seed);
 /* Page gather: copy tokens [0, len) of one stream's layer cache to host as
  * contiguous k[len][Hkv*D] and v[len][Hkv*D] in the cache dtype (8-bit
  * caches: the raw bytes, e4m3 or excess-128 int8; scales via
- * scales_out[n_pages][2][Hkv] when non-NULL). */
+ * scales_out[n_pages][2][Hkv][16] when non-NULL). */
 int qkv_gather(qkv_handle *h, int32_t layer, int32_t stream_id, void *k_host, void *v_host,
                float *scales_out);
 
@@ -314,8 +315,8 @@ int qkv_last_launches(const qkv_handle *h, int64_t *kernels);
  * framework's back breaks its accounting or is not allowed.  This entry point
  * has no counterpart in the reference.  The caller passes everything as device
  * pointers: one layer's pool ([n_pages][2][8][16][128] elements of kv_dtype),
- * its 8-bit scales ([n_pages][2][8] f32, or NULL unless kv_dtype is one of
- * the 8-bit caches), the
+ * its 8-bit scales ([n_pages][2][8][16] f32, or NULL unless kv_dtype is one
+ * of the 8-bit caches), the
  * page table [max_streams][maxp], and per-row slots, lengths (tokens to
  * attend over), queries [n][2048] f32 and outputs [n][2048] f32.  No call
  * allocates: the kernel's scratch is a fixed ~3.5 MB array inside this

@@ -463,7 +463,7 @@ class Decoder:
         k = np.zeros((n, 1024), dt)
         v = np.zeros((n, 1024), dt)
         npg = (n + 15) // 16
-        scales = np.zeros((npg, 2, 8), np.float32)
+        scales = np.zeros((npg, 2, 8, 16), np.float32)   # 8-bit caches: one scale per (page, K|V, head, token)
         self._check(lib.qkv_gather(self.h, layer, s, k.ctypes.data, v.ctypes.data,
                                    _ptr(scales, C.c_float) if kv_dtype in (FP8, E4I8) else None))
         return (k, v, scales) if kv_dtype in (FP8, E4I8) else (k, v)

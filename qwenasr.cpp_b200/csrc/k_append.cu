@@ -149,9 +149,19 @@ __global__ void __launch_bounds__(512) kv_append_kernel(AppendParams p) {
     const int tok = pos & (kPageTokens - 1);
     float inv_scale = 1.0f;
     if constexpr (sizeof(TC) == 1) {
-        // FP8: the (page, kv, head) scale was settled for this batch by
-        // fp8_page_scale_kernel, which ran just before on the same stream.
-        inv_scale = 1.0f / p.scales[(static_cast<size_t>(page) * 2 + kv) * kHkv + g];
+        // 8-bit caches: every stored (token, head) vector gets its own scale,
+        // amax / qmax over its 128 elements (K after norm and RoPE, V raw), so
+        // no stored token is ever re-quantised and no headroom is kept.
+        float amax = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(x[j]));
+#pragma unroll
+        for (int o = 8; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float qmax = (kv == 1 && p.v_int8) ? kI8Max : kE4m3Max;
+        const float scale = amax > 0.0f ? __fdiv_rn(amax, qmax) : 1.0f;
+        inv_scale = amax > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
+        if (l16 == 0)
+            p.scales[((static_cast<size_t>(page) * 2 + kv) * kHkv + g) * kPageTokens + tok] = scale;
     }
     TC *pool = static_cast<TC *>(p.pool);
     TC *dst = pool + ((static_cast<size_t>(page) * 2 + kv) * kHkv + g) * (kPageTokens * kHeadDim) +
@@ -163,110 +173,6 @@ __global__ void __launch_bounds__(512) kv_append_kernel(AppendParams p) {
         }
     }
     PageStore<TC>::put(dst, x, inv_scale);
-}
-
-// 8-bit page scales.  One CTA per page touched by the batch (group = the
-// batch's consecutive rows of one stream inside one page), 16 half-warp units
-// = (K | V) x 8 kv heads.  Each unit takes the absolute maximum of its head
-// over the group's new tokens (K after norm + RoPE, V raw); if the page
-// already holds tokens and the new maximum fits the current scale the scale is
-// kept, otherwise the scale becomes amax / qmax x headroom and the tokens
-// already stored are re-quantised to it.  K1 then stores the new tokens with
-// the settled scale.  e4m3 (qmax 448): headroom x2 while the page will take
-// more tokens, which costs nothing in a floating-point format.  int8 V (qmax
-// 127): headroom x1.25, since every bit of headroom is a bit of precision
-// lost; a page filled in one batch (prefill) gets no headroom either way.
-__global__ void __launch_bounds__(256) fp8_page_scale_kernel(AppendParams p) {
-    pdl_trigger();
-    pdl_wait();   // everything below reads or writes memory of earlier kernels
-    // CTA per row; only the first row of each page group works (block-uniform exit).
-    const int row0 = blockIdx.x;
-    const int slot = p.slots[row0], pos0 = p.positions[row0];
-    if (row0 > 0 && p.slots[row0 - 1] == slot && p.positions[row0 - 1] == pos0 - 1 && (pos0 & (kPageTokens - 1)) != 0)
-        return;
-    if (slot < 0 || slot >= p.max_streams || pos0 < 0 || pos0 / kPageTokens >= p.maxp) return;   // K1 reports it
-    int cnt = 1;
-    while (row0 + cnt < p.n && cnt < kPageTokens && p.slots[row0 + cnt] == slot &&
-           p.positions[row0 + cnt] == pos0 + cnt && ((pos0 + cnt) & (kPageTokens - 1)) != 0)
-        ++cnt;
-    const int page = p.page_table[static_cast<size_t>(slot) * p.maxp + pos0 / kPageTokens];
-    const int tok0 = pos0 & (kPageTokens - 1);
-    const int unit = threadIdx.x >> 4, l16 = threadIdx.x & 15;   // unit 0..7 K heads, 8..15 V heads
-    const int kv = unit >> 3, g = unit & 7;
-    if (page < 0 || page >= p.n_pages) {
-        if (threadIdx.x == 0) report_error(p.err, kErrPageIndex, kWhereAppend, row0, page);
-        return;
-    }
-    float amax = 0.0f;
-    // The group's rows hold positions pos0 .. pos0 + cnt - 1.  Rows are loaded
-    // four at a time before any is normalised (a batch past the group's end
-    // repeats its last row, which leaves the maximum unchanged).
-    const int src_off = kQDim + kv * kKvDim + g * kHeadDim + l16 * 8;
-    for (int r0 = 0; r0 < cnt; r0 += 4) {
-        float x[4][8];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int r = r0 + k < cnt ? r0 + k : cnt - 1;
-            const float *src = p.qkv + static_cast<size_t>(row0 + r) * kQkvDim + src_off;
-            const float4 a = reinterpret_cast<const float4 *>(src)[0];
-            const float4 b = reinterpret_cast<const float4 *>(src)[1];
-            x[k][0] = a.x; x[k][1] = a.y; x[k][2] = a.z; x[k][3] = a.w;
-            x[k][4] = b.x; x[k][5] = b.y; x[k][6] = b.z; x[k][7] = b.w;
-        }
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            if (kv == 0) {   // warp-uniform: warps 0..3 hold K units
-                const int pos = pos0 + (r0 + k < cnt ? r0 + k : cnt - 1);
-                const int safe_pos = pos < p.rope_len ? pos : 0;
-                norm_rope8(x[k], p.k_norm_w + l16 * 8,
-                           p.rope + static_cast<size_t>(safe_pos) * (kHeadDim / 2) + (l16 & 7) * 8, l16, p.eps);
-            }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(x[k][j]));
-        }
-    }
-#pragma unroll
-    for (int o = 8; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    float *sc = p.scales + (static_cast<size_t>(page) * 2 + kv) * kHkv + g;
-    const float old_scale = *sc;
-    const bool has_old = tok0 > 0;
-    const bool fills_page = tok0 + cnt == kPageTokens;
-    const bool i8 = kv == 1 && p.v_int8;   // uniform over the half-warp unit
-    const float qmax = i8 ? kI8Max : kE4m3Max;
-    if (has_old && amax <= qmax * old_scale) return;   // current scale still covers the new tokens
-    const float head = fills_page ? 1.0f : (i8 ? 1.25f : 2.0f);
-    const float new_scale = fmaxf(fmaxf(amax, has_old ? qmax * old_scale : 0.0f) * head / qmax, 1e-30f);
-    if (has_old) {
-        // re-quantise the tokens already in the page to the new scale
-        uint8_t *pool = static_cast<uint8_t *>(p.pool);
-        uint8_t *base = pool + ((static_cast<size_t>(page) * 2 + kv) * kHkv + g) * (kPageTokens * kHeadDim) + l16 * 8;
-        const float ratio = old_scale / new_scale;
-        for (int t = 0; t < tok0; ++t) {
-            uint2 w = *reinterpret_cast<uint2 *>(base + t * kHeadDim);
-            uint32_t lo = 0, hi = 0;
-            if (i8) {
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    lo |= f_to_u8ex(u8ex_to_f((w.x >> (8 * j)) & 0xffu) * ratio) << (8 * j);
-                    hi |= f_to_u8ex(u8ex_to_f((w.y >> (8 * j)) & 0xffu) * ratio) << (8 * j);
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float2 f = e4m3x2_to_f2(static_cast<uint16_t>(((j < 2 ? w.x : w.y) >> (16 * (j & 1))) & 0xffffu));
-                    const uint32_t q0 = f_to_e4m3(f.x * ratio), q1 = f_to_e4m3(f.y * ratio);
-                    const uint32_t pair = q0 | (q1 << 8);
-                    if (j < 2) lo |= pair << (16 * j);
-                    else hi |= pair << (16 * (j - 2));
-                }
-            }
-            *reinterpret_cast<uint2 *>(base + t * kHeadDim) = make_uint2(lo, hi);
-        }
-    }
-    // Only this half-warp unit takes this path (the other half of the warp
-    // may have returned above).
-    __syncwarp(0xffffu << (threadIdx.x & 16));
-    if (l16 == 0) *sc = new_scale;
 }
 
 // Page gather: tokens [0, len) of one stream -> contiguous [len][Hkv*D] (K and V).
@@ -308,7 +214,7 @@ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
 }
 
 // Seeded N(0,1) fill of the given pages (Box-Muller on a counter hash).
-// 8-bit caches: scale 8 / qmax per (page, K|V, head); v_int8 stores V as int8.
+// 8-bit caches: scale 8 / qmax per (page, K|V, head, token); v_int8 stores V as int8.
 template <typename TC>
 __global__ void page_fill_kernel(TC *pool, float *scales, const int *pages, int n, uint64_t seed, int v_int8) {
     const size_t per_page = static_cast<size_t>(2) * kPageHalfElems;
@@ -326,19 +232,16 @@ __global__ void page_fill_kernel(TC *pool, float *scales, const int *pages, int 
             else base[e] = f_to_e4m3(z * (kE4m3Max / 8.0f));
         }
         if constexpr (sizeof(TC) == 1) {
-            if (blockIdx.x == 0 && threadIdx.x < 2 * kHkv)
-                scales[static_cast<size_t>(page) * 2 * kHkv + threadIdx.x] =
-                    8.0f / (v_int8 && threadIdx.x >= kHkv ? kI8Max : kE4m3Max);
+            if (blockIdx.x == 0) {
+                for (int i = threadIdx.x; i < kPageScales; i += blockDim.x)
+                    scales[static_cast<size_t>(page) * kPageScales + i] =
+                        8.0f / (v_int8 && i >= kPageScales / 2 ? kI8Max : kE4m3Max);
+            }
         }
     }
 }
 
 }  // namespace
-
-cudaError_t launch_fp8_page_scale(const AppendParams &p, cudaStream_t st) {
-    if (p.n <= 0) return cudaSuccess;
-    return launch_pdl(fp8_page_scale_kernel, dim3(p.n), dim3(256), 0, st, p);
-}
 
 cudaError_t launch_kv_append(const AppendParams &p, int kv_dtype, cudaStream_t st) {
     if (p.n <= 0) return cudaSuccess;
@@ -349,8 +252,6 @@ cudaError_t launch_kv_append(const AppendParams &p, int kv_dtype, cudaStream_t s
         case kKvE4I8: {
             AppendParams q = p;
             q.v_int8 = kv_dtype == kKvE4I8 ? 1 : 0;
-            const cudaError_t e = launch_fp8_page_scale(q, st);
-            if (e != cudaSuccess) return e;
             return launch_pdl(kv_append_kernel<uint8_t>, dim3(q.n), dim3(512), 0, st, q);
         }
         default: return cudaErrorInvalidValue;

@@ -59,7 +59,7 @@ template <typename TC> __host__ __device__ constexpr uint32_t stage_bytes() {
 template <typename TC> __host__ __device__ constexpr size_t smem_bytes() {
     return static_cast<size_t>(AttnTraits<TC>::NS) * stage_bytes<TC>()    // stages
            + 2 * AttnTraits<TC>::NS * sizeof(uint64_t)                      // full/empty barriers
-           + AttnTraits<TC>::NS * 2 * kHkv * sizeof(float)                  // fp8 scales per stage
+           + AttnTraits<TC>::NS * kPageScales * sizeof(float)               // 8-bit scales per stage
            + consumers<TC>() * 2 * AttnTraits<TC>::CH * sizeof(float)       // p exchange (16B aligned)
            + kHkv * 32 * 8 * sizeof(float)                                  // half-warp O hand-over
            + kHkv * 4 * sizeof(float)                                       // half-warp (m, l) hand-over
@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + static_cast<size_t>(NS) * stage_bytes<TC>());
     uint64_t *empty = full + NS;
     float *sscale = reinterpret_cast<float *>(empty + NS);
-    float *pbuf = sscale + NS * 2 * kHkv;                                  // [kConsumers][2*CH]
+    float *pbuf = sscale + NS * kPageScales;                               // [kConsumers][2*CH]
     float *xo = pbuf + kConsumers * 2 * CH;                                // [kHkv][32 lanes][8]
     float *xml = xo + kHkv * 32 * 8;                                       // [kHkv][m_a, l_a, m_b, l_b]
     int *row_start = reinterpret_cast<int *>(xml + kHkv * 4);             // [kAttnMaxRows + 1]
@@ -356,11 +356,13 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
                                     // K and V halves of a page are contiguous: one copy (a CTA
                                     // issues bulk copies at a bounded rate, so bytes per copy count).
                                     constexpr uint32_t half_bytes = HALF * sizeof(TC);
-                                    mbar_arrive_expect_tx(&full[s], 2 * half_bytes + (kFp8 ? 64u : 0u));
+                                    constexpr uint32_t scale_bytes = kFp8 ? kPageScales * sizeof(float) : 0u;
+                                    mbar_arrive_expect_tx(&full[s], 2 * half_bytes + scale_bytes);
                                     bulk_g2s(dst, pool + kbase, 2 * half_bytes, &full[s], pol);
                                     if constexpr (kFp8) {
-                                        bulk_g2s(sscale + s * 2 * kHkv, p.scales + static_cast<size_t>(page) * 2 * kHkv,
-                                                 64u, &full[s], pol);
+                                        bulk_g2s(sscale + s * kPageScales,
+                                                 p.scales + static_cast<size_t>(page) * kPageScales, scale_bytes,
+                                                 &full[s], pol);
                                     }
                                 } else {
                                     constexpr uint32_t rows_bytes = CH * kHeadDim * sizeof(TC);
@@ -480,10 +482,20 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
                 if (nvalid > 0) {
                     const TC *kst = stages + static_cast<size_t>(s) * (2 * HALF) + g * CH * kHeadDim;
                     const TC *vst = kst + HALF;
-                    float sk = 1.0f, sv = 1.0f;
+                    // 8-bit caches: the lane's token's K scale, and its V scale as a
+                    // ratio to the largest V scale of the chunk's valid tokens (the
+                    // ratio goes into p, the largest scale multiplies the chunk's sum).
+                    float sk = 1.0f, sv = 1.0f, sv_ratio = 1.0f;
                     if constexpr (kFp8) {
-                        sk = sscale[s * 2 * kHkv + g];
-                        sv = sscale[s * 2 * kHkv + kHkv + g];
+                        const float *ss = sscale + s * kPageScales + g * kPageTokens;
+                        sk = ss[my_tok];
+                        const float sv_t = my_tok < nvalid ? ss[kHkv * kPageTokens + my_tok] : 0.0f;
+                        sv = sv_t;
+#pragma unroll
+                        for (int o = 1; o < 32; o <<= 1) {
+                            if (o != HB) sv = fmaxf(sv, __shfl_xor_sync(0xffffffffu, sv, o));
+                        }
+                        sv_ratio = sv > 0.0f ? __fdividef(sv_t, sv) : 0.0f;
                     }
                     // ---- QK ----
                     float part[NV];
@@ -539,7 +551,7 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
                     l_run = l_run * alpha + ps;
                     m_run = m_new;
                     if constexpr (kFp8) {
-                        reinterpret_cast<__half *>(my_p)[my_head * CH + my_tok] = __float2half_rn(pv);
+                        reinterpret_cast<__half *>(my_p)[my_head * CH + my_tok] = __float2half_rn(pv * sv_ratio);
                     } else {
                         my_p[my_head * CH + my_tok] = pv;
                     }

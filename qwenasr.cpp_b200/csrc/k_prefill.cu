@@ -109,9 +109,10 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(PrefillAttnParams p) 
                     db = fmaf(qs[g][1][d0 + e], kv[e], db);
                 }
             }
-            if constexpr (sizeof(TC) == 1) {
-                sk = p.scales[(static_cast<size_t>(page) * 2 + 0) * kHkv + g];
-                sv = p.scales[(static_cast<size_t>(page) * 2 + 1) * kHkv + g];
+            if constexpr (sizeof(TC) == 1) {   // the key's own (token, head) scales
+                const size_t si = (static_cast<size_t>(page) * 2 * kHkv + g) * kPageTokens + key % kPageTokens;
+                sk = p.scales[si];
+                sv = p.scales[si + kHkv * kPageTokens];
             }
             sa = da * sk;
             sb = db * sk;

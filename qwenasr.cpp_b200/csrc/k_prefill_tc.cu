@@ -64,7 +64,7 @@ struct K3Params {
     void *out;              // [rows][2048]
     int out_bf16;
     const void *pool;
-    const float *scales;    // e4m3 cache: [pages][2][8]
+    const float *scales;    // 8-bit caches: [pages][2][8][16]
     const int *page_table;
     int maxp;
     int max_streams;
@@ -274,7 +274,9 @@ __device__ __forceinline__ void store_tile(const K3Params &p, uint8_t *tile, con
         } else {
             // 16 e4m3 = dims 16c .. 16c+15 -> f16 chunks 2c (dims 16c..+7) and 2c+1
             const bool valid = pg[m] >= 0 && pg[m] < p.n_pages;
-            const float sc = __ldg(p.scales + (static_cast<size_t>(valid ? pg[m] : 0) * 2 + kv) * kHkv + g);
+            // the row's own (token, head) scale; row r of the tile is token r % 16 of its page
+            const float sc = __ldg(p.scales + ((static_cast<size_t>(valid ? pg[m] : 0) * 2 + kv) * kHkv + g) * kPageTokens +
+                                   (r & (kPageTokens - 1)));
             const uint32_t s2 = pack_h2(sc, sc);
             const uint32_t ws[4] = {tr.w[m].x, tr.w[m].y, tr.w[m].z, tr.w[m].w};
             const bool i8 = kv == 1 && p.v_int8;

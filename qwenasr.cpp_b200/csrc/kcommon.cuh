@@ -22,6 +22,8 @@ constexpr int kQDim = kHq * kHeadDim;                   // 2048
 constexpr int kKvDim = kHkv * kHeadDim;                 // 1024
 // Elements of one (page, K|V) block: [kHkv][kPageTokens][kHeadDim].
 constexpr int kPageHalfElems = kHkv * kPageTokens * kHeadDim;   // 16384
+// 8-bit caches: one f32 scale per (page, K|V, kv head, token) = 256 per page.
+constexpr int kPageScales = 2 * kHkv * kPageTokens;
 
 // Device error word: first error wins.  The host reads it after a sync.
 struct DevError {

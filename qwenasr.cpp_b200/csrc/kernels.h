@@ -49,7 +49,8 @@ enum ActDtype { kActF32 = 0, kActBF16 = 1 };
 constexpr int kAttnMaxRows = 1024;   // rows (streams) per decode-attention launch
 
 // Pool layout of one layer: [n_pages][2 (K,V)][kHkv][kPageTokens][kHeadDim]
-// elements of the cache dtype; FP8 scales: [n_pages][2][kHkv] f32.
+// elements of the cache dtype; 8-bit scales: [n_pages][2][kHkv][kPageTokens]
+// f32, one per stored (token, head) vector: value = code x scale.
 struct AppendParams {
     int n;                     // rows
     const int *slots;          // [n] stream ids (page-table rows)
@@ -117,9 +118,6 @@ struct PrefillAttnParams {
 };
 
 cudaError_t launch_kv_append(const AppendParams &p, int kv_dtype, cudaStream_t st);
-// FP8 cache: settle each touched page's per-(kv, head) scale before K1 stores
-// (launch_kv_append runs it first for the FP8 cache).
-cudaError_t launch_fp8_page_scale(const AppendParams &p, cudaStream_t st);
 cudaError_t prepare_decode_attn();
 size_t attn_smem_bytes(int kv_dtype);
 cudaError_t launch_decode_attn(const AttendParams &p, int kv_dtype, bool out_bf16, int grid, cudaStream_t st);

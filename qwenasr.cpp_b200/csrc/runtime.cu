@@ -146,7 +146,7 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
     CK(cudaMalloc(&h->pool, h->pool_layer_bytes * c.n_layers));
     CK(cudaMemsetAsync(h->pool, 0, h->pool_layer_bytes * c.n_layers, h->stream));
     if (kv_is_8bit(h->rt.kv_dtype)) {
-        h->scales_layer_elems = static_cast<size_t>(h->n_pages) * 2 * kHkv;
+        h->scales_layer_elems = static_cast<size_t>(h->n_pages) * kPageScales;
         CK(cudaMalloc(&h->scales, h->scales_layer_elems * c.n_layers * sizeof(float)));
         std::vector<float> ones(h->scales_layer_elems * c.n_layers, 1.0f);
         CK(cudaMemcpy(h->scales, ones.data(), ones.size() * sizeof(float), cudaMemcpyHostToDevice));
@@ -1044,7 +1044,7 @@ int qkv_compact(qkv_handle *h, int64_t *moved) {
             CK(launch_page_copy(static_cast<uint8_t *>(h->pool) + h->pool_layer_bytes * static_cast<size_t>(l),
                                 h->page_bytes, d_moves, d_moves + src.size(), static_cast<int>(src.size()), h->stream));
             if (h->scales) {
-                CK(launch_page_copy(h->scales + h->scales_layer_elems * static_cast<size_t>(l), 2 * kHkv * sizeof(float),
+                CK(launch_page_copy(h->scales + h->scales_layer_elems * static_cast<size_t>(l), kPageScales * sizeof(float),
                                     d_moves, d_moves + src.size(), static_cast<int>(src.size()), h->stream));
             }
         }
@@ -1691,10 +1691,10 @@ int qkv_gather(qkv_handle *h, int32_t layer, int32_t stream_id, void *k_host, vo
     CK(cudaMemcpyAsync(v_host, d + bytes, bytes, cudaMemcpyDeviceToHost, h->stream));
     if (scales_out && h->scales) {
         for (size_t i = 0; i < pg->size(); ++i) {
-            CK(cudaMemcpyAsync(scales_out + i * 2 * kHkv,
+            CK(cudaMemcpyAsync(scales_out + i * kPageScales,
                                h->scales + h->scales_layer_elems * static_cast<size_t>(layer) +
-                                   static_cast<size_t>((*pg)[i]) * 2 * kHkv,
-                               2 * kHkv * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+                                   static_cast<size_t>((*pg)[i]) * kPageScales,
+                               kPageScales * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
         }
     }
     return check_device_error(h);

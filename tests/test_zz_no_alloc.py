@@ -62,7 +62,7 @@ def test_noalloc_attention_matches_handle_path(pkg, kv):
     maxp = max(need)
     order = rng.permutation(n_pages)
     pool = np.zeros((n_pages, 2, HKV, PT, D), elem)
-    scales = np.ones((n_pages, 2, HKV), np.float32)
+    scales = np.ones((n_pages, 2, HKV, PT), np.float32)
     table = np.full((len(lens), maxp), -1, np.int32)
     nxt = 0
     for i, (L, got) in enumerate(zip(lens, gathered)):
