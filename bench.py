@@ -575,7 +575,8 @@ def run_model(args) -> int:
     else:
         prompts = synth.config2_prompts(embd, n_streams, seed=1002, gpu=rank)
     max_ctx = max(p.shape[0] for p in prompts) + args.warmup + steps + 8
-    rt = pkg.runtime_config(device=local, weight_dtype=pkg.BF16, kv_dtype=pkg.BF16, max_streams=n_streams,
+    wdt = {"bf16": pkg.BF16, "fp8": pkg.FP8}[args.weights]
+    rt = pkg.runtime_config(device=local, weight_dtype=wdt, kv_dtype=pkg.BF16, max_streams=n_streams,
                             max_context=max_ctx, max_batch_tokens=sum(p.shape[0] for p in prompts),
                             page_order_seed=1002 + rank)
     dec = pkg.Decoder.from_gguf(path, rt, cfg)
@@ -660,8 +661,11 @@ def run_model(args) -> int:
             "metric": f"greedy decode tokens/s (full {'1.7B' if big else '0.6B'} step: KV path + projections + LM head)",
             "value": round(tokens / dt_max, 2), "unit": "tokens/s", "n_gpus": world, "steps": steps,
             "warmup": args.warmup, "ms_per_step": round(dt_max / steps * 1e3, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": ("config3: Qwen3-ASR-1.7B bf16 weights + bf16 paged KV, 64 streams/GPU, "
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16" if args.weights == "bf16" else "fp8 projections (e4m3), bf16 elsewhere",
+            "data": "synthetic",
+            "config": {"weights": args.weights,
+                       "workload": ("config3: Qwen3-ASR-1.7B bf16 weights + bf16 paged KV, 64 streams/GPU, "
                                     "390 audio rows + 20 text tokens, greedy decode") if big else
                                    ("config2: Qwen3-ASR-0.6B bf16 weights + bf16 paged KV, 32 streams/GPU, "
                                     "prompts U[100,400] (90% audio rows), greedy decode"),
@@ -712,7 +716,8 @@ def run_serve(args) -> int:
     max_ctx = 780 + text_tokens + out_hi + 8
     slots_cap = conc + 128
     serve_kv = {"e4i8": pkg.E4I8, "fp8": pkg.FP8}[args.serve_kv]
-    rt = pkg.runtime_config(device=local, weight_dtype=pkg.BF16, kv_dtype=serve_kv, max_streams=slots_cap,
+    rt = pkg.runtime_config(device=local, weight_dtype={"bf16": pkg.BF16, "fp8": pkg.FP8}[args.weights],
+                            kv_dtype=serve_kv, max_streams=slots_cap,
                             max_context=max_ctx, max_pages=slots_cap * ((max_ctx + 15) // 16),
                             max_batch_tokens=32768, page_order_seed=1005 + rank)
     dec = pkg.Decoder.from_gguf(path, rt, cfg)
@@ -962,16 +967,26 @@ def run_gemm(args) -> int:
     dev = torch.device("cuda", local)
     rows, tot_flop, tot_ms = [], 0.0, 0.0
     reps = 20
+    f8 = args.weights == "fp8"
     for M in (32, 64, 1024):
         for name, (N, K) in GEMM_SHAPES.items():
-            ws = [torch.randn(N, K, device=dev).to(torch.bfloat16) for _ in range(4)]
-            x = torch.randn(M, K, device=dev).to(torch.bfloat16)
+            if f8:   # e4m3 codes + one scale per row (the scales' values do not change the timing)
+                ws = [torch.randint(0, 120, (N, K), device=dev, dtype=torch.uint8) for _ in range(4)]
+                x = torch.randint(0, 120, (M, K), device=dev, dtype=torch.uint8)
+                w_s, x_s = torch.ones(N, device=dev), torch.ones(M, device=dev)
+            else:
+                ws = [torch.randn(N, K, device=dev).to(torch.bfloat16) for _ in range(4)]
+                x = torch.randn(M, K, device=dev).to(torch.bfloat16)
             c = torch.empty(M, N, device=dev)
 
             def call(i, st):
-                rc = pkg.lib.qkv_gemm_bf16(x.data_ptr(), ws[i % 4].data_ptr(), c.data_ptr(), M, N, K, 0, st)
+                if f8:
+                    rc = pkg.lib.qkv_gemm_fp8(x.data_ptr(), x_s.data_ptr(), ws[i % 4].data_ptr(), w_s.data_ptr(),
+                                              c.data_ptr(), M, N, K, 0, st)
+                else:
+                    rc = pkg.lib.qkv_gemm_bf16(x.data_ptr(), ws[i % 4].data_ptr(), c.data_ptr(), M, N, K, 0, st)
                 if rc != 0:
-                    raise RuntimeError(f"qkv_gemm_bf16 failed: {rc}")
+                    raise RuntimeError(f"projection GEMM failed: {rc}")
 
             for i in range(args.warmup):
                 call(i, torch.cuda.current_stream(dev).cuda_stream)
@@ -995,21 +1010,24 @@ def run_gemm(args) -> int:
             tot_ms += ms
             rows.append({"M": M, "shape": name, "N": N, "K": K, "us": round(ms * 1e3, 2),
                          "tflops": round(fl / (ms / 1e3) / 1e12, 1),
-                         "weight_gbs": round(N * K * 2 / (ms / 1e3) / 1e9, 1)})
+                         "weight_gbs": round(N * K * (1 if f8 else 2) / (ms / 1e3) / 1e9, 1)})
             del graph
     pk = peaks()
     value = tot_flop / (tot_ms / 1e3) / 1e12
     if rank == 0:
         line = {
-            "metric": "projection GEMM TFLOP/s (tcgen05, bf16 x bf16 -> f32)", "value": round(value, 2),
+            "metric": "projection GEMM TFLOP/s (tcgen05, " + ("e4m3 x e4m3" if f8 else "bf16 x bf16") + " -> f32)",
+            "value": round(value, 2),
             "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(tot_ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic",
+            "dtype": "e4m3" if f8 else "bf16", "data": "synthetic",
             "config": {"workload": "decoder projections of 0.6B and 1.7B at M = 32, 64, 1024 tokens; "
                                    "20 launches per CUDA graph, 4 weight copies", "shapes": rows},
-            "roofline": {"bound": "tensor", "achieved": round(value, 1), "peak": pk["bf16_tflops"],
-                         "unit": "TFLOP/s", "frac": round(value / pk["bf16_tflops"], 4), "traffic": None,
-                         "kernel": "gemm_tc_kernel", "peak_source": pk["source"]},
+            "roofline": {"bound": "tensor", "achieved": round(value, 1),
+                         "peak": pk["bf16_tflops"] * (2 if f8 else 1), "unit": "TFLOP/s",
+                         "frac": round(value / (pk["bf16_tflops"] * (2 if f8 else 1)), 4), "traffic": None,
+                         "kernel": "gemm_tc_kernel",
+                         "peak_source": pk["source"] + (" bf16 x 2 (the nominal fp8/bf16 ratio)" if f8 else "")},
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
@@ -1040,6 +1058,9 @@ def main() -> int:
                     help="serve: 8-bit cache (e4i8 = e4m3 K + int8 V, fp8 = e4m3 K and V)")
     ap.add_argument("--kv-dtype", choices=("bf16", "fp8", "e4i8", "f32"), default="bf16",
                     help="kv workload: cache dtype (bf16 is the config-4 workload)")
+    ap.add_argument("--weights", choices=("bf16", "fp8"), default="bf16",
+                    help="model / model3 / serve: projection weights (fp8 = e4m3 weights and token rows, "
+                         "one scale per row, tcgen05 kind::f8f6f4)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="layers of cache (28 = the workload; fewer only for small profiling captures)")

@@ -75,7 +75,10 @@ typedef struct qkv_model_config {
  * max_seq_len (text-decoder.h:101-116) with a paged pool. */
 typedef struct qkv_runtime_config {
     int32_t device;            /* CUDA device ordinal */
-    int32_t weight_dtype;      /* QKV_F32 or QKV_BF16 (f32 GGUF values are rounded RNE) */
+    int32_t weight_dtype;      /* QKV_F32, QKV_BF16 (f32 GGUF values are rounded RNE) or
+                                  QKV_FP8_E4M3: the four projections of every layer in e4m3
+                                  with one f32 scale per weight row, their inputs quantised to
+                                  e4m3 per token row (embeddings, LM head: bf16) */
     int32_t kv_dtype;          /* QKV_F32, QKV_BF16, QKV_FP8_E4M3 or QKV_E4M3K_I8V */
     int32_t page_tokens;       /* tokens per page; must be 16 */
     int32_t max_streams;       /* stream slots */
@@ -222,6 +225,21 @@ int qkv_kv_attend(qkv_handle *h, int32_t layer, int32_t n, const int32_t *slots_
  * 469-472, 476-493).  Device pointers, current device, `stream` as above. */
 int qkv_gemm_bf16(const void *x, const void *w, float *c, int32_t m, int32_t n, int32_t k, int32_t accumulate,
                   void *stream);
+
+/* Operator: the FP8 form of the projections, on the tensor cores (tcgen05
+ * kind::f8f6f4, e4m3 x e4m3 products accumulated in f32): C[m][n] (+)=
+ * (X[m][k] x x_scale[m]) . (W[n][k] x w_scale[n])^T, X and W e4m3 codes
+ * row-major, one f32 scale per row of each; k a multiple of 128.  A
+ * B200-side weight format with no counterpart in the reference, whose
+ * projections are f32 (text-decoder.cpp:371-373, 465, 469-472).  Device
+ * pointers, current device, `stream` as above. */
+int qkv_gemm_fp8(const void *x, const float *x_scale, const void *w, const float *w_scale, float *c, int32_t m,
+                 int32_t n, int32_t k, int32_t accumulate, void *stream);
+
+/* Rows of bf16 values [rows][k] -> e4m3 codes [rows][k] and one f32 scale per
+ * row (amax / 448; 1 for an all-zero row): the quantiser the FP8 weights and
+ * token rows go through.  Device pointers, `stream` as above. */
+int qkv_quantize_rows_e4m3(const void *x_bf16, int32_t rows, int32_t k, void *codes, float *scales, void *stream);
 
 /* Causal prefill attention over one layer's paged cache (K3 on tcgen05 for
  * bf16/e4m3 caches, the CUDA-core kernel for f32): for each of the n streams

@@ -88,6 +88,8 @@ SIGNATURES = {
     "qkv_kv_attend_noalloc": (C.c_int, [_P, C.c_int32, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, _P,
                                         _P, _P, _P, C.c_char_p, C.c_size_t]),
     "qkv_gemm_bf16": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P]),
+    "qkv_gemm_fp8": (C.c_int, [_P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P]),
+    "qkv_quantize_rows_e4m3": (C.c_int, [_P, C.c_int32, C.c_int32, _P, _P, _P]),
     "qkv_prefill_attend": (C.c_int, [_P, C.c_int32, C.c_int32, _P, _P, _P, _P, _P]),
     "qkv_prefill_attend_q16": (C.c_int, [_P, C.c_int32, C.c_int32, _P, _P, _P, _P, _P]),
     "qkv_tokenizer_open": (C.c_int, [C.c_char_p, C.POINTER(C.c_void_p), C.c_char_p, C.c_size_t]),
@@ -227,7 +229,7 @@ def gguf_tensor(path, name: str, want_data: bool = True):
     dims = [ne[i] for i in range(nd.value)]
     data = None
     if want_data:
-        es = {0: 4, 1: 2, 30: 2}.get(ty.value, 0)
+        es = {0: 4, 1: 2, 24: 1, 30: 2}.get(ty.value, 0)
         nbytes = int(np.prod(dims)) * es
         buf = np.zeros(nbytes, np.uint8)
         rc = lib.qkv_gguf_tensor(str(path).encode(), name.encode(), ne, C.byref(nd), C.byref(ty),

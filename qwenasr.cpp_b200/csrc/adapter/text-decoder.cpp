@@ -48,7 +48,10 @@ bool create(const QwenAsrGgufModel &model, const qkv_model_config &cfg, int max_
     }
     qkv_runtime_config rt{};
     rt.device = ordinal;
-    rt.weight_dtype = env_dtype("QWENASR_B200_WEIGHTS", QKV_F32) == QKV_BF16 ? QKV_BF16 : QKV_F32;
+    {
+        const int wd = env_dtype("QWENASR_B200_WEIGHTS", QKV_F32);
+        rt.weight_dtype = (wd == QKV_BF16 || wd == QKV_FP8_E4M3) ? wd : QKV_F32;
+    }
     rt.kv_dtype = env_dtype("QWENASR_B200_KV", QKV_F32);
     rt.page_tokens = 16;
     rt.max_streams = max_streams;

@@ -19,6 +19,7 @@ size_t ggml_type_size(uint32_t type) {
         case kGgmlF32: return 4;
         case kGgmlF16: return 2;
         case kGgmlBF16: return 2;
+        case kGgmlI8: return 1;
         default: return 0;
     }
 }

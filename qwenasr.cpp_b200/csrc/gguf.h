@@ -16,6 +16,7 @@ namespace qkv {
 enum GgmlType : uint32_t {
     kGgmlF32 = 0,
     kGgmlF16 = 1,
+    kGgmlI8 = 24,      // one byte per element; e4m3 codes in the FP8 projection files
     kGgmlBF16 = 30,
 };
 

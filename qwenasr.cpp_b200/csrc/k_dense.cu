@@ -328,6 +328,75 @@ __global__ void swiglu_kernel(const float *gu, int M, int F, TOut *out) {
     }
 }
 
+// Rows to e4m3 codes with one f32 scale per row (amax / 448, 1 for an all-zero
+// row): the token operand of the FP8 projections, and the weights at load.
+// One CTA per row; the row's values are built once into shared memory:
+//   kQ8Rows:    bf16 input rows [n][K]
+//   kQ8RmsNorm: RMSNorm of f32 rows x [n][K] with weights w (the formula of
+//               rmsnorm_kernel, double sum of squares)
+//   kQ8SwiGLU:  silu(gate) * up of f32 rows gu [n][2K], gate and up
+//               interleaved in blocks of 64 features (as swiglu_kernel reads)
+enum Q8Mode { kQ8Rows = 0, kQ8RmsNorm = 1, kQ8SwiGLU = 2 };
+
+template <int MODE>
+__global__ void __launch_bounds__(256) rows_q8_kernel(const void *in, int K, const float *w, float eps, uint8_t *out,
+                                                      float *scales) {
+    pdl_trigger();
+    pdl_wait();   // the input rows come from the kernels before this one
+    extern __shared__ __align__(16) float vals[];   // [K]
+    __shared__ double dpart[8];
+    __shared__ float fpart[8];
+    __shared__ float s_val;
+    const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float scale_in = 1.0f;
+    if constexpr (MODE == kQ8RmsNorm) {
+        const float *xr = static_cast<const float *>(in) + static_cast<size_t>(r) * K;
+        double ss = 0.0;
+        for (int i = threadIdx.x; i < K; i += blockDim.x) ss += static_cast<double>(xr[i]) * xr[i];
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) dpart[warp] = ss;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double t = 0.0;
+            for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) t += dpart[k];
+            s_val = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(t / static_cast<double>(K)), eps)));
+        }
+        __syncthreads();
+        scale_in = s_val;
+    }
+    float amax = 0.0f;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) {
+        float v;
+        if constexpr (MODE == kQ8Rows) {
+            v = __bfloat162float(static_cast<const __nv_bfloat16 *>(in)[static_cast<size_t>(r) * K + i]);
+        } else if constexpr (MODE == kQ8RmsNorm) {
+            v = __fmul_rn(__fmul_rn(static_cast<const float *>(in)[static_cast<size_t>(r) * K + i], scale_in), w[i]);
+        } else {
+            const float *g = static_cast<const float *>(in) + static_cast<size_t>(r) * 2 * K + (i >> 6) * 128 + (i & 63);
+            const float gv = g[0];
+            v = gv / (1.0f + expf(-gv)) * g[64];
+        }
+        vals[i] = v;
+        amax = fmaxf(amax, fabsf(v));
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) fpart[warp] = amax;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float m = 0.0f;
+        for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) m = fmaxf(m, fpart[k]);
+        const float sc = m > 0.0f ? __fdiv_rn(m, kE4m3Max) : 1.0f;
+        scales[r] = sc;
+        s_val = m > 0.0f ? __fdiv_rn(1.0f, sc) : 0.0f;
+    }
+    __syncthreads();
+    const float inv = s_val;
+    uint8_t *o = out + static_cast<size_t>(r) * K;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) o[i] = f_to_e4m3(vals[i] * inv);
+}
+
 // Split argmax: CTA (r, s) scans slice s of row r (16-byte loads when the
 // row allows them) and writes its (max, index) partial; the last CTA of the
 // row to finish (per-row counter, which it resets) merges the partials in
@@ -679,6 +748,31 @@ cudaError_t launch_swiglu(const float *gu, int M, int F, void *out, int out_dtyp
         return launch_pdl(swiglu_kernel<float>, dim3(blocks), dim3(256), 0, st, gu, M, F, static_cast<float *>(out));
     return launch_pdl(swiglu_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, st, gu, M, F,
                       static_cast<__nv_bfloat16 *>(out));
+}
+
+cudaError_t launch_rows_q8(int mode, const void *in, int n, int K, const float *w, float eps, void *out, float *scales,
+                           cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    if (K <= 0 || K > 12 * 1024) return cudaErrorInvalidValue;
+    const size_t smem = static_cast<size_t>(K) * sizeof(float);
+    uint8_t *o = static_cast<uint8_t *>(out);
+    switch (mode) {
+        case kQ8Rows: return launch_pdl(rows_q8_kernel<kQ8Rows>, dim3(n), dim3(256), smem, st, in, K, w, eps, o, scales);
+        case kQ8RmsNorm:
+            return launch_pdl(rows_q8_kernel<kQ8RmsNorm>, dim3(n), dim3(256), smem, st, in, K, w, eps, o, scales);
+        case kQ8SwiGLU:
+            return launch_pdl(rows_q8_kernel<kQ8SwiGLU>, dim3(n), dim3(256), smem, st, in, K, w, eps, o, scales);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t prepare_rows_q8(int max_k) {
+    const int smem = max_k * static_cast<int>(sizeof(float));
+    cudaError_t e;
+    if ((e = cudaFuncSetAttribute(rows_q8_kernel<kQ8Rows>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem))) return e;
+    if ((e = cudaFuncSetAttribute(rows_q8_kernel<kQ8RmsNorm>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)))
+        return e;
+    return cudaFuncSetAttribute(rows_q8_kernel<kQ8SwiGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
 }
 
 cudaError_t launch_argmax_split(const float *logits, int M, int V, int *ids, float *part_v, int *part_i,

@@ -37,6 +37,9 @@ namespace qkv {
 namespace {
 
 constexpr int kBK = 64;                           // K per stage: one 128-byte swizzle atom of bf16
+// FP8 (e4m3 x e4m3, kind::f8f6f4): a stage holds the same 128-byte rows, i.e.
+// 128 elements of K, and each of its 4 MMAs takes K = 32 (32 bytes, as bf16's 16).
+template <bool F8> constexpr int kBKe = F8 ? 128 : 64;
 constexpr int kBM = 128;                          // weight rows per tile (MMA M)
 constexpr uint32_t kABytes = kBM * kBK * 2;       // 16 KB
 constexpr int kGemmThreads = 256;
@@ -64,6 +67,10 @@ struct TcParams {
     // up f 64t..64t+63]; act[M][N/2] (bf16) = silu(gate) * up, C is unused.
     __nv_bfloat16 *act;
     DevError *err;
+    // FP8 operands: value of W[n][k] = code x w_scale[n], of X[m][k] = code x
+    // x_scale[m]; the epilogue multiplies each accumulator by both.
+    const float *w_scale;
+    const float *x_scale;
 };
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar,
@@ -94,18 +101,29 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(const void *tile) {
     return d;
 }
 
-// Instruction descriptor: bf16 x bf16 -> f32, both K-major, M = 128, N = BN.
-template <int BN> __device__ __forceinline__ uint32_t idesc_bf16() {
-    return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
-           (static_cast<uint32_t>(kBM >> 4) << 24);
+// Instruction descriptor, both operands K-major, f32 accumulator, M = 128,
+// N = BN: bf16 x bf16 (kind::f16, A and B format 1) or e4m3 x e4m3
+// (kind::f8f6f4, A and B format 0).
+template <int BN, bool F8> __device__ __forceinline__ uint32_t idesc_mma() {
+    const uint32_t ab = F8 ? 0u : ((1u << 7) | (1u << 10));
+    return (1u << 4) | ab | (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, int accum) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(da), "l"(db), "r"(idesc), "r"(accum)
-        : "memory");
+template <bool F8>
+__device__ __forceinline__ void mma_issue(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, int accum) {
+    if constexpr (F8) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+            "l"(da), "l"(db), "r"(idesc), "r"(accum)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+            "l"(da), "l"(db), "r"(idesc), "r"(accum)
+            : "memory");
+    }
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
@@ -133,7 +151,7 @@ __device__ __forceinline__ bool bounded_wait(uint64_t *bar, uint32_t parity) {
     return mbar_wait(bar, parity, kWaitLimitCycles);
 }
 
-template <int BN>
+template <int BN, bool F8>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, TcParams p) {
     using T = TcTraits<BN>;
@@ -154,7 +172,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     volatile int *w_issued = failed + 1;     // weight tiles warp 0 has issued (prefetch distance)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ktiles = p.K / kBK;
+    const int ktiles = p.K / kBKe<F8>;
     const int units = p.tiles_n * p.tiles_m * p.splits;
     // The next kernel may start its own set-up now.  Weight tiles depend on no
     // earlier kernel, so their producer starts before pdl_wait; the token-tile
@@ -229,7 +247,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     }
                     uint8_t *dst = tiles + static_cast<size_t>(s) * T::kStage + (is_w ? 0u : kABytes);
                     mbar_arrive_expect_tx(&full[s], bytes);
-                    tma_load_2d(dst, map, (kt0 + i) * kBK, is_w ? n0 : m0, &full[s], pol);
+                    tma_load_2d(dst, map, (kt0 + i) * kBKe<F8>, is_w ? n0 : m0, &full[s], pol);
                     ++it;
                     if (is_w) *w_issued = it;
                 }
@@ -265,14 +283,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     }
                     asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
                                      reinterpret_cast<uint64_t>(&tmW)),
-                                 "r"((kt0 + i) * kBK), "r"(n0)
+                                 "r"((kt0 + i) * kBKe<F8>), "r"(n0)
                                  : "memory");
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t idesc = idesc_bf16<BN>();
+            const uint32_t idesc = idesc_mma<BN, F8>();
             int it = 0, j = 0;
             bool bad = false, any = false;
             for (int u = blockIdx.x; u < units && !bad; u += gridDim.x, ++j) {
@@ -300,9 +318,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     const uint8_t *bb = a + kABytes;
                     const uint64_t da = smem_desc_sw128(a), db = smem_desc_sw128(bb);
 #pragma unroll
-                    for (int kk = 0; kk < kBK / 16; ++kk) {
-                        // advance 16 bf16 = 32 bytes inside the swizzle atom (descriptor units of 16 B)
-                        mma_bf16(d, da + 2ull * kk, db + 2ull * kk, idesc, (i > 0 || kk > 0) ? 1 : 0);
+                    for (int kk = 0; kk < 4; ++kk) {
+                        // advance 32 bytes (16 bf16 or 32 e4m3) inside the swizzle atom
+                        // (descriptor units of 16 B)
+                        mma_issue<F8>(d, da + 2ull * kk, db + 2ull * kk, idesc, (i > 0 || kk > 0) ? 1 : 0);
                     }
                     mma_commit(&empty[s]);
                     any = true;
@@ -351,6 +370,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&acc_empty[b]);
+                }
+                if constexpr (F8) {
+                    // dequantise: weight row n's scale times each token's scale
+                    const float ws = n < p.N ? __ldg(p.w_scale + n) : 0.0f;
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) {
+                        const int m = m0 + c + jj;
+                        const float xs = m < p.M ? p.x_scale[m] : 0.0f;
+                        r[jj] = __float_as_uint(__uint_as_float(r[jj]) * ws * xs);
+                    }
                 }
                 if (fused) {
                     // Rows 0..63 (warps q = 0, 1) are gate features, rows 64..127 (q = 2, 3)
@@ -458,37 +487,41 @@ EncodeTiled encoder() {
     return fn;
 }
 
-// bf16 matrix [rows][K] (row-major), box = box_rows x 64 with the 128-byte swizzle.
-bool make_map(CUtensorMap *m, const void *ptr, int rows, int K, int box_rows) {
+// Matrix [rows][K] (row-major) of bf16 (es = 2) or one-byte codes (es = 1),
+// box = box_rows x one 128-byte row segment (64 bf16 / 128 codes), 128-byte swizzle.
+bool make_map(CUtensorMap *m, const void *ptr, int rows, int K, int box_rows, int es) {
     EncodeTiled enc = encoder();
     if (!enc) return false;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * es};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / es), static_cast<cuuint32_t>(box_rows)};
     const cuuint32_t estr[2] = {1, 1};
-    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+    return enc(m, es == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+               const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 struct MapKey {
     const void *ptr;
-    int rows, K, box;
-    bool operator==(const MapKey &o) const { return ptr == o.ptr && rows == o.rows && K == o.K && box == o.box; }
+    int rows, K, box, es;
+    bool operator==(const MapKey &o) const {
+        return ptr == o.ptr && rows == o.rows && K == o.K && box == o.box && es == o.es;
+    }
 };
 struct MapKeyHash {
     size_t operator()(const MapKey &k) const {
         return std::hash<const void *>()(k.ptr) ^ (static_cast<size_t>(k.rows) * 1000003u) ^
-               (static_cast<size_t>(k.K) << 20) ^ static_cast<size_t>(k.box);
+               (static_cast<size_t>(k.K) << 20) ^ static_cast<size_t>(k.box) ^ (static_cast<size_t>(k.es) << 40);
     }
 };
 
 std::mutex g_map_mu;
 std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
 
-bool cached_map(CUtensorMap *out, const void *ptr, int rows, int K, int box) {
+bool cached_map(CUtensorMap *out, const void *ptr, int rows, int K, int box, int es = 2) {
     std::lock_guard<std::mutex> lock(g_map_mu);
-    const MapKey key{ptr, rows, K, box};
+    const MapKey key{ptr, rows, K, box, es};
     auto it = g_maps.find(key);
     if (it != g_maps.end()) {
         *out = it->second;
@@ -496,14 +529,17 @@ bool cached_map(CUtensorMap *out, const void *ptr, int rows, int K, int box) {
     }
     if (g_maps.size() > 4096) g_maps.clear();
     CUtensorMap m;
-    if (!make_map(&m, ptr, rows, K, box)) return false;
+    if (!make_map(&m, ptr, rows, K, box, es)) return false;
     g_maps.emplace(key, m);
     *out = m;
     return true;
 }
 
 template <int BN> cudaError_t prepare_bn() {
-    return cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(TcTraits<BN>::kSmem));
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(gemm_tc_kernel<BN, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(TcTraits<BN>::kSmem));
 }
 
@@ -528,13 +564,15 @@ bool weight_fastest(int M, int K, int tiles_m) {
     return tiles_m > 1 && static_cast<double>(M) * K * 2.0 > 32.0e6;
 }
 
-template <int BN>
+template <int BN, bool F8 = false>
 cudaError_t launch_bn(const void *X, const void *W, float *C, int M, int N, int K, int accumulate, int splits,
-                      int num_sms, DevError *err, cudaStream_t st, __nv_bfloat16 *act = nullptr) {
+                      int num_sms, DevError *err, cudaStream_t st, __nv_bfloat16 *act = nullptr,
+                      const float *w_scale = nullptr, const float *x_scale = nullptr) {
     CUtensorMap tw, tx;
-    if (!cached_map(&tw, W, N, K, kBM) || !cached_map(&tx, X, M, K, BN)) return cudaErrorInvalidValue;
+    const int es = F8 ? 1 : 2;
+    if (!cached_map(&tw, W, N, K, kBM, es) || !cached_map(&tx, X, M, K, BN, es)) return cudaErrorInvalidValue;
     const int tiles_n = (N + kBM - 1) / kBM, tiles_m = (M + BN - 1) / BN;
-    const int ktiles = K / kBK;
+    const int ktiles = K / kBKe<F8>;
     const int kps = (ktiles + splits - 1) / splits;
     splits = (ktiles + kps - 1) / kps;     // every split owns >= 1 k-tile
     if (act && splits != 1) return cudaErrorInvalidValue;
@@ -550,10 +588,11 @@ cudaError_t launch_bn(const void *X, const void *W, float *C, int M, int N, int 
         }
         if (e != cudaSuccess) return e;
     }
-    TcParams p{M, N, K, kps, tiles_n, tiles_m, splits, weight_fastest(M, K, tiles_m) ? 1 : 0, C, accumulate, act, err};
+    TcParams p{M, N, K, kps, tiles_n, tiles_m, splits, weight_fastest(M, K * es / 2, tiles_m) ? 1 : 0, C, accumulate,
+               act, err, w_scale, x_scale};
     const int units = tiles_n * tiles_m * splits;
     const int grid = units < num_sms ? units : num_sms;
-    return launch_pdl(gemm_tc_kernel<BN>, dim3(grid), dim3(kGemmThreads), TcTraits<BN>::kSmem, st, tw, tx, p);
+    return launch_pdl(gemm_tc_kernel<BN, F8>, dim3(grid), dim3(kGemmThreads), TcTraits<BN>::kSmem, st, tw, tx, p);
 }
 
 // Cost model for the tile width BN and the K split.  One thread issues a
@@ -575,11 +614,11 @@ template <int BN> constexpr double ktile_seconds() {
     return t_mma > t_ld ? (t_mma > t_lat ? t_mma : t_lat) : (t_ld > t_lat ? t_ld : t_lat);
 }
 
-GemmPlan plan_gemm(int M, int N, int K, int num_sms, bool no_split = false) {
+GemmPlan plan_gemm(int M, int N, int K, int num_sms, bool no_split = false, bool f8 = false) {
     const double kHbm = 6.2e12;                     // whole-chip weight streaming
     const double kFixed = 1.5e-6;                   // per-unit fill + epilogue tail
     const double kRed = 250e9;                      // f32 red.add per second, whole chip
-    const int ktiles = K / kBK;
+    const int ktiles = K / (f8 ? kBKe<true> : kBK);   // a k-tile is 128 bytes of K either way
     const int tiles_n = (N + kBM - 1) / kBM;
     const double tk[4] = {ktile_seconds<32>(), ktile_seconds<64>(), ktile_seconds<128>(), ktile_seconds<256>()};
     GemmPlan best{256, 1};
@@ -598,7 +637,7 @@ GemmPlan plan_gemm(int M, int N, int K, int num_sms, bool no_split = false) {
             const long units = static_cast<long>(tiles) * sp;
             const long waves = (units + num_sms - 1) / num_sms;
             double t = waves * (kps * tk[idx] + kFixed);
-            const double t_w = static_cast<double>(N) * K * 2.0 / kHbm;   // weights read from HBM once
+            const double t_w = static_cast<double>(N) * K * (f8 ? 1.0 : 2.0) / kHbm;   // weights read from HBM once
             if (t_w > t) t = t_w;
             if (sp > 1) t += static_cast<double>(M) * N * sp / kRed + 1.0e-6;   // red.add + memset
             if (t < best_t * 0.98) {
@@ -661,6 +700,32 @@ cudaError_t launch_gemm_tc(const void *X, const void *W, float *C, int M, int N,
         case 64: return launch_bn<64>(X, W, C, M, N, K, accumulate, pl.splits, num_sms, err, st);
         case 128: return launch_bn<128>(X, W, C, M, N, K, accumulate, pl.splits, num_sms, err, st);
         default: return launch_bn<256>(X, W, C, M, N, K, accumulate, pl.splits, num_sms, err, st);
+    }
+}
+
+bool gemm_tc_fp8_supported(int M, int N, int K) {
+    return M > 0 && N > 0 && K > 0 && K % kBKe<true> == 0 && encoder() != nullptr;
+}
+
+int gemm_tc_fp8_kernels(int M, int N, int K, int accumulate, int num_sms) {
+    if (!gemm_tc_fp8_supported(M, N, K)) return 0;
+    const GemmPlan pl = plan_gemm(M, N, K, num_sms, false, true);
+    const int ktiles = K / kBKe<true>;
+    const int kps = (ktiles + pl.splits - 1) / pl.splits;
+    const int splits = (ktiles + kps - 1) / kps;
+    return (splits > 1 && !accumulate) ? 2 : 1;
+}
+
+cudaError_t launch_gemm_tc_fp8(const void *X, const float *x_scale, const void *W, const float *w_scale, float *C,
+                               int M, int N, int K, int accumulate, int num_sms, DevError *err, cudaStream_t st) {
+    if (M <= 0 || N <= 0) return cudaSuccess;
+    if (!gemm_tc_fp8_supported(M, N, K) || !x_scale || !w_scale) return cudaErrorInvalidValue;
+    const GemmPlan pl = plan_gemm(M, N, K, num_sms, false, true);
+    switch (pl.bn) {
+        case 32: return launch_bn<32, true>(X, W, C, M, N, K, accumulate, pl.splits, num_sms, err, st, nullptr, w_scale, x_scale);
+        case 64: return launch_bn<64, true>(X, W, C, M, N, K, accumulate, pl.splits, num_sms, err, st, nullptr, w_scale, x_scale);
+        case 128: return launch_bn<128, true>(X, W, C, M, N, K, accumulate, pl.splits, num_sms, err, st, nullptr, w_scale, x_scale);
+        default: return launch_bn<256, true>(X, W, C, M, N, K, accumulate, pl.splits, num_sms, err, st, nullptr, w_scale, x_scale);
     }
 }
 

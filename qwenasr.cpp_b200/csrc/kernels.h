@@ -175,6 +175,18 @@ cudaError_t launch_gemm_tc_swiglu(const void *X, const void *W, void *act, int M
 bool gemm_tc_swiglu_pays(int M, int N2, int K, int num_sms);
 // Kernels one launch_gemm_tc call launches: 2 when a K split first zeroes C.
 int gemm_tc_kernels(int M, int N, int K, int accumulate, int num_sms);
+// FP8 projections (tcgen05 kind::f8f6f4, e4m3 x e4m3 -> f32, K % 128 == 0):
+// C (+)= (X x x_scale[m]) . (W x w_scale[n])^T with one scale per token row
+// of X and per weight row of W; same tiling, split and epilogues as bf16.
+bool gemm_tc_fp8_supported(int M, int N, int K);
+int gemm_tc_fp8_kernels(int M, int N, int K, int accumulate, int num_sms);
+cudaError_t launch_gemm_tc_fp8(const void *X, const float *x_scale, const void *W, const float *w_scale, float *C,
+                               int M, int N, int K, int accumulate, int num_sms, DevError *err, cudaStream_t st);
+// Rows -> e4m3 codes + one f32 scale per row (amax / 448): mode 0 bf16 rows,
+// 1 RMSNorm(f32 rows) x w, 2 SwiGLU of interleaved f32 gate/up rows [n][2K].
+cudaError_t prepare_rows_q8(int max_k);
+cudaError_t launch_rows_q8(int mode, const void *in, int n, int K, const float *w, float eps, void *out, float *scales,
+                           cudaStream_t st);
 cudaError_t launch_gemm_tc(const void *X, const void *W, float *C, int M, int N, int K, int accumulate, int num_sms,
                            DevError *err, cudaStream_t st);
 // Shared-memory opt-in of the dense kernels for rows up to max_k wide.

@@ -110,7 +110,8 @@ int validate_rt(const qkv_runtime_config &r, std::string *e) {
         *e = "runtime config: page_tokens must be 16";
         return QKV_ERR_INVALID_ARG;
     }
-    if (r.kv_dtype < QKV_F32 || r.kv_dtype > QKV_E4M3K_I8V || (r.weight_dtype != QKV_F32 && r.weight_dtype != QKV_BF16)) {
+    if (r.kv_dtype < QKV_F32 || r.kv_dtype > QKV_E4M3K_I8V ||
+        (r.weight_dtype != QKV_F32 && r.weight_dtype != QKV_BF16 && r.weight_dtype != QKV_FP8_E4M3)) {
         *e = "runtime config: bad dtype";
         return QKV_ERR_INVALID_ARG;
     }
@@ -188,6 +189,10 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
         CK(cudaMalloc(&h->attn, R * kQDim * act));
         CK(cudaMalloc(&h->gu, R * 2 * c.intermediate * sizeof(float)));
         CK(cudaMalloc(&h->act, R * c.intermediate * act));
+        if (h->proj_fp8) {
+            CK(cudaMalloc(&h->xq, R * static_cast<size_t>(std::max(c.hidden, std::max(c.intermediate, kQDim)))));
+            CK(cudaMalloc(&h->xq_s, R * sizeof(float)));
+        }
         CK(cudaMalloc(&h->logits, static_cast<size_t>(h->rt.max_streams) * c.vocab * sizeof(float)));
         const size_t ms = static_cast<size_t>(h->rt.max_streams);
         CK(cudaMalloc(&h->am_v, ms * qkv_handle::kArgmaxSlices * sizeof(float)));
@@ -241,6 +246,7 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
         h->fused_swiglu = !(fs && std::strcmp(fs, "0") == 0);
     }
     CK(prepare_dense(std::max(c.hidden, std::max(c.intermediate, kQDim))));
+    CK(prepare_rows_q8(std::max(c.hidden, std::max(c.intermediate, kQDim))));
     (void)gemm_tc_supported(1, 1, 64);   // resolve the tensor-map encoder before any capture
     CK(cudaStreamSynchronize(h->stream));
     return QKV_OK;
@@ -253,6 +259,7 @@ void destroy(qkv_handle *h) {
     for (auto &L : h->layers) {
         cudaFree(L.attn_norm); cudaFree(L.ffn_norm); cudaFree(L.q_norm); cudaFree(L.k_norm);
         cudaFree(L.w_qkv); cudaFree(L.w_o); cudaFree(L.w_gu); cudaFree(L.w_down);
+        cudaFree(L.s_qkv); cudaFree(L.s_o); cudaFree(L.s_gu); cudaFree(L.s_down);
     }
     cudaFree(h->embd); cudaFree(h->w_out); cudaFree(h->out_norm);
     cudaFree(h->ap_norm_w); cudaFree(h->ap_norm_b); cudaFree(h->ap_w0); cudaFree(h->ap_b0); cudaFree(h->ap_w1);
@@ -297,6 +304,7 @@ struct Uploader {
 
     // Copy a GGUF tensor (f32/f16/bf16) to dst (+dst_off elements) in dtype.
     int put(const GgufTensor *t, void *dst, int dtype, size_t dst_off) {
+        if (t->type == kGgmlI8) return fail(h, QKV_ERR_FORMAT, "tensor holds e4m3 codes; load it with FP8 weights: " + t->name);
         if (!staging) CK(cudaMalloc(&staging, staging_bytes));
         const size_t es = ggml_type_size(t->type);
         const int src_code = t->type == kGgmlF32 ? 0 : t->type == kGgmlF16 ? 1 : 2;
@@ -328,6 +336,22 @@ int find_tensor(qkv_handle *h, const GgufFile &f, const std::string &name, const
 int load_weights(qkv_handle *h, const GgufFile &f) {
     const qkv_model_config &c = h->cfg;
     const int64_t H = c.hidden, QD = kQDim, KD = kKvDim, F = c.intermediate, V = c.vocab, D = kHeadDim;
+    if (h->proj_fp8 && (H % 128 != 0 || F % 128 != 0))
+        return fail(h, QKV_ERR_INVALID_ARG, "FP8 weights need hidden and intermediate sizes that are multiples of 128");
+    // FP8 projection files: every projection an I8 tensor of e4m3 codes with
+    // "<name>.scale" (f32, one per row), declared by a metadata key.
+    std::string proj_format;
+    const bool file_fp8 = f.get_str("qwen3-asr.b200.projections", &proj_format);
+    if (file_fp8 && proj_format != "e4m3-row-scale")
+        return fail(h, QKV_ERR_FORMAT, "unknown projection format: " + proj_format);
+    auto find_codes = [&](const GgufTensor *t, const std::string &name, int64_t rows, const GgufTensor **scale) -> int {
+        if (t->type != kGgmlI8) return fail(h, QKV_ERR_FORMAT, "FP8 projection file: not an e4m3 code tensor: " + name);
+        const GgufTensor *s = f.find(name + ".scale");
+        if (!s || s->type != kGgmlF32 || s->ne != std::vector<int64_t>{rows})
+            return fail(h, QKV_ERR_FORMAT, "FP8 projection file: missing or malformed " + name + ".scale");
+        *scale = s;
+        return QKV_OK;
+    };
     const size_t we = h->w_elem;
     Uploader up{h};
     struct DevBuf {
@@ -353,6 +377,52 @@ int load_weights(qkv_handle *h, const GgufFile &f) {
             (rc = find_tensor(h, f, p + "ffn_down.weight", {F, H}, &wd)))
             return rc;
         qkv_handle::Layer &L = h->layers[static_cast<size_t>(l)];
+        if (file_fp8) {
+            // FP8 projection file: e4m3 codes and row scales go up as stored.
+            if (!h->proj_fp8) return fail(h, QKV_ERR_FORMAT, "the file holds FP8 projections: create with FP8 weights");
+            const GgufTensor *sq, *sk, *sv, *so, *sg, *su, *sd;
+            if ((rc = find_codes(wq, p + "attn_q.weight", QD, &sq)) || (rc = find_codes(wk, p + "attn_k.weight", KD, &sk)) ||
+                (rc = find_codes(wv, p + "attn_v.weight", KD, &sv)) ||
+                (rc = find_codes(wo, p + "attn_output.weight", H, &so)) ||
+                (rc = find_codes(wg, p + "ffn_gate.weight", F, &sg)) ||
+                (rc = find_codes(wu, p + "ffn_up.weight", F, &su)) || (rc = find_codes(wd, p + "ffn_down.weight", H, &sd)))
+                return rc;
+            CK(cudaMalloc(&L.attn_norm, H * sizeof(float)));
+            CK(cudaMalloc(&L.ffn_norm, H * sizeof(float)));
+            CK(cudaMalloc(&L.q_norm, D * sizeof(float)));
+            CK(cudaMalloc(&L.k_norm, D * sizeof(float)));
+            CK(cudaMalloc(&L.w_qkv, static_cast<size_t>(QD + 2 * KD) * H));
+            CK(cudaMalloc(&L.s_qkv, static_cast<size_t>(QD + 2 * KD) * sizeof(float)));
+            CK(cudaMalloc(&L.w_o, static_cast<size_t>(H) * QD));
+            CK(cudaMalloc(&L.s_o, static_cast<size_t>(H) * sizeof(float)));
+            CK(cudaMalloc(&L.w_gu, static_cast<size_t>(2 * F) * H));
+            CK(cudaMalloc(&L.s_gu, static_cast<size_t>(2 * F) * sizeof(float)));
+            CK(cudaMalloc(&L.w_down, static_cast<size_t>(H) * F));
+            CK(cudaMalloc(&L.s_down, static_cast<size_t>(H) * sizeof(float)));
+            if ((rc = up.put(an, L.attn_norm, kActF32, 0)) || (rc = up.put(fn, L.ffn_norm, kActF32, 0)) ||
+                (rc = up.put(qn, L.q_norm, kActF32, 0)) || (rc = up.put(kn, L.k_norm, kActF32, 0)))
+                return rc;
+            auto raw = [&](const GgufTensor *t, void *dst, size_t off) -> int {
+                CK(cudaMemcpy(static_cast<uint8_t *>(dst) + off, t->data, t->nbytes, cudaMemcpyHostToDevice));
+                return QKV_OK;
+            };
+            if ((rc = raw(wq, L.w_qkv, 0)) || (rc = raw(wk, L.w_qkv, static_cast<size_t>(QD) * H)) ||
+                (rc = raw(wv, L.w_qkv, static_cast<size_t>(QD + KD) * H)) || (rc = raw(sq, L.s_qkv, 0)) ||
+                (rc = raw(sk, L.s_qkv, static_cast<size_t>(QD) * 4)) || (rc = raw(sv, L.s_qkv, static_cast<size_t>(QD + KD) * 4)) ||
+                (rc = raw(wo, L.w_o, 0)) || (rc = raw(so, L.s_o, 0)) || (rc = raw(wd, L.w_down, 0)) ||
+                (rc = raw(sd, L.s_down, 0)))
+                return rc;
+            // gate | up codes and scales interleaved in 64-row blocks, as the bf16 layout
+            const size_t blk = static_cast<size_t>(64) * H;
+            CK(cudaMemcpy2D(L.w_gu, 2 * blk, wg->data, blk, blk, static_cast<size_t>(F / 64), cudaMemcpyHostToDevice));
+            CK(cudaMemcpy2D(static_cast<uint8_t *>(L.w_gu) + blk, 2 * blk, wu->data, blk, blk, static_cast<size_t>(F / 64),
+                            cudaMemcpyHostToDevice));
+            CK(cudaMemcpy2D(L.s_gu, 128 * sizeof(float), sg->data, 64 * sizeof(float), 64 * sizeof(float),
+                            static_cast<size_t>(F / 64), cudaMemcpyHostToDevice));
+            CK(cudaMemcpy2D(L.s_gu + 64, 128 * sizeof(float), su->data, 64 * sizeof(float), 64 * sizeof(float),
+                            static_cast<size_t>(F / 64), cudaMemcpyHostToDevice));
+            continue;
+        }
         CK(cudaMalloc(&L.attn_norm, H * sizeof(float)));
         CK(cudaMalloc(&L.ffn_norm, H * sizeof(float)));
         CK(cudaMalloc(&L.q_norm, D * sizeof(float)));
@@ -381,6 +451,23 @@ int load_weights(qkv_handle *h, const GgufFile &f) {
                              static_cast<const uint8_t *>(gu_tmp) + static_cast<size_t>(F) * H * we, blk, blk,
                              static_cast<size_t>(F / 64), cudaMemcpyDeviceToDevice, h->stream));
         CK(cudaStreamSynchronize(h->stream));
+        if (h->proj_fp8) {
+            // FP8 projections: e4m3 codes with one scale per weight row (amax / 448),
+            // quantised on the device from the bf16 values just uploaded.
+            auto to_fp8 = [&](void *&w, float *&sc, int64_t rows, int64_t K) -> int {
+                void *codes = nullptr;
+                CK(cudaMalloc(&codes, static_cast<size_t>(rows * K)));
+                CK(cudaMalloc(&sc, static_cast<size_t>(rows) * sizeof(float)));
+                CK(launch_rows_q8(0, w, static_cast<int>(rows), static_cast<int>(K), nullptr, 0.0f, codes, sc, h->stream));
+                CK(cudaStreamSynchronize(h->stream));
+                cudaFree(w);
+                w = codes;
+                return QKV_OK;
+            };
+            if ((rc = to_fp8(L.w_qkv, L.s_qkv, QD + 2 * KD, H)) || (rc = to_fp8(L.w_o, L.s_o, H, QD)) ||
+                (rc = to_fp8(L.w_gu, L.s_gu, 2 * F, H)) || (rc = to_fp8(L.w_down, L.s_down, H, F)))
+                return rc;
+        }
     }
     const GgufTensor *te, *on, *ow;
     if ((rc = find_tensor(h, f, "text.token_embd.weight", {H, V}, &te)) ||
@@ -798,6 +885,47 @@ cudaError_t prefill_attend(qkv_handle *h, int l, int n, const int *slots, const 
     return launch_prefill_attn(pp, h->rt.kv_dtype, out_bf16, st);
 }
 
+// FP8 projection: C (+)= (xq x xq_s) . (W x w_s)^T.
+cudaError_t gemm8(qkv_handle *h, const void *W, const float *w_s, float *C, int M, int N, int K, int accumulate) {
+    h->launches += gemm_tc_fp8_kernels(M, N, K, accumulate, h->num_sms);
+    return launch_gemm_tc_fp8(h->xq, h->xq_s, W, w_s, C, M, N, K, accumulate, h->num_sms, h->d_err, h->stream);
+}
+
+// One layer with FP8 projections: every projection input is quantised to
+// e4m3 rows with a scale per row by the kernel that builds it (RMSNorm,
+// SwiGLU) or right after (the attention output).
+int run_layer_fp8(qkv_handle *h, const qkv_handle::Layer &L, int l, int n, const int *slots, const int *pos,
+                  const int *lens, bool prompt, const int4 *items, int n_items) {
+    const qkv_model_config &c = h->cfg;
+    const float eps = c.rms_norm_eps;
+    int rc;
+    CK(launch_rows_q8(1, h->x, n, c.hidden, L.attn_norm, eps, h->xq, h->xq_s, h->stream));
+    CK(gemm8(h, L.w_qkv, L.s_qkv, h->qkv, n, kQkvDim, c.hidden, 0));
+    if (!prompt) {
+        if ((rc = layer_kv(h, l, n, slots, pos, lens, h->qkv, h->q, h->attn, true, L.q_norm, L.k_norm, h->stream)))
+            return rc;
+    } else {
+        const bool tc = prefill_on_tc(h, items, n_items);
+        AppendParams ap = append_params(h, l, n, slots, pos, h->qkv, tc ? nullptr : h->q, L.q_norm, L.k_norm);
+        if (tc) {
+            ap.q16_out = h->q;
+            ap.q16_scale = attn_scale_log2();
+            ap.q16_f16 = kv_is_8bit(h->rt.kv_dtype) ? 1 : 0;
+        }
+        CK(launch_kv_append(ap, h->rt.kv_dtype, h->stream));
+        CK(prefill_attend(h, l, n, slots, pos, h->q, tc ? h->q : nullptr, h->attn, true, items, n_items, h->stream));
+        h->launches += 2;
+    }
+    CK(launch_rows_q8(0, h->attn, n, kQDim, nullptr, 0.0f, h->xq, h->xq_s, h->stream));
+    CK(gemm8(h, L.w_o, L.s_o, h->x, n, c.hidden, kQDim, 1));
+    CK(launch_rows_q8(1, h->x, n, c.hidden, L.ffn_norm, eps, h->xq, h->xq_s, h->stream));
+    CK(gemm8(h, L.w_gu, L.s_gu, h->gu, n, 2 * c.intermediate, c.hidden, 0));
+    CK(launch_rows_q8(2, h->gu, n, c.intermediate, nullptr, 0.0f, h->xq, h->xq_s, h->stream));
+    CK(gemm8(h, L.w_down, L.s_down, h->x, n, c.hidden, c.intermediate, 1));
+    h->launches += 4;
+    return QKV_OK;
+}
+
 int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int *lens, bool prompt, int l0 = 0,
                int l1 = -1, const int4 *items = nullptr, int n_items = 0) {
     const qkv_model_config &c = h->cfg;
@@ -806,6 +934,10 @@ int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int
     if (l1 < 0) l1 = c.n_layers;
     for (int l = l0; l < l1; ++l) {
         const qkv_handle::Layer &L = h->layers[static_cast<size_t>(l)];
+        if (h->proj_fp8) {
+            if ((rc = run_layer_fp8(h, L, l, n, slots, pos, lens, prompt, items, n_items))) return rc;
+            continue;
+        }
         CK(launch_rmsnorm(h->x, nullptr, n, c.hidden, L.attn_norm, c.rms_norm_eps, h->xn, h->act_dtype, h->stream));
         CK(gemm(h, h->xn, L.w_qkv, h->qkv, n, kQkvDim, c.hidden, 0));
         if (!prompt) {
@@ -929,7 +1061,8 @@ int qkv_create(const char *gguf_path, const qkv_model_config *cfg, const qkv_run
     qkv_handle *h = new qkv_handle();
     h->cfg = c;
     h->rt = *rt;
-    h->w_dtype = rt->weight_dtype == QKV_BF16 ? kActBF16 : kActF32;
+    h->proj_fp8 = rt->weight_dtype == QKV_FP8_E4M3;
+    h->w_dtype = rt->weight_dtype == QKV_F32 ? kActF32 : kActBF16;
     h->act_dtype = h->w_dtype;
     h->w_elem = h->w_dtype == kActBF16 ? 2 : 4;
     if ((rc = host_alloc_guard(h, [&] { return setup_common(h, true); })) ||
@@ -1765,6 +1898,35 @@ int qkv_gemm_bf16(const void *x, const void *w, float *c, int32_t m, int32_t n, 
     if (prep != cudaSuccess) return QKV_ERR_CUDA;
     if (!gemm_tc_supported(m, n, k)) return QKV_ERR_INVALID_ARG;
     return launch_gemm_tc(x, w, c, m, n, k, accumulate ? 1 : 0, sms, nullptr, static_cast<cudaStream_t>(stream)) ==
+                   cudaSuccess
+               ? QKV_OK
+               : QKV_ERR_CUDA;
+}
+
+int qkv_gemm_fp8(const void *x, const float *x_scale, const void *w, const float *w_scale, float *c, int32_t m, int32_t n,
+                 int32_t k, int32_t accumulate, void *stream) {
+    if (!x || !x_scale || !w || !w_scale || !c || m < 0 || n < 0 || k <= 0 || k % 128 != 0) return QKV_ERR_INVALID_ARG;
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return QKV_ERR_NO_DEVICE;
+    static std::once_flag once;
+    static cudaError_t prep = cudaSuccess;
+    std::call_once(once, [] { prep = prepare_gemm_tc(); });
+    if (prep != cudaSuccess) return QKV_ERR_CUDA;
+    if (!gemm_tc_fp8_supported(m, n, k)) return QKV_ERR_INVALID_ARG;
+    return launch_gemm_tc_fp8(x, x_scale, w, w_scale, c, m, n, k, accumulate ? 1 : 0, sms, nullptr,
+                              static_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? QKV_OK
+               : QKV_ERR_CUDA;
+}
+
+int qkv_quantize_rows_e4m3(const void *x_bf16, int32_t rows, int32_t k, void *codes, float *scales, void *stream) {
+    if (!x_bf16 || !codes || !scales || rows < 0 || k <= 0 || k > 12 * 1024) return QKV_ERR_INVALID_ARG;
+    static std::once_flag once;
+    static cudaError_t prep = cudaSuccess;
+    std::call_once(once, [] { prep = prepare_rows_q8(12 * 1024); });
+    if (prep != cudaSuccess) return QKV_ERR_CUDA;
+    return launch_rows_q8(0, x_bf16, rows, k, nullptr, 0.0f, codes, scales, static_cast<cudaStream_t>(stream)) ==
                    cudaSuccess
                ? QKV_OK
                : QKV_ERR_CUDA;

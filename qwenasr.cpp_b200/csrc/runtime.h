@@ -25,6 +25,8 @@ struct qkv_handle {
         void *w_o = nullptr;     // [H][Hq D]
         void *w_gu = nullptr;    // [2F][H]  gate rows, then up rows
         void *w_down = nullptr;  // [H][F]
+        // FP8 projections: one f32 scale per weight row (the codes are in w_*)
+        float *s_qkv = nullptr, *s_o = nullptr, *s_gu = nullptr, *s_down = nullptr;
     };
 
     int device = 0;
@@ -102,6 +104,12 @@ struct qkv_handle {
     int *am_rcnt = nullptr;
     float *d_wout_norm = nullptr;
     bool exact_argmax = true;   // QWENASR_B200_EXACT_ARGMAX=0 turns the re-scoring off
+    // weight_dtype QKV_FP8_E4M3: the four projections hold e4m3 codes with a
+    // scale per weight row and take e4m3 token rows with a scale per row (xq,
+    // xq_s); embeddings, the LM head and the audio projector stay bf16.
+    bool proj_fp8 = false;
+    uint8_t *xq = nullptr;      // [rows][max(H, Hq D, F)] e4m3 token operand
+    float *xq_s = nullptr;      // [rows]
     int *d_out_ids = nullptr;   // [max_rows]
     int *h_out_ids = nullptr;   // pinned
     int4 *d_items = nullptr;    // prefill attention work items

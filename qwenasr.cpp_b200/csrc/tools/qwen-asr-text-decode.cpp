@@ -6,7 +6,7 @@
 //
 //   qwen-asr-text-decode MODEL.gguf INPUT.f32 [--generate N | --prefill | --layer L]
 //                        [--out PATH] [--device auto|gpu|cpu] [--stop-ids a,b,..] [--no-stop]
-//                        [--kv-dtype f32|bf16|fp8|e4i8] [--weights f32|bf16] [--page-size 16] [--gpu N]
+//                        [--kv-dtype f32|bf16|fp8|e4i8] [--weights f32|bf16|fp8] [--page-size 16] [--gpu N]
 //                        (the reference tool's --threads, --backend, --audio-backend, --kv-cache,
 //                         --language and --system are accepted; see main)
 // INPUT.f32 = raw float32 [tokens][hidden] (audio rows already spliced in).
@@ -34,7 +34,7 @@ int usage(const char *argv0) {
     std::cerr << "usage: " << argv0
               << " MODEL.gguf INPUT.f32 [--generate N | --prefill | --layer L] [--out PATH]"
                  " [--device auto|gpu|cpu] [--stop-ids a,b] [--no-stop]"
-                 " [--kv-dtype f32|bf16|fp8|e4i8] [--weights f32|bf16] [--page-size 16] [--gpu N]\n";
+                 " [--kv-dtype f32|bf16|fp8|e4i8] [--weights f32|bf16|fp8] [--page-size 16] [--gpu N]\n";
     return 2;
 }
 
@@ -192,8 +192,11 @@ int main(int argc, char **argv) {
                 return 2;
             }
         } else if (a == "--weights") {
-            weights = need("f32 or bf16");
-            if (weights != "f32" && weights != "bf16") { std::cerr << "--weights must be f32 or bf16\n"; return 2; }
+            weights = need("f32, bf16 or fp8");
+            if (weights != "f32" && weights != "bf16" && weights != "fp8") {
+                std::cerr << "--weights must be f32, bf16 or fp8\n";
+                return 2;
+            }
         } else if (a == "--page-size") {
             if (std::string(need("16")) != "16") { std::cerr << "--page-size: the paged cache has 16-token pages only\n"; return 2; }
         } else if (a == "--gpu") {
@@ -227,7 +230,7 @@ int main(int argc, char **argv) {
     if (!weights.empty()) setenv("QWENASR_B200_WEIGHTS", weights.c_str(), 1);
     if (!gpu.empty()) setenv("QWENASR_B200_DEVICE", gpu.c_str(), 1);
     const std::string kv_shown = switch_value("QWENASR_B200_KV", {"bf16", "fp8", "e4i8"});
-    const std::string weights_shown = switch_value("QWENASR_B200_WEIGHTS", {"bf16"});
+    const std::string weights_shown = switch_value("QWENASR_B200_WEIGHTS", {"bf16", "fp8"});
 
     const auto t_init = std::chrono::steady_clock::now();
     QwenAsrGgufModel model;

@@ -22,7 +22,31 @@ import numpy as np
 
 GGUF_ALIGN = 32
 GGML_F32 = 0
+GGML_I8 = 24
 GGML_BF16 = 30
+# FP8 projection files (a B200-side format; the reference's converter writes f32
+# only): each projection weight is a GGML I8 tensor holding e4m3 codes, followed
+# by "<name>.scale", f32 [rows] (value = code x scale of its row); the metadata
+# key below declares the convention so that no plain int8 tensor is misread.
+FP8_PROJECTIONS_KEY = "qwen3-asr.b200.projections"
+FP8_PROJECTIONS_VALUE = "e4m3-row-scale"
+PROJECTION_SUFFIXES = ("attn_q.weight", "attn_k.weight", "attn_v.weight", "attn_output.weight", "ffn_gate.weight",
+                       "ffn_up.weight", "ffn_down.weight")
+
+
+def quantize_rows_e4m3(a: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """float32 [rows][K] -> (e4m3 codes as uint8 [rows][K], f32 scales [rows]):
+    scale = amax / 448 per row (1 for an all-zero row), code = RNE e4m3 of
+    value x (1 / scale) saturated to +-448 (the device quantiser's rule)."""
+    import torch
+    a = np.ascontiguousarray(a, np.float32)
+    amax = np.abs(a).max(axis=1, keepdims=True)
+    with np.errstate(divide="ignore"):
+        scale = np.where(amax > 0, amax / np.float32(448.0), np.float32(1.0)).astype(np.float32)
+        inv = np.where(amax > 0, np.float32(1.0) / scale, np.float32(0.0)).astype(np.float32)
+    v = np.clip(a * inv, np.float32(-448.0), np.float32(448.0)).astype(np.float32)
+    codes = torch.from_numpy(v).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    return codes, scale[:, 0]
 
 QWEN3_ASR_0_6B = dict(n_layers=28, hidden=1024, n_heads=16, n_kv_heads=8, head_dim=128,
                       intermediate=3072, vocab=151936, rope_theta=1.0e6, rms_norm_eps=1.0e-6)
@@ -240,36 +264,55 @@ def write_gguf(path: str | Path, cfg: ModelConfig | dict, seed: int = 0, std: fl
     norm_init: "normal" -> norm weights ~ N(0,std) like every other tensor;
                "one_plus" -> 1 + N(0,std) (a trained-like scale).
     audio_hidden: > 0 adds the audio projector tensors (tensor_specs).
-    storage: "f32" (GGML type 0, as the reference's converter writes) or
-             "bf16" (GGML type 30: the bf16-rounded values' upper 16 bits).
+    storage: "f32" (GGML type 0, as the reference's converter writes),
+             "bf16" (GGML type 30: the bf16-rounded values' upper 16 bits) or
+             "fp8" (the projections as e4m3 codes + row scales, see
+             FP8_PROJECTIONS_KEY, quantised from the bf16-rounded values;
+             every other tensor f32).
     """
-    if storage not in ("f32", "bf16"):
+    if storage not in ("f32", "bf16", "fp8"):
         raise ValueError(storage)
-    if storage == "bf16":
+    if storage in ("bf16", "fp8"):
         weights = "bf16"
     cfg = ModelConfig.of(cfg) if isinstance(cfg, dict) else cfg
     path = Path(path)
     specs = tensor_specs(cfg, audio_hidden)
     kv = metadata(cfg, f"qwen3-asr-synthetic-{cfg.hidden}", tokenizer)
+    if storage == "fp8":
+        kv.append(_kv_str(FP8_PROJECTIONS_KEY, FP8_PROJECTIONS_VALUE))
+    base_es, base_type = (2, GGML_BF16) if storage == "bf16" else (4, GGML_F32)
+    # (name, numpy shape, GGML type, bytes, generated-tensor index or -1 for a scale)
+    layout = []
+    for idx, (name, shape, _) in enumerate(specs):
+        fp8 = storage == "fp8" and name.endswith(PROJECTION_SUFFIXES)
+        if fp8:
+            layout.append((name, shape, GGML_I8, int(np.prod(shape)), idx))
+            layout.append((name + ".scale", (shape[0],), GGML_F32, shape[0] * 4, -1))
+        else:
+            layout.append((name, shape, base_type, int(np.prod(shape)) * base_es, idx))
     infos = []
     offset = 0
-    es, gtype = (4, GGML_F32) if storage == "f32" else (2, GGML_BF16)
-    for name, shape, _ in specs:
-        nb = int(np.prod(shape)) * es
+    for name, shape, gtype, nb, _ in layout:
         ne = tuple(reversed(shape))
         nm = name.encode()
         infos.append(struct.pack("<Q", len(nm)) + nm + struct.pack("<I", len(ne)) +
                      b"".join(struct.pack("<Q", d) for d in ne) + struct.pack("<IQ", gtype, offset))
         offset += (nb + GGUF_ALIGN - 1) // GGUF_ALIGN * GGUF_ALIGN
-    head = b"GGUF" + struct.pack("<IQQ", 3, len(specs), len(kv)) + b"".join(kv) + b"".join(infos)
+    head = b"GGUF" + struct.pack("<IQQ", 3, len(layout), len(kv)) + b"".join(kv) + b"".join(infos)
     pad = (-len(head)) % GGUF_ALIGN
     rng = np.random.default_rng(seed)
     with open(path, "wb") as f:
         f.write(head + b"\0" * pad)
-        for name, shape, kind in specs:
-            a = _gen_tensor(rng, shape, kind, std, norm_init, weights == "bf16")
-            if storage == "bf16":
-                a = (np.ascontiguousarray(a).view(np.uint32) >> np.uint32(16)).astype(np.uint16)
+        pending_scale = None
+        for name, shape, gtype, nb, idx in layout:
+            if idx < 0:
+                a = pending_scale
+            else:
+                a = _gen_tensor(rng, shape, specs[idx][2], std, norm_init, weights == "bf16")
+                if gtype == GGML_BF16:
+                    a = (np.ascontiguousarray(a).view(np.uint32) >> np.uint32(16)).astype(np.uint16)
+                elif gtype == GGML_I8:
+                    a, pending_scale = quantize_rows_e4m3(a)
             f.write(memoryview(np.ascontiguousarray(a)).cast("B"))
             f.write(b"\0" * ((-a.nbytes) % GGUF_ALIGN))
     return path
@@ -341,8 +384,15 @@ def read_gguf(path: str | Path) -> dict[str, np.ndarray]:
         elif t == GGML_BF16:   # widened to f32 (a copy)
             bits = np.ndarray(shape, dtype=np.uint16, buffer=buf, offset=data0 + off)
             out[name] = (bits.astype(np.uint32) << np.uint32(16)).view(np.float32)
+        elif t == GGML_I8:     # e4m3 codes of an FP8 projection file, dequantised below
+            out[name] = np.ndarray(shape, dtype=np.uint8, buffer=buf, offset=data0 + off)
         else:
-            raise ValueError(f"{name}: only f32 and bf16 tensors are read here")
+            raise ValueError(f"{name}: only f32, bf16 and FP8-projection tensors are read here")
+    for name in [n for n, (_, _, t, _) in zip(list(out), infos) if t == GGML_I8]:
+        import torch
+        scale = out.pop(name + ".scale")
+        codes = torch.from_numpy(np.array(out[name], copy=True)).view(torch.float8_e4m3fn)
+        out[name] = (codes.float().numpy() * scale[:, None]).astype(np.float32)   # value = code x row scale
     return out
 
 

@@ -53,7 +53,7 @@ def test_cli_accepts_reference_flags(case):
     assert rc == 2 and "--audio-backend requires ggml or sched" in err
 
 
-@pytest.mark.parametrize("flags,msg", [(["--kv-dtype", "int8"], "--kv-dtype"), (["--weights", "fp8"], "--weights"),
+@pytest.mark.parametrize("flags,msg", [(["--kv-dtype", "int8"], "--kv-dtype"), (["--weights", "int4"], "--weights"),
                                        (["--page-size", "32"], "16-token pages"), (["--gpu", "x"], "--gpu")])
 def test_cli_rejects_bad_b200_options(case, flags, msg):
     """The B200 options are checked before any file or device is touched."""

@@ -40,6 +40,29 @@ def test_writer_matches_third_party_reader(pkg, synth, tiny_files):
     assert int(f["qwen3-asr.text.hidden_size"].parts[-1][0]) == cfg["hidden"]
 
 
+def test_fp8_projection_file(pkg, synth, tmp_path):
+    """FP8 projection files: each projection an I8 tensor of e4m3 codes plus an
+    f32 "<name>.scale" per row; the native reader sees both, the codes
+    dequantise (code x row scale) to within e4m3's precision of the
+    bf16-rounded values the same seed writes, and everything else is as in
+    the f32 file."""
+    cfg = dict(synth.TINY)
+    p8 = synth.write_gguf(tmp_path / "fp8.gguf", cfg, seed=0, storage="fp8", tokenizer=False)
+    pb = synth.write_gguf(tmp_path / "bf.gguf", cfg, seed=0, weights="bf16", tokenizer=False)
+    dims, ty, codes = pkg.gguf_tensor(p8, "text.blk.1.ffn_down.weight")
+    assert ty == 24 and dims == [cfg["intermediate"], cfg["hidden"]] and codes.nbytes == cfg["hidden"] * cfg["intermediate"]
+    dims, ty, sc = pkg.gguf_tensor(p8, "text.blk.1.ffn_down.weight.scale")
+    assert ty == 0 and dims == [cfg["hidden"]]
+    a, b = synth.read_gguf(p8), synth.read_gguf(pb)
+    assert set(a) == set(b)
+    for name in b:
+        if name.endswith(synth.PROJECTION_SUFFIXES):
+            rows_max = np.abs(b[name]).max(axis=1, keepdims=True)
+            assert np.all(np.abs(a[name] - b[name]) <= rows_max * 2.0 ** -4 + 1e-12), name
+        else:
+            assert np.array_equal(a[name], b[name]), name
+
+
 def test_read_config(pkg, tiny_files):
     cfg, files = tiny_files
     got = pkg.read_gguf_config(files[("bf16", "one_plus")])

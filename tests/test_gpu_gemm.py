@@ -53,3 +53,76 @@ def test_gemm_repeatable(pkg, m, n, k):
         torch.cuda.synchronize()
         outs.append(c)
     assert torch.equal(outs[0], outs[1])
+
+
+# ---- FP8 (e4m3) projections: qkv_quantize_rows_e4m3 + qkv_gemm_fp8 ----
+
+def quantize_rows_torch(x_bf16):
+    """The quantiser's definition: scale = amax / 448 per row (1 for a zero
+    row), codes = RNE e4m3 of x * (1 / scale), saturated to +-448."""
+    xf = x_bf16.float()
+    amax = xf.abs().amax(dim=1, keepdim=True)
+    # tensor / tensor: torch turns a division by a Python scalar into a
+    # multiplication by its reciprocal, which is not the correctly rounded quotient
+    scale = torch.where(amax > 0, amax / torch.full_like(amax, 448.0), torch.ones_like(amax))
+    inv = torch.where(amax > 0, torch.ones_like(scale) / scale, torch.zeros_like(amax))
+    codes = (xf * inv).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    return codes, scale.squeeze(1)
+
+
+def device_quantize(pkg, x_bf16):
+    rows, k = x_bf16.shape
+    codes = torch.empty((rows, k), dtype=torch.uint8, device="cuda")
+    scales = torch.empty(rows, device="cuda")
+    assert pkg.lib.qkv_quantize_rows_e4m3(x_bf16.data_ptr(), rows, k, codes.data_ptr(), scales.data_ptr(), None) == 0
+    torch.cuda.synchronize()
+    return codes, scales
+
+
+def test_quantize_rows_e4m3_matches_definition(pkg):
+    g = torch.Generator(device="cuda").manual_seed(17)
+    x = torch.randn((300, 2048), device="cuda", generator=g)
+    x[3] = 0.0                                # an all-zero row: scale 1, codes 0
+    x[5, 7] = 1e4                             # one outlier row
+    x[9] *= 1e-6                              # tiny values (e4m3 subnormals)
+    xb = x.to(torch.bfloat16)
+    codes, scales = device_quantize(pkg, xb)
+    want_codes, want_scales = quantize_rows_torch(xb)
+    assert torch.equal(scales, want_scales)
+    assert torch.equal(codes, want_codes.view(torch.uint8))
+    assert scales[3].item() == 1.0 and int(codes[3].abs().max().item()) == 0
+
+
+FP8_SHAPES = [(1, 256, 128), (7, 1000, 256), (32, 4096, 1024), (32, 1024, 2048), (33, 384, 512), (64, 6144, 1024),
+              (64, 2048, 6144), (129, 256, 128), (300, 4096, 1024), (512, 4096, 2048), (777, 2048, 6144),
+              (1024, 12288, 2048)]
+
+
+@pytest.mark.parametrize("m,n,k", FP8_SHAPES)
+@pytest.mark.parametrize("accumulate", [0, 1])
+def test_gemm_fp8_matches_dequantised_matmul(pkg, m, n, k, accumulate):
+    """C (+)= (X x x_scale) . (W x w_scale)^T: e4m3 products are exact in f32,
+    so against the f64 matmul of the dequantised operands the bar is f32
+    accumulation, as for the bf16 GEMM (1e-4 relative)."""
+    g = torch.Generator(device="cuda").manual_seed(m * 5 + n + k + accumulate)
+    xq, xs = device_quantize(pkg, torch.randn((m, k), device="cuda", generator=g).to(torch.bfloat16))
+    wq, ws = device_quantize(pkg, (0.05 * torch.randn((n, k), device="cuda", generator=g)).to(torch.bfloat16))
+    base = torch.randn((m, n), device="cuda", generator=g) if accumulate else None
+    c = base.clone() if accumulate else torch.full((m, n), float("nan"), device="cuda")
+    rc = pkg.lib.qkv_gemm_fp8(xq.data_ptr(), xs.data_ptr(), wq.data_ptr(), ws.data_ptr(), c.data_ptr(), m, n, k,
+                              accumulate, None)
+    assert rc == 0
+    torch.cuda.synchronize()
+    xd = xq.view(torch.float8_e4m3fn).double() * xs.double()[:, None]
+    wd = wq.view(torch.float8_e4m3fn).double() * ws.double()[:, None]
+    ref = xd @ wd.t()
+    if accumulate:
+        ref = ref + base.double()
+    err = ((c.double() - ref).abs().max() / ref.abs().max()).item()
+    assert err < 1e-4, err
+
+
+def test_gemm_fp8_rejects_k_not_multiple_of_128(pkg):
+    t = torch.zeros(16, device="cuda")
+    assert pkg.lib.qkv_gemm_fp8(t.data_ptr(), t.data_ptr(), t.data_ptr(), t.data_ptr(), t.data_ptr(), 1, 1, 64, 0,
+                                None) != 0

@@ -374,3 +374,46 @@ def test_bf16_head_argmax_is_the_f32_argmax(pkg, synth, tmp_path, monkeypatch):
                 miss[exact] += int(np.sum(np.asarray(ids) != want))
     print(f"rows whose id differs from the f32 argmax: re-scored {miss['1']}, bf16 logits only {miss['0']} (of {6 * n})")
     assert miss["1"] == 0
+
+
+def test_fp8_weights_deviation(pkg, synth, checker, tiny_files):
+    """FP8 projections (e4m3 weights with a scale per weight row, e4m3 token
+    rows with a scale per row, tcgen05 kind::f8f6f4) with a bf16 cache,
+    against the f32 oracle on the bf16-rounded file: e4m3 keeps 3 mantissa
+    bits of every weight and every projection input, so this is a stated
+    deviation, not a parity bar (printed; held to 80 % agreement)."""
+    cfg, files = tiny_files
+    agree, dev = teacher_forced(pkg, synth, checker, files[("bf16", "one_plus")], 2, 1, n_streams=8, n_steps=64)
+    print(f"fp8 weights + bf16 cache: teacher-forced agreement {agree:.4f}, max rel logit deviation {dev:.3e}")
+    assert agree >= 0.8 and dev < 0.5, (agree, dev)
+
+
+def test_fp8_file_loads_like_device_quantisation(pkg, synth, checker, tmp_path):
+    """An FP8 projection file (e4m3 codes + row scales, written on the host by
+    the device quantiser's rule) and the bf16 file of the same seed quantised
+    on the device at load give the same greedy ids and logits within the
+    split-K atomics' spread; a bf16 handle refuses the FP8 file.  Against the
+    f32 oracle run on the file's own dequantised weights, what remains is the
+    e4m3 rounding of the projection inputs alone (printed)."""
+    cfg = dict(synth.TINY)
+    pb = synth.write_gguf(tmp_path / "bf16.gguf", cfg, seed=0, weights="bf16", norm_init="one_plus", tokenizer=False)
+    p8 = synth.write_gguf(tmp_path / "fp8.gguf", cfg, seed=0, norm_init="one_plus", tokenizer=False, storage="fp8")
+    t8 = synth.read_gguf(p8)
+    xs = prompts(synth, t8, 3, 520, lo=40, hi=120)
+    out = []
+    for path in (pb, p8):
+        with decoder(pkg, path, w=2, kv=1, streams=3, ctx=256, batch_tokens=512) as dec:
+            s = [dec.open() for _ in xs]
+            ids, lg = dec.prefill(s, xs, want_logits=True)
+            steps = [ids]
+            for _ in range(8):
+                steps.append(dec.decode_step(s))
+            out.append((np.asarray(steps), lg))
+    assert np.array_equal(out[0][0], out[1][0])
+    assert rel_err(out[1][1], out[0][1]) < 1e-2
+    with pytest.raises(pkg.QkvError) as ei:
+        decoder(pkg, p8, w=1, kv=1, streams=1, ctx=64)
+    assert ei.value.code == 7
+    om = checker.OracleModel(cfg, t8)
+    dev = max(rel_err(out[1][1][i], om.prefill_logits(x)) for i, x in enumerate(xs))
+    print(f"fp8 file vs the oracle on its own dequantised weights: prefill max rel logit deviation {dev:.3e}")
