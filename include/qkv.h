@@ -238,7 +238,8 @@ int qkv_gemm_fp8(const void *x, const float *x_scale, const void *w, const float
 
 /* Rows of bf16 values [rows][k] -> e4m3 codes [rows][k] and one f32 scale per
  * row (amax / 448; 1 for an all-zero row): the quantiser the FP8 weights and
- * token rows go through.  Device pointers, `stream` as above. */
+ * token rows go through; k a multiple of 4, at most 6144.  Device pointers,
+ * `stream` as above. */
 int qkv_quantize_rows_e4m3(const void *x_bf16, int32_t rows, int32_t k, void *codes, float *scales, void *stream);
 
 /* Causal prefill attention over one layer's paged cache (K3 on tcgen05 for

@@ -337,64 +337,98 @@ __global__ void swiglu_kernel(const float *gu, int M, int F, TOut *out) {
 //   kQ8SwiGLU:  silu(gate) * up of f32 rows gu [n][2K], gate and up
 //               interleaved in blocks of 64 features (as swiglu_kernel reads)
 enum Q8Mode { kQ8Rows = 0, kQ8RmsNorm = 1, kQ8SwiGLU = 2 };
+constexpr int kQ8Threads = 256;
+constexpr int kQ8MaxVec = 6;   // float4 groups per thread: rows up to 256 x 6 x 4 = 6144 wide
 
+// The row stays in registers (kQ8MaxVec groups of 4 per thread, 16-byte
+// loads); K % 4 == 0 (checked at launch).
 template <int MODE>
-__global__ void __launch_bounds__(256) rows_q8_kernel(const void *in, int K, const float *w, float eps, uint8_t *out,
-                                                      float *scales) {
+__global__ void __launch_bounds__(kQ8Threads) rows_q8_kernel(const void *in, int K, const float *w, float eps,
+                                                             uint8_t *out, float *scales) {
     pdl_trigger();
     pdl_wait();   // the input rows come from the kernels before this one
-    extern __shared__ __align__(16) float vals[];   // [K]
-    __shared__ double dpart[8];
-    __shared__ float fpart[8];
+    __shared__ double dpart[kQ8Threads / 32];
+    __shared__ float fpart[kQ8Threads / 32];
     __shared__ float s_val;
     const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float scale_in = 1.0f;
+    const int k4 = K >> 2;
+    float4 v[kQ8MaxVec];
+#pragma unroll
+    for (int g = 0; g < kQ8MaxVec; ++g) {
+        const int i4 = threadIdx.x + kQ8Threads * g;
+        v[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i4 < k4) {
+            if constexpr (MODE == kQ8Rows) {
+                const uint2 b = reinterpret_cast<const uint2 *>(static_cast<const __nv_bfloat16 *>(in) +
+                                                                static_cast<size_t>(r) * K)[i4];
+                v[g] = make_float4(bf16lo(b.x), bf16hi(b.x), bf16lo(b.y), bf16hi(b.y));
+            } else if constexpr (MODE == kQ8RmsNorm) {
+                v[g] = reinterpret_cast<const float4 *>(static_cast<const float *>(in) + static_cast<size_t>(r) * K)[i4];
+            } else {
+                // gate and up interleaved in blocks of 64 features (a group of 4 stays in one block)
+                const int i = 4 * i4;
+                const float *gp = static_cast<const float *>(in) + static_cast<size_t>(r) * 2 * K + (i >> 6) * 128 + (i & 63);
+                const float4 gv = *reinterpret_cast<const float4 *>(gp);
+                const float4 uv = *reinterpret_cast<const float4 *>(gp + 64);
+                v[g] = make_float4(gv.x / (1.0f + expf(-gv.x)) * uv.x, gv.y / (1.0f + expf(-gv.y)) * uv.y,
+                                   gv.z / (1.0f + expf(-gv.z)) * uv.z, gv.w / (1.0f + expf(-gv.w)) * uv.w);
+            }
+        }
+    }
     if constexpr (MODE == kQ8RmsNorm) {
-        const float *xr = static_cast<const float *>(in) + static_cast<size_t>(r) * K;
+        // RMSNorm as rmsnorm_kernel: double sum of squares, then x * scale * w rounded per op
         double ss = 0.0;
-        for (int i = threadIdx.x; i < K; i += blockDim.x) ss += static_cast<double>(xr[i]) * xr[i];
+#pragma unroll
+        for (int g = 0; g < kQ8MaxVec; ++g)
+            ss += static_cast<double>(v[g].x) * v[g].x + static_cast<double>(v[g].y) * v[g].y +
+                  static_cast<double>(v[g].z) * v[g].z + static_cast<double>(v[g].w) * v[g].w;
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         if (lane == 0) dpart[warp] = ss;
         __syncthreads();
         if (threadIdx.x == 0) {
             double t = 0.0;
-            for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) t += dpart[k];
+            for (int k = 0; k < kQ8Threads / 32; ++k) t += dpart[k];
             s_val = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(t / static_cast<double>(K)), eps)));
         }
         __syncthreads();
-        scale_in = s_val;
+        const float sc = s_val;
+#pragma unroll
+        for (int g = 0; g < kQ8MaxVec; ++g) {
+            const int i4 = threadIdx.x + kQ8Threads * g;
+            if (i4 < k4) {
+                const float4 wv = reinterpret_cast<const float4 *>(w)[i4];
+                v[g] = make_float4(__fmul_rn(__fmul_rn(v[g].x, sc), wv.x), __fmul_rn(__fmul_rn(v[g].y, sc), wv.y),
+                                   __fmul_rn(__fmul_rn(v[g].z, sc), wv.z), __fmul_rn(__fmul_rn(v[g].w, sc), wv.w));
+            }
+        }
     }
     float amax = 0.0f;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) {
-        float v;
-        if constexpr (MODE == kQ8Rows) {
-            v = __bfloat162float(static_cast<const __nv_bfloat16 *>(in)[static_cast<size_t>(r) * K + i]);
-        } else if constexpr (MODE == kQ8RmsNorm) {
-            v = __fmul_rn(__fmul_rn(static_cast<const float *>(in)[static_cast<size_t>(r) * K + i], scale_in), w[i]);
-        } else {
-            const float *g = static_cast<const float *>(in) + static_cast<size_t>(r) * 2 * K + (i >> 6) * 128 + (i & 63);
-            const float gv = g[0];
-            v = gv / (1.0f + expf(-gv)) * g[64];
-        }
-        vals[i] = v;
-        amax = fmaxf(amax, fabsf(v));
-    }
+#pragma unroll
+    for (int g = 0; g < kQ8MaxVec; ++g)
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[g].x), fabsf(v[g].y)), fmaxf(fabsf(v[g].z), fabsf(v[g].w))));
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     if (lane == 0) fpart[warp] = amax;
     __syncthreads();
     if (threadIdx.x == 0) {
         float m = 0.0f;
-        for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) m = fmaxf(m, fpart[k]);
+        for (int k = 0; k < kQ8Threads / 32; ++k) m = fmaxf(m, fpart[k]);
         const float sc = m > 0.0f ? __fdiv_rn(m, kE4m3Max) : 1.0f;
         scales[r] = sc;
         s_val = m > 0.0f ? __fdiv_rn(1.0f, sc) : 0.0f;
     }
     __syncthreads();
     const float inv = s_val;
-    uint8_t *o = out + static_cast<size_t>(r) * K;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) o[i] = f_to_e4m3(vals[i] * inv);
+    uint32_t *o = reinterpret_cast<uint32_t *>(out + static_cast<size_t>(r) * K);
+#pragma unroll
+    for (int g = 0; g < kQ8MaxVec; ++g) {
+        const int i4 = threadIdx.x + kQ8Threads * g;
+        if (i4 < k4)
+            o[i4] = static_cast<uint32_t>(f_to_e4m3(v[g].x * inv)) | (static_cast<uint32_t>(f_to_e4m3(v[g].y * inv)) << 8) |
+                    (static_cast<uint32_t>(f_to_e4m3(v[g].z * inv)) << 16) |
+                    (static_cast<uint32_t>(f_to_e4m3(v[g].w * inv)) << 24);
+    }
 }
 
 // Split argmax: CTA (r, s) scans slice s of row r (16-byte loads when the
@@ -753,27 +787,19 @@ cudaError_t launch_swiglu(const float *gu, int M, int F, void *out, int out_dtyp
 cudaError_t launch_rows_q8(int mode, const void *in, int n, int K, const float *w, float eps, void *out, float *scales,
                            cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
-    if (K <= 0 || K > 12 * 1024) return cudaErrorInvalidValue;
-    const size_t smem = static_cast<size_t>(K) * sizeof(float);
+    if (K <= 0 || K % 4 != 0 || K > kQ8Threads * kQ8MaxVec * 4) return cudaErrorInvalidValue;
     uint8_t *o = static_cast<uint8_t *>(out);
     switch (mode) {
-        case kQ8Rows: return launch_pdl(rows_q8_kernel<kQ8Rows>, dim3(n), dim3(256), smem, st, in, K, w, eps, o, scales);
+        case kQ8Rows: return launch_pdl(rows_q8_kernel<kQ8Rows>, dim3(n), dim3(kQ8Threads), 0, st, in, K, w, eps, o, scales);
         case kQ8RmsNorm:
-            return launch_pdl(rows_q8_kernel<kQ8RmsNorm>, dim3(n), dim3(256), smem, st, in, K, w, eps, o, scales);
+            return launch_pdl(rows_q8_kernel<kQ8RmsNorm>, dim3(n), dim3(kQ8Threads), 0, st, in, K, w, eps, o, scales);
         case kQ8SwiGLU:
-            return launch_pdl(rows_q8_kernel<kQ8SwiGLU>, dim3(n), dim3(256), smem, st, in, K, w, eps, o, scales);
+            return launch_pdl(rows_q8_kernel<kQ8SwiGLU>, dim3(n), dim3(kQ8Threads), 0, st, in, K, w, eps, o, scales);
         default: return cudaErrorInvalidValue;
     }
 }
 
-cudaError_t prepare_rows_q8(int max_k) {
-    const int smem = max_k * static_cast<int>(sizeof(float));
-    cudaError_t e;
-    if ((e = cudaFuncSetAttribute(rows_q8_kernel<kQ8Rows>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem))) return e;
-    if ((e = cudaFuncSetAttribute(rows_q8_kernel<kQ8RmsNorm>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)))
-        return e;
-    return cudaFuncSetAttribute(rows_q8_kernel<kQ8SwiGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-}
+int rows_q8_max_k() { return kQ8Threads * kQ8MaxVec * 4; }
 
 cudaError_t launch_argmax_split(const float *logits, int M, int V, int *ids, float *part_v, int *part_i,
                                 int *counters, int max_slices, int num_sms, cudaStream_t st) {

@@ -184,7 +184,7 @@ cudaError_t launch_gemm_tc_fp8(const void *X, const float *x_scale, const void *
                                int M, int N, int K, int accumulate, int num_sms, DevError *err, cudaStream_t st);
 // Rows -> e4m3 codes + one f32 scale per row (amax / 448): mode 0 bf16 rows,
 // 1 RMSNorm(f32 rows) x w, 2 SwiGLU of interleaved f32 gate/up rows [n][2K].
-cudaError_t prepare_rows_q8(int max_k);
+int rows_q8_max_k();   // widest row the quantiser takes (6144)
 cudaError_t launch_rows_q8(int mode, const void *in, int n, int K, const float *w, float eps, void *out, float *scales,
                            cudaStream_t st);
 cudaError_t launch_gemm_tc(const void *X, const void *W, float *C, int M, int N, int K, int accumulate, int num_sms,

@@ -246,7 +246,6 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
         h->fused_swiglu = !(fs && std::strcmp(fs, "0") == 0);
     }
     CK(prepare_dense(std::max(c.hidden, std::max(c.intermediate, kQDim))));
-    CK(prepare_rows_q8(std::max(c.hidden, std::max(c.intermediate, kQDim))));
     (void)gemm_tc_supported(1, 1, 64);   // resolve the tensor-map encoder before any capture
     CK(cudaStreamSynchronize(h->stream));
     return QKV_OK;
@@ -336,8 +335,9 @@ int find_tensor(qkv_handle *h, const GgufFile &f, const std::string &name, const
 int load_weights(qkv_handle *h, const GgufFile &f) {
     const qkv_model_config &c = h->cfg;
     const int64_t H = c.hidden, QD = kQDim, KD = kKvDim, F = c.intermediate, V = c.vocab, D = kHeadDim;
-    if (h->proj_fp8 && (H % 128 != 0 || F % 128 != 0))
-        return fail(h, QKV_ERR_INVALID_ARG, "FP8 weights need hidden and intermediate sizes that are multiples of 128");
+    if (h->proj_fp8 && (H % 128 != 0 || F % 128 != 0 || H > rows_q8_max_k() || F > rows_q8_max_k()))
+        return fail(h, QKV_ERR_INVALID_ARG,
+                    "FP8 weights need hidden and intermediate sizes that are multiples of 128 and at most 6144");
     // FP8 projection files: every projection an I8 tensor of e4m3 codes with
     // "<name>.scale" (f32, one per row), declared by a metadata key.
     std::string proj_format;
@@ -1921,11 +1921,8 @@ int qkv_gemm_fp8(const void *x, const float *x_scale, const void *w, const float
 }
 
 int qkv_quantize_rows_e4m3(const void *x_bf16, int32_t rows, int32_t k, void *codes, float *scales, void *stream) {
-    if (!x_bf16 || !codes || !scales || rows < 0 || k <= 0 || k > 12 * 1024) return QKV_ERR_INVALID_ARG;
-    static std::once_flag once;
-    static cudaError_t prep = cudaSuccess;
-    std::call_once(once, [] { prep = prepare_rows_q8(12 * 1024); });
-    if (prep != cudaSuccess) return QKV_ERR_CUDA;
+    if (!x_bf16 || !codes || !scales || rows < 0 || k <= 0 || k % 4 != 0 || k > rows_q8_max_k())
+        return QKV_ERR_INVALID_ARG;
     return launch_rows_q8(0, x_bf16, rows, k, nullptr, 0.0f, codes, scales, static_cast<cudaStream_t>(stream)) ==
                    cudaSuccess
                ? QKV_OK
