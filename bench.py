@@ -445,8 +445,18 @@ def run_ours(args) -> int:
             line["numa_per_rank"] = numa_ranks
         if cpu is not None:
             line["cpu_baseline"] = cpu
-        print(json.dumps(line), flush=True)
     dec.close()
+    if not args.no_model:
+        # The full model step the ASR user runs (config 2: 0.6B, 32 streams per
+        # GPU, greedy decode), measured after the KV step on the same ranks.
+        margs = argparse.Namespace(**vars(args))
+        margs.steps, margs.warmup, margs.weights = 50, 3, "bf16"
+        m = run_model(margs, ctx=(rank, local, world, dist), big=False)
+        if rank == 0 and m is not None:
+            line["model_decode_config2"] = {"value": m["value"], "unit": "tokens/s", "ms_per_step": m["ms_per_step"],
+                                            "steps": 50, "n_gpus": world, "metric": m["metric"]}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if dist is not None:
         dist.destroy_process_group()
     return 0
@@ -539,9 +549,13 @@ def run_readprobe(args) -> int:
     return 0
 
 
-def run_model(args) -> int:
+def run_model(args, ctx=None, big=None):
     """Config 2: 0.6B, bf16 weights + bf16 paged cache, 32 streams/GPU, prompts
-    U[100, 400] with 90% audio rows, greedy decode; value = decode tokens/s."""
+    U[100, 400] with 90% audio rows, greedy decode; value = decode tokens/s
+    (config 3 with --workload model3).  With ctx = (rank, local, world, dist)
+    from a caller that already set up the ranks, returns rank 0's line as a
+    dict (None elsewhere) instead of printing it, and leaves the process
+    group to the caller."""
     import tempfile
 
     import torch
@@ -549,9 +563,10 @@ def run_model(args) -> int:
     import __graft_entry__ as ge
     pkg = ge.load_package()
     synth = ge.load_synth()
-    rank, local, world, dist = dist_setup(args.gpus)
+    rank, local, world, dist = ctx if ctx is not None else dist_setup(args.gpus)
     torch.cuda.set_device(local)
-    big = args.workload == "model3"
+    if big is None:
+        big = args.workload == "model3"
     cfg = dict(synth.QWEN3_ASR_1_7B if big else synth.QWEN3_ASR_0_6B)
     n_streams = 64 if big else 32
     steps = args.steps
@@ -674,8 +689,11 @@ def run_model(args) -> int:
             "e2e": {"value": round(tokens / dt_max, 2), "unit": "tokens/s", "h2d_bytes_per_step": n_streams * 4 * 4,
                     "d2h_bytes_per_step": n_streams * 4, "note": "qkv_decode_step with host id buffers"},
             "gpu_launches": int(launches), "clocks": sampler.summary()}
-        print(json.dumps(line), flush=True)
+        if ctx is None:
+            print(json.dumps(line), flush=True)
     dec.close()
+    if ctx is not None:
+        return line if rank == 0 else None
     if dist is not None:
         dist.destroy_process_group()
     return 0
@@ -871,6 +889,8 @@ def run_prefill_attn(args) -> int:
     a different 107 MB block (bf16), so 28 of them exceed L2 between reuses).
     value = useful attention TFLOP/s (QK^T and PV of the causal triangle, 16 q
     heads, D = 128); roofline against the measured dense bf16 peak."""
+    global N_LAYERS
+    N_LAYERS = args.layers
     import torch
 
     import __graft_entry__ as ge
@@ -1062,6 +1082,8 @@ def main() -> int:
                     help="model / model3 / serve: projection weights (fp8 = e4m3 weights and token rows, "
                          "one scale per row, tcgen05 kind::f8f6f4)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-model", action="store_true",
+                    help="kv workload: skip the config-2 full-model decode figure added to the line")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="layers of cache (28 = the workload; fewer only for small profiling captures)")
     args = ap.parse_args()

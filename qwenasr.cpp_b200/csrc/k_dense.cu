@@ -601,30 +601,69 @@ __global__ void __launch_bounds__(256) argmax_refine_kernel(const float *logits,
     __syncthreads();
     const float thr = s_thr;
     const float *row = logits + static_cast<size_t>(r) * V;
-    const int ch = (V + S - 1) / S;
-    const int lo = sl * ch, hi = min(V, lo + ch);
-    for (int base = lo + warp * 32; base < hi; base += static_cast<int>(blockDim.x)) {
-        const int j = base + lane;
-        const bool cand = j < hi && row[j] >= thr;
-        unsigned mask = __ballot_sync(0xffffffffu, cand);
-        while (mask) {
-            const int jj = base + __ffs(mask) - 1;
-            mask &= mask - 1;
-            const __nv_bfloat16 *w = W + static_cast<size_t>(jj) * H;
-            float acc = 0.0f;
-            for (int k = lane * 8; k < H; k += 256) {   // H % 8 == 0 (checked at launch)
-                const uint4 q = *reinterpret_cast<const uint4 *>(w + k);
-                acc = fmaf(bf16lo(q.x), hs[k + 0], acc); acc = fmaf(bf16hi(q.x), hs[k + 1], acc);
-                acc = fmaf(bf16lo(q.y), hs[k + 2], acc); acc = fmaf(bf16hi(q.y), hs[k + 3], acc);
-                acc = fmaf(bf16lo(q.z), hs[k + 4], acc); acc = fmaf(bf16hi(q.z), hs[k + 5], acc);
-                acc = fmaf(bf16lo(q.w), hs[k + 6], acc); acc = fmaf(bf16hi(q.w), hs[k + 7], acc);
-            }
+    // Exact f32 score of token jj by the whole warp, merged into the row's key.
+    auto rescore = [&](int jj) {
+        const __nv_bfloat16 *w = W + static_cast<size_t>(jj) * H;
+        float acc = 0.0f;
+        for (int k = lane * 8; k < H; k += 256) {   // H % 8 == 0 (checked at launch)
+            const uint4 q = *reinterpret_cast<const uint4 *>(w + k);
+            acc = fmaf(bf16lo(q.x), hs[k + 0], acc); acc = fmaf(bf16hi(q.x), hs[k + 1], acc);
+            acc = fmaf(bf16lo(q.y), hs[k + 2], acc); acc = fmaf(bf16hi(q.y), hs[k + 3], acc);
+            acc = fmaf(bf16lo(q.z), hs[k + 4], acc); acc = fmaf(bf16hi(q.z), hs[k + 5], acc);
+            acc = fmaf(bf16lo(q.w), hs[k + 6], acc); acc = fmaf(bf16hi(q.w), hs[k + 7], acc);
+        }
 #pragma unroll
-            for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-            if (lane == 0) {
-                const uint32_t u = __float_as_uint(acc);
-                const uint32_t ou = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-                atomicMax(keys + r, (static_cast<unsigned long long>(ou) << 32) | (0xffffffffu - static_cast<uint32_t>(jj)));
+        for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) {
+            const uint32_t u = __float_as_uint(acc);
+            const uint32_t ou = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+            atomicMax(keys + r, (static_cast<unsigned long long>(ou) << 32) | (0xffffffffu - static_cast<uint32_t>(jj)));
+        }
+    };
+    const int nwarps = static_cast<int>(blockDim.x >> 5);
+    if ((V & 3) == 0) {
+        // Slices of whole float4 groups; a warp takes 128 groups (512 logits) per
+        // pass, four independent 16-byte loads per lane in flight at once.
+        const int v4 = V >> 2, ch4 = (v4 + S - 1) / S;
+        const int lo4 = sl * ch4, hi4 = min(v4, lo4 + ch4);
+        const float4 *row4 = reinterpret_cast<const float4 *>(row);
+        for (int c0 = lo4 + warp * 128; c0 < hi4; c0 += nwarps * 128) {
+            float4 a[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int idx = c0 + u * 32 + lane;
+                a[u] = idx < hi4 ? row4[idx] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+            }
+            uint32_t m = 0;   // bit 4u + c: component c of group u is a candidate
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                m |= (a[u].x >= thr ? 1u : 0u) << (4 * u);
+                m |= (a[u].y >= thr ? 1u : 0u) << (4 * u + 1);
+                m |= (a[u].z >= thr ? 1u : 0u) << (4 * u + 2);
+                m |= (a[u].w >= thr ? 1u : 0u) << (4 * u + 3);
+            }
+            unsigned who = __ballot_sync(0xffffffffu, m != 0);
+            while (who) {
+                const int src = __ffs(who) - 1;
+                who &= who - 1;
+                uint32_t mm = __shfl_sync(0xffffffffu, m, src);
+                while (mm) {
+                    const int b = __ffs(mm) - 1;
+                    mm &= mm - 1;
+                    rescore(4 * (c0 + (b >> 2) * 32 + src) + (b & 3));
+                }
+            }
+        }
+    } else {
+        const int ch = (V + S - 1) / S;
+        const int lo = sl * ch, hi = min(V, lo + ch);
+        for (int base = lo + warp * 32; base < hi; base += nwarps * 32) {
+            const int j = base + lane;
+            unsigned mask = __ballot_sync(0xffffffffu, j < hi && row[j] >= thr);
+            while (mask) {
+                const int jj = base + __ffs(mask) - 1;
+                mask &= mask - 1;
+                rescore(jj);
             }
         }
     }
