@@ -117,6 +117,14 @@ __global__ void __launch_bounds__(512) kv_append_kernel(AppendParams p) {
         x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
         x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
     }
+    // The projection left one partial sum per K split: add them in slice order.
+    for (int sl = 1; sl < p.qkv_slices; ++sl) {
+        const float *ps = src + static_cast<size_t>(sl) * p.qkv_slice_stride;
+        const float4 a = reinterpret_cast<const float4 *>(ps)[0];
+        const float4 b = reinterpret_cast<const float4 *>(ps)[1];
+        x[0] += a.x; x[1] += a.y; x[2] += a.z; x[3] += a.w;
+        x[4] += b.x; x[5] += b.y; x[6] += b.z; x[7] += b.w;
+    }
 
     // Warps 0-7 hold q units, 8-11 k units, 12-15 v units: the branch is warp-uniform.
     if (unit < kHq + kHkv) {

@@ -71,6 +71,10 @@ struct TcParams {
     // x_scale[m]; the epilogue multiplies each accumulator by both.
     const float *w_scale;
     const float *x_scale;
+    // Slice mode (> 0, split launches only): split s stores its partial sums
+    // into C + s x slice_stride instead of adding them into C, so C needs no
+    // zeroing, no atomics run, and the reader sums the slices in order.
+    size_t slice_stride;
 };
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar,
@@ -434,6 +438,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
                 if (n < p.N) {
                     float *dst = p.C + static_cast<size_t>(m0 + c) * p.N + n;
+                    const bool to_slice = split && p.slice_stride > 0;
+                    if (to_slice) dst += static_cast<size_t>(kt0 / p.ktiles_per_split) * p.slice_stride;
                     const int mlim = p.M - (m0 + c);
                     if (!split && p.accumulate) {
                         // Read the chunk's 32 C values first (one memory latency, not 32:
@@ -451,7 +457,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                             if (jj < mlim) {
                                 const float v = __uint_as_float(r[jj]);
                                 float *dp = dst + static_cast<size_t>(jj) * p.N;
-                                if (split) atomicAdd(dp, v);
+                                if (split && !to_slice) atomicAdd(dp, v);
                                 else *dp = v;
                             }
                         }
@@ -567,7 +573,7 @@ bool weight_fastest(int M, int K, int tiles_m) {
 template <int BN, bool F8 = false>
 cudaError_t launch_bn(const void *X, const void *W, float *C, int M, int N, int K, int accumulate, int splits,
                       int num_sms, DevError *err, cudaStream_t st, __nv_bfloat16 *act = nullptr,
-                      const float *w_scale = nullptr, const float *x_scale = nullptr) {
+                      const float *w_scale = nullptr, const float *x_scale = nullptr, bool slices = false) {
     CUtensorMap tw, tx;
     const int es = F8 ? 1 : 2;
     if (!cached_map(&tw, W, N, K, kBM, es) || !cached_map(&tx, X, M, K, BN, es)) return cudaErrorInvalidValue;
@@ -576,7 +582,8 @@ cudaError_t launch_bn(const void *X, const void *W, float *C, int M, int N, int 
     const int kps = (ktiles + splits - 1) / splits;
     splits = (ktiles + kps - 1) / kps;     // every split owns >= 1 k-tile
     if (act && splits != 1) return cudaErrorInvalidValue;
-    if (splits > 1 && !accumulate) {
+    if (slices && accumulate) return cudaErrorInvalidValue;
+    if (splits > 1 && !accumulate && !slices) {
         const size_t n = static_cast<size_t>(M) * N;
         cudaError_t e;
         if (n % 4 == 0 && (reinterpret_cast<uintptr_t>(C) & 15) == 0) {
@@ -589,7 +596,7 @@ cudaError_t launch_bn(const void *X, const void *W, float *C, int M, int N, int 
         if (e != cudaSuccess) return e;
     }
     TcParams p{M, N, K, kps, tiles_n, tiles_m, splits, weight_fastest(M, K * es / 2, tiles_m) ? 1 : 0, C, accumulate,
-               act, err, w_scale, x_scale};
+               act, err, w_scale, x_scale, slices && splits > 1 ? static_cast<size_t>(M) * N : size_t{0}};
     const int units = tiles_n * tiles_m * splits;
     const int grid = units < num_sms ? units : num_sms;
     return launch_pdl(gemm_tc_kernel<BN, F8>, dim3(grid), dim3(kGemmThreads), TcTraits<BN>::kSmem, st, tw, tx, p);
@@ -727,6 +734,41 @@ cudaError_t launch_gemm_tc_fp8(const void *X, const float *x_scale, const void *
         case 128: return launch_bn<128, true>(X, W, C, M, N, K, accumulate, pl.splits, num_sms, err, st, nullptr, w_scale, x_scale);
         default: return launch_bn<256, true>(X, W, C, M, N, K, accumulate, pl.splits, num_sms, err, st, nullptr, w_scale, x_scale);
     }
+}
+
+namespace {
+template <bool F8>
+cudaError_t launch_slices(const void *X, const float *x_scale, const void *W, const float *w_scale, float *C, int M,
+                          int N, int K, int max_slices, int num_sms, DevError *err, cudaStream_t st, int *slices) {
+    if (M <= 0 || N <= 0) {
+        *slices = 1;
+        return cudaSuccess;
+    }
+    if (K % kBKe<F8> != 0 || max_slices < 1) return cudaErrorInvalidValue;
+    const GemmPlan pl = plan_gemm(M, N, K, num_sms, false, F8);
+    const int ktiles = K / kBKe<F8>;
+    const int want = pl.splits < max_slices ? pl.splits : max_slices;
+    const int kps = (ktiles + want - 1) / want;
+    *slices = (ktiles + kps - 1) / kps;
+    switch (pl.bn) {
+        case 32: return launch_bn<32, F8>(X, W, C, M, N, K, 0, want, num_sms, err, st, nullptr, w_scale, x_scale, true);
+        case 64: return launch_bn<64, F8>(X, W, C, M, N, K, 0, want, num_sms, err, st, nullptr, w_scale, x_scale, true);
+        case 128: return launch_bn<128, F8>(X, W, C, M, N, K, 0, want, num_sms, err, st, nullptr, w_scale, x_scale, true);
+        default: return launch_bn<256, F8>(X, W, C, M, N, K, 0, want, num_sms, err, st, nullptr, w_scale, x_scale, true);
+    }
+}
+}  // namespace
+
+cudaError_t launch_gemm_tc_slices(const void *X, const void *W, float *C, int M, int N, int K, int max_slices,
+                                  int num_sms, DevError *err, cudaStream_t st, int *slices) {
+    return launch_slices<false>(X, nullptr, W, nullptr, C, M, N, K, max_slices, num_sms, err, st, slices);
+}
+
+cudaError_t launch_gemm_tc_fp8_slices(const void *X, const float *x_scale, const void *W, const float *w_scale,
+                                      float *C, int M, int N, int K, int max_slices, int num_sms, DevError *err,
+                                      cudaStream_t st, int *slices) {
+    if (!x_scale || !w_scale) return cudaErrorInvalidValue;
+    return launch_slices<true>(X, x_scale, W, w_scale, C, M, N, K, max_slices, num_sms, err, st, slices);
 }
 
 bool gemm_tc_swiglu_pays(int M, int N2, int K, int num_sms) {

@@ -73,6 +73,8 @@ struct AppendParams {
     float eps;
     DevError *err;
     int v_int8;                // 8-bit cache: 1 = V stored as int8 (kKvE4I8), 0 = e4m3
+    int qkv_slices;            // qkv holds this many partial-sum slices (>= 1), summed in order
+    size_t qkv_slice_stride;   // floats between slices
 };
 
 struct AttendParams {
@@ -178,6 +180,14 @@ int gemm_tc_kernels(int M, int N, int K, int accumulate, int num_sms);
 // FP8 projections (tcgen05 kind::f8f6f4, e4m3 x e4m3 -> f32, K % 128 == 0):
 // C (+)= (X x x_scale[m]) . (W x w_scale[n])^T with one scale per token row
 // of X and per weight row of W; same tiling, split and epilogues as bf16.
+// Slice mode: C = X . W^T as *slices partial products (one per K split, at
+// most max_slices) in C[s][M][N]; the reader sums them in slice order.  No
+// zeroing kernel, no atomics; C must hold max_slices x M x N floats.
+cudaError_t launch_gemm_tc_slices(const void *X, const void *W, float *C, int M, int N, int K, int max_slices,
+                                  int num_sms, DevError *err, cudaStream_t st, int *slices);
+cudaError_t launch_gemm_tc_fp8_slices(const void *X, const float *x_scale, const void *W, const float *w_scale,
+                                      float *C, int M, int N, int K, int max_slices, int num_sms, DevError *err,
+                                      cudaStream_t st, int *slices);
 bool gemm_tc_fp8_supported(int M, int N, int K);
 int gemm_tc_fp8_kernels(int M, int N, int K, int accumulate, int num_sms);
 cudaError_t launch_gemm_tc_fp8(const void *X, const float *x_scale, const void *W, const float *w_scale, float *C,

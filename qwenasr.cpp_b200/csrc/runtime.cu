@@ -189,6 +189,8 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
         CK(cudaMalloc(&h->attn, R * kQDim * act));
         CK(cudaMalloc(&h->gu, R * 2 * c.intermediate * sizeof(float)));
         CK(cudaMalloc(&h->act, R * c.intermediate * act));
+        CK(cudaMalloc(&h->qkv_sl, static_cast<size_t>(qkv_handle::kQkvMaxSlices) * h->rt.max_streams * kQkvDim *
+                                      sizeof(float)));
         if (h->proj_fp8) {
             CK(cudaMalloc(&h->xq, R * static_cast<size_t>(std::max(c.hidden, std::max(c.intermediate, kQDim)))));
             CK(cudaMalloc(&h->xq_s, R * sizeof(float)));
@@ -267,7 +269,7 @@ void destroy(qkv_handle *h) {
     cudaFree(h->x); cudaFree(h->qkv); cudaFree(h->q); cudaFree(h->gu); cudaFree(h->logits);
     cudaFree(h->am_v); cudaFree(h->am_i); cudaFree(h->am_cnt);
     cudaFree(h->am_keys); cudaFree(h->am_rcnt); cudaFree(h->d_wout_norm);
-    cudaFree(h->xn); cudaFree(h->attn); cudaFree(h->act); cudaFree(h->host_stage);
+    cudaFree(h->xn); cudaFree(h->attn); cudaFree(h->act); cudaFree(h->host_stage); cudaFree(h->qkv_sl);
     cudaFree(h->d_rowbuf); cudaFree(h->d_out_ids); cudaFree(h->d_items); cudaFree(h->part_o); cudaFree(h->part_ml);
     cudaFree(h->counters); cudaFree(h->d_err);
     cudaFreeHost(h->h_page_table); cudaFreeHost(h->h_items); cudaFreeHost(h->h_rowbuf); cudaFreeHost(h->h_out_ids); cudaFreeHost(h->h_err);
@@ -779,6 +781,11 @@ AppendParams append_params(qkv_handle *h, int layer, int n, const int *slots, co
     p.n_pages = h->n_pages;
     p.eps = h->cfg.rms_norm_eps;
     p.err = h->d_err;
+    p.qkv_slices = 1;
+    if (qkv && qkv == h->qkv_sl) {   // the projection left partial-sum slices
+        p.qkv_slices = h->qkv_nsl;
+        p.qkv_slice_stride = h->qkv_sl_stride;
+    }
     return p;
 }
 
@@ -891,6 +898,28 @@ cudaError_t gemm8(qkv_handle *h, const void *W, const float *w_s, float *C, int 
     return launch_gemm_tc_fp8(h->xq, h->xq_s, W, w_s, C, M, N, K, accumulate, h->num_sms, h->d_err, h->stream);
 }
 
+// The qkv projection of one layer: in slice mode for a decode-sized batch on
+// the tensor cores (returns h->qkv_sl), else into h->qkv.
+const float *qkv_projection(qkv_handle *h, const qkv_handle::Layer &L, int n, cudaError_t *e) {
+    const qkv_model_config &c = h->cfg;
+    const bool tc = h->proj_fp8 ? gemm_tc_fp8_supported(n, kQkvDim, c.hidden)
+                                : (h->act_dtype == kActBF16 && h->w_dtype == kActBF16 &&
+                                   gemm_tc_supported(n, kQkvDim, c.hidden));
+    if (tc && h->qkv_sl && n <= h->rt.max_streams) {
+        h->qkv_sl_stride = static_cast<size_t>(n) * kQkvDim;
+        h->launches += 1;
+        *e = h->proj_fp8 ? launch_gemm_tc_fp8_slices(h->xq, h->xq_s, L.w_qkv, L.s_qkv, h->qkv_sl, n, kQkvDim, c.hidden,
+                                                     qkv_handle::kQkvMaxSlices, h->num_sms, h->d_err, h->stream,
+                                                     &h->qkv_nsl)
+                         : launch_gemm_tc_slices(h->xn, L.w_qkv, h->qkv_sl, n, kQkvDim, c.hidden,
+                                                 qkv_handle::kQkvMaxSlices, h->num_sms, h->d_err, h->stream, &h->qkv_nsl);
+        return h->qkv_sl;
+    }
+    *e = h->proj_fp8 ? gemm8(h, L.w_qkv, L.s_qkv, h->qkv, n, kQkvDim, c.hidden, 0)
+                     : gemm(h, h->xn, L.w_qkv, h->qkv, n, kQkvDim, c.hidden, 0);
+    return h->qkv;
+}
+
 // One layer with FP8 projections: every projection input is quantised to
 // e4m3 rows with a scale per row by the kernel that builds it (RMSNorm,
 // SwiGLU) or right after (the attention output).
@@ -900,13 +929,15 @@ int run_layer_fp8(qkv_handle *h, const qkv_handle::Layer &L, int l, int n, const
     const float eps = c.rms_norm_eps;
     int rc;
     CK(launch_rows_q8(1, h->x, n, c.hidden, L.attn_norm, eps, h->xq, h->xq_s, h->stream));
-    CK(gemm8(h, L.w_qkv, L.s_qkv, h->qkv, n, kQkvDim, c.hidden, 0));
+    cudaError_t pe = cudaSuccess;
+    const float *qkv = qkv_projection(h, L, n, &pe);
+    CK(pe);
     if (!prompt) {
-        if ((rc = layer_kv(h, l, n, slots, pos, lens, h->qkv, h->q, h->attn, true, L.q_norm, L.k_norm, h->stream)))
+        if ((rc = layer_kv(h, l, n, slots, pos, lens, qkv, h->q, h->attn, true, L.q_norm, L.k_norm, h->stream)))
             return rc;
     } else {
         const bool tc = prefill_on_tc(h, items, n_items);
-        AppendParams ap = append_params(h, l, n, slots, pos, h->qkv, tc ? nullptr : h->q, L.q_norm, L.k_norm);
+        AppendParams ap = append_params(h, l, n, slots, pos, qkv, tc ? nullptr : h->q, L.q_norm, L.k_norm);
         if (tc) {
             ap.q16_out = h->q;
             ap.q16_scale = attn_scale_log2();
@@ -939,14 +970,16 @@ int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int
             continue;
         }
         CK(launch_rmsnorm(h->x, nullptr, n, c.hidden, L.attn_norm, c.rms_norm_eps, h->xn, h->act_dtype, h->stream));
-        CK(gemm(h, h->xn, L.w_qkv, h->qkv, n, kQkvDim, c.hidden, 0));
+        cudaError_t pe = cudaSuccess;
+        const float *qkv = qkv_projection(h, L, n, &pe);
+        CK(pe);
         if (!prompt) {
-            if ((rc = layer_kv(h, l, n, slots, pos, lens, h->qkv, h->q, h->attn, bf, L.q_norm, L.k_norm, h->stream)))
+            if ((rc = layer_kv(h, l, n, slots, pos, lens, qkv, h->q, h->attn, bf, L.q_norm, L.k_norm, h->stream)))
                 return rc;
         } else {
             // K3 takes q from K1 already scaled and rounded to its operand type.
             const bool tc = prefill_on_tc(h, items, n_items);
-            AppendParams ap = append_params(h, l, n, slots, pos, h->qkv, tc ? nullptr : h->q, L.q_norm, L.k_norm);
+            AppendParams ap = append_params(h, l, n, slots, pos, qkv, tc ? nullptr : h->q, L.q_norm, L.k_norm);
             if (tc) {
                 ap.q16_out = h->q;
                 ap.q16_scale = attn_scale_log2();

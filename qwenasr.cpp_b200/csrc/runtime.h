@@ -108,6 +108,13 @@ struct qkv_handle {
     // scale per weight row and take e4m3 token rows with a scale per row (xq,
     // xq_s); embeddings, the LM head and the audio projector stay bf16.
     bool proj_fp8 = false;
+    // qkv projection of a decode-sized batch in slice mode: one partial sum per
+    // K split in qkv_sl[s][rows][kQkvDim], summed in order by K1 (no zeroing
+    // kernel, no atomics, deterministic).
+    static constexpr int kQkvMaxSlices = 8;
+    float *qkv_sl = nullptr;
+    int qkv_nsl = 1;
+    size_t qkv_sl_stride = 0;
     uint8_t *xq = nullptr;      // [rows][max(H, Hq D, F)] e4m3 token operand
     float *xq_s = nullptr;      // [rows]
     int *d_out_ids = nullptr;   // [max_rows]
