@@ -194,6 +194,32 @@ def test_compaction_preserves_decoding(pkg, synth, tiny_files):
     assert moved >= 0
 
 
+@pytest.mark.parametrize("kv", [1, 2, 3])
+def test_compaction_moves_cache_bytes_and_scales(pkg, synth, tiny_files, kv):
+    """Compaction of a bf16 or 8-bit cache: after two streams close and the
+    pool is compacted, the surviving streams' K/V bytes (and, for the 8-bit
+    caches, their per-token scales) read back identical in every layer, and
+    decoding continues."""
+    cfg, files = tiny_files
+    path = files[("bf16", "one_plus")]
+    xs = prompts(synth, synth.read_gguf(path), 4, 71, lo=20, hi=70)
+    with decoder(pkg, path, w=1, kv=kv, seed=5, batch_tokens=512) as dec:
+        streams, _ = batched_ids(dec, xs, 4)
+        dec.close_stream(streams[0])
+        dec.close_stream(streams[2])
+        keep = [streams[1], streams[3]]
+        before = {(l, s): dec.gather(l, s, kv) for l in range(cfg["n_layers"]) for s in keep}
+        pages_before = [dec.pages(s).tolist() for s in keep]
+        moved = dec.compact()
+        after = {(l, s): dec.gather(l, s, kv) for l in range(cfg["n_layers"]) for s in keep}
+        assert moved > 0 and [dec.pages(s).tolist() for s in keep] != pages_before
+        for key in before:
+            for a, b in zip(before[key], after[key]):
+                assert np.array_equal(a, b), key
+        for _ in range(3):
+            dec.decode_step(keep)
+
+
 def test_stream_reuse_after_close(pkg, synth, checker, tiny_files):
     cfg, files = tiny_files
     path = files[("f32", "normal")]
