@@ -15,19 +15,24 @@
 //
 // CTA = HALVES x 8 consumer warps + 1 producer warp.  Consumer warp g (and,
 // with HALVES = 2, warp g + 8) serves kv head g (q heads 2g and 2g+1).  With
-// two halves, the warps of a head take alternate chunks of the ring, each with
-// its own online-softmax state; at the end of a segment warp g + 8 hands
-// (m, l, O) to warp g through shared memory (bounded flag waits) and warp g
-// merges.  The e4m3 cache uses two halves: a dequant per element on top of the
-// bf16 work needs twice the loads, conversions and FMA chains in flight per SM
-// to keep up with HBM.  A stage must always be consumed by the same half (a
-// warp that skipped a phase of a stage's mbarrier could otherwise see the
-// parity of the phase before it), so NS is a multiple of HALVES.  The producer streams each page chunk (all 8 heads, K and
+// two halves each warp keeps its own online-softmax state; at the end of a
+// segment warp g + 8 hands (m, l, O) to warp g through shared memory (bounded
+// flag waits) and warp g merges.  The halves share a head's work in one of two
+// ways.  bf16: both warps read every stage and each takes 8 of the page's 16
+// tokens, which halves the dependent chain (loads, dots, shuffles, exp2, PV)
+// a warp runs per page, so a stage is handed back sooner and more of the ring
+// is in flight.  8-bit caches: the warps take alternate chunks of a 6-stage
+// ring (a dequant per element on top of the bf16 work needs twice the loads,
+// conversions and FMA chains in flight); a stage must then always be consumed
+// by the same half (a warp that skipped a phase of a stage's mbarrier could
+// otherwise see the parity of the phase before it), so NS is a multiple of
+// HALVES.  The producer streams each page chunk (all 8 heads, K and
 // V) into an NS-stage shared-memory ring with cp.async.bulk (no tensor map,
 // no multicast), completion on mbarriers.  Every wait is bounded.
 //
 // Consumer math per chunk of CH tokens (bf16/fp8: CH = 16 = one page, f32: 8):
-//   QK: lane = (quarter qt, dim group j): tokens qt*CH/4.., dims = 16 per lane
+//   QK: lane = (quarter qt, dim group j): tokens qt*WT/4.. of the warp's WT
+//       tokens (WT = CH, or CH / 2 when the halves split the tokens), dims = 16 per lane
 //       in 16-byte chunks j, j+8, ... (conflict-free smem reads), partial dots
 //       reduce-scattered over the 8 lanes of the quarter.
 //   softmax: online (running max m, sum l) in the log2 domain (q pre-scaled
@@ -45,10 +50,22 @@ namespace qkv {
 
 namespace {
 
+// CH: tokens per ring chunk; NS: ring stages; HALVES: consumer warps per kv
+// head; TSPLIT: with two halves, whether they split each chunk's tokens
+// (true: both read every stage) or take alternate chunks (false).
 template <typename TC> struct AttnTraits;
-template <> struct AttnTraits<__nv_bfloat16> { static constexpr int CH = 16, NS = 3, HALVES = 1; };
-template <> struct AttnTraits<float> { static constexpr int CH = 8, NS = 3, HALVES = 1; };
-template <> struct AttnTraits<uint8_t> { static constexpr int CH = 16, NS = 6, HALVES = 2; };
+template <> struct AttnTraits<__nv_bfloat16> {
+    static constexpr int CH = 16, NS = 3, HALVES = 2;
+    static constexpr bool TSPLIT = true;
+};
+template <> struct AttnTraits<float> {
+    static constexpr int CH = 8, NS = 3, HALVES = 1;
+    static constexpr bool TSPLIT = false;
+};
+template <> struct AttnTraits<uint8_t> {
+    static constexpr int CH = 16, NS = 6, HALVES = 2;
+    static constexpr bool TSPLIT = false;
+};
 
 template <typename TC> __host__ __device__ constexpr int consumers() { return kHkv * AttnTraits<TC>::HALVES; }
 template <typename TC> __host__ __device__ constexpr int threads() { return (consumers<TC>() + 1) * 32; }
@@ -206,10 +223,13 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
     constexpr int kHalves = AttnTraits<TC>::HALVES;
     constexpr int kConsumers = consumers<TC>();
     constexpr int kThreads = threads<TC>();
-    static_assert(NS % kHalves == 0, "each stage must be consumed by one half");
+    constexpr bool kTSplit = AttnTraits<TC>::TSPLIT;
+    static_assert(kTSplit || NS % kHalves == 0, "each stage must be consumed by one half");
+    static_assert(!kTSplit || (kHalves == 2 && sizeof(TC) == 2), "token split: bf16, two halves");
     constexpr int CPP = kPageTokens / CH;          // chunks per page
     constexpr int HALF = kHkv * CH * kHeadDim;      // elements of K (or V) in a stage
-    constexpr int TPQ = CH / 4;                     // tokens per quarter-warp
+    constexpr int WT = kTSplit ? CH / kHalves : CH; // tokens of a chunk one warp takes
+    constexpr int TPQ = WT / 4;                     // tokens per quarter-warp
     constexpr int NV = 2 * TPQ;                     // partial dots per lane
     constexpr int E = Chunk16<TC>::E;               // elements per 16-byte chunk
     constexpr int NC = 16 / E;                      // chunks per lane per row (16 dims)
@@ -264,7 +284,9 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
         for (int k = 0; k < kHkv; ++k) xseq[k] = xack[k] = 0;
         for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kHkv);     // one arrival per kv head: the warp that took the chunk
+            // one arrival per warp that reads the chunk: both halves with a token
+            // split, else the one warp per kv head that took it
+            mbar_init(&empty[s], kTSplit ? kConsumers : kHkv);
         }
         fence_mbar_init();
     }
@@ -408,7 +430,8 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
 
     // ============ consumer warps: warps g and g + 8 <-> kv head g ============
     const int g = warp % kHkv;
-    const int half = warp / kHkv;                   // takes the chunks with iter % 2 == half
+    const int half = warp / kHkv;                   // alternate chunks: takes those with iter % 2 == half;
+                                                    // token split: takes tokens [half * WT, half * WT + WT)
     const int qt = lane >> 3, j = lane & 7;
     const int k_idx = j >> KSHIFT;
     const int my_head = k_idx & 1;                   // which of the two q heads this lane's score is
@@ -463,7 +486,7 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
         for (int jp = j0; jp < j1 && !abort; ++jp) {
 #pragma unroll 1
             for (int cp = 0; cp < CPP; ++cp) {
-                if (iter % kHalves != half) {   // the partner warp takes this chunk
+                if (!kTSplit && iter % kHalves != half) {   // the partner warp takes this chunk
                     ++iter;
                     continue;
                 }
@@ -477,10 +500,11 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
                     abort = true;
                     break;
                 }
-                const int tok0 = jp * kPageTokens + cp * CH;
-                const int nvalid = len - tok0 < CH ? len - tok0 : CH;
+                const int wt0 = kTSplit ? half * WT : 0;    // first token of this warp's share
+                const int tok0 = jp * kPageTokens + cp * CH + wt0;
+                const int nvalid = len - tok0 < WT ? len - tok0 : WT;
                 if (nvalid > 0) {
-                    const TC *kst = stages + static_cast<size_t>(s) * (2 * HALF) + g * CH * kHeadDim;
+                    const TC *kst = stages + static_cast<size_t>(s) * (2 * HALF) + (g * CH + wt0) * kHeadDim;
                     const TC *vst = kst + HALF;
                     // 8-bit caches: the lane's token's K scale, and its V scale as a
                     // ratio to the largest V scale of the chunk's valid tokens (the
@@ -578,9 +602,9 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
                                 axpy2_f16_f32<0>(xb[0], xb[1], x, wb); axpy2_f16_f32<0>(xb[2], xb[3], y, wb);
                             }
                         };
-                        if (nvalid == CH) {     // full page: no per-token guard
+                        if (nvalid == WT) {     // full page: no per-token guard
 #pragma unroll
-                            for (int t4 = 0; t4 < CH; t4 += 4) {
+                            for (int t4 = 0; t4 < WT; t4 += 4) {
                                 const uint2 pa = *reinterpret_cast<const uint2 *>(phalf + t4);
                                 const uint2 pb = *reinterpret_cast<const uint2 *>(phalf + CH + t4);
                                 pv_token(t4 + 0, pa.x, pb.x, 0);
@@ -590,7 +614,7 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
                             }
                         } else {
 #pragma unroll
-                            for (int t4 = 0; t4 < CH; t4 += 4) {
+                            for (int t4 = 0; t4 < WT; t4 += 4) {
                                 const uint2 pa = *reinterpret_cast<const uint2 *>(phalf + t4);
                                 const uint2 pb = *reinterpret_cast<const uint2 *>(phalf + CH + t4);
                                 if (t4 + 0 < nvalid) pv_token(t4 + 0, pa.x, pb.x, 0);
@@ -611,7 +635,7 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
                             ob[e] *= al_b;
                         }
 #pragma unroll
-                        for (int t4 = 0; t4 < CH; t4 += 4) {
+                        for (int t4 = 0; t4 < WT; t4 += 4) {
                             const float4 pa4 = *reinterpret_cast<const float4 *>(my_p + t4);
                             const float4 pb4 = *reinterpret_cast<const float4 *>(my_p + CH + t4);
                             const float pa[4] = {pa4.x, pa4.y, pa4.z, pa4.w};
