@@ -13,174 +13,17 @@
 // Each lane writes its 8 dims with one 16-byte store (bf16) / two (f32).
 #include "kernels.h"
 
+#include "kappend.cuh"
+
 namespace qkv {
 
 namespace {
-
-template <typename TC> struct PageStore;
-template <> struct PageStore<float> {
-    static __device__ __forceinline__ void put(float *dst, const float (&v)[8], float) {
-        reinterpret_cast<float4 *>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
-        reinterpret_cast<float4 *>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
-    }
-};
-template <> struct PageStore<__nv_bfloat16> {
-    static __device__ __forceinline__ void put(__nv_bfloat16 *dst, const float (&v)[8], float) {
-        uint4 w;
-        w.x = pack_bf16x2(v[0], v[1]);
-        w.y = pack_bf16x2(v[2], v[3]);
-        w.z = pack_bf16x2(v[4], v[5]);
-        w.w = pack_bf16x2(v[6], v[7]);
-        *reinterpret_cast<uint4 *>(dst) = w;
-    }
-};
-template <> struct PageStore<uint8_t> {
-    static __device__ __forceinline__ void put(uint8_t *dst, const float (&v)[8], float inv_scale) {
-        uint32_t lo = 0, hi = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) lo |= static_cast<uint32_t>(f_to_e4m3(v[j] * inv_scale)) << (8 * j);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) hi |= static_cast<uint32_t>(f_to_e4m3(v[4 + j] * inv_scale)) << (8 * j);
-        *reinterpret_cast<uint2 *>(dst) = make_uint2(lo, hi);
-    }
-};
-
-// V half of the e4m3-K / int8-V cache: excess-128 int8 bytes.
-struct PageStoreI8 {
-    static __device__ __forceinline__ void put(uint8_t *dst, const float (&v)[8], float inv_scale) {
-        uint32_t lo = 0, hi = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) lo |= f_to_u8ex(v[j] * inv_scale) << (8 * j);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) hi |= f_to_u8ex(v[4 + j] * inv_scale) << (8 * j);
-        *reinterpret_cast<uint2 *>(dst) = make_uint2(lo, hi);
-    }
-};
-
-// Per-head RMSNorm (double mean square, as text-decoder.cpp:542-557) and NEOX
-// RoPE (:604-625) of the 8 dims a half-warp lane holds; lane l16 ^ 8 holds the
-// rotation partners.  Must be called by all 32 lanes of the warp.
-__device__ __forceinline__ void norm_rope8(float (&x)[8], const float *w8, const float2 *cs8, int l16, float eps) {
-    double ss = 0.0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) ss += static_cast<double>(x[j]) * x[j];
-#pragma unroll
-    for (int o = 8; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const double ms = ss / static_cast<double>(kHeadDim);
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(ms), eps)));
-    float y[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) y[j] = __fmul_rn(__fmul_rn(x[j], scale), w8[j]);
-    const bool lower = l16 < 8;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const float other = __shfl_xor_sync(0xffffffffu, y[j], 8);
-        const float2 t = cs8[j];
-        if (lower) {  // row[i] = a*c - b*s   (a = own, b = partner)
-            x[j] = __fsub_rn(__fmul_rn(y[j], t.x), __fmul_rn(other, t.y));
-        } else {      // row[half+i] = b*c + a*s   (b = own, a = partner)
-            x[j] = __fadd_rn(__fmul_rn(y[j], t.x), __fmul_rn(other, t.y));
-        }
-    }
-}
 
 template <typename TC>
 __global__ void __launch_bounds__(512) kv_append_kernel(AppendParams p) {
     pdl_trigger();
     pdl_wait();   // everything below reads or writes memory of earlier kernels
-    const int row = blockIdx.x;
-    const int unit = threadIdx.x >> 4;      // 0..31
-    const int l16 = threadIdx.x & 15;
-    const int slot = p.slots[row];
-    const int pos = p.positions[row];
-    int page = -1;
-    bool ok = slot >= 0 && slot < p.max_streams && pos >= 0 && pos < p.rope_len &&
-              pos / kPageTokens < p.maxp;
-    if (ok) {
-        page = p.page_table[static_cast<size_t>(slot) * p.maxp + pos / kPageTokens];
-        ok = page >= 0 && page < p.n_pages;
-    }
-    if (!ok) {  // block-uniform: nothing is written for this row
-        if (threadIdx.x == 0) report_error(p.err, page < 0 ? kErrPosition : kErrPageIndex, kWhereAppend, row, pos);
-        return;
-    }
-
-    int src_off;
-    if (unit < kHq) src_off = unit * kHeadDim;
-    else if (unit < kHq + kHkv) src_off = kQDim + (unit - kHq) * kHeadDim;
-    else src_off = kQDim + kKvDim + (unit - kHq - kHkv) * kHeadDim;
-    const float *src = p.qkv + static_cast<size_t>(row) * kQkvDim + src_off + l16 * 8;
-    float x[8];
-    {
-        const float4 a = reinterpret_cast<const float4 *>(src)[0];
-        const float4 b = reinterpret_cast<const float4 *>(src)[1];
-        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
-        x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-    }
-    // The projection left one partial sum per K split: add them in slice order.
-    for (int sl = 1; sl < p.qkv_slices; ++sl) {
-        const float *ps = src + static_cast<size_t>(sl) * p.qkv_slice_stride;
-        const float4 a = reinterpret_cast<const float4 *>(ps)[0];
-        const float4 b = reinterpret_cast<const float4 *>(ps)[1];
-        x[0] += a.x; x[1] += a.y; x[2] += a.z; x[3] += a.w;
-        x[4] += b.x; x[5] += b.y; x[6] += b.z; x[7] += b.w;
-    }
-
-    // Warps 0-7 hold q units, 8-11 k units, 12-15 v units: the branch is warp-uniform.
-    if (unit < kHq + kHkv) {
-        // NEOX rotate-half: dim i (< 64) pairs with dim i + 64, held by lane l16 ^ 8.
-        norm_rope8(x, (unit < kHq ? p.q_norm_w : p.k_norm_w) + l16 * 8,
-                   p.rope + static_cast<size_t>(pos) * (kHeadDim / 2) + (l16 & 7) * 8, l16, p.eps);
-    }
-
-    if (unit < kHq) {
-        const size_t off = static_cast<size_t>(row) * kQDim + unit * kHeadDim + l16 * 8;
-        if (p.q16_out) {
-            // Prefill rows for K3: q x scale rounded once to the MMA operand type.
-            const float s = p.q16_scale;
-            uint4 w;
-            if (p.q16_f16) w = make_uint4(pack_h2(x[0] * s, x[1] * s), pack_h2(x[2] * s, x[3] * s),
-                                          pack_h2(x[4] * s, x[5] * s), pack_h2(x[6] * s, x[7] * s));
-            else w = make_uint4(pack_bf16x2(x[0] * s, x[1] * s), pack_bf16x2(x[2] * s, x[3] * s),
-                                pack_bf16x2(x[4] * s, x[5] * s), pack_bf16x2(x[6] * s, x[7] * s));
-            *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.q16_out) + off) = w;
-        }
-        if (p.q_out) {
-            float *dst = p.q_out + off;
-            reinterpret_cast<float4 *>(dst)[0] = make_float4(x[0], x[1], x[2], x[3]);
-            reinterpret_cast<float4 *>(dst)[1] = make_float4(x[4], x[5], x[6], x[7]);
-        }
-        return;
-    }
-    const int kv = unit < kHq + kHkv ? 0 : 1;
-    const int g = (unit - kHq) & (kHkv - 1);
-    const int tok = pos & (kPageTokens - 1);
-    float inv_scale = 1.0f;
-    if constexpr (sizeof(TC) == 1) {
-        // 8-bit caches: every stored (token, head) vector gets its own scale,
-        // amax / qmax over its 128 elements (K after norm and RoPE, V raw), so
-        // no stored token is ever re-quantised and no headroom is kept.
-        float amax = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(x[j]));
-#pragma unroll
-        for (int o = 8; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        const float qmax = (kv == 1 && p.v_int8) ? kI8Max : kE4m3Max;
-        const float scale = amax > 0.0f ? __fdiv_rn(amax, qmax) : 1.0f;
-        inv_scale = amax > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
-        if (l16 == 0)
-            p.scales[((static_cast<size_t>(page) * 2 + kv) * kHkv + g) * kPageTokens + tok] = scale;
-    }
-    TC *pool = static_cast<TC *>(p.pool);
-    TC *dst = pool + ((static_cast<size_t>(page) * 2 + kv) * kHkv + g) * (kPageTokens * kHeadDim) +
-              tok * kHeadDim + l16 * 8;
-    if constexpr (sizeof(TC) == 1) {
-        if (kv == 1 && p.v_int8) {   // warp-uniform (warps 12..15 hold V)
-            PageStoreI8::put(dst, x, inv_scale);
-            return;
-        }
-    }
-    PageStore<TC>::put(dst, x, inv_scale);
+    append_row_unit<TC>(p, blockIdx.x, threadIdx.x >> 4, threadIdx.x & 15);
 }
 
 // Page gather: tokens [0, len) of one stream -> contiguous [len][Hkv*D] (K and V).

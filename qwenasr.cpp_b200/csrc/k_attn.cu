@@ -13,7 +13,8 @@
 // index is unique per segment) and the last of its segments to finish (per kv
 // head, atomic counter) merges them.  Counters reset themselves.
 //
-// CTA = HALVES x 8 consumer warps + 1 producer warp.  Consumer warp g (and,
+// CTA = HALVES x 8 consumer warps + 1 producer warp + 3 append warps (busy
+// only with the append-ahead of the next layer, AttendParams::next).  Consumer warp g (and,
 // with HALVES = 2, warp g + 8) serves kv head g (q heads 2g and 2g+1).  With
 // two halves each warp keeps its own online-softmax state; at the end of a
 // segment warp g + 8 hands (m, l, O) to warp g through shared memory (bounded
@@ -44,6 +45,7 @@
 #include <cstring>
 #include <mutex>
 
+#include "kappend.cuh"
 #include "qkv.h"
 
 namespace qkv {
@@ -68,7 +70,13 @@ template <> struct AttnTraits<uint8_t> {
 };
 
 template <typename TC> __host__ __device__ constexpr int consumers() { return kHkv * AttnTraits<TC>::HALVES; }
-template <typename TC> __host__ __device__ constexpr int threads() { return (consumers<TC>() + 1) * 32; }
+// Warps that do the append-ahead (AttendParams::next), idle otherwise: three
+// keep the CTA at 5 warps per scheduler with the consumers' register budget
+// unchanged.
+constexpr int kAppendWarps = 3;
+template <typename TC> __host__ __device__ constexpr int threads() {
+    return (consumers<TC>() + 1 + kAppendWarps) * 32;
+}
 
 template <typename TC> __host__ __device__ constexpr uint32_t stage_bytes() {
     return 2u * kHkv * AttnTraits<TC>::CH * kHeadDim * sizeof(TC);
@@ -246,7 +254,7 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
     float *xo = pbuf + kConsumers * 2 * CH;                                // [kHkv][32 lanes][8]
     float *xml = xo + kHkv * 32 * 8;                                       // [kHkv][m_a, l_a, m_b, l_b]
     int *row_start = reinterpret_cast<int *>(xml + kHkv * 4);             // [kAttnMaxRows + 1]
-    int *scan = row_start + kAttnMaxRows + 1;       // [0..16] warp totals, [24] abort flag
+    int *scan = row_start + kAttnMaxRows + 1;       // [0..19] warp totals, [24] abort flag
     volatile int *abort_flag = scan + 24;
     volatile int *xseq = scan + 32;                 // [kHkv] segments handed over by warp g + 8
     volatile int *xack = xseq + kHkv;               // [kHkv] segments merged by warp g
@@ -321,6 +329,22 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
         r0 = lo;
     }
 
+    static_assert(kConsumers + 1 + kAppendWarps <= 24, "warp totals must fit below the abort flag");
+    if (warp > kConsumers) {
+        // ===== append warps: K1's work for the next layer (append-ahead) =====
+        // Rows dealt evenly over the G active CTAs, 16 warp tasks per row
+        // (two half-warp units each), after the grid dependency wait: the
+        // next layer's q buffer was read by the launch before this one.
+        const AppendParams &a = p.next;
+        if (a.n <= 0) return;
+        pdl_wait();
+        const int ra = static_cast<int>(c * a.n / G), rb = static_cast<int>((c + 1) * a.n / G);
+        const int aw = warp - kConsumers - 1;
+#pragma unroll 1
+        for (int task = aw; task < (rb - ra) * 16; task += kAppendWarps)
+            append_row_unit<TC>(a, ra + task / 16, 2 * (task % 16) + (lane >> 4), lane & 15);
+        return;
+    }
     if (warp == kConsumers) {
         // ================= producer warp =================
         const uint64_t pol = l2_evict_first_policy();
@@ -439,7 +463,7 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
     float *my_p = pbuf + warp * (2 * CH);
     TOut *out = static_cast<TOut *>(p.out);
 
-    if (p.early) pdl_wait();   // q and the merge scratch come from the preceding kernels
+    if (p.early) pdl_wait();   // q (or qkv) and the merge scratch come from the preceding kernels
     int iter = 0;
     int nseg = 0;                                   // segments finished (both halves count alike)
     int r = r0;

@@ -95,11 +95,18 @@ struct AttendParams {
     float scale_log2;          // log2(e) / sqrt(head_dim)
     DevError *err;
     // 1: the kernel(s) just before this launch on the stream wrote only each
-    // row's LAST page (one new token per row: K1, the e4m3 page-scale pass),
-    // and the row arrays and page table came from copies that finished before
-    // them, so K2 may set up and stream the other pages before its grid
-    // dependency wait.  0: everything waits (any caller).
+    // row's LAST page (one new token per row: K1), or, with the fused append,
+    // wrote no page at all, and the row arrays and page table came from copies
+    // that finished before them, so K2 may set up and stream the other pages
+    // before its grid dependency wait.  0: everything waits (any caller).
     int early;
+    // Append-ahead (KV steps, where every layer's projections are on the
+    // device before the step starts): with next.n > 0, K2 of layer l also
+    // does K1's work for layer l + 1 on its three append warps (rows dealt
+    // evenly over the CTAs, after the grid dependency wait), so that layer's
+    // pages and q are ready when its K2 starts and no append sits between
+    // two attention launches.  next.q_out must not be this launch's q.
+    AppendParams next;
 };
 
 struct PrefillAttnParams {

@@ -183,6 +183,7 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
     const size_t act = h->act_dtype == kActF32 ? 4 : 2;
     CK(cudaMalloc(&h->qkv, R * kQkvDim * sizeof(float)));
     CK(cudaMalloc(&h->q, R * kQDim * sizeof(float)));
+    CK(cudaMalloc(&h->q_alt, static_cast<size_t>(h->rt.max_streams) * kQDim * sizeof(float)));
     if (with_model_scratch) {
         CK(cudaMalloc(&h->x, R * c.hidden * sizeof(float)));
         CK(cudaMalloc(&h->xn, R * c.hidden * act));
@@ -246,6 +247,8 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
         h->prefill_tc = !(pa && std::strcmp(pa, "cuda_core") == 0);
         const char *fs = getenv("QWENASR_B200_FUSED_SWIGLU");
         h->fused_swiglu = !(fs && std::strcmp(fs, "0") == 0);
+        const char *aa = getenv("QWENASR_B200_APPEND_AHEAD");
+        h->append_ahead = !(aa && std::strcmp(aa, "0") == 0);
     }
     CK(prepare_dense(std::max(c.hidden, std::max(c.intermediate, kQDim))));
     (void)gemm_tc_supported(1, 1, 64);   // resolve the tensor-map encoder before any capture
@@ -266,7 +269,7 @@ void destroy(qkv_handle *h) {
     cudaFree(h->ap_norm_w); cudaFree(h->ap_norm_b); cudaFree(h->ap_w0); cudaFree(h->ap_b0); cudaFree(h->ap_w1);
     cudaFree(h->ap_b1);
     cudaFree(h->pool); cudaFree(h->scales); cudaFree(h->d_page_table); cudaFree(h->d_rope);
-    cudaFree(h->x); cudaFree(h->qkv); cudaFree(h->q); cudaFree(h->gu); cudaFree(h->logits);
+    cudaFree(h->x); cudaFree(h->qkv); cudaFree(h->q); cudaFree(h->q_alt); cudaFree(h->gu); cudaFree(h->logits);
     cudaFree(h->am_v); cudaFree(h->am_i); cudaFree(h->am_cnt);
     cudaFree(h->am_keys); cudaFree(h->am_rcnt); cudaFree(h->d_wout_norm);
     cudaFree(h->xn); cudaFree(h->attn); cudaFree(h->act); cudaFree(h->host_stage); cudaFree(h->qkv_sl);
@@ -781,6 +784,7 @@ AppendParams append_params(qkv_handle *h, int layer, int n, const int *slots, co
     p.n_pages = h->n_pages;
     p.eps = h->cfg.rms_norm_eps;
     p.err = h->d_err;
+    p.v_int8 = h->rt.kv_dtype == kKvE4I8 ? 1 : 0;
     p.qkv_slices = 1;
     if (qkv && qkv == h->qkv_sl) {   // the projection left partial-sum slices
         p.qkv_slices = h->qkv_nsl;
@@ -811,7 +815,7 @@ AttendParams attend_params(qkv_handle *h, int layer, int n, const int *slots, co
     return p;
 }
 
-// Append + attend for `n` rows of one layer (rows: slots/pos/lens device arrays).
+// Append + attend for `n` decode rows of one layer (rows: slots/pos/lens device arrays).
 int layer_kv(qkv_handle *h, int layer, int n, const int *slots, const int *pos, const int *lens, const float *qkv,
              float *q, void *out, bool out_bf16, const float *qn, const float *kn, cudaStream_t st) {
     AppendParams ap = append_params(h, layer, n, slots, pos, qkv, q, qn, kn);
@@ -820,6 +824,31 @@ int layer_kv(qkv_handle *h, int layer, int n, const int *slots, const int *pos, 
     at.early = 1;   // K1 just appended one token per row (see AttendParams::early)
     CK(launch_decode_attn(at, h->rt.kv_dtype, out_bf16, h->num_sms, st));
     h->launches += 2;
+    return QKV_OK;
+}
+
+// One layer of a KV step whose every layer's projections are on the device
+// (qkv_l: this layer's rows; qkv_next: layer l + 1's, or null for the last
+// layer).  With the append-ahead, layer 0 gets K1 and every layer's K2 also
+// appends layer l + 1; q alternates between two buffers by layer parity.
+int kv_step_layer(qkv_handle *h, int l, int n, const int *slots, const int *pos, const int *lens, const float *qkv_l,
+                  const float *qkv_next, float *out, cudaStream_t st) {
+    const qkv_handle::Layer &L = h->layers[static_cast<size_t>(l)];
+    if (!h->append_ahead) return layer_kv(h, l, n, slots, pos, lens, qkv_l, h->q, out, false, L.q_norm, L.k_norm, st);
+    float *q_cur = (l & 1) ? h->q_alt : h->q;
+    float *q_next = (l & 1) ? h->q : h->q_alt;
+    if (l == 0) {
+        CK(launch_kv_append(append_params(h, 0, n, slots, pos, qkv_l, q_cur, L.q_norm, L.k_norm), h->rt.kv_dtype, st));
+        h->launches += 1;
+    }
+    AttendParams at = attend_params(h, l, n, slots, lens, q_cur, out);
+    at.early = 1;   // the kernel before (K1 or K2 of layer l - 1) wrote only each row's last page of this layer
+    if (qkv_next) {
+        const qkv_handle::Layer &Ln = h->layers[static_cast<size_t>(l + 1)];
+        at.next = append_params(h, l + 1, n, slots, pos, qkv_next, q_next, Ln.q_norm, Ln.k_norm);
+    }
+    CK(launch_decode_attn(at, h->rt.kv_dtype, false, h->num_sms, st));
+    h->launches += 1;
     return QKV_OK;
 }
 
@@ -1692,11 +1721,11 @@ int qkv_kv_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const float
     if ((rc = row_upload(h, hs, static_cast<size_t>(3 * n), st))) return rc;
     const size_t in_stride = static_cast<size_t>(n) * kQkvDim, out_stride = static_cast<size_t>(n) * kQDim;
     auto body = [&](cudaStream_t on) -> int {
-        for (int l = 0; l < h->cfg.n_layers; ++l) {
-            const qkv_handle::Layer &L = h->layers[static_cast<size_t>(l)];
+        const int L = h->cfg.n_layers;
+        for (int l = 0; l < L; ++l) {
             int r;
-            if ((r = layer_kv(h, l, n, ds, dp, dl, qkv_dev + in_stride * l, h->q, out_dev + out_stride * l, false,
-                              L.q_norm, L.k_norm, on)))
+            if ((r = kv_step_layer(h, l, n, ds, dp, dl, qkv_dev + in_stride * l,
+                                   l + 1 < L ? qkv_dev + in_stride * (l + 1) : nullptr, out_dev + out_stride * l, on)))
                 return r;
         }
         return QKV_OK;
@@ -1721,9 +1750,10 @@ int qkv_kv_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const float
 }
 
 // Host-buffer KV step, pipelined by layer: layer l's inputs go up on
-// copy_in while earlier layers compute, layer l's kernels wait only for its own
-// inputs, and its outputs come back on copy_out as soon as its attention has
-// run, so PCIe traffic in both directions overlaps the kernels.
+// copy_in while earlier layers compute, layer l's kernels wait only for the
+// inputs they read (their own, and layer l + 1's with the append-ahead), and
+// layer l's outputs come back on copy_out as soon as its attention has run,
+// so PCIe traffic in both directions overlaps the kernels.
 int qkv_kv_step_host(qkv_handle *h, int32_t n, const int32_t *stream_ids, const float *qkv_host, float *out_host) {
     const TraceRange trace("qkv_kv_step_host");
     if (!h) return QKV_ERR_INVALID_ARG;
@@ -1779,10 +1809,12 @@ int qkv_kv_step_host(qkv_handle *h, int32_t n, const int32_t *stream_ids, const 
         CK(cudaEventRecord(h->ev_in[static_cast<size_t>(l)], h->copy_in));
     }
     for (int l = 0; l < L; ++l) {
-        const qkv_handle::Layer &Ly = h->layers[static_cast<size_t>(l)];
         CK(cudaStreamWaitEvent(h->stream, h->ev_in[static_cast<size_t>(l)], 0));
-        if ((rc = layer_kv(h, l, n, ds, dp, dl, stage_in + in_stride * l, h->q, stage_out + out_stride * l, false,
-                           Ly.q_norm, Ly.k_norm, h->stream)))
+        // With the append-ahead, layer l's launch also reads layer l + 1's inputs.
+        if (h->append_ahead && l + 1 < L) CK(cudaStreamWaitEvent(h->stream, h->ev_in[static_cast<size_t>(l + 1)], 0));
+        if ((rc = kv_step_layer(h, l, n, ds, dp, dl, stage_in + in_stride * l,
+                                l + 1 < L ? stage_in + in_stride * (l + 1) : nullptr, stage_out + out_stride * l,
+                                h->stream)))
             break;
         CK(cudaEventRecord(h->ev_done[static_cast<size_t>(l)], h->stream));
         CK(cudaStreamWaitEvent(h->copy_out, h->ev_done[static_cast<size_t>(l)], 0));

@@ -66,6 +66,7 @@ struct qkv_handle {
     // scratch (rows = max(max_batch_tokens, max_streams))
     int max_rows = 0;
     float *x = nullptr, *qkv = nullptr, *q = nullptr, *gu = nullptr, *logits = nullptr;
+    float *q_alt = nullptr;   // [max_streams][kQDim]: the second q buffer of the KV step's append-ahead
     float *host_stage = nullptr;    // device staging of qkv_kv_step_host
     size_t host_stage_bytes = 0;
     void *xn = nullptr, *attn = nullptr, *act = nullptr;
@@ -147,6 +148,10 @@ struct qkv_handle {
     // SwiGLU in the gate/up GEMM's epilogue where each CTA gets >= 2 work
     // units (QWENASR_B200_FUSED_SWIGLU=0: the separate SwiGLU kernel).
     bool fused_swiglu = true;
+    // KV steps: K2 of layer l also appends layer l + 1 (AttendParams::next),
+    // so the step is K1 of layer 0 and one launch per layer
+    // (QWENASR_B200_APPEND_AHEAD=0: K1 then K2 for every layer).
+    bool append_ahead = true;
     int last_decode_n = -1;   // a graph is captured only for a batch size seen twice in a row
 };
 

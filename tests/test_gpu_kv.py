@@ -321,6 +321,42 @@ def test_kv_step_host_matches_device(pkg, kv_dtype):
         assert np.array_equal(results["device"][step], results["pageable"][step])
 
 
+@pytest.mark.parametrize("kv_dtype", [0, 1, 2, 3])
+def test_append_ahead_matches_per_layer_append(pkg, monkeypatch, kv_dtype):
+    """The KV step with the append-ahead (the default: K1 for layer 0, then
+    K2 of layer l also appends layer l + 1) against K1 then K2 for every layer
+    (QWENASR_B200_APPEND_AHEAD=0): over three steps of rows whose last page
+    is full, partly full or new, with short and split rows, the outputs and
+    every stored K/V byte (and 8-bit scale) are identical."""
+    lens = (1, 15, 16, 17, 100, 700, 33, 2000, 64, 5)
+    results = {}
+    for fused in ("1", "0"):
+        monkeypatch.setenv("QWENASR_B200_APPEND_AHEAD", fused)
+        dec, qn, kn = kv_handle(pkg, kv_dtype, n_layers=3, seed=4, max_streams=len(lens), max_context=2048)
+        with dec:
+            streams = [dec.open() for _ in lens]
+            for s, L in zip(streams, lens):
+                dec.extend(s, L)
+            dec.fill_random(9)
+            rng = np.random.default_rng(31)
+            outs = []
+            for _ in range(3):
+                qkv = rng.standard_normal((3, len(lens), QKV), dtype=np.float32)
+                dq = torch.from_numpy(qkv).cuda()
+                do = torch.zeros((3, len(lens), HQ * D), device="cuda")
+                dec.kv_step(streams, dq.data_ptr(), do.data_ptr())
+                torch.cuda.synchronize()
+                dec.sync()
+                outs.append(do.cpu().numpy())
+            caches = [dec.gather(layer, s, kv_dtype) for layer in range(3) for s in streams]
+        results[fused] = (outs, caches)
+    for a, b in zip(results["1"][0], results["0"][0]):
+        assert np.isfinite(a).all() and np.array_equal(a, b)
+    for ca, cb in zip(results["1"][1], results["0"][1]):
+        for x, y in zip(ca, cb):
+            assert np.array_equal(x, y)
+
+
 def test_device_error_on_bad_page_table_row(pkg):
     """A row naming a stream that has no pages is reported, not faulted."""
     dec, qn, kn = kv_handle(pkg, 1, seed=0, max_streams=2, max_context=64)
