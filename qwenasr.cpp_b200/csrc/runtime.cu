@@ -284,6 +284,7 @@ void destroy(qkv_handle *h) {
     }
     for (auto &kv : h->decode_graphs) cudaGraphExecDestroy(kv.second.exec);
     for (auto &kv : h->kv_graphs) cudaGraphExecDestroy(kv.second.exec);
+    for (auto &kv : h->kvh_graphs) cudaGraphExecDestroy(kv.second.exec);
     for (auto &ev : h->row_ev) {
         if (ev) cudaEventDestroy(ev);
     }
@@ -1768,6 +1769,8 @@ int qkv_kv_step_host(qkv_handle *h, int32_t n, const int32_t *stream_ids, const 
     const size_t need = (in_elems + out_elems) * sizeof(float);
     if (need > h->host_stage_bytes) {   // device staging, grown on demand and kept
         CK(cudaDeviceSynchronize());
+        for (auto &kv : h->kvh_graphs) cudaGraphExecDestroy(kv.second.exec);
+        h->kvh_graphs.clear();
         cudaFree(h->host_stage);
         h->host_stage = nullptr;
         h->host_stage_bytes = 0;
@@ -1801,31 +1804,64 @@ int qkv_kv_step_host(qkv_handle *h, int32_t n, const int32_t *stream_ids, const 
     if ((rc = row_upload(h, hs, static_cast<size_t>(3 * n), h->stream))) return rc;
     // The staging is free once the work queued so far on h->stream has run
     // (earlier calls' kernels and output copies end there).
-    CK(cudaEventRecord(h->ev_tail, h->stream));
-    CK(cudaStreamWaitEvent(h->copy_in, h->ev_tail, 0));
-    for (int l = 0; l < L; ++l) {
-        CK(cudaMemcpyAsync(stage_in + in_stride * l, qkv_host + in_stride * l, in_stride * sizeof(float),
-                           cudaMemcpyHostToDevice, h->copy_in));
-        CK(cudaEventRecord(h->ev_in[static_cast<size_t>(l)], h->copy_in));
+    auto body = [&]() -> int {
+        CK(cudaEventRecord(h->ev_tail, h->stream));
+        CK(cudaStreamWaitEvent(h->copy_in, h->ev_tail, 0));
+        for (int l = 0; l < L; ++l) {
+            CK(cudaMemcpyAsync(stage_in + in_stride * l, qkv_host + in_stride * l, in_stride * sizeof(float),
+                               cudaMemcpyHostToDevice, h->copy_in));
+            CK(cudaEventRecord(h->ev_in[static_cast<size_t>(l)], h->copy_in));
+        }
+        int r = QKV_OK;
+        for (int l = 0; l < L; ++l) {
+            CK(cudaStreamWaitEvent(h->stream, h->ev_in[static_cast<size_t>(l)], 0));
+            // With the append-ahead, layer l's launch also reads layer l + 1's inputs.
+            if (h->append_ahead && l + 1 < L)
+                CK(cudaStreamWaitEvent(h->stream, h->ev_in[static_cast<size_t>(l + 1)], 0));
+            if ((r = kv_step_layer(h, l, n, ds, dp, dl, stage_in + in_stride * l,
+                                   l + 1 < L ? stage_in + in_stride * (l + 1) : nullptr, stage_out + out_stride * l,
+                                   h->stream)))
+                break;
+            CK(cudaEventRecord(h->ev_done[static_cast<size_t>(l)], h->stream));
+            CK(cudaStreamWaitEvent(h->copy_out, h->ev_done[static_cast<size_t>(l)], 0));
+            CK(cudaMemcpyAsync(out_host + out_stride * l, stage_out + out_stride * l, out_stride * sizeof(float),
+                               cudaMemcpyDeviceToHost, h->copy_out));
+        }
+        // Every copy of this call has run before the stream's later work.
+        CK(cudaEventRecord(h->ev_tail, h->copy_out));
+        CK(cudaStreamWaitEvent(h->stream, h->ev_tail, 0));
+        CK(cudaEventRecord(h->ev_tail, h->copy_in));
+        CK(cudaStreamWaitEvent(h->stream, h->ev_tail, 0));
+        return r;
+    };
+    // Pinned host buffers: the whole sequence (copies on both copy streams,
+    // kernels, the events between them) replays as one graph, which also keeps
+    // the programmatic launch edges between consecutive attention kernels that
+    // eager event waits and records in the stream would cut.  Pageable
+    // buffers take the eager path (their copies cannot be captured).
+    cudaPointerAttributes ai{}, ao{};
+    const bool pinned = cudaPointerGetAttributes(&ai, qkv_host) == cudaSuccess && ai.type == cudaMemoryTypeHost &&
+                        cudaPointerGetAttributes(&ao, out_host) == cudaSuccess && ao.type == cudaMemoryTypeHost;
+    (void)cudaGetLastError();   // an unregistered pointer may leave an error behind on older drivers
+    if (h->use_graphs && pinned) {
+        const auto key = std::make_tuple(n, static_cast<const void *>(qkv_host), static_cast<const void *>(out_host),
+                                         static_cast<const void *>(h->host_stage));
+        auto it = h->kvh_graphs.find(key);
+        if (it == h->kvh_graphs.end()) {
+            if (h->kvh_graphs.size() >= 16) {
+                CK(cudaDeviceSynchronize());
+                for (auto &kv : h->kvh_graphs) cudaGraphExecDestroy(kv.second.exec);
+                h->kvh_graphs.clear();
+            }
+            qkv_handle::Graph g;
+            if ((rc = capture_graph(h, body, &g))) return rc;
+            it = h->kvh_graphs.emplace(key, g).first;
+        }
+        CK(cudaGraphLaunch(it->second.exec, h->stream));
+        h->launches += it->second.kernels;
+    } else {
+        rc = body();
     }
-    for (int l = 0; l < L; ++l) {
-        CK(cudaStreamWaitEvent(h->stream, h->ev_in[static_cast<size_t>(l)], 0));
-        // With the append-ahead, layer l's launch also reads layer l + 1's inputs.
-        if (h->append_ahead && l + 1 < L) CK(cudaStreamWaitEvent(h->stream, h->ev_in[static_cast<size_t>(l + 1)], 0));
-        if ((rc = kv_step_layer(h, l, n, ds, dp, dl, stage_in + in_stride * l,
-                                l + 1 < L ? stage_in + in_stride * (l + 1) : nullptr, stage_out + out_stride * l,
-                                h->stream)))
-            break;
-        CK(cudaEventRecord(h->ev_done[static_cast<size_t>(l)], h->stream));
-        CK(cudaStreamWaitEvent(h->copy_out, h->ev_done[static_cast<size_t>(l)], 0));
-        CK(cudaMemcpyAsync(out_host + out_stride * l, stage_out + out_stride * l, out_stride * sizeof(float),
-                           cudaMemcpyDeviceToHost, h->copy_out));
-    }
-    // Every copy of this call has run before the status read below returns.
-    CK(cudaEventRecord(h->ev_tail, h->copy_out));
-    CK(cudaStreamWaitEvent(h->stream, h->ev_tail, 0));
-    CK(cudaEventRecord(h->ev_tail, h->copy_in));
-    CK(cudaStreamWaitEvent(h->stream, h->ev_tail, 0));
     const int rc2 = check_device_error(h);
     return rc ? rc : rc2;
 }

@@ -140,6 +140,8 @@ struct qkv_handle {
     };
     std::map<int, Graph> decode_graphs;
     std::map<std::tuple<int, const void *, const void *>, Graph> kv_graphs;
+    // Host-buffer KV steps with pinned buffers: (rows, qkv_host, out_host, staging) -> graph.
+    std::map<std::tuple<int, const void *, const void *, const void *>, Graph> kvh_graphs;
     bool use_graphs = true;
     // Prefill attention on the tensor cores (K3) for bf16/e4m3 caches; the
     // environment variable QWENASR_B200_PREFILL_ATTN=cuda_core selects the
