@@ -34,10 +34,10 @@ STREAMS_PER_GPU = 256
 CTX_LO, CTX_HI = 64, 4096
 WORKLOAD_SEED = 1004          # 1000 + config index
 METRIC = "decode tokens/s (KV append+GQA attn) & KV-read HBM GB/s vs 8 TB/s, 1-8 B200"
-# DRAM bytes (read + write) of one K2 launch on this workload, from the ncu
-# capture summarised in profiles/decode_attn_k2_config4.md (same 256 streams
-# and contexts; the capture held 2 layers of cache, a launch reads one).
-K2_NCU_TRAFFIC_BYTES = 1_017_933_000 + 5_662_720
+# DRAM bytes (read + write) of one K2 launch on this workload (with the
+# append-ahead of the next layer), from an ncu capture of the same 256
+# streams and contexts (2 layers of cache held; a launch reads one).
+K2_NCU_TRAFFIC_BYTES = 1_022_283_000 + 4_984_576
 
 
 def peaks() -> dict:
