@@ -312,7 +312,7 @@ def run_ours(args) -> int:
     numa = bind_numa(local) if world > 1 else None
 
     lens = box_lengths(rank, world)
-    total_steps = args.warmup + args.steps + 2 + 8    # + kernel-timing pass + e2e pass
+    total_steps = args.warmup + args.steps + 2 + 14   # + kernel-timing pass + e2e pass (1 + 10 steps)
     max_ctx = int(lens.max()) + total_steps + 16
     pages = int(sum((int(L) + total_steps + 15) // 16 for L in lens)) + 64
     qn, kn = qk_norm_weights()
@@ -386,7 +386,7 @@ def run_ours(args) -> int:
     probe = read_probe(pkg, dec, streams, elem, st, attn_ms)
 
     # e2e: the same step through the C ABI with pinned host buffers (copies in the timed region).
-    e2e_steps = 4
+    e2e_steps = 10
     h_qkv = torch.randn((N_LAYERS, STREAMS_PER_GPU, QKV), generator=torch.Generator().manual_seed(3)).pin_memory()
     h_out = torch.empty((N_LAYERS, STREAMS_PER_GPU, HQ * D)).pin_memory()
     dec.kv_step_host(streams, h_qkv.data_ptr(), h_out.data_ptr())    # warm

@@ -1751,10 +1751,11 @@ int qkv_kv_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const float
 }
 
 // Host-buffer KV step, pipelined by layer: layer l's inputs go up on
-// copy_in while earlier layers compute, layer l's kernels wait only for the
-// inputs they read (their own, and layer l + 1's with the append-ahead), and
-// layer l's outputs come back on copy_out as soon as its attention has run,
-// so PCIe traffic in both directions overlaps the kernels.
+// copy_in a few layers ahead of their use (paced by the attention kernels),
+// layer l's kernels wait only for the inputs they read (their own, and layer
+// l + 1's with the append-ahead), and layer l's outputs come back on
+// copy_out as soon as its attention has run, so PCIe traffic in both
+// directions overlaps the kernels.
 int qkv_kv_step_host(qkv_handle *h, int32_t n, const int32_t *stream_ids, const float *qkv_host, float *out_host) {
     const TraceRange trace("qkv_kv_step_host");
     if (!h) return QKV_ERR_INVALID_ARG;
@@ -1804,15 +1805,24 @@ int qkv_kv_step_host(qkv_handle *h, int32_t n, const int32_t *stream_ids, const 
     if ((rc = row_upload(h, hs, static_cast<size_t>(3 * n), h->stream))) return rc;
     // The staging is free once the work queued so far on h->stream has run
     // (earlier calls' kernels and output copies end there).
+    // Uploads are paced: the first kAhead layers' inputs go up at once, then
+    // layer l + kAhead's once layer l's attention has finished.  Sent back to
+    // back, the 28 uploads (4.2 MB each at config 4) overlap the first layers'
+    // attention at full PCIe rate and slow it far more than the same bytes
+    // spread over the step do (measured: +2.3 ms per step against +0.2 ms).
+    constexpr int kAhead = 4;
+    auto upload = [&](int l) -> int {
+        CK(cudaMemcpyAsync(stage_in + in_stride * l, qkv_host + in_stride * l, in_stride * sizeof(float),
+                           cudaMemcpyHostToDevice, h->copy_in));
+        CK(cudaEventRecord(h->ev_in[static_cast<size_t>(l)], h->copy_in));
+        return QKV_OK;
+    };
     auto body = [&]() -> int {
         CK(cudaEventRecord(h->ev_tail, h->stream));
         CK(cudaStreamWaitEvent(h->copy_in, h->ev_tail, 0));
-        for (int l = 0; l < L; ++l) {
-            CK(cudaMemcpyAsync(stage_in + in_stride * l, qkv_host + in_stride * l, in_stride * sizeof(float),
-                               cudaMemcpyHostToDevice, h->copy_in));
-            CK(cudaEventRecord(h->ev_in[static_cast<size_t>(l)], h->copy_in));
-        }
         int r = QKV_OK;
+        for (int l = 0; l < L && l < kAhead; ++l)
+            if ((r = upload(l))) return r;
         for (int l = 0; l < L; ++l) {
             CK(cudaStreamWaitEvent(h->stream, h->ev_in[static_cast<size_t>(l)], 0));
             // With the append-ahead, layer l's launch also reads layer l + 1's inputs.
@@ -1826,6 +1836,10 @@ int qkv_kv_step_host(qkv_handle *h, int32_t n, const int32_t *stream_ids, const 
             CK(cudaStreamWaitEvent(h->copy_out, h->ev_done[static_cast<size_t>(l)], 0));
             CK(cudaMemcpyAsync(out_host + out_stride * l, stage_out + out_stride * l, out_stride * sizeof(float),
                                cudaMemcpyDeviceToHost, h->copy_out));
+            if (l + kAhead < L) {
+                CK(cudaStreamWaitEvent(h->copy_in, h->ev_done[static_cast<size_t>(l)], 0));
+                if ((r = upload(l + kAhead))) break;
+            }
         }
         // Every copy of this call has run before the stream's later work.
         CK(cudaEventRecord(h->ev_tail, h->copy_out));
