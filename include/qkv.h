@@ -226,6 +226,16 @@ int qkv_kv_attend(qkv_handle *h, int32_t layer, int32_t n, const int32_t *slots_
 int qkv_gemm_bf16(const void *x, const void *w, float *c, int32_t m, int32_t n, int32_t k, int32_t accumulate,
                   void *stream);
 
+/* Operator: the gate/up projection with SwiGLU in the GEMM's epilogue, on
+ * the tensor cores: act[m][n2/2] (bf16) = silu(G) * U, with G and U the rows
+ * of X[m][k] . W^T (bf16 in, f32 accumulation) for W[n2][k] (bf16) holding
+ * gate and up rows interleaved one by one (row 2f = gate feature f, row 2f + 1
+ * = up feature f); n2 even, k a multiple of 64.  silu(g) = g / (1 + exp(-g)),
+ * product rounded once to bf16.  Replaces the reference's gate and up
+ * mul_mat, ggml_silu and ggml_mul (text-decoder.cpp:476-493).  Device
+ * pointers, current device, `stream` as above. */
+int qkv_gemm_swiglu_bf16(const void *x, const void *w, void *act, int32_t m, int32_t n2, int32_t k, void *stream);
+
 /* Operator: the FP8 form of the projections, on the tensor cores (tcgen05
  * kind::f8f6f4, e4m3 x e4m3 products accumulated in f32): C[m][n] (+)=
  * (X[m][k] x x_scale[m]) . (W[n][k] x w_scale[n])^T, X and W e4m3 codes

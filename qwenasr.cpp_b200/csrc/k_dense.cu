@@ -317,12 +317,10 @@ __global__ void swiglu_kernel(const float *gu, int M, int F, TOut *out) {
     const size_t total = static_cast<size_t>(M) * F;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        // gu rows hold gate and up interleaved in blocks of 64 features:
-        // [gate 64t..64t+63 | up 64t..64t+63] for t = 0 .. F/64 - 1.
+        // gu rows hold gate and up interleaved one by one: [g0 u0 g1 u1 ...].
         const size_t m = i / F, jf = i % F;
-        const size_t col = (jf >> 6) * 128 + (jf & 63);
-        const float g = gu[m * 2 * F + col];
-        const float u = gu[m * 2 * F + col + 64];
+        const float2 gv = *reinterpret_cast<const float2 *>(gu + m * 2 * F + 2 * jf);
+        const float g = gv.x, u = gv.y;
         const float s = g / (1.0f + expf(-g));
         put<TOut>(out + i, s * u);
     }
@@ -335,7 +333,7 @@ __global__ void swiglu_kernel(const float *gu, int M, int F, TOut *out) {
 //   kQ8RmsNorm: RMSNorm of f32 rows x [n][K] with weights w (the formula of
 //               rmsnorm_kernel, double sum of squares)
 //   kQ8SwiGLU:  silu(gate) * up of f32 rows gu [n][2K], gate and up
-//               interleaved in blocks of 64 features (as swiglu_kernel reads)
+//               interleaved one by one (as swiglu_kernel reads)
 enum Q8Mode { kQ8Rows = 0, kQ8RmsNorm = 1, kQ8SwiGLU = 2 };
 constexpr int kQ8Threads = 256;
 constexpr int kQ8MaxVec = 6;   // float4 groups per thread: rows up to 256 x 6 x 4 = 6144 wide
@@ -365,11 +363,11 @@ __global__ void __launch_bounds__(kQ8Threads) rows_q8_kernel(const void *in, int
             } else if constexpr (MODE == kQ8RmsNorm) {
                 v[g] = reinterpret_cast<const float4 *>(static_cast<const float *>(in) + static_cast<size_t>(r) * K)[i4];
             } else {
-                // gate and up interleaved in blocks of 64 features (a group of 4 stays in one block)
-                const int i = 4 * i4;
-                const float *gp = static_cast<const float *>(in) + static_cast<size_t>(r) * 2 * K + (i >> 6) * 128 + (i & 63);
-                const float4 gv = *reinterpret_cast<const float4 *>(gp);
-                const float4 uv = *reinterpret_cast<const float4 *>(gp + 64);
+                // gate and up interleaved one by one: features 4 i4 .. 4 i4 + 3 are 8 floats
+                const float *gp = static_cast<const float *>(in) + static_cast<size_t>(r) * 2 * K + 8 * i4;
+                const float4 a = *reinterpret_cast<const float4 *>(gp);
+                const float4 b = *reinterpret_cast<const float4 *>(gp + 4);
+                const float4 gv = make_float4(a.x, a.z, b.x, b.z), uv = make_float4(a.y, a.w, b.y, b.w);
                 v[g] = make_float4(gv.x / (1.0f + expf(-gv.x)) * uv.x, gv.y / (1.0f + expf(-gv.y)) * uv.y,
                                    gv.z / (1.0f + expf(-gv.z)) * uv.z, gv.w / (1.0f + expf(-gv.w)) * uv.w);
             }

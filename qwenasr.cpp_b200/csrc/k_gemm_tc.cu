@@ -51,8 +51,7 @@ template <int BN> struct TcTraits {
     static constexpr int NS = BN <= 32 ? 8 : BN <= 64 ? 8 : BN <= 128 ? 6 : 4;
     static constexpr uint32_t kStage = kABytes + kBBytes;
     static constexpr int kCols = 2 * BN;             // two accumulators (power of two, 64..512 columns)
-    static constexpr size_t kXchBytes = 32 * 64 * sizeof(float);   // fused SwiGLU hand-over [32 tokens][64 rows]
-    static constexpr size_t kSmem = 1024 /*align slack*/ + static_cast<size_t>(NS) * kStage + kXchBytes + 256;
+    static constexpr size_t kSmem = 1024 /*align slack*/ + static_cast<size_t>(NS) * kStage + 256;
 };
 
 struct TcParams {
@@ -63,8 +62,10 @@ struct TcParams {
     float *C;
     int accumulate;   // 0: store (one split) / red.add into a zeroed C; 1: add into C
     // Fused SwiGLU (act != nullptr, one split): W holds gate and up rows
-    // interleaved in 64-row blocks, so weight tile t = [gate f 64t..64t+63 |
-    // up f 64t..64t+63]; act[M][N/2] (bf16) = silu(gate) * up, C is unused.
+    // interleaved one by one (row 2f = gate feature f, row 2f + 1 = up
+    // feature f), so a feature's two accumulator rows sit in adjacent TMEM
+    // lanes of one epilogue warp; act[M][N/2] (bf16) = silu(gate) * up, C is
+    // unused.
     __nv_bfloat16 *act;
     DevError *err;
     // FP8 operands: value of W[n][k] = code x w_scale[n], of X[m][k] = code x
@@ -163,15 +164,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // 1024-byte alignment for the swizzled tiles.
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *tiles = smem;
-    float *xch = reinterpret_cast<float *>(tiles + static_cast<size_t>(T::NS) * T::kStage);   // [32][64]
-    uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(xch) + T::kXchBytes);
+    uint64_t *full = reinterpret_cast<uint64_t *>(tiles + static_cast<size_t>(T::NS) * T::kStage);
     uint64_t *empty = full + T::NS;
     uint64_t *acc_full = empty + T::NS;      // [2] MMA -> epilogue
     uint64_t *acc_empty = acc_full + 2;      // [2] epilogue -> MMA
     uint64_t *mma_done = acc_empty + 2;      // MMA thread's own drain
-    uint64_t *xfull = mma_done + 1;          // fused SwiGLU: both halves written to xch
-    uint64_t *xempty = xfull + 1;            // fused SwiGLU: xch read by both sides
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(xempty + 1);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
     volatile int *failed = reinterpret_cast<volatile int *>(tmem_slot + 1);
     volatile int *w_issued = failed + 1;     // weight tiles warp 0 has issued (prefetch distance)
 
@@ -193,8 +191,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_init(&acc_empty[b], 4);
         }
         mbar_init(mma_done, 1);
-        mbar_init(xfull, 128);
-        mbar_init(xempty, 128);
         *failed = 0;
         *w_issued = 0;
         fence_mbar_init();
@@ -346,7 +342,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         pdl_wait();
         const int q = warp & 3;
         int j = 0;
-        uint32_t xc = 0;       // fused SwiGLU chunks exchanged (xfull / xempty phase)
         for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
             int n0, m0, kt0, nk;
             unit_coords(u, n0, m0, kt0, nk);
@@ -386,54 +381,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     }
                 }
                 if (fused) {
-                    // Rows 0..63 (warps q = 0, 1) are gate features, rows 64..127 (q = 2, 3)
-                    // the matching up features.  Each side hands the other the half of the
-                    // chunk's 32 tokens that the other finishes: gate warps finish tokens
-                    // 0..15, up warps tokens 16..31 (xch rows 0..15 carry up values, rows
-                    // 16..31 gate values).
-                    const uint32_t ph = static_cast<uint32_t>(xc) & 1u;
-                    const int rr = 32 * (q & 1) + lane;            // feature within the tile's 64
-                    const bool gate = q < 2;
-                    // Warp-uniform decisions: the next tcgen05.ld is .sync.aligned.
-                    if (!__all_sync(0xffffffffu, !*failed && bounded_wait(xempty, ph ^ 1u))) {
-                        if (lane == 0) report_error(p.err, kErrWaitTimeout, kWhereGemm, blockIdx.x, -(1 << 24));
-                        *failed = 1;
-                        break;
-                    }
-                    // gate warps pass tokens 16..31, up warps pass tokens 0..15 (register
-                    // indices stay compile-time in both branches)
-                    if (gate) {
-#pragma unroll
-                        for (int jj = 0; jj < 16; ++jj) xch[(16 + jj) * 64 + rr] = __uint_as_float(r[16 + jj]);
-                    } else {
-#pragma unroll
-                        for (int jj = 0; jj < 16; ++jj) xch[jj * 64 + rr] = __uint_as_float(r[jj]);
-                    }
-                    mbar_arrive(xfull);
-                    if (!__all_sync(0xffffffffu, !*failed && bounded_wait(xfull, ph))) {
-                        if (lane == 0) report_error(p.err, kErrWaitTimeout, kWhereGemm, blockIdx.x, -(1 << 25));
-                        *failed = 1;
-                        break;
-                    }
+                    // Lane pairs (2i, 2i + 1) hold gate and up of feature n / 2 for the
+                    // chunk's 32 tokens.  The even lane finishes tokens 0..15, the odd
+                    // lane tokens 16..31: each passes its partner the half it does not
+                    // finish (register indices stay compile-time on both sides).
+                    const bool gate = (lane & 1) == 0;
                     const int F = p.N >> 1;
-                    const int f = (n0 >> 1) + rr;
+                    const int f = n >> 1;
+                    const int t0 = gate ? 0 : 16;
                     const int mlim = p.M - (m0 + c);
-                    auto finish = [&](int t, float g, float u) {
-                        if (t < mlim && f < F) {
-                            const float sl = g * __frcp_rn(1.0f + __expf(-g));
-                            p.act[static_cast<size_t>(m0 + c + t) * F + f] = __float2bfloat16_rn(sl * u);
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) {
+                        const float mine = __uint_as_float(gate ? r[jj] : r[16 + jj]);
+                        const float other = __shfl_xor_sync(0xffffffffu, __uint_as_float(gate ? r[16 + jj] : r[jj]), 1);
+                        const float g = gate ? mine : other, u = gate ? other : mine;
+                        if (t0 + jj < mlim && f < F) {
+                            // the SwiGLU kernel's formula (accurate exp, IEEE divide)
+                            const float sl = g / (1.0f + expf(-g));
+                            p.act[static_cast<size_t>(m0 + c + t0 + jj) * F + f] = __float2bfloat16_rn(sl * u);
                         }
-                    };
-                    if (gate) {
-#pragma unroll
-                        for (int jj = 0; jj < 16; ++jj) finish(jj, __uint_as_float(r[jj]), xch[jj * 64 + rr]);
-                    } else {
-#pragma unroll
-                        for (int jj = 0; jj < 16; ++jj)
-                            finish(16 + jj, xch[(16 + jj) * 64 + rr], __uint_as_float(r[16 + jj]));
                     }
-                    mbar_arrive(xempty);
-                    ++xc;
                     continue;
                 }
                 if (n < p.N) {
@@ -772,9 +739,11 @@ cudaError_t launch_gemm_tc_fp8_slices(const void *X, const float *x_scale, const
 }
 
 bool gemm_tc_swiglu_pays(int M, int N2, int K, int num_sms) {
-    // The SwiGLU epilogue is hidden behind the next unit's MMAs only when every
-    // CTA takes at least two work units.
-    if (K % kBK != 0 || N2 % kBM != 0) return false;
+    // The fused GEMM runs unsplit.  It pays where the plain GEMM would not
+    // split either (the same GEMM, with the SwiGLU launch and the f32 gate/up
+    // round trip gone), and where every CTA takes two or more units anyway.
+    if (K % kBK != 0 || N2 % 2 != 0) return false;
+    if (plan_gemm(M, N2, K, num_sms).splits == 1) return true;
     const GemmPlan pl = plan_gemm(M, N2, K, num_sms, true);
     const long units = static_cast<long>(N2 / kBM) * ((M + pl.bn - 1) / pl.bn);
     return units >= 2L * num_sms;
@@ -783,7 +752,7 @@ bool gemm_tc_swiglu_pays(int M, int N2, int K, int num_sms) {
 cudaError_t launch_gemm_tc_swiglu(const void *X, const void *W, void *act, int M, int N2, int K, int num_sms,
                                   DevError *err, cudaStream_t st) {
     if (M <= 0 || N2 <= 0) return cudaSuccess;
-    if (K % kBK != 0 || N2 % kBM != 0) return cudaErrorInvalidValue;
+    if (K % kBK != 0 || N2 % 2 != 0) return cudaErrorInvalidValue;
     GemmPlan pl = plan_gemm(M, N2, K, num_sms, true);
     __nv_bfloat16 *a = static_cast<__nv_bfloat16 *>(act);
     switch (pl.bn) {

@@ -95,10 +95,10 @@ struct AttendParams {
     float scale_log2;          // log2(e) / sqrt(head_dim)
     DevError *err;
     // 1: the kernel(s) just before this launch on the stream wrote only each
-    // row's LAST page (one new token per row: K1), or, with the fused append,
-    // wrote no page at all, and the row arrays and page table came from copies
-    // that finished before them, so K2 may set up and stream the other pages
-    // before its grid dependency wait.  0: everything waits (any caller).
+    // row's LAST page (one new token per row: K1, or the previous layer's K2
+    // with the append-ahead), and the row arrays and page table came from
+    // copies that finished before them, so K2 may set up and stream the other
+    // pages before its grid dependency wait.  0: everything waits (any caller).
     int early;
     // Append-ahead (KV steps, where every layer's projections are on the
     // device before the step starts): with next.n > 0, K2 of layer l also
@@ -178,7 +178,7 @@ cudaError_t launch_gemm(const void *X, int x_dtype, const void *W, int w_dtype, 
 cudaError_t prepare_gemm_tc();
 bool gemm_tc_supported(int M, int N, int K);
 // act[M][N2/2] (bf16) = silu(gate) * up of X . W^T, W = gate/up rows
-// interleaved in 64-row blocks (N2 % 128 == 0); one K split.
+// interleaved one by one (row 2f gate f, row 2f + 1 up f; N2 even); one K split.
 cudaError_t launch_gemm_tc_swiglu(const void *X, const void *W, void *act, int M, int N2, int K, int num_sms,
                                   DevError *err, cudaStream_t st);
 bool gemm_tc_swiglu_pays(int M, int N2, int K, int num_sms);
@@ -200,7 +200,7 @@ int gemm_tc_fp8_kernels(int M, int N, int K, int accumulate, int num_sms);
 cudaError_t launch_gemm_tc_fp8(const void *X, const float *x_scale, const void *W, const float *w_scale, float *C,
                                int M, int N, int K, int accumulate, int num_sms, DevError *err, cudaStream_t st);
 // Rows -> e4m3 codes + one f32 scale per row (amax / 448): mode 0 bf16 rows,
-// 1 RMSNorm(f32 rows) x w, 2 SwiGLU of interleaved f32 gate/up rows [n][2K].
+// 1 RMSNorm(f32 rows) x w, 2 SwiGLU of f32 gate/up rows [n][2K] interleaved one by one.
 int rows_q8_max_k();   // widest row the quantiser takes (6144)
 cudaError_t launch_rows_q8(int mode, const void *in, int n, int K, const float *w, float eps, void *out, float *scales,
                            cudaStream_t st);

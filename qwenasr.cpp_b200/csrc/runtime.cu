@@ -418,15 +418,15 @@ int load_weights(qkv_handle *h, const GgufFile &f) {
                 (rc = raw(wo, L.w_o, 0)) || (rc = raw(so, L.s_o, 0)) || (rc = raw(wd, L.w_down, 0)) ||
                 (rc = raw(sd, L.s_down, 0)))
                 return rc;
-            // gate | up codes and scales interleaved in 64-row blocks, as the bf16 layout
-            const size_t blk = static_cast<size_t>(64) * H;
-            CK(cudaMemcpy2D(L.w_gu, 2 * blk, wg->data, blk, blk, static_cast<size_t>(F / 64), cudaMemcpyHostToDevice));
-            CK(cudaMemcpy2D(static_cast<uint8_t *>(L.w_gu) + blk, 2 * blk, wu->data, blk, blk, static_cast<size_t>(F / 64),
+            // gate | up codes and scales interleaved row by row, as the bf16 layout
+            const size_t row = static_cast<size_t>(H);
+            CK(cudaMemcpy2D(L.w_gu, 2 * row, wg->data, row, row, static_cast<size_t>(F), cudaMemcpyHostToDevice));
+            CK(cudaMemcpy2D(static_cast<uint8_t *>(L.w_gu) + row, 2 * row, wu->data, row, row, static_cast<size_t>(F),
                             cudaMemcpyHostToDevice));
-            CK(cudaMemcpy2D(L.s_gu, 128 * sizeof(float), sg->data, 64 * sizeof(float), 64 * sizeof(float),
-                            static_cast<size_t>(F / 64), cudaMemcpyHostToDevice));
-            CK(cudaMemcpy2D(L.s_gu + 64, 128 * sizeof(float), su->data, 64 * sizeof(float), 64 * sizeof(float),
-                            static_cast<size_t>(F / 64), cudaMemcpyHostToDevice));
+            CK(cudaMemcpy2D(L.s_gu, 2 * sizeof(float), sg->data, sizeof(float), sizeof(float), static_cast<size_t>(F),
+                            cudaMemcpyHostToDevice));
+            CK(cudaMemcpy2D(L.s_gu + 1, 2 * sizeof(float), su->data, sizeof(float), sizeof(float), static_cast<size_t>(F),
+                            cudaMemcpyHostToDevice));
             continue;
         }
         CK(cudaMalloc(&L.attn_norm, H * sizeof(float)));
@@ -447,15 +447,15 @@ int load_weights(qkv_handle *h, const GgufFile &f) {
             (rc = up.put(wu, gu_tmp, h->w_dtype, static_cast<size_t>(F) * H)) ||
             (rc = up.put(wd, L.w_down, h->w_dtype, 0)))
             return rc;
-        // gate | up -> 64-row blocks interleaved: rows [128t, 128t+64) = gate features
-        // 64t.., rows [128t+64, 128t+128) = the matching up features (the layout the
-        // fused SwiGLU epilogue of the projection GEMM and the SwiGLU kernel read).
-        const size_t blk = static_cast<size_t>(64) * H * we;
-        CK(cudaMemcpy2DAsync(L.w_gu, 2 * blk, gu_tmp, blk, blk, static_cast<size_t>(F / 64), cudaMemcpyDeviceToDevice,
+        // gate | up -> interleaved row by row: row 2f = gate feature f, row 2f + 1 =
+        // up feature f (the layout the fused SwiGLU epilogue of the projection
+        // GEMM, the SwiGLU kernel and the e4m3 row quantiser read).
+        const size_t row = static_cast<size_t>(H) * we;
+        CK(cudaMemcpy2DAsync(L.w_gu, 2 * row, gu_tmp, row, row, static_cast<size_t>(F), cudaMemcpyDeviceToDevice,
                              h->stream));
-        CK(cudaMemcpy2DAsync(static_cast<uint8_t *>(L.w_gu) + blk, 2 * blk,
-                             static_cast<const uint8_t *>(gu_tmp) + static_cast<size_t>(F) * H * we, blk, blk,
-                             static_cast<size_t>(F / 64), cudaMemcpyDeviceToDevice, h->stream));
+        CK(cudaMemcpy2DAsync(static_cast<uint8_t *>(L.w_gu) + row, 2 * row,
+                             static_cast<const uint8_t *>(gu_tmp) + static_cast<size_t>(F) * H * we, row, row,
+                             static_cast<size_t>(F), cudaMemcpyDeviceToDevice, h->stream));
         CK(cudaStreamSynchronize(h->stream));
         if (h->proj_fp8) {
             // FP8 projections: e4m3 codes with one scale per weight row (amax / 448),
@@ -2014,6 +2014,21 @@ int qkv_gemm_bf16(const void *x, const void *w, float *c, int32_t m, int32_t n, 
     if (!gemm_tc_supported(m, n, k)) return QKV_ERR_INVALID_ARG;
     return launch_gemm_tc(x, w, c, m, n, k, accumulate ? 1 : 0, sms, nullptr, static_cast<cudaStream_t>(stream)) ==
                    cudaSuccess
+               ? QKV_OK
+               : QKV_ERR_CUDA;
+}
+
+int qkv_gemm_swiglu_bf16(const void *x, const void *w, void *act, int32_t m, int32_t n2, int32_t k, void *stream) {
+    if (!x || !w || !act || m < 0 || n2 < 0 || n2 % 2 != 0 || k <= 0 || k % 64 != 0) return QKV_ERR_INVALID_ARG;
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return QKV_ERR_NO_DEVICE;
+    static std::once_flag once;
+    static cudaError_t prep = cudaSuccess;
+    std::call_once(once, [] { prep = prepare_gemm_tc(); });
+    if (prep != cudaSuccess) return QKV_ERR_CUDA;
+    if (!gemm_tc_supported(m, n2, k)) return QKV_ERR_INVALID_ARG;
+    return launch_gemm_tc_swiglu(x, w, act, m, n2, k, sms, nullptr, static_cast<cudaStream_t>(stream)) == cudaSuccess
                ? QKV_OK
                : QKV_ERR_CUDA;
 }

@@ -194,6 +194,45 @@ def test_compaction_preserves_decoding(pkg, synth, tiny_files):
     assert moved >= 0
 
 
+def test_fused_swiglu_epilogue_matches_swiglu_kernel(pkg, synth, monkeypatch, tmp_path):
+    """Decode of 64 streams through a 2-layer model with the 1.7B layer
+    shapes (hidden 2048, FFN 6144, bf16 weights), where the gate/up GEMM runs
+    unsplit and takes the fused SwiGLU epilogue (gate and up rows interleaved
+    one by one, partners exchanged by a lane shuffle): the ids equal those of
+    the same GEMM followed by the SwiGLU kernel (QWENASR_B200_FUSED_SWIGLU=0)
+    and the logits agree within 1e-2 relative (both round silu(g) * u to
+    bf16 once, but the two kernels' exp and divide can differ in the last
+    bit, which flips an occasional bf16 rounding: measured 2.0e-3), and the
+    fused run launches one kernel fewer per layer."""
+    cfg = dict(synth.TINY, hidden=2048, intermediate=6144)
+    path = synth.write_gguf(tmp_path / "wide.gguf", cfg, seed=3, weights="bf16", norm_init="one_plus")
+    tensors = synth.read_gguf(path)
+    n = 64
+    xs = []
+    for i in range(n):
+        rng = np.random.default_rng(500 + i)
+        x, _ = synth.prompt_rows(tensors["text.token_embd.weight"], int(rng.integers(8, 40)), rng,
+                                 audio_rows=4, audio_start=1)
+        xs.append(x)
+    runs = {}
+    for fused in ("1", "0"):
+        monkeypatch.setenv("QWENASR_B200_FUSED_SWIGLU", fused)
+        with decoder(pkg, path, w=1, kv=1, streams=n, ctx=64, seed=2, batch_tokens=4096) as dec:
+            streams = [dec.open() for _ in xs]
+            dec.prefill(streams, xs)
+            out = []
+            for _ in range(3):
+                l0 = dec.launches()
+                ids, logits = dec.decode_step(streams, want_logits=True)
+                out.append((ids, logits, dec.launches() - l0))
+        runs[fused] = out
+    for (ia, la, na), (ib, lb, nb) in zip(runs["1"], runs["0"]):
+        d = float(np.max(np.abs(la - lb)) / np.max(np.abs(lb)))
+        print(f"fused vs separate SwiGLU: ids equal {np.array_equal(ia, ib)}, max relative logit difference {d:.3e}")
+        assert np.array_equal(ia, ib) and d < 1e-2, d
+        assert na == nb - cfg["n_layers"], (na, nb)
+
+
 @pytest.mark.parametrize("kv", [1, 2, 3])
 def test_compaction_moves_cache_bytes_and_scales(pkg, synth, tiny_files, kv):
     """Compaction of a bf16 or 8-bit cache: after two streams close and the
