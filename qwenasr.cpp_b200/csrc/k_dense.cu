@@ -28,13 +28,14 @@ template <> __device__ __forceinline__ void put4<__nv_bfloat16>(__nv_bfloat16 *p
 // 256 x 4 x kVec, with 16-byte aligned x and w, stay in registers between the
 // two passes (one read of x, 16-byte loads); others take the element loop.
 template <typename TOut>
-__global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const int *rows, int hidden, const float *w,
-                                                      float eps, TOut *out) {
+__global__ void __launch_bounds__(256) rmsnorm_kernel(float *x, const int *rows, int hidden, const float *w,
+                                                      float eps, TOut *out, ResidualFold fold) {
     constexpr int kVec = 4;
     pdl_trigger();
     pdl_wait();   // everything below reads or writes memory of earlier kernels
     const int r = blockIdx.x;
-    const float *xr = x + static_cast<size_t>(rows ? rows[r] : r) * hidden;
+    const size_t xrow = static_cast<size_t>(rows ? rows[r] : r) * hidden;
+    float *xr = x + xrow;
     TOut *o = out + static_cast<size_t>(r) * hidden;
     const bool vec = (hidden & 3) == 0 && hidden <= 256 * 4 * kVec &&
                      ((reinterpret_cast<uintptr_t>(xr) | reinterpret_cast<uintptr_t>(w)) & 15u) == 0 &&
@@ -48,12 +49,32 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const int 
             const int i4 = threadIdx.x + 256 * k;
             v[k] = i4 < n4 ? reinterpret_cast<const float4 *>(xr)[i4] : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+        if (fold.n > 0) {   // the residual's pending split-K partials, in slice order, written back
+#pragma unroll
+            for (int k = 0; k < kVec; ++k) {
+                const int i4 = threadIdx.x + 256 * k;
+                if (i4 < n4) {
+                    for (int sl = 0; sl < fold.n; ++sl) {
+                        const float4 a = reinterpret_cast<const float4 *>(fold.slices + sl * fold.stride + xrow)[i4];
+                        v[k].x += a.x; v[k].y += a.y; v[k].z += a.z; v[k].w += a.w;
+                    }
+                    reinterpret_cast<float4 *>(xr)[i4] = v[k];
+                }
+            }
+        }
 #pragma unroll
         for (int k = 0; k < kVec; ++k)
             ss += static_cast<double>(v[k].x) * v[k].x + static_cast<double>(v[k].y) * v[k].y +
                   static_cast<double>(v[k].z) * v[k].z + static_cast<double>(v[k].w) * v[k].w;
     } else {
-        for (int i = threadIdx.x; i < hidden; i += blockDim.x) ss += static_cast<double>(xr[i]) * xr[i];
+        for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+            float xv = xr[i];
+            if (fold.n > 0) {
+                for (int sl = 0; sl < fold.n; ++sl) xv += fold.slices[sl * fold.stride + xrow + i];
+                xr[i] = xv;
+            }
+            ss += static_cast<double>(xv) * xv;
+        }
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -83,6 +104,19 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const int 
         }
     } else {
         for (int i = threadIdx.x; i < hidden; i += blockDim.x) put<TOut>(o + i, __fmul_rn(__fmul_rn(xr[i], scale), w[i]));
+    }
+}
+
+// x[r] += the pending split-K slices of row r, in slice order (for readers
+// of the residual other than the RMSNorms, which fold as they read).
+__global__ void __launch_bounds__(256) residual_fold_kernel(float *x, int hidden, ResidualFold fold) {
+    pdl_trigger();
+    pdl_wait();
+    const size_t row = static_cast<size_t>(blockIdx.x) * hidden;
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+        float v = x[row + i];
+        for (int sl = 0; sl < fold.n; ++sl) v += fold.slices[sl * fold.stride + row + i];
+        x[row + i] = v;
     }
 }
 
@@ -342,7 +376,7 @@ constexpr int kQ8MaxVec = 6;   // float4 groups per thread: rows up to 256 x 6 x
 // loads); K % 4 == 0 (checked at launch).
 template <int MODE>
 __global__ void __launch_bounds__(kQ8Threads) rows_q8_kernel(const void *in, int K, const float *w, float eps,
-                                                             uint8_t *out, float *scales) {
+                                                             uint8_t *out, float *scales, ResidualFold fold) {
     pdl_trigger();
     pdl_wait();   // the input rows come from the kernels before this one
     __shared__ double dpart[kQ8Threads / 32];
@@ -361,7 +395,17 @@ __global__ void __launch_bounds__(kQ8Threads) rows_q8_kernel(const void *in, int
                                                                 static_cast<size_t>(r) * K)[i4];
                 v[g] = make_float4(bf16lo(b.x), bf16hi(b.x), bf16lo(b.y), bf16hi(b.y));
             } else if constexpr (MODE == kQ8RmsNorm) {
-                v[g] = reinterpret_cast<const float4 *>(static_cast<const float *>(in) + static_cast<size_t>(r) * K)[i4];
+                float4 *xr = reinterpret_cast<float4 *>(const_cast<float *>(static_cast<const float *>(in)) +
+                                                        static_cast<size_t>(r) * K);
+                v[g] = xr[i4];
+                if (fold.n > 0) {   // the residual's pending split-K partials, in slice order, written back
+                    for (int sl = 0; sl < fold.n; ++sl) {
+                        const float4 a = reinterpret_cast<const float4 *>(fold.slices + sl * fold.stride +
+                                                                          static_cast<size_t>(r) * K)[i4];
+                        v[g].x += a.x; v[g].y += a.y; v[g].z += a.z; v[g].w += a.w;
+                    }
+                    xr[i4] = v[g];
+                }
             } else {
                 // gate and up interleaved one by one: features 4 i4 .. 4 i4 + 3 are 8 floats
                 const float *gp = static_cast<const float *>(in) + static_cast<size_t>(r) * 2 * K + 8 * i4;
@@ -703,13 +747,20 @@ cudaError_t launch_convert(const void *src, int src_ggml_type, void *dst, int ds
     return cudaGetLastError();
 }
 
-cudaError_t launch_rmsnorm(const float *x, const int *rows, int n, int hidden, const float *w, float eps, void *out,
-                           int out_dtype, cudaStream_t st) {
+cudaError_t launch_rmsnorm(float *x, const int *rows, int n, int hidden, const float *w, float eps, void *out,
+                           int out_dtype, cudaStream_t st, ResidualFold fold) {
     if (n <= 0) return cudaSuccess;
+    if (fold.n > 0 && (hidden & 3) != 0) return cudaErrorInvalidValue;
     if (out_dtype == kActF32)
-        return launch_pdl(rmsnorm_kernel<float>, dim3(n), dim3(256), 0, st, x, rows, hidden, w, eps, static_cast<float *>(out));
+        return launch_pdl(rmsnorm_kernel<float>, dim3(n), dim3(256), 0, st, x, rows, hidden, w, eps,
+                          static_cast<float *>(out), fold);
     return launch_pdl(rmsnorm_kernel<__nv_bfloat16>, dim3(n), dim3(256), 0, st, x, rows, hidden, w, eps,
-                      static_cast<__nv_bfloat16 *>(out));
+                      static_cast<__nv_bfloat16 *>(out), fold);
+}
+
+cudaError_t launch_residual_fold(float *x, int n, int hidden, ResidualFold fold, cudaStream_t st) {
+    if (n <= 0 || fold.n <= 0) return cudaSuccess;
+    return launch_pdl(residual_fold_kernel, dim3(n), dim3(256), 0, st, x, hidden, fold);
 }
 
 cudaError_t launch_layernorm(const float *x, int n, int width, const float *w, const float *b, float eps, void *out,
@@ -822,16 +873,20 @@ cudaError_t launch_swiglu(const float *gu, int M, int F, void *out, int out_dtyp
 }
 
 cudaError_t launch_rows_q8(int mode, const void *in, int n, int K, const float *w, float eps, void *out, float *scales,
-                           cudaStream_t st) {
+                           cudaStream_t st, ResidualFold fold) {
     if (n <= 0) return cudaSuccess;
     if (K <= 0 || K % 4 != 0 || K > kQ8Threads * kQ8MaxVec * 4) return cudaErrorInvalidValue;
     uint8_t *o = static_cast<uint8_t *>(out);
     switch (mode) {
-        case kQ8Rows: return launch_pdl(rows_q8_kernel<kQ8Rows>, dim3(n), dim3(kQ8Threads), 0, st, in, K, w, eps, o, scales);
+        case kQ8Rows:
+            return launch_pdl(rows_q8_kernel<kQ8Rows>, dim3(n), dim3(kQ8Threads), 0, st, in, K, w, eps, o, scales,
+                              ResidualFold{});
         case kQ8RmsNorm:
-            return launch_pdl(rows_q8_kernel<kQ8RmsNorm>, dim3(n), dim3(kQ8Threads), 0, st, in, K, w, eps, o, scales);
+            return launch_pdl(rows_q8_kernel<kQ8RmsNorm>, dim3(n), dim3(kQ8Threads), 0, st, in, K, w, eps, o, scales,
+                              fold);
         case kQ8SwiGLU:
-            return launch_pdl(rows_q8_kernel<kQ8SwiGLU>, dim3(n), dim3(kQ8Threads), 0, st, in, K, w, eps, o, scales);
+            return launch_pdl(rows_q8_kernel<kQ8SwiGLU>, dim3(n), dim3(kQ8Threads), 0, st, in, K, w, eps, o, scales,
+                              ResidualFold{});
         default: return cudaErrorInvalidValue;
     }
 }

@@ -588,7 +588,10 @@ template <int BN> constexpr double ktile_seconds() {
     return t_mma > t_ld ? (t_mma > t_lat ? t_mma : t_lat) : (t_ld > t_lat ? t_ld : t_lat);
 }
 
-GemmPlan plan_gemm(int M, int N, int K, int num_sms, bool no_split = false, bool f8 = false) {
+// slices: the launch stores each split's partial sums into its own slice
+// (plain stores, summed by the reader) instead of adding them into C with
+// red.add after a zeroing kernel.
+GemmPlan plan_gemm(int M, int N, int K, int num_sms, bool no_split = false, bool f8 = false, bool slices = false) {
     const double kHbm = 6.2e12;                     // whole-chip weight streaming
     const double kFixed = 1.5e-6;                   // per-unit fill + epilogue tail
     const double kRed = 250e9;                      // f32 red.add per second, whole chip
@@ -613,7 +616,10 @@ GemmPlan plan_gemm(int M, int N, int K, int num_sms, bool no_split = false, bool
             double t = waves * (kps * tk[idx] + kFixed);
             const double t_w = static_cast<double>(N) * K * (f8 ? 1.0 : 2.0) / kHbm;   // weights read from HBM once
             if (t_w > t) t = t_w;
-            if (sp > 1) t += static_cast<double>(M) * N * sp / kRed + 1.0e-6;   // red.add + memset
+            if (sp > 1) {
+                if (slices) t += static_cast<double>(M) * N * sp * 4.0 / 3.0e12;   // slice stores (read back from L2)
+                else t += static_cast<double>(M) * N * sp / kRed + 1.0e-6;         // red.add + the zeroing kernel
+            }
             if (t < best_t * 0.98) {
                 best_t = t;
                 best = {bn, sp};
@@ -712,7 +718,7 @@ cudaError_t launch_slices(const void *X, const float *x_scale, const void *W, co
         return cudaSuccess;
     }
     if (K % kBKe<F8> != 0 || max_slices < 1) return cudaErrorInvalidValue;
-    const GemmPlan pl = plan_gemm(M, N, K, num_sms, false, F8);
+    const GemmPlan pl = plan_gemm(M, N, K, num_sms, false, F8, true);
     const int ktiles = K / kBKe<F8>;
     const int want = pl.splits < max_slices ? pl.splits : max_slices;
     const int kps = (ktiles + want - 1) / want;

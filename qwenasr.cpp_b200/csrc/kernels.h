@@ -155,8 +155,21 @@ cudaError_t launch_page_fill(void *pool_layer, float *scales_layer, int kv_dtype
 
 // ---- dense kernels ----
 // out[r] = rmsnorm(x[rows? rows[r] : r]) * w   (double mean square, as text-decoder.cpp:542-557)
-cudaError_t launch_rmsnorm(const float *x, const int *rows, int n, int hidden, const float *w, float eps,
-                           void *out, int out_dtype, cudaStream_t st);
+// Split-K partial sums of the projection that produced the residual rows
+// (the GEMM's slice mode), folded in by the kernel that reads those rows
+// next: x[r] += slices[s][r] for s = 0, 1, ... n - 1 in that order (slices
+// indexed like x, `stride` floats apart), the sum written back into x.
+// n == 0: nothing to fold.
+struct ResidualFold {
+    const float *slices = nullptr;
+    int n = 0;
+    size_t stride = 0;
+};
+
+cudaError_t launch_rmsnorm(float *x, const int *rows, int n, int hidden, const float *w, float eps,
+                           void *out, int out_dtype, cudaStream_t st, ResidualFold fold = {});
+// x[r] (+)= fold, rows 0..n-1 of width hidden.
+cudaError_t launch_residual_fold(float *x, int n, int hidden, ResidualFold fold, cudaStream_t st);
 // x[r] = embd[ids[r]] as f32
 // Audio projector pieces: LayerNorm (weight, bias) of f32 rows into `out_dtype`;
 // out = act(c + bias) (act = erf GELU or identity) into `out_dtype`.
@@ -203,7 +216,7 @@ cudaError_t launch_gemm_tc_fp8(const void *X, const float *x_scale, const void *
 // 1 RMSNorm(f32 rows) x w, 2 SwiGLU of f32 gate/up rows [n][2K] interleaved one by one.
 int rows_q8_max_k();   // widest row the quantiser takes (6144)
 cudaError_t launch_rows_q8(int mode, const void *in, int n, int K, const float *w, float eps, void *out, float *scales,
-                           cudaStream_t st);
+                           cudaStream_t st, ResidualFold fold = {});
 cudaError_t launch_gemm_tc(const void *X, const void *W, float *C, int M, int N, int K, int accumulate, int num_sms,
                            DevError *err, cudaStream_t st);
 // Shared-memory opt-in of the dense kernels for rows up to max_k wide.

@@ -192,6 +192,8 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
         CK(cudaMalloc(&h->act, R * c.intermediate * act));
         CK(cudaMalloc(&h->qkv_sl, static_cast<size_t>(qkv_handle::kQkvMaxSlices) * h->rt.max_streams * kQkvDim *
                                       sizeof(float)));
+        CK(cudaMalloc(&h->res_sl, static_cast<size_t>(qkv_handle::kResMaxSlices) * h->rt.max_streams * c.hidden *
+                                      sizeof(float)));
         if (h->proj_fp8) {
             CK(cudaMalloc(&h->xq, R * static_cast<size_t>(std::max(c.hidden, std::max(c.intermediate, kQDim)))));
             CK(cudaMalloc(&h->xq_s, R * sizeof(float)));
@@ -247,6 +249,8 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
         h->prefill_tc = !(pa && std::strcmp(pa, "cuda_core") == 0);
         const char *fs = getenv("QWENASR_B200_FUSED_SWIGLU");
         h->fused_swiglu = !(fs && std::strcmp(fs, "0") == 0);
+        const char *rs = getenv("QWENASR_B200_RESIDUAL_SLICES");
+        h->res_slices = rs && std::strcmp(rs, "1") == 0;
         const char *aa = getenv("QWENASR_B200_APPEND_AHEAD");
         h->append_ahead = !(aa && std::strcmp(aa, "0") == 0);
     }
@@ -269,7 +273,7 @@ void destroy(qkv_handle *h) {
     cudaFree(h->ap_norm_w); cudaFree(h->ap_norm_b); cudaFree(h->ap_w0); cudaFree(h->ap_b0); cudaFree(h->ap_w1);
     cudaFree(h->ap_b1);
     cudaFree(h->pool); cudaFree(h->scales); cudaFree(h->d_page_table); cudaFree(h->d_rope);
-    cudaFree(h->x); cudaFree(h->qkv); cudaFree(h->q); cudaFree(h->q_alt); cudaFree(h->gu); cudaFree(h->logits);
+    cudaFree(h->x); cudaFree(h->qkv); cudaFree(h->res_sl); cudaFree(h->q); cudaFree(h->q_alt); cudaFree(h->gu); cudaFree(h->logits);
     cudaFree(h->am_v); cudaFree(h->am_i); cudaFree(h->am_cnt);
     cudaFree(h->am_keys); cudaFree(h->am_rcnt); cudaFree(h->d_wout_norm);
     cudaFree(h->xn); cudaFree(h->attn); cudaFree(h->act); cudaFree(h->host_stage); cudaFree(h->qkv_sl);
@@ -866,7 +870,11 @@ cudaError_t gemm(qkv_handle *h, const void *X, const void *W, float *C, int M, i
 // Logits of the rows listed in d_rows (indices into x) -> ids (device), logits into h->logits.
 int head_and_argmax(qkv_handle *h, int n, const int *d_rows) {
     const qkv_model_config &c = h->cfg;
-    CK(launch_rmsnorm(h->x, d_rows, n, c.hidden, h->out_norm, c.rms_norm_eps, h->xn, h->act_dtype, h->stream));
+    // The final norm also folds the last layer's pending down-projection slices
+    // into the rows it reads (x of the other rows is not read again).
+    CK(launch_rmsnorm(h->x, d_rows, n, c.hidden, h->out_norm, c.rms_norm_eps, h->xn, h->act_dtype, h->stream,
+                      h->res_pending));
+    h->res_pending = ResidualFold{};
     CK(gemm(h, h->xn, h->w_out, h->logits, n, c.vocab, c.hidden, 0));
     CK(launch_argmax_split(h->logits, n, c.vocab, h->d_out_ids, h->am_v, h->am_i, h->am_cnt,
                            qkv_handle::kArgmaxSlices, h->num_sms, h->stream));
@@ -950,15 +958,44 @@ const float *qkv_projection(qkv_handle *h, const qkv_handle::Layer &L, int n, cu
     return h->qkv;
 }
 
+// The o or down projection of one layer, whose result adds to the residual
+// x (X: the bf16 attention output or activation; the FP8 path takes the e4m3
+// rows already in xq).  A decode-sized batch on the tensor cores runs in
+// slice mode: each K split stores its partial sums into res_sl (plain stores,
+// no atomics, x not touched) and the returned fold is added to x, in slice
+// order, by the kernel that reads x next.  Otherwise x += X . W^T here and
+// the fold is empty.
+int residual_projection(qkv_handle *h, const void *W, const float *w_s, const void *X, int n, int K, ResidualFold *fold) {
+    const int H = h->cfg.hidden;
+    *fold = ResidualFold{};
+    const bool tc = h->proj_fp8 ? gemm_tc_fp8_supported(n, H, K)
+                                : (h->act_dtype == kActBF16 && h->w_dtype == kActBF16 && gemm_tc_supported(n, H, K));
+    if (tc && h->res_slices && h->res_sl && n <= h->rt.max_streams) {
+        int nsl = 1;
+        CK(h->proj_fp8 ? launch_gemm_tc_fp8_slices(h->xq, h->xq_s, W, w_s, h->res_sl, n, H, K, qkv_handle::kResMaxSlices,
+                                                   h->num_sms, h->d_err, h->stream, &nsl)
+                       : launch_gemm_tc_slices(X, W, h->res_sl, n, H, K, qkv_handle::kResMaxSlices, h->num_sms, h->d_err,
+                                               h->stream, &nsl));
+        if (h->proj_fp8) h->launches += 1;   // (the bf16 loop counts its projections itself)
+        fold->slices = h->res_sl;
+        fold->n = nsl;
+        fold->stride = static_cast<size_t>(n) * H;
+        return QKV_OK;
+    }
+    CK(h->proj_fp8 ? gemm8(h, W, w_s, h->x, n, H, K, 1) : gemm(h, X, W, h->x, n, H, K, 1));
+    return QKV_OK;
+}
+
 // One layer with FP8 projections: every projection input is quantised to
 // e4m3 rows with a scale per row by the kernel that builds it (RMSNorm,
-// SwiGLU) or right after (the attention output).
+// SwiGLU) or right after (the attention output).  fold: in, the residual's
+// pending slices (the previous layer's down projection); out, this layer's.
 int run_layer_fp8(qkv_handle *h, const qkv_handle::Layer &L, int l, int n, const int *slots, const int *pos,
-                  const int *lens, bool prompt, const int4 *items, int n_items) {
+                  const int *lens, bool prompt, const int4 *items, int n_items, ResidualFold *fold) {
     const qkv_model_config &c = h->cfg;
     const float eps = c.rms_norm_eps;
     int rc;
-    CK(launch_rows_q8(1, h->x, n, c.hidden, L.attn_norm, eps, h->xq, h->xq_s, h->stream));
+    CK(launch_rows_q8(1, h->x, n, c.hidden, L.attn_norm, eps, h->xq, h->xq_s, h->stream, *fold));
     cudaError_t pe = cudaSuccess;
     const float *qkv = qkv_projection(h, L, n, &pe);
     CK(pe);
@@ -978,11 +1015,11 @@ int run_layer_fp8(qkv_handle *h, const qkv_handle::Layer &L, int l, int n, const
         h->launches += 2;
     }
     CK(launch_rows_q8(0, h->attn, n, kQDim, nullptr, 0.0f, h->xq, h->xq_s, h->stream));
-    CK(gemm8(h, L.w_o, L.s_o, h->x, n, c.hidden, kQDim, 1));
-    CK(launch_rows_q8(1, h->x, n, c.hidden, L.ffn_norm, eps, h->xq, h->xq_s, h->stream));
+    if ((rc = residual_projection(h, L.w_o, L.s_o, nullptr, n, kQDim, fold))) return rc;
+    CK(launch_rows_q8(1, h->x, n, c.hidden, L.ffn_norm, eps, h->xq, h->xq_s, h->stream, *fold));
     CK(gemm8(h, L.w_gu, L.s_gu, h->gu, n, 2 * c.intermediate, c.hidden, 0));
     CK(launch_rows_q8(2, h->gu, n, c.intermediate, nullptr, 0.0f, h->xq, h->xq_s, h->stream));
-    CK(gemm8(h, L.w_down, L.s_down, h->x, n, c.hidden, c.intermediate, 1));
+    if ((rc = residual_projection(h, L.w_down, L.s_down, nullptr, n, c.intermediate, fold))) return rc;
     h->launches += 4;
     return QKV_OK;
 }
@@ -993,13 +1030,16 @@ int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int
     const bool bf = h->act_dtype == kActBF16;
     int rc;
     if (l1 < 0) l1 = c.n_layers;
+    ResidualFold fold{};   // x is complete on entry (embeddings, decoder input or the caller's rows)
+    h->res_pending = ResidualFold{};
     for (int l = l0; l < l1; ++l) {
         const qkv_handle::Layer &L = h->layers[static_cast<size_t>(l)];
         if (h->proj_fp8) {
-            if ((rc = run_layer_fp8(h, L, l, n, slots, pos, lens, prompt, items, n_items))) return rc;
+            if ((rc = run_layer_fp8(h, L, l, n, slots, pos, lens, prompt, items, n_items, &fold))) return rc;
             continue;
         }
-        CK(launch_rmsnorm(h->x, nullptr, n, c.hidden, L.attn_norm, c.rms_norm_eps, h->xn, h->act_dtype, h->stream));
+        CK(launch_rmsnorm(h->x, nullptr, n, c.hidden, L.attn_norm, c.rms_norm_eps, h->xn, h->act_dtype, h->stream,
+                          fold));
         cudaError_t pe = cudaSuccess;
         const float *qkv = qkv_projection(h, L, n, &pe);
         CK(pe);
@@ -1019,8 +1059,9 @@ int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int
             CK(prefill_attend(h, l, n, slots, pos, h->q, tc ? h->q : nullptr, h->attn, bf, items, n_items, h->stream));
             h->launches += 2;
         }
-        CK(gemm(h, h->attn, L.w_o, h->x, n, c.hidden, kQDim, 1));
-        CK(launch_rmsnorm(h->x, nullptr, n, c.hidden, L.ffn_norm, c.rms_norm_eps, h->xn, h->act_dtype, h->stream));
+        if ((rc = residual_projection(h, L.w_o, nullptr, h->attn, n, kQDim, &fold))) return rc;
+        CK(launch_rmsnorm(h->x, nullptr, n, c.hidden, L.ffn_norm, c.rms_norm_eps, h->xn, h->act_dtype, h->stream,
+                          fold));
         const bool fused = h->fused_swiglu && h->act_dtype == kActBF16 && h->w_dtype == kActBF16 &&
                            gemm_tc_supported(n, 2 * c.intermediate, c.hidden) &&
                            gemm_tc_swiglu_pays(n, 2 * c.intermediate, c.hidden, h->num_sms);
@@ -1032,9 +1073,10 @@ int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int
             CK(gemm(h, h->xn, L.w_gu, h->gu, n, 2 * c.intermediate, c.hidden, 0));
             CK(launch_swiglu(h->gu, n, c.intermediate, h->act, h->act_dtype, h->stream));
         }
-        CK(gemm(h, h->act, L.w_down, h->x, n, c.hidden, c.intermediate, 1));
+        if ((rc = residual_projection(h, L.w_down, nullptr, h->act, n, c.intermediate, &fold))) return rc;
         h->launches += fused ? 6 : 7;
     }
+    h->res_pending = fold;   // the last down projection: folded by the head (or by the caller)
     return QKV_OK;
 }
 
@@ -1568,6 +1610,11 @@ int qkv_layer_forward(qkv_handle *h, int32_t layer, int32_t tokens, const float 
         if (rc == QKV_OK)
             rc = run_layers(h, tokens, h->d_rowbuf, h->d_rowbuf + tokens, nullptr, true, layer, layer + 1, h->d_items,
                             n_items);
+        if (rc == QKV_OK && h->res_pending.n > 0) {
+            e = launch_residual_fold(h->x, tokens, h->cfg.hidden, h->res_pending, h->stream);
+            h->res_pending = ResidualFold{};
+            if (e != cudaSuccess) rc = cuda_fail(h, e, "layer_forward fold");
+        }
         if (rc == QKV_OK) {
             e = cudaMemcpyAsync(out, h->x, bytes, cudaMemcpyDeviceToHost, h->stream);
             if (e != cudaSuccess) rc = cuda_fail(h, e, "layer_forward download");

@@ -116,6 +116,17 @@ struct qkv_handle {
     float *qkv_sl = nullptr;
     int qkv_nsl = 1;
     size_t qkv_sl_stride = 0;
+    // o and down projections of a decode-sized batch in slice mode: the split
+    // partial sums go to res_sl[s][rows][H] and the next RMSNorm (or the
+    // head's) adds them to the residual x in slice order; res_pending is the
+    // last layer's down projection, still to be folded by the head.
+    // Off by default (QWENASR_B200_RESIDUAL_SLICES=1 turns it on): it keeps
+    // atomics out of the residual, but the folds cost the RMSNorms more than
+    // the red.add they replace (measured 2-4 % per decode step).
+    static constexpr int kResMaxSlices = 8;
+    float *res_sl = nullptr;
+    bool res_slices = false;
+    qkv::ResidualFold res_pending;
     uint8_t *xq = nullptr;      // [rows][max(H, Hq D, F)] e4m3 token operand
     float *xq_s = nullptr;      // [rows]
     int *d_out_ids = nullptr;   // [max_rows]

@@ -233,6 +233,33 @@ def test_fused_swiglu_epilogue_matches_swiglu_kernel(pkg, synth, monkeypatch, tm
         assert na == nb - cfg["n_layers"], (na, nb)
 
 
+@pytest.mark.parametrize("w", [1, 2])
+def test_residual_slices_match_atomic_accumulation(pkg, synth, monkeypatch, tiny_files, w):
+    """QWENASR_B200_RESIDUAL_SLICES=1 (the o and down projections of decode
+    batches store split-K partial sums, which the next RMSNorm or the head's
+    folds into the residual in slice order) against the default (the
+    projections add into the residual with red.add): over prefill and 6
+    decode steps of 4 streams, bf16 and FP8 projections, the ids are equal
+    and the logits agree within 1e-2 relative: only the f32 summation order
+    of the partial sums differs, but that flips an occasional bf16 (or e4m3)
+    rounding of the normalised rows the next projection reads (measured
+    1.2e-3 with bf16 projections)."""
+    cfg, files = tiny_files
+    path = files[("bf16", "one_plus")]
+    xs = prompts(synth, synth.read_gguf(path), 4, 81, lo=10, hi=60)
+    runs = {}
+    for mode in ("1", "0"):
+        monkeypatch.setenv("QWENASR_B200_RESIDUAL_SLICES", mode)
+        with decoder(pkg, path, w=w, kv=1, seed=3, batch_tokens=512) as dec:
+            streams = [dec.open() for _ in xs]
+            out = [dec.prefill(streams, xs, want_logits=True)]
+            out += [dec.decode_step(streams, want_logits=True) for _ in range(6)]
+        runs[mode] = out
+    for (ia, la), (ib, lb) in zip(runs["1"], runs["0"]):
+        assert np.array_equal(ia, ib)
+        assert rel_err(la, lb) < 1e-2, rel_err(la, lb)
+
+
 @pytest.mark.parametrize("kv", [1, 2, 3])
 def test_compaction_moves_cache_bytes_and_scales(pkg, synth, tiny_files, kv):
     """Compaction of a bf16 or 8-bit cache: after two streams close and the
