@@ -232,9 +232,15 @@ int qkv_gemm_bf16(const void *x, const void *w, float *c, int32_t m, int32_t n, 
  * gate and up rows interleaved one by one (row 2f = gate feature f, row 2f + 1
  * = up feature f); n2 even, k a multiple of 64.  silu(g) = g / (1 + exp(-g)),
  * product rounded once to bf16.  Replaces the reference's gate and up
- * mul_mat, ggml_silu and ggml_mul (text-decoder.cpp:476-493).  Device
- * pointers, current device, `stream` as above. */
-int qkv_gemm_swiglu_bf16(const void *x, const void *w, void *act, int32_t m, int32_t n2, int32_t k, void *stream);
+ * mul_mat, ggml_silu and ggml_mul (text-decoder.cpp:476-493).  Optional
+ * stream-K workspace (both NULL: none): `workspace` of workspace_floats f32
+ * and `flags` of 4 x flag_tiles int32, zero before the first call and left
+ * zero by every call; with it, a small batch whose output tiles would leave
+ * SMs idle spreads all of their k-tiles evenly over the SMs.  Calls sharing
+ * a workspace must not overlap.  Device pointers, current device, `stream`
+ * as above. */
+int qkv_gemm_swiglu_bf16(const void *x, const void *w, void *act, int32_t m, int32_t n2, int32_t k, float *workspace,
+                         int32_t *flags, int64_t workspace_floats, int32_t flag_tiles, void *stream);
 
 /* Operator: the FP8 form of the projections, on the tensor cores (tcgen05
  * kind::f8f6f4, e4m3 x e4m3 products accumulated in f32): C[m][n] (+)=

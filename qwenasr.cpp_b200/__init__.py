@@ -88,7 +88,7 @@ SIGNATURES = {
     "qkv_kv_attend_noalloc": (C.c_int, [_P, C.c_int32, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, _P,
                                         _P, _P, _P, C.c_char_p, C.c_size_t]),
     "qkv_gemm_bf16": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P]),
-    "qkv_gemm_swiglu_bf16": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, _P]),
+    "qkv_gemm_swiglu_bf16": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, _P, _P, C.c_int64, C.c_int32, _P]),
     "qkv_gemm_fp8": (C.c_int, [_P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P]),
     "qkv_quantize_rows_e4m3": (C.c_int, [_P, C.c_int32, C.c_int32, _P, _P, _P]),
     "qkv_prefill_attend": (C.c_int, [_P, C.c_int32, C.c_int32, _P, _P, _P, _P, _P]),

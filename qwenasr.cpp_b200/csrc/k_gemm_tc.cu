@@ -76,7 +76,19 @@ struct TcParams {
     // into C + s x slice_stride instead of adding them into C, so C needs no
     // zeroing, no atomics run, and the reader sums the slices in order.
     size_t slice_stride;
+    // Stream-K (sk_ws non-null, one split): CTA c of G takes iterations
+    // [c I / G, (c + 1) I / G) of the launch's I = tiles x k-tiles (tiles in
+    // the unit order), cut into one segment per tile it touches.  The segment
+    // holding a tile's k-tile 0 finishes the tile: it adds, in k order, the
+    // partial sums the tile's other segments (the first segments of the next
+    // CTAs) left in sk_ws[tile][part][128 rows][BN] and runs the epilogue.
+    // sk_flags[tile][4] count the parts each epilogue warp's 32 rows have
+    // received; the finishing warp resets its count.
+    float *sk_ws;
+    int *sk_flags;
 };
+
+constexpr int kSkMaxParts = 4;     // stream-K: partial segments a tile may have
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar,
                                             uint64_t policy) {
@@ -206,18 +218,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    // unit u -> (token tile, weight tile) in the launch's order, then K split
-    auto unit_coords = [&](int u, int &n0, int &m0, int &kt0, int &nk) {
-        const int tiles = p.tiles_m * p.tiles_n;
-        const int sp = u / tiles;
-        const int t = u - sp * tiles;
+    // Work items of this CTA, in order: round-robin units (tile, K split), or
+    // with stream-K one segment per tile of the CTA's iteration range.
+    const int n_tiles = p.tiles_m * p.tiles_n;
+    const bool sk = p.sk_ws != nullptr;
+    const int64_t sk_iters = static_cast<int64_t>(n_tiles) * ktiles;
+    const int64_t sk_beg = sk ? static_cast<int64_t>(blockIdx.x) * sk_iters / gridDim.x : 0;
+    const int64_t sk_end = sk ? static_cast<int64_t>(blockIdx.x + 1) * sk_iters / gridDim.x : 0;
+    auto tile_coords = [&](int t, int &n0, int &m0) {
         const int tm = p.w_fastest ? t / p.tiles_n : t % p.tiles_m;
         const int tn = p.w_fastest ? t % p.tiles_n : t / p.tiles_m;
         n0 = tn * kBM;
         m0 = tm * BN;
+    };
+    auto first_item = [&]() -> int64_t { return sk ? sk_beg : static_cast<int64_t>(blockIdx.x); };
+    auto next_item = [&](int64_t &cur, int &n0, int &m0, int &kt0, int &nk, int &tile) -> bool {
+        if (sk) {
+            if (cur >= sk_end) return false;
+            tile = static_cast<int>(cur / ktiles);
+            kt0 = static_cast<int>(cur - static_cast<int64_t>(tile) * ktiles);
+            const int64_t tile_end = static_cast<int64_t>(tile + 1) * ktiles;
+            const int64_t stop = sk_end < tile_end ? sk_end : tile_end;
+            nk = static_cast<int>(stop - cur);
+            tile_coords(tile, n0, m0);
+            cur = stop;
+            return true;
+        }
+        if (cur >= units) return false;
+        const int u = static_cast<int>(cur);
+        const int sp = u / n_tiles;
+        tile = u - sp * n_tiles;
+        tile_coords(tile, n0, m0);
         kt0 = sp * p.ktiles_per_split;
         const int kt1 = min(ktiles, kt0 + p.ktiles_per_split);
         nk = kt1 > kt0 ? kt1 - kt0 : 0;
+        cur += gridDim.x;
+        return true;
     };
 
     if (warp == 0 || warp == kProducerB) {
@@ -233,9 +269,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
             int it = 0;
             bool bad = false;
-            for (int u = blockIdx.x; u < units && !bad; u += gridDim.x) {
-                int n0, m0, kt0, nk;
-                unit_coords(u, n0, m0, kt0, nk);
+            int64_t cur = first_item();
+            int n0, m0, kt0, nk, tile;
+            while (!bad && next_item(cur, n0, m0, kt0, nk, tile)) {
                 for (int i = 0; i < nk; ++i) {
                     const int s = it % T::NS;
                     const uint32_t ph = static_cast<uint32_t>(it / T::NS) & 1u;
@@ -267,9 +303,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
             int pit = 0;
             bool stop = false;
-            for (int u = blockIdx.x; u < units && !stop; u += gridDim.x) {
-                int n0, m0, kt0, nk;
-                unit_coords(u, n0, m0, kt0, nk);
+            int64_t cur = first_item();
+            int n0, m0, kt0, nk, tile;
+            while (!stop && next_item(cur, n0, m0, kt0, nk, tile)) {
                 for (int i = 0; i < nk; ++i, ++pit) {
                     if (pit >= kAhead) {
                         const long long t0 = clock64();
@@ -293,9 +329,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint32_t idesc = idesc_mma<BN, F8>();
             int it = 0, j = 0;
             bool bad = false, any = false;
-            for (int u = blockIdx.x; u < units && !bad; u += gridDim.x, ++j) {
-                int n0, m0, kt0, nk;
-                unit_coords(u, n0, m0, kt0, nk);
+            int64_t cur = first_item();
+            int n0, m0, kt0, nk, tile;
+            for (; !bad && next_item(cur, n0, m0, kt0, nk, tile); ++j) {
                 const int b = j & 1;
                 if (*failed || !bounded_wait(&acc_empty[b], (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u)) {
                     report_error(p.err, kErrWaitTimeout, kWhereGemm, blockIdx.x, -(1 << 22) - j);
@@ -342,9 +378,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         pdl_wait();
         const int q = warp & 3;
         int j = 0;
-        for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
-            int n0, m0, kt0, nk;
-            unit_coords(u, n0, m0, kt0, nk);
+        int64_t cur = first_item();
+        int n0, m0, kt0, nk, tile;
+        for (; next_item(cur, n0, m0, kt0, nk, tile); ++j) {
             const int b = j & 1;
             const bool have = bounded_wait(&acc_full[b], static_cast<uint32_t>(j >> 1) & 1u);
             tc_fence_after();
@@ -359,6 +395,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int n = n0 + 32 * q + lane;
             const bool split = p.splits > 1;
             const bool fused = p.act != nullptr;
+            // Stream-K: a segment without k-tile 0 is part sk_part of its tile and
+            // leaves its sums in the workspace; the one with k-tile 0 adds the
+            // tile's sk_nparts parts (once they are all in) before its epilogue.
+            int sk_part = -1, sk_nparts = 0;
+            if (sk) {
+                auto cta_of = [&](int64_t pos) {
+                    return ((pos + 1) * static_cast<int64_t>(gridDim.x) + sk_iters - 1) / sk_iters - 1;
+                };
+                const int64_t it0 = static_cast<int64_t>(tile) * ktiles;
+                const int64_t c_head = cta_of(it0);
+                if (kt0 == 0) sk_nparts = static_cast<int>(cta_of(it0 + ktiles - 1) - c_head);
+                else sk_part = static_cast<int>(blockIdx.x - c_head - 1);
+                if (sk_nparts > 0) {
+                    int ok = 1;
+                    if (lane == 0) {
+                        volatile int *f = p.sk_flags + tile * 4 + q;
+                        const long long t0 = clock64();
+                        while (*f < sk_nparts) {
+                            if (*failed || clock64() - t0 > kWaitLimitCycles) {
+                                ok = 0;
+                                break;
+                            }
+                        }
+                    }
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    if (!ok) {
+                        if (lane == 0) {
+                            report_error(p.err, kErrWaitTimeout, kWhereGemm, blockIdx.x, -(1 << 26) - tile);
+                            *failed = 1;
+                        }
+                        // hand the accumulator back so the MMA thread does not wait on it
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&acc_empty[b]);
+                        break;
+                    }
+                    __threadfence();
+                }
+            }
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
                 uint32_t r[32];
@@ -378,6 +453,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         const int m = m0 + c + jj;
                         const float xs = m < p.M ? p.x_scale[m] : 0.0f;
                         r[jj] = __float_as_uint(__uint_as_float(r[jj]) * ws * xs);
+                    }
+                }
+                if (sk_part >= 0) {
+                    // a later piece of its tile: the partial sums go to the workspace only
+                    float *wsp = p.sk_ws + ((static_cast<size_t>(tile) * kSkMaxParts + sk_part) * kBM + 32 * q + lane) * BN + c;
+#pragma unroll
+                    for (int jj = 0; jj < 32; jj += 4)
+                        __stcg(reinterpret_cast<float4 *>(wsp + jj),
+                               make_float4(__uint_as_float(r[jj]), __uint_as_float(r[jj + 1]), __uint_as_float(r[jj + 2]),
+                                           __uint_as_float(r[jj + 3])));
+                    continue;
+                }
+                for (int part = 0; part < sk_nparts; ++part) {
+                    // the tile's later pieces, added in k order
+                    const float *wsp = p.sk_ws + ((static_cast<size_t>(tile) * kSkMaxParts + part) * kBM + 32 * q + lane) * BN + c;
+#pragma unroll
+                    for (int jj = 0; jj < 32; jj += 4) {
+                        const float4 a = __ldcg(reinterpret_cast<const float4 *>(wsp + jj));
+                        r[jj] = __float_as_uint(__uint_as_float(r[jj]) + a.x);
+                        r[jj + 1] = __float_as_uint(__uint_as_float(r[jj + 1]) + a.y);
+                        r[jj + 2] = __float_as_uint(__uint_as_float(r[jj + 2]) + a.z);
+                        r[jj + 3] = __float_as_uint(__uint_as_float(r[jj + 3]) + a.w);
                     }
                 }
                 if (fused) {
@@ -430,6 +527,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         }
                     }
                 }
+            }
+            if (sk_part >= 0) {
+                // this warp's 32 rows of the part are in: count them for the finishing CTA
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) atomicAdd(p.sk_flags + tile * 4 + q, 1);
+            } else if (sk_nparts > 0 && lane == 0) {
+                p.sk_flags[tile * 4 + q] = 0;   // every part arrived and was added: ready for the next launch
             }
         }
     }
@@ -540,7 +645,8 @@ bool weight_fastest(int M, int K, int tiles_m) {
 template <int BN, bool F8 = false>
 cudaError_t launch_bn(const void *X, const void *W, float *C, int M, int N, int K, int accumulate, int splits,
                       int num_sms, DevError *err, cudaStream_t st, __nv_bfloat16 *act = nullptr,
-                      const float *w_scale = nullptr, const float *x_scale = nullptr, bool slices = false) {
+                      const float *w_scale = nullptr, const float *x_scale = nullptr, bool slices = false,
+                      float *sk_ws = nullptr, int *sk_flags = nullptr) {
     CUtensorMap tw, tx;
     const int es = F8 ? 1 : 2;
     if (!cached_map(&tw, W, N, K, kBM, es) || !cached_map(&tx, X, M, K, BN, es)) return cudaErrorInvalidValue;
@@ -562,10 +668,12 @@ cudaError_t launch_bn(const void *X, const void *W, float *C, int M, int N, int 
         }
         if (e != cudaSuccess) return e;
     }
+    if (sk_ws && (splits != 1 || !sk_flags)) return cudaErrorInvalidValue;
     TcParams p{M, N, K, kps, tiles_n, tiles_m, splits, weight_fastest(M, K * es / 2, tiles_m) ? 1 : 0, C, accumulate,
-               act, err, w_scale, x_scale, slices && splits > 1 ? static_cast<size_t>(M) * N : size_t{0}};
+               act, err, w_scale, x_scale, slices && splits > 1 ? static_cast<size_t>(M) * N : size_t{0}, sk_ws,
+               sk_flags};
     const int units = tiles_n * tiles_m * splits;
-    const int grid = units < num_sms ? units : num_sms;
+    const int grid = sk_ws ? num_sms : (units < num_sms ? units : num_sms);
     return launch_pdl(gemm_tc_kernel<BN, F8>, dim3(grid), dim3(kGemmThreads), TcTraits<BN>::kSmem, st, tw, tx, p);
 }
 
@@ -755,15 +863,36 @@ bool gemm_tc_swiglu_pays(int M, int N2, int K, int num_sms) {
     return units >= 2L * num_sms;
 }
 
+// Stream-K for a launch of `tiles` output tiles of k-tiles each on `num_sms`
+// CTAs: worth it when the tiles leave SMs idle, possible when every tile's
+// pieces fit kSkMaxParts and the workspace holds them.
+bool stream_k_fits(int tiles, int ktiles, int bn, int num_sms, size_t ws_floats, int flag_tiles) {
+    if (tiles >= num_sms || bn > 64 || tiles > flag_tiles) return false;
+    if (static_cast<size_t>(tiles) * kSkMaxParts * kBM * bn > ws_floats) return false;
+    const int64_t I = static_cast<int64_t>(tiles) * ktiles, G = num_sms;
+    if (I < 2 * G) return false;   // under two k-tiles per CTA: too little work to split
+    auto cta_of = [&](int64_t pos) { return ((pos + 1) * G + I - 1) / I - 1; };
+    for (int t = 0; t < tiles; ++t) {
+        const int64_t i0 = static_cast<int64_t>(t) * ktiles;
+        if (cta_of(i0 + ktiles - 1) - cta_of(i0) > kSkMaxParts) return false;
+    }
+    return true;
+}
+
 cudaError_t launch_gemm_tc_swiglu(const void *X, const void *W, void *act, int M, int N2, int K, int num_sms,
-                                  DevError *err, cudaStream_t st) {
+                                  DevError *err, cudaStream_t st, float *sk_ws, int *sk_flags, size_t sk_ws_floats,
+                                  int sk_flag_tiles) {
     if (M <= 0 || N2 <= 0) return cudaSuccess;
     if (K % kBK != 0 || N2 % 2 != 0) return cudaErrorInvalidValue;
     GemmPlan pl = plan_gemm(M, N2, K, num_sms, true);
+    const int tiles = ((N2 + kBM - 1) / kBM) * ((M + pl.bn - 1) / pl.bn);
+    const bool use_sk = sk_ws && sk_flags && stream_k_fits(tiles, K / kBK, pl.bn, num_sms, sk_ws_floats, sk_flag_tiles);
+    float *ws = use_sk ? sk_ws : nullptr;
+    int *fl = use_sk ? sk_flags : nullptr;
     __nv_bfloat16 *a = static_cast<__nv_bfloat16 *>(act);
     switch (pl.bn) {
-        case 32: return launch_bn<32>(X, W, nullptr, M, N2, K, 0, 1, num_sms, err, st, a);
-        case 64: return launch_bn<64>(X, W, nullptr, M, N2, K, 0, 1, num_sms, err, st, a);
+        case 32: return launch_bn<32>(X, W, nullptr, M, N2, K, 0, 1, num_sms, err, st, a, nullptr, nullptr, false, ws, fl);
+        case 64: return launch_bn<64>(X, W, nullptr, M, N2, K, 0, 1, num_sms, err, st, a, nullptr, nullptr, false, ws, fl);
         case 128: return launch_bn<128>(X, W, nullptr, M, N2, K, 0, 1, num_sms, err, st, a);
         default: return launch_bn<256>(X, W, nullptr, M, N2, K, 0, 1, num_sms, err, st, a);
     }

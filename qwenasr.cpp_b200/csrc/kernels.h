@@ -192,8 +192,13 @@ cudaError_t prepare_gemm_tc();
 bool gemm_tc_supported(int M, int N, int K);
 // act[M][N2/2] (bf16) = silu(gate) * up of X . W^T, W = gate/up rows
 // interleaved one by one (row 2f gate f, row 2f + 1 up f; N2 even); one K split.
+// With a workspace (sk_ws of sk_ws_floats f32, sk_flags of 4 x sk_flag_tiles
+// ints, zero before first use and left zero) a launch whose tiles would leave
+// SMs idle runs stream-K over all of them (see TcParams).  Calls sharing a
+// workspace must not overlap.
 cudaError_t launch_gemm_tc_swiglu(const void *X, const void *W, void *act, int M, int N2, int K, int num_sms,
-                                  DevError *err, cudaStream_t st);
+                                  DevError *err, cudaStream_t st, float *sk_ws = nullptr, int *sk_flags = nullptr,
+                                  size_t sk_ws_floats = 0, int sk_flag_tiles = 0);
 bool gemm_tc_swiglu_pays(int M, int N2, int K, int num_sms);
 // Kernels one launch_gemm_tc call launches: 2 when a K split first zeroes C.
 int gemm_tc_kernels(int M, int N, int K, int accumulate, int num_sms);

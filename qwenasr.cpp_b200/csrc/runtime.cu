@@ -194,6 +194,12 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
                                       sizeof(float)));
         CK(cudaMalloc(&h->res_sl, static_cast<size_t>(qkv_handle::kResMaxSlices) * h->rt.max_streams * c.hidden *
                                       sizeof(float)));
+        // stream-K of the fused gate/up GEMM: two token tiles of 2F / 128 weight tiles, 4 parts of 128 x 64 each
+        h->sk_flag_tiles = 2 * ((2 * c.intermediate + 127) / 128);
+        h->sk_ws_floats = static_cast<size_t>(h->sk_flag_tiles) * 4 * 128 * 64;
+        CK(cudaMalloc(&h->sk_ws, h->sk_ws_floats * sizeof(float)));
+        CK(cudaMalloc(&h->sk_flags, static_cast<size_t>(h->sk_flag_tiles) * 4 * sizeof(int)));
+        CK(cudaMemset(h->sk_flags, 0, static_cast<size_t>(h->sk_flag_tiles) * 4 * sizeof(int)));
         if (h->proj_fp8) {
             CK(cudaMalloc(&h->xq, R * static_cast<size_t>(std::max(c.hidden, std::max(c.intermediate, kQDim)))));
             CK(cudaMalloc(&h->xq_s, R * sizeof(float)));
@@ -249,6 +255,8 @@ int setup_common(qkv_handle *h, bool with_model_scratch) {
         h->prefill_tc = !(pa && std::strcmp(pa, "cuda_core") == 0);
         const char *fs = getenv("QWENASR_B200_FUSED_SWIGLU");
         h->fused_swiglu = !(fs && std::strcmp(fs, "0") == 0);
+        const char *sk = getenv("QWENASR_B200_STREAM_K");
+        h->stream_k = sk && std::strcmp(sk, "1") == 0;
         const char *rs = getenv("QWENASR_B200_RESIDUAL_SLICES");
         h->res_slices = rs && std::strcmp(rs, "1") == 0;
         const char *aa = getenv("QWENASR_B200_APPEND_AHEAD");
@@ -273,7 +281,7 @@ void destroy(qkv_handle *h) {
     cudaFree(h->ap_norm_w); cudaFree(h->ap_norm_b); cudaFree(h->ap_w0); cudaFree(h->ap_b0); cudaFree(h->ap_w1);
     cudaFree(h->ap_b1);
     cudaFree(h->pool); cudaFree(h->scales); cudaFree(h->d_page_table); cudaFree(h->d_rope);
-    cudaFree(h->x); cudaFree(h->qkv); cudaFree(h->res_sl); cudaFree(h->q); cudaFree(h->q_alt); cudaFree(h->gu); cudaFree(h->logits);
+    cudaFree(h->x); cudaFree(h->qkv); cudaFree(h->res_sl); cudaFree(h->sk_ws); cudaFree(h->sk_flags); cudaFree(h->q); cudaFree(h->q_alt); cudaFree(h->gu); cudaFree(h->logits);
     cudaFree(h->am_v); cudaFree(h->am_i); cudaFree(h->am_cnt);
     cudaFree(h->am_keys); cudaFree(h->am_rcnt); cudaFree(h->d_wout_norm);
     cudaFree(h->xn); cudaFree(h->attn); cudaFree(h->act); cudaFree(h->host_stage); cudaFree(h->qkv_sl);
@@ -1068,7 +1076,8 @@ int run_layers(qkv_handle *h, int n, const int *slots, const int *pos, const int
         if (fused) {
             // gate/up projection with SwiGLU in its epilogue: act (bf16) straight from TMEM
             CK(launch_gemm_tc_swiglu(h->xn, L.w_gu, h->act, n, 2 * c.intermediate, c.hidden, h->num_sms, h->d_err,
-                                     h->stream));
+                                     h->stream, h->stream_k ? h->sk_ws : nullptr, h->sk_flags, h->sk_ws_floats,
+                                     h->sk_flag_tiles));
         } else {
             CK(gemm(h, h->xn, L.w_gu, h->gu, n, 2 * c.intermediate, c.hidden, 0));
             CK(launch_swiglu(h->gu, n, c.intermediate, h->act, h->act_dtype, h->stream));
@@ -2065,8 +2074,10 @@ int qkv_gemm_bf16(const void *x, const void *w, float *c, int32_t m, int32_t n, 
                : QKV_ERR_CUDA;
 }
 
-int qkv_gemm_swiglu_bf16(const void *x, const void *w, void *act, int32_t m, int32_t n2, int32_t k, void *stream) {
+int qkv_gemm_swiglu_bf16(const void *x, const void *w, void *act, int32_t m, int32_t n2, int32_t k, float *workspace,
+                         int32_t *flags, int64_t workspace_floats, int32_t flag_tiles, void *stream) {
     if (!x || !w || !act || m < 0 || n2 < 0 || n2 % 2 != 0 || k <= 0 || k % 64 != 0) return QKV_ERR_INVALID_ARG;
+    if ((workspace != nullptr) != (flags != nullptr) || workspace_floats < 0 || flag_tiles < 0) return QKV_ERR_INVALID_ARG;
     int dev = 0, sms = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
         return QKV_ERR_NO_DEVICE;
@@ -2075,7 +2086,8 @@ int qkv_gemm_swiglu_bf16(const void *x, const void *w, void *act, int32_t m, int
     std::call_once(once, [] { prep = prepare_gemm_tc(); });
     if (prep != cudaSuccess) return QKV_ERR_CUDA;
     if (!gemm_tc_supported(m, n2, k)) return QKV_ERR_INVALID_ARG;
-    return launch_gemm_tc_swiglu(x, w, act, m, n2, k, sms, nullptr, static_cast<cudaStream_t>(stream)) == cudaSuccess
+    return launch_gemm_tc_swiglu(x, w, act, m, n2, k, sms, nullptr, static_cast<cudaStream_t>(stream), workspace, flags,
+                                 static_cast<size_t>(workspace_floats), flag_tiles) == cudaSuccess
                ? QKV_OK
                : QKV_ERR_CUDA;
 }

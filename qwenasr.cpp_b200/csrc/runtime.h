@@ -127,6 +127,15 @@ struct qkv_handle {
     float *res_sl = nullptr;
     bool res_slices = false;
     qkv::ResidualFold res_pending;
+    // Stream-K workspace of the fused gate/up GEMM at decode batches (partial
+    // tiles and per-tile counters, the counters zero between launches).
+    float *sk_ws = nullptr;
+    int *sk_flags = nullptr;
+    size_t sk_ws_floats = 0;
+    int sk_flag_tiles = 0;
+    // QWENASR_B200_STREAM_K=1 spreads a decode batch's fused gate/up GEMM over
+    // all SMs (stream-K); off by default: measured 3-5 % slower per decode step.
+    bool stream_k = false;
     uint8_t *xq = nullptr;      // [rows][max(H, Hq D, F)] e4m3 token operand
     float *xq_s = nullptr;      // [rows]
     int *d_out_ids = nullptr;   // [max_rows]

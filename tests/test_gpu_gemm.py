@@ -56,26 +56,39 @@ def test_gemm_repeatable(pkg, m, n, k):
 
 
 @pytest.mark.parametrize("m,n2,k", [(1, 256, 64), (7, 1024, 256), (33, 384, 512), (64, 12288, 2048),
+                                    (32, 6144, 1024), (5, 6144, 1024), (17, 12288, 2048), (64, 1536, 4096),
                                     (300, 6144, 1024), (1000, 12288, 2048)])
 def test_gemm_swiglu_epilogue(pkg, m, n2, k):
     """qkv_gemm_swiglu_bf16 (SwiGLU in the GEMM's epilogue, gate and up rows
-    interleaved one by one) against torch: silu(g) * u of the f32 product of
-    the same bf16 operands, g and u the even and odd rows.  Every output is
-    written (NaN-filled beforehand) and within one bf16 rounding (2^-8
-    relative) of the reference, plus the GEMM's own 1e-4."""
+    interleaved one by one), with and without a stream-K workspace, against
+    torch: silu(g) * u of the f32 product of the same bf16 operands, g and u
+    the even and odd rows.  Every output is written (NaN-filled beforehand)
+    and within one bf16 rounding (2^-8 relative) of the reference, plus the
+    GEMM's own 1e-4."""
     g_ = torch.Generator(device="cuda").manual_seed(m + n2 + k)
     x = torch.randn((m, k), device="cuda", generator=g_).to(torch.bfloat16)
     w = (0.05 * torch.randn((n2, k), device="cuda", generator=g_)).to(torch.bfloat16)
-    act = torch.full((m, n2 // 2), float("nan"), device="cuda", dtype=torch.bfloat16)
-    assert pkg.lib.qkv_gemm_swiglu_bf16(x.data_ptr(), w.data_ptr(), act.data_ptr(), m, n2, k, None) == 0
-    torch.cuda.synchronize()
     gu = x.float() @ w.float().t()
     g, u = gu[:, 0::2], gu[:, 1::2]
     ref = g / (1.0 + torch.exp(-g)) * u
-    got = act.float()
-    assert torch.isfinite(got).all()
-    err = ((got - ref).abs() / (ref.abs() + 1e-3 * ref.abs().max())).max().item()
-    assert err < 2 ** -8 + 2e-4, err
+    # without and with a stream-K workspace (used where the output tiles would
+    # leave SMs idle: the decode shapes here); the workspace call runs twice
+    tiles = 2 * ((n2 + 127) // 128)
+    ws = torch.empty(tiles * 4 * 128 * 64, device="cuda")
+    flags = torch.zeros(tiles * 4, device="cuda", dtype=torch.int32)
+    outs = []
+    for use_ws in (False, True, True):
+        act = torch.full((m, n2 // 2), float("nan"), device="cuda", dtype=torch.bfloat16)
+        args = (ws.data_ptr(), flags.data_ptr(), ws.numel(), tiles) if use_ws else (None, None, 0, 0)
+        assert pkg.lib.qkv_gemm_swiglu_bf16(x.data_ptr(), w.data_ptr(), act.data_ptr(), m, n2, k, *args, None) == 0
+        torch.cuda.synchronize()
+        got = act.float()
+        assert torch.isfinite(got).all()
+        err = ((got - ref).abs() / (ref.abs() + 1e-3 * ref.abs().max())).max().item()
+        assert err < 2 ** -8 + 2e-4, (use_ws, err)
+        outs.append(act)
+    assert int(flags.abs().sum().item()) == 0          # counters left zero
+    assert torch.equal(outs[1], outs[2])               # stream-K is deterministic
 
 
 # ---- FP8 (e4m3) projections: qkv_quantize_rows_e4m3 + qkv_gemm_fp8 ----
