@@ -842,21 +842,23 @@ int layer_kv(qkv_handle *h, int layer, int n, const int *slots, const int *pos, 
 
 // One layer of a KV step whose every layer's projections are on the device
 // (qkv_l: this layer's rows; qkv_next: layer l + 1's, or null for the last
-// layer).  With the append-ahead, layer 0 gets K1 and every layer's K2 also
-// appends layer l + 1; q alternates between two buffers by layer parity.
+// layer).  With the append-ahead, layers 0 .. ahead_from get K1 and the K2 of
+// every layer from ahead_from on also appends layer l + 1 (ahead_from 1 lets
+// layer 0's attention start on layer 0's inputs alone, for callers whose
+// inputs are still arriving); q alternates between two buffers by layer parity.
 int kv_step_layer(qkv_handle *h, int l, int n, const int *slots, const int *pos, const int *lens, const float *qkv_l,
-                  const float *qkv_next, float *out, cudaStream_t st) {
+                  const float *qkv_next, float *out, cudaStream_t st, int ahead_from = 0) {
     const qkv_handle::Layer &L = h->layers[static_cast<size_t>(l)];
     if (!h->append_ahead) return layer_kv(h, l, n, slots, pos, lens, qkv_l, h->q, out, false, L.q_norm, L.k_norm, st);
     float *q_cur = (l & 1) ? h->q_alt : h->q;
     float *q_next = (l & 1) ? h->q : h->q_alt;
-    if (l == 0) {
-        CK(launch_kv_append(append_params(h, 0, n, slots, pos, qkv_l, q_cur, L.q_norm, L.k_norm), h->rt.kv_dtype, st));
+    if (l <= ahead_from) {
+        CK(launch_kv_append(append_params(h, l, n, slots, pos, qkv_l, q_cur, L.q_norm, L.k_norm), h->rt.kv_dtype, st));
         h->launches += 1;
     }
     AttendParams at = attend_params(h, l, n, slots, lens, q_cur, out);
     at.early = 1;   // the kernel before (K1 or K2 of layer l - 1) wrote only each row's last page of this layer
-    if (qkv_next) {
+    if (qkv_next && l >= ahead_from) {
         const qkv_handle::Layer &Ln = h->layers[static_cast<size_t>(l + 1)];
         at.next = append_params(h, l + 1, n, slots, pos, qkv_next, q_next, Ln.q_norm, Ln.k_norm);
     }
@@ -1881,12 +1883,13 @@ int qkv_kv_step_host(qkv_handle *h, int32_t n, const int32_t *stream_ids, const 
             if ((r = upload(l))) return r;
         for (int l = 0; l < L; ++l) {
             CK(cudaStreamWaitEvent(h->stream, h->ev_in[static_cast<size_t>(l)], 0));
-            // With the append-ahead, layer l's launch also reads layer l + 1's inputs.
-            if (h->append_ahead && l + 1 < L)
+            // With the append-ahead, layer l's launch (from layer 1 on: layer 0's
+            // attention starts on layer 0's inputs alone) also reads layer l + 1's.
+            if (h->append_ahead && l >= 1 && l + 1 < L)
                 CK(cudaStreamWaitEvent(h->stream, h->ev_in[static_cast<size_t>(l + 1)], 0));
             if ((r = kv_step_layer(h, l, n, ds, dp, dl, stage_in + in_stride * l,
                                    l + 1 < L ? stage_in + in_stride * (l + 1) : nullptr, stage_out + out_stride * l,
-                                   h->stream)))
+                                   h->stream, 1)))
                 break;
             CK(cudaEventRecord(h->ev_done[static_cast<size_t>(l)], h->stream));
             CK(cudaStreamWaitEvent(h->copy_out, h->ev_done[static_cast<size_t>(l)], 0));
