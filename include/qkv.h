@@ -279,12 +279,18 @@ int qkv_prefill_attend_q16(qkv_handle *h, int32_t layer, int32_t n, const int32_
 /* One KV-cache step of the microbench: for each of the n streams append one
  * token and attend, for every layer.  qkv[n_layers][n][Hq*D+2*Hkv*D] f32,
  * out[n_layers][n][Hq*D] f32 (layer-major), device pointers; the streams'
- * lengths grow by 1.  stream_ids is a host array. */
+ * lengths grow by 1.  stream_ids is a host array.  Since every layer's
+ * projections are given up front, the attention launch of layer l also
+ * appends layer l + 1's token (the stored bytes are those of the separate
+ * append); a steady batch replays as one CUDA graph. */
 int qkv_kv_step(qkv_handle *h, int32_t n, const int32_t *stream_ids, const float *qkv_dev,
                 float *out_dev, void *stream);
 
 /* qkv_kv_step with pinned-or-pageable HOST qkv/out buffers: the copies in and
- * out are part of the call (synchronising). */
+ * out are part of the call (synchronising), pipelined by layer under the
+ * kernels (each layer's inputs go up a few layers ahead of their use, its
+ * outputs come back as soon as its attention has run).  Pinned buffers
+ * replay copies and kernels as one captured graph per (n, buffers). */
 int qkv_kv_step_host(qkv_handle *h, int32_t n, const int32_t *stream_ids, const float *qkv_host,
                      float *out_host);
 
