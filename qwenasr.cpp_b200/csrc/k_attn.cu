@@ -14,8 +14,9 @@
 // head, atomic counter) merges them.  Counters reset themselves.
 //
 // CTA = HALVES x 8 consumer warps + 1 producer warp + 3 append warps (busy
-// only with the append-ahead of the next layer, AttendParams::next).  Consumer warp g (and,
-// with HALVES = 2, warp g + 8) serves kv head g (q heads 2g and 2g+1).  With
+// only with the append-ahead of the next layer, AttendParams::next).
+// Consumer warp g (and, with HALVES = 2, warp g + 8) serves kv head g (q
+// heads 2g and 2g+1).  With
 // two halves each warp keeps its own online-softmax state; at the end of a
 // segment warp g + 8 hands (m, l, O) to warp g through shared memory (bounded
 // flag waits) and warp g merges.  The halves share a head's work in one of two
@@ -463,7 +464,7 @@ __global__ void __launch_bounds__(threads<TC>(), 1) decode_attn_kernel(AttendPar
     float *my_p = pbuf + warp * (2 * CH);
     TOut *out = static_cast<TOut *>(p.out);
 
-    if (p.early) pdl_wait();   // q (or qkv) and the merge scratch come from the preceding kernels
+    if (p.early) pdl_wait();   // q and the merge scratch come from the preceding kernels
     int iter = 0;
     int nseg = 0;                                   // segments finished (both halves count alike)
     int r = r0;
