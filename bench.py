@@ -112,6 +112,9 @@ class ClockSampler:
         self.rows = []
         self._stop = threading.Event()
         self._t = None
+        # NVML set up here, before the timed region, so sampling starts with it
+        self._nv, self._h = self._nvml_handle()
+        self.source = "nvml 5 ms" if self._h is not None else "nvidia-smi 0.2 s"
 
     def _nvml_handle(self):
         try:
@@ -124,23 +127,24 @@ class ClockSampler:
         except Exception:
             return None, None
 
+    def _nvml_sample(self):
+        nv, h = self._nv, self._h
+        bits = (nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap)
+        try:
+            if not hasattr(self, "_mx"):
+                self._mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+            rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+            self.rows.append([str(self.gpu), str(sm), str(self._mx), "", hex(rs)] +
+                             ["Active" if rs & b else "Not Active" for b in bits])
+        except Exception:
+            pass
+
     def _run(self):
-        nv, h = self._nvml_handle()
-        self.source = "nvml 5 ms" if h is not None else "nvidia-smi 0.2 s"
-        if h is not None:
-            bits = [("hw_slowdown", nv.nvmlClocksEventReasonHwSlowdown),
-                    ("hw_thermal_slowdown", nv.nvmlClocksEventReasonHwThermalSlowdown),
-                    ("sw_thermal_slowdown", nv.nvmlClocksEventReasonSwThermalSlowdown),
-                    ("sw_power_cap", nv.nvmlClocksEventReasonSwPowerCap)]
-            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        if self._h is not None:
             while not self._stop.is_set():
-                try:
-                    sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
-                    rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
-                    self.rows.append([str(self.gpu), str(sm), str(mx), "", hex(rs)] +
-                                     ["Active" if rs & b else "Not Active" for _, b in bits])
-                except Exception:
-                    pass
+                self._nvml_sample()
                 self._stop.wait(0.005)
             return
         while not self._stop.is_set():
@@ -154,6 +158,8 @@ class ClockSampler:
             self._stop.wait(0.2)
 
     def __enter__(self):
+        if self._h is not None:
+            self._nvml_sample()   # one sample as the timed region starts
         self._t = threading.Thread(target=self._run, daemon=True)
         self._t.start()
         return self
@@ -161,6 +167,8 @@ class ClockSampler:
     def __exit__(self, *a):
         self._stop.set()
         self._t.join(timeout=10)
+        if self._h is not None:
+            self._nvml_sample()   # and one as it ends
 
     def summary(self) -> dict:
         if not self.rows:
